@@ -1,0 +1,282 @@
+"""Headline benchmark: decode tokens/s of Llama-3-8B-architecture serving at TP = N B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 launch one process per GPU:
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+
+Workload: 64 concurrent streams, 1024-token uniform-random prompts (seed 0),
+greedy decoding, random-init bf16 weights of the Llama-3-8B architecture, tensor-parallel over the
+N GPUs. All 64 prompts are prefilled first (untimed); then W warm-up decode steps; then:
+
+  * value: K decode steps run by the engine's multi-step decode (CUDA-graph replays with the
+    next step's inputs built on the device), timed with CUDA events between barriers, max over
+    ranks. Each step reads every weight (16 GB at TP1) and the whole KV history, far more than
+    the 126 MB L2, so no flush is needed between steps;
+  * e2e: K more decode steps through the public ``Engine.step()`` API, each including the
+    host-to-device copy of that step's inputs from pinned memory and the device-to-host read of
+    the sampled ids, timed on the host between device synchronisations, max over ranks.
+
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+if HERE not in sys.path:
+    sys.path.insert(0, HERE)
+
+METRIC = "decode tok/s at TP8 (1/2/4/8 GPU); failover pause p99; dead-rank detect ms"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t is not None:
+            self._t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args) -> None:
+    why = ("reference cannot be installed offline: its root pyproject is a uv workspace that setuptools "
+           "cannot build (flat-layout discovery error), its packages need hatchling (absent from the wheelhouse), "
+           "and its engine path is a vLLM 0.31 plugin while vLLM 0.22 is installed")
+    ref_dir = os.path.join(HERE, "baseline", "_ref")
+    if os.path.isdir(ref_dir) and any(n.startswith("everserve") for n in os.listdir(ref_dir)):
+        why = ("reference installed but its decode path is a plugin pinned to vLLM 0.31.0 "
+               "(adapters/vllm/PIN); the installed vLLM is 0.22")
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why}))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="llama-3-8b")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prompt-len", type=int, default=1024)
+    ap.add_argument("--max-tokens", type=int, default=512)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--collective", default="fused", choices=["fused", "nccl"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    assert 4 + args.warmup + 2 * args.steps <= args.max_tokens, "steps exceed the 512-token generation"
+
+    import torch
+    import torch.distributed as dist
+
+    from everserve_b200 import _ext
+    from everserve_b200.engine import Engine, EngineConfig, LocalExecutor, SamplingParams
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    _ext.load()
+    collective = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        from everserve_b200.parallel.collective import make_tp_collective
+
+        collective = make_tp_collective(dev, kind=args.collective)
+
+    cfg = EngineConfig(args.model, device=str(dev), max_batch=args.batch,
+                       max_model_len=args.prompt_len + args.max_tokens + 16, max_prefill_tokens=8192,
+                       tensor_parallel=world, seed=args.seed)
+    ex = LocalExecutor(cfg, rank=rank, collective=collective)
+    eng = Engine(cfg, executor=ex)
+    g = torch.Generator().manual_seed(args.seed)
+    vocab = cfg.model.vocab
+    prompts = torch.randint(0, vocab, (args.batch, args.prompt_len), generator=g).tolist()
+    for p in prompts:
+        eng.add_request(p, SamplingParams(max_tokens=args.max_tokens))
+    # prefill everything (untimed)
+    while eng.scheduler.waiting:
+        eng.step()
+    runner = ex.worker.runner
+    for _ in range(args.warmup):
+        eng.step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm the multi-step path once (graph already captured; decode_loop allocations)
+    eng.decode_steps(2)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    eng.decode_steps(args.steps)
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    dev_ms = max_over_ranks(start.elapsed_time(end))
+
+    # end to end through Engine.step(): H2D of inputs + D2H of sampled ids every step
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.step()
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    clk = clocks.stop()
+
+    # kernel launches of this framework per decode step: count the extension calls of one step
+    launches_per_step = count_launches(eng, ex)
+
+    tokens = args.batch * args.steps
+    value = tokens / (dev_ms / 1e3)
+    e2e = tokens / e2e_s
+    out = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dev_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: uniform-random 1024-token prompts (seed 0), random-init weights",
+        "config": {"model": "Llama-3-8B architecture (32 layers, hidden 4096, 32/8 heads, d 128, ffn 14336, "
+                            "vocab 128256)", "global_batch": args.batch, "seq_len": args.prompt_len,
+                   "parallelism": f"tp{world}", "collective": args.collective if world > 1 else "none",
+                   "l2": "inputs larger than L2 (16 GB of weights / TP and the KV history read every step)"},
+        "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": runner.h2d_bytes,
+                "d2h_bytes_per_step": args.batch * 8},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk,
+        "impl": "ours",
+        "so": os.path.basename(_ext.so_path() or ""),
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def count_launches(eng, ex) -> int:
+    """Kernel launches of the extension in one decode step (the step run eagerly, outside timing)."""
+    ops = ex.worker.model.ops
+    C = ops.C
+    counts = {"n": 0}
+    weights = {"paged_decode": 2}
+
+    class Counting:
+        def __getattr__(self, name):
+            fn = getattr(C, name)
+            if not callable(fn) or name.startswith("gemm_pick") or name == "gemm_tiles":
+                return fn
+
+            def wrapped(*a, **k):
+                counts["n"] += weights.get(name, 1)
+                return fn(*a, **k)
+
+            return wrapped
+
+    coll = getattr(ex.worker.tp, "collective", None)
+    ops.C = Counting()
+    if coll is not None and hasattr(coll, "count_launches"):
+        coll.count_launches(counts)
+    runner = ex.worker.runner
+    saved = runner.use_graphs
+    runner.use_graphs = False
+    try:
+        eng.step()
+    finally:
+        runner.use_graphs = saved
+        ops.C = C
+        if coll is not None and hasattr(coll, "count_launches"):
+            coll.count_launches(None)
+    return counts["n"] + 1  # + the on-device input advance of multi-step decode
+
+
+if __name__ == "__main__":
+    main()

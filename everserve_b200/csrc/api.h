@@ -1,0 +1,74 @@
+// Launch interface of the everserve_b200 sm_100a kernels.
+//
+// The kernels (.cu) see only CUDA headers; the torch bindings (ops.cpp) check tensors and call
+// these launchers with raw pointers on the caller's stream. Every launcher returns a cudaError_t
+// (cudaErrorInvalidValue for a shape it refuses), so the .cu files stay free of torch headers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace es {
+
+// ---- elementwise.cu ---------------------------------------------------------------------------
+cudaError_t launch_rmsnorm(const void* x, void* residual, const void* w, void* y, int64_t rows, int hidden,
+                           int64_t x_stride, int64_t y_stride, float eps, cudaStream_t s);
+cudaError_t launch_rope_kv(const void* qkv, const void* bias, const int64_t* positions, const float* cos_sin,
+                           const int64_t* slots, void* q_out, void* cache, int64_t T, int hq, int hkv, int d,
+                           int block_size, const int64_t* strides5, cudaStream_t s);
+cudaError_t launch_silu_mul(const void* gu, void* out, int64_t rows, int inter, cudaStream_t s);
+cudaError_t launch_embed(const int64_t* ids, const void* table, void* out, int64_t T, int hidden, int64_t vocab,
+                         cudaStream_t s);
+cudaError_t launch_decode_advance(int64_t* st, const int64_t* sampled, const int* bt, int64_t bt_stride, int b, int B,
+                                  int bs, cudaStream_t s);
+cudaError_t launch_argmax(const void* logits, int64_t* out, int64_t rows, int vocab, int64_t stride, cudaStream_t s);
+
+// ---- gemm.cu -------------------------------------------------------------------------------------
+struct GemmArgs {
+  const void* x;  // [M, K] bf16, row stride ldx
+  const void* w;  // [N, K] bf16, row stride ldw
+  void* out;      // [M, N] bf16, row stride ldo
+  const void* residual;  // optional [M, N] bf16, row stride ldr
+  float* ws;             // split-K partials [splits, M, N] (splits > 1)
+  int* counters;         // one per output tile, zero before first use (splits > 1)
+  int* status;           // set non-zero if a bounded wait ran out
+  int64_t M, N, K, ldx, ldw, ldo, ldr;
+  int splits;
+};
+int64_t gemm_pick_bn(int64_t M);
+int64_t gemm_pick_splits(int64_t N, int64_t K, int64_t num_sms);
+int64_t gemm_tiles(int64_t M, int64_t N);  // output tiles (n tiles x m tiles) for counters
+cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t s);
+
+// ---- attention.cu --------------------------------------------------------------------------------
+struct DecodeArgs {
+  const void* q;  // [B, Hq, D]
+  int64_t q_stride;
+  const void* cache;  // [nb, 2, Hkv, bs, D]
+  int64_t s_block, s_kv;
+  const int* block_tables;
+  int64_t bt_stride;
+  const int* ctx_lens;
+  void* out;  // [B, Hq * D] rows of out_stride
+  int64_t out_stride;
+  float* part_o;
+  float* part_ml;
+  int* status;
+  int B, hq, hkv, d, block_size, max_splits, part_tokens;
+  float scale;
+};
+cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t s);
+
+// ---- kvcopy.cu -----------------------------------------------------------------------------------
+struct KvCopyArgs {
+  const int64_t* layer_ptrs;  // device array of per-layer cache addresses
+  const int64_t* slots;       // [n]
+  const int64_t* heads;       // [H]
+  void* staging;              // [L, H, cap, 2, d]
+  int64_t n, L, H, cap, d, block_size;
+  int64_t strides[5];
+  int elem;
+};
+cudaError_t launch_kv_copy(const KvCopyArgs& a, bool gather, cudaStream_t s);
+
+}  // namespace es

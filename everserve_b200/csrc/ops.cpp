@@ -1,0 +1,293 @@
+// Torch bindings of the everserve_b200 sm_100a kernels (module everserve_b200._C).
+//
+// Each binding checks dtypes, shapes and alignment, then calls the kernel's launcher on the
+// current CUDA stream. A refused launch raises; nothing falls back to another implementation.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "api.h"
+
+namespace {
+
+#define ES_CHECK_CUDA(expr)                                                              \
+  do {                                                                                   \
+    cudaError_t _e = (expr);                                                             \
+    TORCH_CHECK(_e == cudaSuccess, #expr " failed: ", cudaGetErrorString(_e));            \
+  } while (0)
+
+void check_bf16(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bf16");
+}
+
+cudaStream_t cur() { return at::cuda::getCurrentCUDAStream(); }
+
+void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w, torch::Tensor y, double eps) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(y, "y");
+  const int hidden = (int)x.size(-1);
+  TORCH_CHECK(x.stride(-1) == 1 && y.stride(-1) == 1, "rows must be contiguous");
+  TORCH_CHECK(w.numel() == hidden, "weight size");
+  const int64_t rows = x.numel() / hidden;
+  const int64_t xs = x.dim() >= 2 ? x.stride(-2) : hidden;
+  const int64_t ys = y.dim() >= 2 ? y.stride(-2) : hidden;
+  void* rp = nullptr;
+  if (residual.has_value()) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->is_contiguous() && residual->numel() == rows * hidden, "residual must be contiguous");
+    rp = residual->data_ptr();
+  }
+  const c10::cuda::CUDAGuard g(x.device());
+  ES_CHECK_CUDA(es::launch_rmsnorm(x.data_ptr(), rp, w.data_ptr(), y.data_ptr(), rows, hidden, xs, ys, (float)eps, cur()));
+}
+
+void rope_kv_write(torch::Tensor qkv, c10::optional<torch::Tensor> bias, torch::Tensor positions,
+                   torch::Tensor cos_sin, torch::Tensor slots, torch::Tensor q_out, torch::Tensor cache, int64_t hq,
+                   int64_t hkv, int64_t block_size, std::vector<int64_t> strides) {
+  check_bf16(qkv, "qkv");
+  check_bf16(q_out, "q_out");
+  check_bf16(cache, "cache");
+  TORCH_CHECK(qkv.is_contiguous() && q_out.is_contiguous(), "qkv and q_out must be contiguous");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && slots.scalar_type() == at::kLong, "int64 positions/slots");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.is_cuda(), "fp32 cos_sin");
+  TORCH_CHECK(strides.size() == 5, "five cache strides");
+  const int64_t T = qkv.size(0);
+  const int d = (int)cos_sin.size(1);
+  TORCH_CHECK(qkv.size(1) == (hq + 2 * hkv) * d, "qkv width");
+  TORCH_CHECK(positions.numel() >= T && slots.numel() >= T, "positions/slots length");
+  const void* bp = nullptr;
+  if (bias.has_value()) {
+    check_bf16(*bias, "bias");
+    bp = bias->data_ptr();
+  }
+  const c10::cuda::CUDAGuard g(qkv.device());
+  ES_CHECK_CUDA(es::launch_rope_kv(qkv.data_ptr(), bp, positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(),
+                                   slots.data_ptr<int64_t>(), q_out.data_ptr(), cache.data_ptr(), T, (int)hq,
+                                   (int)hkv, d, (int)block_size, strides.data(), cur()));
+}
+
+void silu_mul(torch::Tensor gu, torch::Tensor out) {
+  check_bf16(gu, "gate_up");
+  check_bf16(out, "out");
+  TORCH_CHECK(gu.is_contiguous() && out.is_contiguous(), "contiguous");
+  const int inter = (int)out.size(-1);
+  TORCH_CHECK(gu.size(-1) == 2 * inter, "gate_up width");
+  const c10::cuda::CUDAGuard g(gu.device());
+  ES_CHECK_CUDA(es::launch_silu_mul(gu.data_ptr(), out.data_ptr(), out.numel() / inter, inter, cur()));
+}
+
+void embed(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
+  check_bf16(table, "table");
+  check_bf16(out, "out");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_cuda(), "ids must be int64 on the device");
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous(), "contiguous");
+  const c10::cuda::CUDAGuard g(table.device());
+  ES_CHECK_CUDA(es::launch_embed(ids.data_ptr<int64_t>(), table.data_ptr(), out.data_ptr(), ids.numel(),
+                                 (int)table.size(1), table.size(0), cur()));
+}
+
+void argmax(torch::Tensor logits, torch::Tensor out) {
+  check_bf16(logits, "logits");
+  TORCH_CHECK(out.scalar_type() == at::kLong && out.is_cuda(), "out must be int64 on the device");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "[rows, vocab] with contiguous rows");
+  const c10::cuda::CUDAGuard g(logits.device());
+  ES_CHECK_CUDA(es::launch_argmax(logits.data_ptr(), out.data_ptr<int64_t>(), logits.size(0), (int)logits.size(1),
+                                  logits.stride(0), cur()));
+}
+
+void decode_advance(torch::Tensor st, torch::Tensor sampled, torch::Tensor bt, int64_t b, int64_t bs) {
+  TORCH_CHECK(st.scalar_type() == at::kLong && st.dim() == 2 && st.size(0) == 4 && st.is_contiguous(), "state [4, B]");
+  TORCH_CHECK(sampled.scalar_type() == at::kLong && bt.scalar_type() == at::kInt && bt.stride(1) == 1, "dtypes");
+  TORCH_CHECK(sampled.numel() >= b && bt.size(0) >= b && b <= st.size(1), "sizes");
+  const c10::cuda::CUDAGuard g(st.device());
+  ES_CHECK_CUDA(es::launch_decode_advance(st.data_ptr<int64_t>(), sampled.data_ptr<int64_t>(), bt.data_ptr<int>(),
+                                          bt.stride(0), (int)b, (int)st.size(1), (int)bs, cur()));
+}
+
+void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
+               torch::Tensor ws, torch::Tensor counters, torch::Tensor status, int64_t splits) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D operands");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "K-contiguous operands");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K, "K mismatch: x has ", K, ", w has ", w.size(1));
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "out shape");
+  TORCH_CHECK(status.scalar_type() == at::kInt && status.is_cuda(), "status must be int32 on the device");
+  es::GemmArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.out = out.data_ptr();
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ldx = x.stride(0);
+  a.ldw = w.stride(0);
+  a.ldo = out.stride(0);
+  a.splits = (int)splits;
+  a.status = status.data_ptr<int>();
+  if (residual.has_value()) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N && residual->stride(1) == 1, "residual shape");
+    a.residual = residual->data_ptr();
+    a.ldr = residual->stride(0);
+  }
+  if (splits > 1) {
+    TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= splits * M * N, "split-K workspace too small");
+    TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= es::gemm_tiles(M, N),
+                "split-K counters too small");
+    a.ws = ws.data_ptr<float>();
+    a.counters = counters.data_ptr<int>();
+  }
+  const c10::cuda::CUDAGuard g(x.device());
+  ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
+}
+
+void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
+                  torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor status,
+                  int64_t max_splits, int64_t part_tokens, double scale) {
+  check_bf16(q, "q");
+  check_bf16(cache, "cache");
+  check_bf16(out, "out");
+  TORCH_CHECK(cache.dim() == 5 && cache.is_contiguous(), "cache must be contiguous [nb, 2, Hkv, bs, D]");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt, "int32 tables");
+  TORCH_CHECK(part_o.scalar_type() == at::kFloat && part_ml.scalar_type() == at::kFloat, "fp32 scratch");
+  const int B = (int)q.size(0);
+  const int hkv = (int)cache.size(2), bs = (int)cache.size(3), d = (int)cache.size(4);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == d && q.stride(2) == 1 && q.stride(1) == d, "q must be [B, Hq, D]");
+  const int hq = (int)q.size(1);
+  TORCH_CHECK(part_o.numel() >= (int64_t)B * hq * max_splits * d &&
+                  part_ml.numel() >= (int64_t)B * hq * max_splits * 2,
+              "split scratch too small");
+  TORCH_CHECK(out.stride(-1) == 1 && out.size(0) == B, "out rows");
+  TORCH_CHECK(block_tables.dim() == 2 && block_tables.size(0) >= B && ctx_lens.numel() >= B, "tables");
+  es::DecodeArgs a{};
+  a.q = q.data_ptr();
+  a.q_stride = q.stride(0);
+  a.cache = cache.data_ptr();
+  a.s_block = cache.stride(0);
+  a.s_kv = cache.stride(1);
+  a.block_tables = block_tables.data_ptr<int>();
+  a.bt_stride = block_tables.stride(0);
+  a.ctx_lens = ctx_lens.data_ptr<int>();
+  a.out = out.data_ptr();
+  a.out_stride = out.stride(0);
+  a.part_o = part_o.data_ptr<float>();
+  a.part_ml = part_ml.data_ptr<float>();
+  a.status = status.data_ptr<int>();
+  a.B = B;
+  a.hq = hq;
+  a.hkv = hkv;
+  a.d = d;
+  a.block_size = bs;
+  a.max_splits = (int)max_splits;
+  a.part_tokens = (int)part_tokens;
+  a.scale = (float)scale;
+  const c10::cuda::CUDAGuard g(q.device());
+  ES_CHECK_CUDA(es::launch_paged_decode(a, cur()));
+}
+
+void kv_copy(bool gather, torch::Tensor layer_ptrs, torch::Tensor slots, torch::Tensor heads, int64_t staging_ptr,
+             int64_t cap, int64_t d, int64_t block_size, std::vector<int64_t> strides, int64_t elem) {
+  TORCH_CHECK(layer_ptrs.is_cuda() && slots.is_cuda() && heads.is_cuda(), "device index tensors");
+  TORCH_CHECK(layer_ptrs.scalar_type() == at::kLong && slots.scalar_type() == at::kLong &&
+                  heads.scalar_type() == at::kLong,
+              "int64 index tensors");
+  TORCH_CHECK(strides.size() == 5, "five strides");
+  es::KvCopyArgs a{};
+  a.layer_ptrs = layer_ptrs.data_ptr<int64_t>();
+  a.slots = slots.data_ptr<int64_t>();
+  a.heads = heads.data_ptr<int64_t>();
+  a.staging = reinterpret_cast<void*>(staging_ptr);
+  a.n = slots.numel();
+  a.L = layer_ptrs.numel();
+  a.H = heads.numel();
+  a.cap = cap;
+  a.d = d;
+  a.block_size = block_size;
+  for (int i = 0; i < 5; i++) a.strides[i] = strides[i];
+  a.elem = (int)elem;
+  const c10::cuda::CUDAGuard g(slots.device());
+  ES_CHECK_CUDA(es::launch_kv_copy(a, gather, cur()));
+}
+
+// ---- host helpers ---------------------------------------------------------------------------------
+
+int64_t host_register_mapped(int64_t ptr, int64_t bytes) {
+  ES_CHECK_CUDA(cudaHostRegister(reinterpret_cast<void*>(ptr), (size_t)bytes,
+                                 cudaHostRegisterMapped | cudaHostRegisterPortable));
+  void* dev = nullptr;
+  ES_CHECK_CUDA(cudaHostGetDevicePointer(&dev, reinterpret_cast<void*>(ptr), 0));
+  return reinterpret_cast<int64_t>(dev);
+}
+
+void host_unregister(int64_t ptr) { ES_CHECK_CUDA(cudaHostUnregister(reinterpret_cast<void*>(ptr))); }
+
+int64_t device_alloc(int64_t bytes) {
+  void* p = nullptr;
+  ES_CHECK_CUDA(cudaMalloc(&p, (size_t)bytes));
+  ES_CHECK_CUDA(cudaMemset(p, 0, (size_t)bytes));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void device_free(int64_t ptr) { ES_CHECK_CUDA(cudaFree(reinterpret_cast<void*>(ptr))); }
+
+void memset_async(int64_t ptr, int64_t bytes) {
+  ES_CHECK_CUDA(cudaMemsetAsync(reinterpret_cast<void*>(ptr), 0, (size_t)bytes, cur()));
+}
+
+pybind11::bytes ipc_handle(int64_t ptr) {
+  cudaIpcMemHandle_t h;
+  ES_CHECK_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(ptr)));
+  return pybind11::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+
+int64_t ipc_open(const std::string& handle) {
+  TORCH_CHECK(handle.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  ES_CHECK_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr) { ES_CHECK_CUDA(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr))); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "everserve_b200 sm_100a kernels";
+  m.def("rmsnorm", &rmsnorm, "RMSNorm, optionally fused with the residual add");
+  m.def("rope_kv_write", &rope_kv_write, "RoPE on q/k and the paged-KV write of k/v");
+  m.def("silu_mul", &silu_mul, "silu(gate) * up");
+  m.def("embed", &embed, "embedding gather");
+  m.def("argmax", &argmax, "greedy argmax per row");
+  m.def("decode_advance", &decode_advance, "next decode step's inputs from the sampled ids");
+  m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM out = x . w^T (+ residual)");
+  m.def("gemm_pick_bn", &es::gemm_pick_bn);
+  m.def("gemm_pick_splits", &es::gemm_pick_splits);
+  m.def("gemm_tiles", &es::gemm_tiles);
+  m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
+  m.def("kv_gather", [](torch::Tensor lp, torch::Tensor s, torch::Tensor h, int64_t st, int64_t cap, int64_t d,
+                        int64_t bs, std::vector<int64_t> str, int64_t el) { kv_copy(true, lp, s, h, st, cap, d, bs, str, el); },
+        "paged cache -> staging rows, all layers in one launch");
+  m.def("kv_scatter", [](torch::Tensor lp, torch::Tensor s, torch::Tensor h, int64_t st, int64_t cap, int64_t d,
+                         int64_t bs, std::vector<int64_t> str, int64_t el) { kv_copy(false, lp, s, h, st, cap, d, bs, str, el); },
+        "staging rows -> paged cache");
+  m.def("host_register_mapped", &host_register_mapped);
+  m.def("host_unregister", &host_unregister);
+  m.def("device_alloc", &device_alloc);
+  m.def("device_free", &device_free);
+  m.def("memset_async", &memset_async);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+}

@@ -1,0 +1,37 @@
+"""Engine configuration."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from ..models.config import ModelConfig, get_config
+
+
+@dataclass
+class EngineConfig:
+    model: ModelConfig | str
+    device: str = "cuda"
+    dtype: torch.dtype = torch.bfloat16
+    seed: int = 0
+    block_size: int = 16
+    num_blocks: int | None = None  # None: fill `kv_memory_fraction` of the free device memory
+    kv_memory_fraction: float = 0.85
+    max_batch: int = 64
+    max_model_len: int = 4096
+    max_prefill_tokens: int = 8192
+    tensor_parallel: int = 1
+    pipeline_parallel: int = 1
+    use_cuda_graphs: bool = True
+    extra: dict = field(default_factory=dict)
+
+    def __post_init__(self):
+        if isinstance(self.model, str):
+            self.model = get_config(self.model)
+        if self.block_size not in (16, 32):
+            raise ValueError("block_size must be 16 or 32")
+
+    @property
+    def world_size(self) -> int:
+        return self.tensor_parallel * self.pipeline_parallel

@@ -1,0 +1,73 @@
+"""Requests and their per-step state.
+
+A request's ``tokens`` are its prompt followed by its outputs. ``num_computed`` counts the leading
+tokens whose K/V is in the cache. A step feeds a request either its whole uncomputed prompt
+(prefill) or exactly one token at position ``num_computed`` (decode shape). When that position is
+the last token, the sampled id is a new output; when it is earlier (after a resume from committed
+state), the step is a replay of a position that already has an output, and the sampled id must
+equal the recorded one (exact replay).
+
+Reference parity: ``resume_point = min(committed, num_tokens - 1)`` and the one-position-per-step
+replay of adapters/vllm/everserve_vllm/resume.py:16-115.
+"""
+
+from __future__ import annotations
+
+import enum
+import itertools
+from dataclasses import dataclass, field
+
+_ids = itertools.count()
+
+
+class Status(enum.Enum):
+    WAITING = "waiting"
+    RUNNING = "running"
+    FINISHED = "finished"
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    eos_id: int | None = None
+    ignore_eos: bool = True
+
+
+@dataclass
+class Request:
+    prompt: list[int]
+    params: SamplingParams = field(default_factory=SamplingParams)
+    req_id: str = field(default_factory=lambda: f"req-{next(_ids)}")
+    outputs: list[int] = field(default_factory=list)
+    status: Status = Status.WAITING
+    num_computed: int = 0
+    committed: int = 0  # tokens whose K/V the committed-KV store holds
+    blocks: list[int] = field(default_factory=list)
+    arrival: int = 0
+    replay_mismatches: int = 0
+
+    @property
+    def tokens(self) -> list[int]:
+        return self.prompt + self.outputs
+
+    @property
+    def num_tokens(self) -> int:
+        return len(self.prompt) + len(self.outputs)
+
+    @property
+    def finished(self) -> bool:
+        return self.status is Status.FINISHED
+
+    def is_prefill(self) -> bool:
+        return self.num_computed == 0 and len(self.prompt) > 1
+
+    def done_generating(self) -> bool:
+        if len(self.outputs) >= self.params.max_tokens:
+            return True
+        if not self.params.ignore_eos and self.params.eos_id is not None and self.outputs:
+            return self.outputs[-1] == self.params.eos_id
+        return False
+
+    def resume_point(self) -> int:
+        """Where computation restarts after a loss: the committed count, at most the last token."""
+        return min(self.committed, self.num_tokens - 1)

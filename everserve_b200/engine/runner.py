@@ -1,0 +1,204 @@
+"""Model runner: one rank's forward over its KV cache, with CUDA graphs for decode.
+
+Inputs reach the device in one pass per step: the host packs ids, positions, slots and context
+lengths into one pinned int64 buffer and the block tables into one pinned int32 buffer, and two
+asynchronous copies land them in the static device buffers the captured graphs read. Decode runs
+as a graph replay per batch bucket (padded rows have slot -1 and context length 0, which every
+kernel skips). Prefill runs eagerly.
+
+``decode_loop(k)`` runs k decode steps with no host round trip: after each replay a small kernel
+turns the sampled ids into the next step's inputs (position + 1, the slot from the block table).
+The engine uses it for multi-step decoding when no request can finish inside the window.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ..models.llama import DecoderLM, StepInput
+from .scheduler import StepPlan
+
+_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+
+
+class ModelRunner:
+    def __init__(self, model: DecoderLM, num_blocks: int, block_size: int = 16, max_batch: int = 64,
+                 max_model_len: int = 4096, use_graphs: bool = True):
+        self.model = model
+        self.device = model.device
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+        self.max_batch = max_batch
+        self.max_model_len = max_model_len
+        self.max_blocks = (max_model_len + block_size - 1) // block_size
+        self.use_graphs = use_graphs and self.device.type == "cuda"
+        shape = model.kv_cache_shape(num_blocks, block_size)
+        self.caches = [torch.zeros(shape, dtype=model.dtype, device=self.device) for _ in range(model.l1 - model.l0)]
+        self.buckets = [b for b in _BUCKETS if b < max_batch] + [max_batch]
+        B = max_batch
+        pin = self.device.type == "cuda"
+        # host staging: rows = ids, positions, slots, ctx_lens
+        self.h_i64 = torch.zeros(4, B, dtype=torch.int64, pin_memory=pin)
+        self.h_bt = torch.zeros(B, self.max_blocks, dtype=torch.int32, pin_memory=pin)
+        self.h_i64_np = self.h_i64.numpy()
+        self.h_bt_np = self.h_bt.numpy()
+        self.h2d_bytes = 0
+        self.d_i64 = torch.zeros(4, B, dtype=torch.int64, device=self.device)
+        self.d_bt = torch.zeros(B, self.max_blocks, dtype=torch.int32, device=self.device)
+        self.d_ctx32 = torch.zeros(B, dtype=torch.int32, device=self.device)
+        self.d_seq = torch.arange(B, dtype=torch.int64, device=self.device)
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_out: dict[int, torch.Tensor] = {}
+        self.h_out = torch.zeros(B, dtype=torch.int64, pin_memory=pin)
+        self._pool = None
+        if self.device.type == "cuda" and model.ops.kind == "kernel":
+            model.ops.reserve_linear(max(max_batch, 1), model.linear_shapes())
+            model.ops.reserve_attention(max_batch, model.hq, model.d, max_model_len)
+
+    # ---- inputs ----------------------------------------------------------------------------------
+    def _bucket(self, n: int) -> int:
+        for b in self.buckets:
+            if b >= n:
+                return b
+        raise ValueError(f"batch {n} above max_batch {self.max_batch}")
+
+    def stage_decode(self, plan: StepPlan) -> int:
+        """Copy a decode plan's inputs into the static device buffers; returns the bucket size."""
+        n = len(plan.reqs)
+        b = self._bucket(n)
+        h = self.h_i64_np
+        h[:, :b] = 0
+        h[2, :b] = -1
+        bs = self.block_size
+        hbt = self.h_bt_np
+        for i, r in enumerate(plan.reqs):
+            p = r.start_pos
+            bt = r.block_table
+            h[0, i] = r.token_ids[0]
+            h[1, i] = p
+            h[2, i] = bt[p // bs] * bs + p % bs
+            h[3, i] = p + 1
+            hbt[i, : len(bt)] = bt
+        self.d_i64[:, :b].copy_(self.h_i64[:, :b], non_blocking=True)
+        self.d_bt[:b].copy_(self.h_bt[:b], non_blocking=True)
+        self.h2d_bytes = 4 * b * 8 + b * self.max_blocks * 4
+        return b
+
+    def _decode_input(self, b: int) -> StepInput:
+        self.d_ctx32[:b].copy_(self.d_i64[3, :b])
+        return StepInput(ids=self.d_i64[0, :b], positions=self.d_i64[1, :b], slots=self.d_i64[2, :b],
+                         block_tables=self.d_bt[:b], ctx_lens=self.d_ctx32[:b], q_seq=self.d_seq[:b],
+                         logits_idx=self.d_seq[:b], is_decode=True, max_model_len=self.max_model_len)
+
+    def prefill_input(self, plan: StepPlan) -> StepInput:
+        ids, pos, slots, seq, last, ctx = [], [], [], [], [], []
+        bs = self.block_size
+        bt = torch.zeros(len(plan.reqs), self.max_blocks, dtype=torch.int32)
+        for i, r in enumerate(plan.reqs):
+            n = len(r.token_ids)
+            ids += r.token_ids
+            ps = list(range(r.start_pos, r.start_pos + n))
+            pos += ps
+            slots += [r.block_table[p // bs] * bs + p % bs for p in ps]
+            seq += [i] * n
+            last.append(len(ids) - 1)
+            ctx.append(r.start_pos + n)
+            bt[i, : len(r.block_table)] = torch.tensor(r.block_table, dtype=torch.int32)
+        dev = self.device
+        t = lambda v, dt=torch.int64: torch.tensor(v, dtype=dt).to(dev, non_blocking=True)  # noqa: E731
+        return StepInput(ids=t(ids), positions=t(pos), slots=t(slots), block_tables=bt.to(dev),
+                         ctx_lens=t(ctx, torch.int32), q_seq=t(seq), logits_idx=t(last), is_decode=False,
+                         max_model_len=self.max_model_len)
+
+    # ---- forward ---------------------------------------------------------------------------------
+    def forward(self, inp: StepInput, hidden=None, residual=None):
+        return self.model.forward(inp, self.caches, hidden, residual)
+
+    def execute(self, plan: StepPlan, hidden=None, residual=None):
+        """Run one step. Last stage: sampled ids (device int64 [n]); other stages: (hidden, residual)."""
+        if plan.is_prefill:
+            return self.forward(self.prefill_input(plan), hidden, residual)
+        n = len(plan.reqs)
+        b = self.stage_decode(plan)
+        if self.use_graphs and self.model.last and self.model.first:
+            g = self.graphs.get(b)
+            if g is None:
+                self._capture(b)
+                g = self.graphs[b]
+            g.replay()
+            return self.graph_out[b][:n]
+        out = self.forward(self._decode_input(b), hidden, residual)
+        if isinstance(out, tuple):
+            return out[0][:n], out[1][:n]
+        return out[:n]
+
+    def _capture(self, b: int) -> None:
+        # warm up on a side stream (allocator and lazily configured kernels), then capture
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        saved = self.d_i64[:, :b].clone(), self.d_bt[:b].clone()
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.forward(self._decode_input(b))
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.d_i64[:, :b].copy_(saved[0])
+        self.d_bt[:b].copy_(saved[1])
+        g = torch.cuda.CUDAGraph()
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g, pool=self._pool):
+            out = self.forward(self._decode_input(b))
+        self.graphs[b] = g
+        self.graph_out[b] = out
+
+    def capture_all(self) -> None:
+        if not self.use_graphs:
+            return
+        for b in self.buckets:
+            if b not in self.graphs:
+                self._capture(b)
+
+    # ---- multi-step decode -----------------------------------------------------------------------
+    def decode_loop(self, plan: StepPlan, k: int) -> torch.Tensor:
+        """k decode steps from `plan` without host round trips; returns device ids [k, n].
+
+        Every request's block table must already cover positions start_pos .. start_pos + k - 1.
+        """
+        n = len(plan.reqs)
+        b = self.stage_decode(plan)
+        out = torch.empty(k, n, dtype=torch.int64, device=self.device)
+        if self.use_graphs and b not in self.graphs:
+            self._capture(b)
+        bs = self.block_size
+        for i in range(k):
+            if self.use_graphs:
+                self.graphs[b].replay()
+                ids = self.graph_out[b]
+            else:
+                ids = self.forward(self._decode_input(b))
+            out[i] = ids[:n]
+            if i + 1 < k:
+                self._advance(b, ids, bs)
+        return out
+
+    def _advance(self, b: int, ids: torch.Tensor, bs: int) -> None:
+        ops = self.model.ops
+        if ops.kind == "kernel":
+            ops.C.decode_advance(self.d_i64, ids, self.d_bt, b, bs)
+            return
+        d = self.d_i64
+        live = d[3, :b] > 0
+        d[0, :b] = torch.where(live, ids[:b], d[0, :b])
+        d[1, :b] += live.long()
+        d[3, :b] += live.long()
+        pos = d[1, :b]
+        blk = self.d_bt[:b].gather(1, (pos // bs).clamp(max=self.max_blocks - 1)[:, None].to(torch.int64))[:, 0]
+        d[2, :b] = torch.where(live, blk.long() * bs + pos % bs, torch.full_like(pos, -1))
+
+    def fetch(self, ids: torch.Tensor) -> list[int]:
+        """Device -> pinned host copy of sampled ids, synchronised on the copy's stream."""
+        n = ids.numel()
+        self.h_out[:n].copy_(ids.view(-1), non_blocking=True)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+        return self.h_out[:n].tolist()

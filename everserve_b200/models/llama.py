@@ -1,0 +1,306 @@
+"""The pre-norm decoder (Llama 3, Qwen2, Mixtral) with tensor- and pipeline-parallel sharding.
+
+One instance holds one rank's shard: the layers of its pipeline stage, and within each layer its
+tensor-parallel slice (column-parallel qkv/gate_up, row-parallel o/down whose partial outputs the
+collective sums, vocab-parallel embedding/lm_head). MoE layers shard their experts across the
+tensor-parallel group (expert parallelism over the same ranks).
+
+Weights are random-initialised: each full parameter is drawn from a generator seeded by (seed,
+layer, name) and then sliced, so a rank's shard is the same tensor whoever builds it. A spare that
+takes rank r builds exactly rank r's weights.
+
+Arithmetic goes through an op set (``everserve_b200.ops``): the sm_100a kernels on CUDA, the
+PyTorch reference on CPU. The row-parallel linears call ``linear_allreduce`` of the tensor-parallel
+group, which is the fused GEMM + all-reduce when the group has one.
+"""
+
+from __future__ import annotations
+
+import hashlib
+from dataclasses import dataclass
+
+import torch
+
+from ..ops import ops_for, ref, softmax_scale
+from .config import ModelConfig
+
+
+@dataclass
+class StepInput:
+    """One forward's inputs (all on the model's device)."""
+
+    ids: torch.Tensor  # [T] int64 token ids (stage 0)
+    positions: torch.Tensor  # [T] int64
+    slots: torch.Tensor  # [T] int64 cache slots (-1 = padding)
+    block_tables: torch.Tensor  # [B, max_blocks] int32
+    ctx_lens: torch.Tensor  # [B] int32: context length after this step's tokens
+    q_seq: torch.Tensor  # [T] int64: sequence index of each row
+    logits_idx: torch.Tensor  # [B] int64: each sequence's last row
+    is_decode: bool
+    max_model_len: int = 0
+
+
+def _seed_of(seed: int, *parts) -> int:
+    h = hashlib.sha256(repr((seed,) + parts).encode()).digest()
+    return int.from_bytes(h[:8], "little") & ((1 << 63) - 1)
+
+
+class TPGroup:
+    """Tensor-parallel context of one rank. Size 1 needs no collective."""
+
+    def __init__(self, rank: int = 0, size: int = 1, collective=None):
+        self.rank, self.size, self.collective = rank, size, collective
+
+    def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.size == 1:
+            return t
+        return self.collective.all_reduce(t)
+
+    def linear_allreduce(self, ops, x, w, residual=None):
+        """Row-parallel linear followed by the sum over ranks (fused when the collective has it)."""
+        if self.size == 1:
+            return ops.linear(x, w, residual=residual)
+        fused = getattr(self.collective, "linear_allreduce", None)
+        if fused is not None and ops.kind == "kernel":
+            return fused(ops, x, w, residual)
+        y = self.collective.all_reduce(ops.linear(x, w))
+        if residual is not None:
+            y = (y.float() + residual.float()).to(y.dtype)
+        return y
+
+    def all_gather_rows(self, t: torch.Tensor) -> torch.Tensor:
+        """Concatenate each rank's [*, n] tensor along the last dim (rank order)."""
+        if self.size == 1:
+            return t
+        return self.collective.all_gather(t)
+
+
+class DecoderLM:
+    def __init__(self, cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0,
+                 tp: TPGroup | None = None, layer_range: tuple[int, int] | None = None,
+                 init: str = "random"):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.seed = seed
+        self.tp = tp or TPGroup()
+        self.ops = ops_for(self.device)
+        self.l0, self.l1 = layer_range or (0, cfg.layers)
+        self.first = self.l0 == 0
+        self.last = self.l1 == cfg.layers
+        T, r = self.tp.size, self.tp.rank
+        assert cfg.heads % T == 0, "query heads must divide by the tensor-parallel size"
+        self.hq = cfg.heads // T
+        if cfg.kv_heads >= T:
+            assert cfg.kv_heads % T == 0
+            self.hkv = cfg.kv_heads // T
+            self.kv_head0 = r * self.hkv
+        else:  # fewer kv heads than ranks: replicate
+            assert T % cfg.kv_heads == 0
+            self.hkv = 1
+            self.kv_head0 = r * cfg.kv_heads // T
+        self.d = cfg.head_dim
+        self.scale = softmax_scale(cfg.head_dim)
+        if cfg.is_moe:
+            assert cfg.num_experts % T == 0, "experts must divide by the expert-parallel size"
+            self.experts_local = cfg.num_experts // T
+            self.expert0 = r * self.experts_local
+            self.inter = cfg.intermediate
+        else:
+            assert cfg.intermediate % T == 0
+            self.inter = cfg.intermediate // T
+        self.vocab_local = (cfg.vocab + T - 1) // T
+        self.vocab0 = r * self.vocab_local
+        self.cos_sin = ref.cos_sin_table(cfg.head_dim, cfg.max_position, cfg.rope_theta, cfg.rope_scaling).to(self.device)
+        self.weights: dict[str, torch.Tensor] = {}
+        if init == "random":
+            self._init_random()
+
+    # ---- weights -----------------------------------------------------------------------------
+    def _rand(self, name: str, layer: int, shape, std: float = 0.02) -> torch.Tensor:
+        gen_dev = self.device if self.device.type == "cuda" else torch.device("cpu")
+        g = torch.Generator(device=gen_dev)
+        g.manual_seed(_seed_of(self.seed, layer, name))
+        t = torch.randn(*shape, generator=g, device=gen_dev, dtype=torch.float32) * std
+        return t
+
+    def _put(self, key: str, t: torch.Tensor):
+        self.weights[key] = t.to(device=self.device, dtype=self.dtype).contiguous()
+
+    def _init_random(self):
+        c, d = self.cfg, self.cfg.head_dim
+        H = c.hidden
+        qs = slice(self.tp.rank * self.hq * d, (self.tp.rank + 1) * self.hq * d)
+        ks = slice(self.kv_head0 * d, (self.kv_head0 + self.hkv) * d)
+        ones = torch.ones(H)
+        if self.first or (self.last and c.tie_embeddings):
+            emb = self._rand("embed", -1, (c.vocab, H))
+            self._put("embed", self._vocab_slice(emb))
+        for l in range(self.l0, self.l1):
+            p = f"l{l}."
+            q = self._rand("q", l, (c.heads * d, H))[qs]
+            k = self._rand("k", l, (c.kv_heads * d, H))[ks]
+            v = self._rand("v", l, (c.kv_heads * d, H))[ks]
+            self._put(p + "qkv", torch.cat([q, k, v], 0))
+            if c.qkv_bias:
+                bq = self._rand("bq", l, (c.heads * d,), 0.1)[qs]
+                bk = self._rand("bk", l, (c.kv_heads * d,), 0.1)[ks]
+                bv = self._rand("bv", l, (c.kv_heads * d,), 0.1)[ks]
+                self._put(p + "qkv_bias", torch.cat([bq, bk, bv]))
+            self._put(p + "o", self._rand("o", l, (H, c.heads * d))[:, qs])
+            self._put(p + "in_norm", ones)
+            self._put(p + "post_norm", ones)
+            if c.is_moe:
+                self._put(p + "router", self._rand("router", l, (c.num_experts, H)))
+                for e in range(self.expert0, self.expert0 + self.experts_local):
+                    g_ = self._rand(f"gate{e}", l, (c.intermediate, H))
+                    u_ = self._rand(f"up{e}", l, (c.intermediate, H))
+                    self._put(p + f"e{e}.gate_up", torch.cat([g_, u_], 0))
+                    self._put(p + f"e{e}.down", self._rand(f"down{e}", l, (H, c.intermediate)))
+            else:
+                ms = slice(self.tp.rank * self.inter, (self.tp.rank + 1) * self.inter)
+                g_ = self._rand("gate", l, (c.intermediate, H))[ms]
+                u_ = self._rand("up", l, (c.intermediate, H))[ms]
+                self._put(p + "gate_up", torch.cat([g_, u_], 0))
+                self._put(p + "down", self._rand("down", l, (H, c.intermediate))[:, ms])
+        if self.last:
+            self._put("final_norm", ones)
+            if not c.tie_embeddings:
+                self._put("lm_head", self._vocab_slice(self._rand("lm_head", -1, (c.vocab, H))))
+
+    def _vocab_slice(self, t: torch.Tensor) -> torch.Tensor:
+        s = t[self.vocab0 : self.vocab0 + self.vocab_local]
+        if s.shape[0] < self.vocab_local:  # pad the last shard
+            s = torch.cat([s, torch.zeros(self.vocab_local - s.shape[0], t.shape[1], device=t.device, dtype=t.dtype)])
+        return s
+
+    def linear_shapes(self) -> list[tuple[int, int]]:
+        """(N, K) of every weight the forward multiplies by, for scratch sizing."""
+        out = set()
+        for k, w in self.weights.items():
+            if w.dim() == 2 and k not in ("embed",):
+                out.add((w.shape[0], w.shape[1]))
+        if "embed" in self.weights and self.last and self.cfg.tie_embeddings:
+            out.add(tuple(self.weights["embed"].shape))
+        return sorted(out)
+
+    # ---- KV cache ------------------------------------------------------------------------------
+    def kv_cache_shape(self, num_blocks: int, block_size: int) -> tuple[int, ...]:
+        return (num_blocks, 2, self.hkv, block_size, self.d)
+
+    def bytes_per_block(self, block_size: int) -> int:
+        return 2 * self.hkv * block_size * self.d * torch.tensor([], dtype=self.dtype).element_size() * (self.l1 - self.l0)
+
+    # ---- forward -------------------------------------------------------------------------------
+    def embed(self, ids: torch.Tensor) -> torch.Tensor:
+        ops = self.ops
+        if self.tp.size == 1:
+            return ops.embed(ids, self.weights["embed"])
+        # vocab-parallel: each rank looks up the ids in its slice, the sum over ranks fills the rest
+        local = ids - self.vocab0
+        mine = (local >= 0) & (local < self.vocab_local)
+        x = ops.embed(torch.where(mine, local, torch.zeros_like(local)), self.weights["embed"])
+        x = x * mine[:, None].to(x.dtype)
+        return self.tp.all_reduce(x)
+
+    def forward(self, inp: StepInput, caches: list[torch.Tensor], hidden: torch.Tensor | None = None,
+                residual: torch.Tensor | None = None):
+        """Run this stage. Returns (hidden, residual) for a middle stage, next-token ids for the last."""
+        ops, c, W = self.ops, self.cfg, self.weights
+        if self.first:
+            x = self.embed(inp.ids)
+            residual = x
+            h = ops.rmsnorm(x, W[f"l{self.l0}.in_norm"], c.rms_eps)
+        else:
+            h = ops.rmsnorm(hidden, W[f"l{self.l0}.in_norm"], c.rms_eps, residual)
+        bs = caches[0].shape[3] if caches else 16
+        for i, l in enumerate(range(self.l0, self.l1)):
+            p = f"l{l}."
+            cache = caches[i]
+            qkv = ops.linear(h, W[p + "qkv"])
+            q = ops.rope_kv_write(qkv, W.get(p + "qkv_bias"), inp.positions, self.cos_sin, inp.slots, cache,
+                                  self.hq, self.hkv, bs)
+            if inp.is_decode:
+                if ops.kind == "kernel":
+                    a = ops.decode_attention(q, cache, inp.block_tables, inp.ctx_lens, self.scale,
+                                             inp.max_model_len or None)
+                else:
+                    a = ops.decode_attention(q, cache, inp.block_tables, inp.ctx_lens, self.scale)
+            else:
+                a = ops.prefill_attention(q, cache, inp.block_tables, inp.ctx_lens, inp.q_seq, inp.positions,
+                                          self.scale)
+            a = a.reshape(a.shape[0], self.hq * self.d)
+            o = self.tp.linear_allreduce(ops, a, W[p + "o"])
+            h = ops.rmsnorm(o, W[p + "post_norm"], c.rms_eps, residual)
+            if c.is_moe:
+                m = self._moe(h, p)
+            else:
+                gu = ops.linear(h, W[p + "gate_up"])
+                act = ops.silu_mul(gu)
+                m = self.tp.linear_allreduce(ops, act, W[p + "down"])
+            nxt = f"l{l + 1}.in_norm" if l + 1 < self.l1 else None
+            if nxt is not None:
+                h = ops.rmsnorm(m, W[nxt], c.rms_eps, residual)
+            else:
+                hidden = m
+        if not self.last:
+            return hidden, residual
+        h = ops.rmsnorm(hidden, W["final_norm"], c.rms_eps, residual)
+        h_last = h.index_select(0, inp.logits_idx) if h.shape[0] != inp.logits_idx.shape[0] else h
+        head = W["embed"] if c.tie_embeddings else W["lm_head"]
+        logits = ops.linear(h_last, head)
+        return self._greedy(logits)
+
+    def logits(self, inp: StepInput, caches, hidden=None, residual=None):
+        """Full-vocab logits of each sequence's last row (tests and the CPU oracle)."""
+        saved = self._greedy
+        out = {}
+
+        def grab(lg):
+            out["l"] = lg
+            return saved(lg)
+
+        self._greedy = grab
+        try:
+            self.forward(inp, caches, hidden, residual)
+        finally:
+            self._greedy = saved
+        lg = out["l"]
+        if self.tp.size > 1:
+            lg = self.tp.all_gather_rows(lg.contiguous())
+        return lg[:, : self.cfg.vocab]
+
+    def _greedy(self, logits: torch.Tensor) -> torch.Tensor:
+        ops = self.ops
+        if self.tp.size == 1:
+            return ops.argmax(logits[:, : self.cfg.vocab] if logits.shape[1] != self.cfg.vocab else logits)
+        # vocab-parallel greedy: local (value, index) pairs, gathered, best value then lowest index
+        idx = ops.argmax(logits)
+        val = logits.gather(1, idx[:, None]).float()
+        valid_n = min(self.vocab_local, self.cfg.vocab - self.vocab0)
+        val = torch.where(idx[:, None] < valid_n, val, torch.full_like(val, float("-inf")))
+        pair = torch.cat([val, (idx + self.vocab0).float()[:, None]], dim=1)  # [B, 2]
+        allp = self.tp.all_gather_rows(pair.contiguous()).view(pair.shape[0], self.tp.size, 2)
+        best = allp[:, :, 0].argmax(dim=1)  # first rank holding the max value = lowest index
+        return allp[torch.arange(pair.shape[0], device=pair.device), best, 1].long()
+
+    # ---- MoE -----------------------------------------------------------------------------------
+    def _moe(self, h: torch.Tensor, p: str) -> torch.Tensor:
+        """Top-k softmax mixture over this rank's experts; the sum over ranks combines them."""
+        ops, c, W = self.ops, self.cfg, self.weights
+        router_logits = ops.linear(h, W[p + "router"]).float()
+        probs = torch.softmax(router_logits, dim=-1)
+        topv, topi = torch.topk(probs, c.top_k, dim=-1)
+        topv = topv / topv.sum(-1, keepdim=True)
+        out = torch.zeros(h.shape[0], c.hidden, dtype=torch.float32, device=h.device)
+        for e in range(self.expert0, self.expert0 + self.experts_local):
+            sel = (topi == e)
+            rows = sel.any(-1).nonzero(as_tuple=True)[0]
+            if rows.numel() == 0:
+                continue
+            wgt = (topv * sel).sum(-1)[rows]
+            xe = h.index_select(0, rows)
+            gu = ops.linear(xe, W[p + f"e{e}.gate_up"])
+            ye = ops.linear(ops.silu_mul(gu), W[p + f"e{e}.down"])
+            out.index_add_(0, rows, ye.float() * wgt[:, None])
+        return self.tp.all_reduce(out.to(h.dtype))

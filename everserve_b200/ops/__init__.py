@@ -1,0 +1,203 @@
+"""Decoder ops: the sm_100a kernels for CUDA tensors, the PyTorch reference for CPU tensors.
+
+``ops_for(device)`` returns the op set a model runs with. :class:`KernelOps` calls only the
+compiled kernels (it raises if the extension is missing) and owns their scratch memory: the
+split-K workspace and tile counters of the GEMM, the split-KV partials of decode attention and a
+status word that bounded waits set. :class:`RefOps` is the CPU engine's arithmetic.
+"""
+
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from . import ref
+from .. import _ext
+
+__all__ = ["KernelOps", "RefOps", "ops_for", "ref"]
+
+
+class RefOps:
+    """PyTorch reference ops (CPU engine, fp32)."""
+
+    kind = "ref"
+
+    def __init__(self, device: torch.device | str = "cpu"):
+        self.device = torch.device(device)
+
+    def embed(self, ids, table):
+        return table[ids]
+
+    def rmsnorm(self, x, w, eps, residual=None):
+        return ref.rmsnorm(x, w, eps, residual)
+
+    def linear(self, x, w, bias=None, residual=None):
+        return ref.linear(x, w, bias, residual)
+
+    def rope_kv_write(self, qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size):
+        return ref.rope_kv_write(qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size)
+
+    def decode_attention(self, q, cache, block_tables, ctx_lens, scale):
+        B = q.shape[0]
+        seq = torch.arange(B, device=q.device)
+        return ref.paged_attention(q, cache, block_tables, ctx_lens, seq, ctx_lens.long() - 1, scale)
+
+    def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale):
+        return ref.paged_attention(q, cache, block_tables, ctx_lens, q_seq, q_pos, scale)
+
+    def silu_mul(self, gu):
+        return ref.silu_mul(gu)
+
+    def argmax(self, logits):
+        return ref.argmax(logits)
+
+    def check_status(self):
+        return 0
+
+
+class KernelOps:
+    """The sm_100a kernels on one CUDA device, with their scratch memory."""
+
+    kind = "kernel"
+    PART_TOKENS = 256  # positions per decode-attention split (fixed: batch-invariant results)
+    SPLITK_MAX_M = 256  # split-K only for decode-sized token counts
+
+    def __init__(self, device: torch.device | str):
+        self.device = torch.device(device)
+        assert self.device.type == "cuda", "KernelOps runs on CUDA devices"
+        self.C = _ext.load()
+        props = torch.cuda.get_device_properties(self.device)
+        self.num_sms = props.multi_processor_count
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._ws = torch.empty(0, dtype=torch.float32, device=self.device)
+        self._ctr = torch.zeros(0, dtype=torch.int32, device=self.device)
+        self._part_o = torch.empty(0, dtype=torch.float32, device=self.device)
+        self._part_ml = torch.empty(0, dtype=torch.float32, device=self.device)
+        self._splits: dict[tuple[int, int], int] = {}
+        self._lock = threading.Lock()
+
+    # ---- scratch ------------------------------------------------------------------------------
+    def splits_for(self, M: int, N: int, K: int) -> int:
+        if M > self.SPLITK_MAX_M:
+            return 1
+        key = (N, K)
+        s = self._splits.get(key)
+        if s is None:
+            s = int(self.C.gemm_pick_splits(N, K, self.num_sms))
+            self._splits[key] = s
+        return s
+
+    def _ensure(self, name: str, numel: int, dtype, zero: bool = False) -> torch.Tensor:
+        buf = getattr(self, name)
+        if buf.numel() >= numel:
+            return buf
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(f"{name} scratch must be reserved before CUDA graph capture ({numel} elements)")
+        new = (torch.zeros if zero else torch.empty)(max(numel, 1), dtype=dtype, device=self.device)
+        setattr(self, name, new)
+        return new
+
+    def reserve_linear(self, max_m: int, shapes: list[tuple[int, int]]):
+        """Size the GEMM scratch for every (N, K) weight at up to max_m tokens."""
+        ws = ctr = 0
+        for m in sorted({min(max_m, self.SPLITK_MAX_M), max_m}):
+            for n, k in shapes:
+                s = self.splits_for(m, n, k)
+                if s > 1:
+                    ws = max(ws, s * m * n)
+                    ctr = max(ctr, int(self.C.gemm_tiles(m, n)))
+        self._ensure("_ws", ws, torch.float32)
+        self._ensure("_ctr", ctr, torch.int32, zero=True)
+
+    def max_splits(self, max_model_len: int) -> int:
+        return max(1, (max_model_len + self.PART_TOKENS - 1) // self.PART_TOKENS)
+
+    def reserve_attention(self, max_batch: int, hq: int, d: int, max_model_len: int):
+        ms = self.max_splits(max_model_len)
+        self._ensure("_part_o", max_batch * hq * ms * d, torch.float32)
+        self._ensure("_part_ml", max_batch * hq * ms * 2, torch.float32)
+
+    # ---- ops ----------------------------------------------------------------------------------
+    def embed(self, ids, table):
+        out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device)
+        self.C.embed(ids, table, out)
+        return out
+
+    def rmsnorm(self, x, w, eps, residual=None):
+        y = torch.empty_like(x)
+        self.C.rmsnorm(x, residual, w, y, eps)
+        return y
+
+    def linear(self, x, w, bias=None, residual=None, out=None):
+        M, K = x.shape
+        N = w.shape[0]
+        if out is None:
+            out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+        s = self.splits_for(M, N, K)
+        if s > 1:
+            self._ensure("_ws", s * M * N, torch.float32)
+            self._ensure("_ctr", int(self.C.gemm_tiles(M, N)), torch.int32, zero=True)
+        if bias is not None:
+            # bias folds into the residual input of the epilogue
+            b = bias.expand(M, N) if residual is None else residual + bias
+            residual = b.contiguous()
+        self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, s)
+        return out
+
+    def rope_kv_write(self, qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size):
+        T = qkv.shape[0]
+        d = cos_sin.shape[1]
+        q = torch.empty(T, hq, d, dtype=qkv.dtype, device=qkv.device)
+        self.C.rope_kv_write(qkv, bias, positions, cos_sin, slots, q, cache, hq, hkv, block_size,
+                             list(cache.stride()[i] for i in (0, 3, 2, 1, 4)))
+        return q
+
+    def decode_attention(self, q, cache, block_tables, ctx_lens, scale, max_model_len=None):
+        B, hq, d = q.shape
+        bs = cache.shape[3]
+        if max_model_len is None:
+            max_model_len = block_tables.shape[1] * bs
+        ms = self.max_splits(max_model_len)
+        self.reserve_attention(B, hq, d, max_model_len)
+        out = torch.empty(B, hq, d, dtype=q.dtype, device=q.device)
+        self.C.paged_decode(q, cache, block_tables, ctx_lens, out, self._part_o, self._part_ml, self.status,
+                            ms, self.PART_TOKENS, scale)
+        return out
+
+    def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale):
+        # prefill runs once per request and is outside the decode loop; reference math on device
+        return ref.paged_attention(q, cache, block_tables, ctx_lens, q_seq, q_pos, scale)
+
+    def silu_mul(self, gu):
+        out = torch.empty(*gu.shape[:-1], gu.shape[-1] // 2, dtype=gu.dtype, device=gu.device)
+        self.C.silu_mul(gu, out)
+        return out
+
+    def argmax(self, logits):
+        out = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+        self.C.argmax(logits, out)
+        return out
+
+    def check_status(self) -> int:
+        """Read (and clear) the status word that bounded waits set; non-zero means a timeout."""
+        v = int(self.status.item())
+        if v:
+            self.status.zero_()
+        return v
+
+
+_CACHE: dict[str, object] = {}
+
+
+def ops_for(device: torch.device | str):
+    dev = torch.device(device)
+    key = str(dev)
+    if key not in _CACHE:
+        _CACHE[key] = KernelOps(dev) if dev.type == "cuda" else RefOps(dev)
+    return _CACHE[key]
+
+
+def softmax_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

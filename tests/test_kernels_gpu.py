@@ -1,0 +1,207 @@
+"""Numerics of the sm_100a kernels against fp32 PyTorch references of the same ops."""
+
+import math
+
+import pytest
+import torch
+
+from everserve_b200 import _ext
+from everserve_b200.ops import KernelOps, ref
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def kops():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return KernelOps("cuda:0")
+
+
+def close(a, b, rtol=2e-2, atol=2e-2):
+    torch.testing.assert_close(a.float(), b.float(), rtol=rtol, atol=atol)
+
+
+def test_extension_is_native():
+    C = _ext.load()
+    assert C.__file__.endswith(".so")
+
+
+@pytest.mark.parametrize("hidden", [256, 896, 4096, 8192])
+@pytest.mark.parametrize("rows", [1, 7, 64])
+def test_rmsnorm(kops, hidden, rows):
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(rows, hidden, device="cuda", generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(hidden, device="cuda", generator=g)).bfloat16()
+    y = kops.rmsnorm(x, w, 1e-5)
+    close(y, ref.rmsnorm(x.float(), w.float(), 1e-5))
+    r = torch.randn(rows, hidden, device="cuda", generator=g).bfloat16()
+    r_ref = r.clone()
+    y2 = kops.rmsnorm(x, w, 1e-5, residual=r)
+    expect_r = (x.float() + r_ref.float()).bfloat16()
+    assert torch.equal(r, expect_r)
+    close(y2, ref.rmsnorm(expect_r.float(), w.float(), 1e-5))
+
+
+@pytest.mark.parametrize("hq,hkv,d,bias", [(32, 8, 128, False), (14, 2, 64, True), (4, 1, 128, False)])
+def test_rope_kv_write(kops, hq, hkv, d, bias):
+    T, bs, nb = 37, 16, 8
+    g = torch.Generator(device="cuda").manual_seed(1)
+    qkv = torch.randn(T, (hq + 2 * hkv) * d, device="cuda", generator=g).bfloat16()
+    b = torch.randn((hq + 2 * hkv) * d, device="cuda", generator=g).bfloat16() if bias else None
+    cs = ref.cos_sin_table(d, 4096, 5e5).cuda()
+    pos = torch.randint(0, 4000, (T,), device="cuda", generator=g)
+    slots = torch.randperm(nb * bs, device="cuda", generator=g)[:T]
+    slots[3] = -1
+    cache = torch.zeros(nb, 2, hkv, bs, d, device="cuda", dtype=torch.bfloat16)
+    cache_ref = cache.clone().float()
+    q = kops.rope_kv_write(qkv, b, pos, cs, slots, cache, hq, hkv, bs)
+    q_ref = ref.rope_kv_write(qkv.float(), None if b is None else b.float(), pos, cs, slots, cache_ref, hq, hkv, bs)
+    close(q, q_ref)
+    close(cache, cache_ref)
+
+
+def test_silu_mul_embed_argmax(kops):
+    g = torch.Generator(device="cuda").manual_seed(2)
+    gu = torch.randn(19, 2 * 1024, device="cuda", generator=g).bfloat16()
+    close(kops.silu_mul(gu), ref.silu_mul(gu.float()))
+    table = torch.randn(1000, 256, device="cuda", generator=g).bfloat16()
+    ids = torch.randint(0, 1000, (33,), device="cuda", generator=g)
+    assert torch.equal(kops.embed(ids, table), table[ids])
+    logits = torch.randn(9, 128256, device="cuda", generator=g).bfloat16()
+    logits[2, 5] = 100.0
+    logits[2, 7] = 100.0  # tie: the lower index wins
+    am = kops.argmax(logits)
+    assert torch.equal(am, torch.argmax(logits.float(), dim=-1))
+    assert am[2].item() == 5
+    odd = torch.randn(3, 1001, device="cuda", generator=g).bfloat16()
+    assert torch.equal(kops.argmax(odd), torch.argmax(odd.float(), dim=-1))
+
+
+GEMM_SHAPES = [
+    (1, 128, 64), (7, 200, 256), (16, 4096, 4096), (33, 6144, 4096), (64, 4096, 14336),
+    (64, 28672, 4096), (100, 512, 1024), (256, 1024, 512), (300, 768, 4096), (1000, 4096, 896),
+    (64, 4096, 512), (64, 1000, 1792), (5, 384, 4104),
+]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm(kops, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
+    y = kops.linear(x, w)
+    expect = x.float() @ w.float().t()
+    close(y, expect, rtol=2e-2, atol=2e-2)
+    assert kops.check_status() == 0
+
+
+def test_gemm_residual_and_splits(kops):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    M, N, K = 48, 4096, 4096
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) / 64).bfloat16()
+    r = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    y = kops.linear(x, w, residual=r)
+    close(y, x.float() @ w.float().t() + r.float())
+    # explicit split counts agree with the unsplit product
+    C = kops.C
+    out1 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm_bf16(x, w, out1, None, kops._ws, kops._ctr, kops.status, 1)
+    for s in (2, 4, 8):
+        kops._ensure("_ws", s * M * N, torch.float32)
+        out = torch.empty_like(out1)
+        C.gemm_bf16(x, w, out, None, kops._ws, kops._ctr, kops.status, s)
+        close(out, out1, rtol=1e-2, atol=1e-2)
+        # the same split count twice gives the same bits
+        out_b = torch.empty_like(out1)
+        C.gemm_bf16(x, w, out_b, None, kops._ws, kops._ctr, kops.status, s)
+        assert torch.equal(out, out_b)
+
+
+def test_gemm_batch_invariant(kops):
+    """A row's result does not depend on the other rows of the batch (exact replay needs this)."""
+    g = torch.Generator(device="cuda").manual_seed(4)
+    N, K = 4096, 4096
+    w = (torch.randn(N, K, device="cuda", generator=g) / 64).bfloat16()
+    x = torch.randn(64, K, device="cuda", generator=g).bfloat16()
+    full = kops.linear(x, w)
+    for m in (1, 3, 17, 40):
+        part = kops.linear(x[:m].contiguous(), w)
+        assert torch.equal(part, full[:m]), f"rows differ at M={m}"
+
+
+@pytest.mark.parametrize("hq,hkv,d,bs", [(32, 8, 128, 16), (4, 1, 128, 16), (14, 2, 64, 16), (64, 8, 128, 32),
+                                         (8, 8, 64, 32)])
+def test_paged_decode(kops, hq, hkv, d, bs):
+    g = torch.Generator(device="cuda").manual_seed(5)
+    lens = [1, 15, 16, 17, 64, 255, 256, 257, 700, 1029]
+    B = len(lens)
+    max_len = 1100
+    mb = (max_len + bs - 1) // bs
+    nb = B * mb + 3
+    cache = torch.randn(nb, 2, hkv, bs, d, device="cuda", generator=g).bfloat16()
+    perm = torch.randperm(nb, device="cuda", generator=g)[: B * mb].view(B, mb).int()
+    ctx = torch.tensor(lens, device="cuda", dtype=torch.int32)
+    q = torch.randn(B, hq, d, device="cuda", generator=g).bfloat16()
+    scale = 1 / math.sqrt(d)
+    out = kops.decode_attention(q, cache, perm, ctx, scale, max_len)
+    seq = torch.arange(B, device="cuda")
+    expect = ref.paged_attention(q.float(), cache.float(), perm, ctx, seq, ctx.long() - 1, scale)
+    close(out, expect, rtol=2e-2, atol=2e-2)
+    assert kops.check_status() == 0
+    # batch invariance: one sequence alone gives the same bits
+    one = kops.decode_attention(q[7:8].contiguous(), cache, perm[7:8].contiguous(), ctx[7:8].contiguous(), scale,
+                                max_len)
+    assert torch.equal(one, out[7:8])
+
+
+def test_kv_gather_scatter(kops):
+    C = kops.C
+    g = torch.Generator(device="cuda").manual_seed(6)
+    L, nb, hkv, bs, d = 3, 10, 4, 16, 128
+    caches = [torch.randn(nb, 2, hkv, bs, d, device="cuda", generator=g).bfloat16() for _ in range(L)]
+    ptrs = torch.tensor([c.data_ptr() for c in caches], device="cuda", dtype=torch.int64)
+    slots = torch.tensor([5, 17, -1, 100, 159], device="cuda")
+    heads = torch.tensor([1, 3], device="cuda")
+    cap = 8
+    staging = torch.full((L, 2, cap, 2, d), 7.0, device="cuda").bfloat16()
+    strides = [caches[0].stride(i) for i in (0, 3, 2, 1, 4)]
+    C.kv_gather(ptrs, slots, heads, staging.data_ptr(), cap, d, bs, strides, 2)
+    for l in range(L):
+        for hi, h in enumerate([1, 3]):
+            for t, s in enumerate(slots.tolist()):
+                if s < 0:
+                    assert torch.count_nonzero(staging[l, hi, t]) == 0
+                    continue
+                assert torch.equal(staging[l, hi, t, 0], caches[l][s // bs, 0, h, s % bs])
+                assert torch.equal(staging[l, hi, t, 1], caches[l][s // bs, 1, h, s % bs])
+    # scatter into zeroed caches restores exactly those rows
+    fresh = [torch.zeros_like(c) for c in caches]
+    ptrs2 = torch.tensor([c.data_ptr() for c in fresh], device="cuda", dtype=torch.int64)
+    C.kv_scatter(ptrs2, slots, heads, staging.data_ptr(), cap, d, bs, strides, 2)
+    for l in range(L):
+        for h in (1, 3):
+            for s in slots.tolist():
+                if s >= 0:
+                    assert torch.equal(fresh[l][s // bs, :, h, s % bs], caches[l][s // bs, :, h, s % bs])
+        assert torch.count_nonzero(fresh[l][:, :, 0]) == 0
+
+
+def test_kv_gather_to_mapped_host(kops):
+    """The gather writes straight into pinned, device-mapped host memory (the store's rows)."""
+    C = kops.C
+    L, nb, hkv, bs, d, cap = 2, 4, 2, 16, 64, 4
+    caches = [torch.randn(nb, 2, hkv, bs, d, device="cuda").bfloat16() for _ in range(L)]
+    ptrs = torch.tensor([c.data_ptr() for c in caches], device="cuda", dtype=torch.int64)
+    host = torch.zeros(L * hkv * cap * 2 * d, dtype=torch.bfloat16)
+    dev_ptr = C.host_register_mapped(host.data_ptr(), host.numel() * 2)
+    try:
+        slots = torch.tensor([0, 33, 63], device="cuda")
+        heads = torch.arange(hkv, device="cuda")
+        C.kv_gather(ptrs, slots, heads, dev_ptr, cap, d, bs, [caches[0].stride(i) for i in (0, 3, 2, 1, 4)], 2)
+        torch.cuda.synchronize()
+        view = host.view(L, hkv, cap, 2, d)
+        assert torch.equal(view[1, 1, 1, 0], caches[1][33 // bs, 0, 1, 33 % bs].cpu())
+    finally:
+        C.host_unregister(host.data_ptr())
