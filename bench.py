@@ -159,8 +159,12 @@ def main() -> None:
     for p in prompts:
         eng.add_request(p, SamplingParams(max_tokens=args.max_tokens))
     # prefill everything (untimed)
+    t_pf = time.perf_counter()
     while eng.scheduler.waiting:
         eng.step()
+    torch.cuda.synchronize()
+    print(f"[bench] prefill of {args.batch}x{args.prompt_len} tokens: {time.perf_counter() - t_pf:.2f} s",
+          file=sys.stderr)
     runner = ex.worker.runner
     for _ in range(args.warmup):
         eng.step()

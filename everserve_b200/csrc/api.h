@@ -29,15 +29,16 @@ struct GemmArgs {
   const void* w;  // [N, K] bf16, row stride ldw
   void* out;      // [M, N] bf16, row stride ldo
   const void* residual;  // optional [M, N] bf16, row stride ldr
-  float* ws;             // split-K partials [splits, M, N] (splits > 1)
-  int* counters;         // one per output tile, zero before first use (splits > 1)
+  float* ws;             // unused (split-K partials live in cluster shared memory)
+  uint32_t* sync;        // unused
   int* status;           // set non-zero if a bounded wait ran out
   int64_t M, N, K, ldx, ldw, ldo, ldr;
-  int splits;
+  int num_sms;           // SMs of the device (sizes the split-K clusters)
 };
 int64_t gemm_pick_bn(int64_t M);
-int64_t gemm_pick_splits(int64_t N, int64_t K, int64_t num_sms);
-int64_t gemm_tiles(int64_t M, int64_t N);  // output tiles (n tiles x m tiles) for counters
+int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms);
+int64_t gemm_ws_floats(int64_t num_sms);
+int64_t gemm_sync_words(int64_t num_sms);
 cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t s);
 
 // ---- attention.cu --------------------------------------------------------------------------------
@@ -55,6 +56,8 @@ struct DecodeArgs {
   float* part_ml;
   int* status;
   int B, hq, hkv, d, block_size, max_splits, part_tokens;
+  int64_t num_blocks;
+  int stages;  // K/V ring depth (2..4)
   float scale;
 };
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t s);

@@ -1,30 +1,33 @@
 // Paged attention for decode: one query token per sequence against its paged K/V history.
 //
 // Cache layout (one layer): [num_blocks, 2 (k, v), kv_heads, block_size, head_dim] bf16, so the
-// K (or V) rows of one (block, kv head) are one contiguous run of block_size * head_dim * 2 bytes.
-// A CTA owns one (sequence, kv head, split of part_tokens positions) and serves the G query heads
-// that share the kv head (GQA). One thread issues one-dimensional bulk async copies of whole
-// blocks into a 3-stage shared-memory ring (mbarrier completion), so a CTA keeps ~64 KB of K/V in
-// flight with a handful of instructions; 128 threads compute q.k, an online softmax and p.v out of
-// shared memory. Each split writes (o / l, m, l) and a second kernel merges the splits in split
-// order. The split length is fixed, so a sequence's result never depends on the batch around it.
+// K (or V) rows of one (block, kv head) are one contiguous tile of block_size * head_dim * 2 bytes.
+// A CTA owns one (sequence, kv head, split of part_tokens positions) and serves the G <= 8 query
+// heads that share the kv head (GQA). Thread 0 streams whole K and V tiles into a 3-stage shared
+// ring with TMA (128-byte swizzle, so the tensor-core fragment loads below are bank-conflict free);
+// each of the 4 warps takes one block of every stage and computes S = q.K^T and O += P.V with
+// mma.sync m16n8k16 (the G query heads padded to 16 rows: decode attention is memory-bound, the
+// tensor cores only remove the SIMT arithmetic from the critical path), keeping its own online
+// softmax state. The warps merge at the end, each split writes (o / l, m, l), and a second kernel
+// merges the splits in split order. The split length is fixed per engine, so a sequence's result
+// never depends on the batch around it.
+#include <cuda.h>
+
 #include "api.h"
 #include "common.cuh"
 #include "ptx.cuh"
+#include "tmap.h"
 
 namespace es {
 namespace attn {
 
 constexpr int kThreads = 128;
-constexpr int kChunk = 64;   // positions per pipeline stage
-constexpr int kStages = 3;
+constexpr int kWarps = 4;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeParams {
   const __nv_bfloat16* q;  // [B, Hq, D] rows of q_stride elements
   int64_t q_stride;
-  const __nv_bfloat16* cache;
-  int64_t s_block, s_kv;  // element strides of the cache layout
   const int* block_tables;
   int bt_stride;
   const int* ctx_lens;
@@ -35,201 +38,203 @@ struct DecodeParams {
   int* status;
 };
 
-template <int G, int D, int BS>
+template <int D, int BS, int kStages>
 struct DecodeCfg {
-  static constexpr int DPT = (D == 128 && G <= 4) ? 16 : 8;  // dims per thread in q.k
-  static constexpr int TPT = D / DPT;                         // threads per position in q.k
-  static constexpr int TOK = kThreads / TPT;                  // positions per q.k pass
-  static constexpr int VPT = DPT / 8;                         // uint4 per thread per position
-  static constexpr int DT = D / 8;                            // threads per row in p.v
-  static constexpr int TL = kThreads / DT;                    // position lanes in p.v
-  static constexpr int CB = kChunk / BS;                      // blocks per stage
-  static constexpr int kTileElems = kChunk * D;
-  static constexpr size_t kSmem = 2ull * kStages * kTileElems * 2       // K and V rings
-                                  + (size_t)G * D * 4                    // q (fp32, prescaled)
-                                  + (size_t)G * kChunk * 4               // logits / probabilities
-                                  + 3ull * 8 * 4                         // running m, l, rescale
-                                  + kStages * 8 + 16;                    // mbarriers
-  static_assert((size_t)TL * G * D * 4 <= 2ull * kStages * kTileElems * 2, "reduction buffer fits the rings");
-  static_assert(kChunk % BS == 0 && kChunk % TOK == 0, "chunk shape");
+  static constexpr int kTileBytes = BS * D * 2;             // one (block, kv head) of K or V
+  static constexpr int kStageBytes = kWarps * 2 * kTileBytes;
+  static constexpr int kRowsPerTok = D / 64;                 // 128-byte TMA rows per position
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 128;
+  static_assert(kWarps * 8 * D * 4 + kWarps * 8 * 2 * 4 <= kStages * kStageBytes, "merge buffer fits the ring");
 };
 
-template <int G, int D, int BS>
-__global__ void __launch_bounds__(kThreads) decode_kernel(DecodeParams p) {
-  using C = DecodeCfg<G, D, BS>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  __nv_bfloat16* kbuf = reinterpret_cast<__nv_bfloat16*>(smem);
-  __nv_bfloat16* vbuf = kbuf + kStages * C::kTileElems;
-  float* qs = reinterpret_cast<float*>(vbuf + kStages * C::kTileElems);
-  float* lg = qs + G * D;
-  float* mrun = lg + G * kChunk;
-  float* lrun = mrun + 8;
-  float* scl = lrun + 8;
-  uint64_t* full = reinterpret_cast<uint64_t*>(scl + 8);
-  float* red = reinterpret_cast<float*>(smem);  // aliases the rings once they are drained
+// byte offset of element (t, d) of a K/V tile written by TMA with 128-byte swizzle
+template <int D>
+ES_DEVICE uint32_t swz(int t, int d) {
+  const int hr = t * (D / 64) + (d >> 6);
+  const int chunk = (d & 63) >> 3;
+  return (uint32_t)(hr * 128 + ((chunk ^ (hr & 7)) << 4) + (d & 7) * 2);
+}
+
+template <int D, int BS, int kStages>
+__global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ CUtensorMap cmap, DecodeParams p) {
+  using C = DecodeCfg<D, BS, kStages>;
+  constexpr int NT = D / 8;  // n-tiles of the output
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * C::kStageBytes);
 
   const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int ctx = p.ctx_lens[b];
   const int s0 = split * p.part_tokens;
   if (s0 >= ctx) return;
   const int s1 = min(ctx, s0 + p.part_tokens);
-  const int nchunks = (s1 - s0 + kChunk - 1) / kChunk;
+  const int blk0 = s0 / BS, blk1 = (s1 + BS - 1) / BS;
+  const int nchunks = (blk1 - blk0 + kWarps - 1) / kWarps;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int G = p.hq / p.hkv;
   const int* bt = p.block_tables + (size_t)b * p.bt_stride;
-  const size_t head_off = (size_t)kvh * BS * D;
 
   if (tid == 0) {
+    ptx::prefetch_tmap(&cmap);
     for (int s = 0; s < kStages; s++) ptx::mbar_init(&full[s], 1);
     ptx::fence_mbar_init();
-  }
-  // q of the G heads, fp32, prescaled so the softmax runs in base 2
-  for (int i = tid; i < G * D; i += kThreads) {
-    const int g = i / D, e = i % D;
-    qs[i] = bf2f(p.q[(size_t)b * p.q_stride + (size_t)(kvh * G + g) * D + e]) * p.scale_log2;
-  }
-  if (tid < G) {
-    mrun[tid] = -INFINITY;
-    lrun[tid] = 0.f;
   }
   __syncthreads();
 
   auto issue = [&](int c) {
-    const int t0 = s0 + c * kChunk;
-    const int t1 = min(s1, t0 + kChunk);
-    const int blk0 = t0 / BS;
-    const int nblk = (t1 + BS - 1) / BS - blk0;
     const int st = c % kStages;
-    constexpr uint32_t kBlockBytes = BS * D * 2;
-    ptx::mbar_arrive_expect_tx(&full[st], 2u * kBlockBytes * nblk);
-    for (int i = 0; i < nblk; i++) {
-      const int64_t phys = bt[blk0 + i];
-      const __nv_bfloat16* src = p.cache + phys * p.s_block + head_off;
-      ptx::bulk_g2s(kbuf + st * C::kTileElems + i * BS * D, src, kBlockBytes, &full[st]);
-      ptx::bulk_g2s(vbuf + st * C::kTileElems + i * BS * D, src + p.s_kv, kBlockBytes, &full[st]);
+    const int first = blk0 + c * kWarps;
+    const int n = min(kWarps, blk1 - first);
+    ptx::mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * C::kTileBytes * n));
+    for (int i = 0; i < n; i++) {
+      const int64_t phys = bt[first + i];
+      const int row_k = (int)(((phys * 2 + 0) * p.hkv + kvh) * BS * C::kRowsPerTok);
+      const int row_v = (int)(((phys * 2 + 1) * p.hkv + kvh) * BS * C::kRowsPerTok);
+      uint8_t* dst = ring + st * C::kStageBytes + i * 2 * C::kTileBytes;
+      ptx::tma_load_2d(dst, &cmap, 0, row_k, &full[st]);
+      ptx::tma_load_2d(dst + C::kTileBytes, &cmap, 0, row_v, &full[st]);
     }
   };
-
   if (tid == 0) {
     for (int c = 0; c < kStages - 1 && c < nchunks; c++) issue(c);
   }
 
-  // q.k mapping: position group grp, sub-lane sub; the thread's v-th uint4 is row index sub + v*TPT
-  const int grp = tid / C::TPT, sub = tid % C::TPT;
-  float qr[G][C::DPT];
+  // q fragments (rows = the G heads, zero above G; rows 8..15 are always zero)
+  uint32_t qa[D / 16][2];
+  {
+    const __nv_bfloat16* qrow = p.q + (size_t)b * p.q_stride + (size_t)(kvh * G + gid) * D;
 #pragma unroll
-  for (int g = 0; g < G; g++)
+    for (int ks = 0; ks < D / 16; ks++) {
+      if (gid < G) {
+        qa[ks][0] = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + tig * 2);
+        qa[ks][1] = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + tig * 2);
+      } else {
+        qa[ks][0] = qa[ks][1] = 0u;
+      }
+    }
+  }
+  float o[NT][4];
 #pragma unroll
-    for (int v = 0; v < C::VPT; v++)
-#pragma unroll
-      for (int e = 0; e < 8; e++) qr[g][v * 8 + e] = qs[g * D + (sub + v * C::TPT) * 8 + e];
-
-  // p.v mapping: position lane tl, 8-dim column dc
-  const int tl = tid / C::DT, dc = tid % C::DT;
-  float acc[G][8];
-#pragma unroll
-  for (int g = 0; g < G; g++)
-#pragma unroll
-    for (int e = 0; e < 8; e++) acc[g][e] = 0.f;
+  for (int i = 0; i < NT; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // row gid; l is this thread's partial sum
 
   bool failed = false;
   for (int c = 0; c < nchunks; c++) {
     if (tid == 0 && c + kStages - 1 < nchunks) issue(c + kStages - 1);
     const int st = c % kStages;
     const bool ok = ptx::mbar_wait(&full[st], (c / kStages) & 1);
-    if (__syncthreads_or(!ok)) {  // every thread leaves together, so no barrier is left half-met
+    if (__syncthreads_or(!ok)) {
       failed = true;
       break;
     }
-    const int t0 = s0 + c * kChunk;
-    const int nvalid = min(kChunk, s1 - t0);
-    const __nv_bfloat16* kt = kbuf + st * C::kTileElems;
-    const __nv_bfloat16* vt = vbuf + st * C::kTileElems;
-    // q.k
+    const int blk = blk0 + c * kWarps + warp;
+    if (blk < blk1) {
+      const uint32_t kbase = ptx::smem_u32(ring + st * C::kStageBytes + warp * 2 * C::kTileBytes);
+      const uint32_t vbase = kbase + C::kTileBytes;
 #pragma unroll
-    for (int pass = 0; pass < kChunk / C::TOK; pass++) {
-      const int j = pass * C::TOK + grp;
-      float s[G];
+      for (int tb = 0; tb < BS / 16; tb++) {
+        const int tok0 = blk * BS + tb * 16;  // global position of the step's first row
+        // S = q . K^T for 16 positions (two n-tiles of 8)
+        float s[2][4];
 #pragma unroll
-      for (int g = 0; g < G; g++) s[g] = 0.f;
-      if (j < nvalid) {
-        const uint4* row = reinterpret_cast<const uint4*>(kt + j * D);
+        for (int j = 0; j < 2; j++) {
+          s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
 #pragma unroll
-        for (int v = 0; v < C::VPT; v++) {
-          float kf[8];
-          unpack8(row[sub + v * C::TPT], kf);
+          for (int kp = 0; kp < D / 32; kp++) {
+            uint32_t b0, b1, b2, b3;
+            const int t = tb * 16 + j * 8 + (lane & 7);
+            const int d = kp * 32 + (lane >> 3) * 8;
+            ptx::ldmatrix_x4(kbase + swz<D>(t, d), b0, b1, b2, b3);
+            const uint32_t a0[4] = {qa[2 * kp][0], 0u, qa[2 * kp][1], 0u};
+            const uint32_t a1[4] = {qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u};
+            ptx::mma_bf16_16816(s[j], a0, b0, b1);
+            ptx::mma_bf16_16816(s[j], a1, b2, b3);
+          }
+        }
+        // online softmax on row gid (this thread: positions tig*2+{0,1} of each n-tile)
+        float v[4];
+        float mx = -INFINITY;
 #pragma unroll
-          for (int g = 0; g < G; g++)
+        for (int j = 0; j < 2; j++) {
 #pragma unroll
-            for (int e = 0; e < 8; e++) s[g] += qr[g][v * 8 + e] * kf[e];
+          for (int e = 0; e < 2; e++) {
+            const int pos = tok0 + j * 8 + tig * 2 + e;
+            const float x = pos < s1 ? s[j][e] * p.scale_log2 : -INFINITY;
+            v[j * 2 + e] = x;
+            mx = fmaxf(mx, x);
+          }
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const bool none = m_new == -INFINITY;  // no valid position seen yet
+        const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+        float pr[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) pr[i] = none ? 0.f : exp2f(v[i] - m_new);
+        l_run = l_run * alpha + (pr[0] + pr[1] + pr[2] + pr[3]);
+        m_run = m_new;
+#pragma unroll
+        for (int i = 0; i < NT; i++) {
+          o[i][0] *= alpha;
+          o[i][1] *= alpha;
+        }
+        const uint32_t pa[4] = {ptx::pack_bf16x2(pr[0], pr[1]), 0u, ptx::pack_bf16x2(pr[2], pr[3]), 0u};
+        // O += P . V
+#pragma unroll
+        for (int np = 0; np < D / 16; np++) {
+          uint32_t b0, b1, b2, b3;
+          const int mi = lane >> 3;
+          const int t = tb * 16 + (mi & 1) * 8 + (lane & 7);
+          const int d = np * 16 + (mi >> 1) * 8;
+          ptx::ldmatrix_x4_trans(vbase + swz<D>(t, d), b0, b1, b2, b3);
+          ptx::mma_bf16_16816(o[2 * np], pa, b0, b1);
+          ptx::mma_bf16_16816(o[2 * np + 1], pa, b2, b3);
         }
       }
-#pragma unroll
-      for (int g = 0; g < G; g++) {
-#pragma unroll
-        for (int o = C::TPT / 2; o > 0; o >>= 1) s[g] += __shfl_xor_sync(0xffffffffu, s[g], o);
-      }
-      if (sub == 0) {
-#pragma unroll
-        for (int g = 0; g < G; g++) lg[g * kChunk + j] = j < nvalid ? s[g] : -INFINITY;
-      }
     }
-    __syncthreads();
-    // online softmax, one warp per head
-    for (int g = warp; g < G; g += kThreads / 32) {
-      const float a = lg[g * kChunk + lane], bb = lg[g * kChunk + lane + 32];
-      const float mx = warp_max(fmaxf(a, bb));
-      const float mold = mrun[g];
-      const float mnew = fmaxf(mold, mx);
-      const float pa = exp2f(a - mnew), pb = exp2f(bb - mnew);
-      lg[g * kChunk + lane] = pa;
-      lg[g * kChunk + lane + 32] = pb;
-      const float sum = warp_sum(pa + pb);
-      if (lane == 0) {
-        const float f = exp2f(mold - mnew);
-        scl[g] = f;
-        lrun[g] = lrun[g] * f + sum;
-        mrun[g] = mnew;
-      }
-    }
-    __syncthreads();
-    // p.v
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-      const float f = scl[g];
-#pragma unroll
-      for (int e = 0; e < 8; e++) acc[g][e] *= f;
-    }
-    for (int j = tl; j < nvalid; j += C::TL) {
-      float vf[8];
-      unpack8(reinterpret_cast<const uint4*>(vt + j * D)[dc], vf);
-#pragma unroll
-      for (int g = 0; g < G; g++) {
-        const float pj = lg[g * kChunk + j];
-#pragma unroll
-        for (int e = 0; e < 8; e++) acc[g][e] += pj * vf[e];
-      }
-    }
-    __syncthreads();
+    __syncthreads();  // the stage is free for the next issue
   }
   if (failed) {
     if (tid == 0 && p.status) atomicExch(p.status, (int)kTimeout);
     return;
   }
-  // merge the position lanes in lane order
+  // merge the warps: row gid's (m, l, o) of each warp, then combine in warp order
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  float* red_o = reinterpret_cast<float*>(ring);  // [warp][8][D]
+  float* red_ml = red_o + kWarps * 8 * D;         // [warp][8][2]
+  if (gid < G) {
 #pragma unroll
-  for (int g = 0; g < G; g++)
-#pragma unroll
-    for (int e = 0; e < 8; e++) red[(tl * G + g) * D + dc * 8 + e] = acc[g][e];
+    for (int i = 0; i < NT; i++) {
+      red_o[(warp * 8 + gid) * D + i * 8 + tig * 2] = o[i][0];
+      red_o[(warp * 8 + gid) * D + i * 8 + tig * 2 + 1] = o[i][1];
+    }
+    if (tig == 0) {
+      red_ml[(warp * 8 + gid) * 2] = m_run;
+      red_ml[(warp * 8 + gid) * 2 + 1] = l_run;
+    }
+  }
   __syncthreads();
   for (int i = tid; i < G * D; i += kThreads) {
     const int g = i / D, e = i % D;
-    float o = 0.f;
-    for (int l = 0; l < C::TL; l++) o += red[(l * G + g) * D + e];
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) M = fmaxf(M, red_ml[(w * 8 + g) * 2]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) {
+      const float mw = red_ml[(w * 8 + g) * 2];
+      const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+      num += red_o[(w * 8 + g) * D + e] * f;
+      den += red_ml[(w * 8 + g) * 2 + 1] * f;
+    }
     const size_t row = ((size_t)b * p.hq + kvh * G + g) * p.max_splits + split;
-    p.part_o[row * D + e] = o / lrun[g];
+    p.part_o[row * D + e] = num / den;
     if (e == 0) {
-      p.part_ml[row * 2] = mrun[g];
-      p.part_ml[row * 2 + 1] = lrun[g];
+      p.part_ml[row * 2] = M;
+      p.part_ml[row * 2 + 1] = den;
     }
   }
 }
@@ -255,33 +260,26 @@ __global__ void decode_merge_kernel(const float* __restrict__ part_o, const floa
   }
 }
 
-template <int G, int D, int BS>
-cudaError_t launch_decode(const DecodeParams& p, int B, cudaStream_t stream) {
-  using C = DecodeCfg<G, D, BS>;
+template <int D, int BS, int S>
+cudaError_t launch_decode(const CUtensorMap& map, const DecodeParams& p, int B, cudaStream_t stream) {
+  using C = DecodeCfg<D, BS, S>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(decode_kernel<G, D, BS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<D, BS, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) return e;
     configured = true;
   }
   dim3 grid(B, p.hkv, p.max_splits);
-  decode_kernel<G, D, BS><<<grid, kThreads, C::kSmem, stream>>>(p);
+  decode_kernel<D, BS, S><<<grid, kThreads, C::kSmem, stream>>>(map, p);
   return cudaGetLastError();
 }
 
 template <int D, int BS>
-cudaError_t dispatch_g(int G, const DecodeParams& p, int B, cudaStream_t s) {
-  switch (G) {
-    case 1: return launch_decode<1, D, BS>(p, B, s);
-    case 2: return launch_decode<2, D, BS>(p, B, s);
-    case 3: return launch_decode<3, D, BS>(p, B, s);
-    case 4: return launch_decode<4, D, BS>(p, B, s);
-    case 5: return launch_decode<5, D, BS>(p, B, s);
-    case 6: return launch_decode<6, D, BS>(p, B, s);
-    case 7: return launch_decode<7, D, BS>(p, B, s);
-    case 8: return launch_decode<8, D, BS>(p, B, s);
-    default: return cudaErrorInvalidValue;
+cudaError_t launch_stages(int stages, const CUtensorMap& map, const DecodeParams& p, int B, cudaStream_t stream) {
+  switch (stages) {
+    case 2: return launch_decode<D, BS, 2>(map, p, B, stream);
+    case 4: return launch_decode<D, BS, 4>(map, p, B, stream);
+    default: return launch_decode<D, BS, 3>(map, p, B, stream);
   }
 }
 
@@ -289,14 +287,12 @@ cudaError_t dispatch_g(int G, const DecodeParams& p, int B, cudaStream_t s) {
 
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (a.B == 0) return cudaSuccess;
-  if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.part_tokens % attn::kChunk != 0 || a.max_splits <= 0)
+  if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.hq / a.hkv > 8 || a.part_tokens % 64 != 0 || a.max_splits <= 0)
     return cudaErrorInvalidValue;
+  if (a.s_kv != (int64_t)a.hkv * a.block_size * a.d || a.s_block != 2 * a.s_kv) return cudaErrorInvalidValue;
   attn::DecodeParams p{};
   p.q = static_cast<const __nv_bfloat16*>(a.q);
   p.q_stride = a.q_stride;
-  p.cache = static_cast<const __nv_bfloat16*>(a.cache);
-  p.s_block = a.s_block;
-  p.s_kv = a.s_kv;
   p.block_tables = a.block_tables;
   p.bt_stride = (int)a.bt_stride;
   p.ctx_lens = a.ctx_lens;
@@ -308,12 +304,16 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   p.part_tokens = a.part_tokens;
   p.scale_log2 = a.scale * attn::kLog2e;
   p.status = a.status;
-  const int G = a.hq / a.hkv;
-  cudaError_t e;
-  if (a.d == 128 && a.block_size == 16) e = attn::dispatch_g<128, 16>(G, p, a.B, stream);
-  else if (a.d == 64 && a.block_size == 16) e = attn::dispatch_g<64, 16>(G, p, a.B, stream);
-  else if (a.d == 128 && a.block_size == 32) e = attn::dispatch_g<128, 32>(G, p, a.B, stream);
-  else if (a.d == 64 && a.block_size == 32) e = attn::dispatch_g<64, 32>(G, p, a.B, stream);
+  // the layer's cache as rows of 64 elements (128 bytes); one box = one (block, kv head) tile
+  const int64_t rows = a.num_blocks * 2 * a.hkv * a.block_size * (a.d / 64);
+  const int box_rows = a.block_size * (a.d / 64);
+  CUtensorMap map;
+  cudaError_t e = tmap::bf16_2d(&map, const_cast<void*>(a.cache), rows, 64, 64, box_rows, 64);
+  if (e != cudaSuccess) return e;
+  if (a.d == 128 && a.block_size == 16) e = attn::launch_stages<128, 16>(a.stages, map, p, a.B, stream);
+  else if (a.d == 64 && a.block_size == 16) e = attn::launch_stages<64, 16>(a.stages, map, p, a.B, stream);
+  else if (a.d == 128 && a.block_size == 32) e = attn::launch_stages<128, 32>(a.stages, map, p, a.B, stream);
+  else if (a.d == 64 && a.block_size == 32) e = attn::launch_stages<64, 32>(a.stages, map, p, a.B, stream);
   else return cudaErrorInvalidValue;
   if (e != cudaSuccess) return e;
   dim3 mgrid(a.B, a.hq);

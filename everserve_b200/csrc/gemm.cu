@@ -2,18 +2,23 @@
 // in, fp32 accumulate in TMEM, bf16 out.
 //
 // Design (sm_100a):
-//   * swap-AB: the MMA's M side (128 TMEM lanes) runs over the weight rows and its N side over
-//     tokens, so a decode batch of 1..256 tokens fills one MMA without padding the weights;
+//   * swap-AB: the MMA's M side (128 TMEM lanes) runs over weight rows, its N side over tokens,
+//     so a decode batch of 1..256 tokens is one MMA tile without padding the weights;
 //   * one CTA = one 128-row weight slice x one token tile x one K split. Warp 0 lane 0 issues TMA
-//     loads into a STAGES-deep ring of 128-byte-swizzled shared tiles, warp 1 lane 0 issues
-//     tcgen05.mma (128 x BN x 16) into TMEM, all four warps drain TMEM with tcgen05.ld;
-//   * split-K for the decode shapes, whose weight streaming needs every SM: each split writes its
-//     fp32 partial into a workspace and the last CTA of a tile (a device counter) sums the
-//     partials in split order, so the result does not depend on which split finishes last;
-//   * the number of splits depends on (N, K) only, never on the token count: a row of the output is
-//     the same function of its inputs whatever else is in the batch.
+//     loads into a STAGES-deep ring of 128-byte-swizzled tiles, warp 1 lane 0 issues
+//     tcgen05.mma into TMEM, warps 2-5 drain TMEM (tcgen05.ld) in the epilogue;
+//   * split-K for the decode shapes, whose weight streaming needs every SM: the S CTAs that
+//     share a tile form one thread-block cluster. Each writes its fp32 partial into its own
+//     shared memory, a cluster barrier publishes them, and CTA j sums rows [j*128/S, ...) of the
+//     tile over the S partials in rank order through distributed shared memory. No partial
+//     touches global memory and no CTA polls;
+//   * S depends on (N, K, #SMs) only, never on the token count, so a row's result is the same
+//     whatever else is in the batch.
 // Every mbarrier wait is bounded by the global timer; a wait that runs out writes a status word.
 #include <cuda.h>
+
+#include <algorithm>
+#include <cstdlib>
 
 #include "api.h"
 #include "common.cuh"
@@ -25,32 +30,32 @@ namespace gemm {
 
 constexpr int BM = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 64;   // bf16 per k-block: one 128-byte swizzle row
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;
 
+// decode tiles (BN <= 64) run two CTAs per SM so one CTA's start-up and reduction overlap the
+// other's streaming; larger tiles run one CTA per SM with a deeper ring
 template <int BN>
 struct Cfg {
-  static constexpr int kStages = BN <= 64 ? 8 : (BN == 128 ? 6 : 4);
+  static constexpr int kCps = BN <= 64 ? 2 : 1;
+  static constexpr int kStages = BN <= 64 ? 4 : (BN == 128 ? 6 : 4);
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  // tiles + barriers + tmem slot, plus 1 KB so the tile base can be aligned to 1024
   static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+  static_assert(BN * BM * 4 <= kStages * kStageBytes, "the partial tile fits the drained ring");
 };
 
 struct Params {
   __nv_bfloat16* out;
-  const __nv_bfloat16* residual;  // optional, same shape as out
-  float* ws;                      // [splits, M, N] fp32 when splits > 1
-  int* counters;                  // one per (n tile, m tile) when splits > 1
+  const __nv_bfloat16* residual;
   int* status;
-  int M, N, K;
-  int ldo, ldr;
-  int kb_total, kb_per_split, splits;
+  int M, N, ldo, ldr;
+  int kb, splits;
 };
 
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, Cfg<BN>::kCps)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, Params p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -61,16 +66,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + C::kStages;
   uint64_t* done = empty + C::kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  __shared__ int s_last;
+  float* partial = reinterpret_cast<float*>(smem);  // [BN][BM] once the ring is drained
   __shared__ int s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BM;
   const int m0 = blockIdx.y * BN;
+  const int S = p.splits;
   const int split = blockIdx.z;
-  const int kb0 = split * p.kb_per_split;
-  const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
-  const int nkb = kb1 - kb0;
+  const int kps = (p.kb + S - 1) / S;
+  const int kb0 = split * kps;
+  const int nkb = max(0, min(p.kb, kb0 + kps) - kb0);
 
   if (threadIdx.x == 0) {
     s_fail = 0;
@@ -83,21 +89,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(done, 1);
     ptx::fence_mbar_init();
   }
-  if (warp == 2) ptx::tmem_alloc(tmem_slot, C::kTmemCols);
+  if (warp == 1) ptx::tmem_alloc(tmem_slot, C::kTmemCols);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // producer: TMA ring
     for (int i = 0; i < nkb; i++) {
       const int s = i % C::kStages;
-      if (i >= C::kStages) {
-        if (!ptx::mbar_wait(&empty[s], ((i / C::kStages) - 1) & 1)) {
-          s_fail = 1;
-          break;
-        }
+      if (i >= C::kStages && !ptx::mbar_wait(&empty[s], ((i / C::kStages) - 1) & 1)) {
+        s_fail = 1;
+        break;
       }
       ptx::mbar_arrive_expect_tx(&full[s], C::kStageBytes);
       const int kx = (kb0 + i) * BK;
@@ -105,7 +108,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tma_load_2d(b_tiles + s * C::kBBytes, &tmap_x, kx, m0, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
-    // MMA issuer
     constexpr uint32_t idesc = ptx::idesc_bf16_f32(BM, BN);
     for (int i = 0; i < nkb; i++) {
       const int s = i % C::kStages;
@@ -117,96 +119,112 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t ad = ptx::sw128_kmajor_desc(ptx::smem_u32(a_tiles + s * C::kABytes));
       const uint64_t bd = ptx::sw128_kmajor_desc(ptx::smem_u32(b_tiles + s * C::kBBytes));
 #pragma unroll
-      for (int k = 0; k < BK / 16; k++) {
-        // advancing 16 bf16 (32 bytes) along K inside the swizzle atom adds 2 to the address field
-        ptx::mma_f16_ss(tmem, ad + 2 * k, bd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
-      }
+      for (int kk = 0; kk < BK / 16; kk++)
+        ptx::mma_f16_ss(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
       ptx::mma_commit(&empty[s]);
     }
-    ptx::mma_commit(done);
+    ptx::mma_commit(done);  // always arrives, so the epilogue never waits for nothing
   }
   __syncwarp();
 
-  // epilogue: warp w owns TMEM lanes [32w, 32w + 32) = weight rows n0 + 32w + lane
-  const bool ok = ptx::mbar_wait(done, 0);
-  ptx::tc_fence_after();
-  if (!ok) s_fail = 1;
-  const int n = n0 + warp * 32 + lane;
-  const bool nvalid = n < p.N;
   const int mrem = p.M - m0;
-  if (p.splits == 1) {
+  if (warp >= 2) {
+    const int q = warp & 3;  // TMEM lane quadrant of this warp
+    const int r = q * 32 + lane;
+    const int n = n0 + r;
+    if (!ptx::mbar_wait(done, 0)) s_fail = 1;
+    ptx::tc_fence_after();
+    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
       float v[16];
-      ptx::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
-      if (nvalid) {
+      ptx::tmem_ld16(taddr + c0, v);
+      if (nkb == 0) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] = 0.f;
+      }
+      if (S > 1) {
+        // the ring is drained (all MMAs completed before `done`), so its smem holds the partial
+#pragma unroll
+        for (int j = 0; j < 16; j++) partial[(c0 + j) * BM + r] = v[j];
+      } else if (n < p.N) {
 #pragma unroll
         for (int j = 0; j < 16; j++) {
           if (c0 + j < mrem) {
-            const int m = m0 + c0 + j;
-            float r = v[j];
-            if (p.residual) r += bf2f(p.residual[(size_t)m * p.ldr + n]);
-            p.out[(size_t)m * p.ldo + n] = f2bf(r);
+            const size_t m = (size_t)(m0 + c0 + j);
+            float o = v[j];
+            if (p.residual) o += bf2f(p.residual[m * p.ldr + n]);
+            p.out[m * p.ldo + n] = f2bf(o);
           }
         }
       }
     }
-  } else {
-    float* ws = p.ws + (size_t)split * p.M * p.N;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      float v[16];
-      ptx::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
-      if (nvalid) {
+  }
+  if (S > 1) {
+    // publish the partials to the cluster, then reduce this CTA's row slice over all of them
+    ptx::cluster_sync();
+    const uint32_t rank = ptx::cluster_rank();
+    const int rows = ((BM / S) + 3) & ~3;
+    const int r0 = min(BM, (int)rank * rows);
+    const int r1 = (int)rank + 1 == S ? BM : min(BM, r0 + rows);
+    const int span4 = (r1 - r0) >> 2;
+    const int mcount = min(BN, mrem);
+    const int total = span4 * mcount;
+    const uint32_t local = ptx::smem_u32(partial);
+    for (int e = threadIdx.x; e < total; e += kThreads) {
+      const int col = e / span4, row = r0 + (e % span4) * 4;
+      const uint32_t off = (uint32_t)((col * BM + row) * 4);
+      float4 acc = ptx::ld_cluster_v4(ptx::map_cluster(local + off, 0));
+      for (int k = 1; k < S; k++) {
+        const float4 v = ptx::ld_cluster_v4(ptx::map_cluster(local + off, (uint32_t)k));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const size_t m = (size_t)(m0 + col);
+      float o[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-          if (c0 + j < mrem) __stcg(ws + (size_t)(m0 + c0 + j) * p.N + n, v[j]);
+      for (int z = 0; z < 4; z++) {
+        const int n = n0 + row + z;
+        if (n < p.N) {
+          if (p.residual) o[z] += bf2f(p.residual[m * p.ldr + n]);
+          p.out[m * p.ldo + n] = f2bf(o[z]);
         }
       }
     }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int* ctr = p.counters + blockIdx.y * gridDim.x + blockIdx.x;
-      const int prev = atomicAdd(ctr, 1);
-      s_last = (prev == p.splits - 1);
-      if (s_last) *ctr = 0;  // ready for the next call (and the next graph replay)
-    }
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      // sum the partials in split order: thread = weight row, loop over tokens
-      const int mcount = min(BN, mrem);
-      for (int c = 0; c < mcount; c++) {
-        if (nvalid) {
-          const size_t off = (size_t)(m0 + c) * p.N + n;
-          float acc = 0.f;
-          for (int s = 0; s < p.splits; s++) acc += __ldcg(p.ws + (size_t)s * p.M * p.N + off);
-          if (p.residual) acc += bf2f(p.residual[(size_t)(m0 + c) * p.ldr + n]);
-          p.out[(size_t)(m0 + c) * p.ldo + n] = f2bf(acc);
-        }
-      }
-    }
+    ptx::cluster_sync();  // no CTA leaves while another still reads its shared memory
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 2) ptx::tmem_dealloc(tmem, C::kTmemCols);
+  if (warp == 1) ptx::tmem_dealloc(tmem, C::kTmemCols);
   if (threadIdx.x == 0 && s_fail && p.status) atomicExch(p.status, (int)kTimeout);
 }
 
 template <int BN>
-cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, int tiles_n, int tiles_m,
-                   cudaStream_t stream) {
+cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, dim3 grid, cudaStream_t stream) {
   using C = Cfg<BN>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
     configured = true;
   }
-  dim3 grid(tiles_n, tiles_m, p.splits);
-  gemm_kernel<BN><<<grid, kThreads, C::kSmem, stream>>>(mw, mx, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = p.splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN>, mw, mx, p);
 }
 
 }  // namespace gemm
@@ -219,35 +237,23 @@ int64_t gemm_pick_bn(int64_t M) {
   return 256;
 }
 
-int64_t gemm_tiles(int64_t M, int64_t N) {
-  const int64_t bn = gemm_pick_bn(M);
-  return ((N + gemm::BM - 1) / gemm::BM) * ((M + bn - 1) / bn);
-}
-
-// Split count for a weight of N rows and K columns: enough CTAs to give every SM a slice of the
-// weight, never below 4 k-blocks per split. A function of (N, K) only.
-int64_t gemm_pick_splits(int64_t N, int64_t K, int64_t num_sms) {
+// Cluster split for an N x K weight at decode sizes: as many CTAs per tile as the SM slots allow
+// (two per SM for decode tiles), at most 16 (the non-portable cluster limit) and at least 4
+// k-blocks each. A function of (N, K, #SMs) only.
+int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms) {
+  if (M > 64) return 1;
   const int64_t tiles = (N + gemm::BM - 1) / gemm::BM;
   const int64_t kb = (K + gemm::BK - 1) / gemm::BK;
-  if (tiles >= num_sms) return 1;
-  int64_t best = 1;
-  double best_score = 0.0;
-  for (int64_t s = 1; s <= 16; s++) {
-    if (kb / s < 4) break;
-    const int64_t kps = (kb + s - 1) / s;
-    const int64_t real = (kb + kps - 1) / kps;  // splits that actually hold k-blocks
-    if (real != s) continue;
-    const int64_t ctas = tiles * s;
-    const int64_t waves = (ctas + num_sms - 1) / num_sms;
-    const double util = (double)ctas / (double)(waves * num_sms);
-    const double score = util - 0.01 * (double)s;  // prefer fewer splits at equal utilisation
-    if (score > best_score + 1e-9) {
-      best_score = score;
-      best = s;
-    }
-  }
-  return best;
+  const int64_t slots = num_sms * 2;
+  int64_t s = std::max<int64_t>(1, slots / tiles);
+  s = std::min<int64_t>(s, 16);
+  s = std::min<int64_t>(s, std::max<int64_t>(1, kb / 4));
+  while (s > 1 && (kb + s - 1) / s * (s - 1) >= kb) s--;  // every split holds k-blocks
+  return s;
 }
+
+int64_t gemm_ws_floats(int64_t) { return 1; }
+int64_t gemm_sync_words(int64_t) { return 1; }
 
 cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return cudaSuccess;
@@ -255,39 +261,31 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || reinterpret_cast<uintptr_t>(a.w) % 16 != 0)
     return cudaErrorInvalidValue;
   const int BN = (int)gemm_pick_bn(a.M);
-  const int tiles_n = (int)((a.N + gemm::BM - 1) / gemm::BM);
-  const int tiles_m = (int)((a.M + BN - 1) / BN);
-  const int kb_total = (int)((a.K + gemm::BK - 1) / gemm::BK);
-  if (a.splits < 1 || a.splits > kb_total) return cudaErrorInvalidValue;
-  const int kps = (kb_total + a.splits - 1) / a.splits;
-  if ((kb_total + kps - 1) / kps != a.splits) return cudaErrorInvalidValue;
-  if (a.splits > 1 && (a.ws == nullptr || a.counters == nullptr)) return cudaErrorInvalidValue;
-  if (tiles_m > 65535) return cudaErrorInvalidValue;
   gemm::Params p{};
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.residual = static_cast<const __nv_bfloat16*>(a.residual);
-  p.ws = a.ws;
-  p.counters = a.counters;
   p.status = a.status;
   p.M = (int)a.M;
   p.N = (int)a.N;
-  p.K = (int)a.K;
   p.ldo = (int)a.ldo;
   p.ldr = (int)a.ldr;
-  p.kb_total = kb_total;
-  p.kb_per_split = kps;
-  p.splits = a.splits;
+  p.kb = (int)((a.K + gemm::BK - 1) / gemm::BK);
+  p.splits = (int)gemm_pick_splits(a.M, a.N, a.K, a.num_sms);
+  const unsigned tiles_n = (unsigned)((a.N + gemm::BM - 1) / gemm::BM);
+  const unsigned tiles_m = (unsigned)((a.M + BN - 1) / BN);
+  if (tiles_m > 65535) return cudaErrorInvalidValue;
+  dim3 grid(tiles_n, tiles_m, (unsigned)p.splits);
   CUtensorMap mw, mx;
   cudaError_t e = tmap::bf16_2d(&mw, const_cast<void*>(a.w), a.N, a.K, a.ldw, gemm::BM, gemm::BK);
   if (e != cudaSuccess) return e;
   e = tmap::bf16_2d(&mx, const_cast<void*>(a.x), a.M, a.K, a.ldx, BN, gemm::BK);
   if (e != cudaSuccess) return e;
   switch (BN) {
-    case 16: return gemm::launch<16>(mw, mx, p, tiles_n, tiles_m, stream);
-    case 32: return gemm::launch<32>(mw, mx, p, tiles_n, tiles_m, stream);
-    case 64: return gemm::launch<64>(mw, mx, p, tiles_n, tiles_m, stream);
-    case 128: return gemm::launch<128>(mw, mx, p, tiles_n, tiles_m, stream);
-    default: return gemm::launch<256>(mw, mx, p, tiles_n, tiles_m, stream);
+    case 16: return gemm::launch<16>(mw, mx, p, grid, stream);
+    case 32: return gemm::launch<32>(mw, mx, p, grid, stream);
+    case 64: return gemm::launch<64>(mw, mx, p, grid, stream);
+    case 128: return gemm::launch<128>(mw, mx, p, grid, stream);
+    default: return gemm::launch<256>(mw, mx, p, grid, stream);
   }
 }
 

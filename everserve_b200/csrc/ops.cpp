@@ -112,7 +112,7 @@ void decode_advance(torch::Tensor st, torch::Tensor sampled, torch::Tensor bt, i
 }
 
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
-               torch::Tensor ws, torch::Tensor counters, torch::Tensor status, int64_t splits) {
+               torch::Tensor ws, torch::Tensor sync, torch::Tensor status, int64_t num_sms) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
@@ -122,6 +122,8 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
   TORCH_CHECK(w.size(1) == K, "K mismatch: x has ", K, ", w has ", w.size(1));
   TORCH_CHECK(out.size(0) == M && out.size(1) == N, "out shape");
   TORCH_CHECK(status.scalar_type() == at::kInt && status.is_cuda(), "status must be int32 on the device");
+  TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= es::gemm_ws_floats(num_sms), "stream-K workspace too small");
+  TORCH_CHECK(sync.scalar_type() == at::kInt && sync.numel() >= es::gemm_sync_words(num_sms), "sync words too small");
   es::GemmArgs a{};
   a.x = x.data_ptr();
   a.w = w.data_ptr();
@@ -132,20 +134,15 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
   a.ldx = x.stride(0);
   a.ldw = w.stride(0);
   a.ldo = out.stride(0);
-  a.splits = (int)splits;
   a.status = status.data_ptr<int>();
+  a.ws = ws.data_ptr<float>();
+  a.sync = reinterpret_cast<uint32_t*>(sync.data_ptr<int>());
+  a.num_sms = (int)num_sms;
   if (residual.has_value()) {
     check_bf16(*residual, "residual");
     TORCH_CHECK(residual->size(0) == M && residual->size(1) == N && residual->stride(1) == 1, "residual shape");
     a.residual = residual->data_ptr();
     a.ldr = residual->stride(0);
-  }
-  if (splits > 1) {
-    TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= splits * M * N, "split-K workspace too small");
-    TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= es::gemm_tiles(M, N),
-                "split-K counters too small");
-    a.ws = ws.data_ptr<float>();
-    a.counters = counters.data_ptr<int>();
   }
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
@@ -153,7 +150,7 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
 
 void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
                   torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor status,
-                  int64_t max_splits, int64_t part_tokens, double scale) {
+                  int64_t max_splits, int64_t part_tokens, double scale, int64_t stages) {
   check_bf16(q, "q");
   check_bf16(cache, "cache");
   check_bf16(out, "out");
@@ -188,6 +185,8 @@ void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tabl
   a.hkv = hkv;
   a.d = d;
   a.block_size = bs;
+  a.num_blocks = cache.size(0);
+  a.stages = (int)stages;
   a.max_splits = (int)max_splits;
   a.part_tokens = (int)part_tokens;
   a.scale = (float)scale;
@@ -274,7 +273,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM out = x . w^T (+ residual)");
   m.def("gemm_pick_bn", &es::gemm_pick_bn);
   m.def("gemm_pick_splits", &es::gemm_pick_splits);
-  m.def("gemm_tiles", &es::gemm_tiles);
+  m.def("gemm_ws_floats", &es::gemm_ws_floats);
+  m.def("gemm_sync_words", &es::gemm_sync_words);
   m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
   m.def("kv_gather", [](torch::Tensor lp, torch::Tensor s, torch::Tensor h, int64_t st, int64_t cap, int64_t d,
                         int64_t bs, std::vector<int64_t> str, int64_t el) { kv_copy(true, lp, s, h, st, cap, d, bs, str, el); },

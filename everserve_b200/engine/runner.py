@@ -198,7 +198,9 @@ class ModelRunner:
     def fetch(self, ids: torch.Tensor) -> list[int]:
         """Device -> pinned host copy of sampled ids, synchronised on the copy's stream."""
         n = ids.numel()
-        self.h_out[:n].copy_(ids.view(-1), non_blocking=True)
+        if n > self.h_out.numel():
+            self.h_out = torch.zeros(n, dtype=torch.int64, pin_memory=self.device.type == "cuda")
+        self.h_out[:n].copy_(ids.reshape(-1), non_blocking=True)
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
         return self.h_out[:n].tolist()

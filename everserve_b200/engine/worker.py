@@ -32,6 +32,8 @@ class Worker:
         self.pipe = pipe  # stage transport (send/recv of hidden + residual), None for pp == 1
         self.device = torch.device(device or cfg.device)
         if self.device.type == "cuda":
+            if self.device.index is None:
+                self.device = torch.device("cuda", torch.cuda.current_device())
             torch.cuda.set_device(self.device)
         self.tp = TPGroup(self.column, tp, collective)
         layers = stage_layers(cfg.model.layers, pp, self.stage)

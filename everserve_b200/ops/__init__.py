@@ -62,7 +62,7 @@ class KernelOps:
 
     kind = "kernel"
     PART_TOKENS = 256  # positions per decode-attention split (fixed: batch-invariant results)
-    SPLITK_MAX_M = 256  # split-K only for decode-sized token counts
+    ATTN_STAGES = 3
 
     def __init__(self, device: torch.device | str):
         self.device = torch.device(device)
@@ -75,20 +75,9 @@ class KernelOps:
         self._ctr = torch.zeros(0, dtype=torch.int32, device=self.device)
         self._part_o = torch.empty(0, dtype=torch.float32, device=self.device)
         self._part_ml = torch.empty(0, dtype=torch.float32, device=self.device)
-        self._splits: dict[tuple[int, int], int] = {}
         self._lock = threading.Lock()
 
     # ---- scratch ------------------------------------------------------------------------------
-    def splits_for(self, M: int, N: int, K: int) -> int:
-        if M > self.SPLITK_MAX_M:
-            return 1
-        key = (N, K)
-        s = self._splits.get(key)
-        if s is None:
-            s = int(self.C.gemm_pick_splits(N, K, self.num_sms))
-            self._splits[key] = s
-        return s
-
     def _ensure(self, name: str, numel: int, dtype, zero: bool = False) -> torch.Tensor:
         buf = getattr(self, name)
         if buf.numel() >= numel:
@@ -99,17 +88,10 @@ class KernelOps:
         setattr(self, name, new)
         return new
 
-    def reserve_linear(self, max_m: int, shapes: list[tuple[int, int]]):
-        """Size the GEMM scratch for every (N, K) weight at up to max_m tokens."""
-        ws = ctr = 0
-        for m in sorted({min(max_m, self.SPLITK_MAX_M), max_m}):
-            for n, k in shapes:
-                s = self.splits_for(m, n, k)
-                if s > 1:
-                    ws = max(ws, s * m * n)
-                    ctr = max(ctr, int(self.C.gemm_tiles(m, n)))
-        self._ensure("_ws", ws, torch.float32)
-        self._ensure("_ctr", ctr, torch.int32, zero=True)
+    def reserve_linear(self, max_m: int = 0, shapes=None):
+        """The GEMM's stream-K scratch: one fp32 partial tile per SM and the sync words."""
+        self._ensure("_ws", int(self.C.gemm_ws_floats(self.num_sms)), torch.float32)
+        self._ensure("_ctr", int(self.C.gemm_sync_words(self.num_sms)), torch.int32, zero=True)
 
     def max_splits(self, max_model_len: int) -> int:
         return max(1, (max_model_len + self.PART_TOKENS - 1) // self.PART_TOKENS)
@@ -135,15 +117,12 @@ class KernelOps:
         N = w.shape[0]
         if out is None:
             out = torch.empty(M, N, dtype=x.dtype, device=x.device)
-        s = self.splits_for(M, N, K)
-        if s > 1:
-            self._ensure("_ws", s * M * N, torch.float32)
-            self._ensure("_ctr", int(self.C.gemm_tiles(M, N)), torch.int32, zero=True)
+        self.reserve_linear()
         if bias is not None:
             # bias folds into the residual input of the epilogue
             b = bias.expand(M, N) if residual is None else residual + bias
             residual = b.contiguous()
-        self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, s)
+        self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, self.num_sms)
         return out
 
     def rope_kv_write(self, qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size):
@@ -163,7 +142,7 @@ class KernelOps:
         self.reserve_attention(B, hq, d, max_model_len)
         out = torch.empty(B, hq, d, dtype=q.dtype, device=q.device)
         self.C.paged_decode(q, cache, block_tables, ctx_lens, out, self._part_o, self._part_ml, self.status,
-                            ms, self.PART_TOKENS, scale)
+                            ms, self.PART_TOKENS, scale, self.ATTN_STAGES)
         return out
 
     def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale):
