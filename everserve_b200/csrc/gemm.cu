@@ -34,10 +34,10 @@ constexpr int kThreads = 192;
 
 // decode tiles (BN <= 64) run two CTAs per SM so one CTA's start-up and reduction overlap the
 // other's streaming; larger tiles run one CTA per SM with a deeper ring
-template <int BN>
+template <int BN, int CPS = (BN <= 64 ? 2 : 1)>
 struct Cfg {
-  static constexpr int kCps = BN <= 64 ? 2 : 1;
-  static constexpr int kStages = BN <= 64 ? 4 : (BN == 128 ? 6 : 4);
+  static constexpr int kCps = CPS;
+  static constexpr int kStages = CPS == 2 ? 4 : (BN <= 64 ? 8 : (BN == 128 ? 6 : 4));
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -54,10 +54,10 @@ struct Params {
   int kb, splits;
 };
 
-template <int BN>
-__global__ void __launch_bounds__(kThreads, Cfg<BN>::kCps)
+template <int BN, int CPS>
+__global__ void __launch_bounds__(kThreads, CPS)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, Params p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, CPS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_tiles = smem;
@@ -201,14 +201,14 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::kCps)
   if (threadIdx.x == 0 && s_fail && p.status) atomicExch(p.status, (int)kTimeout);
 }
 
-template <int BN>
+template <int BN, int CPS = (BN <= 64 ? 2 : 1)>
 cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, dim3 grid, cudaStream_t stream) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, CPS>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    e = cudaFuncSetAttribute(gemm_kernel<BN, CPS>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured = true;
   }
@@ -224,7 +224,7 @@ cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p
   attr[0].val.clusterDim.z = p.splits;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN>, mw, mx, p);
+  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, CPS>, mw, mx, p);
 }
 
 }  // namespace gemm
@@ -237,18 +237,39 @@ int64_t gemm_pick_bn(int64_t M) {
   return 256;
 }
 
-// Cluster split for an N x K weight at decode sizes: as many CTAs per tile as the SM slots allow
-// (two per SM for decode tiles), at most 16 (the non-portable cluster limit) and at least 4
-// k-blocks each. A function of (N, K, #SMs) only.
-int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms) {
-  if (M > 64) return 1;
-  const int64_t tiles = (N + gemm::BM - 1) / gemm::BM;
-  const int64_t kb = (K + gemm::BK - 1) / gemm::BK;
-  const int64_t slots = num_sms * 2;
+// Cluster split for an N x K weight at decode sizes: as many CTAs per tile as the SM slots allow,
+// at most 16 (the non-portable cluster limit) and at least 4 k-blocks each. One CTA per SM with a
+// deep ring when that still splits each tile 4 ways (or as far as two per SM would, with no more
+// tiles than SMs); otherwise two per SM. A function of (N, K, #SMs) only.
+static int64_t split_for(int64_t tiles, int64_t kb, int64_t slots) {
   int64_t s = std::max<int64_t>(1, slots / tiles);
   s = std::min<int64_t>(s, 16);
   s = std::min<int64_t>(s, std::max<int64_t>(1, kb / 4));
   while (s > 1 && (kb + s - 1) / s * (s - 1) >= kb) s--;  // every split holds k-blocks
+  return s;
+}
+
+void gemm_plan(int64_t M, int64_t N, int64_t K, int64_t num_sms, int* splits, int* cps) {
+  if (M > 64) {
+    *splits = 1;
+    *cps = 1;
+    return;
+  }
+  const int64_t tiles = (N + gemm::BM - 1) / gemm::BM;
+  const int64_t kb = (K + gemm::BK - 1) / gemm::BK;
+  const int64_t s1 = split_for(tiles, kb, num_sms), s2 = split_for(tiles, kb, 2 * num_sms);
+  if (s1 >= 4 || (s1 == s2 && tiles <= num_sms)) {
+    *splits = (int)s1;
+    *cps = 1;
+  } else {
+    *splits = (int)s2;
+    *cps = 2;
+  }
+}
+
+int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms) {
+  int s, c;
+  gemm_plan(M, N, K, num_sms, &s, &c);
   return s;
 }
 
@@ -270,7 +291,8 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.ldo = (int)a.ldo;
   p.ldr = (int)a.ldr;
   p.kb = (int)((a.K + gemm::BK - 1) / gemm::BK);
-  p.splits = (int)gemm_pick_splits(a.M, a.N, a.K, a.num_sms);
+  int cps = 1;
+  gemm_plan(a.M, a.N, a.K, a.num_sms, &p.splits, &cps);
   const unsigned tiles_n = (unsigned)((a.N + gemm::BM - 1) / gemm::BM);
   const unsigned tiles_m = (unsigned)((a.M + BN - 1) / BN);
   if (tiles_m > 65535) return cudaErrorInvalidValue;
@@ -281,9 +303,9 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   e = tmap::bf16_2d(&mx, const_cast<void*>(a.x), a.M, a.K, a.ldx, BN, gemm::BK);
   if (e != cudaSuccess) return e;
   switch (BN) {
-    case 16: return gemm::launch<16>(mw, mx, p, grid, stream);
-    case 32: return gemm::launch<32>(mw, mx, p, grid, stream);
-    case 64: return gemm::launch<64>(mw, mx, p, grid, stream);
+    case 16: return cps == 1 ? gemm::launch<16, 1>(mw, mx, p, grid, stream) : gemm::launch<16, 2>(mw, mx, p, grid, stream);
+    case 32: return cps == 1 ? gemm::launch<32, 1>(mw, mx, p, grid, stream) : gemm::launch<32, 2>(mw, mx, p, grid, stream);
+    case 64: return cps == 1 ? gemm::launch<64, 1>(mw, mx, p, grid, stream) : gemm::launch<64, 2>(mw, mx, p, grid, stream);
     case 128: return gemm::launch<128>(mw, mx, p, grid, stream);
     default: return gemm::launch<256>(mw, mx, p, grid, stream);
   }
