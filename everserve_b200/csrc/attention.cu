@@ -13,6 +13,8 @@
 // never depends on the batch around it.
 #include <cuda.h>
 
+#include <cstring>
+
 #include "api.h"
 #include "common.cuh"
 #include "ptx.cuh"
@@ -324,3 +326,137 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace es
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free entry point (declared and documented in es_noalloc.h; no counterpart in the
+// reference). Its split-KV scratch is this file-scope device array, not caller memory.
+#include <mutex>
+
+#include "es_noalloc.h"
+
+namespace {
+
+constexpr size_t kNoAllocFloats = (size_t)ES_NOALLOC_PART_FLOATS + ES_NOALLOC_ML_FLOATS + 64;  // + status word
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+thread_local const char* g_noalloc_err = "";
+
+// The array's device address on the current device, looked up once per device.
+cudaError_t noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) {
+    g_noalloc_err = "device index above the supported maximum";
+    return cudaErrorInvalidDevice;
+  }
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      g_noalloc_err = "cudaGetSymbolAddress of the scratch array failed";
+      return e;
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int es_noalloc_setup(void) {
+  float* p = nullptr;
+  return (int)noalloc_scratch(&p);
+}
+
+extern "C" __attribute__((visibility("default"))) const char* es_noalloc_last_error(void) { return g_noalloc_err; }
+
+extern "C" __attribute__((visibility("default"))) int es_noalloc_status(void* stream, int* status) {
+  float* base = nullptr;
+  cudaError_t e = noalloc_scratch(&base);
+  if (e != cudaSuccess) return (int)e;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* st = reinterpret_cast<int*>(base + ES_NOALLOC_PART_FLOATS + ES_NOALLOC_ML_FLOATS);
+  e = cudaMemcpyAsync(status, st, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return (int)e;
+  return (int)cudaStreamSynchronize(s);
+}
+
+extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
+    const void* q, int64_t q_stride, const void* cache, int64_t num_blocks, int kv_heads, int block_size,
+    int head_dim, const int* block_tables, int64_t bt_stride, const int* ctx_lens, void* out, int64_t out_stride,
+    int batch, int q_heads, int max_model_len, float scale, void* stream) {
+  using namespace es;
+  g_noalloc_err = "";
+  if (batch == 0) return (int)cudaSuccess;
+  constexpr int kPart = 256;  // positions per split, the regular entry point's default
+  if (batch < 0 || kv_heads <= 0 || q_heads % kv_heads != 0 || q_heads / kv_heads > 8 || max_model_len <= 0) {
+    g_noalloc_err = "bad shape: q_heads must be 1..8 times kv_heads and max_model_len positive";
+    return (int)cudaErrorInvalidValue;
+  }
+  if (!((head_dim == 128 || head_dim == 64) && (block_size == 16 || block_size == 32))) {
+    g_noalloc_err = "head_dim must be 64 or 128 and block_size 16 or 32";
+    return (int)cudaErrorInvalidValue;
+  }
+  const int64_t splits = (max_model_len + kPart - 1) / kPart;
+  if ((int64_t)batch * q_heads * splits * head_dim > ES_NOALLOC_PART_FLOATS ||
+      (int64_t)batch * q_heads * splits * 2 > ES_NOALLOC_ML_FLOATS) {
+    g_noalloc_err = "batch * q_heads * ceil(max_model_len / 256) * head_dim exceeds the fixed scratch (2^21 floats)";
+    return (int)cudaErrorInvalidValue;
+  }
+  float* base = nullptr;
+  cudaError_t e = noalloc_scratch(&base);
+  if (e != cudaSuccess) return (int)e;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = reinterpret_cast<int*>(base + ES_NOALLOC_PART_FLOATS + ES_NOALLOC_ML_FLOATS);
+  e = cudaMemsetAsync(status, 0, sizeof(int), s);  // the status word starts each call at zero
+  if (e != cudaSuccess) return (int)e;
+  attn::DecodeParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_stride = q_stride;
+  p.block_tables = block_tables;
+  p.bt_stride = (int)bt_stride;
+  p.ctx_lens = ctx_lens;
+  p.part_o = base;
+  p.part_ml = base + ES_NOALLOC_PART_FLOATS;
+  p.hq = q_heads;
+  p.hkv = kv_heads;
+  p.max_splits = (int)splits;
+  p.part_tokens = kPart;
+  p.scale_log2 = scale * attn::kLog2e;
+  p.status = status;
+  // tensor map encoded on the stack (no cache: nothing is allocated, not even on the host heap)
+  tmap::EncodeFn enc = tmap::encoder();
+  if (enc == nullptr) {
+    g_noalloc_err = "cuTensorMapEncodeTiled is not available";
+    return (int)cudaErrorNotSupported;
+  }
+  const int64_t rows = num_blocks * 2 * kv_heads * block_size * (head_dim / 64);
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  const cuuint64_t dims[2] = {64, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {128};
+  const cuuint32_t box[2] = {64, (cuuint32_t)(block_size * (head_dim / 64))};
+  const cuuint32_t estr[2] = {1, 1};
+  if (reinterpret_cast<uintptr_t>(cache) % 16 != 0 ||
+      enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(cache), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+    g_noalloc_err = "the cache cannot be described by a TMA map (alignment or size)";
+    return (int)cudaErrorInvalidValue;
+  }
+  if (head_dim == 128 && block_size == 16) e = attn::launch_stages<128, 16>(3, map, p, batch, s);
+  else if (head_dim == 64 && block_size == 16) e = attn::launch_stages<64, 16>(3, map, p, batch, s);
+  else if (head_dim == 128 && block_size == 32) e = attn::launch_stages<128, 32>(3, map, p, batch, s);
+  else e = attn::launch_stages<64, 32>(3, map, p, batch, s);
+  if (e != cudaSuccess) return (int)e;
+  dim3 mgrid(batch, q_heads);
+  attn::decode_merge_kernel<<<mgrid, head_dim, 0, s>>>(p.part_o, p.part_ml, ctx_lens, static_cast<__nv_bfloat16*>(out),
+                                                       out_stride, q_heads, (int)splits, kPart, head_dim);
+  return (int)cudaGetLastError();
+}
