@@ -23,6 +23,18 @@ cudaError_t launch_decode_advance(int64_t* st, const int64_t* sampled, const int
                                   int bs, cudaStream_t s);
 cudaError_t launch_argmax(const void* logits, int64_t* out, int64_t rows, int vocab, int64_t stride, cudaStream_t s);
 
+// ---- comm.cu (peer-memory collectives; layout in comm.cuh) ----------------------------------
+struct CommArgs {
+  const uint64_t* peers;  // device [8]: each row's symmetric buffer (0 = unmapped)
+  const int32_t* order;   // device [9]: member count, rows in member order
+  uint32_t* call;         // device [2]: call counter, CTAs finished in the current call
+  void* ctrl;             // device address of this member's host-mapped control words
+  int row;                // this member's row
+};
+int64_t comm_buffer_bytes();
+int64_t comm_max_elems();
+cudaError_t launch_fdar(const void* inp, void* out, int64_t n, const CommArgs& c, cudaStream_t s);
+
 // ---- gemm.cu -------------------------------------------------------------------------------------
 struct GemmArgs {
   const void* x;  // [M, K] bf16, row stride ldx
@@ -40,6 +52,9 @@ int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms);
 int64_t gemm_ws_floats(int64_t num_sms);
 int64_t gemm_sync_words(int64_t num_sms);
 cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t s);
+// out = sum over the group's members (member order) of x_r . w_r^T (+ residual): the row-parallel
+// GEMM with its all-reduce fused into the epilogue (decode sizes, M <= 64).
+cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStream_t s);
 
 // ---- attention.cu --------------------------------------------------------------------------------
 struct DecodeArgs {

@@ -1,0 +1,112 @@
+// Peer-memory collectives of a tensor-parallel group over NVLink (one process per GPU).
+//
+// Every member owns one symmetric buffer in its device memory, exported by CUDA IPC and mapped by
+// the others:
+//   flags: uint32 [2 parity][kMaxRows sender][kFlagSlots]
+//   data : bytes  [2 parity][kMaxRows sender][kDataBytes]
+// A call pushes this member's contribution into every member's buffer at its own sender row
+// (remote stores over NVLink), raises one flag per slot on every member, then waits only on its own
+// buffer (local polls) for every member's flag and sums the members' rows in member order in fp32.
+// The member order is a device table, so a captured CUDA graph follows a membership change
+// without recapture; a spare in the position of a lost rank sums in that rank's place, which keeps
+// the result bit-identical across the change.
+//
+// Calls are numbered by a per-buffer call counter in device memory (the last CTA of a call
+// advances it); the number is the flag value and its low bit the parity, so a member one call
+// ahead writes the other half of the buffer.
+//
+// Failure detection: every wait is bounded. After `bound_ns` (host-written, 0 = off) a waiting CTA
+// ORs the rows it still waits for into the host-visible late mask and keeps waiting; the host's
+// abort word (polled every 1024 spins) or a hard limit ends the wait, the call returns garbage and
+// the status word says why. Nothing here traps or spins without a bound.
+#pragma once
+
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace es {
+namespace comm {
+
+constexpr int kMaxRows = 8;            // members: up to seven ranks and a spare
+constexpr int kFlagSlots = 4096;
+constexpr size_t kDataBytes = 1 << 21;  // 2 MiB per sender per parity
+constexpr size_t kFlagBytes = (size_t)2 * kMaxRows * kFlagSlots * 4;
+constexpr size_t kBufferBytes = kFlagBytes + (size_t)2 * kMaxRows * kDataBytes;
+constexpr uint64_t kHardLimitNs = 5000000000ull;  // a wait never outlives 5 s
+
+// Host-mapped control words of one member (pinned host memory the device reads and writes).
+struct Ctrl {
+  uint32_t abort;      // host: non-zero makes waiting kernels leave
+  uint32_t late;       // device: mask of rows a wait has been waiting for past bound_ns
+  uint64_t bound_ns;   // host: 0 = never name late members
+  uint32_t status;     // device: last failure (kTimeout / kAborted)
+  uint32_t pad[3];
+};
+
+// Device view of a member's place in the group (kernel parameter, by value).
+struct View {
+  const uint64_t* peers;  // [kMaxRows] base address of each row's buffer (0 = not mapped)
+  const int32_t* order;   // [1 + kMaxRows]: count, rows in member order
+  uint32_t* call;         // [2]: call counter, CTAs done in the current call
+  Ctrl* ctrl;             // host-mapped control words of this member (device address)
+  int row;                // this member's row
+};
+
+ES_DEVICE uint32_t* flag_ptr(uint64_t base, uint32_t parity, int sender, int slot) {
+  return reinterpret_cast<uint32_t*>(base) + ((size_t)parity * kMaxRows + sender) * kFlagSlots + slot;
+}
+ES_DEVICE char* data_ptr(uint64_t base, uint32_t parity, int sender) {
+  return reinterpret_cast<char*>(base) + kFlagBytes + ((size_t)parity * kMaxRows + sender) * kDataBytes;
+}
+
+// Wait until every member's flag for `slot` in this member's buffer equals `seq`. Called by one
+// thread; returns kOk, kAborted or kTimeout.
+ES_DEVICE int wait_members(const View& v, uint64_t my_base, uint32_t parity, int slot, uint32_t seq,
+                           const int* order, int count) {
+  const uint64_t t0 = global_ns();
+  uint64_t bound = 0;
+  bool named = false;
+  uint32_t spins = 0;
+  for (int i = 0; i < count; i++) {
+    const int sender = order[i];
+    const uint32_t* f = flag_ptr(my_base, parity, sender, slot);
+    while (ld_acquire_sys(f) != seq) {
+      if ((++spins & 1023u) == 0) {
+        volatile Ctrl* c = v.ctrl;
+        if (c->abort) return kAborted;
+        const uint64_t now = global_ns() - t0;
+        if (bound == 0) bound = c->bound_ns;
+        if (!named && bound != 0 && now > bound) {
+          uint32_t mask = 0;
+          for (int k = i; k < count; k++)
+            if (ld_acquire_sys(flag_ptr(my_base, parity, order[k], slot)) != seq) mask |= 1u << order[k];
+          // host-mapped memory: a plain read-modify-write (device atomics on mapped host memory are
+          // not guaranteed); a bit a concurrent CTA drops is named again by that CTA's own wait
+          volatile Ctrl* cw = v.ctrl;
+          cw->late = cw->late | mask;
+          named = true;
+        }
+        if (now > kHardLimitNs) return kTimeout;
+      }
+    }
+  }
+  return kOk;
+}
+
+// Called by thread 0 of every CTA at the end of a call: the last CTA advances the call counter.
+ES_DEVICE void finish_call(const View& v, uint32_t seq, int failure) {
+  if (failure != kOk) {
+    volatile Ctrl* cw = v.ctrl;
+    cw->status = (uint32_t)failure;
+  }
+  __threadfence();
+  if (atomicAdd(v.call + 1, 1u) == gridDim.x * gridDim.y * gridDim.z - 1) {
+    v.call[1] = 0;
+    __threadfence();
+    atomicExch(v.call, seq);
+  }
+}
+
+}  // namespace comm
+}  // namespace es

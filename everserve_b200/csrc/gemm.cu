@@ -19,8 +19,11 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
+#include <unordered_map>
 
 #include "api.h"
+#include "comm.cuh"
 #include "common.cuh"
 #include "ptx.cuh"
 #include "tmap.h"
@@ -54,9 +57,11 @@ struct Params {
   int kb, splits;
 };
 
-template <int BN, int CPS>
+// kAR: the row-parallel variant whose epilogue sums the tile over the group's members (comm.cuh)
+template <int BN, int CPS, bool kAR>
 __global__ void __launch_bounds__(kThreads, CPS)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, Params p,
+                comm::View cv) {
   using C = Cfg<BN, CPS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -68,6 +73,9 @@ __global__ void __launch_bounds__(kThreads, CPS)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   float* partial = reinterpret_cast<float*>(smem);  // [BN][BM] once the ring is drained
   __shared__ int s_fail;
+  __shared__ uint32_t s_seq;
+  __shared__ int s_order[comm::kMaxRows];
+  __shared__ int s_count;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BM;
@@ -80,6 +88,12 @@ __global__ void __launch_bounds__(kThreads, CPS)
 
   if (threadIdx.x == 0) {
     s_fail = 0;
+    if (kAR) {
+      s_seq = cv.call[0] + 1;
+      const int cnt = cv.order[0];
+      s_count = cnt < 0 ? 0 : (cnt > comm::kMaxRows ? comm::kMaxRows : cnt);
+      for (int i = 0; i < s_count; i++) s_order[i] = cv.order[1 + i];
+    }
     ptx::prefetch_tmap(&tmap_w);
     ptx::prefetch_tmap(&tmap_x);
     for (int s = 0; s < C::kStages; s++) {
@@ -143,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
 #pragma unroll
         for (int j = 0; j < 16; j++) v[j] = 0.f;
       }
-      if (S > 1) {
+      if (S > 1 || kAR) {
         // the ring is drained (all MMAs completed before `done`), so its smem holds the partial
 #pragma unroll
         for (int j = 0; j < 16; j++) partial[(c0 + j) * BM + r] = v[j];
@@ -160,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
       }
     }
   }
-  if (S > 1) {
+  if (S > 1 || kAR) {
     // publish the partials to the cluster, then reduce this CTA's row slice over all of them
     ptx::cluster_sync();
     const uint32_t rank = ptx::cluster_rank();
@@ -171,6 +185,8 @@ __global__ void __launch_bounds__(kThreads, CPS)
     const int mcount = min(BN, mrem);
     const int total = span4 * mcount;
     const uint32_t local = ptx::smem_u32(partial);
+    const uint32_t seq = kAR ? s_seq : 0u, parity = seq & 1u;
+    const int slot = blockIdx.x * S + (int)rank;
     for (int e = threadIdx.x; e < total; e += kThreads) {
       const int col = e / span4, row = r0 + (e % span4) * 4;
       const uint32_t off = (uint32_t)((col * BM + row) * 4);
@@ -181,6 +197,14 @@ __global__ void __launch_bounds__(kThreads, CPS)
         acc.y += v.y;
         acc.z += v.z;
         acc.w += v.w;
+      }
+      if (kAR) {
+        // this member's bf16 partial (what an unfused GEMM would output) to every member
+        const uint2 packed = make_uint2(ptx::pack_bf16x2(acc.x, acc.y), ptx::pack_bf16x2(acc.z, acc.w));
+        const size_t boff = ((size_t)(blockIdx.x * BN + col) * BM + row) * 2;
+        for (int k = 0; k < s_count; k++)
+          *reinterpret_cast<uint2*>(comm::data_ptr(cv.peers[s_order[k]], parity, cv.row) + boff) = packed;
+        continue;
       }
       const size_t m = (size_t)(m0 + col);
       float o[4] = {acc.x, acc.y, acc.z, acc.w};
@@ -193,22 +217,64 @@ __global__ void __launch_bounds__(kThreads, CPS)
         }
       }
     }
+    if (kAR) {
+      __threadfence_system();
+      __syncthreads();
+      if (threadIdx.x < s_count)
+        st_release_sys(comm::flag_ptr(cv.peers[s_order[threadIdx.x]], parity, cv.row, slot), seq);
+      const uint64_t my_base = cv.peers[cv.row];
+      if (threadIdx.x == 0) {
+        const int w = comm::wait_members(cv, my_base, parity, slot, seq, s_order, s_count);
+        if (w != kOk) s_fail = w;
+      }
+      __syncthreads();
+      if (s_fail == kOk) {
+        for (int e = threadIdx.x; e < total; e += kThreads) {
+          const int col = e / span4, row = r0 + (e % span4) * 4;
+          const size_t boff = ((size_t)(blockIdx.x * BN + col) * BM + row) * 2;
+          float o[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int k = 0; k < s_count; k++) {
+            const uint2 w = *reinterpret_cast<const uint2*>(comm::data_ptr(my_base, parity, s_order[k]) + boff);
+            const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+            const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+            o[0] += lo.x;
+            o[1] += lo.y;
+            o[2] += hi.x;
+            o[3] += hi.y;
+          }
+          const size_t m = (size_t)(m0 + col);
+#pragma unroll
+          for (int z = 0; z < 4; z++) {
+            const int n = n0 + row + z;
+            if (n < p.N) {
+              if (p.residual) o[z] += bf2f(p.residual[m * p.ldr + n]);
+              p.out[m * p.ldo + n] = f2bf(o[z]);
+            }
+          }
+        }
+      }
+    }
     ptx::cluster_sync();  // no CTA leaves while another still reads its shared memory
   }
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 1) ptx::tmem_dealloc(tmem, C::kTmemCols);
-  if (threadIdx.x == 0 && s_fail && p.status) atomicExch(p.status, (int)kTimeout);
+  if (threadIdx.x == 0) {
+    if (s_fail && p.status) atomicExch(p.status, s_fail == kAborted ? (int)kAborted : (int)kTimeout);
+    if (kAR) comm::finish_call(cv, s_seq, s_fail == kAborted ? (int)kAborted : (s_fail ? (int)kTimeout : (int)kOk));
+  }
 }
 
-template <int BN, int CPS = (BN <= 64 ? 2 : 1)>
-cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, dim3 grid, cudaStream_t stream) {
+template <int BN, int CPS = (BN <= 64 ? 2 : 1), bool kAR = false>
+cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, dim3 grid, cudaStream_t stream,
+                   const comm::View& cv = comm::View{}) {
   using C = Cfg<BN, CPS>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<BN, CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_kernel<BN, CPS, kAR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(gemm_kernel<BN, CPS>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    e = cudaFuncSetAttribute(gemm_kernel<BN, CPS, kAR>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured = true;
   }
@@ -224,7 +290,39 @@ cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p
   attr[0].val.clusterDim.z = p.splits;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, CPS>, mw, mx, p);
+  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, CPS, kAR>, mw, mx, p, cv);
+}
+
+// The largest split whose clusters all fit on the device at once (the fused all-reduce waits on
+// peers, so every CTA of the grid must be resident together).
+template <int BN, int CPS>
+int resident_split(int tiles, int want) {
+  using C = Cfg<BN, CPS>;
+  cudaError_t e =
+      cudaFuncSetAttribute(gemm_kernel<BN, CPS, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return 0;
+  e = cudaFuncSetAttribute(gemm_kernel<BN, CPS, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return 0;
+  for (int s = want; s >= 1; s--) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles, 1, s);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<BN, CPS, true>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    if (clusters >= tiles) return s;
+  }
+  return 0;
 }
 
 }  // namespace gemm
@@ -309,6 +407,63 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     case 128: return gemm::launch<128>(mw, mx, p, grid, stream);
     default: return gemm::launch<256>(mw, mx, p, grid, stream);
   }
+}
+
+}  // namespace es
+
+namespace es {
+
+cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStream_t stream) {
+  if (a.M == 0 || a.N == 0) return cudaSuccess;
+  if (a.M > 64 || a.K % 8 != 0 || (a.ldx * 2) % 16 != 0 || (a.ldw * 2) % 16 != 0) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || reinterpret_cast<uintptr_t>(a.w) % 16 != 0)
+    return cudaErrorInvalidValue;
+  constexpr int BN = 64;  // one token tile for every decode batch: the plan never depends on M
+  const int tiles = (int)((a.N + gemm::BM - 1) / gemm::BM);
+  if ((size_t)tiles * BN * gemm::BM * 2 > comm::kDataBytes) return cudaErrorInvalidValue;
+  gemm::Params p{};
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.residual = static_cast<const __nv_bfloat16*>(a.residual);
+  p.status = a.status;
+  p.M = (int)a.M;
+  p.N = (int)a.N;
+  p.ldo = (int)a.ldo;
+  p.ldr = (int)a.ldr;
+  p.kb = (int)((a.K + gemm::BK - 1) / gemm::BK);
+  int cps = 1;
+  gemm_plan(BN, a.N, a.K, a.num_sms, &p.splits, &cps);
+  // every CTA waits on peers: the whole grid must be resident at once
+  static std::mutex mu;
+  static std::unordered_map<long long, int> fit;
+  const long long key = ((long long)tiles << 20) | ((long long)p.splits << 4) | cps;
+  int s_fit;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = fit.find(key);
+    if (it == fit.end()) {
+      s_fit = cps == 1 ? gemm::resident_split<BN, 1>(tiles, p.splits) : gemm::resident_split<BN, 2>(tiles, p.splits);
+      fit.emplace(key, s_fit);
+    } else {
+      s_fit = it->second;
+    }
+  }
+  if (s_fit <= 0) return cudaErrorInvalidConfiguration;
+  p.splits = s_fit;
+  if (tiles * p.splits > comm::kFlagSlots) return cudaErrorInvalidValue;
+  comm::View v{};
+  v.peers = c.peers;
+  v.order = c.order;
+  v.call = c.call;
+  v.ctrl = reinterpret_cast<comm::Ctrl*>(c.ctrl);
+  v.row = c.row;
+  CUtensorMap mw, mx;
+  cudaError_t e = tmap::bf16_2d(&mw, const_cast<void*>(a.w), a.N, a.K, a.ldw, gemm::BM, gemm::BK);
+  if (e != cudaSuccess) return e;
+  e = tmap::bf16_2d(&mx, const_cast<void*>(a.x), a.M, a.K, a.ldx, BN, gemm::BK);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)tiles, 1, (unsigned)p.splits);
+  return cps == 1 ? gemm::launch<BN, 1, true>(mw, mx, p, grid, stream, v)
+                  : gemm::launch<BN, 2, true>(mw, mx, p, grid, stream, v);
 }
 
 }  // namespace es

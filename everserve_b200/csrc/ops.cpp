@@ -148,6 +148,63 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
 }
 
+es::CommArgs comm_args(torch::Tensor peers, torch::Tensor order, torch::Tensor call, int64_t ctrl, int64_t row) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong && peers.numel() >= 8, "peers: int64[8] on the device");
+  TORCH_CHECK(order.is_cuda() && order.scalar_type() == at::kInt && order.numel() >= 9, "order: int32[9] on the device");
+  TORCH_CHECK(call.is_cuda() && call.scalar_type() == at::kInt && call.numel() >= 2, "call: int32[2] on the device");
+  TORCH_CHECK(ctrl != 0 && row >= 0 && row < 8, "control words and row");
+  es::CommArgs c{};
+  c.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  c.order = order.data_ptr<int32_t>();
+  c.call = reinterpret_cast<uint32_t*>(call.data_ptr<int32_t>());
+  c.ctrl = reinterpret_cast<void*>(ctrl);
+  c.row = (int)row;
+  return c;
+}
+
+void fdar(torch::Tensor inp, torch::Tensor out, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
+          int64_t ctrl, int64_t row) {
+  check_bf16(inp, "inp");
+  check_bf16(out, "out");
+  TORCH_CHECK(inp.is_contiguous() && out.is_contiguous() && inp.numel() == out.numel(), "contiguous, same size");
+  const c10::cuda::CUDAGuard g(inp.device());
+  ES_CHECK_CUDA(es::launch_fdar(inp.data_ptr(), out.data_ptr(), inp.numel(), comm_args(peers, order, call, ctrl, row),
+                                cur()));
+}
+
+void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
+                    torch::Tensor status, int64_t num_sms, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
+                    int64_t ctrl, int64_t row) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D operands");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "K-contiguous operands");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N, "shapes");
+  TORCH_CHECK(M <= 64, "the fused all-reduce GEMM takes decode batches (M <= 64)");
+  es::GemmArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.out = out.data_ptr();
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ldx = x.stride(0);
+  a.ldw = w.stride(0);
+  a.ldo = out.stride(0);
+  a.status = status.data_ptr<int>();
+  a.num_sms = (int)num_sms;
+  if (residual.has_value()) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N && residual->stride(1) == 1, "residual shape");
+    a.residual = residual->data_ptr();
+    a.ldr = residual->stride(0);
+  }
+  const c10::cuda::CUDAGuard g(x.device());
+  ES_CHECK_CUDA(es::launch_gemm_allreduce(a, comm_args(peers, order, call, ctrl, row), cur()));
+}
+
 void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
                   torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor status,
                   int64_t max_splits, int64_t part_tokens, double scale, int64_t stages) {
@@ -276,6 +333,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ws_floats", &es::gemm_ws_floats);
   m.def("gemm_sync_words", &es::gemm_sync_words);
   m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
+  m.def("fdar", &fdar, "failure-detecting all-reduce over peer memory (member order)");
+  m.def("gemm_allreduce", &gemm_allreduce, "row-parallel GEMM with the all-reduce fused into its epilogue");
+  m.def("comm_buffer_bytes", &es::comm_buffer_bytes);
+  m.def("comm_max_elems", &es::comm_max_elems);
   m.def("kv_gather", [](torch::Tensor lp, torch::Tensor s, torch::Tensor h, int64_t st, int64_t cap, int64_t d,
                         int64_t bs, std::vector<int64_t> str, int64_t el) { kv_copy(true, lp, s, h, st, cap, d, bs, str, el); },
         "paged cache -> staging rows, all layers in one launch");

@@ -1,0 +1,187 @@
+"""The tensor-parallel collective on peer memory: fused GEMM + all-reduce and a failure-detecting
+all-reduce, with NCCL for what the kernels do not take.
+
+One instance per rank. It owns the rank's symmetric buffer (device memory outside torch's
+allocator, exported by CUDA IPC), maps every member's buffer, and keeps three small device tables
+the kernels read on every launch (so captured CUDA graphs follow membership changes): the member
+buffers' addresses, the member order, and the call counter. Its control words live in the slot
+region (``parallel.slot``), mapped into the device.
+
+Implements the reference's slot-collective protocol (core/everserve/comm/slot.py:22-48):
+``can_take``, ``all_reduce_into``, ``set_members``, ``abort``, ``resume``, ``variant``.
+"""
+
+from __future__ import annotations
+
+import os
+import uuid
+
+import torch
+import torch.distributed as dist
+
+from .. import _ext
+from .nccl import GroupCollective
+from .slot import MAX_ROWS, SlotRegion
+
+
+class FusedTPCollective:
+    variant = "p2p"
+
+    def __init__(self, device: torch.device, group=None, region: SlotRegion | None = None, row: int | None = None,
+                 members: list[int] | None = None, region_name: str | None = None):
+        self.C = _ext.load()
+        self.device = torch.device(device)
+        self.group = group
+        self.nccl = GroupCollective(group)
+        self.size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.row = self.rank if row is None else row
+        self._own_region = region is None
+        if region is None:
+            name = region_name or self._agree_name()
+            if self.rank == 0:
+                region = SlotRegion.create(name)
+            dist.barrier(group)
+            if self.rank != 0:
+                region = SlotRegion.open(name)
+        self.region = region
+        self.max_elems = int(self.C.comm_max_elems())
+        with torch.cuda.device(self.device):
+            self.region.map_device(self.C)
+            self.ctrl = self.region.ctrl_device(self.row)
+            self.own = int(self.C.device_alloc(int(self.C.comm_buffer_bytes())))
+            self.peers = torch.zeros(MAX_ROWS, dtype=torch.int64, device=self.device)
+            self.order = torch.zeros(1 + MAX_ROWS, dtype=torch.int32, device=self.device)
+            self.call = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.region.set_pid(self.row, os.getpid())
+        self.region.publish(self.row, bytes(self.C.ipc_handle(self.own)))
+        self._addrs = [0] * MAX_ROWS
+        self._addrs[self.row] = self.own
+        self._opened: dict[int, int] = {}
+        self.members = list(members) if members is not None else list(range(self.size))
+        dist.barrier(group)
+        self._open(self.members)
+        self._write_order()
+        self._counting = None
+
+    def _agree_name(self) -> str:
+        obj = [f"es_slot_{os.getpid()}_{uuid.uuid4().hex[:8]}"]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(self.group, 0) if self.group else 0, group=self.group)
+        return obj[0]
+
+    # ---- tables --------------------------------------------------------------------------------
+    def _open(self, rows) -> None:
+        changed = False
+        for r in rows:
+            if r == self.row or r in self._opened:
+                continue
+            with torch.cuda.device(self.device):
+                self._opened[r] = int(self.C.ipc_open(self.region.handle(r)))
+            self._addrs[r] = self._opened[r]
+            changed = True
+        with torch.cuda.device(self.device):
+            self.peers.copy_(torch.tensor(self._addrs, dtype=torch.int64))
+        del changed
+
+    def _write_order(self) -> None:
+        rows = [len(self.members), *self.members] + [0] * (MAX_ROWS - len(self.members))
+        self.region.set_order(self.row, self.members)
+        with torch.cuda.device(self.device):
+            self.order.copy_(torch.tensor(rows, dtype=torch.int32))
+
+    def _comm(self):
+        return self.peers, self.order, self.call, self.ctrl, self.row
+
+    # ---- slot-collective protocol --------------------------------------------------------------
+    def can_take(self, t: torch.Tensor) -> bool:
+        return (t.dtype == torch.bfloat16 and t.is_contiguous() and t.device == self.device
+                and t.numel() <= self.max_elems and t.data_ptr() % 16 == 0)
+
+    def all_reduce_into(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        if self.can_take(inp) and out.is_contiguous() and out.data_ptr() % 16 == 0:
+            self.C.fdar(inp, out, *self._comm())
+            return out
+        if out.data_ptr() != inp.data_ptr():
+            out.copy_(inp)
+        return self.nccl.all_reduce(out)
+
+    def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        return self.all_reduce_into(t, t)
+
+    def linear_allreduce(self, ops, x: torch.Tensor, w: torch.Tensor, residual=None) -> torch.Tensor:
+        """Row-parallel linear summed over the members; one fused kernel at decode sizes."""
+        if x.shape[0] <= 64 and x.dtype == torch.bfloat16:
+            out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+            self.C.gemm_allreduce(x, w, out, residual, ops.status, ops.num_sms, *self._comm())
+            return out
+        y = self.all_reduce(ops.linear(x, w))
+        if residual is not None:
+            y = (y.float() + residual.float()).to(y.dtype)
+        return y
+
+    def all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        return self.nccl.all_gather(t)
+
+    def set_members(self, members, epoch: int = 0) -> None:
+        """Program the member order (rows in rank position); call with this member quiescent."""
+        del epoch
+        self.members = [int(m) for m in members]
+        self._open(self.members)
+        self._write_order()
+
+    def abort(self) -> None:
+        self.region.set_abort([self.row], 1)
+
+    def resume(self) -> None:
+        """Zero the call counter and this member's own buffer once the stream is idle."""
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            self.call.zero_()
+            self.C.memset_async(self.own, int(self.C.comm_buffer_bytes()))
+            torch.cuda.synchronize(self.device)
+        self.region.clear_late(self.row)
+        self.region.set_abort([self.row], 0)
+
+    def status(self) -> int:
+        return self.region.status(self.row)
+
+    def late_rows(self) -> list[int]:
+        m = self.region.late(self.row)
+        return [r for r in range(MAX_ROWS) if m >> r & 1]
+
+    def set_bound_ns(self, ns: int) -> None:
+        self.region.set_bound_ns([self.row], ns)
+
+    def count_launches(self, counts) -> None:
+        """Bench hook: count this collective's kernel launches into counts['n'] (None stops)."""
+        if counts is None:
+            if self._counting is not None:
+                self.C = self._counting
+                self._counting = None
+            return
+        real = self.C
+        self._counting = real
+
+        class Counting:
+            def __getattr__(self, name):
+                fn = getattr(real, name)
+                if name in ("fdar", "gemm_allreduce"):
+                    def wrapped(*a, **k):
+                        counts["n"] += 1
+                        return fn(*a, **k)
+                    return wrapped
+                return fn
+
+        self.C = Counting()
+
+    def close(self) -> None:
+        for p in self._opened.values():
+            try:
+                self.C.ipc_close(p)
+            except RuntimeError:
+                pass
+        self._opened.clear()
+        if self.own:
+            self.C.device_free(self.own)
+            self.own = 0
+        self.region.close(self.C, unlink=self._own_region and self.rank == 0)
