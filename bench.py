@@ -241,6 +241,12 @@ def main() -> None:
     }
     if rank == 0:
         print(json.dumps(out), flush=True)
+    # graphs that hold NCCL calls go before the process group, or its teardown waits for them
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    eng.shutdown()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

@@ -25,7 +25,9 @@ cudaError_t launch_argmax(const void* logits, int64_t* out, int64_t rows, int vo
 
 // ---- comm.cu (peer-memory collectives; layout in comm.cuh) ----------------------------------
 struct CommArgs {
+  uint32_t* seqs;         // device [2 * 4096]: LL call counters of this member
   const uint64_t* peers;  // device [8]: each row's symmetric buffer (0 = unmapped)
+  uint64_t mc;            // NVLS multicast address of the buffers (0: P2P stores)
   const int32_t* order;   // device [9]: member count, rows in member order
   uint32_t* call;         // device [2]: call counter, CTAs finished in the current call
   void* ctrl;             // device address of this member's host-mapped control words
@@ -33,6 +35,7 @@ struct CommArgs {
 };
 int64_t comm_buffer_bytes();
 int64_t comm_max_elems();
+int64_t comm_ll_max_elems();
 cudaError_t launch_fdar(const void* inp, void* out, int64_t n, const CommArgs& c, cudaStream_t s);
 
 // ---- gemm.cu -------------------------------------------------------------------------------------

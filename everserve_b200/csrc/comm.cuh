@@ -32,7 +32,13 @@ constexpr int kMaxRows = 8;            // members: up to seven ranks and a spare
 constexpr int kFlagSlots = 4096;
 constexpr size_t kDataBytes = 1 << 21;  // 2 MiB per sender per parity
 constexpr size_t kFlagBytes = (size_t)2 * kMaxRows * kFlagSlots * 4;
-constexpr size_t kBufferBytes = kFlagBytes + (size_t)2 * kMaxRows * kDataBytes;
+// LL regions: 8-byte words (seq << 32 | two bf16). The GEMM epilogue's words, then small fdar's.
+constexpr size_t kLLGemmBytes = 1 << 21;  // per sender per parity: tiles * 64 * 128 / 2 words
+constexpr size_t kLLSmallBytes = 1 << 21; // per sender per parity: 256 Ki words = 512 Ki elements
+constexpr size_t kLLGemmOff = kFlagBytes + (size_t)2 * kMaxRows * kDataBytes;
+constexpr size_t kLLSmallOff = kLLGemmOff + (size_t)2 * kMaxRows * kLLGemmBytes;
+constexpr size_t kBufferBytes = kLLSmallOff + (size_t)2 * kMaxRows * kLLSmallBytes;
+constexpr int kSeqSlots = 4096;  // per-slot LL call counters (this member's device memory)
 constexpr uint64_t kHardLimitNs = 5000000000ull;  // a wait never outlives 5 s
 
 // Host-mapped control words of one member (pinned host memory the device reads and writes).
@@ -46,12 +52,82 @@ struct Ctrl {
 
 // Device view of a member's place in the group (kernel parameter, by value).
 struct View {
+  uint32_t* seqs;         // [2 * kSeqSlots] LL call counters: GEMM slots, then small-fdar blocks
   const uint64_t* peers;  // [kMaxRows] base address of each row's buffer (0 = not mapped)
+  uint64_t mc;            // multicast (NVLS) address of the group's buffers; 0: push with P2P stores
   const int32_t* order;   // [1 + kMaxRows]: count, rows in member order
   uint32_t* call;         // [2]: call counter, CTAs done in the current call
   Ctrl* ctrl;             // host-mapped control words of this member (device address)
   int row;                // this member's row
 };
+
+// ---- NVLS multicast stores: one store reaches the same offset of every member's buffer ------------
+ES_DEVICE void mc_st_v4(void* mc_addr, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr), "f"(__uint_as_float(v.x)),
+               "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)), "f"(__uint_as_float(v.w))
+               : "memory");
+}
+ES_DEVICE void mc_st_v2(void* mc_addr, uint2 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(mc_addr), "f"(__uint_as_float(v.x)),
+               "f"(__uint_as_float(v.y))
+               : "memory");
+}
+ES_DEVICE void mc_st_release_u32(void* mc_addr, uint32_t v) {
+  asm volatile("multimem.st.release.sys.global.u32 [%0], %1;" ::"l"(mc_addr), "r"(v) : "memory");
+}
+// Order this thread's accesses through the multicast alias against unicast accesses to the buffer.
+ES_DEVICE void fence_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
+ES_DEVICE uint64_t* ll_gemm_ptr(uint64_t base, uint32_t parity, int sender) {
+  return reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(base) + kLLGemmOff +
+                                     ((size_t)parity * kMaxRows + sender) * kLLGemmBytes);
+}
+ES_DEVICE uint64_t* ll_small_ptr(uint64_t base, uint32_t parity, int sender) {
+  return reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(base) + kLLSmallOff +
+                                     ((size_t)parity * kMaxRows + sender) * kLLSmallBytes);
+}
+ES_DEVICE void st_u64_relaxed(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+ES_DEVICE uint64_t ld_u64_relaxed(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+ES_DEVICE void mc_st_u64(void* mc_addr, uint64_t v) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(mc_addr),
+               "f"(__uint_as_float((uint32_t)v)), "f"(__uint_as_float((uint32_t)(v >> 32)))
+               : "memory");
+}
+
+// Poll one LL word of `sender` until it carries `seq`; returns its two bf16 (as bits) or reports
+// a failure through `fail` (aborted / hard limit). `t0`, `named` and `spins` persist per thread.
+ES_DEVICE uint32_t ll_wait(const View& v, const uint64_t* w, uint32_t seq, int sender, uint64_t& t0, bool& named,
+                           uint32_t& spins, int& fail) {
+  uint64_t x = ld_u64_relaxed(w);
+  while ((uint32_t)(x >> 32) != seq) {
+    if ((++spins & 1023u) == 0) {
+      volatile Ctrl* c = v.ctrl;
+      if (t0 == 0) t0 = global_ns();
+      if (c->abort) {
+        fail = kAborted;
+        return 0;
+      }
+      const uint64_t now = global_ns() - t0;
+      const uint64_t bound = c->bound_ns;
+      if (!named && bound != 0 && now > bound) {
+        c->late = c->late | (1u << sender);
+        named = true;
+      }
+      if (now > kHardLimitNs) {
+        fail = kTimeout;
+        return 0;
+      }
+    }
+    x = ld_u64_relaxed(w);
+  }
+  return (uint32_t)x;
+}
 
 ES_DEVICE uint32_t* flag_ptr(uint64_t base, uint32_t parity, int sender, int slot) {
   return reinterpret_cast<uint32_t*>(base) + ((size_t)parity * kMaxRows + sender) * kFlagSlots + slot;
@@ -91,6 +167,7 @@ ES_DEVICE int wait_members(const View& v, uint64_t my_base, uint32_t parity, int
       }
     }
   }
+  if (v.mc) fence_alias();
   return kOk;
 }
 

@@ -89,7 +89,6 @@ __global__ void __launch_bounds__(kThreads, CPS)
   if (threadIdx.x == 0) {
     s_fail = 0;
     if (kAR) {
-      s_seq = cv.call[0] + 1;
       const int cnt = cv.order[0];
       s_count = cnt < 0 ? 0 : (cnt > comm::kMaxRows ? comm::kMaxRows : cnt);
       for (int i = 0; i < s_count; i++) s_order[i] = cv.order[1 + i];
@@ -185,8 +184,15 @@ __global__ void __launch_bounds__(kThreads, CPS)
     const int mcount = min(BN, mrem);
     const int total = span4 * mcount;
     const uint32_t local = ptx::smem_u32(partial);
-    const uint32_t seq = kAR ? s_seq : 0u, parity = seq & 1u;
     const int slot = blockIdx.x * S + (int)rank;
+    if (kAR) {
+      if (threadIdx.x == 0) {
+        s_seq = cv.seqs[slot] + 1;  // this slot's call number (every member makes the same calls)
+        cv.seqs[slot] = s_seq;
+      }
+      __syncthreads();
+    }
+    const uint32_t seq = kAR ? s_seq : 0u, parity = seq & 1u;
     for (int e = threadIdx.x; e < total; e += kThreads) {
       const int col = e / span4, row = r0 + (e % span4) * 4;
       const uint32_t off = (uint32_t)((col * BM + row) * 4);
@@ -199,11 +205,22 @@ __global__ void __launch_bounds__(kThreads, CPS)
         acc.w += v.w;
       }
       if (kAR) {
-        // this member's bf16 partial (what an unfused GEMM would output) to every member
-        const uint2 packed = make_uint2(ptx::pack_bf16x2(acc.x, acc.y), ptx::pack_bf16x2(acc.z, acc.w));
-        const size_t boff = ((size_t)(blockIdx.x * BN + col) * BM + row) * 2;
-        for (int k = 0; k < s_count; k++)
-          *reinterpret_cast<uint2*>(comm::data_ptr(cv.peers[s_order[k]], parity, cv.row) + boff) = packed;
+        // this member's bf16 partial (what an unfused GEMM would output) as two LL words, to every
+        // member: each word carries the call number, so it is its own arrival flag
+        const size_t widx = ((size_t)(blockIdx.x * BN + col) * BM + row) / 2;
+        const uint64_t w0 = ((uint64_t)seq << 32) | ptx::pack_bf16x2(acc.x, acc.y);
+        const uint64_t w1 = ((uint64_t)seq << 32) | ptx::pack_bf16x2(acc.z, acc.w);
+        if (cv.mc) {
+          uint64_t* d = comm::ll_gemm_ptr(cv.mc, parity, cv.row) + widx;
+          comm::mc_st_u64(d, w0);
+          comm::mc_st_u64(d + 1, w1);
+        } else {
+          for (int k = 0; k < s_count; k++) {
+            uint64_t* d = comm::ll_gemm_ptr(cv.peers[s_order[k]], parity, cv.row) + widx;
+            comm::st_u64_relaxed(d, w0);
+            comm::st_u64_relaxed(d + 1, w1);
+          }
+        }
         continue;
       }
       const size_t m = (size_t)(m0 + col);
@@ -218,40 +235,42 @@ __global__ void __launch_bounds__(kThreads, CPS)
       }
     }
     if (kAR) {
-      __threadfence_system();
-      __syncthreads();
-      if (threadIdx.x < s_count)
-        st_release_sys(comm::flag_ptr(cv.peers[s_order[threadIdx.x]], parity, cv.row, slot), seq);
+      // sum every member's words in member order (polling the words themselves)
       const uint64_t my_base = cv.peers[cv.row];
-      if (threadIdx.x == 0) {
-        const int w = comm::wait_members(cv, my_base, parity, slot, seq, s_order, s_count);
-        if (w != kOk) s_fail = w;
-      }
-      __syncthreads();
-      if (s_fail == kOk) {
-        for (int e = threadIdx.x; e < total; e += kThreads) {
-          const int col = e / span4, row = r0 + (e % span4) * 4;
-          const size_t boff = ((size_t)(blockIdx.x * BN + col) * BM + row) * 2;
-          float o[4] = {0.f, 0.f, 0.f, 0.f};
-          for (int k = 0; k < s_count; k++) {
-            const uint2 w = *reinterpret_cast<const uint2*>(comm::data_ptr(my_base, parity, s_order[k]) + boff);
-            const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
-            const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
-            o[0] += lo.x;
-            o[1] += lo.y;
-            o[2] += hi.x;
-            o[3] += hi.y;
-          }
-          const size_t m = (size_t)(m0 + col);
+      uint64_t t0 = 0;
+      bool named = false;
+      uint32_t spins = 0;
+      int fail = kOk;
+      for (int e = threadIdx.x; e < total && fail == kOk; e += kThreads) {
+        const int col = e / span4, row = r0 + (e % span4) * 4;
+        const size_t widx = ((size_t)(blockIdx.x * BN + col) * BM + row) / 2;
+        float o[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int k = 0; k < s_count && fail == kOk; k++) {
+          const uint64_t* src = comm::ll_gemm_ptr(my_base, parity, s_order[k]) + widx;
+          const uint32_t a = comm::ll_wait(cv, src, seq, s_order[k], t0, named, spins, fail);
+          const uint32_t b = comm::ll_wait(cv, src + 1, seq, s_order[k], t0, named, spins, fail);
+          const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a));
+          const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b));
+          o[0] += lo.x;
+          o[1] += lo.y;
+          o[2] += hi.x;
+          o[3] += hi.y;
+        }
+        if (fail != kOk) break;
+        const size_t m = (size_t)(m0 + col);
 #pragma unroll
-          for (int z = 0; z < 4; z++) {
-            const int n = n0 + row + z;
-            if (n < p.N) {
-              if (p.residual) o[z] += bf2f(p.residual[m * p.ldr + n]);
-              p.out[m * p.ldo + n] = f2bf(o[z]);
-            }
+        for (int z = 0; z < 4; z++) {
+          const int n = n0 + row + z;
+          if (n < p.N) {
+            if (p.residual) o[z] += bf2f(p.residual[m * p.ldr + n]);
+            p.out[m * p.ldo + n] = f2bf(o[z]);
           }
         }
+      }
+      if (fail != kOk) {
+        s_fail = fail;
+        volatile comm::Ctrl* cw = cv.ctrl;
+        cw->status = (uint32_t)fail;
       }
     }
     ptx::cluster_sync();  // no CTA leaves while another still reads its shared memory
@@ -261,7 +280,6 @@ __global__ void __launch_bounds__(kThreads, CPS)
   if (warp == 1) ptx::tmem_dealloc(tmem, C::kTmemCols);
   if (threadIdx.x == 0) {
     if (s_fail && p.status) atomicExch(p.status, s_fail == kAborted ? (int)kAborted : (int)kTimeout);
-    if (kAR) comm::finish_call(cv, s_seq, s_fail == kAborted ? (int)kAborted : (s_fail ? (int)kTimeout : (int)kOk));
   }
 }
 
@@ -420,7 +438,7 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
     return cudaErrorInvalidValue;
   constexpr int BN = 64;  // one token tile for every decode batch: the plan never depends on M
   const int tiles = (int)((a.N + gemm::BM - 1) / gemm::BM);
-  if ((size_t)tiles * BN * gemm::BM * 2 > comm::kDataBytes) return cudaErrorInvalidValue;
+  if ((size_t)tiles * BN * gemm::BM * 4 > comm::kLLGemmBytes || c.seqs == nullptr) return cudaErrorInvalidValue;
   gemm::Params p{};
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.residual = static_cast<const __nv_bfloat16*>(a.residual);
@@ -449,9 +467,11 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
   }
   if (s_fit <= 0) return cudaErrorInvalidConfiguration;
   p.splits = s_fit;
-  if (tiles * p.splits > comm::kFlagSlots) return cudaErrorInvalidValue;
+  if (tiles * p.splits > comm::kSeqSlots) return cudaErrorInvalidValue;
   comm::View v{};
+  v.seqs = c.seqs;
   v.peers = c.peers;
+  v.mc = c.mc;
   v.order = c.order;
   v.call = c.call;
   v.ctrl = reinterpret_cast<comm::Ctrl*>(c.ctrl);

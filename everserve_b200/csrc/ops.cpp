@@ -148,7 +148,9 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
 }
 
-es::CommArgs comm_args(torch::Tensor peers, torch::Tensor order, torch::Tensor call, int64_t ctrl, int64_t row) {
+es::CommArgs comm_args(torch::Tensor peers, torch::Tensor order, torch::Tensor call, int64_t ctrl, int64_t row,
+                       int64_t mc, torch::Tensor seqs) {
+  TORCH_CHECK(seqs.is_cuda() && seqs.scalar_type() == at::kInt && seqs.numel() >= 8192, "seqs: int32[8192] on the device");
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong && peers.numel() >= 8, "peers: int64[8] on the device");
   TORCH_CHECK(order.is_cuda() && order.scalar_type() == at::kInt && order.numel() >= 9, "order: int32[9] on the device");
   TORCH_CHECK(call.is_cuda() && call.scalar_type() == at::kInt && call.numel() >= 2, "call: int32[2] on the device");
@@ -159,22 +161,24 @@ es::CommArgs comm_args(torch::Tensor peers, torch::Tensor order, torch::Tensor c
   c.call = reinterpret_cast<uint32_t*>(call.data_ptr<int32_t>());
   c.ctrl = reinterpret_cast<void*>(ctrl);
   c.row = (int)row;
+  c.mc = (uint64_t)mc;
+  c.seqs = reinterpret_cast<uint32_t*>(seqs.data_ptr<int32_t>());
   return c;
 }
 
 void fdar(torch::Tensor inp, torch::Tensor out, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
-          int64_t ctrl, int64_t row) {
+          int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs) {
   check_bf16(inp, "inp");
   check_bf16(out, "out");
   TORCH_CHECK(inp.is_contiguous() && out.is_contiguous() && inp.numel() == out.numel(), "contiguous, same size");
   const c10::cuda::CUDAGuard g(inp.device());
-  ES_CHECK_CUDA(es::launch_fdar(inp.data_ptr(), out.data_ptr(), inp.numel(), comm_args(peers, order, call, ctrl, row),
+  ES_CHECK_CUDA(es::launch_fdar(inp.data_ptr(), out.data_ptr(), inp.numel(), comm_args(peers, order, call, ctrl, row, mc, seqs),
                                 cur()));
 }
 
 void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
                     torch::Tensor status, int64_t num_sms, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
-                    int64_t ctrl, int64_t row) {
+                    int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
@@ -202,7 +206,7 @@ void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::op
     a.ldr = residual->stride(0);
   }
   const c10::cuda::CUDAGuard g(x.device());
-  ES_CHECK_CUDA(es::launch_gemm_allreduce(a, comm_args(peers, order, call, ctrl, row), cur()));
+  ES_CHECK_CUDA(es::launch_gemm_allreduce(a, comm_args(peers, order, call, ctrl, row, mc, seqs), cur()));
 }
 
 void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
@@ -337,6 +341,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_allreduce", &gemm_allreduce, "row-parallel GEMM with the all-reduce fused into its epilogue");
   m.def("comm_buffer_bytes", &es::comm_buffer_bytes);
   m.def("comm_max_elems", &es::comm_max_elems);
+  m.def("comm_ll_max_elems", &es::comm_ll_max_elems);
   m.def("kv_gather", [](torch::Tensor lp, torch::Tensor s, torch::Tensor h, int64_t st, int64_t cap, int64_t d,
                         int64_t bs, std::vector<int64_t> str, int64_t el) { kv_copy(true, lp, s, h, st, cap, d, bs, str, el); },
         "paged cache -> staging rows, all layers in one launch");

@@ -48,7 +48,14 @@ class LocalExecutor:
         return self.worker.runner.decode_loop(plan, k)
 
     def shutdown(self):
-        pass
+        """Release the graphs, then the collective's peer mappings and buffers."""
+        import gc
+
+        self.worker.runner.release_graphs()
+        gc.collect()
+        coll = self.worker.tp.collective
+        if coll is not None and hasattr(coll, "close"):
+            coll.close()
 
 
 class Engine:

@@ -151,6 +151,14 @@ class ModelRunner:
         self.graphs[b] = g
         self.graph_out[b] = out
 
+    def release_graphs(self) -> None:
+        """Drop every captured graph (a graph holding NCCL calls must go before the process group)."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        self.graphs.clear()
+        self.graph_out.clear()
+        self._pool = None
+
     def capture_all(self) -> None:
         if not self.use_graphs:
             return

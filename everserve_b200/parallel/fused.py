@@ -25,10 +25,14 @@ from .slot import MAX_ROWS, SlotRegion
 
 
 class FusedTPCollective:
-    variant = "p2p"
+    """``nvls=True`` pushes through an NVSwitch multicast mapping of the members' buffers (one copy
+    leaves each GPU); the buffers then come from torch's symmetric-memory rendezvous and the
+    members are fixed (rows = ranks). The default P2P variant pushes with stores into each
+    member's IPC-mapped buffer and supports membership changes; it is the one used wherever a
+    member may die (a dead process bound to a multicast object is not survivable on this pool)."""
 
     def __init__(self, device: torch.device, group=None, region: SlotRegion | None = None, row: int | None = None,
-                 members: list[int] | None = None, region_name: str | None = None):
+                 members: list[int] | None = None, region_name: str | None = None, nvls: bool = False):
         self.C = _ext.load()
         self.device = torch.device(device)
         self.group = group
@@ -46,23 +50,52 @@ class FusedTPCollective:
                 region = SlotRegion.open(name)
         self.region = region
         self.max_elems = int(self.C.comm_max_elems())
+        self.nvls = bool(nvls)
+        self.mc = 0
+        self._symm = None
+        self._addrs = [0] * MAX_ROWS
+        self._opened: dict[int, int] = {}
+        nbytes = int(self.C.comm_buffer_bytes())
         with torch.cuda.device(self.device):
             self.region.map_device(self.C)
             self.ctrl = self.region.ctrl_device(self.row)
-            self.own = int(self.C.device_alloc(int(self.C.comm_buffer_bytes())))
             self.peers = torch.zeros(MAX_ROWS, dtype=torch.int64, device=self.device)
             self.order = torch.zeros(1 + MAX_ROWS, dtype=torch.int32, device=self.device)
             self.call = torch.zeros(2, dtype=torch.int32, device=self.device)
+            self.seqs = torch.zeros(8192, dtype=torch.int32, device=self.device)
+            if self.nvls:
+                import torch.distributed._symmetric_memory as symm_mem
+
+                self._symm = symm_mem.empty(nbytes, dtype=torch.uint8, device=self.device)
+                self._symm.zero_()
+                torch.cuda.synchronize(self.device)
+                name = (group or dist.group.WORLD).group_name
+                h = symm_mem.rendezvous(self._symm, name)
+                self.mc = int(getattr(h, "multicast_ptr", 0) or 0)
+                if not self.mc:
+                    raise RuntimeError("no NVLS multicast mapping for this group")
+                for r, ptr in enumerate(h.buffer_ptrs):
+                    self._addrs[r] = int(ptr)
+                self.own = self._addrs[self.row]
+            else:
+                self.own = int(self.C.device_alloc(nbytes))
+                self._addrs[self.row] = self.own
         self.region.set_pid(self.row, os.getpid())
-        self.region.publish(self.row, bytes(self.C.ipc_handle(self.own)))
-        self._addrs = [0] * MAX_ROWS
-        self._addrs[self.row] = self.own
-        self._opened: dict[int, int] = {}
+        if not self.nvls:
+            self.region.publish(self.row, bytes(self.C.ipc_handle(self.own)))
         self.members = list(members) if members is not None else list(range(self.size))
         dist.barrier(group)
-        self._open(self.members)
+        if self.nvls:
+            with torch.cuda.device(self.device):
+                self.peers.copy_(torch.tensor(self._addrs, dtype=torch.int64))
+        else:
+            self._open(self.members)
         self._write_order()
         self._counting = None
+        if self.nvls:
+            self.variant = "nvls"
+        else:
+            self.variant = "p2p"
 
     def _agree_name(self) -> str:
         obj = [f"es_slot_{os.getpid()}_{uuid.uuid4().hex[:8]}"]
@@ -90,7 +123,7 @@ class FusedTPCollective:
             self.order.copy_(torch.tensor(rows, dtype=torch.int32))
 
     def _comm(self):
-        return self.peers, self.order, self.call, self.ctrl, self.row
+        return self.peers, self.order, self.call, self.ctrl, self.row, self.mc, self.seqs
 
     # ---- slot-collective protocol --------------------------------------------------------------
     def can_take(self, t: torch.Tensor) -> bool:
@@ -125,6 +158,8 @@ class FusedTPCollective:
     def set_members(self, members, epoch: int = 0) -> None:
         """Program the member order (rows in rank position); call with this member quiescent."""
         del epoch
+        if self.nvls and list(members) != self.members:
+            raise RuntimeError("the NVLS variant has fixed members; use the P2P variant for membership changes")
         self.members = [int(m) for m in members]
         self._open(self.members)
         self._write_order()
@@ -137,7 +172,11 @@ class FusedTPCollective:
         with torch.cuda.device(self.device):
             torch.cuda.synchronize(self.device)
             self.call.zero_()
-            self.C.memset_async(self.own, int(self.C.comm_buffer_bytes()))
+            self.seqs.zero_()
+            if self._symm is not None:
+                self._symm.zero_()
+            else:
+                self.C.memset_async(self.own, int(self.C.comm_buffer_bytes()))
             torch.cuda.synchronize(self.device)
         self.region.clear_late(self.row)
         self.region.set_abort([self.row], 0)
@@ -181,7 +220,8 @@ class FusedTPCollective:
             except RuntimeError:
                 pass
         self._opened.clear()
-        if self.own:
+        if self.own and not self.nvls:
             self.C.device_free(self.own)
-            self.own = 0
+        self.own = 0
+        self._symm = None
         self.region.close(self.C, unlink=self._own_region and self.rank == 0)
