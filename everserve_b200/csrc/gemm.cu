@@ -354,12 +354,12 @@ int64_t gemm_pick_bn(int64_t M) {
 }
 
 // Cluster split for an N x K weight at decode sizes: as many CTAs per tile as the SM slots allow,
-// at most 16 (the non-portable cluster limit) and at least 4 k-blocks each. One CTA per SM with a
+// at most 8 (the portable cluster size) and at least 4 k-blocks each. One CTA per SM with a
 // deep ring when that still splits each tile 4 ways (or as far as two per SM would, with no more
 // tiles than SMs); otherwise two per SM. A function of (N, K, #SMs) only.
 static int64_t split_for(int64_t tiles, int64_t kb, int64_t slots) {
   int64_t s = std::max<int64_t>(1, slots / tiles);
-  s = std::min<int64_t>(s, 16);
+  s = std::min<int64_t>(s, 8);  // portable cluster size: a cluster of 16 needs 16 free SMs in one GPC
   s = std::min<int64_t>(s, std::max<int64_t>(1, kb / 4));
   while (s > 1 && (kb + s - 1) / s * (s - 1) >= kb) s--;  // every split holds k-blocks
   return s;

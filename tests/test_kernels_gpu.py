@@ -82,6 +82,8 @@ GEMM_SHAPES = [
     (1, 128, 64), (7, 200, 256), (16, 4096, 4096), (33, 6144, 4096), (64, 4096, 14336),
     (64, 28672, 4096), (100, 512, 1024), (256, 1024, 512), (300, 768, 4096), (1000, 4096, 896),
     (64, 4096, 512), (64, 1000, 1792), (5, 384, 4104),
+    # tensor-parallel-8 shapes of the 8B model: qkv (6 tiles), o, gate_up, down, lm_head shard
+    (64, 768, 4096), (64, 4096, 512), (64, 3584, 4096), (64, 4096, 1792), (64, 16032, 4096),
 ]
 
 
