@@ -1,0 +1,235 @@
+#include "telemetry.h"
+
+#include <poll.h>
+#include <sys/socket.h>
+#include <unistd.h>
+
+#include <cstring>
+
+#include "net.h"
+
+namespace es {
+
+static const double kBuckets[] = {0.0005, 0.001, 0.0025, 0.005, 0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1, 2.5, 5, 10, 30};
+constexpr int kNBuckets = sizeof(kBuckets) / sizeof(kBuckets[0]);
+
+Registry& metrics() {
+  static Registry r;
+  return r;
+}
+
+std::string Registry::key(const Labels& l) {
+  std::string k;
+  for (size_t i = 0; i < l.size(); i++) {
+    k += (i ? "," : "") + l[i].first + "=\"";
+    for (char c : l[i].second) {
+      if (c == '"' || c == '\\') k.push_back('\\');
+      k.push_back(c == '\n' ? ' ' : c);
+    }
+    k += "\"";
+  }
+  return k;
+}
+
+void Registry::describe(const std::string& name, const std::string& help, const std::string& type) {
+  std::lock_guard<std::mutex> g(mu_);
+  meta_[name] = {help, type};
+}
+
+void Registry::inc(const std::string& name, const Labels& l, double v) {
+  std::lock_guard<std::mutex> g(mu_);
+  values_[name][key(l)] += v;
+}
+
+void Registry::set(const std::string& name, const Labels& l, double v) {
+  std::lock_guard<std::mutex> g(mu_);
+  values_[name][key(l)] = v;
+}
+
+void Registry::observe(const std::string& name, const Labels& l, double v) {
+  std::lock_guard<std::mutex> g(mu_);
+  Hist& h = hists_[name][key(l)];
+  if (h.counts.empty()) h.counts.assign(kNBuckets, 0);
+  for (int i = 0; i < kNBuckets; i++)
+    if (v <= kBuckets[i]) h.counts[i] += 1;
+  h.sum += v;
+  h.n += 1;
+}
+
+double Registry::value(const std::string& name, const Labels& l) const {
+  std::lock_guard<std::mutex> g(mu_);
+  auto it = values_.find(name);
+  if (it == values_.end()) return 0;
+  auto jt = it->second.find(key(l));
+  return jt == it->second.end() ? 0 : jt->second;
+}
+
+std::string Registry::exposition() const {
+  std::lock_guard<std::mutex> g(mu_);
+  std::string o;
+  auto header = [&](const std::string& name, const char* dflt_type) {
+    auto m = meta_.find(name);
+    if (m != meta_.end()) {
+      o += "# HELP " + name + " " + m->second.first + "\n# TYPE " + name + " " + m->second.second + "\n";
+    } else {
+      o += "# TYPE " + name + " " + dflt_type + "\n";
+    }
+  };
+  for (auto& kv : values_) {
+    header(kv.first, "gauge");
+    for (auto& s : kv.second) {
+      char num[64];
+      snprintf(num, sizeof(num), "%.17g", s.second);
+      o += kv.first + (s.first.empty() ? "" : "{" + s.first + "}") + " " + num + "\n";
+    }
+  }
+  for (auto& kv : hists_) {
+    header(kv.first, "histogram");
+    for (auto& s : kv.second) {
+      const std::string sep = s.first.empty() ? "" : ",";
+      for (int i = 0; i < kNBuckets; i++) {
+        char le[32];
+        snprintf(le, sizeof(le), "%g", kBuckets[i]);
+        o += kv.first + "_bucket{" + s.first + sep + "le=\"" + le + "\"} " + std::to_string((uint64_t)s.second.counts[i]) +
+             "\n";
+      }
+      o += kv.first + "_bucket{" + s.first + sep + "le=\"+Inf\"} " + std::to_string(s.second.n) + "\n";
+      char sum[64];
+      snprintf(sum, sizeof(sum), "%.17g", s.second.sum);
+      o += kv.first + "_sum" + (s.first.empty() ? "" : "{" + s.first + "}") + " " + sum + "\n";
+      o += kv.first + "_count" + (s.first.empty() ? "" : "{" + s.first + "}") + " " + std::to_string(s.second.n) + "\n";
+    }
+  }
+  return o;
+}
+
+static bool read_request(int fd, HttpRequest& req) {
+  std::string buf;
+  char tmp[8192];
+  size_t header_end = std::string::npos;
+  while (header_end == std::string::npos) {
+    pollfd pf{fd, POLLIN, 0};
+    if (::poll(&pf, 1, 2000) <= 0) return false;
+    const ssize_t n = ::recv(fd, tmp, sizeof(tmp), 0);
+    if (n <= 0) return false;
+    buf.append(tmp, size_t(n));
+    header_end = buf.find("\r\n\r\n");
+    if (buf.size() > (1 << 20)) return false;
+  }
+  const auto line_end = buf.find("\r\n");
+  const std::string line = buf.substr(0, line_end);
+  const auto sp1 = line.find(' '), sp2 = line.rfind(' ');
+  if (sp1 == std::string::npos || sp2 == sp1) return false;
+  req.method = line.substr(0, sp1);
+  req.path = line.substr(sp1 + 1, sp2 - sp1 - 1);
+  size_t content_len = 0;
+  std::string headers = buf.substr(line_end + 2, header_end - line_end - 2);
+  for (size_t p = 0; p < headers.size();) {
+    size_t e = headers.find("\r\n", p);
+    if (e == std::string::npos) e = headers.size();
+    std::string h = headers.substr(p, e - p);
+    for (auto& c : h) c = (char)tolower(c);
+    if (h.rfind("content-length:", 0) == 0) content_len = (size_t)atol(h.substr(15).c_str());
+    p = e + 2;
+  }
+  req.body = buf.substr(header_end + 4);
+  while (req.body.size() < content_len) {
+    pollfd pf{fd, POLLIN, 0};
+    if (::poll(&pf, 1, 2000) <= 0) return false;
+    const ssize_t n = ::recv(fd, tmp, sizeof(tmp), 0);
+    if (n <= 0) return false;
+    req.body.append(tmp, size_t(n));
+  }
+  return true;
+}
+
+static const char* reason(int s) {
+  switch (s) {
+    case 200: return "OK";
+    case 201: return "Created";
+    case 400: return "Bad Request";
+    case 404: return "Not Found";
+    case 409: return "Conflict";
+    default: return "Error";
+  }
+}
+
+bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::string* err) {
+  Address a;
+  if (!Address::parse(addr, a)) {
+    if (err) *err = "bad address " + addr;
+    return false;
+  }
+  const int lfd = listen_on(a, err);
+  if (lfd < 0) return false;
+  loop.watch(lfd, [lfd, route]() {
+    while (true) {
+      const int fd = ::accept4(lfd, nullptr, nullptr, SOCK_CLOEXEC);
+      if (fd < 0) return;
+      HttpRequest req;
+      HttpResponse resp;
+      if (!read_request(fd, req)) {
+        ::close(fd);
+        continue;
+      }
+      const std::string path = req.path.substr(0, req.path.find('?'));
+      if (req.method == "GET" && path == "/metrics") {
+        resp.body = metrics().exposition();
+      } else if (req.method == "GET" && path == "/healthz") {
+        resp.body = "ok\n";
+      } else if (!(route && route(req, resp))) {
+        resp.status = 404;
+        resp.body = "not found\n";
+      }
+      std::string out = "HTTP/1.1 " + std::to_string(resp.status) + " " + reason(resp.status) +
+                        "\r\nContent-Type: " + resp.content_type + "\r\nContent-Length: " + std::to_string(resp.body.size()) +
+                        "\r\nConnection: close\r\n\r\n" + resp.body;
+      size_t off = 0;
+      while (off < out.size()) {
+        const ssize_t w = ::send(fd, out.data() + off, out.size() - off, MSG_NOSIGNAL);
+        if (w <= 0) break;
+        off += size_t(w);
+      }
+      ::close(fd);
+    }
+  });
+  return true;
+}
+
+int http_request(const std::string& addr, const std::string& method, const std::string& path, const std::string& body,
+                 std::string& out) {
+  Address a;
+  if (!Address::parse(addr, a)) return -1;
+  const int fd = connect_to(a, 3000);
+  if (fd < 0) return -1;
+  std::string req = method + " " + path + " HTTP/1.1\r\nHost: " + a.host + "\r\nContent-Length: " +
+                    std::to_string(body.size()) + "\r\nConnection: close\r\n\r\n" + body;
+  size_t off = 0;
+  while (off < req.size()) {
+    const ssize_t w = ::send(fd, req.data() + off, req.size() - off, MSG_NOSIGNAL);
+    if (w < 0) {
+      pollfd pf{fd, POLLOUT, 0};
+      ::poll(&pf, 1, 1000);
+      continue;
+    }
+    off += size_t(w);
+  }
+  std::string resp;
+  char tmp[8192];
+  while (true) {
+    pollfd pf{fd, POLLIN, 0};
+    if (::poll(&pf, 1, 5000) <= 0) break;
+    const ssize_t n = ::recv(fd, tmp, sizeof(tmp), 0);
+    if (n <= 0) break;
+    resp.append(tmp, size_t(n));
+  }
+  ::close(fd);
+  const auto sp = resp.find(' ');
+  if (sp == std::string::npos) return -1;
+  const int status = atoi(resp.c_str() + sp + 1);
+  const auto be = resp.find("\r\n\r\n");
+  out = be == std::string::npos ? "" : resp.substr(be + 4);
+  return status;
+}
+
+}  // namespace es

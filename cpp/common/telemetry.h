@@ -1,0 +1,58 @@
+// Per-process telemetry: a Prometheus registry (counters, gauges, histograms with labels) and a
+// small HTTP endpoint serving /metrics, /healthz and any routes a process adds (the coordinator's
+// operator API). Metric names are stable: add, never rename.
+#pragma once
+
+#include <cstdint>
+#include <functional>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace es {
+
+using Labels = std::vector<std::pair<std::string, std::string>>;
+
+class Registry {
+ public:
+  void describe(const std::string& name, const std::string& help, const std::string& type);
+  void inc(const std::string& name, const Labels& l = {}, double v = 1.0);
+  void set(const std::string& name, const Labels& l, double v);
+  void observe(const std::string& name, const Labels& l, double v);  // histogram (seconds buckets)
+  double value(const std::string& name, const Labels& l = {}) const;
+  std::string exposition() const;
+
+ private:
+  struct Hist {
+    std::vector<double> counts;
+    double sum = 0;
+    uint64_t n = 0;
+  };
+  static std::string key(const Labels& l);
+  mutable std::mutex mu_;
+  std::map<std::string, std::pair<std::string, std::string>> meta_;  // name -> help, type
+  std::map<std::string, std::map<std::string, double>> values_;
+  std::map<std::string, std::map<std::string, Hist>> hists_;
+};
+
+Registry& metrics();
+
+struct HttpRequest {
+  std::string method, path, body;
+};
+struct HttpResponse {
+  int status = 200;
+  std::string content_type = "text/plain; version=0.0.4";
+  std::string body;
+};
+using HttpRoute = std::function<bool(const HttpRequest&, HttpResponse&)>;  // true: handled
+
+class Loop;
+// Serve HTTP on `addr` ("host:port") from `loop`: /metrics, /healthz, then `route`.
+bool serve_http(Loop& loop, const std::string& addr, HttpRoute route = nullptr, std::string* err = nullptr);
+// A blocking HTTP request (used by the CLI); returns the status code, or -1.
+int http_request(const std::string& addr, const std::string& method, const std::string& path, const std::string& body,
+                 std::string& out);
+
+}  // namespace es

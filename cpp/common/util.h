@@ -1,0 +1,55 @@
+// Logging, CRC32C, a small JSON reader, file mapping and process helpers for the control plane.
+#pragma once
+
+#include <cstdint>
+#include <cstdio>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace es {
+
+// ---- logs: text by default, one JSON object per line when EVERSERVE_LOG_FORMAT=json ------------
+void log_init(const char* component);
+void logf(const char* level, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+#define ES_INFO(...) ::es::logf("info", __VA_ARGS__)
+#define ES_WARN(...) ::es::logf("warn", __VA_ARGS__)
+#define ES_ERROR(...) ::es::logf("error", __VA_ARGS__)
+
+// ---- CRC32C (Castagnoli polynomial 0x82F63B78, reflected), table-driven ------------------------
+uint32_t crc32c(const void* data, size_t n, uint32_t crc = 0);
+
+// ---- JSON ----------------------------------------------------------------------------------------
+struct Json {
+  enum Kind { Null, Bool, Number, String, Array, Object } kind = Null;
+  bool b = false;
+  double num = 0;
+  std::string str;
+  std::vector<Json> arr;
+  std::vector<std::pair<std::string, Json>> obj;
+  const Json* get(const std::string& k) const;
+  static bool parse(const std::string& text, Json& out, std::string* err = nullptr);
+  std::string dump() const;
+};
+std::string json_escape(const std::string& s);
+
+// ---- files ---------------------------------------------------------------------------------------
+// A shared file mapping (MAP_SHARED), created at `size` when `create`.
+struct Mapping {
+  void* addr = nullptr;
+  size_t size = 0;
+  std::string path;
+  ~Mapping();
+  static std::unique_ptr<Mapping> open(const std::string& path, size_t size, bool create, std::string* err = nullptr);
+};
+bool mkdirs(const std::string& path, int mode = 0770);
+bool read_file(const std::string& path, std::string& out);
+bool write_file_atomic(const std::string& path, const std::string& data);
+std::string env_or(const char* name, const std::string& dflt);
+
+// ---- processes -----------------------------------------------------------------------------------
+// /proc/<pid>/stat state: 'R','S','D','Z','X',... or 0 when the process does not exist.
+char proc_state(int pid);
+
+}  // namespace es
