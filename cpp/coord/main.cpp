@@ -1,1 +1,781 @@
-int main(){return 0;}
+// everserve-coord: the coordinator, the single writer of membership epochs (one per cluster).
+//
+//   everserve-coord --listen unix:/run/everserve/coord.sock --policy policy.json --spec-store DIR
+//                   [--lease FILE] [--api-addr host:port] [--metrics-addr host:port]
+//                   [--node-loss-misses 3] [--delivery-timeout-ms 130000]
+// Flags also read EVERSERVE_LISTEN, EVERSERVE_POLICY, EVERSERVE_SPEC_STORE, EVERSERVE_LEASE,
+// EVERSERVE_API_ADDR, EVERSERVE_METRICS_ADDR, EVERSERVE_NODE_LOSS_MISSES.
+//
+// Node daemons link to it (coord.proto). From their hellos and worker events it keeps a view of
+// every engine: its epoch, which node holds each rank, and the spares. A loss (a rank reported
+// lost, a worker connection that ended, a node whose heartbeats stopped) folds into the engine's
+// pending losses; the transition machine then
+//   claim    -> chooses the outcome by policy (REPLACE with a spare per lost rank, ...), epoch + 1,
+//   log      -> writes the change to the spec store BEFORE any node hears of it,
+//   deliver  -> one Deliver per node (its surviving ranks, its spares that take ranks),
+//   acks     -> every node answers Delivered with its processes' acks (bounded),
+//   commit   -> MembershipCommitted to every node of the engine, and the spec store is updated;
+// any failure on the way abandons the change (the engine is down; its processes are told).
+// A lease (a locked file holding the term) makes this process the writer; every message to a
+// daemon carries the term, and daemons ignore older terms. On start, a change logged but not
+// committed by an earlier holder is delivered again once the daemons have linked.
+#include <fcntl.h>
+#include <signal.h>
+#include <sys/file.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <deque>
+#include <map>
+#include <set>
+
+#include "everserve_pb.h"
+#include "net.h"
+#include "state.h"
+#include "telemetry.h"
+#include "util.h"
+
+using namespace es;
+
+namespace {
+
+struct Holder {
+  std::string node;
+  uint32_t device = 0;
+  uint32_t pid = 0;
+  std::string host;
+};
+
+struct InFlight {
+  signals::Change change;
+  std::string cause;
+  std::map<std::string, coord::Deliver> deliveries;  // node -> what it was sent
+  std::set<std::string> waiting;                      // nodes that owe Delivered
+  std::vector<signals::Ack> acks;
+  uint64_t reported_us = 0, delivered_us = 0, started_ms = 0;
+  std::vector<std::pair<uint32_t, SpareSeat>> take;
+};
+
+struct Engine {
+  std::string name;
+  uint64_t epoch = 0;
+  uint32_t world = 0;
+  std::map<uint32_t, Holder> workers;
+  std::vector<SpareSeat> spares;
+  std::set<std::string> head_nodes;
+  std::set<uint32_t> pending;
+  std::set<uint32_t> departing;  // planned departures among pending
+  uint64_t first_report_us = 0;
+  std::string cause;
+  bool down = false;
+  std::unique_ptr<InFlight> in_flight;
+};
+
+struct Node {
+  std::string name;
+  uint64_t conn = 0;
+  uint64_t last_seen_ms = 0;
+  uint32_t heartbeat_ms = 500;
+  bool linked = false;
+  bool cordoned = false;
+  int64_t drain_by_ms = 0;
+};
+
+struct Event {
+  uint64_t seq;
+  uint64_t at_ms;
+  std::string text;
+};
+
+struct Coordinator {
+  Loop loop;
+  Policy policy;
+  std::string spec_dir;
+  uint64_t term = 1;
+  uint32_t loss_misses = 3;
+  uint64_t delivery_timeout_ms = 130000;
+  std::map<std::string, Engine> engines;
+  std::map<std::string, Node> nodes;
+  std::map<uint64_t, std::string> conn_node;
+  uint64_t next_request = 1;
+  std::deque<Event> events;
+  uint64_t event_seq = 0;
+
+  void event(const std::string& text) {
+    events.push_back({++event_seq, now_ms(), text});
+    if (events.size() > 4096) events.pop_front();
+    ES_INFO("%s", text.c_str());
+  }
+
+  Engine& engine(const std::string& name) {
+    Engine& e = engines[name];
+    if (e.name.empty()) {
+      e.name = name;
+      e.world = policy.world_size(name);
+    }
+    return e;
+  }
+
+  void to_node(const std::string& node, coord::CoordToDaemon& m) {
+    auto it = nodes.find(node);
+    if (it == nodes.end() || !it->second.linked) return;
+    m.term = term;
+    loop.send(it->second.conn, m.serialize());
+  }
+
+  std::set<std::string> engine_nodes(const Engine& e) {
+    std::set<std::string> out = e.head_nodes;
+    for (auto& [r, h] : e.workers) out.insert(h.node);
+    for (auto& s : e.spares) out.insert(s.node);
+    return out;
+  }
+
+  // ---- spec store ------------------------------------------------------------------------------
+  std::string status_path(const std::string& engine) const { return spec_dir + "/" + engine + ".status"; }
+
+  void write_status(const Engine& e, const InFlight* f, const coord::Committed* committed) {
+    if (spec_dir.empty()) return;
+    spec::EngineStatus st;
+    st.engine = e.name;
+    for (auto& [r, h] : e.workers) {
+      spec::Assignment a;
+      a.rank = r;
+      a.epoch = e.epoch;
+      a.node = h.node;
+      a.host = h.host;
+      st.assignments.push_back(a);
+    }
+    if (f != nullptr) {
+      st.has_change = true;
+      st.change.change = f->change;
+      st.change.has_change = true;
+      st.change.world_size = e.world;
+      st.change.taking = f->change.take;
+      for (auto& [node, d] : f->deliveries) {
+        spec::NodeDelivery nd;
+        nd.node = node;
+        nd.to_ranks = d.to_ranks;
+        nd.to_spares = d.to_spares;
+        nd.take = d.take;
+        st.change.deliveries.push_back(nd);
+      }
+      if (committed != nullptr) {
+        st.change.committed = *committed;
+        st.change.has_committed = true;
+      }
+    }
+    mkdirs(spec_dir);
+    if (!write_file_atomic(status_path(e.name), st.serialize()))
+      ES_ERROR("cannot write the spec store at %s", spec_dir.c_str());
+    metrics().inc("everserve_spec_writes_total");
+  }
+
+  // ---- the transition machine ------------------------------------------------------------------
+  void report_loss(const std::string& name, const std::vector<uint32_t>& ranks, uint64_t epoch, const std::string& cause,
+                   bool planned = false) {
+    Engine& e = engine(name);
+    if (epoch != 0 && epoch < e.epoch) {
+      metrics().inc("everserve_fenced_total");
+      return;  // a report from before the last change: stale
+    }
+    bool any = false;
+    for (uint32_t r : ranks) {
+      if (!e.workers.count(r)) {
+        metrics().inc("everserve_unheard_ranks_lost_total");
+        continue;
+      }
+      if (e.pending.insert(r).second) any = true;
+      if (planned) e.departing.insert(r);
+    }
+    if (!any) return;
+    if (e.first_report_us == 0) e.first_report_us = now_us();
+    e.cause = cause;
+    event("engine " + name + ": lost ranks reported (" + cause + ")");
+    drive(e);
+  }
+
+  void drive(Engine& e) {
+    if (e.in_flight || e.pending.empty() || e.down) return;
+    const uint64_t t0 = now_us();
+    Choice c = choose_outcome(policy, e.name, e.pending, e.spares);
+    metrics().observe("everserve_change_decision_seconds", {{"engine", e.name}}, (now_us() - t0) * 1e-6);
+    if (c.outcome == 0) {
+      abandon(e, "no outcome: " + c.why);
+      return;
+    }
+    auto f = std::make_unique<InFlight>();
+    f->change.epoch = e.epoch + 1;
+    f->change.outcome = c.outcome;
+    f->change.lost.assign(e.pending.begin(), e.pending.end());
+    f->change.departing.assign(e.departing.begin(), e.departing.end());
+    f->cause = e.cause;
+    f->take = c.take;
+    for (auto& [rank, seat] : c.take) {
+      signals::Take t;
+      t.rank = rank;
+      t.node = seat.node;
+      t.device = seat.device;
+      f->change.take.push_back(t);
+    }
+    f->reported_us = e.first_report_us;
+    f->started_ms = now_ms();
+    // one delivery per node: its surviving (or departing) ranks and its taking spares
+    for (auto& [r, h] : e.workers) {
+      const bool lost_now = e.pending.count(r) && !e.departing.count(r);
+      if (lost_now) continue;
+      auto& d = f->deliveries[h.node];
+      d.to_ranks.push_back(r);
+    }
+    for (auto& [rank, seat] : c.take) {
+      auto& d = f->deliveries[seat.node];
+      d.to_spares.push_back(rank);
+      signals::Take t;
+      t.rank = rank;
+      t.node = seat.node;
+      t.device = seat.device;
+      d.take.push_back(t);
+    }
+    for (auto& hn : e.head_nodes) f->deliveries[hn];  // the head hears the change on its node
+    for (auto& [node, d] : f->deliveries) {
+      d.request_id = next_request++;
+      d.engine = e.name;
+      d.change = f->change;
+      d.has_change = true;
+    }
+    // logged before any node hears of it
+    write_status(e, f.get(), nullptr);
+    f->delivered_us = now_us();
+    for (auto& [node, d] : f->deliveries) {
+      auto nit = nodes.find(node);
+      if (nit == nodes.end() || !nit->second.linked) {
+        e.in_flight = std::move(f);
+        abandon(e, "node " + node + " is not linked");
+        return;
+      }
+      f->waiting.insert(node);
+      coord::CoordToDaemon m;
+      m.has_deliver = true;
+      m.deliver = d;
+      to_node(node, m);
+    }
+    e.pending.clear();
+    e.departing.clear();
+    e.first_report_us = 0;
+    metrics().set("everserve_changes_in_flight", {{"engine", e.name}}, 1);
+    event("engine " + e.name + ": change to epoch " + std::to_string(f->change.epoch) + " delivered to " +
+          std::to_string(f->deliveries.size()) + " node(s)");
+    e.in_flight = std::move(f);
+    const std::string name = e.name;
+    const uint64_t epoch = e.in_flight->change.epoch;
+    loop.every(delivery_timeout_ms, [this, name, epoch] {
+      Engine& en = engines[name];
+      if (en.in_flight && en.in_flight->change.epoch == epoch) abandon(en, "acks timed out");
+    }, false);
+    if (e.in_flight->waiting.empty()) commit(e);
+  }
+
+  void delivered(const std::string& node, const coord::Delivered& d) {
+    auto it = engines.find(d.engine);
+    if (it == engines.end() || !it->second.in_flight) return;
+    Engine& e = it->second;
+    InFlight& f = *e.in_flight;
+    if (d.epoch != f.change.epoch || !f.waiting.count(node)) return;
+    for (auto& a : d.acks) f.acks.push_back(a);
+    if (!d.error.empty()) {
+      abandon(e, "node " + node + ": " + d.error);
+      return;
+    }
+    f.waiting.erase(node);
+    if (f.waiting.empty()) commit(e);
+  }
+
+  void commit(Engine& e) {
+    InFlight& f = *e.in_flight;
+    const uint64_t acked_us = now_us();
+    // the new membership: lost ranks leave, the spares that took them hold them
+    for (uint32_t r : f.change.lost) e.workers.erase(r);
+    for (auto& [rank, seat] : f.take) {
+      Holder h;
+      h.node = seat.node;
+      h.device = seat.device;
+      h.pid = seat.pid;
+      e.workers[rank] = h;
+      e.spares.erase(std::remove_if(e.spares.begin(), e.spares.end(),
+                                    [&](const SpareSeat& s) { return s.node == seat.node && s.device == seat.device; }),
+                     e.spares.end());
+    }
+    e.epoch = f.change.epoch;
+    coord::Committed c;
+    c.engine = e.name;
+    c.outcome = f.change.outcome;
+    c.lost = f.change.lost;
+    c.take = f.change.take;
+    c.has_membership = true;
+    auto& mc = c.membership;
+    mc.epoch = e.epoch;
+    for (auto& [r, h] : e.workers) {
+      mc.active_ranks.push_back(r);
+      signals::RankPlacement p;
+      p.rank = r;
+      p.node = h.node;
+      p.device = h.device;
+      p.has_device = true;
+      p.host = h.host;
+      mc.members.push_back(p);
+    }
+    mc.world_size = e.world ? e.world : (uint32_t)e.workers.size();
+    mc.lost = f.change.lost;
+    mc.reported_at_us = f.reported_us;
+    mc.delivered_at_us = f.delivered_us;
+    mc.acknowledged_at_us = acked_us;
+    mc.committed_at_us = now_us();
+    mc.acks = f.acks;
+    mc.pause_ms = (uint32_t)((mc.committed_at_us - (f.reported_us ? f.reported_us : f.delivered_us)) / 1000);
+    write_status(e, &f, &c);
+    coord::CoordToDaemon m;
+    m.has_committed = true;
+    m.committed = c;
+    for (auto& node : engine_nodes(e)) to_node(node, m);
+    for (auto& [node, d] : f.deliveries)
+      if (!engine_nodes(e).count(node)) to_node(node, m);
+    const double secs = (mc.committed_at_us - (f.reported_us ? f.reported_us : f.delivered_us)) * 1e-6;
+    metrics().inc("everserve_changes_total",
+                  {{"engine", e.name}, {"cause", f.cause}, {"outcome", std::to_string(f.change.outcome)}, {"verdict", "committed"}});
+    metrics().observe("everserve_change_seconds", {{"engine", e.name}}, secs);
+    metrics().set("everserve_changes_in_flight", {{"engine", e.name}}, 0);
+    event("engine " + e.name + ": epoch " + std::to_string(e.epoch) + " committed in " + std::to_string(secs * 1e3) +
+          " ms");
+    e.in_flight.reset();
+    update_gauges();
+    drive(e);  // losses that arrived during the change
+  }
+
+  void abandon(Engine& e, const std::string& why) {
+    const uint64_t epoch = e.in_flight ? e.in_flight->change.epoch : e.epoch + 1;
+    coord::CoordToDaemon m;
+    m.has_abandon = true;
+    m.abandon.engine = e.name;
+    m.abandon.epoch = epoch;
+    m.abandon.detail = why;
+    std::set<std::string> targets = engine_nodes(e);
+    if (e.in_flight)
+      for (auto& [node, d] : e.in_flight->deliveries) targets.insert(node);
+    for (auto& node : targets) to_node(node, m);
+    metrics().inc("everserve_changes_total",
+                  {{"engine", e.name}, {"cause", e.cause}, {"outcome", "0"}, {"verdict", "abandoned"}});
+    metrics().set("everserve_changes_in_flight", {{"engine", e.name}}, 0);
+    metrics().set("everserve_engine_down", {{"engine", e.name}}, 1);
+    e.down = true;
+    e.in_flight.reset();
+    e.pending.clear();
+    event("engine " + e.name + ": change abandoned, engine down: " + why);
+  }
+
+  void update_gauges() {
+    uint64_t linked = 0, workers = 0;
+    for (auto& [n, node] : nodes) linked += node.linked;
+    for (auto& [name, e] : engines) {
+      workers += e.workers.size();
+      metrics().set("everserve_spares", {{"engine", name}, {"state", "standing"}}, (double)e.spares.size());
+    }
+    metrics().set("everserve_daemons_connected", {}, (double)linked);
+    metrics().set("everserve_workers_registered", {}, (double)workers);
+  }
+
+  // ---- daemon links ----------------------------------------------------------------------------
+  void on_worker_event(const std::string& node, const coord::WorkerEvent& ev) {
+    Engine& e = engine(ev.engine);
+    using K = coord::WorkerEvent_Kind;
+    switch (ev.kind) {
+      case K::WorkerEvent_Kind_WORKER_REGISTERED: {
+        Holder h;
+        h.node = node;
+        h.device = ev.device;
+        h.pid = ev.pid;
+        h.host = ev.host;
+        e.workers[ev.rank] = h;
+        e.epoch = std::max(e.epoch, ev.epoch);
+        if (e.down && e.workers.size() >= std::max<uint32_t>(1, e.world)) {
+          e.down = false;
+          metrics().set("everserve_engine_down", {{"engine", e.name}}, 0);
+        }
+        break;
+      }
+      case K::WorkerEvent_Kind_SPARE_REGISTERED: {
+        SpareSeat s;
+        s.node = node;
+        s.device = ev.device;
+        s.for_rank = ev.any_rank ? -1 : (int64_t)ev.rank;
+        s.pid = ev.pid;
+        e.spares.push_back(s);
+        break;
+      }
+      case K::WorkerEvent_Kind_HEAD_REGISTERED: e.head_nodes.insert(node); break;
+      case K::WorkerEvent_Kind_WORKER_DEPARTED: {
+        auto it = e.workers.find(ev.rank);
+        if (it != e.workers.end() && it->second.node == node && ev.cause != signals::StopCause_STOP_CAUSE_STOPPED)
+          report_loss(ev.engine, {ev.rank}, 0, "departed");
+        else if (it != e.workers.end() && it->second.node == node)
+          e.workers.erase(it);
+        break;
+      }
+      case K::WorkerEvent_Kind_SPARE_DEPARTED:
+        e.spares.erase(std::remove_if(e.spares.begin(), e.spares.end(),
+                                      [&](const SpareSeat& s) { return s.node == node && s.device == ev.device; }),
+                       e.spares.end());
+        break;
+      case K::WorkerEvent_Kind_HEAD_DEPARTED: e.head_nodes.erase(node); break;
+      default: break;
+    }
+    update_gauges();
+  }
+
+  void from_daemon(Conn& c, const std::string& frame) {
+    coord::DaemonToCoord m;
+    if (!m.parse(frame)) return;
+    std::string node = conn_node.count(c.id) ? conn_node[c.id] : "";
+    if (m.has_hello) {
+      if (m.hello.protocol != 0 && m.hello.protocol < signals::ProtocolOldest_PROTOCOL_OLDEST) {
+        ES_WARN("node %s speaks protocol %u, older than supported", m.hello.node.c_str(), m.hello.protocol);
+        loop.close(c.id);
+        return;
+      }
+      node = m.hello.node;
+      conn_node[c.id] = node;
+      Node& n = nodes[node];
+      n.name = node;
+      n.conn = c.id;
+      n.linked = true;
+      n.last_seen_ms = now_ms();
+      n.heartbeat_ms = m.hello.heartbeat_ms ? m.hello.heartbeat_ms : 500;
+      for (auto& st : m.hello.engines) {
+        Engine& e = engine(st.engine);
+        e.epoch = std::max(e.epoch, st.epoch);
+      }
+      event("node " + node + " linked");
+      update_gauges();
+      return;
+    }
+    if (node.empty()) return;  // nothing before a hello
+    nodes[node].last_seen_ms = now_ms();
+    if (m.has_heartbeat) return;
+    if (m.has_bye) {
+      nodes[node].linked = false;
+      return;
+    }
+    if (m.has_worker_event) on_worker_event(node, m.worker_event);
+    else if (m.has_lost_report) {
+      std::vector<uint32_t> ranks(m.lost_report.lost.ranks.begin(), m.lost_report.lost.ranks.end());
+      report_loss(m.lost_report.engine, ranks, m.lost_report.lost.epoch,
+                  m.lost_report.lost.reason == signals::Reason_REASON_NOTICE ? "notice" : "fault",
+                  m.lost_report.lost.reason == signals::Reason_REASON_NOTICE);
+    } else if (m.has_notice_report) {
+      report_loss(m.notice_report.engine, {m.notice_report.notice.rank}, 0, "notice", true);
+    } else if (m.has_delivered) {
+      delivered(node, m.delivered);
+    } else if (m.has_join_report) {
+      // joins are opaque bytes between the head and the ranks: relay to every node of the engine
+      coord::CoordToDaemon out;
+      out.has_forward_join = true;
+      out.forward_join.engine = m.join_report.engine;
+      out.forward_join.join = m.join_report.join;
+      out.forward_join.has_join = true;
+      out.forward_join.to_clients = !m.join_report.from_client;
+      auto it = engines.find(m.join_report.engine);
+      if (it != engines.end())
+        for (auto& n : engine_nodes(it->second)) to_node(n, out);
+    } else if (m.has_role_asked) {
+      coord::CoordToDaemon out;
+      out.has_role_answer = true;
+      out.role_answer.request_id = m.role_asked.request_id;
+      out.role_answer.engine = m.role_asked.engine;
+      out.role_answer.rank = m.role_asked.rank;
+      Engine& e = engine(m.role_asked.engine);
+      out.role_answer.epoch = e.epoch;
+      out.role_answer.role = e.workers.count(m.role_asked.rank) ? signals::Role_ROLE_SPARE : signals::Role_ROLE_WORKER;
+      to_node(node, out);
+    } else if (m.has_node_notice) {
+      drain(node, m.node_notice.deadline_ms, "node notice: " + m.node_notice.source);
+    } else if (m.has_replay_ask || m.has_replay_offer) {
+      coord::CoordToDaemon out;
+      std::string eng;
+      if (m.has_replay_ask) {
+        out.has_replay_ask = true;
+        out.replay_ask = m.replay_ask;
+        eng = m.replay_ask.engine;
+      } else {
+        out.has_replay_offer = true;
+        out.replay_offer = m.replay_offer;
+        eng = m.replay_offer.engine;
+      }
+      auto it = engines.find(eng);
+      if (it != engines.end())
+        for (auto& n : engine_nodes(it->second)) to_node(n, out);
+    }
+  }
+
+  void link_closed(Conn& c) {
+    auto it = conn_node.find(c.id);
+    if (it == conn_node.end()) return;
+    const std::string node = it->second;
+    conn_node.erase(it);
+    Node& n = nodes[node];
+    if (n.conn != c.id) return;
+    n.linked = false;
+    node_lost(node, "link ended");
+  }
+
+  void node_lost(const std::string& node, const std::string& why) {
+    event("node " + node + " lost: " + why);
+    for (auto& [name, e] : engines) {
+      std::vector<uint32_t> ranks;
+      for (auto& [r, h] : e.workers)
+        if (h.node == node) ranks.push_back(r);
+      e.spares.erase(std::remove_if(e.spares.begin(), e.spares.end(), [&](const SpareSeat& s) { return s.node == node; }),
+                     e.spares.end());
+      if (e.in_flight && e.in_flight->waiting.count(node)) abandon(e, "node " + node + " lost during the change");
+      if (!ranks.empty()) report_loss(name, ranks, 0, "node lost");
+    }
+    update_gauges();
+  }
+
+  void check_heartbeats() {
+    const uint64_t now = now_ms();
+    for (auto& [name, n] : nodes) {
+      if (n.linked && now - n.last_seen_ms > (uint64_t)n.heartbeat_ms * loss_misses) {
+        n.linked = false;
+        loop.close(n.conn);
+        node_lost(name, std::to_string(loss_misses) + " heartbeats missed");
+      }
+    }
+  }
+
+  void drain(const std::string& node, int64_t deadline_ms, const std::string& why) {
+    Node& n = nodes[node];
+    n.drain_by_ms = deadline_ms ? deadline_ms : (int64_t)now_ms();
+    event("node " + node + " draining (" + why + ")");
+    for (auto& [name, e] : engines) {
+      std::vector<uint32_t> ranks;
+      for (auto& [r, h] : e.workers)
+        if (h.node == node) ranks.push_back(r);
+      if (!ranks.empty()) report_loss(name, ranks, 0, "notice", true);
+    }
+  }
+
+  // ---- operator API ----------------------------------------------------------------------------
+  std::string engine_json(const Engine& e) {
+    std::string w = "[";
+    bool first = true;
+    for (auto& [r, h] : e.workers) {
+      w += std::string(first ? "" : ",") + "{\"rank\":" + std::to_string(r) + ",\"node\":\"" + json_escape(h.node) +
+           "\",\"device\":" + std::to_string(h.device) + "}";
+      first = false;
+    }
+    w += "]";
+    std::string s = "[";
+    first = true;
+    for (auto& sp : e.spares) {
+      s += std::string(first ? "" : ",") + "{\"node\":\"" + json_escape(sp.node) + "\",\"device\":" +
+           std::to_string(sp.device) + ",\"forRank\":" + std::to_string(sp.for_rank) + "}";
+      first = false;
+    }
+    s += "]";
+    return "{\"metadata\":{\"name\":\"" + json_escape(e.name) + "\"},\"status\":{\"epoch\":" + std::to_string(e.epoch) +
+           ",\"worldSize\":" + std::to_string(e.world) + ",\"down\":" + (e.down ? "true" : "false") +
+           ",\"changing\":" + (e.in_flight ? "true" : "false") + ",\"workers\":" + w + ",\"spares\":" + s + "}}";
+  }
+
+  bool api(const HttpRequest& req, HttpResponse& resp) {
+    resp.content_type = "application/json";
+    const std::string path = req.path.substr(0, req.path.find('?'));
+    if (req.method == "GET" && path == "/v1/engines") {
+      std::string o = "{\"items\":[";
+      bool first = true;
+      for (auto& [n, e] : engines) {
+        o += (first ? "" : ",") + engine_json(e);
+        first = false;
+      }
+      resp.body = o + "]}";
+      return true;
+    }
+    if (req.method == "GET" && path.rfind("/v1/engines/", 0) == 0) {
+      const std::string name = path.substr(12);
+      auto it = engines.find(name);
+      if (it == engines.end()) return false;
+      resp.body = engine_json(it->second);
+      return true;
+    }
+    if (req.method == "GET" && path == "/v1/nodes") {
+      std::string o = "{\"items\":[";
+      bool first = true;
+      for (auto& [name, n] : nodes) {
+        o += std::string(first ? "" : ",") + "{\"metadata\":{\"name\":\"" + json_escape(name) + "\"},\"spec\":{\"unschedulable\":" +
+             (n.cordoned ? "true" : "false") + ",\"drainByMs\":" + std::to_string(n.drain_by_ms) + "},\"status\":{\"linked\":" +
+             (n.linked ? "true" : "false") + "}}";
+        first = false;
+      }
+      resp.body = o + "]}";
+      return true;
+    }
+    if (req.method == "PUT" && path.rfind("/v1/nodes/", 0) == 0) {
+      std::string rest = path.substr(10);
+      const auto slash = rest.find('/');
+      const std::string node = rest.substr(0, slash), verb = slash == std::string::npos ? "" : rest.substr(slash + 1);
+      Node& n = nodes[node];
+      n.name = node;
+      if (verb == "cordon") n.cordoned = true;
+      else if (verb == "uncordon") n.cordoned = false;
+      else if (verb == "drain") {
+        n.cordoned = true;
+        drain(node, 0, "operator");
+      } else if (verb == "undrain") n.drain_by_ms = 0;
+      else return false;
+      resp.body = "{\"node\":\"" + json_escape(node) + "\",\"done\":\"" + verb + "\"}";
+      return true;
+    }
+    if (req.method == "GET" && path == "/v1/watch") {
+      uint64_t since = 0;
+      const auto q = req.path.find("since=");
+      if (q != std::string::npos) since = std::stoull(req.path.substr(q + 6));
+      std::string o = "{\"events\":[";
+      bool first = true;
+      for (auto& ev : events)
+        if (ev.seq > since) {
+          o += std::string(first ? "" : ",") + "{\"seq\":" + std::to_string(ev.seq) + ",\"atMs\":" + std::to_string(ev.at_ms) +
+               ",\"text\":\"" + json_escape(ev.text) + "\"}";
+          first = false;
+        }
+      resp.body = o + "]}";
+      return true;
+    }
+    if (req.method == "POST" && path.rfind("/v1/engines/", 0) == 0 && path.size() > 7 &&
+        path.compare(path.size() - 7, 7, "/stacks") == 0) {
+      const std::string name = path.substr(12, path.size() - 12 - 7);
+      auto it = engines.find(name);
+      if (it == engines.end()) return false;
+      coord::CoordToDaemon m;
+      m.has_stacks = true;
+      m.stacks.request_id = next_request++;
+      m.stacks.engine = name;
+      for (auto& node : engine_nodes(it->second)) to_node(node, m);
+      resp.body = "{\"requested\":" + std::to_string(m.stacks.request_id) + "}";
+      return true;
+    }
+    if (req.method == "GET" && path == "/v1/openapi") {
+      resp.body =
+          "{\"openapi\":\"3.0.0\",\"info\":{\"title\":\"everserve coordinator\",\"version\":\"1\"},\"paths\":{"
+          "\"/v1/engines\":{\"get\":{}},\"/v1/engines/{name}\":{\"get\":{}},\"/v1/engines/{name}/stacks\":{\"post\":{}},"
+          "\"/v1/nodes\":{\"get\":{}},\"/v1/nodes/{name}/{cordon|uncordon|drain|undrain}\":{\"put\":{}},"
+          "\"/v1/watch\":{\"get\":{}}}}";
+      return true;
+    }
+    return false;
+  }
+};
+
+// A lease on a file: an exclusive lock held for the process's life; the term it records goes up
+// by one with every holder.
+bool take_lease(const std::string& path, uint64_t& term, std::string& err) {
+  const int fd = ::open(path.c_str(), O_RDWR | O_CREAT, 0660);
+  if (fd < 0) {
+    err = "cannot open the lease " + path;
+    return false;
+  }
+  while (flock(fd, LOCK_EX | LOCK_NB) != 0) {
+    ES_INFO("waiting for the lease %s", path.c_str());
+    sleep(1);
+  }
+  std::string data;
+  char buf[4096];
+  ssize_t n;
+  while ((n = ::read(fd, buf, sizeof(buf))) > 0) data.append(buf, size_t(n));
+  coord::LeaseRecord rec;
+  if (!data.empty()) rec.parse(data);
+  rec.term += 1;
+  rec.holder = "pid" + std::to_string(getpid());
+  rec.renewed_at_ms = (int64_t)now_ms();
+  const std::string out = rec.serialize();
+  if (ftruncate(fd, 0) != 0 || pwrite(fd, out.data(), out.size(), 0) != (ssize_t)out.size()) {
+    err = "cannot write the lease";
+    return false;
+  }
+  fsync(fd);
+  term = rec.term;
+  return true;  // the fd stays open (and locked) until exit
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  log_init("coord");
+  signal(SIGPIPE, SIG_IGN);
+  Coordinator co;
+  std::string listen = env_or("EVERSERVE_LISTEN", "unix:/tmp/everserve-coord.sock");
+  std::string policy_path = env_or("EVERSERVE_POLICY", "");
+  co.spec_dir = env_or("EVERSERVE_SPEC_STORE", "");
+  std::string lease = env_or("EVERSERVE_LEASE", "");
+  std::string api_addr = env_or("EVERSERVE_API_ADDR", "");
+  std::string metrics_addr = env_or("EVERSERVE_METRICS_ADDR", "");
+  co.loss_misses = (uint32_t)std::stoul(env_or("EVERSERVE_NODE_LOSS_MISSES", "3"));
+  for (int i = 1; i + 1 < argc; i += 2) {
+    const std::string k = argv[i], v = argv[i + 1];
+    if (k == "--listen") listen = v;
+    else if (k == "--policy") policy_path = v;
+    else if (k == "--spec-store") co.spec_dir = v;
+    else if (k == "--lease") lease = v;
+    else if (k == "--api-addr") api_addr = v;
+    else if (k == "--metrics-addr") metrics_addr = v;
+    else if (k == "--node-loss-misses") co.loss_misses = (uint32_t)std::stoul(v);
+    else if (k == "--delivery-timeout-ms") co.delivery_timeout_ms = std::stoull(v);
+    else {
+      fprintf(stderr, "unknown flag %s\n", k.c_str());
+      return 2;
+    }
+  }
+  std::string err;
+  if (!policy_path.empty()) {
+    std::string text;
+    if (!read_file(policy_path, text) || !parse_policy(text, co.policy, err)) {
+      ES_ERROR("policy %s: %s", policy_path.c_str(), err.c_str());
+      return 1;
+    }
+  } else {
+    co.policy.outcomes = {signals::Outcome_OUTCOME_REPLACE};
+  }
+  if (!lease.empty() && !take_lease(lease, co.term, err)) {
+    ES_ERROR("%s", err.c_str());
+    return 1;
+  }
+  metrics().describe("everserve_changes_total", "Membership changes by engine, cause, outcome and verdict", "counter");
+  metrics().describe("everserve_change_seconds", "From the first loss report to the commit", "histogram");
+  metrics().describe("everserve_change_decision_seconds", "Time to choose an outcome", "histogram");
+  metrics().describe("everserve_changes_in_flight", "1 while an engine's change is in flight", "gauge");
+  metrics().describe("everserve_daemons_connected", "Linked node daemons", "gauge");
+  metrics().describe("everserve_workers_registered", "Workers of every engine", "gauge");
+  metrics().describe("everserve_spares", "Spares by engine and state", "gauge");
+  metrics().describe("everserve_engine_down", "1 for an engine whose change was abandoned", "gauge");
+  metrics().describe("everserve_spec_writes_total", "Writes to the spec store", "counter");
+  metrics().describe("everserve_fenced_total", "Reports dropped as older than the engine's epoch", "counter");
+  metrics().describe("everserve_unheard_ranks_lost_total", "Loss reports naming ranks the coordinator does not hold", "counter");
+  Address a;
+  if (!Address::parse(listen, a) || !co.loop.listen(a, [&](Conn& c) {
+        c.on_frame = [&](Conn& cc, const std::string& f) { co.from_daemon(cc, f); };
+        c.on_close = [&](Conn& cc) { co.link_closed(cc); };
+      }, &err)) {
+    ES_ERROR("listen %s: %s", listen.c_str(), err.c_str());
+    return 1;
+  }
+  if (!api_addr.empty() &&
+      !serve_http(co.loop, api_addr, [&](const HttpRequest& r, HttpResponse& s) { return co.api(r, s); }, &err)) {
+    ES_ERROR("api %s: %s", api_addr.c_str(), err.c_str());
+    return 1;
+  }
+  if (!metrics_addr.empty() && metrics_addr != api_addr && !serve_http(co.loop, metrics_addr, nullptr, &err)) {
+    ES_ERROR("metrics %s: %s", metrics_addr.c_str(), err.c_str());
+    return 1;
+  }
+  co.loop.every(100, [&] { co.check_heartbeats(); });
+  ES_INFO("coordinator term %llu listening on %s", (unsigned long long)co.term, listen.c_str());
+  co.loop.run();
+  return 0;
+}

@@ -1,1 +1,593 @@
-int main(){return 0;}
+// everserve-node: the per-node daemon.
+//
+//   everserve-node --node NAME --socket unix:/run/everserve/node.sock --coordinator ADDR
+//                  [--heartbeat-ms 500] [--metrics-addr host:port] [--ack-timeout-ms 120000]
+//                  [--mirror-socket ADDR] [--discovery-dir DIR]
+// Flags also read EVERSERVE_NODE, EVERSERVE_SOCKET, EVERSERVE_COORDINATOR, EVERSERVE_HEARTBEAT_MS,
+// EVERSERVE_METRICS_ADDR, EVERSERVE_MIRROR_SOCKET, EVERSERVE_DISCOVERY_DIR.
+//
+// Processes of the node (workers, spares, heads, clients) connect to the Unix socket and speak
+// signals.proto. The daemon:
+//   * records each Register and reports it to the coordinator (WorkerEvent); a connection that
+//     ends without a Goodbye is reported as departed (STOP_CAUSE_LOST);
+//   * forwards RankLost / Notice / Join / cover reports / replay offers up;
+//   * delivers a coordinator's Change to the named ranks and spares, collects their Acks (bounded
+//     by the ack timeout) and answers Delivered; relays MembershipCommitted / Abandon / joins /
+//     cover plans / replay messages down to the engine's processes;
+//   * links to the coordinator with a hello and heartbeats, reconnecting with jittered backoff;
+//     reports made while unlinked are held and sent on the next link. Messages from an older
+//     coordinator term than the highest seen are ignored (fencing).
+#include <signal.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <deque>
+#include <map>
+#include <random>
+#include <set>
+
+#include "everserve_pb.h"
+#include "net.h"
+#include "telemetry.h"
+#include "util.h"
+
+using namespace es;
+
+namespace {
+
+struct Proc {
+  uint64_t conn = 0;
+  std::string engine;
+  uint32_t rank = 0;
+  int32_t role = signals::Role_ROLE_UNDECIDED;
+  bool any_rank = false;
+  uint32_t pid = 0;
+  uint32_t device = 0;
+  bool registered = false;
+  bool said_goodbye = false;
+  signals::Register reg;
+};
+
+struct PendingDelivery {
+  coord::Deliver deliver;
+  std::set<uint64_t> waiting;  // process connections that owe an Ack
+  std::vector<signals::Ack> acks;
+  uint64_t deadline_ms = 0;
+};
+
+struct Daemon {
+  std::string node;
+  std::string coordinator;
+  uint32_t heartbeat_ms = 500;
+  uint64_t ack_timeout_ms = 120000;
+  std::string mirror_socket;
+  Loop loop;
+  std::map<uint64_t, Proc> procs;
+  uint64_t coord_conn = 0;
+  uint64_t term = 0;
+  std::deque<std::string> held;  // reports made while unlinked
+  std::map<uint64_t, PendingDelivery> deliveries;
+  std::map<std::string, uint64_t> epochs;
+  uint64_t instance = 0;
+  uint64_t backoff_ms = 100;
+  std::mt19937_64 rng{std::random_device{}()};
+
+  // ---- up: to the coordinator ------------------------------------------------------------------
+  void up(const coord::DaemonToCoord& m) {
+    const std::string b = m.serialize();
+    if (coord_conn == 0 || !loop.send(coord_conn, b)) {
+      held.push_back(b);
+      if (held.size() > 10000) held.pop_front();
+    }
+  }
+
+  coord::EngineState engine_state(const std::string& e) {
+    coord::EngineState s;
+    s.engine = e;
+    s.epoch = epochs[e];
+    for (auto& [id, p] : procs) {
+      if (!p.registered || p.engine != e) continue;
+      if (p.role == signals::Role_ROLE_WORKER) s.workers.push_back(p.rank);
+      else if (p.role == signals::Role_ROLE_SPARE) (p.any_rank ? s.any_spares : s.spares).push_back(p.rank);
+    }
+    return s;
+  }
+
+  void send_hello() {
+    coord::DaemonToCoord m;
+    m.has_hello = true;
+    m.hello.node = node;
+    m.hello.heartbeat_ms = heartbeat_ms;
+    m.hello.protocol = signals::Protocol_PROTOCOL_VERSION;
+    m.hello.protocol_oldest = signals::ProtocolOldest_PROTOCOL_OLDEST;
+    m.hello.term = term;
+    std::set<std::string> engines;
+    for (auto& [id, p] : procs)
+      if (p.registered) engines.insert(p.engine);
+    for (auto& e : engines) m.hello.engines.push_back(engine_state(e));
+    loop.send(coord_conn, m.serialize());
+  }
+
+  void link() {
+    if (coordinator.empty() || coord_conn != 0) return;
+    Address a;
+    std::string err;
+    int fd = -1;
+    if (Address::parse(coordinator, a)) fd = connect_to(a, 1000, &err);
+    if (fd < 0) {
+      std::uniform_int_distribution<uint64_t> jit(0, backoff_ms / 2);
+      const uint64_t wait = backoff_ms + jit(rng);
+      backoff_ms = std::min<uint64_t>(backoff_ms * 2, 2000);
+      loop.every(wait, [this] { link(); }, false);
+      return;
+    }
+    backoff_ms = 100;
+    Conn* c = loop.adopt(fd, coordinator);
+    coord_conn = c->id;
+    c->on_frame = [this](Conn&, const std::string& f) { from_coordinator(f); };
+    c->on_close = [this](Conn&) {
+      ES_WARN("coordinator link lost");
+      metrics().set("everserve_node_linked", {}, 0);
+      coord_conn = 0;
+      loop.every(100, [this] { link(); }, false);
+    };
+    send_hello();
+    while (!held.empty()) {
+      loop.send(coord_conn, held.front());
+      held.pop_front();
+    }
+    metrics().set("everserve_node_linked", {}, 1);
+    ES_INFO("linked to coordinator %s", coordinator.c_str());
+  }
+
+  // ---- down: from the coordinator --------------------------------------------------------------
+  void to_engine(const std::string& engine, const signals::Signal& s, bool workers = true, bool spares = true,
+                 bool heads = true) {
+    const std::string b = s.serialize();
+    for (auto& [id, p] : procs) {
+      if (!p.registered || p.engine != engine) continue;
+      const bool w = p.role == signals::Role_ROLE_WORKER, sp = p.role == signals::Role_ROLE_SPARE,
+                 h = p.role == signals::Role_ROLE_HEAD || p.role == signals::Role_ROLE_CLIENT;
+      if ((w && workers) || (sp && spares) || (h && heads)) loop.send(id, b);
+    }
+  }
+
+  void from_coordinator(const std::string& frame) {
+    coord::CoordToDaemon m;
+    if (!m.parse(frame)) {
+      ES_WARN("malformed coordinator message");
+      return;
+    }
+    if (m.term < term) return;  // an old coordinator: fenced
+    term = std::max(term, m.term);
+    if (m.has_deliver) {
+      deliver(m.deliver);
+    } else if (m.has_committed) {
+      epochs[m.committed.engine] = std::max(epochs[m.committed.engine], m.committed.membership.epoch);
+      signals::Signal s;
+      s.has_membership_committed = true;
+      s.membership_committed = m.committed.membership;
+      to_engine(m.committed.engine, s);
+      // a spare that took a rank is a worker of the new membership
+      for (auto& t : m.committed.take)
+        for (auto& [id, p] : procs)
+          if (p.registered && p.engine == m.committed.engine && p.role == signals::Role_ROLE_SPARE &&
+              (p.rank == t.rank || p.any_rank) && t.node == node && (t.device == p.device)) {
+            p.role = signals::Role_ROLE_WORKER;
+            p.rank = t.rank;
+            p.any_rank = false;
+            break;
+          }
+    } else if (m.has_abandon) {
+      signals::Signal s;
+      s.has_abandoned = true;
+      s.abandoned.epoch = m.abandon.epoch;
+      s.abandoned.detail = m.abandon.detail;
+      to_engine(m.abandon.engine, s);
+    } else if (m.has_forward_change) {
+      signals::Signal s;
+      s.has_change = true;
+      s.change = m.forward_change.change;
+      to_engine(m.forward_change.engine, s, false, false, true);
+    } else if (m.has_forward_notice) {
+      signals::Signal s;
+      s.has_notice = true;
+      s.notice = m.forward_notice.notice;
+      to_engine(m.forward_notice.engine, s);
+    } else if (m.has_forward_join) {
+      signals::Signal s;
+      s.has_join = true;
+      s.join = m.forward_join.join;
+      if (m.forward_join.to_clients) {
+        to_engine(m.forward_join.engine, s, false, false, true);
+      } else {
+        for (auto& [id, p] : procs)
+          if (p.registered && p.engine == m.forward_join.engine && p.rank == m.forward_join.join.rank &&
+              (p.role == signals::Role_ROLE_WORKER || p.role == signals::Role_ROLE_SPARE))
+            loop.send(id, s.serialize());
+      }
+    } else if (m.has_cover_plan) {
+      signals::Signal s;
+      s.has_cover_plan = true;
+      s.cover_plan = m.cover_plan;
+      to_engine(m.cover_plan.engine, s);
+    } else if (m.has_group_id) {
+      signals::Signal s;
+      s.has_group_id = true;
+      s.group_id = m.group_id;
+      to_engine(m.group_id.engine, s);
+    } else if (m.has_engine_policy) {
+      signals::Signal s;
+      s.has_engine_policy = true;
+      s.engine_policy = m.engine_policy;
+      to_engine(m.engine_policy.engine, s);
+    } else if (m.has_engine_placement) {
+      signals::Signal s;
+      s.has_engine_placement = true;
+      s.engine_placement = m.engine_placement;
+      to_engine(m.engine_placement.engine, s);
+    } else if (m.has_instance_state) {
+      signals::Signal s;
+      s.has_instance_state = true;
+      s.instance_state = m.instance_state;
+      to_engine(m.instance_state.engine, s, false, false, true);
+    } else if (m.has_role_answer) {
+      for (auto& [id, p] : procs)
+        if (p.engine == m.role_answer.engine && p.role == signals::Role_ROLE_UNDECIDED) {
+          signals::Signal s;
+          s.has_role_assigned = true;
+          s.role_assigned.engine = m.role_answer.engine;
+          s.role_assigned.rank = m.role_answer.rank;
+          s.role_assigned.epoch = m.role_answer.epoch;
+          s.role_assigned.role = m.role_answer.role;
+          s.role_assigned.refusal = m.role_answer.refusal;
+          loop.send(id, s.serialize());
+          if (m.role_answer.refusal.empty()) {
+            p.role = m.role_answer.role;
+            p.rank = m.role_answer.rank;
+          }
+          break;
+        }
+    } else if (m.has_stacks) {
+      for (auto& [id, p] : procs)
+        if (p.registered && p.engine == m.stacks.engine && (!m.stacks.has_rank || p.rank == m.stacks.rank)) {
+          signals::Signal s;
+          s.has_dump_stacks = true;
+          s.dump_stacks.request_id = m.stacks.request_id;
+          s.dump_stacks.reason = "operator";
+          loop.send(id, s.serialize());
+        }
+    } else if (m.has_replay_ask || m.has_replay_offer) {
+      signals::Signal s;
+      if (m.has_replay_ask) {
+        s.has_replay_ask = true;
+        s.replay_ask = m.replay_ask;
+        to_engine(m.replay_ask.engine, s, false, false, true);
+      } else {
+        s.has_replay_offer = true;
+        s.replay_offer = m.replay_offer;
+        to_engine(m.replay_offer.engine, s, false, true, false);
+      }
+    }
+  }
+
+  void deliver(const coord::Deliver& d) {
+    PendingDelivery pd;
+    pd.deliver = d;
+    pd.deadline_ms = now_ms() + ack_timeout_ms;
+    signals::Signal s;
+    s.has_change = true;
+    s.change = d.change;
+    s.change.delivered_at_us = now_us();
+    const std::string b = s.serialize();
+    for (auto& [id, p] : procs) {
+      if (!p.registered || p.engine != d.engine) continue;
+      bool named = false;
+      if (p.role == signals::Role_ROLE_WORKER)
+        named = std::find(d.to_ranks.begin(), d.to_ranks.end(), p.rank) != d.to_ranks.end();
+      else if (p.role == signals::Role_ROLE_SPARE)
+        named = std::any_of(d.take.begin(), d.take.end(), [&](const signals::Take& t) {
+          return (t.rank == p.rank || p.any_rank) && t.node == node && t.device == p.device;
+        });
+      if (named) {
+        loop.send(id, b);
+        pd.waiting.insert(id);
+      } else if (p.role == signals::Role_ROLE_HEAD || p.role == signals::Role_ROLE_CLIENT) {
+        loop.send(id, b);  // the head learns of the change to cut its step; it does not ack
+      }
+    }
+    deliveries[d.request_id] = std::move(pd);
+    maybe_delivered(d.request_id);
+  }
+
+  void maybe_delivered(uint64_t rid, const std::string& error = "") {
+    auto it = deliveries.find(rid);
+    if (it == deliveries.end()) return;
+    if (!it->second.waiting.empty() && error.empty()) return;
+    coord::DaemonToCoord m;
+    m.has_delivered = true;
+    m.delivered.request_id = rid;
+    m.delivered.engine = it->second.deliver.engine;
+    m.delivered.epoch = it->second.deliver.change.epoch;
+    m.delivered.acks = it->second.acks;
+    m.delivered.error = error;
+    deliveries.erase(it);
+    up(m);
+  }
+
+  // ---- processes -------------------------------------------------------------------------------
+  void worker_event(const Proc& p, int32_t kind, int32_t cause, const std::string& detail) {
+    coord::DaemonToCoord m;
+    m.has_worker_event = true;
+    auto& ev = m.worker_event;
+    ev.engine = p.engine;
+    ev.kind = kind;
+    ev.rank = p.rank;
+    ev.device = p.device;
+    ev.pid = p.pid;
+    ev.launcher_pid = p.reg.launcher_pid;
+    ev.any_rank = p.any_rank;
+    ev.cause = cause;
+    ev.detail = detail;
+    ev.epoch = epochs[p.engine];
+    ev.host = p.reg.host;
+    if (p.reg.has_identity) {
+      ev.identity = p.reg.identity;
+      ev.has_identity = true;
+    }
+    if (p.reg.has_compile_cache) {
+      ev.compile_cache = p.reg.compile_cache;
+      ev.has_compile_cache = true;
+    }
+    ev.has_connection = true;
+    ev.connection.instance = instance;
+    ev.connection.serial = p.conn;
+    ev.connection.pid = p.pid;
+    up(m);
+  }
+
+  static int32_t registered_kind(int32_t role) {
+    switch (role) {
+      case signals::Role_ROLE_WORKER: return coord::WorkerEvent_Kind_WORKER_REGISTERED;
+      case signals::Role_ROLE_SPARE: return coord::WorkerEvent_Kind_SPARE_REGISTERED;
+      case signals::Role_ROLE_HEAD: return coord::WorkerEvent_Kind_HEAD_REGISTERED;
+      default: return coord::WorkerEvent_Kind_KIND_UNSPECIFIED;
+    }
+  }
+  static int32_t departed_kind(int32_t role) {
+    switch (role) {
+      case signals::Role_ROLE_WORKER: return coord::WorkerEvent_Kind_WORKER_DEPARTED;
+      case signals::Role_ROLE_SPARE: return coord::WorkerEvent_Kind_SPARE_DEPARTED;
+      case signals::Role_ROLE_HEAD: return coord::WorkerEvent_Kind_HEAD_DEPARTED;
+      case signals::Role_ROLE_UNDECIDED: return coord::WorkerEvent_Kind_UNDECIDED_DEPARTED;
+      default: return coord::WorkerEvent_Kind_KIND_UNSPECIFIED;
+    }
+  }
+
+  void from_process(Conn& c, const std::string& frame) {
+    signals::Signal s;
+    if (!s.parse(frame)) {
+      ES_WARN("malformed signal from a process");
+      return;
+    }
+    Proc& p = procs[c.id];
+    p.conn = c.id;
+    if (s.has_register) {
+      const auto& r = s.register_;
+      if (r.protocol != 0 && r.protocol < signals::ProtocolOldest_PROTOCOL_OLDEST) {
+        signals::Signal g;
+        g.has_goodbye = true;
+        g.goodbye.cause = signals::StopCause_STOP_CAUSE_REFUSED;
+        g.goodbye.detail = "protocol " + std::to_string(r.protocol) + " is older than this daemon's oldest";
+        loop.send(c.id, g.serialize());
+        return;
+      }
+      p.engine = r.engine;
+      p.rank = r.rank;
+      p.role = r.role;
+      p.any_rank = r.any_rank;
+      p.pid = r.launcher_pid;
+      p.device = r.has_member ? r.member.device : 0;
+      p.reg = r;
+      p.registered = true;
+      metrics().inc("everserve_node_registrations_total", {{"role", std::to_string(r.role)}});
+      if (r.role == signals::Role_ROLE_UNDECIDED) {
+        coord::DaemonToCoord m;
+        m.has_role_asked = true;
+        m.role_asked.request_id = c.id;
+        m.role_asked.engine = r.engine;
+        m.role_asked.rank = r.rank;
+        m.role_asked.host = r.host;
+        up(m);
+      } else if (r.role != signals::Role_ROLE_CLIENT) {
+        worker_event(p, registered_kind(r.role), 0, "");
+      }
+      ES_INFO("registered %s rank %u role %d (conn %llu)", r.engine.c_str(), r.rank, r.role,
+              (unsigned long long)c.id);
+    } else if (s.has_ack) {
+      for (auto& [rid, pd] : deliveries) {
+        if (pd.waiting.erase(c.id)) {
+          signals::Ack a = s.ack;
+          a.received_at_us = now_us();
+          pd.acks.push_back(a);
+          if (!a.error.empty()) {
+            maybe_delivered(rid, "rank " + std::to_string(a.rank) + ": " + a.error);
+          } else {
+            maybe_delivered(rid);
+          }
+          break;
+        }
+      }
+    } else if (s.has_rank_lost) {
+      coord::DaemonToCoord m;
+      m.has_lost_report = true;
+      m.lost_report.engine = p.engine;
+      m.lost_report.lost = s.rank_lost;
+      m.lost_report.has_lost = true;
+      up(m);
+    } else if (s.has_notice) {
+      coord::DaemonToCoord m;
+      m.has_notice_report = true;
+      m.notice_report.engine = p.engine;
+      m.notice_report.notice = s.notice;
+      m.notice_report.has_notice = true;
+      up(m);
+    } else if (s.has_join) {
+      coord::DaemonToCoord m;
+      m.has_join_report = true;
+      m.join_report.engine = s.join.engine.empty() ? p.engine : s.join.engine;
+      m.join_report.join = s.join;
+      m.join_report.has_join = true;
+      m.join_report.from_client = p.role == signals::Role_ROLE_HEAD || p.role == signals::Role_ROLE_CLIENT;
+      up(m);
+    } else if (s.has_goodbye) {
+      p.said_goodbye = true;
+    } else if (s.has_group_formed || s.has_group_failed || s.has_group_released || s.has_group_ready) {
+      coord::DaemonToCoord m;
+      m.has_cover_report = true;
+      if (s.has_group_formed) {
+        m.cover_report.has_formed = true;
+        m.cover_report.formed = s.group_formed;
+      } else if (s.has_group_failed) {
+        m.cover_report.has_failed = true;
+        m.cover_report.failed = s.group_failed;
+      } else if (s.has_group_released) {
+        m.cover_report.has_released = true;
+        m.cover_report.released = s.group_released;
+      } else {
+        m.cover_report.has_ready = true;
+        m.cover_report.ready = s.group_ready;
+      }
+      up(m);
+    } else if (s.has_group_id) {
+      coord::DaemonToCoord m;
+      m.has_group_id = true;
+      m.group_id = s.group_id;
+      up(m);
+    } else if (s.has_release_leaked) {
+      coord::DaemonToCoord m;
+      m.has_release_leaked = true;
+      m.release_leaked.leak = s.release_leaked;
+      m.release_leaked.has_leak = true;
+      up(m);
+    } else if (s.has_stacks_dumped) {
+      coord::DaemonToCoord m;
+      m.has_stacks_sent = true;
+      m.stacks_sent.request_id = s.stacks_dumped.request_id;
+      m.stacks_sent.pid = p.pid;
+      m.stacks_sent.answered = true;
+      m.stacks_sent.text = s.stacks_dumped.text.substr(0, 1 << 20);
+      up(m);
+    } else if (s.has_replay_ask || s.has_replay_offer) {
+      coord::DaemonToCoord m;
+      if (s.has_replay_ask) {
+        m.has_replay_ask = true;
+        m.replay_ask = s.replay_ask;
+      } else {
+        m.has_replay_offer = true;
+        m.replay_offer = s.replay_offer;
+      }
+      up(m);
+    }
+  }
+
+  void process_closed(Conn& c) {
+    auto it = procs.find(c.id);
+    if (it == procs.end()) return;
+    Proc p = it->second;
+    procs.erase(it);
+    // a named process that went away owes no Ack any more: report the delivery with an error
+    for (auto& [rid, pd] : deliveries)
+      if (pd.waiting.erase(c.id)) {
+        signals::Ack a;
+        a.rank = p.rank;
+        a.epoch = pd.deliver.change.epoch;
+        a.error = "process departed before its ack";
+        pd.acks.push_back(a);
+        maybe_delivered(rid, "rank " + std::to_string(p.rank) + " departed during the change");
+        break;
+      }
+    if (p.registered && p.role != signals::Role_ROLE_CLIENT)
+      worker_event(p, departed_kind(p.role),
+                   p.said_goodbye ? signals::StopCause_STOP_CAUSE_STOPPED : signals::StopCause_STOP_CAUSE_LOST,
+                   p.said_goodbye ? "goodbye" : "connection ended");
+  }
+
+  void tick() {
+    if (coord_conn != 0) {
+      coord::DaemonToCoord m;
+      m.has_heartbeat = true;
+      loop.send(coord_conn, m.serialize());
+    }
+    const uint64_t now = now_ms();
+    std::vector<uint64_t> expired;
+    for (auto& [rid, pd] : deliveries)
+      if (now > pd.deadline_ms) expired.push_back(rid);
+    for (auto rid : expired) maybe_delivered(rid, "acks timed out");
+    uint64_t workers = 0;
+    for (auto& [id, p] : procs) workers += p.registered && p.role == signals::Role_ROLE_WORKER;
+    metrics().set("everserve_node_workers", {}, (double)workers);
+  }
+};
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  log_init("node");
+  signal(SIGPIPE, SIG_IGN);
+  Daemon d;
+  d.node = env_or("EVERSERVE_NODE", "node0");
+  std::string socket = env_or("EVERSERVE_SOCKET", "unix:/tmp/everserve-node.sock");
+  d.coordinator = env_or("EVERSERVE_COORDINATOR", "");
+  d.heartbeat_ms = (uint32_t)std::stoul(env_or("EVERSERVE_HEARTBEAT_MS", "500"));
+  d.mirror_socket = env_or("EVERSERVE_MIRROR_SOCKET", "");
+  std::string metrics_addr = env_or("EVERSERVE_METRICS_ADDR", "");
+  std::string discovery = env_or("EVERSERVE_DISCOVERY_DIR", "");
+  for (int i = 1; i + 1 < argc; i += 2) {
+    const std::string k = argv[i], v = argv[i + 1];
+    if (k == "--node") d.node = v;
+    else if (k == "--socket") socket = v;
+    else if (k == "--coordinator") d.coordinator = v;
+    else if (k == "--heartbeat-ms") d.heartbeat_ms = (uint32_t)std::stoul(v);
+    else if (k == "--ack-timeout-ms") d.ack_timeout_ms = std::stoull(v);
+    else if (k == "--metrics-addr") metrics_addr = v;
+    else if (k == "--mirror-socket") d.mirror_socket = v;
+    else if (k == "--discovery-dir") discovery = v;
+    else {
+      fprintf(stderr, "unknown flag %s\n", k.c_str());
+      return 2;
+    }
+  }
+  d.instance = (now_us() << 8) ^ (uint64_t)getpid();
+  metrics().describe("everserve_node_linked", "1 while the daemon is linked to the coordinator", "gauge");
+  metrics().describe("everserve_node_workers", "Workers registered on this node", "gauge");
+  Address a;
+  std::string err;
+  if (!Address::parse(socket, a) || !d.loop.listen(a, [&](Conn& c) {
+        c.on_frame = [&](Conn& cc, const std::string& f) { d.from_process(cc, f); };
+        c.on_close = [&](Conn& cc) { d.process_closed(cc); };
+      }, &err)) {
+    ES_ERROR("listen %s: %s", socket.c_str(), err.c_str());
+    return 1;
+  }
+  if (!discovery.empty()) {
+    // the discovery record (discovery.proto DaemonRecord, binary) for clients that look nodes up
+    mkdirs(discovery);
+    std::string rec;
+    pbwire::put_len(rec, 1, d.node);
+    pbwire::put_len(rec, 2, socket);
+    pbwire::put_varint(rec, 4, now_ms());
+    pbwire::put_varint(rec, 5, (uint32_t)getpid());
+    if (!d.mirror_socket.empty()) pbwire::put_len(rec, 6, d.mirror_socket);
+    write_file_atomic(discovery + "/" + d.node + ".daemon", rec);
+  }
+  if (!metrics_addr.empty() && !serve_http(d.loop, metrics_addr, nullptr, &err)) {
+    ES_ERROR("metrics %s: %s", metrics_addr.c_str(), err.c_str());
+    return 1;
+  }
+  d.link();
+  d.loop.every(d.heartbeat_ms, [&] { d.tick(); });
+  ES_INFO("node %s serving %s, coordinator %s", d.node.c_str(), socket.c_str(), d.coordinator.c_str());
+  d.loop.run();
+  return 0;
+}
