@@ -102,10 +102,13 @@ class Engine:
         if self.connector is not None:
             self.connector.end_step(plan, self.scheduler)
         out = self.scheduler.update(plan, tokens)
-        if self.connector is not None:
-            for req_id, _, fin in out:
-                if fin:
+        tell = getattr(self.executor, "finished", None)
+        for req_id, _, fin in out:
+            if fin:
+                if self.connector is not None:
                     self.connector.finished(req_id)
+                if tell is not None:
+                    tell(req_id)
         return out
 
     def decode_steps(self, k: int) -> list[list[int]]:

@@ -168,7 +168,18 @@ class Scheduler:
 
     # ---- resume ----------------------------------------------------------------------------------
     def resume_from_committed(self) -> None:
-        """After a membership change: restart every running request at its committed point."""
+        """After a membership change: restart every running request at its committed point.
+
+        A request with nothing committed goes back to the waiting queue (its prompt is prefilled
+        again, in prefill shape as the first time); the others restart at ``min(committed, n - 1)``
+        and replay their uncommitted positions one per step in decode shape.
+        """
+        for req in sorted([r for r in self.running if r.committed == 0], key=lambda r: -r.arrival):
+            self.running.remove(req)
+            self.bm.free(req.blocks)
+            req.num_computed = 0
+            req.status = Status.WAITING
+            self.waiting.appendleft(req)
         for req in self.running:
             req.num_computed = req.resume_point()
-        self.one_token_replay = True
+        self.one_token_replay = any(r.num_computed < r.num_tokens - 1 for r in self.running)

@@ -1,0 +1,146 @@
+"""A one-node control plane in a directory: coordinator, node daemon and KV store.
+
+    with ControlPlane(workdir, engines=[{"name": "e0", "pipelineParallel": 2}]) as cp:
+        ... cp.daemon_socket, cp.store_socket, cp.api ...
+
+It starts the C++ binaries (``cpp/bin``; built with ``make -C cpp`` when missing) with their
+sockets, spec store, lease and logs under ``workdir``, waits for them to listen, and stops them
+on exit. The policy file it writes is ``everserve.policy.v1.Policy`` in proto3 JSON.
+
+This is the bare-metal layout of the reference's deploy/baremetal units (one coordinator per
+cluster, one daemon and one store per node), for tests, benchmarks and single-node serving.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import socket
+import subprocess
+import time
+
+_ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+BIN = os.path.join(_ROOT, "cpp", "bin")
+
+
+def binary(name: str) -> str:
+    path = os.path.join(BIN, name)
+    if not os.path.exists(path):
+        subprocess.run(["make", "-C", os.path.join(_ROOT, "cpp"), f"-j{os.cpu_count() or 4}"], check=True,
+                       stdout=subprocess.DEVNULL)
+    return path
+
+
+def free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def wait_listening(addr: str, timeout_s: float = 15.0) -> None:
+    deadline = time.monotonic() + timeout_s
+    while time.monotonic() < deadline:
+        try:
+            if addr.startswith("unix:"):
+                s = socket.socket(socket.AF_UNIX)
+                s.connect(addr[5:])
+            else:
+                host, _, port = addr.rpartition(":")
+                s = socket.create_connection((host, int(port)), timeout=0.2)
+            s.close()
+            return
+        except OSError:
+            time.sleep(0.02)
+    raise TimeoutError(f"{addr} is not listening")
+
+
+class ControlPlane:
+    def __init__(self, workdir: str, engines: list[dict] | None = None, node: str = "n0",
+                 outcomes=("OUTCOME_REPLACE",), heartbeat_ms: int = 500, store_slots: int = 1 << 16,
+                 store_budget: int = 8 << 30, ack_timeout_ms: int = 120000):
+        self.dir = os.path.abspath(workdir)
+        os.makedirs(self.dir, exist_ok=True)
+        self.node = node
+        self.coord_socket = f"unix:{self.dir}/coord.sock"
+        self.daemon_socket = f"unix:{self.dir}/{node}.sock"
+        self.store_socket = f"unix:{self.dir}/store-{node}.sock"
+        self.api = f"127.0.0.1:{free_port()}"
+        self.policy_path = os.path.join(self.dir, "policy.json")
+        with open(self.policy_path, "w") as f:
+            json.dump({"outcomesInOrder": list(outcomes), "engines": engines or []}, f)
+        self.heartbeat_ms = heartbeat_ms
+        self.store_slots = store_slots
+        self.store_budget = store_budget
+        self.ack_timeout_ms = ack_timeout_ms
+        self.procs: dict[str, subprocess.Popen] = {}
+        self._logs = []
+
+    def _run(self, name: str, args: list[str]) -> None:
+        log = open(os.path.join(self.dir, f"{name}.log"), "w")  # noqa: SIM115
+        self._logs.append(log)
+        self.procs[name] = subprocess.Popen(args, stdout=log, stderr=subprocess.STDOUT)
+
+    def start(self) -> "ControlPlane":
+        self._run("store", [binary("everserve-store"), "--socket", self.store_socket, "--data-dir",
+                            os.path.join(self.dir, "store"), "--slots", str(self.store_slots), "--budget-bytes",
+                            str(self.store_budget)])
+        self._run("coord", [binary("everserve-coord"), "--listen", self.coord_socket, "--policy", self.policy_path,
+                            "--spec-store", os.path.join(self.dir, "spec"), "--lease", os.path.join(self.dir, "lease"),
+                            "--api-addr", self.api])
+        wait_listening(self.coord_socket)
+        self._run("node", [binary("everserve-node"), "--node", self.node, "--socket", self.daemon_socket,
+                           "--coordinator", self.coord_socket, "--heartbeat-ms", str(self.heartbeat_ms),
+                           "--ack-timeout-ms", str(self.ack_timeout_ms), "--mirror-socket", self.store_socket])
+        wait_listening(self.store_socket)
+        wait_listening(self.daemon_socket)
+        wait_listening(self.api)
+        return self
+
+    def get(self, path: str) -> dict:
+        import http.client
+
+        host, _, port = self.api.rpartition(":")
+        c = http.client.HTTPConnection(host, int(port), timeout=5)
+        c.request("GET", path)
+        body = c.getresponse().read()
+        c.close()
+        return json.loads(body)
+
+    def engine_view(self, name: str) -> dict:
+        return self.get(f"/v1/engines/{name}")
+
+    def wait_spares(self, engine: str, n: int, timeout_s: float = 600.0) -> None:
+        deadline = time.monotonic() + timeout_s
+        while time.monotonic() < deadline:
+            try:
+                if len(self.engine_view(engine)["status"]["spares"]) >= n:
+                    return
+            except (OSError, KeyError, ValueError):
+                pass
+            time.sleep(0.1)
+        raise TimeoutError(f"{n} spare(s) of {engine} did not register")
+
+    def log(self, name: str) -> str:
+        with open(os.path.join(self.dir, f"{name}.log")) as f:
+            return f.read()
+
+    def stop(self) -> None:
+        for p in reversed(list(self.procs.values())):
+            if p.poll() is None:
+                p.terminate()
+        for p in self.procs.values():
+            try:
+                p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                p.kill()
+                p.wait()
+        for f in self._logs:
+            f.close()
+
+    def __enter__(self) -> "ControlPlane":
+        return self.start()
+
+    def __exit__(self, *exc) -> None:
+        self.stop()

@@ -1,0 +1,310 @@
+"""The head's executor for a multi-process engine, and its failover at a step boundary.
+
+``MultiprocExecutor`` spawns one rank process per position (``everserve_b200.serving.rank``) plus
+the spares, hosts the engine's rendezvous store (groups of every epoch form under ``e<epoch>/``)
+and a carrier socket per rank, and registers with the node daemon as the engine's head
+(``ROLE_HEAD``). Each step it sends the plan to every rank and collects the replies; the last
+stage's column 0 returns the sampled ids.
+
+When a rank is lost (its link ends, or a rank reports a failed step), the step raises
+:class:`RankLost`. The failover step wrapper (:func:`failover`, installed with
+``Engine.wrap_step``) then runs :meth:`MultiprocExecutor.complete_change`:
+
+1. wait for the coordinator's ``MembershipCommitted`` (or ``Abandoned``: the engine is down);
+   the coordinator has already delivered the ``Change`` to the survivors and to the spare, and the
+   spare restored the lost rank's committed KV before it acked;
+2. release departing ranks (a planned departure finishes its step and drains its commits);
+3. offer a ``Join`` to each spare that took a rank (through the daemons and the coordinator) and
+   wait for it to link;
+4. ``boundary``: every member forms the new epoch's groups and reports what its cache holds;
+5. resume: each running request's committed count is the minimum over the ranks, and the
+   scheduler restarts every request at ``min(committed, n - 1)``; the uncommitted tail is replayed
+   one position per step in decode shape, so the outputs are the no-fault outputs.
+
+Reference parity: EverserveExecutor and its change completion of
+adapters/vllm/everserve_vllm/executor.py:126-853 (cut step, new ring, boundary, join offers,
+install, resume) and the step-loop hook of serving.py:44-86.
+"""
+
+from __future__ import annotations
+
+import os
+import pickle
+import signal
+import subprocess
+import sys
+import time
+from dataclasses import dataclass, field
+
+import torch.distributed as dist
+
+from ..contract.daemon import DaemonClient
+from ..engine.config import EngineConfig
+from ..runtime.layout import ParallelLayout
+from .carrier import CarrierServer, Link, LinkClosed
+
+
+class RankLost(RuntimeError):
+    def __init__(self, ranks, detail: str = ""):
+        super().__init__(f"ranks {sorted(ranks)} lost: {detail}")
+        self.ranks = sorted(ranks)
+        self.detail = detail
+
+
+class EngineDown(RuntimeError):
+    """The coordinator abandoned the change: the engine cannot continue."""
+
+
+@dataclass
+class ChangeRecord:
+    epoch: int
+    lost: list
+    outcome: int
+    t_detect: float
+    t_committed: float = 0.0
+    t_joined: float = 0.0
+    t_ready: float = 0.0
+    t_resumed: float = 0.0
+    t_fault: float = 0.0  # when the fault was injected (host-side injection only)
+    coordinator: dict = field(default_factory=dict)
+
+    def as_dict(self) -> dict:
+        """Milestones in ms from the fault when it is known (else from the head's detection)."""
+        t0 = self.t_fault or self.t_detect
+        ms = lambda t: round((t - t0) * 1e3, 3) if t else None  # noqa: E731
+        return {"epoch": self.epoch, "lost": self.lost, "outcome": self.outcome, "from": "fault" if self.t_fault
+                else "detect", "detected_ms": ms(self.t_detect), "committed_ms": ms(self.t_committed),
+                "joined_ms": ms(self.t_joined), "ready_ms": ms(self.t_ready), "resumed_ms": ms(self.t_resumed),
+                "coordinator": self.coordinator}
+
+
+class MultiprocExecutor:
+    def __init__(self, cfg: EngineConfig, engine: str = "engine", daemon: str = "", store: str = "",
+                 spares: tuple[int, ...] = (), device: str = "cpu", dtype: str = "float32", node: str = "",
+                 env: dict | None = None, threads: int = 0, step_timeout_s: float = 300.0,
+                 change_timeout_s: float = 120.0, log_dir: str | None = None, start_timeout_s: float = 600.0):
+        self.cfg = cfg
+        self.engine = engine
+        self.layout = ParallelLayout(cfg.tensor_parallel, cfg.pipeline_parallel)
+        self.step_timeout_s = step_timeout_s
+        self.change_timeout_s = change_timeout_s
+        self.carrier = CarrierServer()
+        self.rdzv = dist.TCPStore("127.0.0.1", 0, is_master=True, wait_for_workers=False)
+        self.rdzv_addr = f"127.0.0.1:{self.rdzv.port}"
+        self.log_dir = log_dir
+        self.procs: dict[str, subprocess.Popen] = {}
+        self._logs = []
+        base = [sys.executable, "-m", "everserve_b200.serving.rank", "--engine", engine, "--model", cfg.model.name,
+                "--tp", str(cfg.tensor_parallel), "--pp", str(cfg.pipeline_parallel), "--device", device,
+                "--dtype", dtype, "--seed", str(cfg.seed), "--block-size", str(cfg.block_size),
+                "--max-batch", str(cfg.max_batch), "--max-model-len", str(cfg.max_model_len),
+                "--rdzv", self.rdzv_addr, "--head", self.carrier.address]
+        if cfg.num_blocks:
+            base += ["--num-blocks", str(cfg.num_blocks)]
+        if daemon:
+            base += ["--daemon", daemon]
+        if store:
+            base += ["--store", store]
+        if node:
+            base += ["--node", node]
+        if threads:
+            base += ["--threads", str(threads)]
+        e = dict(os.environ)
+        root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        e["PYTHONPATH"] = os.pathsep.join([root] + [p for p in e.get("PYTHONPATH", "").split(os.pathsep) if p])
+        e.update(env or {})
+        for r in range(self.layout.world):
+            self._spawn(f"rank{r}", base + ["--role", "worker", "--rank", str(r)], e)
+        for i, r in enumerate(spares):
+            self._spawn(f"spare{i}-for{r}", base + ["--role", "spare", "--rank", str(r)], e)
+        self.links: dict[int, Link] = {}
+        deadline = time.monotonic() + start_timeout_s
+        while len(self.links) < self.layout.world:
+            self._check_started()
+            try:
+                link = self.carrier.wait_link(min(1.0, max(0.01, deadline - time.monotonic())))
+            except TimeoutError:
+                if time.monotonic() > deadline:
+                    raise
+                continue
+            self.links[link.hello["rank"]] = link
+        self.num_blocks = min(link.hello["num_blocks"] for link in self.links.values())
+        self.epoch = 0
+        self._boundary(0)
+        self.client = DaemonClient(daemon, engine, node=node) if daemon else None
+        self.changes: list[ChangeRecord] = []
+        self.decode_steps_run = 0
+        self.kill_at_decode_step: tuple[int, int] | None = None  # (decode step, rank): host-side fault injection
+        self.t_kill = 0.0
+        self._finished: list[str] = []
+
+    # ---- processes -------------------------------------------------------------------------------
+    def _spawn(self, name: str, args: list[str], env: dict) -> None:
+        out = subprocess.DEVNULL
+        if self.log_dir:
+            os.makedirs(self.log_dir, exist_ok=True)
+            out = open(os.path.join(self.log_dir, f"{name}.log"), "w")  # noqa: SIM115
+            self._logs.append(out)
+        self.procs[name] = subprocess.Popen(args, env=env, stdout=out, stderr=subprocess.STDOUT)
+
+    def _check_started(self) -> None:
+        for name, p in self.procs.items():
+            if p.poll() is not None and not name.startswith("spare"):
+                raise RuntimeError(f"{name} exited with {p.returncode} during start-up")
+
+    def pid_of(self, rank: int) -> int:
+        return int(self.links[rank].hello["pid"])
+
+    # ---- steps -----------------------------------------------------------------------------------
+    def execute(self, plan):
+        msg = {"op": "step", "epoch": self.epoch, "plan": plan}
+        if self._finished:
+            self._broadcast({"op": "finished", "ids": self._finished})
+            self._finished = []
+        victim = None
+        if not plan.is_prefill:
+            self.decode_steps_run += 1
+            if self.kill_at_decode_step and self.decode_steps_run == self.kill_at_decode_step[0]:
+                victim = self.kill_at_decode_step[1]
+                self.kill_at_decode_step = None
+        lost, errors = set(), {}
+        for r, link in self.links.items():
+            try:
+                link.send(msg)
+            except LinkClosed:
+                lost.add(r)
+        if victim is not None:
+            self.t_kill = time.monotonic()
+            os.kill(self.pid_of(victim), signal.SIGKILL)  # the fault: SIGKILL mid-step
+        ids = None
+        for r, link in self.links.items():
+            if r in lost:
+                continue
+            try:
+                while True:
+                    reply = link.get(timeout=self.step_timeout_s)
+                    if reply.get("step") == plan.step:
+                        break
+            except LinkClosed:
+                lost.add(r)
+                continue
+            if reply["op"] == "error":
+                errors[r] = reply["error"]
+            elif "ids" in reply:
+                ids = reply["ids"]
+        if lost or errors:
+            raise RankLost(lost or set(errors), "; ".join(f"rank {r}: {e}" for r, e in errors.items()) or "link ended")
+        return ids
+
+    def fetch(self, ids):
+        return ids
+
+    def finished(self, req_id: str) -> None:
+        self._finished.append(req_id)
+
+    def decode_loop(self, plan, k):
+        raise NotImplementedError("multi-step decode runs in one process; the multi-process engine steps singly")
+
+    def _broadcast(self, msg: dict) -> None:
+        for link in self.links.values():
+            try:
+                link.send(msg)
+            except LinkClosed:
+                pass
+
+    def _boundary(self, epoch: int) -> dict[int, dict]:
+        for link in self.links.values():
+            link.send({"op": "boundary", "epoch": epoch})
+        computed = {}
+        for r, link in self.links.items():
+            while True:
+                reply = link.get(timeout=self.change_timeout_s)
+                if reply["op"] in ("ready", "error") and reply.get("epoch") == epoch:
+                    break
+            if reply["op"] == "error":
+                raise RankLost({r}, f"boundary of epoch {epoch}: {reply['error']}")
+            computed[r] = reply["computed"]
+        return computed
+
+    # ---- membership change -----------------------------------------------------------------------
+    def complete_change(self, engine, t_detect: float | None = None) -> ChangeRecord:
+        if self.client is None:
+            raise EngineDown("no daemon link: a lost rank cannot be replaced")
+        t_detect = t_detect or time.monotonic()
+        h = self.client.wait_committed(timeout_s=self.change_timeout_s, after_epoch=self.epoch)
+        if h.kind == "abandoned":
+            raise EngineDown(f"the coordinator abandoned epoch {h.epoch}: {h.detail}")
+        mc = h.committed
+        rec = ChangeRecord(mc.epoch, list(mc.lost), 0, t_detect, t_committed=time.monotonic(), t_fault=self.t_kill)
+        self.t_kill = 0.0
+        rec.coordinator = {"reported_to_committed_ms": (mc.committed_at_us - mc.reported_at_us) / 1e3
+                           if mc.reported_at_us else None, "pause_ms": mc.pause_ms}
+        lost = [r for r in mc.lost]
+        for r in lost:
+            link = self.links.pop(r, None)
+            if link is None:
+                continue
+            if not link.closed.is_set():
+                try:  # a planned departure: it drains its commits and leaves
+                    link.send({"op": "release"})
+                    while link.get(timeout=self.change_timeout_s).get("op") != "released":
+                        pass
+                except (LinkClosed, TimeoutError):
+                    pass
+            link.close()
+        payload = pickle.dumps({"carrier": self.carrier.address, "epoch": mc.epoch})
+        for r in lost:
+            self.client.join(r, mc.epoch, payload)
+        for r in lost:
+            link = self.carrier.wait_link(self.change_timeout_s, want=lambda hl, r=r: int(hl["rank"]) == r)
+            self.links[r] = link
+        rec.t_joined = time.monotonic()
+        rec.outcome = 1 if lost else 0  # OUTCOME_REPLACE: a spare holds each lost rank
+        self.links = dict(sorted(self.links.items()))
+        computed = self._boundary(mc.epoch)
+        rec.t_ready = time.monotonic()
+        self.epoch = mc.epoch
+        sch = engine.scheduler
+        for req in sch.running:
+            req.committed = min(int(c.get(req.req_id, 0)) for c in computed.values())
+        sch.resume_from_committed()
+        rec.t_resumed = time.monotonic()
+        self.changes.append(rec)
+        return rec
+
+    def shutdown(self) -> None:
+        for link in self.links.values():
+            try:
+                link.send({"op": "stop"})
+            except LinkClosed:
+                pass
+        deadline = time.monotonic() + 30
+        for p in self.procs.values():
+            if p.poll() is None and not any(p.pid == int(link.hello["pid"]) for link in self.links.values()):
+                p.terminate()
+            try:
+                p.wait(timeout=max(0.1, deadline - time.monotonic()))
+            except subprocess.TimeoutExpired:
+                p.kill()
+                p.wait()
+        if self.client is not None:
+            self.client.close()
+        self.carrier.close()
+        for f in self._logs:
+            f.close()
+
+
+def failover(executor: MultiprocExecutor, engine):
+    """The step wrapper: a step that loses a rank completes the membership change and retries."""
+
+    def wrap(step_fn):
+        def step():
+            while True:
+                try:
+                    return step_fn()
+                except RankLost:
+                    executor.complete_change(engine, t_detect=time.monotonic())
+
+        return step
+
+    return wrap

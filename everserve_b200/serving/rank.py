@@ -1,0 +1,298 @@
+"""A rank process of a multi-process engine: a worker, or a spare standing for a rank.
+
+    python -m everserve_b200.serving.rank --role worker --rank 1 --engine e0 --model qwen2.5-0.5b \
+        --tp 1 --pp 2 --head 127.0.0.1:PORT --rdzv 127.0.0.1:PORT --daemon unix:/run/n0.sock \
+        --store unix:/run/store.sock [--device cpu] [--dtype float32] [--num-blocks N]
+    python -m everserve_b200.serving.rank --role spare --rank 1 ...   # stands for rank 1
+
+A worker builds its shard (stage layers, tensor column, paged KV cache), registers with its node's
+daemon (``ROLE_WORKER``), links to the head and serves ops:
+
+* ``step``: run the plan (receive the previous stage's output, forward, send to the next stage),
+  then commit the step's KV rows and the requests' computed counts to the node's store
+  (``MirrorCommittedKV``: a gather into a mapped staging file and a sender thread), fence the
+  commit ``depth`` steps back, and reply (the last stage's column 0 with the sampled ids);
+* ``boundary``: form the new epoch's groups (a rendezvous with every member of the epoch) and
+  reply with what its cache holds (per-request computed counts);
+* ``release``: a departing rank drains its commits and leaves (Goodbye, exit 0);
+* ``stop``: leave.
+
+A membership change reaches the rank through the daemon first (``Change``): the rank refuses its
+live groups (so a send to a dead peer errors instead of waiting) unless only departures are
+planned, and acks. The head then cuts the step and sends ``boundary``.
+
+A spare builds the same shard ahead of time (weights, cache, a warm-up forward) and registers as
+``ROLE_SPARE`` for its rank. When a ``Change`` names it in ``take``, it restores the lost rank's
+committed KV from its node's store before it acks; the head's ``Join`` offer then tells it where to
+link, it catches up on rows committed since its restore (a departing rank commits until the
+boundary) and serves as the rank from then on.
+
+Reference parity: the worker side of adapters/vllm/everserve_vllm/worker.py:1089-1266 (bootstrap,
+boundary, resume, release_position) and the spare of spare_main.py / spare.py:96-281 (stand,
+restore before the ack, join, catch-up).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import os
+import pickle
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+from ..contract.daemon import DaemonConnection
+from ..engine.config import EngineConfig
+from ..engine.worker import Worker
+from ..proto import signals as sp
+from ..runtime.groups import Exchange, GroupCollective, SwappableGroups
+from ..runtime.layout import ParallelLayout
+from ..runtime.runtime import Runtime
+from ..state.kvcopy import PagedKV
+from ..state.mirror import DEPTH, MirrorClient, MirrorCommittedKV
+from .carrier import CarrierClient
+
+_DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
+
+
+def _store(addr: str, timeout_s: float = 60.0):
+    host, _, port = addr.rpartition(":")
+    return dist.TCPStore(host, int(port), is_master=False, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+class RankProcess:
+    def __init__(self, a: argparse.Namespace):
+        self.a = a
+        self.engine = a.engine
+        self.spare = a.role == "spare"
+        self.rank = a.rank
+        self.layout = ParallelLayout(a.tp, a.pp)
+        dev = torch.device(a.device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        self.device = dev
+        self.cfg = EngineConfig(model=a.model, device=str(dev), dtype=_DTYPES[a.dtype], seed=a.seed,
+                                block_size=a.block_size, num_blocks=a.num_blocks, max_batch=a.max_batch,
+                                max_model_len=a.max_model_len, tensor_parallel=a.tp, pipeline_parallel=a.pp,
+                                use_cuda_graphs=False)
+        self.runtime = Runtime(self.rank)
+        self.rdzv = _store(a.rdzv)
+        self.groups = SwappableGroups(self.rdzv, self.rank, self.layout, dev, timeout_s=a.group_timeout)
+        mc = self.cfg.model
+        self.exchange = Exchange(self.groups, mc.hidden, self.cfg.dtype) if a.pp > 1 else None
+        coll = GroupCollective(self.groups) if a.tp > 1 else None
+        t0 = time.monotonic()
+        self.worker = Worker(self.cfg, rank=self.rank, collective=coll, pipe=self.exchange, device=str(dev))
+        self.caches = self.worker.runner.caches
+        hkv = max(1, mc.kv_heads // a.tp)
+        self.kv = PagedKV("heads_blocked", self.worker.num_blocks, a.block_size, hkv, mc.head_dim)
+        self.ckv = None
+        if a.store:
+            self.ckv = MirrorCommittedKV(MirrorClient(a.store), self.engine, self.rank, self.caches, self.kv,
+                                         store_slots=self.worker.num_blocks * a.block_size)
+        self.load_s = time.monotonic() - t0
+        self.computed: dict[str, int] = {}
+        self._commits: list[int] = []
+        self.carrier: CarrierClient | None = None
+        self.joined = threading.Event()
+        self.join_payload: dict | None = None
+        self.leaving = False
+        self.taken = False
+        self.daemon = None
+        if a.daemon:
+            self.daemon = DaemonConnection(a.daemon, self.engine, self, role=sp.ROLE_SPARE if self.spare else sp.ROLE_WORKER,
+                                           stage=[self.layout.stage(self.rank)], node=a.node)
+
+    # ---- participant (daemon reader thread) ------------------------------------------------------
+    def identity(self) -> tuple[int, int]:
+        return self.rank, self.device.index or 0 if self.device.type == "cuda" else 0
+
+    def on_change(self, change) -> str | None:
+        self.runtime.trace("change", epoch=change.epoch)
+        if self.spare and not self.taken:
+            takes = [t for t in change.take if t.rank == self.rank]
+            if not takes:
+                return None
+            try:
+                counts = self.ckv.restore(self.rank) if self.ckv is not None else {}
+            except Exception as e:  # noqa: BLE001 - reported in the ack
+                return f"restore failed: {e}"
+            self.computed = dict(counts)
+            self.taken = True
+            self.runtime.stage_change(change)
+            self.runtime.trace("restored", rows_step=self.ckv.restored_step if self.ckv else -1)
+            return None
+        self.runtime.stage_change(change)
+        if self.rank in change.departing:
+            self.leaving = True  # finish the step; the head releases this rank at the boundary
+        elif not set(change.lost) <= set(change.departing):
+            self.groups.refuse()
+        return None
+
+    def on_notice(self, rank: int, deadline_ms: int) -> None:
+        self.runtime.trace("notice", rank=rank, deadline_ms=deadline_ms)
+
+    def on_abandoned(self, epoch: int, detail: str) -> None:
+        self.runtime.trace("abandoned", epoch=epoch, detail=detail)
+        self.runtime.fault.set()
+
+    def on_committed(self, committed) -> None:
+        self.runtime.trace("committed", epoch=committed.epoch)
+
+    def on_join(self, join) -> None:
+        try:
+            self.join_payload = pickle.loads(join.payload)
+        except Exception:  # noqa: BLE001 - a malformed offer is ignored
+            return
+        self.joined.set()
+
+    def on_displaced(self, epoch: int, why: str) -> None:
+        self.runtime.trace("displaced", epoch=epoch, why=why)
+
+    # ---- serving ---------------------------------------------------------------------------------
+    def warm(self) -> None:
+        """One forward of a dummy step so the first real step pays no lazy set-up."""
+        from ..engine.scheduler import ScheduledReq, StepPlan
+
+        if self.layout.world > 1:
+            return  # a lone forward of a middle stage has no peer; warm-up happens on the first step
+        plan = StepPlan(0, False, [ScheduledReq("warm", [1], 0, [0], True)])
+        self.worker.execute(plan)
+
+    def link(self, address: str) -> None:
+        hello = {"rank": self.rank, "pid": os.getpid(), "role": "spare" if self.spare else "worker",
+                 "num_blocks": self.worker.num_blocks, "computed": dict(self.computed), "load_s": self.load_s}
+        self.carrier = CarrierClient(address, hello)
+
+    def serve(self) -> int:
+        assert self.carrier is not None
+        while True:
+            try:
+                msg = self.carrier.recv()
+            except (ConnectionError, OSError, EOFError):
+                return 1  # the head is gone
+            op = msg["op"]
+            if op == "step":
+                self._step(msg)
+            elif op == "boundary":
+                self._boundary(msg)
+            elif op == "finished":
+                if self.ckv is not None and self.layout.stage(self.rank) == 0 and self.layout.column(self.rank) == 0:
+                    for rid in msg["ids"]:
+                        self.ckv.finished(rid)
+                for rid in msg["ids"]:
+                    self.computed.pop(rid, None)
+            elif op == "release":
+                self._drain()
+                self.carrier.send({"op": "released", "rank": self.rank})
+                if self.daemon is not None:
+                    self.daemon.close(sp.STOP_CAUSE_STOPPED)
+                return 0
+            elif op == "stop":
+                self._drain()
+                if self.daemon is not None:
+                    self.daemon.close(sp.STOP_CAUSE_STOPPED)
+                return 0
+
+    def _drain(self) -> None:
+        if self.ckv is not None and self._commits:
+            try:
+                self.ckv.fence(self._commits[-1], timeout_s=30.0)
+            except Exception:  # noqa: BLE001
+                pass
+
+    def _step(self, msg: dict) -> None:
+        plan = msg["plan"]
+        if msg.get("fail_at") == plan.step and self.rank == msg.get("fail_rank"):
+            os.kill(os.getpid(), 9)  # fault injection on the host: this process dies mid-decode
+        try:
+            if msg["epoch"] != self.runtime.epoch:
+                raise RuntimeError(f"step of epoch {msg['epoch']} on a rank at epoch {self.runtime.epoch}")
+            out = self.worker.execute(plan)
+            counts = {r.req_id: r.start_pos + len(r.token_ids) for r in plan.reqs}
+            self.computed.update(counts)
+            if self.ckv is not None:
+                slots = [s for row in plan.slots(self.a.block_size) for s in row]
+                self.ckv.commit(self.runtime.epoch, plan.step, counts, slots)
+                self._commits.append(plan.step)
+                if len(self._commits) > DEPTH:
+                    self.ckv.fence(self._commits[-1 - DEPTH])
+                del self._commits[:-(DEPTH + 1)]
+            reply = {"op": "done", "step": plan.step, "rank": self.rank}
+            if out is not None and self.layout.column(self.rank) == 0:
+                reply["ids"] = out.tolist() if isinstance(out, torch.Tensor) else list(out)
+        except Exception as e:  # noqa: BLE001 - the head decides what a failed step means
+            reply = {"op": "error", "step": plan.step, "rank": self.rank, "error": f"{type(e).__name__}: {e}"}
+        self.carrier.send(reply)
+
+    def _boundary(self, msg: dict) -> None:
+        epoch = int(msg["epoch"])
+        t0 = time.monotonic()
+        try:
+            if self.spare and self.ckv is not None and self.ckv.restored_step >= 0:
+                # rows the departing (or last) holder committed after the restore
+                counts = self.ckv.restore(self.rank, since_step=self.ckv.restored_step + 1)
+                self.computed.update(counts)
+            self.groups.form(epoch, self.rank)
+            self.runtime.at_boundary(epoch)
+            reply = {"op": "ready", "epoch": epoch, "rank": self.rank, "computed": dict(self.computed),
+                     "form_s": time.monotonic() - t0}
+        except Exception as e:  # noqa: BLE001
+            reply = {"op": "error", "epoch": epoch, "rank": self.rank, "error": f"{type(e).__name__}: {e}"}
+        self.carrier.send(reply)
+
+    def close(self) -> None:
+        if self.ckv is not None:
+            self.ckv.close()
+
+
+def parse(argv=None) -> argparse.Namespace:
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--role", choices=["worker", "spare"], default="worker")
+    p.add_argument("--rank", type=int, required=True)
+    p.add_argument("--engine", default="engine")
+    p.add_argument("--model", default="qwen2.5-0.5b")
+    p.add_argument("--tp", type=int, default=1)
+    p.add_argument("--pp", type=int, default=1)
+    p.add_argument("--device", default="cpu")
+    p.add_argument("--dtype", default="float32", choices=list(_DTYPES))
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--block-size", type=int, default=16)
+    p.add_argument("--num-blocks", type=int, default=None)
+    p.add_argument("--max-batch", type=int, default=16)
+    p.add_argument("--max-model-len", type=int, default=512)
+    p.add_argument("--head", default="", help="the head's carrier address (workers)")
+    p.add_argument("--rdzv", required=True, help="host:port of the engine's rendezvous store")
+    p.add_argument("--daemon", default=os.environ.get("EVERSERVE_SOCKET", ""))
+    p.add_argument("--store", default=os.environ.get("EVERSERVE_MIRROR_SOCKET", ""))
+    p.add_argument("--node", default=os.environ.get("EVERSERVE_NODE", ""))
+    p.add_argument("--group-timeout", type=float, default=30.0)
+    p.add_argument("--threads", type=int, default=0)
+    return p.parse_args(argv)
+
+
+def main(argv=None) -> int:
+    a = parse(argv)
+    if a.threads:
+        torch.set_num_threads(a.threads)
+    rp = RankProcess(a)
+    try:
+        if rp.spare:
+            rp.warm()
+            while not rp.joined.wait(0.1):
+                pass
+            assert rp.join_payload is not None
+            rp.link(rp.join_payload["carrier"])
+        else:
+            rp.link(a.head)
+        return rp.serve()
+    finally:
+        rp.close()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -147,6 +147,7 @@ class MirrorCommittedKV:
         self._ack_cond = threading.Condition()
         self._error: BaseException | None = None
         self._committed: dict[str, int] = {}
+        self.restored_step = -1  # the last step a restore covered
         self._pending_slots: list[int] = []
         self._history: list[dict] = []
         self.stats_record = {"commits": 0, "fence_waits": 0, "fence_wait_s": 0.0, "bytes": 0}
@@ -318,6 +319,7 @@ class MirrorCommittedKV:
     def restore(self, dead_rank: int, moves=None, since_step: int = 0) -> dict[str, int]:
         """Write `dead_rank`'s committed rows into this rank's caches; returns committed counts."""
         rep = self.client.restore(self.engine, dead_rank, since_step)
+        self.restored_step = int(rep.step)
         for ref in rep.tables:
             layer, head = divmod(ref.layer, TABLE_STRIDE)
             if layer >= len(self.caches) or head not in self.heads:

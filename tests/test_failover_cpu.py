@@ -1,0 +1,80 @@
+"""Failover on the CPU tier: a pipeline-parallel engine loses a rank mid-decode and a spare takes it.
+
+TP1 PP2 (world size 2) plus one spare standing for rank 1, with the C++ coordinator, node daemon
+and KV store. Rank 1 is SIGKILLed at decode step 20; the coordinator replaces it with the spare,
+which restores rank 1's committed KV from the store; the engine resumes every stream from its
+committed tokens and every stream must complete token-identical to the no-fault run.
+
+The default runs a narrow model of the same architecture (fast); ``ES_FULL_CONFIG1=1`` runs the
+full Qwen2.5-0.5B shape (24 layers, hidden 896, vocab 151936) with 8 streams x 128-token prompts
+and 64 greedy tokens, the reference's own configuration.
+"""
+
+import os
+import random
+
+import pytest
+import torch
+
+from everserve_b200.engine.config import EngineConfig
+from everserve_b200.engine.engine import Engine
+from everserve_b200.models.config import get_config
+from everserve_b200.serving.cluster import ControlPlane
+from everserve_b200.serving.executor import MultiprocExecutor, failover
+
+FULL = os.environ.get("ES_FULL_CONFIG1") == "1"
+MODEL = "qwen2.5-0.5b" if FULL else "tiny-qwen"
+STREAMS, PROMPT, TOKENS, KILL_AT = 8, 128, (64 if FULL else 28), 20
+
+
+def _prompts():
+    rng = random.Random(0)
+    vocab = get_config(MODEL).vocab
+    return [[rng.randrange(vocab) for _ in range(PROMPT)] for _ in range(STREAMS)]
+
+
+def _run(workdir, kill_at=None, spares=(1,)):
+    cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
+                       max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
+    with ControlPlane(str(workdir), engines=[{"name": "e0", "pipelineParallel": 2}]) as cp:
+        ex = MultiprocExecutor(cfg, engine="e0", daemon=cp.daemon_socket, store=cp.store_socket, spares=spares,
+                               node="n0", log_dir=str(workdir / "logs"), threads=2)
+        try:
+            if spares:
+                cp.wait_spares("e0", len(spares))
+            eng = Engine(cfg, executor=ex)
+            eng.wrap_step(failover(ex, eng))
+            if kill_at is not None:
+                ex.kill_at_decode_step = (kill_at, 1)
+            out = eng.generate(_prompts(), max_tokens=TOKENS)
+            mism = sum(r.replay_mismatches for r in eng.scheduler.requests.values())
+            view = cp.engine_view("e0")
+            return out, ex.changes, mism, view
+        finally:
+            ex.shutdown()
+
+
+@pytest.mark.slow
+def test_sigkill_rank1_spare_takes_over_token_identical(tmp_path):
+    base, changes0, _, _ = _run(tmp_path / "nofault", spares=())
+    assert changes0 == []
+    out, changes, mism, view = _run(tmp_path / "fault", kill_at=KILL_AT)
+    assert len(changes) == 1
+    rec = changes[0].as_dict()
+    assert rec["lost"] == [1] and rec["epoch"] == 1
+    assert rec["from"] == "fault" and rec["resumed_ms"] is not None
+    assert mism == 0
+    assert out == base, "streams differ from the no-fault run"
+    assert all(len(o) == TOKENS for o in out)
+    # the coordinator's view: epoch 1, the spare holds rank 1, no spare left standing
+    st = view["status"]
+    assert st["epoch"] == 1 and not st["down"] and st["spares"] == []
+    assert sorted(w["rank"] for w in st["workers"]) == [0, 1]
+
+
+@pytest.mark.slow
+def test_loss_without_spare_abandons(tmp_path):
+    from everserve_b200.serving.executor import EngineDown
+
+    with pytest.raises(EngineDown):
+        _run(tmp_path / "nospare", kill_at=3, spares=())
