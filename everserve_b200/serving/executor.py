@@ -135,6 +135,7 @@ class MultiprocExecutor:
         self.changes: list[ChangeRecord] = []
         self.decode_steps_run = 0
         self.kill_at_decode_step: tuple[int, int] | None = None  # (decode step, rank): host-side fault injection
+        self.notice_at_decode_step: tuple[int, int] | None = None  # (decode step, rank): a planned departure
         self.t_kill = 0.0
         self._finished: list[str] = []
 
@@ -167,6 +168,10 @@ class MultiprocExecutor:
             if self.kill_at_decode_step and self.decode_steps_run == self.kill_at_decode_step[0]:
                 victim = self.kill_at_decode_step[1]
                 self.kill_at_decode_step = None
+            if self.notice_at_decode_step and self.decode_steps_run == self.notice_at_decode_step[0]:
+                self.t_kill = time.monotonic()
+                self.notice(self.notice_at_decode_step[1])
+                self.notice_at_decode_step = None
         lost, errors = set(), {}
         for r, link in self.links.items():
             try:
@@ -227,6 +232,15 @@ class MultiprocExecutor:
         return computed
 
     # ---- membership change -----------------------------------------------------------------------
+    def notice(self, rank: int, deadline_ms: int = 0) -> None:
+        """Announce a planned departure of `rank` (drain): it finishes its step and leaves."""
+        if self.client is None:
+            raise EngineDown("no daemon link")
+        self.client.notice(rank, deadline_ms or int(time.time() * 1000) + 30_000)
+
+    def change_pending(self) -> bool:
+        return self.client is not None and self.client.pending_change.is_set()
+
     def complete_change(self, engine, t_detect: float | None = None) -> ChangeRecord:
         if self.client is None:
             raise EngineDown("no daemon link: a lost rank cannot be replaced")
@@ -301,9 +315,13 @@ def failover(executor: MultiprocExecutor, engine):
         def step():
             while True:
                 try:
-                    return step_fn()
+                    out = step_fn()
                 except RankLost:
                     executor.complete_change(engine, t_detect=time.monotonic())
+                    continue
+                if executor.change_pending():  # a planned change: complete it at this boundary
+                    executor.complete_change(engine, t_detect=time.monotonic())
+                return out
 
         return step
 

@@ -78,3 +78,25 @@ def test_loss_without_spare_abandons(tmp_path):
 
     with pytest.raises(EngineDown):
         _run(tmp_path / "nospare", kill_at=3, spares=())
+
+
+@pytest.mark.slow
+def test_planned_departure_spare_catches_up(tmp_path):
+    base, _, _, _ = _run(tmp_path / "nofault", spares=())
+    cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
+                       max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
+    with ControlPlane(str(tmp_path / "drain"), engines=[{"name": "e0", "pipelineParallel": 2}]) as cp:
+        ex = MultiprocExecutor(cfg, engine="e0", daemon=cp.daemon_socket, store=cp.store_socket, spares=(1,),
+                               node="n0", log_dir=str(tmp_path / "drain" / "logs"), threads=2)
+        try:
+            cp.wait_spares("e0", 1)
+            eng = Engine(cfg, executor=ex)
+            eng.wrap_step(failover(ex, eng))
+            ex.notice_at_decode_step = (10, 1)
+            out = eng.generate(_prompts(), max_tokens=TOKENS)
+            assert len(ex.changes) == 1 and ex.changes[0].lost == [1]
+            assert out == base
+            # the departing rank left cleanly (released, exit 0)
+            assert ex.procs["rank1"].wait(timeout=30) == 0
+        finally:
+            ex.shutdown()
