@@ -29,7 +29,7 @@ install, resume) and the step-loop hook of serving.py:44-86.
 from __future__ import annotations
 
 import os
-import pickle
+import secrets
 import signal
 import subprocess
 import sys
@@ -38,6 +38,7 @@ from dataclasses import dataclass, field
 
 import torch.distributed as dist
 
+from ..contract import join as joinfmt
 from ..contract.daemon import DaemonClient
 from ..engine.config import EngineConfig
 from ..runtime.layout import ParallelLayout
@@ -88,7 +89,8 @@ class MultiprocExecutor:
         self.layout = ParallelLayout(cfg.tensor_parallel, cfg.pipeline_parallel)
         self.step_timeout_s = step_timeout_s
         self.change_timeout_s = change_timeout_s
-        self.carrier = CarrierServer()
+        self.token = secrets.token_hex(16)
+        self.carrier = CarrierServer(token=self.token)
         self.rdzv = dist.TCPStore("127.0.0.1", 0, is_master=True, wait_for_workers=False)
         self.rdzv_addr = f"127.0.0.1:{self.rdzv.port}"
         self.log_dir = log_dir
@@ -113,6 +115,7 @@ class MultiprocExecutor:
         root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         e["PYTHONPATH"] = os.pathsep.join([root] + [p for p in e.get("PYTHONPATH", "").split(os.pathsep) if p])
         e.update(env or {})
+        e["EVERSERVE_CARRIER_TOKEN"] = self.token
         for r in range(self.layout.world):
             self._spawn(f"rank{r}", base + ["--role", "worker", "--rank", str(r)], e)
         for i, r in enumerate(spares):
@@ -254,11 +257,13 @@ class MultiprocExecutor:
         rec.coordinator = {"reported_to_committed_ms": (mc.committed_at_us - mc.reported_at_us) / 1e3
                            if mc.reported_at_us else None, "pause_ms": mc.pause_ms}
         lost = [r for r in mc.lost]
+        departed = set()
         for r in lost:
             link = self.links.pop(r, None)
             if link is None:
                 continue
             if not link.closed.is_set():
+                departed.add(r)
                 try:  # a planned departure: it drains its commits and leaves
                     link.send({"op": "release"})
                     while link.get(timeout=self.change_timeout_s).get("op") != "released":
@@ -266,9 +271,10 @@ class MultiprocExecutor:
                 except (LinkClosed, TimeoutError):
                     pass
             link.close()
-        payload = pickle.dumps({"carrier": self.carrier.address, "epoch": mc.epoch})
         for r in lost:
-            self.client.join(r, mc.epoch, payload)
+            offer = joinfmt.Offer(rank=r, epoch=mc.epoch, carrier=self.carrier.address, token=self.token,
+                                  faulted=r not in departed)
+            self.client.join(r, mc.epoch, joinfmt.encode(offer))
         for r in lost:
             link = self.carrier.wait_link(self.change_timeout_s, want=lambda hl, r=r: int(hl["rank"]) == r)
             self.links[r] = link

@@ -37,7 +37,6 @@ from __future__ import annotations
 import argparse
 import datetime
 import os
-import pickle
 import sys
 import threading
 import time
@@ -45,6 +44,7 @@ import time
 import torch
 import torch.distributed as dist
 
+from ..contract import join as joinfmt
 from ..contract.daemon import DaemonConnection
 from ..engine.config import EngineConfig
 from ..engine.worker import Worker
@@ -99,7 +99,7 @@ class RankProcess:
         self._commits: list[int] = []
         self.carrier: CarrierClient | None = None
         self.joined = threading.Event()
-        self.join_payload: dict | None = None
+        self.offer: joinfmt.Offer | None = None
         self.leaving = False
         self.taken = False
         self.daemon = None
@@ -145,10 +145,13 @@ class RankProcess:
 
     def on_join(self, join) -> None:
         try:
-            self.join_payload = pickle.loads(join.payload)
-        except Exception:  # noqa: BLE001 - a malformed offer is ignored
+            offer = joinfmt.decode(join.payload)
+        except joinfmt.JoinFormatError as e:
+            self.runtime.trace("join refused", why=str(e))
             return
-        self.joined.set()
+        if isinstance(offer, joinfmt.Offer) and offer.rank == self.rank:
+            self.offer = offer
+            self.joined.set()
 
     def on_displaced(self, epoch: int, why: str) -> None:
         self.runtime.trace("displaced", epoch=epoch, why=why)
@@ -163,8 +166,8 @@ class RankProcess:
         plan = StepPlan(0, False, [ScheduledReq("warm", [1], 0, [0], True)])
         self.worker.execute(plan)
 
-    def link(self, address: str) -> None:
-        hello = {"rank": self.rank, "pid": os.getpid(), "role": "spare" if self.spare else "worker",
+    def link(self, address: str, token: str) -> None:
+        hello = {"rank": self.rank, "pid": os.getpid(), "role": "spare" if self.spare else "worker", "token": token,
                  "num_blocks": self.worker.num_blocks, "computed": dict(self.computed), "load_s": self.load_s}
         self.carrier = CarrierClient(address, hello)
 
@@ -285,10 +288,10 @@ def main(argv=None) -> int:
             rp.warm()
             while not rp.joined.wait(0.1):
                 pass
-            assert rp.join_payload is not None
-            rp.link(rp.join_payload["carrier"])
+            assert rp.offer is not None
+            rp.link(rp.offer.carrier, rp.offer.token)
         else:
-            rp.link(a.head)
+            rp.link(a.head, os.environ.get("EVERSERVE_CARRIER_TOKEN", ""))
         return rp.serve()
     finally:
         rp.close()
