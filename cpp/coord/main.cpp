@@ -58,6 +58,7 @@ struct InFlight {
 
 struct Engine {
   std::string name;
+  std::string fingerprint;  // the first worker's identity fingerprint
   uint64_t epoch = 0;
   uint32_t world = 0;
   std::map<uint32_t, Holder> workers;
@@ -197,7 +198,7 @@ struct Coordinator {
   void drive(Engine& e) {
     if (e.in_flight || e.pending.empty() || e.down) return;
     const uint64_t t0 = now_us();
-    Choice c = choose_outcome(policy, e.name, e.pending, e.spares);
+    Choice c = choose_outcome(policy, e.name, e.pending, e.spares, e.fingerprint);
     metrics().observe("everserve_change_decision_seconds", {{"engine", e.name}}, (now_us() - t0) * 1e-6);
     if (c.outcome == 0) {
       abandon(e, "no outcome: " + c.why);
@@ -383,6 +384,14 @@ struct Coordinator {
   }
 
   // ---- daemon links ----------------------------------------------------------------------------
+  static std::string fingerprint_of(const coord::WorkerEvent& ev) {
+    if (!ev.has_identity) return "";
+    const auto& id = ev.identity;
+    return id.engine_commit + "|" + id.torch_version + "|" + id.model + "|" + id.checkpoint_digest + "|" +
+           id.model_dtype + "|" + id.kv_format.dtype + ":" + std::to_string(id.kv_format.block_size) + "|" +
+           std::to_string(id.layout.tensor) + "x" + std::to_string(id.layout.pipeline) + "|" + id.step.digest;
+  }
+
   void on_worker_event(const std::string& node, const coord::WorkerEvent& ev) {
     Engine& e = engine(ev.engine);
     using K = coord::WorkerEvent_Kind;
@@ -394,6 +403,7 @@ struct Coordinator {
         h.pid = ev.pid;
         h.host = ev.host;
         e.workers[ev.rank] = h;
+        if (e.fingerprint.empty()) e.fingerprint = fingerprint_of(ev);
         e.epoch = std::max(e.epoch, ev.epoch);
         if (e.down && e.workers.size() >= std::max<uint32_t>(1, e.world)) {
           e.down = false;
@@ -407,6 +417,11 @@ struct Coordinator {
         s.device = ev.device;
         s.for_rank = ev.any_rank ? -1 : (int64_t)ev.rank;
         s.pid = ev.pid;
+        s.fingerprint = fingerprint_of(ev);
+        if (!e.fingerprint.empty() && !s.fingerprint.empty() && s.fingerprint != e.fingerprint) {
+          metrics().inc("everserve_spares_mismatched_total", {{"engine", e.name}});
+          event("engine " + e.name + ": spare on " + node + " has another software identity; it cannot take a rank");
+        }
         e.spares.push_back(s);
         break;
       }

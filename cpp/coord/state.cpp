@@ -63,7 +63,7 @@ bool parse_policy(const std::string& json, Policy& out, std::string& err) {
 }
 
 Choice choose_outcome(const Policy& p, const std::string& engine, const std::set<uint32_t>& lost,
-                      const std::vector<SpareSeat>& spares) {
+                      const std::vector<SpareSeat>& spares, const std::string& fingerprint) {
   Choice c;
   if (p.max_concurrent_losses && lost.size() > p.max_concurrent_losses) {
     c.why = "more concurrent losses than the policy allows";
@@ -73,6 +73,9 @@ Choice choose_outcome(const Policy& p, const std::string& engine, const std::set
   for (int32_t want : p.outcomes) {
     if (want == signals::Outcome_OUTCOME_REPLACE) {
       std::vector<bool> used(spares.size(), false);
+      for (size_t i = 0; i < spares.size(); i++)  // another build cannot take a rank exactly
+        if (!fingerprint.empty() && !spares[i].fingerprint.empty() && spares[i].fingerprint != fingerprint)
+          used[i] = true;
       std::vector<std::pair<uint32_t, SpareSeat>> take;
       bool all = true;
       for (uint32_t r : lost) {

@@ -35,6 +35,7 @@ struct SpareSeat {
   uint32_t device = 0;
   int64_t for_rank = -1;  // -1: any rank
   uint32_t pid = 0;
+  std::string fingerprint;  // what must match the engine's ranks for an exact take ("" unknown)
 };
 
 struct Choice {
@@ -46,7 +47,9 @@ struct Choice {
 // REPLACE when a spare stands for every lost rank (its own rank first, then any-rank spares in
 // node order), else SHRINK when the policy allows it and the model is placement independent,
 // else nothing: the engine is abandoned. The preference order is the policy's.
+// A spare whose fingerprint is known and differs from the engine's (another build, model, KV
+// format or step configuration) is not eligible.
 Choice choose_outcome(const Policy& p, const std::string& engine, const std::set<uint32_t>& lost,
-                      const std::vector<SpareSeat>& spares);
+                      const std::vector<SpareSeat>& spares, const std::string& fingerprint = "");
 
 }  // namespace es

@@ -168,7 +168,8 @@ class DaemonConnection(HearsEngine):
     """A worker's or spare's connection (see the module doc)."""
 
     def __init__(self, path: str, engine: str, participant: Participant, role: int = sp.ROLE_WORKER,
-                 any_rank: bool = False, stage: Sequence[int] = (), timeout_s: float = 10.0, node: str = ""):
+                 any_rank: bool = False, stage: Sequence[int] = (), timeout_s: float = 10.0, node: str = "",
+                 identity=None):
         super().__init__()
         self.engine_name = engine
         self.participant = participant
@@ -182,6 +183,8 @@ class DaemonConnection(HearsEngine):
         reg = sp.Register(engine=engine, rank=rank, role=role, any_rank=any_rank, protocol=PROTOCOL,
                           protocol_oldest=PROTOCOL_OLDEST, launcher_pid=os.getpid(), host=own_host(),
                           stage=list(stage), member=sp.Member(node=self.node, device=device))
+        if identity is not None:
+            reg.identity.CopyFrom(identity)
         self._link.send(sp.Signal(register=reg))
         self._reader = threading.Thread(target=self._serve, name=f"daemon-{engine}-{rank}", daemon=True)
         self._reader.start()

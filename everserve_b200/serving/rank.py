@@ -104,8 +104,11 @@ class RankProcess:
         self.taken = False
         self.daemon = None
         if a.daemon:
+            from ..contract.identity import identity
+
             self.daemon = DaemonConnection(a.daemon, self.engine, self, role=sp.ROLE_SPARE if self.spare else sp.ROLE_WORKER,
-                                           stage=[self.layout.stage(self.rank)], node=a.node)
+                                           stage=[self.layout.stage(self.rank)], node=a.node,
+                                           identity=identity(self.cfg, self.engine))
 
     # ---- participant (daemon reader thread) ------------------------------------------------------
     def identity(self) -> tuple[int, int]:

@@ -1,0 +1,52 @@
+"""Settings read from the environment, with the defaults the runtime uses.
+
+| variable | default | meaning |
+|---|---|---|
+| ``EVERSERVE_DETECT_STEPS`` | 3 | a collective waits this many measured step periods before it names late members |
+| ``EVERSERVE_DETECT_FLOOR_MS`` | 30 | ... but never less than this |
+| ``EVERSERVE_HANG_S`` | 10 | a late member that is alive is hung after this long |
+| ``EVERSERVE_POLL_MS`` | 2 | the failure detector's poll period |
+| ``EVERSERVE_RELEASE_BOUND_MS`` | 10000 | how long a boundary waits for a refused group's release |
+| ``EVERSERVE_STEP_SAMPLE`` | 16 | steps measured before the bound is set from the step period |
+| ``EVERSERVE_NODE`` | host name | this node's name in the control plane |
+
+Reference parity: adapters/vllm/everserve_vllm/settings.py:54-99 (same defaults: 3 steps, a 30 ms
+floor, 10 s to hung, a 2 ms poll).
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+from dataclasses import dataclass
+
+
+def _f(name: str, default: float) -> float:
+    v = os.environ.get(name, "")
+    try:
+        return float(v) if v else default
+    except ValueError:
+        raise ValueError(f"{name}={v!r} is not a number") from None
+
+
+@dataclass(frozen=True)
+class Settings:
+    detect_steps: float = 3.0
+    detect_floor_ms: float = 30.0
+    hang_s: float = 10.0
+    poll_ms: float = 2.0
+    release_bound_ms: float = 10000.0
+    step_sample: int = 16
+    node: str = ""
+
+    def bound_ns(self, step_period_s: float) -> int:
+        """The collective's wait bound for a measured step period."""
+        return int(max(self.detect_steps * step_period_s * 1e3, self.detect_floor_ms) * 1e6)
+
+
+def load() -> Settings:
+    return Settings(
+        detect_steps=_f("EVERSERVE_DETECT_STEPS", 3.0), detect_floor_ms=_f("EVERSERVE_DETECT_FLOOR_MS", 30.0),
+        hang_s=_f("EVERSERVE_HANG_S", 10.0), poll_ms=_f("EVERSERVE_POLL_MS", 2.0),
+        release_bound_ms=_f("EVERSERVE_RELEASE_BOUND_MS", 10000.0), step_sample=int(_f("EVERSERVE_STEP_SAMPLE", 16)),
+        node=os.environ.get("EVERSERVE_NODE", socket.gethostname()))
