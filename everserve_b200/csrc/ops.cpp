@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "api.h"
+#include "vmm.h"
 
 namespace {
 
@@ -321,6 +322,38 @@ int64_t ipc_open(const std::string& handle) {
 
 void ipc_close(int64_t ptr) { ES_CHECK_CUDA(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr))); }
 
+int cur_device() {
+  int d = 0;
+  ES_CHECK_CUDA(cudaGetDevice(&d));
+  return d;
+}
+
+// (ptr, size, handle, fd) of a new exportable buffer on the current device, zeroed.
+std::tuple<int64_t, int64_t, int64_t, int64_t> vmm_create(int64_t bytes) {
+  es::vmm::Buffer b;
+  const char* err = "";
+  TORCH_CHECK(es::vmm::create(cur_device(), (uint64_t)bytes, b, &err), "VMM allocation: ", err);
+  ES_CHECK_CUDA(cudaMemset(reinterpret_cast<void*>(b.ptr), 0, b.size));
+  return {(int64_t)b.ptr, (int64_t)b.size, (int64_t)b.handle, (int64_t)b.fd};
+}
+
+// (ptr, size, handle) of another process's buffer, mapped for the current device.
+std::tuple<int64_t, int64_t, int64_t> vmm_import(int64_t fd, int64_t bytes) {
+  es::vmm::Buffer b;
+  const char* err = "";
+  TORCH_CHECK(es::vmm::import(cur_device(), (int)fd, (uint64_t)bytes, b, &err), "VMM import: ", err);
+  return {(int64_t)b.ptr, (int64_t)b.size, (int64_t)b.handle};
+}
+
+void vmm_release(int64_t ptr, int64_t size, int64_t handle, int64_t fd) {
+  es::vmm::Buffer b;
+  b.ptr = (uint64_t)ptr;
+  b.size = (uint64_t)size;
+  b.handle = (uint64_t)handle;
+  b.fd = (int)fd;
+  es::vmm::release(b);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -356,4 +389,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
+  m.def("vmm_create", &vmm_create, "exportable device buffer (driver VMM): (ptr, size, handle, fd)");
+  m.def("vmm_import", &vmm_import, "map another process's exported buffer: (ptr, size, handle)");
+  m.def("vmm_release", &vmm_release);
 }

@@ -78,7 +78,14 @@ TINY_MIXTRAL = ModelConfig(
     intermediate=256, rope_theta=1e6, rms_eps=1e-5, num_experts=4, top_k=2, max_position=2048,
 )
 
-REGISTRY = {c.name: c for c in (QWEN2_5_0_5B, LLAMA3_8B, LLAMA3_70B, MIXTRAL_8X7B, TINY_LLAMA, TINY_QWEN, TINY_MIXTRAL)}
+# a small model whose tensor-parallel shards still meet the GPU kernels' tile sizes (TP <= 4)
+SMALL_LLAMA = ModelConfig(
+    name="small-llama", vocab=4096, hidden=1024, layers=4, heads=16, kv_heads=8, head_dim=64,
+    intermediate=2048, rope_theta=5e5, rms_eps=1e-5, max_position=4096,
+)
+
+REGISTRY = {c.name: c for c in (QWEN2_5_0_5B, LLAMA3_8B, LLAMA3_70B, MIXTRAL_8X7B, TINY_LLAMA, TINY_QWEN, TINY_MIXTRAL,
+                                SMALL_LLAMA)}
 
 
 def get_config(name: str) -> ModelConfig:

@@ -1,8 +1,9 @@
 """The tensor-parallel collective on peer memory: fused GEMM + all-reduce and a failure-detecting
 all-reduce, with NCCL for what the kernels do not take.
 
-One instance per rank. It owns the rank's symmetric buffer (device memory outside torch's
-allocator, exported by CUDA IPC), maps every member's buffer, and keeps three small device tables
+One instance per rank. It owns the rank's symmetric buffer (a driver VMM allocation outside
+torch's allocator, shared by file descriptor: ``parallel.symm``; its memory outlives a member that
+dies, so survivors' bounded waits end cleanly), maps every member's buffer, and keeps small device tables
 the kernels read on every launch (so captured CUDA graphs follow membership changes): the member
 buffers' addresses, the member order, and the call counter. Its control words live in the slot
 region (``parallel.slot``), mapped into the device.
@@ -21,7 +22,8 @@ import torch.distributed as dist
 
 from .. import _ext
 from .nccl import GroupCollective
-from .slot import MAX_ROWS, SlotRegion
+from .slot import HANDLE_BYTES, MAX_ROWS, SlotRegion
+from .symm import PeerMapping, SymmetricBuffer
 
 
 class FusedTPCollective:
@@ -32,13 +34,29 @@ class FusedTPCollective:
     member may die (a dead process bound to a multicast object is not survivable on this pool)."""
 
     def __init__(self, device: torch.device, group=None, region: SlotRegion | None = None, row: int | None = None,
-                 members: list[int] | None = None, region_name: str | None = None, nvls: bool = False):
+                 members: list[int] | None = None, region_name: str | None = None, nvls: bool = False,
+                 barrier=None):
+        """With `group` (a torch.distributed group) the members are its ranks and NCCL carries what
+        the kernels do not take. Detached (no group: `region`, `row`, `members` and a `barrier`
+        callable given) the members are rows of an existing region and every collective runs on
+        the peer-memory kernels (large all-reduces in chunks, all-gathers as sums of disjoint
+        slices), so a membership change needs no communicator at all."""
         self.C = _ext.load()
         self.device = torch.device(device)
         self.group = group
-        self.nccl = GroupCollective(group)
-        self.size = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.detached = group is None and region is not None
+        if self.detached:
+            if members is None or row is None or barrier is None:
+                raise ValueError("a detached collective needs its region row, members and a barrier")
+            self.nccl = None
+            self.size = len(members)
+            self.rank = members.index(row) if row in members else -1
+            self._barrier = barrier
+        else:
+            self.nccl = GroupCollective(group)
+            self.size = dist.get_world_size(group)
+            self.rank = dist.get_rank(group)
+            self._barrier = lambda: dist.barrier(group)
         self.row = self.rank if row is None else row
         self._own_region = region is None
         if region is None:
@@ -78,13 +96,15 @@ class FusedTPCollective:
                     self._addrs[r] = int(ptr)
                 self.own = self._addrs[self.row]
             else:
-                self.own = int(self.C.device_alloc(nbytes))
+                self._buf = SymmetricBuffer(self.C, nbytes, self._sock_path(self.row))
+                self.own = self._buf.ptr
                 self._addrs[self.row] = self.own
         self.region.set_pid(self.row, os.getpid())
         if not self.nvls:
-            self.region.publish(self.row, bytes(self.C.ipc_handle(self.own)))
+            name = os.path.basename(self._sock_path(self.row)).encode()
+            self.region.publish(self.row, name + bytes(HANDLE_BYTES - len(name)))
         self.members = list(members) if members is not None else list(range(self.size))
-        dist.barrier(group)
+        self._barrier()
         if self.nvls:
             with torch.cuda.device(self.device):
                 self.peers.copy_(torch.tensor(self._addrs, dtype=torch.int64))
@@ -103,18 +123,30 @@ class FusedTPCollective:
         return obj[0]
 
     # ---- tables --------------------------------------------------------------------------------
+    def _sock_path(self, row: int) -> str:
+        return f"{self.region.path}.r{row}.fd"
+
     def _open(self, rows) -> None:
-        changed = False
         for r in rows:
             if r == self.row or r in self._opened:
                 continue
+            name = self.region.handle(r).rstrip(b"\0").decode()
             with torch.cuda.device(self.device):
-                self._opened[r] = int(self.C.ipc_open(self.region.handle(r)))
-            self._addrs[r] = self._opened[r]
-            changed = True
+                self._opened[r] = PeerMapping(self.C, os.path.join(os.path.dirname(self.region.path), name))
+            self._addrs[r] = self._opened[r].ptr
         with torch.cuda.device(self.device):
             self.peers.copy_(torch.tensor(self._addrs, dtype=torch.int64))
-        del changed
+
+    def release_rows(self, rows) -> None:
+        """Unmap rows that are no longer members (call with this member quiescent)."""
+        torch.cuda.synchronize(self.device)
+        for r in rows:
+            m = self._opened.pop(r, None)
+            if m is not None:
+                m.close()
+                self._addrs[r] = 0
+        with torch.cuda.device(self.device):
+            self.peers.copy_(torch.tensor(self._addrs, dtype=torch.int64))
 
     def _write_order(self) -> None:
         rows = [len(self.members), *self.members] + [0] * (MAX_ROWS - len(self.members))
@@ -134,9 +166,21 @@ class FusedTPCollective:
         if self.can_take(inp) and out.is_contiguous() and out.data_ptr() % 16 == 0:
             self.C.fdar(inp, out, *self._comm())
             return out
+        if self.nccl is None:
+            return self._chunked_all_reduce(inp, out)
         if out.data_ptr() != inp.data_ptr():
             out.copy_(inp)
         return self.nccl.all_reduce(out)
+
+    def _chunked_all_reduce(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """A tensor above one call's size (or not bf16) in calls the kernels take."""
+        src = inp.reshape(-1).to(torch.bfloat16).contiguous()
+        dst = torch.empty_like(src)
+        step = self.max_elems - self.max_elems % 8
+        for i in range(0, src.numel(), step):
+            self.C.fdar(src[i : i + step], dst[i : i + step], *self._comm())
+        out.copy_(dst.view(out.shape).to(out.dtype))
+        return out
 
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         return self.all_reduce_into(t, t)
@@ -153,7 +197,27 @@ class FusedTPCollective:
         return y
 
     def all_gather(self, t: torch.Tensor) -> torch.Tensor:
-        return self.nccl.all_gather(t)
+        """Every member's tensor concatenated along the last dim, in member (rank) order."""
+        if self.nccl is not None:
+            return self.nccl.all_gather(t)
+        if self.size == 1:
+            return t
+        n = t.shape[-1]
+        if t.dtype == torch.bfloat16:
+            full = torch.zeros(*t.shape[:-1], n * self.size, dtype=torch.bfloat16, device=t.device)
+            full[..., self.rank * n : (self.rank + 1) * n] = t
+            flat = full.reshape(-1)
+            self.all_reduce_into(flat, flat)  # x + 0 is exact: disjoint slices sum to the gather
+            return full
+        # other dtypes travel as their bytes, one byte per bf16 element (0..255 are exact in bf16)
+        raw = t.contiguous().view(torch.uint8).reshape(*t.shape[:-1], -1)
+        nb = raw.shape[-1]
+        full = torch.zeros(*raw.shape[:-1], nb * self.size, dtype=torch.bfloat16, device=t.device)
+        full[..., self.rank * nb : (self.rank + 1) * nb] = raw.to(torch.bfloat16)
+        flat = full.reshape(-1)
+        self.all_reduce_into(flat, flat)
+        got = full.to(torch.uint8).reshape(*raw.shape[:-1], self.size, nb)
+        return got.view(t.dtype).reshape(*t.shape[:-1], n * self.size)
 
     def set_members(self, members, epoch: int = 0) -> None:
         """Program the member order (rows in rank position); call with this member quiescent."""
@@ -161,6 +225,9 @@ class FusedTPCollective:
         if self.nvls and list(members) != self.members:
             raise RuntimeError("the NVLS variant has fixed members; use the P2P variant for membership changes")
         self.members = [int(m) for m in members]
+        self.size = len(self.members)
+        if self.row in self.members:
+            self.rank = self.members.index(self.row)
         self._open(self.members)
         self._write_order()
 
@@ -179,6 +246,7 @@ class FusedTPCollective:
                 self.C.memset_async(self.own, int(self.C.comm_buffer_bytes()))
             torch.cuda.synchronize(self.device)
         self.region.clear_late(self.row)
+        self.region.set_u32(self.row, 16, 0)  # status
         self.region.set_abort([self.row], 0)
 
     def status(self) -> int:
@@ -214,14 +282,14 @@ class FusedTPCollective:
         self.C = Counting()
 
     def close(self) -> None:
-        for p in self._opened.values():
+        for m in self._opened.values():
             try:
-                self.C.ipc_close(p)
+                m.close()
             except RuntimeError:
                 pass
         self._opened.clear()
         if self.own and not self.nvls:
-            self.C.device_free(self.own)
+            self._buf.close()
         self.own = 0
         self._symm = None
         self.region.close(self.C, unlink=self._own_region and self.rank == 0)

@@ -83,7 +83,8 @@ class MultiprocExecutor:
     def __init__(self, cfg: EngineConfig, engine: str = "engine", daemon: str = "", store: str = "",
                  spares: tuple[int, ...] = (), device: str = "cpu", dtype: str = "float32", node: str = "",
                  env: dict | None = None, threads: int = 0, step_timeout_s: float = 300.0,
-                 change_timeout_s: float = 120.0, log_dir: str | None = None, start_timeout_s: float = 600.0):
+                 change_timeout_s: float = 120.0, log_dir: str | None = None, start_timeout_s: float = 600.0,
+                 devices: list[int] | None = None):
         self.cfg = cfg
         self.engine = engine
         self.layout = ParallelLayout(cfg.tensor_parallel, cfg.pipeline_parallel)
@@ -111,15 +112,33 @@ class MultiprocExecutor:
             base += ["--node", node]
         if threads:
             base += ["--threads", str(threads)]
+        self.region = None
+        self.rows = {r: r for r in range(self.layout.world)}  # rank position -> slot-region row
+        gpu = self.gpu = device.startswith("cuda")
+        if gpu and cfg.tensor_parallel > 1:
+            from ..parallel.slot import MAX_ROWS, SlotRegion
+
+            if self.layout.world + len(spares) > MAX_ROWS:
+                raise ValueError(f"{self.layout.world} ranks + {len(spares)} spares exceed the region's {MAX_ROWS} rows")
+            self.region_name = f"es_{engine}_{os.getpid()}_{secrets.token_hex(4)}"
+            self.region = SlotRegion.create(self.region_name)
+            base += ["--region", self.region_name]
         e = dict(os.environ)
         root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         e["PYTHONPATH"] = os.pathsep.join([root] + [p for p in e.get("PYTHONPATH", "").split(os.pathsep) if p])
         e.update(env or {})
         e["EVERSERVE_CARRIER_TOKEN"] = self.token
+        def dev_args(i: int) -> list[str]:
+            if not gpu:
+                return []
+            return ["--device", f"cuda:{(devices or list(range(64)))[i]}"]
+
         for r in range(self.layout.world):
-            self._spawn(f"rank{r}", base + ["--role", "worker", "--rank", str(r)], e)
+            self._spawn(f"rank{r}", base + ["--role", "worker", "--rank", str(r), "--row", str(r)] + dev_args(r), e)
         for i, r in enumerate(spares):
-            self._spawn(f"spare{i}-for{r}", base + ["--role", "spare", "--rank", str(r)], e)
+            row = self.layout.world + i
+            self._spawn(f"spare{i}-for{r}", base + ["--role", "spare", "--rank", str(r), "--row", str(row)]
+                        + dev_args(row), e)
         self.links: dict[int, Link] = {}
         deadline = time.monotonic() + start_timeout_s
         while len(self.links) < self.layout.world:
@@ -175,6 +194,11 @@ class MultiprocExecutor:
                 self.t_kill = time.monotonic()
                 self.notice(self.notice_at_decode_step[1])
                 self.notice_at_decode_step = None
+        if victim is not None and self.gpu:
+            # on GPUs a rank leaves between steps (its kernels done), never mid-kernel
+            msg = dict(msg, fail_at=plan.step, fail_rank=victim)
+            self.t_kill = time.monotonic()
+            victim = None
         lost, errors = set(), {}
         for r, link in self.links.items():
             try:
@@ -221,8 +245,11 @@ class MultiprocExecutor:
                 pass
 
     def _boundary(self, epoch: int) -> dict[int, dict]:
+        for r, link in self.links.items():
+            if "row" in link.hello:
+                self.rows[r] = int(link.hello["row"])
         for link in self.links.values():
-            link.send({"op": "boundary", "epoch": epoch})
+            link.send({"op": "boundary", "epoch": epoch, "rows": dict(self.rows)})
         computed = {}
         for r, link in self.links.items():
             while True:
@@ -310,6 +337,8 @@ class MultiprocExecutor:
         if self.client is not None:
             self.client.close()
         self.carrier.close()
+        if self.region is not None:
+            self.region.close(unlink=True)
         for f in self._logs:
             f.close()
 

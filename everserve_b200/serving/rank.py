@@ -84,7 +84,16 @@ class RankProcess:
         self.groups = SwappableGroups(self.rdzv, self.rank, self.layout, dev, timeout_s=a.group_timeout)
         mc = self.cfg.model
         self.exchange = Exchange(self.groups, mc.hidden, self.cfg.dtype) if a.pp > 1 else None
-        coll = GroupCollective(self.groups) if a.tp > 1 else None
+        self.row = a.row if a.row is not None else self.rank
+        self.rows = {r: r for r in range(self.layout.world)}  # rank position -> slot-region row
+        self.region = None
+        self.watch = None
+        coll = None
+        if a.tp > 1 and dev.type == "cuda":
+            coll = self._fused_collective(dev)
+        elif a.tp > 1:
+            coll = GroupCollective(self.groups)
+        self.collective = coll
         t0 = time.monotonic()
         self.worker = Worker(self.cfg, rank=self.rank, collective=coll, pipe=self.exchange, device=str(dev))
         self.caches = self.worker.runner.caches
@@ -110,6 +119,55 @@ class RankProcess:
                                            stage=[self.layout.stage(self.rank)], node=a.node,
                                            identity=identity(self.cfg, self.engine))
 
+    # ---- the peer-memory tensor-parallel collective (GPUs) ----------------------------------------
+    def _stage_rows(self) -> list[int]:
+        stage = self.layout.stage(self.rank)
+        ranks = [r for r in range(self.layout.world) if self.layout.stage(r) == stage]
+        return [self.rows[r] for r in sorted(ranks, key=self.layout.column)]
+
+    def _store_barrier(self, tag: str, rows: list[int], timeout_s: float = 60.0) -> None:
+        self.rdzv.set(f"{tag}/{self.row}", b"1")
+        self.rdzv.wait([f"{tag}/{r}" for r in rows], datetime.timedelta(seconds=timeout_s))
+
+    def _fused_collective(self, dev):
+        from ..parallel.fused import FusedTPCollective
+        from ..parallel.slot import SlotRegion
+        from ..runtime.slotwatch import SlotWatch
+        from ..settings import load as load_settings
+
+        self.settings = load_settings()
+        self.region = SlotRegion.open(self.a.region)
+        members = self._stage_rows()
+        if self.spare:
+            barrier = lambda: None  # noqa: E731 - a spare maps the members and waits for its take
+        else:
+            barrier = lambda: self._store_barrier("tp/e0", members)  # noqa: E731
+        coll = FusedTPCollective(dev, region=self.region, row=self.row, members=members, barrier=barrier)
+        coll.set_bound_ns(self.settings.bound_ns(0.0))
+        if not self.spare:
+            self._start_watch(coll, members)
+        return coll
+
+    def _start_watch(self, coll, members) -> None:
+        from ..runtime.slotwatch import SlotWatch
+
+        if self.watch is not None:
+            self.watch.stop()
+
+        def lost(ranks, why):
+            coll.abort()  # the kernels waiting on the dead member leave now
+            self.runtime.trace("slotwatch", ranks=ranks, why=why)
+            if self.daemon is not None:
+                try:
+                    self.daemon.report_lost(ranks, f"slotwatch: {why}", reason=sp.REASON_FAULT)
+                except OSError:
+                    pass
+
+        by_row = {row: r for r, row in self.rows.items()}
+        self.watch = SlotWatch(self.region, self.row, lost, rank_of_row=lambda row: by_row.get(row, row),
+                               members=members, poll_s=self.settings.poll_ms / 1e3,
+                               hang_s=self.settings.hang_s).start()
+
     # ---- participant (daemon reader thread) ------------------------------------------------------
     def identity(self) -> tuple[int, int]:
         return self.rank, self.device.index or 0 if self.device.type == "cuda" else 0
@@ -134,6 +192,8 @@ class RankProcess:
             self.leaving = True  # finish the step; the head releases this rank at the boundary
         elif not set(change.lost) <= set(change.departing):
             self.groups.refuse()
+            if self.region is not None:
+                self.collective.abort()
         return None
 
     def on_notice(self, rank: int, deadline_ms: int) -> None:
@@ -170,7 +230,8 @@ class RankProcess:
         self.worker.execute(plan)
 
     def link(self, address: str, token: str) -> None:
-        hello = {"rank": self.rank, "pid": os.getpid(), "role": "spare" if self.spare else "worker", "token": token,
+        hello = {"rank": self.rank, "row": self.row, "pid": os.getpid(), "role": "spare" if self.spare else "worker",
+                 "token": token,
                  "num_blocks": self.worker.num_blocks, "computed": dict(self.computed), "load_s": self.load_s}
         self.carrier = CarrierClient(address, hello)
 
@@ -214,11 +275,23 @@ class RankProcess:
     def _step(self, msg: dict) -> None:
         plan = msg["plan"]
         if msg.get("fail_at") == plan.step and self.rank == msg.get("fail_rank"):
-            os.kill(os.getpid(), 9)  # fault injection on the host: this process dies mid-decode
+            # host-side fault injection: the process dies between steps, nothing of it in flight
+            if self.device.type == "cuda":
+                torch.cuda.synchronize(self.device)
+            os.kill(os.getpid(), 9)
         try:
             if msg["epoch"] != self.runtime.epoch:
                 raise RuntimeError(f"step of epoch {msg['epoch']} on a rank at epoch {self.runtime.epoch}")
             out = self.worker.execute(plan)
+            if self.region is not None:
+                if isinstance(out, torch.Tensor):
+                    out = out.cpu()
+                else:
+                    torch.cuda.synchronize(self.device)
+                st = self.collective.status() or self.worker.model.ops.check_status()
+                if st:
+                    raise RuntimeError(f"a collective of step {plan.step} failed (status {st}, late rows "
+                                       f"{self.collective.late_rows()})")
             counts = {r.req_id: r.start_pos + len(r.token_ids) for r in plan.reqs}
             self.computed.update(counts)
             if self.ckv is not None:
@@ -244,6 +317,16 @@ class RankProcess:
                 counts = self.ckv.restore(self.rank, since_step=self.ckv.restored_step + 1)
                 self.computed.update(counts)
             self.groups.form(epoch, self.rank)
+            if "rows" in msg:
+                self.rows = {int(r): int(row) for r, row in msg["rows"].items()}
+            if self.region is not None:
+                members = self._stage_rows()
+                gone = [r for r in self.collective.members if r not in members]
+                self.collective.set_members(members, epoch)
+                self.collective.release_rows(gone)
+                self.collective.resume()
+                self._store_barrier(f"tp/e{epoch}", members)
+                self._start_watch(self.collective, members)
             self.runtime.at_boundary(epoch)
             reply = {"op": "ready", "epoch": epoch, "rank": self.rank, "computed": dict(self.computed),
                      "form_s": time.monotonic() - t0}
@@ -252,8 +335,12 @@ class RankProcess:
         self.carrier.send(reply)
 
     def close(self) -> None:
+        if self.watch is not None:
+            self.watch.stop()
         if self.ckv is not None:
             self.ckv.close()
+        if self.region is not None:
+            self.collective.close()
 
 
 def parse(argv=None) -> argparse.Namespace:
@@ -277,6 +364,8 @@ def parse(argv=None) -> argparse.Namespace:
     p.add_argument("--store", default=os.environ.get("EVERSERVE_MIRROR_SOCKET", ""))
     p.add_argument("--node", default=os.environ.get("EVERSERVE_NODE", ""))
     p.add_argument("--group-timeout", type=float, default=30.0)
+    p.add_argument("--region", default="", help="slot region name (GPU tensor parallelism)")
+    p.add_argument("--row", type=int, default=None, help="this process's row in the slot region")
     p.add_argument("--threads", type=int, default=0)
     return p.parse_args(argv)
 
