@@ -16,6 +16,7 @@
 #include <cstring>
 
 #include "api.h"
+#include "launch.h"
 #include "common.cuh"
 #include "ptx.cuh"
 #include "tmap.h"
@@ -59,6 +60,8 @@ ES_DEVICE uint32_t swz(int t, int d) {
 
 template <int D, int BS, int kStages>
 __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ CUtensorMap cmap, DecodeParams p) {
+  pdl_wait();
+  pdl_launch();
   using C = DecodeCfg<D, BS, kStages>;
   constexpr int NT = D / 8;  // n-tiles of the output
   extern __shared__ uint8_t smem_raw[];
@@ -245,6 +248,8 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
 __global__ void decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                     const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out,
                                     int64_t out_stride, int hq, int max_splits, int part_tokens, int d) {
+  pdl_wait();
+  pdl_launch();
   const int b = blockIdx.x, h = blockIdx.y;
   const int ctx = ctx_lens[b];
   const int ns = min(max_splits, (ctx + part_tokens - 1) / part_tokens);
@@ -272,8 +277,7 @@ cudaError_t launch_decode(const CUtensorMap& map, const DecodeParams& p, int B, 
     configured = true;
   }
   dim3 grid(B, p.hkv, p.max_splits);
-  decode_kernel<D, BS, S><<<grid, kThreads, C::kSmem, stream>>>(map, p);
-  return cudaGetLastError();
+  return launch_ex(decode_kernel<D, BS, S>, grid, dim3(kThreads), C::kSmem, stream, 0, map, p);
 }
 
 template <int D, int BS>
@@ -319,10 +323,9 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   else return cudaErrorInvalidValue;
   if (e != cudaSuccess) return e;
   dim3 mgrid(a.B, a.hq);
-  attn::decode_merge_kernel<<<mgrid, a.d, 0, stream>>>(a.part_o, a.part_ml, a.ctx_lens,
-                                                       static_cast<__nv_bfloat16*>(a.out), a.out_stride, a.hq,
-                                                       a.max_splits, a.part_tokens, a.d);
-  return cudaGetLastError();
+  return launch_ex(attn::decode_merge_kernel, mgrid, dim3(a.d), 0, stream, 0, (const float*)a.part_o,
+                   (const float*)a.part_ml, a.ctx_lens, static_cast<__nv_bfloat16*>(a.out), a.out_stride, a.hq,
+                   a.max_splits, a.part_tokens, a.d);
 }
 
 }  // namespace es

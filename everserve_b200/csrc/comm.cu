@@ -7,6 +7,7 @@
 // the members' chunks in member order in fp32 (one rounding) into `out`. Decode-size tensors (up
 // to 1 Mi elements, the data region of one sender) take this path; larger ones go to NCCL.
 #include "api.h"
+#include "launch.h"
 #include "comm.cuh"
 
 namespace es {
@@ -18,6 +19,8 @@ constexpr int kChunk = 4096;  // elements per CTA and flag slot
 
 __global__ void __launch_bounds__(kThreads) fdar_kernel(const __nv_bfloat16* __restrict__ inp,
                                                         __nv_bfloat16* __restrict__ out, int n, View v) {
+  pdl_wait();
+  pdl_launch();
   __shared__ uint32_t s_seq;
   __shared__ int s_order[kMaxRows];
   __shared__ int s_count;
@@ -96,6 +99,8 @@ constexpr int kLLThreads = 256;
 
 __global__ void __launch_bounds__(kLLThreads) fdar_ll_kernel(const __nv_bfloat16* __restrict__ inp,
                                                              __nv_bfloat16* __restrict__ out, int n, View v) {
+  pdl_wait();
+  pdl_launch();
   __shared__ uint32_t s_seq;
   __shared__ int s_order[kMaxRows];
   __shared__ int s_count;
@@ -166,14 +171,12 @@ cudaError_t launch_fdar(const void* inp, void* out, int64_t n, const CommArgs& c
   if (n <= comm_ll_max_elems()) {
     const int words = (int)((n + 1) / 2);
     const int grid = (words + comm::kLLThreads - 1) / comm::kLLThreads;
-    comm::fdar_ll_kernel<<<grid, comm::kLLThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(inp),
-                                                                 static_cast<__nv_bfloat16*>(out), (int)n, v);
-    return cudaGetLastError();
+    return launch_ex(comm::fdar_ll_kernel, dim3(grid), dim3(comm::kLLThreads), 0, stream, 0,
+                     static_cast<const __nv_bfloat16*>(inp), static_cast<__nv_bfloat16*>(out), (int)n, v);
   }
   const int grid = (int)((n + comm::kChunk - 1) / comm::kChunk);
-  comm::fdar_kernel<<<grid, comm::kThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(inp),
-                                                         static_cast<__nv_bfloat16*>(out), (int)n, v);
-  return cudaGetLastError();
+  return launch_ex(comm::fdar_kernel, dim3(grid), dim3(comm::kThreads), 0, stream, 0,
+                   static_cast<const __nv_bfloat16*>(inp), static_cast<__nv_bfloat16*>(out), (int)n, v);
 }
 
 }  // namespace es

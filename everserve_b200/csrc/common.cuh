@@ -27,6 +27,16 @@ ES_DEVICE uint64_t global_ns() {
   return t;
 }
 
+// Programmatic dependent launch (PDL). A kernel launched with the programmatic-serialization
+// attribute may start while the previous kernel of its stream finishes. `pdl_wait` blocks the
+// calling thread until that kernel has completed and its writes are visible: every read of data a
+// previous kernel produced, and every global write, comes after it. Only reads of data no kernel
+// of the step writes (weights) may come before. `pdl_launch` lets the next kernel start launching;
+// kernels call it after their wait, so at most two kernels of a stream overlap. Both are no-ops
+// for a launch without the attribute.
+ES_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+ES_DEVICE void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 ES_DEVICE float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 ES_DEVICE __nv_bfloat16 f2bf(float x) { return __float2bfloat16_rn(x); }
 

@@ -8,6 +8,7 @@
 
 #include "api.h"
 #include "common.cuh"
+#include "launch.h"
 
 namespace es {
 namespace {
@@ -20,6 +21,8 @@ template <int VPT, bool kResidual>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                int hidden, int x_stride, int y_stride, float eps) {
+  pdl_wait();
+  pdl_launch();
   __shared__ float red[32];
   const int t = blockIdx.x;
   const int nvec = hidden >> 3;
@@ -72,6 +75,8 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv
                                const int64_t* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
                                __nv_bfloat16* __restrict__ cache, int hq, int hkv, int d, int block_size,
                                int64_t s_block, int64_t s_off, int64_t s_head, int64_t s_kv) {
+  pdl_wait();
+  pdl_launch();
   const int t = blockIdx.x;
   const int half = d >> 1;
   const int row = (hq + 2 * hkv) * d;
@@ -119,6 +124,8 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv
 // out[t, i] = silu(g[t, i]) * u[t, i], g and u the two halves of gate_up's row.
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int inter,
                                 int64_t rows) {
+  pdl_wait();
+  pdl_launch();
   const int nvec = inter >> 3;
   const int64_t total = rows * nvec;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -140,6 +147,8 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloa
 // st: [4, B] int64 rows (ids, positions, slots, context lengths); rows with context 0 are padding.
 __global__ void decode_advance_kernel(int64_t* __restrict__ st, const int64_t* __restrict__ sampled,
                                       const int* __restrict__ bt, int bt_stride, int b, int B, int bs) {
+  pdl_wait();
+  pdl_launch();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= b) return;
   if (st[3 * B + i] <= 0) return;
@@ -153,6 +162,8 @@ __global__ void decode_advance_kernel(int64_t* __restrict__ st, const int64_t* _
 // ---------------------------------------------------------------------------------------------
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              __nv_bfloat16* __restrict__ out, int hidden, int64_t vocab) {
+  pdl_wait();
+  pdl_launch();
   const int t = blockIdx.x;
   int64_t id = ids[t];
   if (id < 0 || id >= vocab) id = 0;
@@ -165,6 +176,8 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat1
 // Greedy argmax over a bf16 row; ties go to the lowest index (torch.argmax's rule).
 __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t* __restrict__ out, int vocab,
                               int64_t stride) {
+  pdl_wait();
+  pdl_launch();
   const __nv_bfloat16* row = logits + blockIdx.x * stride;
   float best = -INFINITY;
   int idx = 0x7fffffff;
@@ -230,8 +243,8 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t*
 cudaError_t launch_decode_advance(int64_t* st, const int64_t* sampled, const int* bt, int64_t bt_stride, int b, int B,
                                   int bs, cudaStream_t stream) {
   if (b == 0) return cudaSuccess;
-  decode_advance_kernel<<<(b + 127) / 128, 128, 0, stream>>>(st, sampled, bt, (int)bt_stride, b, B, bs);
-  return cudaGetLastError();
+  return launch_ex(decode_advance_kernel, dim3((b + 127) / 128), dim3(128), 0, stream, 0, st, sampled, bt,
+                   (int)bt_stride, b, B, bs);
 }
 
 cudaError_t launch_rmsnorm(const void* x, void* residual, const void* w, void* y, int64_t rows, int hidden,
@@ -247,11 +260,11 @@ cudaError_t launch_rmsnorm(const void* x, void* residual, const void* w, void* y
   auto wp = static_cast<const __nv_bfloat16*>(w);
   auto yp = static_cast<__nv_bfloat16*>(y);
   const int xs = (int)x_stride, ys = (int)y_stride;
-#define ES_LAUNCH_RMS(V)                                                                               \
-  if (rp)                                                                                              \
-    rmsnorm_kernel<V, true><<<rows, threads, 0, stream>>>(xp, rp, wp, yp, hidden, xs, ys, eps);        \
-  else                                                                                                 \
-    rmsnorm_kernel<V, false><<<rows, threads, 0, stream>>>(xp, rp, wp, yp, hidden, xs, ys, eps);
+#define ES_LAUNCH_RMS(V)                                                                                      \
+  return rp ? launch_ex(rmsnorm_kernel<V, true>, dim3((unsigned)rows), dim3(threads), 0, stream, 0, xp, rp, wp, yp, \
+                        hidden, xs, ys, eps)                                                                      \
+            : launch_ex(rmsnorm_kernel<V, false>, dim3((unsigned)rows), dim3(threads), 0, stream, 0, xp, rp, wp, yp, \
+                        hidden, xs, ys, eps);
   if (vpt == 1) {
     ES_LAUNCH_RMS(1)
   } else if (vpt == 2) {
@@ -260,7 +273,6 @@ cudaError_t launch_rmsnorm(const void* x, void* residual, const void* w, void* y
     ES_LAUNCH_RMS(4)
   }
 #undef ES_LAUNCH_RMS
-  return cudaGetLastError();
 }
 
 cudaError_t launch_rope_kv(const void* qkv, const void* bias, const int64_t* positions, const float* cos_sin,
@@ -268,11 +280,10 @@ cudaError_t launch_rope_kv(const void* qkv, const void* bias, const int64_t* pos
                            int block_size, const int64_t* st, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   if (d % 2 != 0 || st[4] != 1) return cudaErrorInvalidValue;
-  rope_kv_kernel<<<T, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(bias),
-                                        positions, cos_sin, slots, static_cast<__nv_bfloat16*>(q_out),
-                                        static_cast<__nv_bfloat16*>(cache), hq, hkv, d, block_size, st[0], st[1], st[2],
-                                        st[3]);
-  return cudaGetLastError();
+  return launch_ex(rope_kv_kernel, dim3((unsigned)T), dim3(256), 0, stream, 0, static_cast<const __nv_bfloat16*>(qkv),
+                   static_cast<const __nv_bfloat16*>(bias), positions, cos_sin, slots,
+                   static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(cache), hq, hkv, d, block_size,
+                   st[0], st[1], st[2], st[3]);
 }
 
 cudaError_t launch_silu_mul(const void* gu, void* out, int64_t rows, int inter, cudaStream_t stream) {
@@ -281,25 +292,23 @@ cudaError_t launch_silu_mul(const void* gu, void* out, int64_t rows, int inter, 
   const int64_t total = rows * (inter / 8);
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
-  silu_mul_kernel<<<blocks, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(gu),
-                                                  static_cast<__nv_bfloat16*>(out), inter, rows);
-  return cudaGetLastError();
+  return launch_ex(silu_mul_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, 0,
+                   static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(out), inter, rows);
 }
 
 cudaError_t launch_embed(const int64_t* ids, const void* table, void* out, int64_t T, int hidden, int64_t vocab,
                          cudaStream_t stream) {
   if (hidden % 8 != 0) return cudaErrorInvalidValue;
   if (T == 0) return cudaSuccess;
-  embed_kernel<<<T, 128, 0, stream>>>(ids, static_cast<const __nv_bfloat16*>(table), static_cast<__nv_bfloat16*>(out),
-                                      hidden, vocab);
-  return cudaGetLastError();
+  return launch_ex(embed_kernel, dim3((unsigned)T), dim3(128), 0, stream, 0, ids,
+                   static_cast<const __nv_bfloat16*>(table), static_cast<__nv_bfloat16*>(out), hidden, vocab);
 }
 
 cudaError_t launch_argmax(const void* logits, int64_t* out, int64_t rows, int vocab, int64_t stride,
                           cudaStream_t stream) {
   if (rows == 0) return cudaSuccess;
-  argmax_kernel<<<rows, 1024, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), out, vocab, stride);
-  return cudaGetLastError();
+  return launch_ex(argmax_kernel, dim3((unsigned)rows), dim3(1024), 0, stream, 0,
+                   static_cast<const __nv_bfloat16*>(logits), out, vocab, stride);
 }
 
 }  // namespace es

@@ -25,6 +25,7 @@
 #include "api.h"
 #include "comm.cuh"
 #include "common.cuh"
+#include "launch.h"
 #include "ptx.cuh"
 #include "tmap.h"
 
@@ -88,11 +89,6 @@ __global__ void __launch_bounds__(kThreads, CPS)
 
   if (threadIdx.x == 0) {
     s_fail = 0;
-    if (kAR) {
-      const int cnt = cv.order[0];
-      s_count = cnt < 0 ? 0 : (cnt > comm::kMaxRows ? comm::kMaxRows : cnt);
-      for (int i = 0; i < s_count; i++) s_order[i] = cv.order[1 + i];
-    }
     ptx::prefetch_tmap(&tmap_w);
     ptx::prefetch_tmap(&tmap_x);
     for (int s = 0; s < C::kStages; s++) {
@@ -107,9 +103,29 @@ __global__ void __launch_bounds__(kThreads, CPS)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const bool producer = warp == 0 && lane == 0;
+  if (!producer) {
+    pdl_wait();  // everything below reads what the previous kernel wrote, or writes global memory
+    pdl_launch();
+  }
+  if (kAR && threadIdx.x == 64) {
+    const int cnt = cv.order[0];
+    s_count = cnt < 0 ? 0 : (cnt > comm::kMaxRows ? comm::kMaxRows : cnt);
+    for (int i = 0; i < s_count; i++) s_order[i] = cv.order[1 + i];
+  }
 
-  if (warp == 0 && lane == 0) {
-    for (int i = 0; i < nkb; i++) {
+  if (producer) {
+    // the weight tiles of the first stages depend on no kernel of the step: stream them while the
+    // previous kernel finishes, then the activation tiles once it has
+    const int pre = min(nkb, C::kStages);
+    for (int i = 0; i < pre; i++) {
+      ptx::mbar_arrive_expect_tx(&full[i], C::kStageBytes);
+      ptx::tma_load_2d(a_tiles + i * C::kABytes, &tmap_w, (kb0 + i) * BK, n0, &full[i]);
+    }
+    pdl_wait();
+    pdl_launch();
+    for (int i = 0; i < pre; i++) ptx::tma_load_2d(b_tiles + i * C::kBBytes, &tmap_x, (kb0 + i) * BK, m0, &full[i]);
+    for (int i = pre; i < nkb; i++) {
       const int s = i % C::kStages;
       if (i >= C::kStages && !ptx::mbar_wait(&empty[s], ((i / C::kStages) - 1) & 1)) {
         s_fail = 1;
@@ -296,19 +312,7 @@ cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::kSmem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = p.splits;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_kernel<BN, CPS, kAR>, mw, mx, p, cv);
+  return launch_ex(gemm_kernel<BN, CPS, kAR>, grid, dim3(kThreads), C::kSmem, stream, p.splits, mw, mx, p, cv);
 }
 
 // The largest split whose clusters all fit on the device at once (the fused all-reduce waits on

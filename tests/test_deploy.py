@@ -1,0 +1,56 @@
+"""Deployment artefacts: alert and dashboard metric names exist in the binaries; the bare-metal
+smoke script (coordinator, two daemons and stores, drain, node loss) passes."""
+
+import json
+import os
+import re
+import subprocess
+
+import yaml
+
+from cpp_bins import ROOT, binary
+
+DEPLOY = os.path.join(ROOT, "deploy")
+
+
+def _exported() -> set:
+    names = set()
+    for d, _, files in os.walk(os.path.join(ROOT, "cpp")):
+        for f in files:
+            if f.endswith(".cpp"):
+                names |= set(re.findall(r'"(everserve_[a-z_]+)"', open(os.path.join(d, f)).read()))
+    return names
+
+
+def _metrics_in(expr: str) -> set:
+    out = set()
+    for m in re.findall(r"everserve_[a-z_]+", expr):
+        for suffix in ("_bucket", "_sum", "_count"):
+            if m.endswith(suffix):
+                m = m[: -len(suffix)]
+        out.add(m)
+    return out
+
+
+def test_alert_and_dashboard_metrics_exist():
+    exported = _exported()
+    rules = yaml.safe_load(open(os.path.join(DEPLOY, "grafana", "alerts.yml")))
+    used = set()
+    for g in rules["groups"]:
+        for r in g["rules"]:
+            used |= _metrics_in(r["expr"])
+    dash = json.load(open(os.path.join(DEPLOY, "grafana", "everserve.json")))
+    for p in dash["panels"]:
+        for t in p["targets"]:
+            used |= _metrics_in(t["expr"])
+    missing = sorted(used - exported)
+    assert not missing, f"metrics named by alerts/dashboard but not exported: {missing}"
+
+
+def test_baremetal_smoke():
+    for b in ("everserve-coord", "everserve-node", "everserve-store", "everserve-ctl"):
+        binary(b)
+    r = subprocess.run(["bash", os.path.join(DEPLOY, "baremetal", "smoke.sh")], capture_output=True, text=True,
+                       timeout=60)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "smoke: ok" in r.stdout
