@@ -119,6 +119,8 @@ def main() -> None:
     ap.add_argument("--max-tokens", type=int, default=512)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--collective", default="fused", choices=["fused", "nccl"])
+    ap.add_argument("--deadline", type=float, default=300.0,
+                    help="seconds after which a run that has not finished reports a failure and exits")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -136,6 +138,7 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    _watchdog(args.deadline, rank)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     _ext.load()
@@ -169,6 +172,7 @@ def main() -> None:
     for _ in range(args.warmup):
         eng.step()
     torch.cuda.synchronize()
+    _check_status(ex, rank, "warm-up")
 
     def barrier():
         if world > 1:
@@ -209,6 +213,7 @@ def main() -> None:
     barrier()
     clk = clocks.stop()
 
+    _check_status(ex, rank, "timed steps")
     # kernel launches of this framework per decode step: count the extension calls of one step
     launches_per_step = count_launches(eng, ex)
 
@@ -250,6 +255,37 @@ def main() -> None:
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def _fail(rank: int, why: str, code: int) -> None:
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "error": why, "impl": "ours"}), flush=True)
+    print(f"[bench] rank {rank}: {why}", file=sys.stderr, flush=True)
+    os._exit(code)
+
+
+def _watchdog(deadline_s: float, rank: int) -> None:
+    """A run that has not finished by the deadline reports it and exits (a peer that stopped
+    answering must not keep every GPU of the job waiting)."""
+    import threading
+
+    def fire():
+        _fail(rank, f"no result within {deadline_s:.0f} s", 3)
+
+    t = threading.Timer(deadline_s, fire)
+    t.daemon = True
+    t.start()
+
+
+def _check_status(ex, rank: int, where: str) -> None:
+    """A bounded wait that ran out leaves a status word; a run with one is not a measurement."""
+    st = ex.worker.model.ops.check_status()
+    coll = getattr(ex.worker.tp, "collective", None)
+    cst = coll.status() if coll is not None and hasattr(coll, "status") else 0
+    if st or cst:
+        late = coll.late_rows() if coll is not None and hasattr(coll, "late_rows") else []
+        _fail(rank, f"a bounded wait ran out during {where} (kernel status {st}, collective status {cst}, "
+                    f"late rows {late})", 4)
 
 
 def count_launches(eng, ex) -> int:

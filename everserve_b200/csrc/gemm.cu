@@ -200,12 +200,14 @@ __global__ void __launch_bounds__(kThreads, CPS)
     const int mcount = min(BN, mrem);
     const int total = span4 * mcount;
     const uint32_t local = ptx::smem_u32(partial);
-    const int slot = blockIdx.x * S + (int)rank;
     if (kAR) {
-      if (threadIdx.x == 0) {
-        s_seq = cv.seqs[slot] + 1;  // this slot's call number (every member makes the same calls)
-        cv.seqs[slot] = s_seq;
-      }
+      // One call number per output tile, shared by the cluster's CTAs: every word of the tile in
+      // this call carries it, and consecutive calls of any fused GEMM over the tile alternate its
+      // parity half. (A number per cluster rank would not: two GEMMs with different splits give a
+      // word to different ranks, and a member one kernel ahead could overwrite words a slower
+      // member still polls.) Rank 0 advances it after the last cluster barrier, once every CTA of
+      // the cluster has read it; every member makes the same calls, so the numbers agree.
+      if (threadIdx.x == 0) s_seq = cv.seqs[blockIdx.x] + 1;
       __syncthreads();
     }
     const uint32_t seq = kAR ? s_seq : 0u, parity = seq & 1u;
@@ -290,6 +292,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
       }
     }
     ptx::cluster_sync();  // no CTA leaves while another still reads its shared memory
+    if (kAR && rank == 0 && threadIdx.x == 0) cv.seqs[blockIdx.x] = s_seq;
   }
   ptx::tc_fence_before();
   __syncthreads();

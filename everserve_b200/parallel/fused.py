@@ -15,6 +15,7 @@ Implements the reference's slot-collective protocol (core/everserve/comm/slot.py
 from __future__ import annotations
 
 import os
+import threading
 import uuid
 
 import torch
@@ -72,7 +73,8 @@ class FusedTPCollective:
         self.mc = 0
         self._symm = None
         self._addrs = [0] * MAX_ROWS
-        self._opened: dict[int, int] = {}
+        self._opened: dict[int, PeerMapping] = {}
+        self._map_lock = threading.RLock()
         nbytes = int(self.C.comm_buffer_bytes())
         with torch.cuda.device(self.device):
             self.region.map_device(self.C)
@@ -127,6 +129,10 @@ class FusedTPCollective:
         return f"{self.region.path}.r{row}.fd"
 
     def _open(self, rows) -> None:
+        with self._map_lock:
+            self._open_locked(rows)
+
+    def _open_locked(self, rows) -> None:
         for r in rows:
             if r == self.row or r in self._opened:
                 continue
@@ -136,6 +142,11 @@ class FusedTPCollective:
             self._addrs[r] = self._opened[r].ptr
         with torch.cuda.device(self.device):
             self.peers.copy_(torch.tensor(self._addrs, dtype=torch.int64))
+
+    def premap(self, rows) -> None:
+        """Map buffers of rows that may become members (a standing spare's) ahead of time."""
+        with self._map_lock:
+            self._open(rows)
 
     def release_rows(self, rows) -> None:
         """Unmap rows that are no longer members (call with this member quiescent)."""

@@ -88,6 +88,7 @@ class RankProcess:
         self.rows = {r: r for r in range(self.layout.world)}  # rank position -> slot-region row
         self.region = None
         self.watch = None
+        self._closing = threading.Event()
         coll = None
         if a.tp > 1 and dev.type == "cuda":
             coll = self._fused_collective(dev)
@@ -146,7 +147,23 @@ class RankProcess:
         coll.set_bound_ns(self.settings.bound_ns(0.0))
         if not self.spare:
             self._start_watch(coll, members)
+            threading.Thread(target=self._premap_spares, args=(coll,), name="premap", daemon=True).start()
         return coll
+
+    def _premap_spares(self, coll) -> None:
+        """Map every standing spare's buffer ahead of a change, so the boundary only rewrites the
+        member table (a non-member row's address is never read by the kernels)."""
+        from ..parallel.slot import MAX_ROWS, OFF_PUBLISHED
+
+        while not self._closing.is_set():
+            for row in range(self.layout.world, MAX_ROWS):
+                if row in coll._opened or not self.region.u32(row, OFF_PUBLISHED):
+                    continue
+                try:
+                    coll.premap([row])
+                except Exception as e:  # noqa: BLE001 - mapped at the boundary instead
+                    self.runtime.trace("premap failed", row=row, why=str(e))
+            self._closing.wait(0.5)
 
     def _start_watch(self, coll, members) -> None:
         from ..runtime.slotwatch import SlotWatch
@@ -335,6 +352,7 @@ class RankProcess:
         self.carrier.send(reply)
 
     def close(self) -> None:
+        self._closing.set()
         if self.watch is not None:
             self.watch.stop()
         if self.ckv is not None:

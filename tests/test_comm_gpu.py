@@ -70,6 +70,21 @@ def _worker(rank: int, world: int, port: int, results, nvls: bool = False):
         dist.all_gather(allf, fused)
         out["gemm_ar_same_on_ranks"] = all(torch.equal(allf[0], f) for f in allf)
         out["status"] = coll.status() + kops.check_status()
+        # 2b. fused GEMMs of different K (so different cluster splits) back to back, as o_proj and
+        # down_proj alternate in decode: the words of one must never be taken for the other's
+        ok = True
+        for it in range(6):
+            for K2 in (512, 1792):
+                g2 = torch.Generator(device="cpu").manual_seed(1000 + 10 * it + K2 + rank)
+                x2 = torch.randn(64, K2, generator=g2).bfloat16().to(dev)
+                w2 = (torch.randn(4096, K2, generator=torch.Generator().manual_seed(K2 + rank)) / 64).bfloat16().to(dev)
+                f2 = coll.linear_allreduce(kops, x2, w2)
+                p2 = kops.linear(x2, w2)
+                ps2 = [torch.empty_like(p2) for _ in range(world)]
+                dist.all_gather(ps2, p2)
+                ok &= bool(torch.allclose(f2.float(), ref.member_sum(ps2).float(), rtol=2e-2, atol=2e-2))
+        out["alternating_splits_close"] = ok
+        out["status"] += coll.status() + kops.check_status()
         # 3. a member that never enters the call: named late, released by the abort word (P2P only:
         # no member of an NVLS group is ever left behind on this pool)
         torch.cuda.synchronize()
@@ -133,6 +148,7 @@ def test_peer_collectives(nvls):
         o = res[r]
         assert o["fdar_exact"], o
         assert o["gemm_ar_close"] and o["gemm_ar_same_on_ranks"], o
+        assert o["alternating_splits_close"], o
         assert o["status"] == 0, o
         if not nvls:
             assert o["after_resume"], o
