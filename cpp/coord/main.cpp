@@ -29,6 +29,7 @@
 #include <map>
 #include <set>
 
+#include "cover.h"
 #include "everserve_pb.h"
 #include "net.h"
 #include "state.h"
@@ -70,6 +71,13 @@ struct Engine {
   std::string cause;
   bool down = false;
   std::unique_ptr<InFlight> in_flight;
+  // the cover plan last sent, and which members reported each planned group formed
+  uint64_t cover_gen = 0;
+  std::string cover_sig;
+  signals::CoverPlan cover;
+  std::vector<std::vector<uint32_t>> cover_covers;
+  std::map<std::string, std::set<std::string>> cover_formed;
+  std::map<std::string, std::string> cover_failed;
 };
 
 struct Node {
@@ -348,6 +356,7 @@ struct Coordinator {
           " ms");
     e.in_flight.reset();
     update_gauges();
+    replan(e);
     drive(e);  // losses that arrived during the change
   }
 
@@ -381,6 +390,86 @@ struct Coordinator {
     }
     metrics().set("everserve_daemons_connected", {}, (double)linked);
     metrics().set("everserve_workers_registered", {}, (double)workers);
+  }
+
+  // ---- cover plans -----------------------------------------------------------------------------
+  static std::string member_key(const signals::SetMember& m) {
+    return m.has_spare ? "R" + std::to_string(m.spare.for_rank) + "@" + m.spare.node + ":" +
+                             std::to_string(m.spare.device)
+                       : std::to_string(m.rank);
+  }
+
+  void replan(Engine& e) {
+    if (!policy.cover_enabled || e.down || e.in_flight) return;
+    CoverInput in;
+    in.engine = e.name;
+    in.epoch = e.epoch;
+    auto ep = policy.engines.find(e.name);
+    in.tp = ep != policy.engines.end() ? ep->second.tensor : std::max<uint32_t>(1, (uint32_t)e.workers.size());
+    in.pp = ep != policy.engines.end() ? ep->second.pipeline : 1;
+    if (e.workers.size() < (size_t)in.tp * in.pp) return;  // not every rank registered yet
+    for (auto& [r, h] : e.workers) in.holders[r] = {h.node, h.device};
+    in.spares = e.spares;
+    in.max_groups_per_gpu = policy.cover_max_groups_per_gpu;
+    std::vector<std::vector<uint32_t>> covers;
+    signals::CoverPlan plan = plan_cover(in, &covers);
+    const std::string sig = plan.serialize();
+    if (sig == e.cover_sig) return;
+    e.cover_sig = sig;
+    plan.generation = ++e.cover_gen;
+    e.cover = plan;
+    e.cover_covers = covers;
+    e.cover_formed.clear();
+    e.cover_failed.clear();
+    coord::CoordToDaemon m;
+    m.has_cover_plan = true;
+    m.cover_plan = plan;
+    for (auto& node : engine_nodes(e)) to_node(node, m);
+    metrics().inc("everserve_cover_plans_total", {{"engine", e.name}});
+    event("engine " + e.name + ": cover plan " + std::to_string(plan.generation) + " (" +
+          std::to_string(plan.sets.size()) + " sets, " + std::to_string(plan.groups.size()) + " groups)");
+    update_cover_gauge(e);
+  }
+
+  bool set_covered(const Engine& e, size_t i) const {
+    for (uint32_t g : e.cover.sets[i].groups) {
+      const auto& grp = e.cover.groups[g];
+      auto it = e.cover_formed.find(spans_key(grp.spans));
+      if (it == e.cover_formed.end() || it->second.size() < grp.spans.size()) return false;
+    }
+    return true;
+  }
+
+  void update_cover_gauge(const Engine& e) {
+    double n = 0;
+    for (size_t i = 0; i < e.cover.sets.size(); i++) n += set_covered(e, i);
+    metrics().set("everserve_engine_covered_sets", {{"engine", e.name}}, n);
+  }
+
+  void on_cover_report(const coord::CoverReport& r) {
+    const signals::GroupFormed* f = r.has_formed ? &r.formed : nullptr;
+    std::string engine_name;
+    uint64_t gen = 0;
+    std::vector<signals::SetMember> spans;
+    signals::SetMember who;
+    if (r.has_formed) engine_name = r.formed.engine, gen = r.formed.generation, spans = r.formed.spans, who = r.formed.member;
+    else if (r.has_failed) engine_name = r.failed.engine, gen = r.failed.generation, spans = r.failed.spans, who = r.failed.member;
+    else if (r.has_released) engine_name = r.released.engine, gen = r.released.generation, spans = r.released.spans, who = r.released.member;
+    else return;
+    auto it = engines.find(engine_name);
+    if (it == engines.end() || it->second.cover_gen != gen) return;  // a report of an older plan
+    Engine& e = it->second;
+    const std::string k = spans_key(spans);
+    if (f) {
+      e.cover_formed[k].insert(member_key(who));
+      metrics().observe("everserve_cover_form_seconds", {{"engine", e.name}}, f->seconds);
+    } else if (r.has_failed) {
+      e.cover_failed[k] = r.failed.error;
+      metrics().inc("everserve_cover_failures_total", {{"engine", e.name}});
+    } else {
+      e.cover_formed[k].erase(member_key(who));
+    }
+    update_cover_gauge(e);
   }
 
   // ---- daemon links ----------------------------------------------------------------------------
@@ -443,6 +532,7 @@ struct Coordinator {
       default: break;
     }
     update_gauges();
+    replan(e);
   }
 
   void from_daemon(Conn& c, const std::string& frame) {
@@ -511,6 +601,8 @@ struct Coordinator {
       to_node(node, out);
     } else if (m.has_node_notice) {
       drain(node, m.node_notice.deadline_ms, "node notice: " + m.node_notice.source);
+    } else if (m.has_cover_report) {
+      on_cover_report(m.cover_report);
     } else if (m.has_replay_ask || m.has_replay_offer) {
       coord::CoordToDaemon out;
       std::string eng;
@@ -595,9 +687,19 @@ struct Coordinator {
       first = false;
     }
     s += "]";
+    std::string cov = "{\"generation\":" + std::to_string(e.cover_gen) + ",\"sets\":[";
+    for (size_t i = 0; i < e.cover.sets.size(); i++) {
+      std::string ranks = "[";
+      if (i < e.cover_covers.size())
+        for (size_t k = 0; k < e.cover_covers[i].size(); k++)
+          ranks += (k ? "," : "") + std::to_string(e.cover_covers[i][k]);
+      cov += std::string(i ? "," : "") + "{\"purpose\":\"" + json_escape(e.cover.sets[i].purpose) + "\",\"covers\":" +
+             ranks + "],\"covered\":" + (set_covered(e, i) ? "true" : "false") + "}";
+    }
+    cov += "]}";
     return "{\"metadata\":{\"name\":\"" + json_escape(e.name) + "\"},\"status\":{\"epoch\":" + std::to_string(e.epoch) +
            ",\"worldSize\":" + std::to_string(e.world) + ",\"down\":" + (e.down ? "true" : "false") +
-           ",\"changing\":" + (e.in_flight ? "true" : "false") + ",\"workers\":" + w + ",\"spares\":" + s + "}}";
+           ",\"changing\":" + (e.in_flight ? "true" : "false") + ",\"workers\":" + w + ",\"spares\":" + s + ",\"cover\":" + cov + "}}";
   }
 
   bool api(const HttpRequest& req, HttpResponse& resp) {
@@ -770,6 +872,10 @@ int main(int argc, char** argv) {
   metrics().describe("everserve_spares", "Spares by engine and state", "gauge");
   metrics().describe("everserve_engine_down", "1 for an engine whose change was abandoned", "gauge");
   metrics().describe("everserve_spec_writes_total", "Writes to the spec store", "counter");
+  metrics().describe("everserve_cover_plans_total", "Cover plans sent per engine", "counter");
+  metrics().describe("everserve_engine_covered_sets", "Planned member sets whose groups every member formed", "gauge");
+  metrics().describe("everserve_cover_form_seconds", "Time a member took to form a planned group", "histogram");
+  metrics().describe("everserve_cover_failures_total", "Planned groups a member failed to form", "counter");
   metrics().describe("everserve_fenced_total", "Reports dropped as older than the engine's epoch", "counter");
   metrics().describe("everserve_unheard_ranks_lost_total", "Loss reports naming ranks the coordinator does not hold", "counter");
   Address a;

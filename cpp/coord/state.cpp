@@ -40,6 +40,10 @@ bool parse_policy(const std::string& json, Policy& out, std::string& err) {
   if (out.outcomes.empty()) out.outcomes = {signals::Outcome_OUTCOME_REPLACE};
   out.max_concurrent_losses = u32(j.get("maxConcurrentLosses"), 0);
   out.notice_min_ms = u32(j.get("noticeMinMs"), 0);
+  if (const Json* cv = j.get("cover")) {
+    if (const Json* en = cv->get("enabled")) out.cover_enabled = en->b;
+    out.cover_max_groups_per_gpu = u32(cv->get("maxGroupsPerGpu"), 0);
+  }
   if (const Json* es = j.get("engines")) {
     for (auto& e : es->arr) {
       EnginePolicy ep;

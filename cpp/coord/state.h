@@ -23,6 +23,8 @@ struct Policy {
   std::vector<int32_t> outcomes;  // signals::Outcome values, in preference order
   uint32_t max_concurrent_losses = 0;  // 0: no limit
   uint32_t notice_min_ms = 0;
+  bool cover_enabled = false;       // plan groups ahead of losses (policy "cover.enabled")
+  uint32_t cover_max_groups_per_gpu = 0;
   std::map<std::string, EnginePolicy> engines;
   uint32_t world_size(const std::string& engine) const;
 };

@@ -5,8 +5,8 @@ Every epoch has its own groups. They are built from the engine's rendezvous stor
 any process restarting and without the default process group (whose membership cannot change).
 Ranks keep their logical positions across epochs: a spare holds the rank it took.
 
-* :class:`EpochGroups` - one epoch's groups for one rank: the world group (pipeline sends and
-  receives) and its stage's tensor-parallel group. gloo on the CPU, NCCL on GPUs.
+* :class:`EpochGroups` - one epoch's groups for one rank: its column's pipeline group (sends and
+  receives between stages) and its stage's tensor-parallel group. gloo on the CPU, NCCL on GPUs.
 * :class:`Exchange` - the pipeline transport: a stage's output (hidden state and residual, one
   ``[2, n, hidden]`` tensor) goes to the same column of the next stage.
 * :class:`GroupCollective` - the model's tensor-parallel all-reduce / all-gather over an epoch's
@@ -46,12 +46,20 @@ def _make_pg(store, prefix: str, rank: int, size: int, device: torch.device, tim
 
 
 class EpochGroups:
+    """`pipe`: the rank's column across the stages (group rank = stage), for the pipeline's sends
+    and receives; `tp`: the rank's stage (group rank = column). A pipe group formed ahead of the
+    change (a cover group over the same members) can be handed in as `pipe`."""
+
     def __init__(self, store, epoch: int, rank: int, layout: ParallelLayout, device: torch.device,
-                 timeout_s: float = 30.0):
+                 timeout_s: float = 30.0, pipe=None):
         self.epoch, self.rank, self.layout, self.device = epoch, rank, layout, device
         self.world_size = layout.world
-        self.world = _make_pg(store, f"e{epoch}/world/", rank, layout.world, device, timeout_s) \
-            if layout.world > 1 else None
+        pp = layout.pipeline_parallel
+        self.adopted = pipe is not None
+        self.pipe = pipe
+        if self.pipe is None and pp > 1:
+            col = layout.column(rank) + layout.replica(rank) * layout.tensor_parallel
+            self.pipe = _make_pg(store, f"e{epoch}/pipe{col}/", layout.stage(rank), pp, device, timeout_s)
         tp = layout.tensor_parallel
         self.tp = None
         if tp > 1:
@@ -59,7 +67,7 @@ class EpochGroups:
             self.tp = _make_pg(store, f"e{epoch}/tp{stage}/", layout.column(rank), tp, device, timeout_s)
 
     def abort(self) -> None:
-        for pg in (self.world, self.tp):
+        for pg in (self.pipe, self.tp):
             if pg is None:
                 continue
             try:
@@ -80,11 +88,12 @@ class SwappableGroups:
         self.refused = threading.Event()
         self._lock = threading.Lock()
 
-    def form(self, epoch: int, rank: int | None = None) -> EpochGroups:
-        """Build the epoch's groups (a rendezvous with every member of the epoch)."""
+    def form(self, epoch: int, rank: int | None = None, pipe=None) -> EpochGroups:
+        """Build the epoch's groups (a rendezvous with every member of the epoch), adopting `pipe`
+        when a pre-formed pipeline group over the epoch's members is at hand."""
         if rank is not None:
             self.rank = rank
-        g = EpochGroups(self.store, epoch, self.rank, self.layout, self.device, self.timeout_s)
+        g = EpochGroups(self.store, epoch, self.rank, self.layout, self.device, self.timeout_s, pipe=pipe)
         with self._lock:
             old, self.current = self.current, g
             self.refused.clear()
@@ -114,15 +123,13 @@ class Exchange:
 
     def send_hidden(self, hidden: torch.Tensor, residual: torch.Tensor) -> None:
         g = self.groups.live()
-        dst = g.layout.next_stage(g.rank)
         buf = torch.stack([hidden.to(self.dtype), residual.to(self.dtype)]).contiguous()
-        g.world.send([buf], dst, 0).wait()
+        g.pipe.send([buf], g.layout.stage(g.rank) + 1, 0).wait()
 
     def recv_hidden(self, n: int) -> tuple[torch.Tensor, torch.Tensor]:
         g = self.groups.live()
-        src = g.layout.prev_stage(g.rank)
         buf = torch.empty(2, n, self.hidden, dtype=self.dtype, device=g.device)
-        g.world.recv([buf], src, 0).wait()
+        g.pipe.recv([buf], g.layout.stage(g.rank) - 1, 0).wait()
         return buf[0], buf[1]
 
 

@@ -59,7 +59,7 @@ def wait_listening(addr: str, timeout_s: float = 15.0) -> None:
 class ControlPlane:
     def __init__(self, workdir: str, engines: list[dict] | None = None, node: str = "n0",
                  outcomes=("OUTCOME_REPLACE",), heartbeat_ms: int = 500, store_slots: int = 1 << 16,
-                 store_budget: int = 8 << 30, ack_timeout_ms: int = 120000):
+                 store_budget: int = 8 << 30, ack_timeout_ms: int = 120000, cover: bool = True):
         self.dir = os.path.abspath(workdir)
         os.makedirs(self.dir, exist_ok=True)
         self.node = node
@@ -69,7 +69,7 @@ class ControlPlane:
         self.api = f"127.0.0.1:{free_port()}"
         self.policy_path = os.path.join(self.dir, "policy.json")
         with open(self.policy_path, "w") as f:
-            json.dump({"outcomesInOrder": list(outcomes), "engines": engines or []}, f)
+            json.dump({"outcomesInOrder": list(outcomes), "engines": engines or [], "cover": {"enabled": cover}}, f)
         self.heartbeat_ms = heartbeat_ms
         self.store_slots = store_slots
         self.store_budget = store_budget

@@ -245,11 +245,28 @@ class MultiprocExecutor:
                 pass
 
     def _boundary(self, epoch: int) -> dict[int, dict]:
+        members = {}
         for r, link in self.links.items():
             if "row" in link.hello:
                 self.rows[r] = int(link.hello["row"])
+            members[r] = link.hello.get("key", str(r))
+        # a pre-formed pipeline group is adopted only if every member holds it (two phases)
+        adopt = False
+        if self.layout.pipeline_parallel > 1 and any(not str(k).isdigit() for k in members.values()):
+            for link in self.links.values():
+                link.send({"op": "cover_query", "epoch": epoch, "members": members})
+            have = []
+            for link in self.links.values():
+                while True:
+                    reply = link.get(timeout=self.change_timeout_s)
+                    if reply["op"] == "cover_have" and reply.get("epoch") == epoch:
+                        break
+                have.append(bool(reply["have"]))
+            adopt = all(have)
         for link in self.links.values():
-            link.send({"op": "boundary", "epoch": epoch, "rows": dict(self.rows)})
+            link.send({"op": "boundary", "epoch": epoch, "rows": dict(self.rows), "members": members,
+                       "adopt": adopt})
+        self.adopted = {}
         computed = {}
         for r, link in self.links.items():
             while True:
@@ -259,6 +276,10 @@ class MultiprocExecutor:
             if reply["op"] == "error":
                 raise RankLost({r}, f"boundary of epoch {epoch}: {reply['error']}")
             computed[r] = reply["computed"]
+            self.adopted[r] = bool(reply.get("adopted"))
+        # after the boundary every process is its rank in later plans
+        for r, link in self.links.items():
+            link.hello["key"] = str(r)
         return computed
 
     # ---- membership change -----------------------------------------------------------------------
@@ -310,6 +331,7 @@ class MultiprocExecutor:
         self.links = dict(sorted(self.links.items()))
         computed = self._boundary(mc.epoch)
         rec.t_ready = time.monotonic()
+        rec.coordinator["pre_formed_groups"] = sorted(r for r, a in self.adopted.items() if a)
         self.epoch = mc.epoch
         sch = engine.scheduler
         for req in sch.running:

@@ -113,6 +113,14 @@ class RankProcess:
         self.leaving = False
         self.taken = False
         self.daemon = None
+        self.cover = None
+        self.key = f"R{self.rank}@{a.node}:{self.identity()[1]}" if self.spare else str(self.rank)
+        if a.daemon and a.pp > 1:
+            from ..runtime.cover import Cover
+
+            self.cover = Cover(self.rdzv, self.key, self.engine, dev,
+                               report=lambda r: self.daemon.report(r) if self.daemon is not None else None,
+                               timeout_s=a.group_timeout)
         if a.daemon:
             from ..contract.identity import identity
 
@@ -191,6 +199,8 @@ class RankProcess:
 
     def on_change(self, change) -> str | None:
         self.runtime.trace("change", epoch=change.epoch)
+        if self.cover is not None:
+            self.cover.freeze()
         if self.spare and not self.taken:
             takes = [t for t in change.take if t.rank == self.rank]
             if not takes:
@@ -233,6 +243,16 @@ class RankProcess:
             self.offer = offer
             self.joined.set()
 
+    def _column_keys(self, members: dict) -> list[str]:
+        """This rank's column across the stages, in stage order, by the keys cover plans use."""
+        rs = sorted((int(r) for r in members if self.layout.column(int(r)) == self.layout.column(self.rank)
+                     and self.layout.replica(int(r)) == self.layout.replica(self.rank)))
+        return [str(members[r] if r in members else members[str(r)]) for r in rs]
+
+    def on_cover_plan(self, plan) -> None:
+        if self.cover is not None:
+            self.cover.apply(plan)
+
     def on_displaced(self, epoch: int, why: str) -> None:
         self.runtime.trace("displaced", epoch=epoch, why=why)
 
@@ -248,7 +268,7 @@ class RankProcess:
 
     def link(self, address: str, token: str) -> None:
         hello = {"rank": self.rank, "row": self.row, "pid": os.getpid(), "role": "spare" if self.spare else "worker",
-                 "token": token,
+                 "token": token, "key": self.key,
                  "num_blocks": self.worker.num_blocks, "computed": dict(self.computed), "load_s": self.load_s}
         self.carrier = CarrierClient(address, hello)
 
@@ -264,6 +284,10 @@ class RankProcess:
                 self._step(msg)
             elif op == "boundary":
                 self._boundary(msg)
+            elif op == "cover_query":
+                keys = self._column_keys(msg["members"])
+                self.carrier.send({"op": "cover_have", "epoch": msg["epoch"], "rank": self.rank,
+                                   "have": bool(self.cover is not None and self.cover.has(keys))})
             elif op == "finished":
                 if self.ckv is not None and self.layout.stage(self.rank) == 0 and self.layout.column(self.rank) == 0:
                     for rid in msg["ids"]:
@@ -333,7 +357,16 @@ class RankProcess:
                 # rows the departing (or last) holder committed after the restore
                 counts = self.ckv.restore(self.rank, since_step=self.ckv.restored_step + 1)
                 self.computed.update(counts)
-            self.groups.form(epoch, self.rank)
+            pipe = None
+            if self.cover is not None and msg.get("adopt"):
+                pipe = self.cover.take(self._column_keys(msg["members"]))
+                if pipe is None:
+                    raise RuntimeError("the head chose a pre-formed group this rank does not hold")
+            g = self.groups.form(epoch, self.rank, pipe=pipe)
+            if self.cover is not None:
+                self.cover.set_me(str(self.rank))
+                self.cover.unfreeze()
+            self.runtime.trace("groups", epoch=epoch, adopted=g.adopted)
             if "rows" in msg:
                 self.rows = {int(r): int(row) for r, row in msg["rows"].items()}
             if self.region is not None:
@@ -346,13 +379,15 @@ class RankProcess:
                 self._start_watch(self.collective, members)
             self.runtime.at_boundary(epoch)
             reply = {"op": "ready", "epoch": epoch, "rank": self.rank, "computed": dict(self.computed),
-                     "form_s": time.monotonic() - t0}
+                     "form_s": time.monotonic() - t0, "adopted": g.adopted}
         except Exception as e:  # noqa: BLE001
             reply = {"op": "error", "epoch": epoch, "rank": self.rank, "error": f"{type(e).__name__}: {e}"}
         self.carrier.send(reply)
 
     def close(self) -> None:
         self._closing.set()
+        if self.cover is not None:
+            self.cover.close()
         if self.watch is not None:
             self.watch.stop()
         if self.ckv is not None:

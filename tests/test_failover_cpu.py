@@ -42,6 +42,7 @@ def _run(workdir, kill_at=None, spares=(1,)):
         try:
             if spares:
                 cp.wait_spares("e0", len(spares))
+                _wait_covered(cp, "e0")
             eng = Engine(cfg, executor=ex)
             eng.wrap_step(failover(ex, eng))
             if kill_at is not None:
@@ -54,6 +55,19 @@ def _run(workdir, kill_at=None, spares=(1,)):
             ex.shutdown()
 
 
+def _wait_covered(cp, engine, timeout_s=60.0):
+    """The coordinator's cover plan for the spare is formed by every member."""
+    import time
+
+    deadline = time.monotonic() + timeout_s
+    while time.monotonic() < deadline:
+        sets = cp.engine_view(engine)["status"]["cover"]["sets"]
+        if any(s["covers"] and s["covered"] for s in sets):
+            return
+        time.sleep(0.05)
+    raise TimeoutError(f"no covered replacement set: {cp.engine_view(engine)['status']['cover']}")
+
+
 @pytest.mark.slow
 def test_sigkill_rank1_spare_takes_over_token_identical(tmp_path):
     base, changes0, _, _ = _run(tmp_path / "nofault", spares=())
@@ -63,6 +77,7 @@ def test_sigkill_rank1_spare_takes_over_token_identical(tmp_path):
     rec = changes[0].as_dict()
     assert rec["lost"] == [1] and rec["epoch"] == 1
     assert rec["from"] == "fault" and rec["resumed_ms"] is not None
+    assert rec["coordinator"]["pre_formed_groups"] == [0, 1]  # the cover group was adopted
     assert mism == 0
     assert out == base, "streams differ from the no-fault run"
     assert all(len(o) == TOKENS for o in out)
