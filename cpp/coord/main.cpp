@@ -392,6 +392,29 @@ struct Coordinator {
     metrics().set("everserve_workers_registered", {}, (double)workers);
   }
 
+  // ---- spares the daemons launch ---------------------------------------------------------------
+  void launch_spares(const std::string& node) {
+    for (auto& [name, ep] : policy.engines) {
+      if (ep.launch_command.empty()) continue;
+      for (auto& slot : ep.spare_slots) {
+        if (slot.node != node) continue;
+        coord::CoordToDaemon m;
+        m.has_launch_spare = true;
+        auto& ls = m.launch_spare;
+        ls.engine = name;
+        if (slot.rank >= 0) {
+          ls.rank = (uint32_t)slot.rank;
+          ls.has_rank = true;
+        }
+        ls.device = slot.device;
+        ls.command = ep.launch_command;
+        ls.env = ep.launch_env;
+        to_node(node, m);
+        event("engine " + name + ": spare launch asked of " + node + ":" + std::to_string(slot.device));
+      }
+    }
+  }
+
   // ---- cover plans -----------------------------------------------------------------------------
   static std::string member_key(const signals::SetMember& m) {
     return m.has_spare ? "R" + std::to_string(m.spare.for_rank) + "@" + m.spare.node + ":" +
@@ -559,6 +582,7 @@ struct Coordinator {
       }
       event("node " + node + " linked");
       update_gauges();
+      launch_spares(node);
       return;
     }
     if (node.empty()) return;  // nothing before a hello
@@ -611,9 +635,11 @@ struct Coordinator {
         out.replay_ask = m.replay_ask;
         eng = m.replay_ask.engine;
       } else {
+        // an offer goes back to the node of the process that asked
         out.has_replay_offer = true;
         out.replay_offer = m.replay_offer;
-        eng = m.replay_offer.engine;
+        to_node(m.replay_offer.to.node, out);
+        return;
       }
       auto it = engines.find(eng);
       if (it != engines.end())

@@ -60,6 +60,20 @@ bool parse_policy(const std::string& json, Policy& out, std::string& err) {
       if (const Json* sn = e.get("spareNodes"))
         for (auto& s : sn->arr) ep.spare_nodes.push_back(s.str);
       if (const Json* rb = e.get("releaseBoundMs")) ep.release_bound_ms = (int64_t)u32(rb, 0);
+      if (const Json* sl = e.get("spares"))
+        for (auto& x : sl->arr) {
+          SpareSlotPolicy slot;
+          if (const Json* n = x.get("node")) slot.node = n->str;
+          slot.device = u32(x.get("device"), 0);
+          if (const Json* r = x.get("rank")) slot.rank = (int64_t)u32(r, 0);
+          ep.spare_slots.push_back(slot);
+        }
+      if (const Json* sl = e.get("spareLaunch")) {
+        if (const Json* c = sl->get("command"))
+          for (auto& a : c->arr) ep.launch_command.push_back(a.str);
+        if (const Json* env = sl->get("env"))
+          for (auto& [k, v] : env->obj) ep.launch_env[k] = v.str;
+      }
       out.engines[ep.name] = ep;
     }
   }

@@ -11,12 +11,21 @@
 
 namespace es {
 
+struct SpareSlotPolicy {
+  std::string node;
+  uint32_t device = 0;
+  int64_t rank = -1;  // -1: any rank
+};
+
 struct EnginePolicy {
   std::string name;
   uint32_t tensor = 1, pipeline = 1, data = 1, expert = 1;
   bool placement_independent = false;
   std::vector<std::string> spare_nodes;
   int64_t release_bound_ms = -1;
+  std::vector<SpareSlotPolicy> spare_slots;   // where the daemons launch this engine's spares
+  std::vector<std::string> launch_command;    // how (empty: the engine launches its own)
+  std::map<std::string, std::string> launch_env;
 };
 
 struct Policy {

@@ -18,6 +18,7 @@
 //     reports made while unlinked are held and sent on the next link. Messages from an older
 //     coordinator term than the highest seen are ignored (fencing).
 #include <signal.h>
+#include <sys/wait.h>
 #include <unistd.h>
 
 #include <algorithm>
@@ -48,6 +49,19 @@ struct Proc {
   signals::Register reg;
 };
 
+// A spare this daemon launched for the coordinator (LaunchSpare) and keeps running: a spare that
+// exits before it takes a rank is started again after a backoff (1 s, doubling to 30 s; reset
+// after a minute of running). One that took a rank is a worker and no longer supervised.
+struct Supervised {
+  coord::LaunchSpare spec;
+  pid_t pid = 0;
+  uint64_t started_ms = 0;
+  uint64_t backoff_ms = 1000;
+  uint64_t next_start_ms = 0;
+  uint32_t starts = 0;
+  bool taken = false;
+};
+
 struct PendingDelivery {
   coord::Deliver deliver;
   std::set<uint64_t> waiting;  // process connections that owe an Ack
@@ -71,6 +85,8 @@ struct Daemon {
   uint64_t instance = 0;
   uint64_t backoff_ms = 100;
   std::mt19937_64 rng{std::random_device{}()};
+  std::string socket;  // this daemon's process socket (handed to the spares it launches)
+  std::map<std::string, Supervised> supervised;  // engine:device -> launched spare
 
   // ---- up: to the coordinator ------------------------------------------------------------------
   void up(const coord::DaemonToCoord& m) {
@@ -174,6 +190,8 @@ struct Daemon {
           if (p.registered && p.engine == m.committed.engine && p.role == signals::Role_ROLE_SPARE &&
               (p.rank == t.rank || p.any_rank) && t.node == node && (t.device == p.device)) {
             p.role = signals::Role_ROLE_WORKER;
+            for (auto& [key, sv] : supervised)
+              if (sv.pid != 0 && (uint32_t)sv.pid == p.pid) sv.taken = true;
             p.rank = t.rank;
             p.any_rank = false;
             break;
@@ -264,10 +282,14 @@ struct Daemon {
         s.replay_ask = m.replay_ask;
         to_engine(m.replay_ask.engine, s, false, false, true);
       } else {
+        // an offer goes to the connection that asked (its ProcessRef), registered or not
         s.has_replay_offer = true;
         s.replay_offer = m.replay_offer;
-        to_engine(m.replay_offer.engine, s, false, true, false);
+        const auto& to = m.replay_offer.to;
+        if (to.node == node && to.instance == instance && procs.count(to.serial)) loop.send(to.serial, s.serialize());
       }
+    } else if (m.has_launch_spare) {
+      launch_spare(m.launch_spare);
     }
   }
 
@@ -483,6 +505,10 @@ struct Daemon {
       if (s.has_replay_ask) {
         m.has_replay_ask = true;
         m.replay_ask = s.replay_ask;
+        m.replay_ask.asker.node = node;  // where the offer must come back to
+        m.replay_ask.asker.instance = instance;
+        m.replay_ask.asker.serial = c.id;
+        m.replay_ask.has_asker = true;
       } else {
         m.has_replay_offer = true;
         m.replay_offer = s.replay_offer;
@@ -511,6 +537,80 @@ struct Daemon {
       worker_event(p, departed_kind(p.role),
                    p.said_goodbye ? signals::StopCause_STOP_CAUSE_STOPPED : signals::StopCause_STOP_CAUSE_LOST,
                    p.said_goodbye ? "goodbye" : "connection ended");
+  }
+
+  // ---- spares launched for the coordinator -----------------------------------------------------
+  void launch_spare(const coord::LaunchSpare& spec) {
+    const std::string key = spec.engine + ":" + std::to_string(spec.device);
+    if (spec.command.empty()) return;
+    auto it = supervised.find(key);
+    if (it != supervised.end() && !it->second.taken) return;  // already standing (or starting)
+    Supervised sv;
+    sv.spec = spec;
+    supervised[key] = sv;
+    start_spare(supervised[key]);
+  }
+
+  void start_spare(Supervised& sv) {
+    std::vector<std::string> envs;
+    for (char** e = environ; *e; e++) envs.emplace_back(*e);
+    auto set = [&](const std::string& k, const std::string& v) { envs.push_back(k + "=" + v); };
+    for (auto& [k, v] : sv.spec.env) set(k, v);
+    set("EVERSERVE_ENGINE", sv.spec.engine);
+    set("EVERSERVE_SPARE_RANK", sv.spec.has_rank ? std::to_string(sv.spec.rank) : "any");
+    set("EVERSERVE_DEVICE", std::to_string(sv.spec.device));
+    set("EVERSERVE_SOCKET", socket);
+    set("EVERSERVE_NODE", node);
+    if (!mirror_socket.empty()) set("EVERSERVE_MIRROR_SOCKET", mirror_socket);
+    const pid_t pid = fork();
+    if (pid < 0) {
+      ES_ERROR("cannot fork a spare for %s", sv.spec.engine.c_str());
+      sv.next_start_ms = now_ms() + sv.backoff_ms;
+      return;
+    }
+    if (pid == 0) {
+      setpgid(0, 0);
+      std::vector<char*> argv, envp;
+      for (auto& a : sv.spec.command) argv.push_back(const_cast<char*>(a.c_str()));
+      argv.push_back(nullptr);
+      for (auto& e : envs) envp.push_back(const_cast<char*>(e.c_str()));
+      envp.push_back(nullptr);
+      execvpe(argv[0], argv.data(), envp.data());
+      _exit(127);
+    }
+    sv.pid = pid;
+    sv.started_ms = now_ms();
+    sv.starts++;
+    metrics().inc("everserve_node_spare_starts_total", {{"engine", sv.spec.engine}});
+    ES_INFO("launched a spare for %s on device %u (pid %d, start %u)", sv.spec.engine.c_str(), sv.spec.device, (int)pid,
+            sv.starts);
+  }
+
+  void supervise() {
+    int status = 0;
+    pid_t pid;
+    while ((pid = waitpid(-1, &status, WNOHANG)) > 0) {
+      for (auto& [key, sv] : supervised) {
+        if (sv.pid != pid) continue;
+        sv.pid = 0;
+        if (sv.taken) break;
+        const uint64_t ran = now_ms() - sv.started_ms;
+        if (ran > 60000) sv.backoff_ms = 1000;
+        sv.next_start_ms = now_ms() + sv.backoff_ms;
+        ES_WARN("spare of %s on device %u exited (status %d) after %llu ms; again in %llu ms", sv.spec.engine.c_str(),
+                sv.spec.device, status, (unsigned long long)ran, (unsigned long long)sv.backoff_ms);
+        sv.backoff_ms = std::min<uint64_t>(sv.backoff_ms * 2, 30000);
+        break;
+      }
+    }
+    const uint64_t now = now_ms();
+    for (auto& [key, sv] : supervised)
+      if (!sv.taken && sv.pid == 0 && now >= sv.next_start_ms) start_spare(sv);
+  }
+
+  void stop_spares() {
+    for (auto& [key, sv] : supervised)
+      if (sv.pid > 0 && !sv.taken) kill(-sv.pid, SIGTERM);
   }
 
   void tick() {
@@ -559,6 +659,7 @@ int main(int argc, char** argv) {
     }
   }
   d.instance = (now_us() << 8) ^ (uint64_t)getpid();
+  d.socket = socket;
   metrics().describe("everserve_node_linked", "1 while the daemon is linked to the coordinator", "gauge");
   metrics().describe("everserve_node_workers", "Workers registered on this node", "gauge");
   Address a;
@@ -571,15 +672,13 @@ int main(int argc, char** argv) {
     return 1;
   }
   if (!discovery.empty()) {
-    // the discovery record (discovery.proto DaemonRecord, binary) for clients that look nodes up
+    // the discovery record (discovery.proto DaemonRecord in proto3 JSON) for processes that look
+    // their node's daemon up
     mkdirs(discovery);
-    std::string rec;
-    pbwire::put_len(rec, 1, d.node);
-    pbwire::put_len(rec, 2, socket);
-    pbwire::put_varint(rec, 4, now_ms());
-    pbwire::put_varint(rec, 5, (uint32_t)getpid());
-    if (!d.mirror_socket.empty()) pbwire::put_len(rec, 6, d.mirror_socket);
-    write_file_atomic(discovery + "/" + d.node + ".daemon", rec);
+    const std::string rec = "{\"node\":\"" + json_escape(d.node) + "\",\"address\":\"" + json_escape(socket) +
+                            "\",\"startedAtMs\":\"" + std::to_string(now_ms()) + "\",\"pid\":" +
+                            std::to_string(getpid()) + ",\"mirrorAddress\":\"" + json_escape(d.mirror_socket) + "\"}";
+    write_file_atomic(discovery + "/" + d.node + ".json", rec);
   }
   if (!metrics_addr.empty() && !serve_http(d.loop, metrics_addr, nullptr, &err)) {
     ES_ERROR("metrics %s: %s", metrics_addr.c_str(), err.c_str());
@@ -587,6 +686,13 @@ int main(int argc, char** argv) {
   }
   d.link();
   d.loop.every(d.heartbeat_ms, [&] { d.tick(); });
+  d.loop.every(100, [&] { d.supervise(); });
+  static Daemon* self = &d;
+  signal(SIGTERM, [](int) {
+    self->stop_spares();
+    _exit(0);
+  });
+  metrics().describe("everserve_node_spare_starts_total", "Spares this daemon started (restarts included)", "counter");
   ES_INFO("node %s serving %s, coordinator %s", d.node.c_str(), socket.c_str(), d.coordinator.c_str());
   d.loop.run();
   return 0;

@@ -87,6 +87,7 @@ class MultiprocExecutor:
                  devices: list[int] | None = None):
         self.cfg = cfg
         self.engine = engine
+        self._closed = False
         self.layout = ParallelLayout(cfg.tensor_parallel, cfg.pipeline_parallel)
         self.step_timeout_s = step_timeout_s
         self.change_timeout_s = change_timeout_s
@@ -104,6 +105,7 @@ class MultiprocExecutor:
                 "--rdzv", self.rdzv_addr, "--head", self.carrier.address]
         if cfg.num_blocks:
             base += ["--num-blocks", str(cfg.num_blocks)]
+        self._startup_args = list(base[3:])  # the engine's configuration, for spares a daemon launches
         if daemon:
             base += ["--daemon", daemon]
         if store:
@@ -123,6 +125,7 @@ class MultiprocExecutor:
             self.region_name = f"es_{engine}_{os.getpid()}_{secrets.token_hex(4)}"
             self.region = SlotRegion.create(self.region_name)
             base += ["--region", self.region_name]
+            self._startup_args += ["--region", self.region_name]
         e = dict(os.environ)
         root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         e["PYTHONPATH"] = os.pathsep.join([root] + [p for p in e.get("PYTHONPATH", "").split(os.pathsep) if p])
@@ -154,6 +157,11 @@ class MultiprocExecutor:
         self.epoch = 0
         self._boundary(0)
         self.client = DaemonClient(daemon, engine, node=node) if daemon else None
+        self._next_row = self.layout.world + len(spares)
+        if self.client is not None:
+            import threading
+
+            threading.Thread(target=self._answer_replays, name="replay-offers", daemon=True).start()
         self.changes: list[ChangeRecord] = []
         self.decode_steps_run = 0
         self.kill_at_decode_step: tuple[int, int] | None = None  # (decode step, rank): host-side fault injection
@@ -282,6 +290,26 @@ class MultiprocExecutor:
             link.hello["key"] = str(r)
         return computed
 
+    def _answer_replays(self) -> None:
+        """Answer spares that a daemon launched with the engine's start-up record."""
+        import json
+        import queue
+
+        while not self._closed:
+            try:
+                ask = self.client.replay_asks.get(timeout=0.5)
+            except queue.Empty:
+                continue
+            row = None
+            if self.region is not None:
+                row = self._next_row
+                self._next_row += 1
+            rec = {"args": self._startup_args, "row": row, "gpu": self.gpu, "world": self.layout.world}
+            try:
+                self.client.offer_replay(ask, json.dumps(rec))
+            except OSError:
+                return
+
     # ---- membership change -----------------------------------------------------------------------
     def notice(self, rank: int, deadline_ms: int = 0) -> None:
         """Announce a planned departure of `rank` (drain): it finishes its step and leaves."""
@@ -342,6 +370,7 @@ class MultiprocExecutor:
         return rec
 
     def shutdown(self) -> None:
+        self._closed = True
         for link in self.links.values():
             try:
                 link.send({"op": "stop"})

@@ -115,3 +115,46 @@ def test_planned_departure_spare_catches_up(tmp_path):
             assert ex.procs["rank1"].wait(timeout=30) == 0
         finally:
             ex.shutdown()
+
+
+@pytest.mark.slow
+def test_daemon_launched_spare_replays_startup_and_takes_over(tmp_path):
+    """The policy places a spare for rank 1 on n0; the daemon launches it, it fetches the
+    engine's start-up record from the head (ReplayAsk/ReplayOffer), stands, and takes rank 1
+    after rank 1 is killed. A spare that exits before any fault is started again."""
+    import sys
+    import time
+
+    base, _, _, _ = _run(tmp_path / "nofault", spares=())
+    cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
+                       max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
+    engines = [{"name": "e0", "pipelineParallel": 2, "spares": [{"node": "n0", "device": 0, "rank": 1}],
+                "spareLaunch": {"command": [sys.executable, "-m", "everserve_b200.serving.spare"],
+                                "env": {"PYTHONPATH": os.path.dirname(os.path.dirname(os.path.abspath(__file__)))}}}]
+    with ControlPlane(str(tmp_path / "launched"), engines=engines) as cp:
+        ex = MultiprocExecutor(cfg, engine="e0", daemon=cp.daemon_socket, store=cp.store_socket, spares=(),
+                               node="n0", log_dir=str(tmp_path / "launched" / "logs"), threads=2)
+        try:
+            cp.wait_spares("e0", 1, timeout_s=300)
+            # supervision: the standing spare is killed; the daemon starts another
+            first = cp.engine_view("e0")["status"]["spares"]
+            import signal as sig
+
+            pid = int(open(os.path.join(cp.dir, "node.log")).read().split("(pid ")[1].split(",")[0])
+            os.kill(pid, sig.SIGKILL)
+            deadline = time.monotonic() + 120
+            while time.monotonic() < deadline:
+                log = open(os.path.join(cp.dir, "node.log")).read()
+                if "start 2)" in log and cp.engine_view("e0")["status"]["spares"]:
+                    break
+                time.sleep(0.2)
+            assert "start 2)" in open(os.path.join(cp.dir, "node.log")).read()
+            assert first
+            _wait_covered(cp, "e0")
+            eng = Engine(cfg, executor=ex)
+            eng.wrap_step(failover(ex, eng))
+            ex.kill_at_decode_step = (KILL_AT, 1)
+            out = eng.generate(_prompts(), max_tokens=TOKENS)
+            assert len(ex.changes) == 1 and out == base
+        finally:
+            ex.shutdown()
