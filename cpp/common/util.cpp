@@ -1,3 +1,5 @@
+#include <algorithm>
+#include <dirent.h>
 #include "util.h"
 
 #include <errno.h>
@@ -301,6 +303,19 @@ std::unique_ptr<Mapping> Mapping::open(const std::string& path, size_t size, boo
     return nullptr;
   }
   return m;
+}
+
+std::vector<std::string> list_dir(const std::string& dir) {
+  std::vector<std::string> out;
+  DIR* d = ::opendir(dir.c_str());
+  if (!d) return out;
+  while (dirent* e = ::readdir(d)) {
+    const std::string n = e->d_name;
+    if (n != "." && n != "..") out.push_back(n);
+  }
+  ::closedir(d);
+  std::sort(out.begin(), out.end());
+  return out;
 }
 
 bool mkdirs(const std::string& path, int mode) {

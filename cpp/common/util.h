@@ -43,6 +43,8 @@ struct Mapping {
   ~Mapping();
   static std::unique_ptr<Mapping> open(const std::string& path, size_t size, bool create, std::string* err = nullptr);
 };
+// Names of the entries of a directory (no "." or ".."); empty when it cannot be read.
+std::vector<std::string> list_dir(const std::string& dir);
 bool mkdirs(const std::string& path, int mode = 0770);
 bool read_file(const std::string& path, std::string& out);
 bool write_file_atomic(const std::string& path, const std::string& data);

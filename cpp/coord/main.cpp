@@ -78,6 +78,9 @@ struct Engine {
   std::vector<std::vector<uint32_t>> cover_covers;
   std::map<std::string, std::set<std::string>> cover_formed;
   std::map<std::string, std::string> cover_failed;
+  // a change an earlier lease holder logged but did not commit: finished once its nodes link
+  bool has_resume = false;
+  spec::ChangeLog resume;
 };
 
 struct Node {
@@ -103,6 +106,7 @@ struct Coordinator {
   uint64_t term = 1;
   uint32_t loss_misses = 3;
   uint64_t delivery_timeout_ms = 130000;
+  bool exit_after_log = false;  // host-side fault injection for tests: the coordinator dies mid-change
   std::map<std::string, Engine> engines;
   std::map<std::string, Node> nodes;
   std::map<uint64_t, std::string> conn_node;
@@ -253,6 +257,18 @@ struct Coordinator {
     }
     // logged before any node hears of it
     write_status(e, f.get(), nullptr);
+    if (exit_after_log) {
+      ES_WARN("exiting after logging the change (EVERSERVE_COORD_EXIT_AFTER_LOG)");
+      _exit(17);
+    }
+    e.pending.clear();
+    e.departing.clear();
+    e.first_report_us = 0;
+    start_delivery(e, std::move(f));
+  }
+
+  // Deliver a logged change to every node it names and wait for their acks (bounded).
+  void start_delivery(Engine& e, std::unique_ptr<InFlight> f) {
     f->delivered_us = now_us();
     for (auto& [node, d] : f->deliveries) {
       auto nit = nodes.find(node);
@@ -267,9 +283,6 @@ struct Coordinator {
       m.deliver = d;
       to_node(node, m);
     }
-    e.pending.clear();
-    e.departing.clear();
-    e.first_report_us = 0;
     metrics().set("everserve_changes_in_flight", {{"engine", e.name}}, 1);
     event("engine " + e.name + ": change to epoch " + std::to_string(f->change.epoch) + " delivered to " +
           std::to_string(f->deliveries.size()) + " node(s)");
@@ -390,6 +403,65 @@ struct Coordinator {
     }
     metrics().set("everserve_daemons_connected", {}, (double)linked);
     metrics().set("everserve_workers_registered", {}, (double)workers);
+  }
+
+  // ---- takeover: views from the spec store and the daemons' announcements ----------------------
+  void load_spec() {
+    if (spec_dir.empty()) return;
+    std::vector<std::string> files = list_dir(spec_dir);
+    for (auto& f : files) {
+      if (f.size() < 8 || f.compare(f.size() - 7, 7, ".status") != 0) continue;
+      std::string data;
+      spec::EngineStatus st;
+      if (!read_file(spec_dir + "/" + f, data) || !st.parse(data) || st.engine.empty()) continue;
+      Engine& e = engine(st.engine);
+      for (auto& a : st.assignments) e.epoch = std::max(e.epoch, a.epoch);
+      if (st.has_change && st.change.has_change) {
+        if (st.change.has_committed) {
+          e.epoch = std::max(e.epoch, st.change.change.epoch);
+        } else {
+          e.has_resume = true;
+          e.resume = st.change;
+          e.epoch = std::max(e.epoch, st.change.change.epoch - 1);
+          event("engine " + e.name + ": change to epoch " + std::to_string(st.change.change.epoch) +
+                " was logged by the previous lease holder and is not committed; finishing it");
+        }
+      }
+    }
+  }
+
+  void try_resume(Engine& e) {
+    if (!e.has_resume || e.in_flight) return;
+    for (auto& nd : e.resume.deliveries) {
+      auto it = nodes.find(nd.node);
+      if (it == nodes.end() || !it->second.linked) return;  // wait for every node it names
+    }
+    auto f = std::make_unique<InFlight>();
+    f->change = e.resume.change;
+    f->cause = "resumed";
+    f->started_ms = now_ms();
+    for (auto& t : e.resume.change.take) {
+      SpareSeat seat;
+      seat.node = t.node;
+      seat.device = t.device;
+      for (auto& sp : e.spares)
+        if (sp.node == t.node && sp.device == t.device) seat = sp;
+      f->take.emplace_back(t.rank, seat);
+    }
+    for (auto& nd : e.resume.deliveries) {
+      coord::Deliver d;
+      d.request_id = next_request++;
+      d.engine = e.name;
+      d.change = f->change;
+      d.has_change = true;
+      d.to_ranks = nd.to_ranks;
+      d.to_spares = nd.to_spares;
+      d.take = nd.take;
+      f->deliveries[nd.node] = d;
+    }
+    e.has_resume = false;
+    e.down = false;
+    start_delivery(e, std::move(f));
   }
 
   // ---- spares the daemons launch ---------------------------------------------------------------
@@ -530,6 +602,10 @@ struct Coordinator {
         s.for_rank = ev.any_rank ? -1 : (int64_t)ev.rank;
         s.pid = ev.pid;
         s.fingerprint = fingerprint_of(ev);
+        // a daemon announces its processes again on every link: one seat per (node, device)
+        e.spares.erase(std::remove_if(e.spares.begin(), e.spares.end(),
+                                      [&](const SpareSeat& x) { return x.node == node && x.device == ev.device; }),
+                       e.spares.end());
         if (!e.fingerprint.empty() && !s.fingerprint.empty() && s.fingerprint != e.fingerprint) {
           metrics().inc("everserve_spares_mismatched_total", {{"engine", e.name}});
           event("engine " + e.name + ": spare on " + node + " has another software identity; it cannot take a rank");
@@ -583,6 +659,9 @@ struct Coordinator {
       event("node " + node + " linked");
       update_gauges();
       launch_spares(node);
+      loop.every(200, [this] {
+        for (auto& [name, en] : engines) try_resume(en);
+      }, false);
       return;
     }
     if (node.empty()) return;  // nothing before a hello
@@ -889,6 +968,8 @@ int main(int argc, char** argv) {
     ES_ERROR("%s", err.c_str());
     return 1;
   }
+  co.exit_after_log = env_or("EVERSERVE_COORD_EXIT_AFTER_LOG", "") == "1";
+  co.load_spec();
   metrics().describe("everserve_changes_total", "Membership changes by engine, cause, outcome and verdict", "counter");
   metrics().describe("everserve_change_seconds", "From the first loss report to the commit", "histogram");
   metrics().describe("everserve_change_decision_seconds", "Time to choose an outcome", "histogram");

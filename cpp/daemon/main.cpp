@@ -152,6 +152,10 @@ struct Daemon {
       loop.send(coord_conn, held.front());
       held.pop_front();
     }
+    // a coordinator that took the lease over knows nothing of this node's processes: announce them
+    for (auto& [id, p] : procs)
+      if (p.registered && registered_kind(p.role) != coord::WorkerEvent_Kind_KIND_UNSPECIFIED)
+        worker_event(p, registered_kind(p.role), 0, "");
     metrics().set("everserve_node_linked", {}, 1);
     ES_INFO("linked to coordinator %s", coordinator.c_str());
   }

@@ -59,7 +59,10 @@ def wait_listening(addr: str, timeout_s: float = 15.0) -> None:
 class ControlPlane:
     def __init__(self, workdir: str, engines: list[dict] | None = None, node: str = "n0",
                  outcomes=("OUTCOME_REPLACE",), heartbeat_ms: int = 500, store_slots: int = 1 << 16,
-                 store_budget: int = 8 << 30, ack_timeout_ms: int = 120000, cover: bool = True):
+                 store_budget: int = 8 << 30, ack_timeout_ms: int = 120000, cover: bool = True,
+                 standby: bool = False, coord_env: dict | None = None):
+        """`standby`: a second coordinator waits for the lease and takes over when the first
+        exits. `coord_env`: extra environment of the first coordinator."""
         self.dir = os.path.abspath(workdir)
         os.makedirs(self.dir, exist_ok=True)
         self.node = node
@@ -74,22 +77,31 @@ class ControlPlane:
         self.store_slots = store_slots
         self.store_budget = store_budget
         self.ack_timeout_ms = ack_timeout_ms
+        self.standby = standby
+        self.coord_env = coord_env or {}
         self.procs: dict[str, subprocess.Popen] = {}
         self._logs = []
 
-    def _run(self, name: str, args: list[str]) -> None:
+    def _run(self, name: str, args: list[str], env: dict | None = None) -> None:
         log = open(os.path.join(self.dir, f"{name}.log"), "w")  # noqa: SIM115
         self._logs.append(log)
-        self.procs[name] = subprocess.Popen(args, stdout=log, stderr=subprocess.STDOUT)
+        e = None
+        if env:
+            e = dict(os.environ)
+            e.update(env)
+        self.procs[name] = subprocess.Popen(args, stdout=log, stderr=subprocess.STDOUT, env=e)
 
     def start(self) -> "ControlPlane":
         self._run("store", [binary("everserve-store"), "--socket", self.store_socket, "--data-dir",
                             os.path.join(self.dir, "store"), "--slots", str(self.store_slots), "--budget-bytes",
                             str(self.store_budget)])
-        self._run("coord", [binary("everserve-coord"), "--listen", self.coord_socket, "--policy", self.policy_path,
-                            "--spec-store", os.path.join(self.dir, "spec"), "--lease", os.path.join(self.dir, "lease"),
-                            "--api-addr", self.api])
+        coord = [binary("everserve-coord"), "--listen", self.coord_socket, "--policy", self.policy_path,
+                 "--spec-store", os.path.join(self.dir, "spec"), "--lease", os.path.join(self.dir, "lease"),
+                 "--api-addr", self.api]
+        self._run("coord", coord, self.coord_env)
         wait_listening(self.coord_socket)
+        if self.standby:
+            self._run("coord-standby", coord)  # blocks on the lease until the first one exits
         self._run("node", [binary("everserve-node"), "--node", self.node, "--socket", self.daemon_socket,
                            "--coordinator", self.coord_socket, "--heartbeat-ms", str(self.heartbeat_ms),
                            "--ack-timeout-ms", str(self.ack_timeout_ms), "--mirror-socket", self.store_socket])

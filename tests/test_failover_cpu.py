@@ -158,3 +158,29 @@ def test_daemon_launched_spare_replays_startup_and_takes_over(tmp_path):
             assert len(ex.changes) == 1 and out == base
         finally:
             ex.shutdown()
+
+
+@pytest.mark.slow
+def test_coordinator_dies_mid_change_standby_finishes_it(tmp_path):
+    """The active coordinator logs the change to the spec store and dies before any node hears of
+    it; the standby takes the lease, reads the log, waits for the daemon to link again and
+    finishes the change. The streams stay token-identical."""
+    base, _, _, _ = _run(tmp_path / "nofault", spares=())
+    cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
+                       max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
+    with ControlPlane(str(tmp_path / "takeover"), engines=[{"name": "e0", "pipelineParallel": 2}], standby=True,
+                      coord_env={"EVERSERVE_COORD_EXIT_AFTER_LOG": "1"}) as cp:
+        ex = MultiprocExecutor(cfg, engine="e0", daemon=cp.daemon_socket, store=cp.store_socket, spares=(1,),
+                               node="n0", log_dir=str(tmp_path / "takeover" / "logs"), threads=2)
+        try:
+            cp.wait_spares("e0", 1)
+            eng = Engine(cfg, executor=ex)
+            eng.wrap_step(failover(ex, eng))
+            ex.kill_at_decode_step = (KILL_AT, 1)
+            out = eng.generate(_prompts(), max_tokens=TOKENS)
+            assert cp.procs["coord"].poll() == 17  # the first coordinator died after logging
+            assert "finishing it" in cp.log("coord-standby")
+            assert len(ex.changes) == 1 and out == base
+            assert cp.engine_view("e0")["status"]["epoch"] == 1
+        finally:
+            ex.shutdown()
