@@ -1,3 +1,6 @@
+#include <algorithm>
+#include <cctype>
+#include <cstdlib>
 #include "telemetry.h"
 
 #include <poll.h>
@@ -194,6 +197,66 @@ bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::strin
     }
   });
   return true;
+}
+
+static std::string dechunk(const std::string& b) {
+  std::string out;
+  size_t i = 0;
+  while (i < b.size()) {
+    const size_t le = b.find("\r\n", i);
+    if (le == std::string::npos) break;
+    const size_t n = std::strtoul(b.substr(i, le - i).c_str(), nullptr, 16);
+    if (n == 0) break;
+    out += b.substr(le + 2, n);
+    i = le + 2 + n + 2;
+  }
+  return out;
+}
+
+int http_request_ex(const std::string& addr, const std::string& method, const std::string& path,
+                    const std::vector<std::string>& headers, const std::string& body, std::string& out, int timeout_ms) {
+  Address a;
+  if (!Address::parse(addr, a)) return -1;
+  const int fd = connect_to(a, timeout_ms);
+  if (fd < 0) return -1;
+  std::string req = method + " " + path + " HTTP/1.1\r\nHost: " + a.host + "\r\nContent-Length: " +
+                    std::to_string(body.size()) + "\r\nConnection: close\r\n";
+  for (auto& h : headers) req += h + "\r\n";
+  req += "\r\n" + body;
+  const uint64_t deadline = now_ms() + (uint64_t)timeout_ms;
+  size_t off = 0;
+  while (off < req.size() && now_ms() < deadline) {
+    const ssize_t w = ::send(fd, req.data() + off, req.size() - off, MSG_NOSIGNAL);
+    if (w < 0) {
+      pollfd pf{fd, POLLOUT, 0};
+      ::poll(&pf, 1, 100);
+      continue;
+    }
+    off += size_t(w);
+  }
+  std::string resp;
+  char tmp[8192];
+  while (now_ms() < deadline) {
+    pollfd pf{fd, POLLIN, 0};
+    if (::poll(&pf, 1, (int)std::max<int64_t>(1, (int64_t)(deadline - now_ms()))) <= 0) break;
+    const ssize_t n = ::recv(fd, tmp, sizeof(tmp), 0);
+    if (n <= 0) break;
+    resp.append(tmp, size_t(n));
+  }
+  ::close(fd);
+  const auto sp = resp.find(' ');
+  if (sp == std::string::npos) return -1;
+  const int status = atoi(resp.c_str() + sp + 1);
+  const auto be = resp.find("\r\n\r\n");
+  if (be == std::string::npos) {
+    out.clear();
+    return status;
+  }
+  std::string head = resp.substr(0, be);
+  for (auto& c : head) c = (char)std::tolower((unsigned char)c);
+  out = resp.substr(be + 4);
+  if (head.find("transfer-encoding: chunked") != std::string::npos) out = dechunk(out);
+  return status;
 }
 
 int http_request(const std::string& addr, const std::string& method, const std::string& path, const std::string& body,

@@ -54,5 +54,10 @@ bool serve_http(Loop& loop, const std::string& addr, HttpRoute route = nullptr, 
 // A blocking HTTP request (used by the CLI); returns the status code, or -1.
 int http_request(const std::string& addr, const std::string& method, const std::string& path, const std::string& body,
                  std::string& out);
+// The same with extra request headers ("Name: value" lines) and a bound on the whole exchange;
+// chunked response bodies are decoded.
+int http_request_ex(const std::string& addr, const std::string& method, const std::string& path,
+                    const std::vector<std::string>& headers, const std::string& body, std::string& out,
+                    int timeout_ms = 2000);
 
 }  // namespace es

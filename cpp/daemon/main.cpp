@@ -29,6 +29,7 @@
 
 #include "everserve_pb.h"
 #include "net.h"
+#include "notice.h"
 #include "telemetry.h"
 #include "util.h"
 
@@ -647,6 +648,9 @@ int main(int argc, char** argv) {
   d.mirror_socket = env_or("EVERSERVE_MIRROR_SOCKET", "");
   std::string metrics_addr = env_or("EVERSERVE_METRICS_ADDR", "");
   std::string discovery = env_or("EVERSERVE_DISCOVERY_DIR", "");
+  std::string notice_source = env_or("EVERSERVE_NOTICE_SOURCE", "");
+  std::string notice_endpoint = env_or("EVERSERVE_NOTICE_ENDPOINT", "");
+  uint32_t notice_interval = 1000;
   for (int i = 1; i + 1 < argc; i += 2) {
     const std::string k = argv[i], v = argv[i + 1];
     if (k == "--node") d.node = v;
@@ -657,6 +661,9 @@ int main(int argc, char** argv) {
     else if (k == "--metrics-addr") metrics_addr = v;
     else if (k == "--mirror-socket") d.mirror_socket = v;
     else if (k == "--discovery-dir") discovery = v;
+    else if (k == "--notice-source") notice_source = v;
+    else if (k == "--notice-endpoint") notice_endpoint = v;
+    else if (k == "--notice-interval-ms") notice_interval = (uint32_t)std::stoul(v);
     else {
       fprintf(stderr, "unknown flag %s\n", k.c_str());
       return 2;
@@ -691,6 +698,26 @@ int main(int argc, char** argv) {
   d.link();
   d.loop.every(d.heartbeat_ms, [&] { d.tick(); });
   d.loop.every(100, [&] { d.supervise(); });
+  std::unique_ptr<NoticeWatcher> notices;
+  if (!notice_source.empty()) {
+    notices = std::make_unique<NoticeWatcher>(notice_source, notice_endpoint, d.node, notice_interval);
+    if (!notices->start(&err)) {
+      ES_ERROR("%s", err.c_str());
+      return 2;
+    }
+    d.loop.every(100, [&] {
+      NodeNoticeEvent ev;
+      if (!notices->take(ev)) return;
+      ES_WARN("node notice from %s: %s (deadline %lld)", ev.source.c_str(), ev.detail.c_str(), (long long)ev.deadline_ms);
+      coord::DaemonToCoord m;
+      m.has_node_notice = true;
+      m.node_notice.deadline_ms = ev.deadline_ms;
+      m.node_notice.reason = signals::Reason_REASON_NOTICE;
+      m.node_notice.source = ev.source;
+      m.node_notice.detail = ev.detail;
+      d.up(m);
+    });
+  }
   static Daemon* self = &d;
   signal(SIGTERM, [](int) {
     self->stop_spares();

@@ -60,7 +60,7 @@ class ControlPlane:
     def __init__(self, workdir: str, engines: list[dict] | None = None, node: str = "n0",
                  outcomes=("OUTCOME_REPLACE",), heartbeat_ms: int = 500, store_slots: int = 1 << 16,
                  store_budget: int = 8 << 30, ack_timeout_ms: int = 120000, cover: bool = True,
-                 standby: bool = False, coord_env: dict | None = None):
+                 standby: bool = False, coord_env: dict | None = None, node_args: list[str] | None = None):
         """`standby`: a second coordinator waits for the lease and takes over when the first
         exits. `coord_env`: extra environment of the first coordinator."""
         self.dir = os.path.abspath(workdir)
@@ -78,6 +78,7 @@ class ControlPlane:
         self.store_budget = store_budget
         self.ack_timeout_ms = ack_timeout_ms
         self.standby = standby
+        self.node_args = list(node_args or [])
         self.coord_env = coord_env or {}
         self.procs: dict[str, subprocess.Popen] = {}
         self._logs = []
@@ -104,7 +105,8 @@ class ControlPlane:
             self._run("coord-standby", coord)  # blocks on the lease until the first one exits
         self._run("node", [binary("everserve-node"), "--node", self.node, "--socket", self.daemon_socket,
                            "--coordinator", self.coord_socket, "--heartbeat-ms", str(self.heartbeat_ms),
-                           "--ack-timeout-ms", str(self.ack_timeout_ms), "--mirror-socket", self.store_socket])
+                           "--ack-timeout-ms", str(self.ack_timeout_ms), "--mirror-socket", self.store_socket]
+                  + self.node_args)
         wait_listening(self.store_socket)
         wait_listening(self.daemon_socket)
         wait_listening(self.api)
