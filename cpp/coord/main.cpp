@@ -81,10 +81,12 @@ struct Engine {
   // a change an earlier lease holder logged but did not commit: finished once its nodes link
   bool has_resume = false;
   spec::ChangeLog resume;
+  std::map<uint32_t, std::vector<std::string>> replicas;  // rank -> replica stores last asked for
 };
 
 struct Node {
   std::string name;
+  std::string replica_address;  // the node's store, for rows replicated to it
   uint64_t conn = 0;
   uint64_t last_seen_ms = 0;
   uint32_t heartbeat_ms = 500;
@@ -370,6 +372,7 @@ struct Coordinator {
     e.in_flight.reset();
     update_gauges();
     replan(e);
+    replicate(e);
     drive(e);  // losses that arrived during the change
   }
 
@@ -462,6 +465,34 @@ struct Coordinator {
     e.has_resume = false;
     e.down = false;
     start_delivery(e, std::move(f));
+  }
+
+  // ---- replication: each rank's rows also go to the stores of the nodes that may restore it ---
+  void replicate(Engine& e) {
+    auto ep = policy.engines.find(e.name);
+    for (auto& [r, h] : e.workers) {
+      std::set<std::string> target_nodes;
+      if (ep != policy.engines.end() && !ep->second.replica_nodes.empty()) {
+        for (auto& n : ep->second.replica_nodes) target_nodes.insert(n);
+      } else {
+        for (auto& sp : e.spares)  // the nodes whose spares may take this rank
+          if (sp.for_rank < 0 || sp.for_rank == (int64_t)r) target_nodes.insert(sp.node);
+      }
+      target_nodes.erase(h.node);
+      std::vector<std::string> targets;
+      for (auto& n : target_nodes) {
+        auto it = nodes.find(n);
+        if (it != nodes.end() && !it->second.replica_address.empty()) targets.push_back(it->second.replica_address);
+      }
+      if (e.replicas[r] == targets) continue;
+      e.replicas[r] = targets;
+      coord::CoordToDaemon m;
+      m.has_replicate_targets = true;
+      m.replicate_targets.engine = e.name;
+      m.replicate_targets.rank = r;
+      m.replicate_targets.targets = targets;
+      to_node(h.node, m);
+    }
   }
 
   // ---- spares the daemons launch ---------------------------------------------------------------
@@ -632,6 +663,7 @@ struct Coordinator {
     }
     update_gauges();
     replan(e);
+    replicate(e);
   }
 
   void from_daemon(Conn& c, const std::string& frame) {
@@ -652,6 +684,7 @@ struct Coordinator {
       n.linked = true;
       n.last_seen_ms = now_ms();
       n.heartbeat_ms = m.hello.heartbeat_ms ? m.hello.heartbeat_ms : 500;
+      n.replica_address = m.hello.mirror_replica_address;
       for (auto& st : m.hello.engines) {
         Engine& e = engine(st.engine);
         e.epoch = std::max(e.epoch, st.epoch);

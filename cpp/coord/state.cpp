@@ -60,6 +60,8 @@ bool parse_policy(const std::string& json, Policy& out, std::string& err) {
       if (const Json* sn = e.get("spareNodes"))
         for (auto& s : sn->arr) ep.spare_nodes.push_back(s.str);
       if (const Json* rb = e.get("releaseBoundMs")) ep.release_bound_ms = (int64_t)u32(rb, 0);
+      if (const Json* rn = e.get("replicaNodes"))
+        for (auto& n : rn->arr) ep.replica_nodes.push_back(n.str);
       if (const Json* sl = e.get("spares"))
         for (auto& x : sl->arr) {
           SpareSlotPolicy slot;

@@ -23,6 +23,7 @@ struct EnginePolicy {
   bool placement_independent = false;
   std::vector<std::string> spare_nodes;
   int64_t release_bound_ms = -1;
+  std::vector<std::string> replica_nodes;     // whose stores take the ranks' rows (empty: the spares' nodes)
   std::vector<SpareSlotPolicy> spare_slots;   // where the daemons launch this engine's spares
   std::vector<std::string> launch_command;    // how (empty: the engine launches its own)
   std::map<std::string, std::string> launch_env;

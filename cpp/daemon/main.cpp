@@ -28,6 +28,7 @@
 #include <set>
 
 #include "everserve_pb.h"
+#include "frame.h"
 #include "net.h"
 #include "notice.h"
 #include "telemetry.h"
@@ -87,6 +88,8 @@ struct Daemon {
   uint64_t backoff_ms = 100;
   std::mt19937_64 rng{std::random_device{}()};
   std::string socket;  // this daemon's process socket (handed to the spares it launches)
+  std::string replica_address;  // where this node's store takes replicated rows (announced in the hello)
+  std::map<std::string, std::vector<std::string>> replicate_sent;  // engine:rank -> targets told to the store
   std::map<std::string, Supervised> supervised;  // engine:device -> launched spare
 
   // ---- up: to the coordinator ------------------------------------------------------------------
@@ -118,6 +121,7 @@ struct Daemon {
     m.hello.protocol = signals::Protocol_PROTOCOL_VERSION;
     m.hello.protocol_oldest = signals::ProtocolOldest_PROTOCOL_OLDEST;
     m.hello.term = term;
+    m.hello.mirror_replica_address = replica_address;
     std::set<std::string> engines;
     for (auto& [id, p] : procs)
       if (p.registered) engines.insert(p.engine);
@@ -295,6 +299,8 @@ struct Daemon {
       }
     } else if (m.has_launch_spare) {
       launch_spare(m.launch_spare);
+    } else if (m.has_replicate_targets) {
+      replicate(m.replicate_targets);
     }
   }
 
@@ -544,6 +550,30 @@ struct Daemon {
                    p.said_goodbye ? "goodbye" : "connection ended");
   }
 
+  // ---- replication targets: the coordinator names which stores take a rank's rows --------------
+  void replicate(const coord::ReplicateTargets& t) {
+    if (mirror_socket.empty()) return;
+    const std::string key = t.engine + ":" + std::to_string(t.rank);
+    if (replicate_sent[key] == t.targets) return;
+    mirror::MirrorRequest req;
+    req.has_replicate = true;
+    req.replicate.engine = t.engine;
+    req.replicate.rank = t.rank;
+    req.replicate.targets = t.targets;
+    req.replicate.node = node;
+    Address a;
+    std::string err, reply;
+    int fd = -1;
+    if (Address::parse(mirror_socket, a)) fd = connect_to(a, 1000, &err);
+    if (fd < 0) {
+      ES_WARN("replication targets for %s: store unreachable (%s)", key.c_str(), err.c_str());
+      return;
+    }
+    if (write_frame(fd, req.serialize()) && read_frame(fd, reply, 2000)) replicate_sent[key] = t.targets;
+    ::close(fd);
+    ES_INFO("store of %s replicates %s to %zu target(s)", node.c_str(), key.c_str(), t.targets.size());
+  }
+
   // ---- spares launched for the coordinator -----------------------------------------------------
   void launch_spare(const coord::LaunchSpare& spec) {
     const std::string key = spec.engine + ":" + std::to_string(spec.device);
@@ -661,6 +691,7 @@ int main(int argc, char** argv) {
     else if (k == "--metrics-addr") metrics_addr = v;
     else if (k == "--mirror-socket") d.mirror_socket = v;
     else if (k == "--discovery-dir") discovery = v;
+    else if (k == "--replica-address") d.replica_address = v;
     else if (k == "--notice-source") notice_source = v;
     else if (k == "--notice-endpoint") notice_endpoint = v;
     else if (k == "--notice-interval-ms") notice_interval = (uint32_t)std::stoul(v);

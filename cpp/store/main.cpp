@@ -14,6 +14,7 @@
 #include <signal.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <condition_variable>
 #include <cstring>
 #include <deque>
@@ -163,7 +164,18 @@ void handle(Storage& st, Carrier& carrier, Loop& loop, Conn& c, const std::strin
     if (st.caught_up(req.caught_up)) rep.has_done = true;
     else err = "stale epoch";
   } else if (req.has_replicate) {
+    const auto before = st.replicas(req.replicate.engine, req.replicate.rank);
     st.set_replicas(req.replicate.engine, req.replicate.rank, req.replicate.targets);
+    // a new target first gets everything the rank has written (queued ahead of its next commits)
+    for (const auto& target : req.replicate.targets) {
+      if (std::find(before.begin(), before.end(), target) != before.end()) continue;
+      for (auto& part : st.snapshot_of(req.replicate.engine, req.replicate.rank, kMaxFrame - 4096)) {
+        mirror::MirrorRequest out;
+        out.has_replicated = true;
+        out.replicated = std::move(part);
+        carrier.push(target, out.serialize());
+      }
+    }
     rep.has_done = true;
   } else if (req.has_replicated) {
     if (st.apply_replicated(req.replicated, err)) {

@@ -324,6 +324,55 @@ std::vector<mirror::Replicated> Storage::replicated_of(const mirror::Commit& c, 
   return out;
 }
 
+std::vector<mirror::Replicated> Storage::snapshot_of(const std::string& engine, uint32_t rank,
+                                                     size_t max_bytes) const {
+  std::vector<mirror::Replicated> out;
+  auto e = engines_.find(engine);
+  if (e == engines_.end()) return out;
+  auto r = e->second.ranks.find(rank);
+  if (r == e->second.ranks.end()) return out;
+  auto fresh = [&]() {
+    mirror::Replicated m;
+    m.engine = engine;
+    m.rank = rank;
+    m.epoch = r->second.epoch;
+    m.step = r->second.step;
+    return m;
+  };
+  mirror::Replicated cur = fresh();
+  for (auto& [rid, n] : r->second.committed) {
+    cur.request_ids.push_back(rid);
+    cur.committed_tokens.push_back(n);
+  }
+  size_t bytes = 0;
+  for (auto& [id, t] : r->second.tables) {
+    mirror::ReplicatedTable rt;
+    rt.table = id;
+    rt.dtype = t.dtype;
+    rt.shape = t.shape;
+    const char* rows = static_cast<const char*>(t.rows->addr);
+    for (size_t s = 0; s < t.written_step.size(); s++) {
+      if (t.written_step[s] == 0) continue;
+      if (bytes + rt.data.size() + t.row_bytes > max_bytes && (!cur.tables.empty() || !rt.slots.empty())) {
+        if (!rt.slots.empty()) cur.tables.push_back(rt);
+        out.push_back(std::move(cur));
+        cur = fresh();
+        bytes = 0;
+        rt.slots.clear();
+        rt.data.clear();
+        rt.crc32c.clear();
+      }
+      rt.slots.push_back((int64_t)s);
+      rt.data.append(rows + s * t.row_bytes, t.row_bytes);
+      rt.crc32c.push_back(t.crc[s]);
+    }
+    bytes += rt.data.size();
+    if (!rt.slots.empty()) cur.tables.push_back(std::move(rt));
+  }
+  out.push_back(std::move(cur));
+  return out;
+}
+
 bool Storage::apply_replicated(const mirror::Replicated& m, std::string& err) {
   EngineState& eng = engines_[m.engine];
   RankState& r = eng.ranks[m.rank];

@@ -68,6 +68,9 @@ class Storage {
   // The rows a commit wrote, as replication messages of at most `max_bytes` each.
   std::vector<mirror::Replicated> replicated_of(const mirror::Commit& c, size_t max_bytes) const;
   bool apply_replicated(const mirror::Replicated& r, std::string& err);
+  // Every written row of a rank (and its committed counts), as replication messages: what a new
+  // replica needs before the rank's next commits reach it.
+  std::vector<mirror::Replicated> snapshot_of(const std::string& engine, uint32_t rank, size_t max_bytes) const;
   void set_replicas(const std::string& engine, uint32_t rank, const std::vector<std::string>& targets);
   std::vector<std::string> replicas(const std::string& engine, uint32_t rank) const;
   size_t in_use() const { return in_use_; }

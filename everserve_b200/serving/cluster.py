@@ -31,12 +31,19 @@ def binary(name: str) -> str:
     return path
 
 
+_handed: set[int] = set()
+
+
 def free_port() -> int:
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
+    """A loopback port no one listens on, never the same one twice in this process."""
+    while True:
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+        s.close()
+        if port not in _handed:
+            _handed.add(port)
+            return port
 
 
 def wait_listening(addr: str, timeout_s: float = 15.0) -> None:
@@ -57,7 +64,7 @@ def wait_listening(addr: str, timeout_s: float = 15.0) -> None:
 
 
 class ControlPlane:
-    def __init__(self, workdir: str, engines: list[dict] | None = None, node: str = "n0",
+    def __init__(self, workdir: str, engines: list[dict] | None = None, node: str = "n0", extra_nodes=(),
                  outcomes=("OUTCOME_REPLACE",), heartbeat_ms: int = 500, store_slots: int = 1 << 16,
                  store_budget: int = 8 << 30, ack_timeout_ms: int = 120000, cover: bool = True,
                  standby: bool = False, coord_env: dict | None = None, node_args: list[str] | None = None):
@@ -66,9 +73,13 @@ class ControlPlane:
         self.dir = os.path.abspath(workdir)
         os.makedirs(self.dir, exist_ok=True)
         self.node = node
+        self.nodes = [node] + list(extra_nodes)
         self.coord_socket = f"unix:{self.dir}/coord.sock"
-        self.daemon_socket = f"unix:{self.dir}/{node}.sock"
-        self.store_socket = f"unix:{self.dir}/store-{node}.sock"
+        self.daemon_sockets = {n: f"unix:{self.dir}/{n}.sock" for n in self.nodes}
+        self.store_sockets = {n: f"unix:{self.dir}/store-{n}.sock" for n in self.nodes}
+        self.replica_addrs = {n: f"127.0.0.1:{free_port()}" for n in self.nodes}
+        self.daemon_socket = self.daemon_sockets[node]
+        self.store_socket = self.store_sockets[node]
         self.api = f"127.0.0.1:{free_port()}"
         self.policy_path = os.path.join(self.dir, "policy.json")
         with open(self.policy_path, "w") as f:
@@ -93,9 +104,12 @@ class ControlPlane:
         self.procs[name] = subprocess.Popen(args, stdout=log, stderr=subprocess.STDOUT, env=e)
 
     def start(self) -> "ControlPlane":
-        self._run("store", [binary("everserve-store"), "--socket", self.store_socket, "--data-dir",
-                            os.path.join(self.dir, "store"), "--slots", str(self.store_slots), "--budget-bytes",
-                            str(self.store_budget)])
+        for n in self.nodes:
+            self._run("store" if n == self.node else f"store-{n}",
+                      [binary("everserve-store"), "--socket", self.store_sockets[n], "--data-dir",
+                       os.path.join(self.dir, "store" if n == self.node else f"store-{n}"), "--slots",
+                       str(self.store_slots), "--budget-bytes", str(self.store_budget), "--replica-listen",
+                       self.replica_addrs[n]])
         coord = [binary("everserve-coord"), "--listen", self.coord_socket, "--policy", self.policy_path,
                  "--spec-store", os.path.join(self.dir, "spec"), "--lease", os.path.join(self.dir, "lease"),
                  "--api-addr", self.api]
@@ -103,12 +117,15 @@ class ControlPlane:
         wait_listening(self.coord_socket)
         if self.standby:
             self._run("coord-standby", coord)  # blocks on the lease until the first one exits
-        self._run("node", [binary("everserve-node"), "--node", self.node, "--socket", self.daemon_socket,
-                           "--coordinator", self.coord_socket, "--heartbeat-ms", str(self.heartbeat_ms),
-                           "--ack-timeout-ms", str(self.ack_timeout_ms), "--mirror-socket", self.store_socket]
-                  + self.node_args)
-        wait_listening(self.store_socket)
-        wait_listening(self.daemon_socket)
+        for n in self.nodes:
+            self._run("node" if n == self.node else f"node-{n}",
+                      [binary("everserve-node"), "--node", n, "--socket", self.daemon_sockets[n],
+                       "--coordinator", self.coord_socket, "--heartbeat-ms", str(self.heartbeat_ms),
+                       "--ack-timeout-ms", str(self.ack_timeout_ms), "--mirror-socket", self.store_sockets[n],
+                       "--replica-address", self.replica_addrs[n]] + self.node_args)
+        for n in self.nodes:
+            wait_listening(self.store_sockets[n])
+            wait_listening(self.daemon_sockets[n])
         wait_listening(self.api)
         return self
 

@@ -84,7 +84,9 @@ class MultiprocExecutor:
                  spares: tuple[int, ...] = (), device: str = "cpu", dtype: str = "float32", node: str = "",
                  env: dict | None = None, threads: int = 0, step_timeout_s: float = 300.0,
                  change_timeout_s: float = 120.0, log_dir: str | None = None, start_timeout_s: float = 600.0,
-                 devices: list[int] | None = None):
+                 devices: list[int] | None = None, spare_places: list[dict] | None = None):
+        """`spare_places[i]`: where spare i runs when not on the head's node: its node's daemon
+        and store sockets and the node name ({"daemon": ..., "store": ..., "node": ...})."""
         self.cfg = cfg
         self.engine = engine
         self._closed = False
@@ -140,8 +142,12 @@ class MultiprocExecutor:
             self._spawn(f"rank{r}", base + ["--role", "worker", "--rank", str(r), "--row", str(r)] + dev_args(r), e)
         for i, r in enumerate(spares):
             row = self.layout.world + i
+            place = []
+            if spare_places and i < len(spare_places) and spare_places[i]:
+                sp = spare_places[i]
+                place = ["--daemon", sp["daemon"], "--store", sp["store"], "--node", sp["node"]]
             self._spawn(f"spare{i}-for{r}", base + ["--role", "spare", "--rank", str(r), "--row", str(row)]
-                        + dev_args(row), e)
+                        + dev_args(row) + place, e)
         self.links: dict[int, Link] = {}
         deadline = time.monotonic() + start_timeout_s
         while len(self.links) < self.layout.world:
@@ -364,6 +370,8 @@ class MultiprocExecutor:
         sch = engine.scheduler
         for req in sch.running:
             req.committed = min(int(c.get(req.req_id, 0)) for c in computed.values())
+        rec.coordinator["committed_tokens"] = sorted({req.committed for req in sch.running})
+        rec.coordinator["known_tokens"] = sorted({req.num_tokens for req in sch.running})
         sch.resume_from_committed()
         rec.t_resumed = time.monotonic()
         self.changes.append(rec)

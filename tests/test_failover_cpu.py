@@ -78,6 +78,7 @@ def test_sigkill_rank1_spare_takes_over_token_identical(tmp_path):
     assert rec["lost"] == [1] and rec["epoch"] == 1
     assert rec["from"] == "fault" and rec["resumed_ms"] is not None
     assert rec["coordinator"]["pre_formed_groups"] == [0, 1]  # the cover group was adopted
+    assert min(rec["coordinator"]["committed_tokens"]) > PROMPT  # resumed from restored decode rows
     assert mism == 0
     assert out == base, "streams differ from the no-fault run"
     assert all(len(o) == TOKENS for o in out)
@@ -182,5 +183,36 @@ def test_coordinator_dies_mid_change_standby_finishes_it(tmp_path):
             assert "finishing it" in cp.log("coord-standby")
             assert len(ex.changes) == 1 and out == base
             assert cp.engine_view("e0")["status"]["epoch"] == 1
+        finally:
+            ex.shutdown()
+
+
+@pytest.mark.slow
+def test_spare_on_another_node_restores_from_its_replica(tmp_path):
+    """Ranks on n0, the spare for rank 1 on n1 with its own daemon and store. The coordinator has
+    n0's store replicate rank 1's rows to n1's store (a snapshot, then every commit); after rank 1
+    is killed the spare restores from its own node's store and the streams stay identical."""
+    base, _, _, _ = _run(tmp_path / "nofault", spares=())
+    cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
+                       max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
+    with ControlPlane(str(tmp_path / "two"), engines=[{"name": "e0", "pipelineParallel": 2}],
+                      extra_nodes=["n1"]) as cp:
+        place = {"daemon": cp.daemon_sockets["n1"], "store": cp.store_sockets["n1"], "node": "n1"}
+        ex = MultiprocExecutor(cfg, engine="e0", daemon=cp.daemon_socket, store=cp.store_socket, spares=(1,),
+                               node="n0", log_dir=str(tmp_path / "two" / "logs"), threads=2, spare_places=[place])
+        try:
+            cp.wait_spares("e0", 1)
+            _wait_covered(cp, "e0")
+            eng = Engine(cfg, executor=ex)
+            eng.wrap_step(failover(ex, eng))
+            ex.kill_at_decode_step = (KILL_AT, 1)
+            out = eng.generate(_prompts(), max_tokens=TOKENS)
+            assert len(ex.changes) == 1 and out == base
+            # the spare resumed from rows it restored (decode positions), not from a re-prefill
+            committed = ex.changes[0].coordinator["committed_tokens"]
+            assert min(committed) > PROMPT, ex.changes[0].coordinator
+            view = cp.engine_view("e0")["status"]
+            assert {w["rank"]: w["node"] for w in view["workers"]} == {0: "n0", 1: "n1"}
+            assert "replicates e0:1" in cp.log("node")
         finally:
             ex.shutdown()
