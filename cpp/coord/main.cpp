@@ -99,6 +99,7 @@ struct Event {
   uint64_t seq;
   uint64_t at_ms;
   std::string text;
+  std::string engine;  // the engine it concerns ("" for node events)
 };
 
 struct Coordinator {
@@ -117,7 +118,9 @@ struct Coordinator {
   uint64_t event_seq = 0;
 
   void event(const std::string& text) {
-    events.push_back({++event_seq, now_ms(), text});
+    std::string eng;
+    if (text.rfind("engine ", 0) == 0) eng = text.substr(7, text.find(':') == std::string::npos ? 0 : text.find(':') - 7);
+    events.push_back({++event_seq, now_ms(), text, eng});
     if (events.size() > 4096) events.pop_front();
     ES_INFO("%s", text.c_str());
   }
@@ -825,6 +828,31 @@ struct Coordinator {
       first = false;
     }
     s += "]";
+    // conditions, as an operator reads them
+    const uint32_t world = e.world ? e.world : (uint32_t)e.workers.size();
+    size_t covered = 0, replacements = 0;
+    for (size_t i = 0; i < e.cover.sets.size(); i++) {
+      if (i < e.cover_covers.size() && !e.cover_covers[i].empty()) {
+        replacements++;
+        covered += set_covered(e, i);
+      }
+    }
+    auto cond = [](const std::string& type, bool status, const std::string& reason) {
+      return "{\"type\":\"" + type + "\",\"status\":\"" + (status ? "True" : "False") + "\",\"reason\":\"" +
+             json_escape(reason) + "\"}";
+    };
+    const bool ready = !e.down && !e.in_flight && e.workers.size() >= world && world > 0;
+    std::string conds = "[" +
+        cond("Ready", ready, e.down ? "a change was abandoned" : e.in_flight ? "a change is in flight"
+                                   : e.workers.size() < world ? "ranks missing" : "serving") + "," +
+        cond("Progressing", (bool)e.in_flight, e.in_flight ? "change to epoch " + std::to_string(e.in_flight->change.epoch) : "") + "," +
+        cond("Degraded", e.down || e.spares.empty(), e.down ? "engine down" : e.spares.empty() ? "no standing spare" : "") + "," +
+        cond("Covered", replacements > 0 && covered == replacements,
+             std::to_string(covered) + " of " + std::to_string(replacements) + " replacement sets formed") + "]";
+    for (auto& [type, st] : std::vector<std::pair<std::string, bool>>{
+             {"Ready", ready}, {"Progressing", (bool)e.in_flight}, {"Degraded", e.down || e.spares.empty()},
+             {"Covered", replacements > 0 && covered == replacements}})
+      metrics().set("everserve_engine_condition", {{"engine", e.name}, {"type", type}}, st ? 1 : 0);
     std::string cov = "{\"generation\":" + std::to_string(e.cover_gen) + ",\"sets\":[";
     for (size_t i = 0; i < e.cover.sets.size(); i++) {
       std::string ranks = "[";
@@ -837,7 +865,7 @@ struct Coordinator {
     cov += "]}";
     return "{\"metadata\":{\"name\":\"" + json_escape(e.name) + "\"},\"status\":{\"epoch\":" + std::to_string(e.epoch) +
            ",\"worldSize\":" + std::to_string(e.world) + ",\"down\":" + (e.down ? "true" : "false") +
-           ",\"changing\":" + (e.in_flight ? "true" : "false") + ",\"workers\":" + w + ",\"spares\":" + s + ",\"cover\":" + cov + "}}";
+           ",\"changing\":" + (e.in_flight ? "true" : "false") + ",\"workers\":" + w + ",\"spares\":" + s + ",\"cover\":" + cov + ",\"conditions\":" + conds + "}}";
   }
 
   bool api(const HttpRequest& req, HttpResponse& resp) {
@@ -888,6 +916,20 @@ struct Coordinator {
       resp.body = "{\"node\":\"" + json_escape(node) + "\",\"done\":\"" + verb + "\"}";
       return true;
     }
+    if (req.method == "GET" && path.rfind("/v1/engines/", 0) == 0 && path.size() > 7 &&
+        path.compare(path.size() - 7, 7, "/events") == 0) {
+      const std::string name = path.substr(12, path.size() - 12 - 7);
+      std::string o = "{\"engine\":\"" + json_escape(name) + "\",\"events\":[";
+      bool first = true;
+      for (auto& ev : events)
+        if (ev.engine == name) {
+          o += std::string(first ? "" : ",") + "{\"seq\":" + std::to_string(ev.seq) + ",\"atMs\":" +
+               std::to_string(ev.at_ms) + ",\"text\":\"" + json_escape(ev.text) + "\"}";
+          first = false;
+        }
+      resp.body = o + "]}";
+      return true;
+    }
     if (req.method == "GET" && path == "/v1/watch") {
       uint64_t since = 0;
       const auto q = req.path.find("since=");
@@ -919,7 +961,7 @@ struct Coordinator {
     if (req.method == "GET" && path == "/v1/openapi") {
       resp.body =
           "{\"openapi\":\"3.0.0\",\"info\":{\"title\":\"everserve coordinator\",\"version\":\"1\"},\"paths\":{"
-          "\"/v1/engines\":{\"get\":{}},\"/v1/engines/{name}\":{\"get\":{}},\"/v1/engines/{name}/stacks\":{\"post\":{}},"
+          "\"/v1/engines\":{\"get\":{}},\"/v1/engines/{name}\":{\"get\":{}},\"/v1/engines/{name}/events\":{\"get\":{}},\"/v1/engines/{name}/stacks\":{\"post\":{}},"
           "\"/v1/nodes\":{\"get\":{}},\"/v1/nodes/{name}/{cordon|uncordon|drain|undrain}\":{\"put\":{}},"
           "\"/v1/watch\":{\"get\":{}}}}";
       return true;
@@ -1013,6 +1055,7 @@ int main(int argc, char** argv) {
   metrics().describe("everserve_engine_down", "1 for an engine whose change was abandoned", "gauge");
   metrics().describe("everserve_spec_writes_total", "Writes to the spec store", "counter");
   metrics().describe("everserve_cover_plans_total", "Cover plans sent per engine", "counter");
+  metrics().describe("everserve_engine_condition", "1 when an engine condition (Ready, Progressing, Degraded, Covered) holds", "gauge");
   metrics().describe("everserve_engine_covered_sets", "Planned member sets whose groups every member formed", "gauge");
   metrics().describe("everserve_cover_form_seconds", "Time a member took to form a planned group", "histogram");
   metrics().describe("everserve_cover_failures_total", "Planned groups a member failed to form", "counter");

@@ -4,6 +4,7 @@
 //   everserve-ctl [--api host:port] watch [--since N] [--once]
 //   everserve-ctl [--api host:port] cordon|uncordon|drain|undrain NODE
 //   everserve-ctl [--api host:port] stacks ENGINE
+//   everserve-ctl [--api host:port] events ENGINE
 //   everserve-ctl [--api host:port] openapi
 //   everserve-ctl check [--policy FILE]
 // The API address also comes from EVERSERVE_API_ADDR. Subcommands follow the reference CLI's
@@ -26,6 +27,7 @@ static int usage() {
           "       everserve-ctl [--api ADDR] watch [--since N] [--once]\n"
           "       everserve-ctl [--api ADDR] cordon|uncordon|drain|undrain NODE\n"
           "       everserve-ctl [--api ADDR] stacks ENGINE\n"
+          "       everserve-ctl [--api ADDR] events ENGINE\n"
           "       everserve-ctl [--api ADDR] openapi\n"
           "       everserve-ctl check --policy FILE\n");
   return 2;
@@ -60,6 +62,10 @@ int main(int argc, char** argv) {
   if (verb == "cordon" || verb == "uncordon" || verb == "drain" || verb == "undrain") {
     if (args.size() < 2) return usage();
     return call(api, "PUT", "/v1/nodes/" + args[1] + "/" + verb);
+  }
+  if (verb == "events") {
+    if (args.size() < 2) return usage();
+    return call(api, "GET", "/v1/engines/" + args[1] + "/events");
   }
   if (verb == "stacks") {
     if (args.size() < 2) return usage();

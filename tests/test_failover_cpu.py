@@ -85,6 +85,8 @@ def test_sigkill_rank1_spare_takes_over_token_identical(tmp_path):
     # the coordinator's view: epoch 1, the spare holds rank 1, no spare left standing
     st = view["status"]
     assert st["epoch"] == 1 and not st["down"] and st["spares"] == []
+    conds = {c["type"]: c["status"] for c in st["conditions"]}
+    assert conds["Ready"] == "True" and conds["Progressing"] == "False" and conds["Degraded"] == "True"
     assert sorted(w["rank"] for w in st["workers"]) == [0, 1]
 
 
