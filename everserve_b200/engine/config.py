@@ -24,6 +24,7 @@ class EngineConfig:
     tensor_parallel: int = 1
     pipeline_parallel: int = 1
     use_cuda_graphs: bool = True
+    checkpoint: str | None = None  # a Hugging Face safetensors directory; None: random-init from `seed`
     extra: dict = field(default_factory=dict)
 
     def __post_init__(self):

@@ -24,7 +24,7 @@ def stage_layers(num_layers: int, pp: int, stage: int) -> tuple[int, int]:
 
 
 class Worker:
-    def __init__(self, cfg: EngineConfig, rank: int = 0, collective=None, pipe=None, device=None):
+    def __init__(self, cfg: EngineConfig, rank: int = 0, collective=None, pipe=None, device=None, weights=None):
         self.cfg = cfg
         self.rank = rank
         tp, pp = cfg.tensor_parallel, cfg.pipeline_parallel
@@ -37,7 +37,15 @@ class Worker:
             torch.cuda.set_device(self.device)
         self.tp = TPGroup(self.column, tp, collective)
         layers = stage_layers(cfg.model.layers, pp, self.stage)
-        self.model = DecoderLM(cfg.model, self.device, cfg.dtype, cfg.seed, self.tp, layers)
+        init = "none" if (cfg.checkpoint or weights is not None) else "random"
+        self.model = DecoderLM(cfg.model, self.device, cfg.dtype, cfg.seed, self.tp, layers, init=init)
+        if weights is not None:  # a resident copy (pinned host memory): copied in, no init
+            for k, t in weights.items():
+                self.model._put(k, t)
+        elif cfg.checkpoint:
+            from ..models.weights import load_hf_checkpoint
+
+            load_hf_checkpoint(self.model, cfg.checkpoint)
         self.num_blocks = cfg.num_blocks or self._auto_blocks()
         self.runner = ModelRunner(self.model, self.num_blocks, cfg.block_size, cfg.max_batch, cfg.max_model_len,
                                   cfg.use_cuda_graphs and pp == 1)

@@ -84,7 +84,8 @@ class MultiprocExecutor:
                  spares: tuple[int, ...] = (), device: str = "cpu", dtype: str = "float32", node: str = "",
                  env: dict | None = None, threads: int = 0, step_timeout_s: float = 300.0,
                  change_timeout_s: float = 120.0, log_dir: str | None = None, start_timeout_s: float = 600.0,
-                 devices: list[int] | None = None, spare_places: list[dict] | None = None):
+                 devices: list[int] | None = None, spare_places: list[dict] | None = None,
+                 resident_spares: bool = False):
         """`spare_places[i]`: where spare i runs when not on the head's node: its node's daemon
         and store sockets and the node name ({"daemon": ..., "store": ..., "node": ...})."""
         self.cfg = cfg
@@ -107,6 +108,8 @@ class MultiprocExecutor:
                 "--rdzv", self.rdzv_addr, "--head", self.carrier.address]
         if cfg.num_blocks:
             base += ["--num-blocks", str(cfg.num_blocks)]
+        if cfg.checkpoint:
+            base += ["--checkpoint", cfg.checkpoint]
         self._startup_args = list(base[3:])  # the engine's configuration, for spares a daemon launches
         if daemon:
             base += ["--daemon", daemon]
@@ -147,7 +150,7 @@ class MultiprocExecutor:
                 sp = spare_places[i]
                 place = ["--daemon", sp["daemon"], "--store", sp["store"], "--node", sp["node"]]
             self._spawn(f"spare{i}-for{r}", base + ["--role", "spare", "--rank", str(r), "--row", str(row)]
-                        + dev_args(row) + place, e)
+                        + dev_args(row) + place + (["--resident"] if resident_spares else []), e)
         self.links: dict[int, Link] = {}
         deadline = time.monotonic() + start_timeout_s
         while len(self.links) < self.layout.world:

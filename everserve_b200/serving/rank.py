@@ -78,7 +78,7 @@ class RankProcess:
         self.cfg = EngineConfig(model=a.model, device=str(dev), dtype=_DTYPES[a.dtype], seed=a.seed,
                                 block_size=a.block_size, num_blocks=a.num_blocks, max_batch=a.max_batch,
                                 max_model_len=a.max_model_len, tensor_parallel=a.tp, pipeline_parallel=a.pp,
-                                use_cuda_graphs=False)
+                                use_cuda_graphs=False, checkpoint=a.checkpoint)
         self.runtime = Runtime(self.rank)
         self.rdzv = _store(a.rdzv)
         self.groups = SwappableGroups(self.rdzv, self.rank, self.layout, dev, timeout_s=a.group_timeout)
@@ -96,14 +96,15 @@ class RankProcess:
             coll = GroupCollective(self.groups)
         self.collective = coll
         t0 = time.monotonic()
-        self.worker = Worker(self.cfg, rank=self.rank, collective=coll, pipe=self.exchange, device=str(dev))
-        self.caches = self.worker.runner.caches
-        hkv = max(1, mc.kv_heads // a.tp)
-        self.kv = PagedKV("heads_blocked", self.worker.num_blocks, a.block_size, hkv, mc.head_dim)
+        self.worker = None
         self.ckv = None
-        if a.store:
-            self.ckv = MirrorCommittedKV(MirrorClient(a.store), self.engine, self.rank, self.caches, self.kv,
-                                         store_slots=self.worker.num_blocks * a.block_size)
+        self.host_weights = None
+        if self.spare and a.resident and dev.type == "cuda":
+            # a resident spare holds its shard in pinned host memory and no device memory while it
+            # stands; the shard is copied to the device when it takes the rank
+            self.host_weights = self._host_shard(coll)
+        else:
+            self._build_worker(coll)
         self.load_s = time.monotonic() - t0
         self.computed: dict[str, int] = {}
         self._commits: list[int] = []
@@ -127,6 +128,25 @@ class RankProcess:
             self.daemon = DaemonConnection(a.daemon, self.engine, self, role=sp.ROLE_SPARE if self.spare else sp.ROLE_WORKER,
                                            stage=[self.layout.stage(self.rank)], node=a.node,
                                            identity=identity(self.cfg, self.engine))
+
+    def _build_worker(self, coll=None, weights=None) -> None:
+        a, mc = self.a, self.cfg.model
+        self.worker = Worker(self.cfg, rank=self.rank, collective=coll if coll is not None else self.collective,
+                             pipe=self.exchange, device=str(self.device), weights=weights)
+        self.caches = self.worker.runner.caches
+        hkv = max(1, mc.kv_heads // a.tp)
+        self.kv = PagedKV("heads_blocked", self.worker.num_blocks, a.block_size, hkv, mc.head_dim)
+        if a.store:
+            self.ckv = MirrorCommittedKV(MirrorClient(a.store), self.engine, self.rank, self.caches, self.kv,
+                                         store_slots=self.worker.num_blocks * a.block_size)
+
+    def _host_shard(self, coll) -> dict:
+        """The rank's weights in pinned host memory (made on the device, then moved off it)."""
+        w = Worker(self.cfg, rank=self.rank, collective=coll, pipe=self.exchange, device=str(self.device))
+        host = {k: t.to("cpu").pin_memory() for k, t in w.model.weights.items()}
+        del w
+        torch.cuda.empty_cache()
+        return host
 
     # ---- the peer-memory tensor-parallel collective (GPUs) ----------------------------------------
     def _stage_rows(self) -> list[int]:
@@ -206,6 +226,11 @@ class RankProcess:
             if not takes:
                 return None
             try:
+                if self.worker is None:  # a resident spare: its shard goes to the device now
+                    t_copy = time.monotonic()
+                    self._build_worker(weights=self.host_weights)
+                    self.host_weights = None
+                    self.runtime.trace("resident shard copied", seconds=time.monotonic() - t_copy)
                 counts = self.ckv.restore(self.rank) if self.ckv is not None else {}
             except Exception as e:  # noqa: BLE001 - reported in the ack
                 return f"restore failed: {e}"
@@ -261,7 +286,7 @@ class RankProcess:
         """One forward of a dummy step so the first real step pays no lazy set-up."""
         from ..engine.scheduler import ScheduledReq, StepPlan
 
-        if self.layout.world > 1:
+        if self.layout.world > 1 or self.worker is None:
             return  # a lone forward of a middle stage has no peer; warm-up happens on the first step
         plan = StepPlan(0, False, [ScheduledReq("warm", [1], 0, [0], True)])
         self.worker.execute(plan)
@@ -420,6 +445,9 @@ def parse(argv=None) -> argparse.Namespace:
     p.add_argument("--region", default="", help="slot region name (GPU tensor parallelism)")
     p.add_argument("--row", type=int, default=None, help="this process's row in the slot region")
     p.add_argument("--threads", type=int, default=0)
+    p.add_argument("--checkpoint", default=None, help="Hugging Face safetensors directory (default: random init)")
+    p.add_argument("--resident", action="store_true",
+                   help="a spare keeps its shard in pinned host memory until it takes a rank (GPUs)")
     return p.parse_args(argv)
 
 
