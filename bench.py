@@ -6,7 +6,7 @@ For N > 1 launch one process per GPU:
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N --steps K --warmup W
 
-Workload: 64 concurrent streams, 1024-token uniform-random prompts (seed 0),
+Workload (the Llama-3-8B serving configuration): 64 concurrent streams, 1024-token uniform-random prompts (seed 0),
 greedy decoding, random-init bf16 weights of the Llama-3-8B architecture, tensor-parallel over the
 N GPUs. All 64 prompts are prefilled first (untimed); then W warm-up decode steps; then:
 

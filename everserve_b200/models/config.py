@@ -1,8 +1,8 @@
-"""Model architectures the engine serves, with the shapes the BASELINE configurations name.
+"""Model architectures the engine serves, with the shapes of the benchmark configurations.
 
 Every model is a pre-norm decoder (RMSNorm, RoPE, GQA attention, SwiGLU MLP or a top-k softmax
 mixture of SwiGLU experts). Weights are random-initialised from a seed (no checkpoints are
-available offline); ``load_safetensors`` in :mod:`everserve_b200.models.weights` reads real ones.
+available offline); ``load_hf_checkpoint`` in :mod:`everserve_b200.models.weights` reads real ones.
 """
 
 from __future__ import annotations

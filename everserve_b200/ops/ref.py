@@ -1,6 +1,6 @@
 """PyTorch reference implementations of every decoder op.
 
-These are the arithmetic of the CPU engine (fp32 on CPU, the reference tier and the BASELINE's
+These are the arithmetic of the CPU engine (fp32 on CPU, the reference tier and the
 CPU/gloo configuration) and the numerical oracle of the sm_100a kernels: each kernel's test
 compares against the function here evaluated in fp32.
 

@@ -1,4 +1,4 @@
-"""Collective microbenchmark on the GPUs of one node, one process per GPU.
+"""Collective microbenchmark (the failure-detecting all-reduce configuration) on the GPUs of one node, one process per GPU.
 
     python -m torch.distributed.run --nproc-per-node N -m everserve_b200.perf.collectives [--sizes ...]
 
