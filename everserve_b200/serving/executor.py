@@ -85,9 +85,11 @@ class MultiprocExecutor:
                  env: dict | None = None, threads: int = 0, step_timeout_s: float = 300.0,
                  change_timeout_s: float = 120.0, log_dir: str | None = None, start_timeout_s: float = 600.0,
                  devices: list[int] | None = None, spare_places: list[dict] | None = None,
-                 resident_spares: bool = False):
+                 resident_spares: bool = False, local_ranks: list[int] | None = None):
         """`spare_places[i]`: where spare i runs when not on the head's node: its node's daemon
-        and store sockets and the node name ({"daemon": ..., "store": ..., "node": ...})."""
+        and store sockets and the node name ({"daemon": ..., "store": ..., "node": ...}).
+        `local_ranks`: the ranks this head starts itself (default: all); node agents
+        (``everserve_b200.serving.node``) start the others on their nodes."""
         self.cfg = cfg
         self.engine = engine
         self._closed = False
@@ -141,7 +143,16 @@ class MultiprocExecutor:
                 return []
             return ["--device", f"cuda:{(devices or list(range(64)))[i]}"]
 
-        for r in range(self.layout.world):
+        # the head's daemon link first: ranks that node agents start elsewhere ask it for the
+        # engine's start-up record before they can link
+        self.client = DaemonClient(daemon, engine, node=node) if daemon else None
+        self._next_row = self.layout.world + len(spares)
+        if self.client is not None:
+            import threading
+
+            threading.Thread(target=self._answer_replays, name="replay-offers", daemon=True).start()
+        self.local_ranks = list(range(self.layout.world)) if local_ranks is None else list(local_ranks)
+        for r in self.local_ranks:
             self._spawn(f"rank{r}", base + ["--role", "worker", "--rank", str(r), "--row", str(r)] + dev_args(r), e)
         for i, r in enumerate(spares):
             row = self.layout.world + i
@@ -165,12 +176,6 @@ class MultiprocExecutor:
         self.num_blocks = min(link.hello["num_blocks"] for link in self.links.values())
         self.epoch = 0
         self._boundary(0)
-        self.client = DaemonClient(daemon, engine, node=node) if daemon else None
-        self._next_row = self.layout.world + len(spares)
-        if self.client is not None:
-            import threading
-
-            threading.Thread(target=self._answer_replays, name="replay-offers", daemon=True).start()
         self.changes: list[ChangeRecord] = []
         self.decode_steps_run = 0
         self.kill_at_decode_step: tuple[int, int] | None = None  # (decode step, rank): host-side fault injection
@@ -313,7 +318,8 @@ class MultiprocExecutor:
             if self.region is not None:
                 row = self._next_row
                 self._next_row += 1
-            rec = {"args": self._startup_args, "row": row, "gpu": self.gpu, "world": self.layout.world}
+            rec = {"args": self._startup_args, "row": row, "gpu": self.gpu, "world": self.layout.world,
+                   "token": self.token}
             try:
                 self.client.offer_replay(ask, json.dumps(rec))
             except OSError:

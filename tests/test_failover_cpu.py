@@ -218,3 +218,31 @@ def test_spare_on_another_node_restores_from_its_replica(tmp_path):
             assert "replicates e0:1" in cp.log("node")
         finally:
             ex.shutdown()
+
+
+@pytest.mark.slow
+def test_node_agent_starts_remote_ranks(tmp_path):
+    """The head starts rank 0 on n0; a node agent on n1 fetches the start-up record through the
+    control plane and starts rank 1 there. The two-node engine serves the same tokens."""
+    import subprocess
+    import sys
+
+    base, _, _, _ = _run(tmp_path / "nofault", spares=())
+    cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
+                       max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
+    with ControlPlane(str(tmp_path / "agents"), engines=[{"name": "e0", "pipelineParallel": 2}],
+                      extra_nodes=["n1"]) as cp:
+        env = dict(os.environ, EVERSERVE_SOCKET=cp.daemon_sockets["n1"], EVERSERVE_MIRROR_SOCKET=cp.store_sockets["n1"],
+                   EVERSERVE_NODE="n1", PYTHONPATH=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        agent = subprocess.Popen([sys.executable, "-m", "everserve_b200.serving.node", "--engine", "e0", "--ranks", "1",
+                                  "--threads", "2"], env=env)
+        ex = MultiprocExecutor(cfg, engine="e0", daemon=cp.daemon_socket, store=cp.store_socket, spares=(),
+                               node="n0", log_dir=str(tmp_path / "agents" / "logs"), threads=2, local_ranks=[0])
+        try:
+            out = Engine(cfg, executor=ex).generate(_prompts(), max_tokens=TOKENS)
+            assert out == base
+            view = cp.engine_view("e0")["status"]
+            assert {w["rank"]: w["node"] for w in view["workers"]} == {0: "n0", 1: "n1"}
+        finally:
+            ex.shutdown()
+            assert agent.wait(timeout=60) == 0
