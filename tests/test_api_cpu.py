@@ -1,0 +1,35 @@
+"""The completions server over a CPU engine: plain and streamed completions equal Engine.generate."""
+
+import json
+
+import torch
+from fastapi.testclient import TestClient
+
+from everserve_b200.engine.config import EngineConfig
+from everserve_b200.engine.engine import Engine
+from everserve_b200.serving.api import EngineLoop, build_app
+
+
+def _cfg():
+    return EngineConfig("tiny-llama", device="cpu", dtype=torch.float32, num_blocks=64, max_batch=8, max_model_len=128)
+
+
+def test_completions_match_generate():
+    want = Engine(_cfg()).generate([[5, 6, 7], [1, 2]], max_tokens=5)
+    loop = EngineLoop(Engine(_cfg()))
+    try:
+        c = TestClient(build_app(loop, "tiny-llama", 512))
+        assert c.get("/ready").json()["ready"]
+        r = c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 5}).json()
+        assert r["choices"][0]["token_ids"] == want[0]
+        assert r["usage"]["completion_tokens"] == 5
+        with c.stream("POST", "/v1/completions", json={"prompt": [1, 2], "max_tokens": 5, "stream": True}) as s:
+            lines = [ln for ln in s.iter_lines() if ln.startswith("data: ")]
+        assert lines[-1] == "data: [DONE]"
+        toks = [json.loads(ln[6:])["choices"][0]["token_ids"][0] for ln in lines[:-1]]
+        assert toks == want[1]
+        assert c.get("/v1/models").json()["data"][0]["id"] == "tiny-llama"
+        r = c.post("/v1/completions", json={"prompt": "hi", "max_tokens": 2}).json()
+        assert len(r["choices"][0]["token_ids"]) == 2
+    finally:
+        loop.close()
