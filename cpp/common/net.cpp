@@ -1,4 +1,5 @@
 #include "net.h"
+#include "tls.h"
 
 #include <arpa/inet.h>
 #include <errno.h>
@@ -148,7 +149,7 @@ int connect_to(const Address& a, int timeout_ms, std::string* err) {
 bool Loop::listen(const Address& a, AcceptFn on_accept, std::string* err) {
   const int fd = listen_on(a, err);
   if (fd < 0) return false;
-  listeners_.push_back({fd, std::move(on_accept)});
+  listeners_.push_back({fd, std::move(on_accept), !a.unix_socket});
   return true;
 }
 
@@ -158,9 +159,32 @@ Conn* Loop::adopt(int fd, const std::string& peer) {
   c->id = next_id_++;
   c->fd = fd;
   c->peer = peer;
+  sockaddr_storage ss{};
+  socklen_t sl = sizeof(ss);
+  if (tls::enabled() && getsockname(fd, (sockaddr*)&ss, &sl) == 0 && ss.ss_family == AF_INET) {
+    c->ssl = tls::new_client(fd);  // an outgoing TCP link: it speaks first
+    c->handshaking = true;
+    c->hs_want_write = true;
+  }
   Conn* raw = c.get();
   conns_[raw->id] = std::move(c);
   return raw;
+}
+
+void Loop::progress_handshake(Conn& c) {
+  bool ww = false;
+  const int r = tls::handshake(c.ssl, &ww);
+  if (r == 1) {
+    c.handshaking = false;
+    c.peer_cn = tls::peer_name(c.ssl);
+    flush_conn(c);
+    read_conn(c);  // data that came with the last handshake message is already in the session
+  } else if (r == 0) {
+    c.hs_want_write = ww;
+  } else {
+    c.closing = true;
+    c.out.clear();
+  }
 }
 
 Conn* Loop::conn(uint64_t id) {
@@ -195,6 +219,20 @@ void Loop::cancel(uint64_t timer) {
 void Loop::watch(int fd, std::function<void()> on_readable) { watched_[fd] = std::move(on_readable); }
 
 void Loop::flush_conn(Conn& c) {
+  if (c.ssl) {
+    if (c.handshaking) return;  // queued until the session is up
+    while (!c.out.empty()) {
+      const long w = tls::write(c.ssl, c.out.data(), c.out.size());
+      if (w == -1) return;
+      if (w < 0) {
+        c.closing = true;
+        c.out.clear();
+        return;
+      }
+      c.out.erase(0, size_t(w));
+    }
+    return;
+  }
   while (!c.out.empty()) {
     const ssize_t w = ::send(c.fd, c.out.data(), c.out.size(), MSG_NOSIGNAL);
     if (w < 0) {
@@ -209,8 +247,23 @@ void Loop::flush_conn(Conn& c) {
 
 void Loop::read_conn(Conn& c) {
   char buf[65536];
+  if (c.ssl && c.handshaking) {
+    progress_handshake(c);
+    return;
+  }
   while (true) {
-    const ssize_t n = ::recv(c.fd, buf, sizeof(buf), 0);
+    ssize_t n;
+    if (c.ssl) {
+      const long r = tls::read(c.ssl, buf, sizeof(buf));
+      if (r == -1) break;
+      n = r == -2 ? -1 : r;
+      if (n < 0) {
+        c.closing = true;
+        break;
+      }
+    } else {
+      n = ::recv(c.fd, buf, sizeof(buf), 0);
+    }
     if (n < 0) {
       if (errno == EAGAIN || errno == EINTR) break;
       c.closing = true;
@@ -239,6 +292,7 @@ void Loop::drop(uint64_t id) {
   std::unique_ptr<Conn> c = std::move(it->second);
   conns_.erase(it);
   if (c->on_close) c->on_close(*c);
+  tls::free_session(c->ssl);
   ::close(c->fd);
 }
 
@@ -251,7 +305,8 @@ void Loop::run() {
     std::vector<uint64_t> ids;
     for (auto& kv : conns_) {
       short ev = POLLIN;
-      if (!kv.second->out.empty()) ev |= POLLOUT;
+      if (kv.second->handshaking) ev = kv.second->hs_want_write ? POLLOUT : POLLIN;
+      else if (!kv.second->out.empty()) ev |= POLLOUT;
       pfds.push_back({kv.second->fd, ev, 0});
       ids.push_back(kv.first);
     }
@@ -266,6 +321,16 @@ void Loop::run() {
           const int fd = ::accept4(listeners_[i].fd, nullptr, nullptr, SOCK_CLOEXEC);
           if (fd < 0) break;
           Conn* c = adopt(fd, "accepted");
+          if (c->ssl) {  // adopt took an accepted socket for an outgoing one
+            tls::free_session(c->ssl);
+            c->ssl = nullptr;
+            c->handshaking = false;
+          }
+          if (listeners_[i].tcp && tls::enabled()) {
+            c->ssl = tls::new_server(fd);
+            c->handshaking = true;
+            c->hs_want_write = false;
+          }
           listeners_[i].on_accept(*c);
         }
       }
@@ -285,6 +350,10 @@ void Loop::run() {
       Conn* c = conn(ids[j]);
       if (c == nullptr) continue;
       const short re = pfds[i + j].revents;
+      if (c->handshaking) {
+        if (re & (POLLIN | POLLOUT | POLLHUP | POLLERR)) progress_handshake(*c);
+        continue;
+      }
       if (re & (POLLIN | POLLHUP | POLLERR)) read_conn(*c);
       c = conn(ids[j]);
       if (c != nullptr && (re & POLLOUT)) flush_conn(*c);

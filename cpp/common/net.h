@@ -43,6 +43,12 @@ struct Conn {
   std::function<void(Conn&, const std::string&)> on_frame;
   std::function<void(Conn&)> on_close;
   void* user = nullptr;  // handler state (owned by the handler)
+  // TCP links when TLS is configured (tls.h): the session, its handshake state, and the peer's
+  // certificate name once the handshake is done
+  void* ssl = nullptr;
+  bool handshaking = false;
+  bool hs_want_write = false;
+  std::string peer_cn;
 };
 
 class Loop {
@@ -68,7 +74,9 @@ class Loop {
   struct Listener {
     int fd;
     AcceptFn on_accept;
+    bool tcp;
   };
+  void progress_handshake(Conn& c);
   struct Timer {
     uint64_t id, due, period;
     bool repeat;

@@ -2,6 +2,7 @@
 #include <cctype>
 #include <cstdlib>
 #include "telemetry.h"
+#include "tls.h"
 
 #include <poll.h>
 #include <sys/socket.h>
@@ -106,14 +107,12 @@ std::string Registry::exposition() const {
   return o;
 }
 
-static bool read_request(int fd, HttpRequest& req) {
+static bool read_request(tls::Stream& st, HttpRequest& req) {
   std::string buf;
   char tmp[8192];
   size_t header_end = std::string::npos;
   while (header_end == std::string::npos) {
-    pollfd pf{fd, POLLIN, 0};
-    if (::poll(&pf, 1, 2000) <= 0) return false;
-    const ssize_t n = ::recv(fd, tmp, sizeof(tmp), 0);
+    const long n = st.read_some(tmp, sizeof(tmp), 2000);
     if (n <= 0) return false;
     buf.append(tmp, size_t(n));
     header_end = buf.find("\r\n\r\n");
@@ -137,9 +136,7 @@ static bool read_request(int fd, HttpRequest& req) {
   }
   req.body = buf.substr(header_end + 4);
   while (req.body.size() < content_len) {
-    pollfd pf{fd, POLLIN, 0};
-    if (::poll(&pf, 1, 2000) <= 0) return false;
-    const ssize_t n = ::recv(fd, tmp, sizeof(tmp), 0);
+    const long n = st.read_some(tmp, sizeof(tmp), 2000);
     if (n <= 0) return false;
     req.body.append(tmp, size_t(n));
   }
@@ -169,10 +166,13 @@ bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::strin
     while (true) {
       const int fd = ::accept4(lfd, nullptr, nullptr, SOCK_CLOEXEC);
       if (fd < 0) return;
+      tls::Stream st;
+      std::string terr;
+      if (!tls::accept_stream(fd, 2000, st, &terr)) continue;  // HTTPS when TLS is configured
       HttpRequest req;
       HttpResponse resp;
-      if (!read_request(fd, req)) {
-        ::close(fd);
+      if (!read_request(st, req)) {
+        st.close();
         continue;
       }
       const std::string path = req.path.substr(0, req.path.find('?'));
@@ -187,13 +187,8 @@ bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::strin
       std::string out = "HTTP/1.1 " + std::to_string(resp.status) + " " + reason(resp.status) +
                         "\r\nContent-Type: " + resp.content_type + "\r\nContent-Length: " + std::to_string(resp.body.size()) +
                         "\r\nConnection: close\r\n\r\n" + resp.body;
-      size_t off = 0;
-      while (off < out.size()) {
-        const ssize_t w = ::send(fd, out.data() + off, out.size() - off, MSG_NOSIGNAL);
-        if (w <= 0) break;
-        off += size_t(w);
-      }
-      ::close(fd);
+      st.write_all(out, 2000);
+      st.close();
     }
   });
   return true;
@@ -217,33 +212,25 @@ int http_request_ex(const std::string& addr, const std::string& method, const st
                     const std::vector<std::string>& headers, const std::string& body, std::string& out, int timeout_ms) {
   Address a;
   if (!Address::parse(addr, a)) return -1;
-  const int fd = connect_to(a, timeout_ms);
-  if (fd < 0) return -1;
+  tls::Stream st;
+  if (!tls::connect_stream(a, timeout_ms, st, nullptr)) return -1;
   std::string req = method + " " + path + " HTTP/1.1\r\nHost: " + a.host + "\r\nContent-Length: " +
                     std::to_string(body.size()) + "\r\nConnection: close\r\n";
   for (auto& h : headers) req += h + "\r\n";
   req += "\r\n" + body;
   const uint64_t deadline = now_ms() + (uint64_t)timeout_ms;
-  size_t off = 0;
-  while (off < req.size() && now_ms() < deadline) {
-    const ssize_t w = ::send(fd, req.data() + off, req.size() - off, MSG_NOSIGNAL);
-    if (w < 0) {
-      pollfd pf{fd, POLLOUT, 0};
-      ::poll(&pf, 1, 100);
-      continue;
-    }
-    off += size_t(w);
+  if (!st.write_all(req, timeout_ms)) {
+    st.close();
+    return -1;
   }
   std::string resp;
   char tmp[8192];
   while (now_ms() < deadline) {
-    pollfd pf{fd, POLLIN, 0};
-    if (::poll(&pf, 1, (int)std::max<int64_t>(1, (int64_t)(deadline - now_ms()))) <= 0) break;
-    const ssize_t n = ::recv(fd, tmp, sizeof(tmp), 0);
+    const long n = st.read_some(tmp, sizeof(tmp), (int)std::max<int64_t>(1, (int64_t)(deadline - now_ms())));
     if (n <= 0) break;
     resp.append(tmp, size_t(n));
   }
-  ::close(fd);
+  st.close();
   const auto sp = resp.find(' ');
   if (sp == std::string::npos) return -1;
   const int status = atoi(resp.c_str() + sp + 1);
@@ -261,38 +248,7 @@ int http_request_ex(const std::string& addr, const std::string& method, const st
 
 int http_request(const std::string& addr, const std::string& method, const std::string& path, const std::string& body,
                  std::string& out) {
-  Address a;
-  if (!Address::parse(addr, a)) return -1;
-  const int fd = connect_to(a, 3000);
-  if (fd < 0) return -1;
-  std::string req = method + " " + path + " HTTP/1.1\r\nHost: " + a.host + "\r\nContent-Length: " +
-                    std::to_string(body.size()) + "\r\nConnection: close\r\n\r\n" + body;
-  size_t off = 0;
-  while (off < req.size()) {
-    const ssize_t w = ::send(fd, req.data() + off, req.size() - off, MSG_NOSIGNAL);
-    if (w < 0) {
-      pollfd pf{fd, POLLOUT, 0};
-      ::poll(&pf, 1, 1000);
-      continue;
-    }
-    off += size_t(w);
-  }
-  std::string resp;
-  char tmp[8192];
-  while (true) {
-    pollfd pf{fd, POLLIN, 0};
-    if (::poll(&pf, 1, 5000) <= 0) break;
-    const ssize_t n = ::recv(fd, tmp, sizeof(tmp), 0);
-    if (n <= 0) break;
-    resp.append(tmp, size_t(n));
-  }
-  ::close(fd);
-  const auto sp = resp.find(' ');
-  if (sp == std::string::npos) return -1;
-  const int status = atoi(resp.c_str() + sp + 1);
-  const auto be = resp.find("\r\n\r\n");
-  out = be == std::string::npos ? "" : resp.substr(be + 4);
-  return status;
+  return http_request_ex(addr, method, path, {}, body, out, 8000);
 }
 
 }  // namespace es

@@ -34,6 +34,7 @@
 #include "net.h"
 #include "state.h"
 #include "telemetry.h"
+#include "tls.h"
 #include "util.h"
 
 using namespace es;
@@ -679,6 +680,13 @@ struct Coordinator {
         loop.close(c.id);
         return;
       }
+      if (!c.peer_cn.empty() && c.peer_cn != m.hello.node) {
+        ES_WARN("a daemon with the certificate of %s said it is node %s: refused", c.peer_cn.c_str(),
+                m.hello.node.c_str());
+        metrics().inc("everserve_refused_links_total");
+        loop.close(c.id);
+        return;
+      }
       node = m.hello.node;
       conn_node[c.id] = node;
       Node& n = nodes[node];
@@ -1004,6 +1012,13 @@ bool take_lease(const std::string& path, uint64_t& term, std::string& err) {
 }  // namespace
 
 int main(int argc, char** argv) {
+  {
+    std::string terr;
+    if (!es::tls::configure_from_env(&terr)) {
+      fprintf(stderr, "TLS: %s\n", terr.c_str());
+      return 2;
+    }
+  }
   log_init("coord");
   signal(SIGPIPE, SIG_IGN);
   Coordinator co;

@@ -7,6 +7,7 @@
 //   everserve-ctl [--api host:port] events ENGINE
 //   everserve-ctl [--api host:port] openapi
 //   everserve-ctl check [--policy FILE]
+//   everserve-ctl certs init DIR | certs issue DIR NAME   (the cluster CA and per-process certificates)
 // The API address also comes from EVERSERVE_API_ADDR. Subcommands follow the reference CLI's
 // operator verbs (controller/src/cli/*.rs; controller/README.md:100-115).
 #include <unistd.h>
@@ -17,6 +18,7 @@
 
 #include "../coord/state.h"
 #include "telemetry.h"
+#include "tls.h"
 #include "util.h"
 
 using namespace es;
@@ -29,7 +31,8 @@ static int usage() {
           "       everserve-ctl [--api ADDR] stacks ENGINE\n"
           "       everserve-ctl [--api ADDR] events ENGINE\n"
           "       everserve-ctl [--api ADDR] openapi\n"
-          "       everserve-ctl check --policy FILE\n");
+          "       everserve-ctl check --policy FILE\n"
+          "       everserve-ctl certs init DIR [--days N] | certs issue DIR NAME [--days N]\n");
   return 2;
 }
 
@@ -45,6 +48,13 @@ static int call(const std::string& api, const std::string& method, const std::st
 }
 
 int main(int argc, char** argv) {
+  {
+    std::string terr;
+    if (!es::tls::configure_from_env(&terr)) {
+      fprintf(stderr, "TLS: %s\n", terr.c_str());
+      return 2;
+    }
+  }
   std::string api = env_or("EVERSERVE_API_ADDR", "127.0.0.1:7681");
   std::vector<std::string> args;
   for (int i = 1; i < argc; i++) {
@@ -99,6 +109,30 @@ int main(int argc, char** argv) {
       if (once) return 0;
       usleep(500 * 1000);
     }
+  }
+  if (verb == "certs") {
+    // certs init DIR [--days N] | certs issue DIR NAME [--days N]
+    int days = 365;
+    for (size_t i = 1; i + 1 < args.size(); i++)
+      if (args[i] == "--days") days = std::stoi(args[i + 1]);
+    std::string err;
+    if (args.size() >= 3 && args[1] == "init") {
+      if (!tls::make_ca(args[2], days, &err)) {
+        fprintf(stderr, "%s\n", err.c_str());
+        return 1;
+      }
+      printf("CA written to %s (ca.key, ca.crt)\n", args[2].c_str());
+      return 0;
+    }
+    if (args.size() >= 4 && args[1] == "issue") {
+      if (!tls::issue(args[2], args[3], days, &err)) {
+        fprintf(stderr, "%s\n", err.c_str());
+        return 1;
+      }
+      printf("certificate for %s written to %s\n", args[3].c_str(), args[2].c_str());
+      return 0;
+    }
+    return usage();
   }
   if (verb == "check") {
     std::string path;

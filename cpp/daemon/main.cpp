@@ -32,6 +32,7 @@
 #include "net.h"
 #include "notice.h"
 #include "telemetry.h"
+#include "tls.h"
 #include "util.h"
 
 using namespace es;
@@ -668,6 +669,13 @@ struct Daemon {
 }  // namespace
 
 int main(int argc, char** argv) {
+  {
+    std::string terr;
+    if (!es::tls::configure_from_env(&terr)) {
+      fprintf(stderr, "TLS: %s\n", terr.c_str());
+      return 2;
+    }
+  }
   log_init("node");
   signal(SIGPIPE, SIG_IGN);
   Daemon d;

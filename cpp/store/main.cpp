@@ -23,6 +23,7 @@
 
 #include "everserve_pb.h"
 #include "net.h"
+#include "tls.h"
 #include "storage.h"
 #include "telemetry.h"
 #include "util.h"
@@ -58,7 +59,7 @@ class Carrier {
 
  private:
   void run() {
-    std::map<std::string, int> fds;
+    std::map<std::string, tls::Stream> links;  // TLS when configured (the targets are TCP)
     while (true) {
       std::pair<std::string, std::string> item;
       {
@@ -69,25 +70,23 @@ class Carrier {
         bytes_ -= item.second.size();
       }
       for (int attempt = 0; attempt < 2; attempt++) {
-        int& fd = fds[item.first];
-        if (fd <= 0) {
+        tls::Stream& st = links[item.first];
+        if (st.fd < 0) {
           Address a;
           std::string err;
-          if (!Address::parse(item.first, a) || (fd = connect_to(a, 2000, &err)) < 0) {
-            fd = 0;
+          if (!Address::parse(item.first, a) || !tls::connect_stream(a, 2000, st, &err)) {
             metrics().inc("everserve_store_replication_link_failures_total");
             break;
           }
         }
         std::string reply;
-        if (write_frame(fd, item.second) && read_frame(fd, reply, 10000)) {
+        if (st.write_frame(item.second, 10000) && st.read_frame(reply, 10000)) {
           mirror::MirrorReply r;
           if (r.parse(reply) && r.error.empty()) metrics().inc("everserve_store_replicated_total");
           else metrics().inc("everserve_store_replication_link_failures_total");
           break;
         }
-        ::close(fd);
-        fd = 0;
+        st.close();
       }
     }
   }
@@ -196,6 +195,13 @@ void handle(Storage& st, Carrier& carrier, Loop& loop, Conn& c, const std::strin
 }  // namespace
 
 int main(int argc, char** argv) {
+  {
+    std::string terr;
+    if (!es::tls::configure_from_env(&terr)) {
+      fprintf(stderr, "TLS: %s\n", terr.c_str());
+      return 2;
+    }
+  }
   log_init("store");
   signal(SIGPIPE, SIG_IGN);
   Options o;
