@@ -49,12 +49,25 @@ struct GemmArgs {
   int* status;           // set non-zero if a bounded wait ran out
   int64_t M, N, K, ldx, ldw, ldo, ldr;
   int num_sms;           // SMs of the device (sizes the split-K clusters)
+  // optional epilogue terms, in this order: out = x.w^T * scale[m] + pre[m, n] (then the
+  // all-reduce of the fused variant), + residual[m, n]. `scale` (fp32, one per row of x) weights a
+  // mixture expert's rows by their routing weight; `pre` (bf16, row stride ldp) carries the rank's
+  // sum over the experts before it, so the experts of a rank combine in a fixed order.
+  const float* scale = nullptr;
+  const void* pre = nullptr;
+  int64_t ldp = 0;
+  int two_shot = 0;  // fused all-reduce: 1 = reduce-scatter to tile owners, then all-gather
 };
 int64_t gemm_pick_bn(int64_t M);
 int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms);
 int64_t gemm_ws_floats(int64_t num_sms);
 int64_t gemm_sync_words(int64_t num_sms);
 cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t s);
+// Mixture routing: per token softmax over E logits (bf16 rows of `stride`), top k (ties to the
+// lowest index), renormalised; scale[e, t] for this rank's experts e0 .. e0 + el - 1 (0 when not
+// chosen). E <= 64, el <= 32.
+cudaError_t launch_moe_route(const void* logits, int64_t stride, int T, int E, int k, int e0, int el, float* scale,
+                             cudaStream_t s);
 // out = sum over the group's members (member order) of x_r . w_r^T (+ residual): the row-parallel
 // GEMM with its all-reduce fused into the epilogue (decode sizes, M <= 64).
 cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStream_t s);

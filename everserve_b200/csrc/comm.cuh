@@ -37,7 +37,9 @@ constexpr size_t kLLGemmBytes = 1 << 21;  // per sender per parity: tiles * 64 *
 constexpr size_t kLLSmallBytes = 1 << 21; // per sender per parity: 256 Ki words = 512 Ki elements
 constexpr size_t kLLGemmOff = kFlagBytes + (size_t)2 * kMaxRows * kDataBytes;
 constexpr size_t kLLSmallOff = kLLGemmOff + (size_t)2 * kMaxRows * kLLGemmBytes;
-constexpr size_t kBufferBytes = kLLSmallOff + (size_t)2 * kMaxRows * kLLSmallBytes;
+constexpr size_t kLLResOff = kLLSmallOff + (size_t)2 * kMaxRows * kLLSmallBytes;
+// the two-shot fused GEMM's results: [2 parity][kLLGemmBytes], each word written by its tile's owner
+constexpr size_t kBufferBytes = kLLResOff + (size_t)2 * kLLGemmBytes;
 constexpr int kSeqSlots = 4096;  // per-slot LL call counters (this member's device memory)
 constexpr uint64_t kHardLimitNs = 5000000000ull;  // a wait never outlives 5 s
 
@@ -78,6 +80,9 @@ ES_DEVICE void mc_st_release_u32(void* mc_addr, uint32_t v) {
 // Order this thread's accesses through the multicast alias against unicast accesses to the buffer.
 ES_DEVICE void fence_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
 
+ES_DEVICE uint64_t* ll_res_ptr(uint64_t base, uint32_t parity) {
+  return reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(base) + kLLResOff + (size_t)parity * kLLGemmBytes);
+}
 ES_DEVICE uint64_t* ll_gemm_ptr(uint64_t base, uint32_t parity, int sender) {
   return reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(base) + kLLGemmOff +
                                      ((size_t)parity * kMaxRows + sender) * kLLGemmBytes);

@@ -238,7 +238,65 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t*
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Mixture routing: softmax over E expert logits, the top k (ties to the lowest index), their
+// probabilities renormalised, and for this rank's experts [e0, e0 + el) the weight of each token
+// (0 where the expert is not among the token's top k). One warp per token, E <= 64.
+__global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, int64_t stride, int T, int E, int k,
+                                 int e0, int el, float* __restrict__ scale) {
+  pdl_wait();
+  pdl_launch();
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const __nv_bfloat16* row = logits + (size_t)t * stride;
+  float x0 = lane < E ? bf2f(row[lane]) : -INFINITY;
+  float x1 = lane + 32 < E ? bf2f(row[lane + 32]) : -INFINITY;
+  float m = fmaxf(x0, x1);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float p0 = lane < E ? expf(x0 - m) : 0.f, p1 = lane + 32 < E ? expf(x1 - m) : 0.f;
+  float sum = p0 + p1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  p0 /= sum;
+  p1 /= sum;
+  // top k by repeated arg-max (ties to the lowest index)
+  bool s0 = false, s1 = false;
+  float chosen = 0.f;
+  for (int r = 0; r < k; r++) {
+    float bv = -1.f;
+    int bi = 0x7fffffff;
+    if (!s0 && lane < E) bv = p0, bi = lane;
+    if (!s1 && lane + 32 < E && (p1 > bv)) bv = p1, bi = lane + 32;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+    }
+    if (bi == lane) s0 = true;
+    if (bi == lane + 32) s1 = true;
+    chosen += bv;
+  }
+  for (int e = 0; e < el; e++) {  // the same trip count on every lane: the shuffles take the warp
+    const int g = e0 + e;
+    const float v0 = __shfl_sync(0xffffffffu, s0 ? p0 : 0.f, g & 31);
+    const float v1 = __shfl_sync(0xffffffffu, s1 ? p1 : 0.f, g & 31);
+    if (lane == 0) scale[(size_t)e * T + t] = (g < 32 ? v0 : v1) / chosen;
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_moe_route(const void* logits, int64_t stride, int T, int E, int k, int e0, int el, float* scale,
+                             cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  if (E > 64 || k < 1 || k > E || el > 32 || e0 < 0 || e0 + el > E) return cudaErrorInvalidValue;
+  constexpr int kWarps = 4;
+  return launch_ex(moe_route_kernel, dim3((unsigned)((T + kWarps - 1) / kWarps)), dim3(32 * kWarps), 0, stream, 0,
+                   static_cast<const __nv_bfloat16*>(logits), stride, T, E, k, e0, el, scale);
+}
 
 cudaError_t launch_decode_advance(int64_t* st, const int64_t* sampled, const int* bt, int64_t bt_stride, int b, int B,
                                   int bs, cudaStream_t stream) {

@@ -56,7 +56,18 @@ struct Params {
   int* status;
   int M, N, ldo, ldr;
   int kb, splits;
+  const float* scale;          // per row of x (token): multiplies the product (nullable)
+  const __nv_bfloat16* pre;    // added to the (scaled) product before any reduction (nullable)
+  int ldp;
+  int two_shot;                // fused all-reduce as reduce-scatter to tile owners + all-gather
 };
+
+// the product's epilogue terms before a reduction over members: acc * scale[m] + pre[m, n]
+ES_DEVICE float pre_terms(const Params& p, float acc, size_t m, int n) {
+  if (p.scale) acc *= p.scale[m];
+  if (p.pre) acc += bf2f(p.pre[m * p.ldp + n]);
+  return acc;
+}
 
 // kAR: the row-parallel variant whose epilogue sums the tile over the group's members (comm.cuh)
 template <int BN, int CPS, bool kAR>
@@ -181,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
         for (int j = 0; j < 16; j++) {
           if (c0 + j < mrem) {
             const size_t m = (size_t)(m0 + c0 + j);
-            float o = v[j];
+            float o = pre_terms(p, v[j], m, n);
             if (p.residual) o += bf2f(p.residual[m * p.ldr + n]);
             p.out[m * p.ldo + n] = f2bf(o);
           }
@@ -222,13 +233,27 @@ __global__ void __launch_bounds__(kThreads, CPS)
         acc.z += v.z;
         acc.w += v.w;
       }
+      if (p.scale || p.pre) {
+        const size_t mm = (size_t)(m0 + col);
+        const int nn = n0 + row;
+        acc.x = pre_terms(p, acc.x, mm, min(nn, p.N - 1));
+        acc.y = pre_terms(p, acc.y, mm, min(nn + 1, p.N - 1));
+        acc.z = pre_terms(p, acc.z, mm, min(nn + 2, p.N - 1));
+        acc.w = pre_terms(p, acc.w, mm, min(nn + 3, p.N - 1));
+      }
       if (kAR) {
         // this member's bf16 partial (what an unfused GEMM would output) as two LL words, to every
         // member: each word carries the call number, so it is its own arrival flag
         const size_t widx = ((size_t)(blockIdx.x * BN + col) * BM + row) / 2;
         const uint64_t w0 = ((uint64_t)seq << 32) | ptx::pack_bf16x2(acc.x, acc.y);
         const uint64_t w1 = ((uint64_t)seq << 32) | ptx::pack_bf16x2(acc.z, acc.w);
-        if (cv.mc) {
+        if (p.two_shot) {
+          // reduce-scatter: only the tile's owner takes the partials (1/count of the words a
+          // one-shot push sends)
+          uint64_t* d = comm::ll_gemm_ptr(cv.peers[s_order[blockIdx.x % s_count]], parity, cv.row) + widx;
+          comm::st_u64_relaxed(d, w0);
+          comm::st_u64_relaxed(d + 1, w1);
+        } else if (cv.mc) {
           uint64_t* d = comm::ll_gemm_ptr(cv.mc, parity, cv.row) + widx;
           comm::mc_st_u64(d, w0);
           comm::mc_st_u64(d + 1, w1);
@@ -253,8 +278,11 @@ __global__ void __launch_bounds__(kThreads, CPS)
       }
     }
     if (kAR) {
-      // sum every member's words in member order (polling the words themselves)
+      // sum every member's words in member order (polling the words themselves). Two-shot: only
+      // the tile's owner sums, then pushes the sums to the others, who poll for them instead.
       const uint64_t my_base = cv.peers[cv.row];
+      const int owner_row = s_count > 0 ? s_order[blockIdx.x % s_count] : cv.row;
+      const bool owner = !p.two_shot || owner_row == cv.row;
       uint64_t t0 = 0;
       bool named = false;
       uint32_t spins = 0;
@@ -263,7 +291,19 @@ __global__ void __launch_bounds__(kThreads, CPS)
         const int col = e / span4, row = r0 + (e % span4) * 4;
         const size_t widx = ((size_t)(blockIdx.x * BN + col) * BM + row) / 2;
         float o[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int k = 0; k < s_count && fail == kOk; k++) {
+        if (!owner) {
+          const uint64_t* src = comm::ll_res_ptr(my_base, parity) + widx;
+          const uint32_t a = comm::ll_wait(cv, src, seq, owner_row, t0, named, spins, fail);
+          const uint32_t b = comm::ll_wait(cv, src + 1, seq, owner_row, t0, named, spins, fail);
+          if (fail != kOk) break;
+          const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a));
+          const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&b));
+          o[0] = lo.x;
+          o[1] = lo.y;
+          o[2] = hi.x;
+          o[3] = hi.y;
+        }
+        for (int k = 0; owner && k < s_count && fail == kOk; k++) {
           const uint64_t* src = comm::ll_gemm_ptr(my_base, parity, s_order[k]) + widx;
           const uint32_t a = comm::ll_wait(cv, src, seq, s_order[k], t0, named, spins, fail);
           const uint32_t b = comm::ll_wait(cv, src + 1, seq, s_order[k], t0, named, spins, fail);
@@ -275,6 +315,23 @@ __global__ void __launch_bounds__(kThreads, CPS)
           o[3] += hi.y;
         }
         if (fail != kOk) break;
+        if (p.two_shot && owner) {
+          // all-gather: the reduced words (rounded to bf16 once, as every member will use them)
+          const uint64_t r0w = ((uint64_t)seq << 32) | ptx::pack_bf16x2(o[0], o[1]);
+          const uint64_t r1w = ((uint64_t)seq << 32) | ptx::pack_bf16x2(o[2], o[3]);
+          for (int k = 0; k < s_count; k++) {
+            if (s_order[k] == cv.row) continue;
+            uint64_t* d = comm::ll_res_ptr(cv.peers[s_order[k]], parity) + widx;
+            comm::st_u64_relaxed(d, r0w);
+            comm::st_u64_relaxed(d + 1, r1w);
+          }
+          const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r0w));
+          const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r1w));
+          o[0] = lo.x;  // the owner uses the same rounded sums as everyone else
+          o[1] = lo.y;
+          o[2] = hi.x;
+          o[3] = hi.y;
+        }
         const size_t m = (size_t)(m0 + col);
 #pragma unroll
         for (int z = 0; z < 4; z++) {
@@ -414,6 +471,9 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.ldo = (int)a.ldo;
   p.ldr = (int)a.ldr;
   p.kb = (int)((a.K + gemm::BK - 1) / gemm::BK);
+  p.scale = a.scale;
+  p.pre = static_cast<const __nv_bfloat16*>(a.pre);
+  p.ldp = (int)a.ldp;
   int cps = 1;
   gemm_plan(a.M, a.N, a.K, a.num_sms, &p.splits, &cps);
   const unsigned tiles_n = (unsigned)((a.N + gemm::BM - 1) / gemm::BM);
@@ -455,6 +515,10 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
   p.ldo = (int)a.ldo;
   p.ldr = (int)a.ldr;
   p.kb = (int)((a.K + gemm::BK - 1) / gemm::BK);
+  p.scale = a.scale;
+  p.pre = static_cast<const __nv_bfloat16*>(a.pre);
+  p.ldp = (int)a.ldp;
+  p.two_shot = c.mc ? 0 : a.two_shot;  // the multicast variant pushes once already
   int cps = 1;
   gemm_plan(BN, a.N, a.K, a.num_sms, &p.splits, &cps);
   // every CTA waits on peers: the whole grid must be resident at once

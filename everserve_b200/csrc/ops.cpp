@@ -112,8 +112,24 @@ void decode_advance(torch::Tensor st, torch::Tensor sampled, torch::Tensor bt, i
                                           bt.stride(0), (int)b, (int)st.size(1), (int)bs, cur()));
 }
 
+// The optional mixture terms of a GEMM epilogue: a per-row fp32 scale and a bf16 accumulator.
+void mixture_terms(es::GemmArgs& a, const c10::optional<torch::Tensor>& scale, const c10::optional<torch::Tensor>& pre) {
+  if (scale.has_value() && scale->defined()) {
+    TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->is_cuda() && scale->is_contiguous() &&
+                    scale->numel() >= a.M, "scale: fp32[M] on the device");
+    a.scale = scale->data_ptr<float>();
+  }
+  if (pre.has_value() && pre->defined()) {
+    check_bf16(*pre, "pre");
+    TORCH_CHECK(pre->size(0) == a.M && pre->size(1) == a.N && pre->stride(1) == 1, "pre shape");
+    a.pre = pre->data_ptr();
+    a.ldp = pre->stride(0);
+  }
+}
+
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
-               torch::Tensor ws, torch::Tensor sync, torch::Tensor status, int64_t num_sms) {
+               torch::Tensor ws, torch::Tensor sync, torch::Tensor status, int64_t num_sms,
+               c10::optional<torch::Tensor> scale, c10::optional<torch::Tensor> pre) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
@@ -145,8 +161,20 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
     a.residual = residual->data_ptr();
     a.ldr = residual->stride(0);
   }
+  mixture_terms(a, scale, pre);
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
+}
+
+torch::Tensor moe_route(torch::Tensor logits, int64_t k, int64_t e0, int64_t el) {
+  check_bf16(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits: [T, E] rows");
+  const int64_t T = logits.size(0), E = logits.size(1);
+  auto scale = torch::empty({el, T}, logits.options().dtype(at::kFloat));
+  const c10::cuda::CUDAGuard g(logits.device());
+  ES_CHECK_CUDA(es::launch_moe_route(logits.data_ptr(), logits.stride(0), (int)T, (int)E, (int)k, (int)e0, (int)el,
+                                     scale.data_ptr<float>(), cur()));
+  return scale;
 }
 
 es::CommArgs comm_args(torch::Tensor peers, torch::Tensor order, torch::Tensor call, int64_t ctrl, int64_t row,
@@ -179,7 +207,8 @@ void fdar(torch::Tensor inp, torch::Tensor out, torch::Tensor peers, torch::Tens
 
 void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
                     torch::Tensor status, int64_t num_sms, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
-                    int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs) {
+                    int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs, c10::optional<torch::Tensor> scale,
+                    c10::optional<torch::Tensor> pre, int64_t two_shot) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
@@ -206,6 +235,8 @@ void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::op
     a.residual = residual->data_ptr();
     a.ldr = residual->stride(0);
   }
+  mixture_terms(a, scale, pre);
+  a.two_shot = (int)two_shot;
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_allreduce(a, comm_args(peers, order, call, ctrl, row, mc, seqs), cur()));
 }
@@ -364,14 +395,23 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed", &embed, "embedding gather");
   m.def("argmax", &argmax, "greedy argmax per row");
   m.def("decode_advance", &decode_advance, "next decode step's inputs from the sampled ids");
-  m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM out = x . w^T (+ residual)");
+  m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM out = x . w^T * scale + pre (+ residual)", pybind11::arg("x"),
+        pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("residual"), pybind11::arg("ws"), pybind11::arg("sync"),
+        pybind11::arg("status"), pybind11::arg("num_sms"), pybind11::arg("scale") = pybind11::none(),
+        pybind11::arg("pre") = pybind11::none());
   m.def("gemm_pick_bn", &es::gemm_pick_bn);
   m.def("gemm_pick_splits", &es::gemm_pick_splits);
   m.def("gemm_ws_floats", &es::gemm_ws_floats);
   m.def("gemm_sync_words", &es::gemm_sync_words);
   m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
+  m.def("moe_route", &moe_route, "mixture routing: per-token weights of this rank's experts [el, T]");
   m.def("fdar", &fdar, "failure-detecting all-reduce over peer memory (member order)");
-  m.def("gemm_allreduce", &gemm_allreduce, "row-parallel GEMM with the all-reduce fused into its epilogue");
+  m.def("gemm_allreduce", &gemm_allreduce, "row-parallel GEMM with the all-reduce fused into its epilogue",
+        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("residual"), pybind11::arg("status"),
+        pybind11::arg("num_sms"), pybind11::arg("peers"), pybind11::arg("order"), pybind11::arg("call"),
+        pybind11::arg("ctrl"), pybind11::arg("row"), pybind11::arg("mc"), pybind11::arg("seqs"),
+        pybind11::arg("scale") = pybind11::none(), pybind11::arg("pre") = pybind11::none(),
+        pybind11::arg("two_shot") = 0);
   m.def("comm_buffer_bytes", &es::comm_buffer_bytes);
   m.def("comm_max_elems", &es::comm_max_elems);
   m.def("comm_ll_max_elems", &es::comm_ll_max_elems);

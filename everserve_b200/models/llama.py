@@ -56,14 +56,15 @@ class TPGroup:
             return t
         return self.collective.all_reduce(t)
 
-    def linear_allreduce(self, ops, x, w, residual=None):
-        """Row-parallel linear followed by the sum over ranks (fused when the collective has it)."""
+    def linear_allreduce(self, ops, x, w, residual=None, scale=None, pre=None):
+        """Row-parallel linear (x . w^T * scale + pre) followed by the sum over ranks, then the
+        residual; one fused kernel when the collective has it."""
         if self.size == 1:
-            return ops.linear(x, w, residual=residual)
+            return ops.linear(x, w, residual=residual, scale=scale, pre=pre)
         fused = getattr(self.collective, "linear_allreduce", None)
         if fused is not None and ops.kind == "kernel":
-            return fused(ops, x, w, residual)
-        y = self.collective.all_reduce(ops.linear(x, w))
+            return fused(ops, x, w, residual, scale=scale, pre=pre)
+        y = self.collective.all_reduce(ops.linear(x, w, scale=scale, pre=pre))
         if residual is not None:
             y = (y.float() + residual.float()).to(y.dtype)
         return y
@@ -286,21 +287,26 @@ class DecoderLM:
 
     # ---- MoE -----------------------------------------------------------------------------------
     def _moe(self, h: torch.Tensor, p: str) -> torch.Tensor:
-        """Top-k softmax mixture over this rank's experts; the sum over ranks combines them."""
+        """Top-k softmax mixture over this rank's experts, combined over the ranks.
+
+        Tokens are replicated over the expert-parallel group (its attention is tensor-parallel), so
+        dispatch is local: a routing kernel turns the router logits into each local expert's weight
+        per token (0 for tokens not routed to it). Each expert runs on every token (a decode step
+        reads each expert's weights once whatever the token count, so the extra rows cost no
+        bandwidth) with its routing weight applied in the down projection's epilogue, and the
+        experts of a rank accumulate in expert order through the epilogue's `pre` input. The last
+        expert's down projection carries the combine over the ranks (the fused all-reduce). No host
+        synchronisation, so the layer is captured in CUDA graphs; fixed orders, so results are
+        deterministic.
+        """
         ops, c, W = self.ops, self.cfg, self.weights
-        router_logits = ops.linear(h, W[p + "router"]).float()
-        probs = torch.softmax(router_logits, dim=-1)
-        topv, topi = torch.topk(probs, c.top_k, dim=-1)
-        topv = topv / topv.sum(-1, keepdim=True)
-        out = torch.zeros(h.shape[0], c.hidden, dtype=torch.float32, device=h.device)
-        for e in range(self.expert0, self.expert0 + self.experts_local):
-            sel = (topi == e)
-            rows = sel.any(-1).nonzero(as_tuple=True)[0]
-            if rows.numel() == 0:
-                continue
-            wgt = (topv * sel).sum(-1)[rows]
-            xe = h.index_select(0, rows)
-            gu = ops.linear(xe, W[p + f"e{e}.gate_up"])
-            ye = ops.linear(ops.silu_mul(gu), W[p + f"e{e}.down"])
-            out.index_add_(0, rows, ye.float() * wgt[:, None])
-        return self.tp.all_reduce(out.to(h.dtype))
+        # the router's product is a few experts wide: a plain matmul, not a weight-streaming GEMM
+        logits = (h.float() @ W[p + "router"].float().t()).to(h.dtype)
+        scales = ops.moe_route(logits, c.top_k, self.expert0, self.experts_local)
+        acc = None
+        for i, e in enumerate(range(self.expert0, self.expert0 + self.experts_local)):
+            act = ops.silu_mul(ops.linear(h, W[p + f"e{e}.gate_up"]))
+            if i == self.experts_local - 1:
+                return self.tp.linear_allreduce(ops, act, W[p + f"e{e}.down"], scale=scales[i], pre=acc)
+            acc = ops.linear(act, W[p + f"e{e}.down"], scale=scales[i], pre=acc)
+        return acc

@@ -33,8 +33,11 @@ class RefOps:
     def rmsnorm(self, x, w, eps, residual=None):
         return ref.rmsnorm(x, w, eps, residual)
 
-    def linear(self, x, w, bias=None, residual=None):
-        return ref.linear(x, w, bias, residual)
+    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None):
+        return ref.linear(x, w, bias, residual, scale, pre)
+
+    def moe_route(self, logits, k, e0, el):
+        return ref.moe_route(logits, k, e0, el)
 
     def rope_kv_write(self, qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size):
         return ref.rope_kv_write(qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size)
@@ -112,7 +115,7 @@ class KernelOps:
         self.C.rmsnorm(x, residual, w, y, eps)
         return y
 
-    def linear(self, x, w, bias=None, residual=None, out=None):
+    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None):
         M, K = x.shape
         N = w.shape[0]
         if out is None:
@@ -122,8 +125,11 @@ class KernelOps:
             # bias folds into the residual input of the epilogue
             b = bias.expand(M, N) if residual is None else residual + bias
             residual = b.contiguous()
-        self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, self.num_sms)
+        self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, self.num_sms, scale, pre)
         return out
+
+    def moe_route(self, logits, k, e0, el):
+        return self.C.moe_route(logits.contiguous(), k, e0, el)
 
     def rope_kv_write(self, qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size):
         T = qkv.shape[0]

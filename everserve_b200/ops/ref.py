@@ -135,13 +135,29 @@ def silu_mul(gu: torch.Tensor) -> torch.Tensor:
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
-           residual: torch.Tensor | None = None) -> torch.Tensor:
+           residual: torch.Tensor | None = None, scale: torch.Tensor | None = None,
+           pre: torch.Tensor | None = None) -> torch.Tensor:
+    """x . w^T * scale[m] + pre + bias + residual (fp32, one rounding): the GEMM epilogue's order."""
     y = x.float() @ w.float().t()
+    if scale is not None:
+        y = y * scale.float()[:, None]
+    if pre is not None:
+        y = y + pre.float()
     if bias is not None:
         y = y + bias.float()
     if residual is not None:
         y = y + residual.float()
     return y.to(x.dtype)
+
+
+def moe_route(logits: torch.Tensor, k: int, e0: int, el: int) -> torch.Tensor:
+    """Per-token weights of experts e0 .. e0 + el - 1: softmax, top k with ties to the lowest index,
+    renormalised over the k; 0 for an expert not chosen. Returns fp32 [el, T]."""
+    p = torch.softmax(logits.float(), dim=-1)
+    order = torch.argsort(-p, dim=-1, stable=True)[:, :k]
+    chosen = torch.zeros_like(p).scatter_(1, order, 1.0)
+    w = p * chosen / (p * chosen).sum(-1, keepdim=True)
+    return w[:, e0 : e0 + el].t().contiguous()
 
 
 def argmax(logits: torch.Tensor) -> torch.Tensor:

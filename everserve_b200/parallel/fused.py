@@ -69,6 +69,7 @@ class FusedTPCollective:
                 region = SlotRegion.open(name)
         self.region = region
         self.max_elems = int(self.C.comm_max_elems())
+        self.two_shot = 1 if os.environ.get("ES_AR_TWO_SHOT", "0") == "1" else 0
         self.nvls = bool(nvls)
         self.mc = 0
         self._symm = None
@@ -196,13 +197,17 @@ class FusedTPCollective:
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         return self.all_reduce_into(t, t)
 
-    def linear_allreduce(self, ops, x: torch.Tensor, w: torch.Tensor, residual=None) -> torch.Tensor:
-        """Row-parallel linear summed over the members; one fused kernel at decode sizes."""
+    def linear_allreduce(self, ops, x: torch.Tensor, w: torch.Tensor, residual=None, scale=None,
+                         pre=None) -> torch.Tensor:
+        """Row-parallel linear (x . w^T * scale + pre) summed over the members, then the residual;
+        one fused kernel at decode sizes. ES_AR_TWO_SHOT=1 makes the fused sum a reduce-scatter to
+        each tile's owner and an all-gather (a quarter of the one-shot push's NVLink bytes at 8)."""
         if x.shape[0] <= 64 and x.dtype == torch.bfloat16:
             out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
-            self.C.gemm_allreduce(x, w, out, residual, ops.status, ops.num_sms, *self._comm())
+            self.C.gemm_allreduce(x, w, out, residual, ops.status, ops.num_sms, *self._comm(), scale, pre,
+                                  self.two_shot)
             return out
-        y = self.all_reduce(ops.linear(x, w))
+        y = self.all_reduce(ops.linear(x, w, scale=scale, pre=pre))
         if residual is not None:
             y = (y.float() + residual.float()).to(y.dtype)
         return y

@@ -4,7 +4,7 @@ import pytest
 import torch
 
 from everserve_b200.engine import Engine, EngineConfig, SamplingParams
-from everserve_b200.models.config import TINY_LLAMA, TINY_QWEN
+from everserve_b200.models.config import TINY_LLAMA, TINY_MIXTRAL, TINY_QWEN
 from everserve_b200.ops import RefOps
 
 pytestmark = pytest.mark.gpu
@@ -15,7 +15,7 @@ def _cfg(model, graphs=True):
                         use_cuda_graphs=graphs)
 
 
-@pytest.mark.parametrize("model", [TINY_LLAMA, TINY_QWEN])
+@pytest.mark.parametrize("model", [TINY_LLAMA, TINY_QWEN, TINY_MIXTRAL])
 def test_kernel_forward_matches_reference(cuda, model):
     eng = Engine(_cfg(model, graphs=False))
     worker = eng.executor.worker

@@ -116,6 +116,32 @@ def test_gemm_residual_and_repeat(kops):
     assert kops.check_status() == 0
 
 
+@pytest.mark.parametrize("M,N,K", [(48, 4096, 4096), (5, 2048, 14336), (128, 1024, 2048)])
+def test_gemm_scale_and_pre(kops, M, N, K):
+    """The mixture epilogue: x . w^T * scale[m] + pre (+ residual), split and unsplit tiles."""
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
+    scale = torch.rand(M, device="cuda", generator=g)
+    pre = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    r = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    y = kops.linear(x, w, residual=r, scale=scale, pre=pre)
+    close(y, ref.linear(x, w, None, r, scale, pre))
+    y2 = kops.linear(x, w, scale=scale)
+    close(y2, (x.float() @ w.float().t()) * scale[:, None])
+    assert kops.check_status() == 0
+
+
+@pytest.mark.parametrize("E,k,e0,el", [(8, 2, 0, 8), (8, 2, 4, 2), (64, 6, 8, 16), (4, 1, 1, 3)])
+def test_moe_route(kops, E, k, e0, el):
+    g = torch.Generator(device="cuda").manual_seed(E * 10 + k)
+    logits = (torch.randn(37, E, device="cuda", generator=g) * 2).bfloat16()
+    got = kops.moe_route(logits, k, e0, el)
+    want = ref.moe_route(logits, k, e0, el)
+    assert torch.equal(got > 0, want > 0)
+    torch.testing.assert_close(got, want, rtol=1e-5, atol=1e-6)
+
+
 def test_gemm_batch_invariant(kops):
     """A row's result does not depend on the other rows of the batch (exact replay needs this)."""
     g = torch.Generator(device="cuda").manual_seed(4)
