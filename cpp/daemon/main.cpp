@@ -18,6 +18,7 @@
 //     reports made while unlinked are held and sent on the next link. Messages from an older
 //     coordinator term than the highest seen are ignored (fencing).
 #include <signal.h>
+#include <sys/socket.h>
 #include <sys/wait.h>
 #include <unistd.h>
 
@@ -49,8 +50,42 @@ struct Proc {
   uint32_t device = 0;
   bool registered = false;
   bool said_goodbye = false;
+  bool reported_gone = false;  // its departure was reported (by the process watcher or the close)
+  int os_pid = 0;              // the peer's pid in this daemon's pid namespace (SO_PEERCRED), 0 unknown
   signals::Register reg;
 };
+
+// A process is leaving once the kernel has started its exit (PF_EXITING), it is a zombie or gone,
+// or SIGKILL is pending: that is seen within the poll period, well before its sockets close (the
+// kernel tears down a large address space before it closes the process's files).
+static bool proc_dying(int pid) {
+  std::string stat;
+  if (!read_file("/proc/" + std::to_string(pid) + "/stat", stat)) return true;
+  const auto rp = stat.rfind(')');
+  if (rp == std::string::npos || rp + 2 >= stat.size()) return true;
+  const char state = stat[rp + 2];
+  if (state == 'Z' || state == 'X' || state == 'x') return true;
+  // fields after the state: ppid pgrp session tty_nr tpgid flags
+  unsigned long flags = 0;
+  int field = 0;
+  size_t i = rp + 3;
+  while (i < stat.size() && field < 6) {
+    while (i < stat.size() && stat[i] == ' ') i++;
+    size_t j = i;
+    while (j < stat.size() && stat[j] != ' ') j++;
+    if (field == 5) flags = std::strtoul(stat.substr(i, j - i).c_str(), nullptr, 10);
+    field++;
+    i = j;
+  }
+  if (flags & 0x4) return true;  // PF_EXITING
+  std::string status;
+  if (!read_file("/proc/" + std::to_string(pid) + "/status", status)) return true;
+  for (const char* key : {"ShdPnd:", "SigPnd:"}) {
+    const auto k = status.find(key);
+    if (k != std::string::npos && (std::strtoull(status.c_str() + k + 7, nullptr, 16) & (1ull << 8))) return true;
+  }
+  return false;
+}
 
 // A spare this daemon launched for the coordinator (LaunchSpare) and keeps running: a spare that
 // exits before it takes a rank is started again after a backoff (1 s, doubling to 30 s; reset
@@ -424,6 +459,11 @@ struct Daemon {
       p.device = r.has_member ? r.member.device : 0;
       p.reg = r;
       p.registered = true;
+      {
+        ucred cred{};
+        socklen_t len = sizeof(cred);
+        if (getsockopt(c.fd, SOL_SOCKET, SO_PEERCRED, &cred, &len) == 0 && cred.pid > 0) p.os_pid = cred.pid;
+      }
       metrics().inc("everserve_node_registrations_total", {{"role", std::to_string(r.role)}});
       if (r.role == signals::Role_ROLE_UNDECIDED) {
         coord::DaemonToCoord m;
@@ -545,10 +585,33 @@ struct Daemon {
         maybe_delivered(rid, "rank " + std::to_string(p.rank) + " departed during the change");
         break;
       }
-    if (p.registered && p.role != signals::Role_ROLE_CLIENT)
+    if (p.registered && p.role != signals::Role_ROLE_CLIENT && !p.reported_gone)
       worker_event(p, departed_kind(p.role),
                    p.said_goodbye ? signals::StopCause_STOP_CAUSE_STOPPED : signals::StopCause_STOP_CAUSE_LOST,
                    p.said_goodbye ? "goodbye" : "connection ended");
+  }
+
+  // ---- the process watcher: a dying worker is reported before its connection closes --------------
+  void watch_processes() {
+    for (auto& [id, p] : procs) {
+      if (!p.registered || p.reported_gone || p.os_pid <= 0 || p.said_goodbye) continue;
+      if (p.role != signals::Role_ROLE_WORKER && p.role != signals::Role_ROLE_SPARE) continue;
+      if (!proc_dying(p.os_pid)) continue;
+      p.reported_gone = true;
+      metrics().inc("everserve_node_processes_lost_total", {{"engine", p.engine}});
+      ES_WARN("process %d (%s rank %u) is exiting: reported lost", p.os_pid, p.engine.c_str(), p.rank);
+      worker_event(p, departed_kind(p.role), signals::StopCause_STOP_CAUSE_LOST, "process exiting");
+      for (auto& [rid, pd] : deliveries)
+        if (pd.waiting.erase(id)) {
+          signals::Ack a;
+          a.rank = p.rank;
+          a.epoch = pd.deliver.change.epoch;
+          a.error = "process departed before its ack";
+          pd.acks.push_back(a);
+          maybe_delivered(rid, "rank " + std::to_string(p.rank) + " departed during the change");
+          break;
+        }
+    }
   }
 
   // ---- replication targets: the coordinator names which stores take a rank's rows --------------
@@ -689,6 +752,7 @@ int main(int argc, char** argv) {
   std::string notice_source = env_or("EVERSERVE_NOTICE_SOURCE", "");
   std::string notice_endpoint = env_or("EVERSERVE_NOTICE_ENDPOINT", "");
   uint32_t notice_interval = 1000;
+  uint64_t proc_poll_ms = std::stoull(env_or("EVERSERVE_PROC_POLL_MS", "2"));
   for (int i = 1; i + 1 < argc; i += 2) {
     const std::string k = argv[i], v = argv[i + 1];
     if (k == "--node") d.node = v;
@@ -700,6 +764,7 @@ int main(int argc, char** argv) {
     else if (k == "--mirror-socket") d.mirror_socket = v;
     else if (k == "--discovery-dir") discovery = v;
     else if (k == "--replica-address") d.replica_address = v;
+    else if (k == "--proc-poll-ms") proc_poll_ms = std::stoull(v);
     else if (k == "--notice-source") notice_source = v;
     else if (k == "--notice-endpoint") notice_endpoint = v;
     else if (k == "--notice-interval-ms") notice_interval = (uint32_t)std::stoul(v);
@@ -737,6 +802,7 @@ int main(int argc, char** argv) {
   d.link();
   d.loop.every(d.heartbeat_ms, [&] { d.tick(); });
   d.loop.every(100, [&] { d.supervise(); });
+  d.loop.every(proc_poll_ms, [&] { d.watch_processes(); });
   std::unique_ptr<NoticeWatcher> notices;
   if (!notice_source.empty()) {
     notices = std::make_unique<NoticeWatcher>(notice_source, notice_endpoint, d.node, notice_interval);
@@ -763,6 +829,7 @@ int main(int argc, char** argv) {
     _exit(0);
   });
   metrics().describe("everserve_node_spare_starts_total", "Spares this daemon started (restarts included)", "counter");
+  metrics().describe("everserve_node_processes_lost_total", "Engine processes the watcher found exiting", "counter");
   ES_INFO("node %s serving %s, coordinator %s", d.node.c_str(), socket.c_str(), d.coordinator.c_str());
   d.loop.run();
   return 0;

@@ -306,6 +306,7 @@ class DaemonClient(HearsEngine):
         self.replay_asks: queue.Queue = queue.Queue()
         self.epoch = 0
         self.pending_change = threading.Event()
+        self.last_change = None
         self._on_heard = on_heard
         self._reader = threading.Thread(target=self._serve, name=f"daemon-client-{engine}", daemon=True)
         self._reader.start()
@@ -319,6 +320,7 @@ class DaemonClient(HearsEngine):
             kind = _kind(sig)
             h = None
             if kind == "change":
+                self.last_change = sig.change
                 self.pending_change.set()
                 h = Heard(sig.change.epoch, "change", change=sig.change)
             elif kind == "membership_committed":

@@ -1,0 +1,121 @@
+"""Failover latency: dead-rank detection, change commit, resume and the streams' pause.
+
+    python -m everserve_b200.perf.failover [--trials 20] [--model tiny-qwen] [--full] [--device cpu]
+
+Each trial starts the control plane (coordinator, daemon, store) and a TP1 PP2 engine with a
+spare for rank 1, generates 8 streams, kills rank 1 at a random decode step (SIGKILL on the CPU
+tier; between steps on GPUs) and checks every stream against a no-fault run. Per trial it records,
+from the fault (the coordinator's stamps are wall-clock microseconds of the same host):
+
+  * detect_ms   - the coordinator received the loss (its ``reported_at_us``);
+  * commit_ms   - the coordinator committed the new membership;
+  * resumed_ms  - the head resumed the engine (groups formed, requests restarted);
+  * pause_ms    - the longest gap between two steps that produced tokens, around the fault: what a
+                  client of the streams sees.
+
+It prints one JSON line with p50 / p99 / max of each and the token-identity verdict.
+``--full`` uses the Qwen2.5-0.5B shape (128-token prompts, 64 tokens, kill at decode step 20).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import shutil
+import tempfile
+import time
+
+import torch
+
+
+def _pct(xs, q):
+    xs = sorted(xs)
+    if not xs:
+        return None
+    k = min(len(xs) - 1, max(0, int(round(q / 100 * (len(xs) - 1)))))
+    return round(xs[k], 3)
+
+
+def run_trial(workdir, model, prompts, tokens, kill_at, device, dtype):
+    from ..engine.config import EngineConfig
+    from ..engine.engine import Engine
+    from ..serving.cluster import ControlPlane
+    from ..serving.executor import MultiprocExecutor, failover
+
+    cfg = EngineConfig(model=model, device=device, dtype=dtype, num_blocks=256, max_batch=len(prompts),
+                       max_model_len=len(prompts[0]) + tokens + 16, pipeline_parallel=2, use_cuda_graphs=False)
+    with ControlPlane(workdir, engines=[{"name": "e0", "pipelineParallel": 2}]) as cp:
+        ex = MultiprocExecutor(cfg, engine="e0", daemon=cp.daemon_socket, store=cp.store_socket,
+                               spares=(1,) if kill_at else (), node="n0", threads=2,
+                               device="cuda" if device.startswith("cuda") else "cpu",
+                               dtype="bfloat16" if device.startswith("cuda") else "float32")
+        try:
+            if kill_at:
+                cp.wait_spares("e0", 1)
+            eng = Engine(cfg, executor=ex)
+            eng.wrap_step(failover(ex, eng))
+            if kill_at:
+                ex.kill_at_decode_step = (kill_at, 1)
+            from ..engine.request import SamplingParams
+
+            ids = [eng.add_request(p, SamplingParams(max_tokens=tokens)) for p in prompts]
+            stamps = []
+            while eng.has_work():
+                out = eng.step()
+                if any(tok is not None for _, tok, _ in out):
+                    stamps.append(time.monotonic())
+            outs = [eng.request(i).outputs for i in ids]
+            rec = ex.changes[0] if ex.changes else None
+            return outs, rec, stamps
+        finally:
+            ex.shutdown()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--trials", type=int, default=10)
+    ap.add_argument("--model", default="tiny-qwen")
+    ap.add_argument("--full", action="store_true", help="Qwen2.5-0.5B shape, 128-token prompts, 64 tokens")
+    ap.add_argument("--device", default="cpu")
+    ap.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args()
+    model = "qwen2.5-0.5b" if a.full else a.model
+    from ..models.config import get_config
+
+    vocab = get_config(model).vocab
+    prompt_len, tokens = (128, 64) if a.full else (64, 32)
+    rng = random.Random(a.seed)
+    prompts = [[rng.randrange(vocab) for _ in range(prompt_len)] for _ in range(8)]
+    dtype = torch.bfloat16 if a.device.startswith("cuda") else torch.float32
+    root = tempfile.mkdtemp(prefix="es-failover-")
+    try:
+        base, _, _ = run_trial(os.path.join(root, "base"), model, prompts, tokens, 0, a.device, dtype)
+        rows = []
+        for t in range(a.trials):
+            kill_at = 20 if a.full else rng.randrange(3, tokens - 4)
+            outs, rec, stamps = run_trial(os.path.join(root, f"t{t}"), model, prompts, tokens, kill_at, a.device, dtype)
+            d = rec.as_dict()
+            t_fault = rec.t_fault_wall
+            rep_us = rec.coordinator.get("reported_at_us")
+            gaps = [b - a_ for a_, b in zip(stamps, stamps[1:])]
+            rows.append({
+                "kill_at": kill_at, "identical": outs == base,
+                "detect_ms": (rep_us / 1e3 - t_fault * 1e3) if rep_us else None,
+                "commit_ms": d["committed_ms"], "resumed_ms": d["resumed_ms"],
+                "pause_ms": max(gaps) * 1e3 if gaps else None,
+            })
+        summary = {"metric": "failover pause p99; dead-rank detect ms", "model": model, "device": a.device,
+                   "trials": len(rows), "token_identical": all(r["identical"] for r in rows)}
+        for k in ("detect_ms", "commit_ms", "resumed_ms", "pause_ms"):
+            xs = [r[k] for r in rows if r[k] is not None]
+            summary[k] = {"p50": _pct(xs, 50), "p99": _pct(xs, 99), "max": round(max(xs), 3) if xs else None}
+        summary["rows"] = rows
+        print(json.dumps(summary))
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -115,6 +115,13 @@ class SwappableGroups:
         return self.current
 
 
+def _wait(groups: "SwappableGroups", work) -> None:
+    """Wait for a c10d operation. One with a dead peer ends with an error: on gloo when the kernel
+    closes the peer's sockets, on NCCL when a change refuses the groups (they are aborted). gloo's
+    point-to-point work only completes inside wait(), so it cannot be polled instead."""
+    work.wait()
+
+
 class Exchange:
     """Pipeline transport between the same column of adjacent stages."""
 
@@ -124,12 +131,12 @@ class Exchange:
     def send_hidden(self, hidden: torch.Tensor, residual: torch.Tensor) -> None:
         g = self.groups.live()
         buf = torch.stack([hidden.to(self.dtype), residual.to(self.dtype)]).contiguous()
-        g.pipe.send([buf], g.layout.stage(g.rank) + 1, 0).wait()
+        _wait(self.groups, g.pipe.send([buf], g.layout.stage(g.rank) + 1, 0))
 
     def recv_hidden(self, n: int) -> tuple[torch.Tensor, torch.Tensor]:
         g = self.groups.live()
         buf = torch.empty(2, n, self.hidden, dtype=self.dtype, device=g.device)
-        g.pipe.recv([buf], g.layout.stage(g.rank) - 1, 0).wait()
+        _wait(self.groups, g.pipe.recv([buf], g.layout.stage(g.rank) - 1, 0))
         return buf[0], buf[1]
 
 
@@ -142,7 +149,7 @@ class GroupCollective:
     def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         g = self.groups.live()
         if g.tp is not None:
-            g.tp.allreduce([t]).wait()
+            _wait(self.groups, g.tp.allreduce([t]))
         return t
 
     def all_gather(self, t: torch.Tensor) -> torch.Tensor:
@@ -151,5 +158,5 @@ class GroupCollective:
             return t
         t = t.contiguous()
         parts = [torch.empty_like(t) for _ in range(g.layout.tensor_parallel)]
-        g.tp.allgather([parts], [t]).wait()
+        _wait(self.groups, g.tp.allgather([parts], [t]))
         return torch.cat(parts, dim=-1)

@@ -30,6 +30,10 @@ class LinkClosed(ConnectionError):
     pass
 
 
+class StepAbandoned(RuntimeError):
+    """The caller's `abandon` check said to stop waiting."""
+
+
 def _send(sock: socket.socket, lock: threading.Lock, msg: dict) -> None:
     data = pickle.dumps(msg, protocol=pickle.HIGHEST_PROTOCOL)
     with lock:
@@ -60,15 +64,18 @@ class Link:
             self.closed.set()
             raise LinkClosed(f"rank {self.rank}: {e}") from e
 
-    def get(self, timeout: float | None = None) -> dict:
-        """The next message; raises LinkClosed once the link ended and the inbox is empty."""
+    def get(self, timeout: float | None = None, abandon=None) -> dict:
+        """The next message; raises LinkClosed once the link ended and the inbox is empty, and
+        StepAbandoned when `abandon()` turns true while waiting."""
         deadline = None if timeout is None else time.monotonic() + timeout
         while True:
             try:
-                return self.inbox.get(timeout=0.05)
+                return self.inbox.get(timeout=0.002 if abandon is not None else 0.05)
             except queue.Empty:
                 if self.closed.is_set() and self.inbox.empty():
                     raise LinkClosed(f"rank {self.rank}'s link ended") from None
+                if abandon is not None and abandon():
+                    raise StepAbandoned(f"stopped waiting for rank {self.rank}") from None
                 if deadline is not None and time.monotonic() > deadline:
                     raise TimeoutError(f"rank {self.rank} sent nothing within {timeout} s") from None
 

@@ -35,15 +35,34 @@ _handed: set[int] = set()
 
 
 def free_port() -> int:
-    """A loopback port no one listens on, never the same one twice in this process."""
+    """A loopback port no one listens on, never the same one twice in this process.
+
+    Ports come from below the kernel's ephemeral range, so a port handed out now and bound later
+    (a standby coordinator binds its API only when it takes the lease) is not given meanwhile to
+    some other socket's implicit bind."""
+    import random
+
+    lo = 20000
+    try:
+        with open("/proc/sys/net/ipv4/ip_local_port_range") as f:
+            eph = int(f.read().split()[0])
+    except (OSError, ValueError):
+        eph = 32768
+    hi = max(lo + 1000, eph - 1)
+    rng = random.Random()
     while True:
+        port = rng.randrange(lo, hi)
+        if port in _handed:
+            continue
         s = socket.socket()
-        s.bind(("127.0.0.1", 0))
-        port = s.getsockname()[1]
-        s.close()
-        if port not in _handed:
-            _handed.add(port)
-            return port
+        try:
+            s.bind(("127.0.0.1", port))
+        except OSError:
+            continue
+        finally:
+            s.close()
+        _handed.add(port)
+        return port
 
 
 def wait_listening(addr: str, timeout_s: float = 15.0) -> None:

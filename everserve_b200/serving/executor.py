@@ -42,7 +42,7 @@ from ..contract import join as joinfmt
 from ..contract.daemon import DaemonClient
 from ..engine.config import EngineConfig
 from ..runtime.layout import ParallelLayout
-from .carrier import CarrierServer, Link, LinkClosed
+from .carrier import CarrierServer, Link, LinkClosed, StepAbandoned
 
 
 class RankLost(RuntimeError):
@@ -67,6 +67,7 @@ class ChangeRecord:
     t_ready: float = 0.0
     t_resumed: float = 0.0
     t_fault: float = 0.0  # when the fault was injected (host-side injection only)
+    t_fault_wall: float = 0.0  # the same instant on the wall clock (the coordinator's stamps are wall time)
     coordinator: dict = field(default_factory=dict)
 
     def as_dict(self) -> dict:
@@ -180,7 +181,7 @@ class MultiprocExecutor:
         self.decode_steps_run = 0
         self.kill_at_decode_step: tuple[int, int] | None = None  # (decode step, rank): host-side fault injection
         self.notice_at_decode_step: tuple[int, int] | None = None  # (decode step, rank): a planned departure
-        self.t_kill = 0.0
+        self.t_kill = self.t_kill_wall = 0.0
         self._finished: list[str] = []
 
     # ---- processes -------------------------------------------------------------------------------
@@ -219,7 +220,7 @@ class MultiprocExecutor:
         if victim is not None and self.gpu:
             # on GPUs a rank leaves between steps (its kernels done), never mid-kernel
             msg = dict(msg, fail_at=plan.step, fail_rank=victim)
-            self.t_kill = time.monotonic()
+            self.t_kill, self.t_kill_wall = time.monotonic(), time.time()
             victim = None
         lost, errors = set(), {}
         for r, link in self.links.items():
@@ -228,7 +229,7 @@ class MultiprocExecutor:
             except LinkClosed:
                 lost.add(r)
         if victim is not None:
-            self.t_kill = time.monotonic()
+            self.t_kill, self.t_kill_wall = time.monotonic(), time.time()
             os.kill(self.pid_of(victim), signal.SIGKILL)  # the fault: SIGKILL mid-step
         ids = None
         for r, link in self.links.items():
@@ -236,12 +237,15 @@ class MultiprocExecutor:
                 continue
             try:
                 while True:
-                    reply = link.get(timeout=self.step_timeout_s)
+                    reply = link.get(timeout=self.step_timeout_s, abandon=self._fault_pending)
                     if reply.get("step") == plan.step:
                         break
             except LinkClosed:
                 lost.add(r)
                 continue
+            except StepAbandoned:
+                # the coordinator's change for a fault is already under way: cut the step now
+                raise RankLost(sorted(self.client.last_change.lost), "a membership change is pending") from None
             if reply["op"] == "error":
                 errors[r] = reply["error"]
             elif "ids" in reply:
@@ -249,6 +253,13 @@ class MultiprocExecutor:
         if lost or errors:
             raise RankLost(lost or set(errors), "; ".join(f"rank {r}: {e}" for r, e in errors.items()) or "link ended")
         return ids
+
+    def _fault_pending(self) -> bool:
+        """A change for a fault (not only planned departures) reached this head."""
+        if self.client is None or not self.client.pending_change.is_set():
+            return False
+        ch = self.client.last_change
+        return ch is not None and ch.epoch > self.epoch and not set(ch.lost) <= set(ch.departing)
 
     def fetch(self, ids):
         return ids
@@ -343,17 +354,24 @@ class MultiprocExecutor:
         if h.kind == "abandoned":
             raise EngineDown(f"the coordinator abandoned epoch {h.epoch}: {h.detail}")
         mc = h.committed
-        rec = ChangeRecord(mc.epoch, list(mc.lost), 0, t_detect, t_committed=time.monotonic(), t_fault=self.t_kill)
+        rec = ChangeRecord(mc.epoch, list(mc.lost), 0, t_detect, t_committed=time.monotonic(), t_fault=self.t_kill,
+                           t_fault_wall=self.t_kill_wall if self.t_kill else 0.0)
         self.t_kill = 0.0
         rec.coordinator = {"reported_to_committed_ms": (mc.committed_at_us - mc.reported_at_us) / 1e3
-                           if mc.reported_at_us else None, "pause_ms": mc.pause_ms}
+                           if mc.reported_at_us else None, "pause_ms": mc.pause_ms,
+                           # the coordinator's wall clock: comparable with time.time() on one host
+                           "reported_at_us": mc.reported_at_us, "committed_at_us": mc.committed_at_us,
+                           "delivered_at_us": mc.delivered_at_us,
+                           "acks_at_us": {int(a.rank): int(a.received_at_us) for a in mc.acks}}
         lost = [r for r in mc.lost]
+        ch = self.client.last_change
+        planned = set(ch.departing) if ch is not None and ch.epoch == mc.epoch else set()
         departed = set()
         for r in lost:
             link = self.links.pop(r, None)
             if link is None:
                 continue
-            if not link.closed.is_set():
+            if r in planned and not link.closed.is_set():
                 departed.add(r)
                 try:  # a planned departure: it drains its commits and leaves
                     link.send({"op": "release"})

@@ -22,11 +22,9 @@ def binary(name: str) -> str:
 
 
 def free_port() -> int:
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+    from everserve_b200.serving.cluster import free_port as fp
+
+    return fp()
 
 
 def wait_socket(path: str, timeout: float = 10.0) -> None:
