@@ -117,6 +117,8 @@ struct Coordinator {
   uint64_t next_request = 1;
   std::deque<Event> events;
   uint64_t event_seq = 0;
+  // stack dumps by request: (node, pid) -> text, kept for the last 64 requests
+  std::map<uint64_t, std::vector<std::pair<std::string, std::string>>> stacks;
 
   void event(const std::string& text) {
     std::string eng;
@@ -748,6 +750,11 @@ struct Coordinator {
       to_node(node, out);
     } else if (m.has_node_notice) {
       drain(node, m.node_notice.deadline_ms, "node notice: " + m.node_notice.source);
+    } else if (m.has_stacks_sent) {
+      auto& v = stacks[m.stacks_sent.request_id];
+      v.emplace_back(node + ":" + std::to_string(m.stacks_sent.pid),
+                     m.stacks_sent.answered ? m.stacks_sent.text : "(no answer: " + m.stacks_sent.error + ")");
+      while (stacks.size() > 64) stacks.erase(stacks.begin());
     } else if (m.has_cover_report) {
       on_cover_report(m.cover_report);
     } else if (m.has_replay_ask || m.has_replay_offer) {
@@ -938,6 +945,20 @@ struct Coordinator {
       resp.body = o + "]}";
       return true;
     }
+    if (req.method == "GET" && path.rfind("/v1/stacks/", 0) == 0) {
+      const uint64_t id = std::stoull(path.substr(11));
+      auto it = stacks.find(id);
+      std::string o = "{\"request\":" + std::to_string(id) + ",\"processes\":[";
+      bool first = true;
+      if (it != stacks.end())
+        for (auto& [who, text] : it->second) {
+          o += std::string(first ? "" : ",") + "{\"process\":\"" + json_escape(who) + "\",\"stacks\":\"" +
+               json_escape(text) + "\"}";
+          first = false;
+        }
+      resp.body = o + "]}";
+      return true;
+    }
     if (req.method == "GET" && path == "/v1/watch") {
       uint64_t since = 0;
       const auto q = req.path.find("since=");
@@ -969,7 +990,7 @@ struct Coordinator {
     if (req.method == "GET" && path == "/v1/openapi") {
       resp.body =
           "{\"openapi\":\"3.0.0\",\"info\":{\"title\":\"everserve coordinator\",\"version\":\"1\"},\"paths\":{"
-          "\"/v1/engines\":{\"get\":{}},\"/v1/engines/{name}\":{\"get\":{}},\"/v1/engines/{name}/events\":{\"get\":{}},\"/v1/engines/{name}/stacks\":{\"post\":{}},"
+          "\"/v1/engines\":{\"get\":{}},\"/v1/engines/{name}\":{\"get\":{}},\"/v1/engines/{name}/events\":{\"get\":{}},\"/v1/engines/{name}/stacks\":{\"post\":{}},\"/v1/stacks/{request}\":{\"get\":{}},"
           "\"/v1/nodes\":{\"get\":{}},\"/v1/nodes/{name}/{cordon|uncordon|drain|undrain}\":{\"put\":{}},"
           "\"/v1/watch\":{\"get\":{}}}}";
       return true;

@@ -50,6 +50,7 @@ struct Proc {
   uint32_t device = 0;
   bool registered = false;
   bool said_goodbye = false;
+  int32_t goodbye_cause = 0;   // the cause its Goodbye named (STOPPED when it named none)
   bool reported_gone = false;  // its departure was reported (by the process watcher or the close)
   int os_pid = 0;              // the peer's pid in this daemon's pid namespace (SO_PEERCRED), 0 unknown
   signals::Register reg;
@@ -516,6 +517,7 @@ struct Daemon {
       up(m);
     } else if (s.has_goodbye) {
       p.said_goodbye = true;
+      p.goodbye_cause = s.goodbye.cause ? s.goodbye.cause : signals::StopCause_STOP_CAUSE_STOPPED;
     } else if (s.has_group_formed || s.has_group_failed || s.has_group_released || s.has_group_ready) {
       coord::DaemonToCoord m;
       m.has_cover_report = true;
@@ -586,8 +588,7 @@ struct Daemon {
         break;
       }
     if (p.registered && p.role != signals::Role_ROLE_CLIENT && !p.reported_gone)
-      worker_event(p, departed_kind(p.role),
-                   p.said_goodbye ? signals::StopCause_STOP_CAUSE_STOPPED : signals::StopCause_STOP_CAUSE_LOST,
+      worker_event(p, departed_kind(p.role), p.said_goodbye ? p.goodbye_cause : signals::StopCause_STOP_CAUSE_LOST,
                    p.said_goodbye ? "goodbye" : "connection ended");
   }
 
