@@ -8,6 +8,7 @@
 #include <netinet/in.h>
 #include <netinet/tcp.h>
 #include <poll.h>
+#include <sys/eventfd.h>
 #include <sys/socket.h>
 #include <sys/un.h>
 #include <unistd.h>
@@ -217,6 +218,35 @@ void Loop::cancel(uint64_t timer) {
 }
 
 void Loop::watch(int fd, std::function<void()> on_readable) { watched_[fd] = std::move(on_readable); }
+
+Loop::Loop() {
+  wake_fd_ = ::eventfd(0, EFD_NONBLOCK | EFD_CLOEXEC);
+  if (wake_fd_ >= 0)
+    watch(wake_fd_, [this] {
+      uint64_t n;
+      while (::read(wake_fd_, &n, sizeof n) > 0) {
+      }
+      std::vector<std::function<void()>> tasks;
+      {
+        std::lock_guard<std::mutex> g(post_mu_);
+        tasks.swap(posted_);
+      }
+      for (auto& t : tasks) t();
+    });
+}
+
+Loop::~Loop() {
+  if (wake_fd_ >= 0) ::close(wake_fd_);
+}
+
+void Loop::post(std::function<void()> fn) {
+  {
+    std::lock_guard<std::mutex> g(post_mu_);
+    posted_.push_back(std::move(fn));
+  }
+  const uint64_t one = 1;
+  if (wake_fd_ >= 0) (void)!::write(wake_fd_, &one, sizeof one);
+}
 
 void Loop::flush_conn(Conn& c) {
   if (c.ssl) {

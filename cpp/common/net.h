@@ -8,6 +8,7 @@
 
 #include <cstdint>
 #include <functional>
+#include <mutex>
 #include <map>
 #include <memory>
 #include <string>
@@ -54,6 +55,10 @@ struct Conn {
 class Loop {
  public:
   using AcceptFn = std::function<void(Conn&)>;
+  Loop();
+  ~Loop();
+  Loop(const Loop&) = delete;
+  Loop& operator=(const Loop&) = delete;
   // Listen on `a`; each accepted connection is passed to `on_accept` to install its handlers.
   bool listen(const Address& a, AcceptFn on_accept, std::string* err = nullptr);
   // Adopt a connected socket (an outgoing link).
@@ -69,6 +74,8 @@ class Loop {
   void watch(int fd, std::function<void()> on_readable);
   void run();
   void stop() { running_ = false; }
+  // Run `fn` on the loop's thread (the one call that other threads may make).
+  void post(std::function<void()> fn);
 
  private:
   struct Listener {
@@ -91,6 +98,9 @@ class Loop {
   std::map<int, std::function<void()>> watched_;
   uint64_t next_id_ = 1;
   bool running_ = true;
+  int wake_fd_ = -1;  // eventfd: a posted task is waiting
+  std::mutex post_mu_;
+  std::vector<std::function<void()>> posted_;
 };
 
 }  // namespace es

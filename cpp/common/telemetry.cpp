@@ -1,16 +1,22 @@
-#include <algorithm>
-#include <cctype>
-#include <cstdlib>
 #include "telemetry.h"
-#include "tls.h"
 
+#include <fcntl.h>
 #include <poll.h>
 #include <sys/socket.h>
 #include <unistd.h>
 
+#include <algorithm>
+#include <atomic>
+#include <cctype>
+#include <chrono>
+#include <condition_variable>
+#include <cstdlib>
 #include <cstring>
+#include <memory>
+#include <thread>
 
 #include "net.h"
+#include "tls.h"
 
 namespace es {
 
@@ -150,8 +156,66 @@ static const char* reason(int s) {
     case 400: return "Bad Request";
     case 404: return "Not Found";
     case 409: return "Conflict";
+    case 500: return "Internal Server Error";
+    case 503: return "Service Unavailable";
     default: return "Error";
   }
+}
+
+// One connection: handshake, request, answer. /metrics and /healthz are answered here (the
+// registry has its own lock); a route runs on the loop's thread, since it reads the process's
+// state, and the connection waits for it at most 10 s.
+static void serve_http_conn(Loop* loop, int fd, HttpRoute route) {
+  tls::Stream st;
+  std::string terr;
+  if (!tls::accept_stream(fd, 5000, st, &terr)) return;  // HTTPS when TLS is configured
+  HttpRequest req;
+  HttpResponse resp;
+  if (!read_request(st, req)) {
+    st.close();
+    return;
+  }
+  const std::string path = req.path.substr(0, req.path.find('?'));
+  if (req.method == "GET" && path == "/metrics") {
+    resp.body = metrics().exposition();
+  } else if (req.method == "GET" && path == "/healthz") {
+    resp.body = "ok\n";
+  } else if (route) {
+    struct Pending {
+      std::mutex mu;
+      std::condition_variable cv;
+      bool done = false, handled = false;
+      HttpResponse resp;
+    };
+    auto pend = std::make_shared<Pending>();
+    loop->post([pend, route, req] {
+      HttpResponse r;
+      const bool h = route(req, r);
+      std::lock_guard<std::mutex> g(pend->mu);
+      pend->resp = std::move(r);
+      pend->handled = h;
+      pend->done = true;
+      pend->cv.notify_all();
+    });
+    std::unique_lock<std::mutex> lk(pend->mu);
+    if (!pend->cv.wait_for(lk, std::chrono::seconds(10), [&] { return pend->done; })) {
+      resp.status = 503;
+      resp.body = "busy\n";
+    } else if (pend->handled) {
+      resp = pend->resp;
+    } else {
+      resp.status = 404;
+      resp.body = "not found\n";
+    }
+  } else {
+    resp.status = 404;
+    resp.body = "not found\n";
+  }
+  std::string out = "HTTP/1.1 " + std::to_string(resp.status) + " " + reason(resp.status) +
+                    "\r\nContent-Type: " + resp.content_type + "\r\nContent-Length: " + std::to_string(resp.body.size()) +
+                    "\r\nConnection: close\r\n\r\n" + resp.body;
+  st.write_all(out, 5000);
+  st.close();
 }
 
 bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::string* err) {
@@ -162,35 +226,33 @@ bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::strin
   }
   const int lfd = listen_on(a, err);
   if (lfd < 0) return false;
-  loop.watch(lfd, [lfd, route]() {
-    while (true) {
+  // the listener blocks on its own thread; a slow client holds only its connection's thread,
+  // never the loop (whose latency is the control plane's)
+  const int flags = fcntl(lfd, F_GETFL, 0);
+  fcntl(lfd, F_SETFL, flags & ~O_NONBLOCK);
+  Loop* lp = &loop;
+  std::thread([lfd, lp, route] {
+    static std::atomic<int> active{0};
+    for (;;) {
       const int fd = ::accept4(lfd, nullptr, nullptr, SOCK_CLOEXEC);
-      if (fd < 0) return;
-      tls::Stream st;
-      std::string terr;
-      if (!tls::accept_stream(fd, 2000, st, &terr)) continue;  // HTTPS when TLS is configured
-      HttpRequest req;
-      HttpResponse resp;
-      if (!read_request(st, req)) {
-        st.close();
+      if (fd < 0) {
+        if (errno == EINTR || errno == ECONNABORTED || errno == EMFILE || errno == ENFILE) {
+          if (errno == EMFILE || errno == ENFILE) usleep(10000);
+          continue;
+        }
+        return;
+      }
+      if (active.load() >= 64) {  // bounded: beyond this, connections wait their turn here
+        serve_http_conn(lp, fd, route);
         continue;
       }
-      const std::string path = req.path.substr(0, req.path.find('?'));
-      if (req.method == "GET" && path == "/metrics") {
-        resp.body = metrics().exposition();
-      } else if (req.method == "GET" && path == "/healthz") {
-        resp.body = "ok\n";
-      } else if (!(route && route(req, resp))) {
-        resp.status = 404;
-        resp.body = "not found\n";
-      }
-      std::string out = "HTTP/1.1 " + std::to_string(resp.status) + " " + reason(resp.status) +
-                        "\r\nContent-Type: " + resp.content_type + "\r\nContent-Length: " + std::to_string(resp.body.size()) +
-                        "\r\nConnection: close\r\n\r\n" + resp.body;
-      st.write_all(out, 2000);
-      st.close();
+      active++;
+      std::thread([lp, fd, route] {
+        serve_http_conn(lp, fd, route);
+        active--;
+      }).detach();
     }
-  });
+  }).detach();
   return true;
 }
 

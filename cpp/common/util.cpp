@@ -5,7 +5,10 @@
 #include <errno.h>
 #include <fcntl.h>
 #include <sys/mman.h>
+#include <poll.h>
+#include <signal.h>
 #include <sys/stat.h>
+#include <sys/wait.h>
 #include <unistd.h>
 
 #include <cmath>
@@ -211,7 +214,7 @@ const Json* Json::get(const std::string& k) const {
 }
 
 bool Json::parse(const std::string& text, Json& out, std::string* err) {
-  JP p{text};
+  JP p{text, 0, {}};
   if (!p.value(out)) {
     if (err) *err = p.err;
     return false;
@@ -362,6 +365,58 @@ char proc_state(int pid) {
   const auto rp = s.rfind(')');
   if (rp == std::string::npos || rp + 2 >= s.size()) return 0;
   return s[rp + 2];
+}
+
+}  // namespace es
+
+namespace es {
+
+bool run_capture(const std::vector<std::string>& argv, int timeout_ms, std::string& out) {
+  if (argv.empty()) return false;
+  int fds[2];
+  if (pipe2(fds, O_CLOEXEC) != 0) return false;
+  const pid_t pid = fork();
+  if (pid < 0) {
+    ::close(fds[0]);
+    ::close(fds[1]);
+    return false;
+  }
+  if (pid == 0) {
+    dup2(fds[1], 1);
+    const int devnull = open("/dev/null", O_WRONLY);
+    if (devnull >= 0) dup2(devnull, 2);
+    std::vector<char*> a;
+    for (auto& s : argv) a.push_back(const_cast<char*>(s.c_str()));
+    a.push_back(nullptr);
+    execvp(a[0], a.data());
+    _exit(127);
+  }
+  ::close(fds[1]);
+  out.clear();
+  const uint64_t deadline = now_ms() + (uint64_t)timeout_ms;
+  bool timed_out = false;
+  char buf[4096];
+  for (;;) {
+    const int64_t left = (int64_t)deadline - (int64_t)now_ms();
+    if (left <= 0) {
+      timed_out = true;
+      break;
+    }
+    pollfd p{fds[0], POLLIN, 0};
+    const int r = poll(&p, 1, (int)left);
+    if (r < 0 && errno == EINTR) continue;
+    if (r <= 0) continue;
+    const ssize_t n = ::read(fds[0], buf, sizeof buf);
+    if (n < 0 && errno == EINTR) continue;
+    if (n <= 0) break;
+    out.append(buf, (size_t)n);
+  }
+  ::close(fds[0]);
+  if (timed_out) kill(pid, SIGKILL);
+  int status = 0;
+  while (waitpid(pid, &status, 0) < 0 && errno == EINTR) {
+  }
+  return !timed_out && WIFEXITED(status) && WEXITSTATUS(status) == 0;
 }
 
 }  // namespace es

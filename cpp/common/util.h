@@ -49,6 +49,9 @@ bool mkdirs(const std::string& path, int mode = 0770);
 bool read_file(const std::string& path, std::string& out);
 bool write_file_atomic(const std::string& path, const std::string& data);
 std::string env_or(const char* name, const std::string& dflt);
+// Run `argv` (PATH searched) and capture its standard output; false if it cannot start, exits
+// non-zero, or runs past `timeout_ms` (then it is killed).
+bool run_capture(const std::vector<std::string>& argv, int timeout_ms, std::string& out);
 
 // ---- processes -----------------------------------------------------------------------------------
 // /proc/<pid>/stat state: 'R','S','D','Z','X',... or 0 when the process does not exist.

@@ -31,6 +31,7 @@
 
 #include "cover.h"
 #include "everserve_pb.h"
+#include "topology.h"
 #include "net.h"
 #include "state.h"
 #include "telemetry.h"
@@ -64,7 +65,10 @@ struct Engine {
   uint64_t epoch = 0;
   uint32_t world = 0;
   std::map<uint32_t, Holder> workers;
-  std::vector<SpareSeat> spares;
+  std::vector<SpareSeat> spares;  // the admitted spares, in node and device order
+  // every spare that registered, by (node, device), and why those not admitted are refused
+  std::map<std::pair<std::string, uint32_t>, SpareSeat> standing;
+  std::map<std::pair<std::string, uint32_t>, std::string> refused;
   std::set<std::string> head_nodes;
   std::set<uint32_t> pending;
   std::set<uint32_t> departing;  // planned departures among pending
@@ -119,6 +123,11 @@ struct Coordinator {
   uint64_t event_seq = 0;
   // stack dumps by request: (node, pid) -> text, kept for the last 64 requests
   std::map<uint64_t, std::vector<std::pair<std::string, std::string>>> stacks;
+  Topology topo;  // every node's devices, from the daemons' hellos
+  std::map<std::string, PoolSpec> pools;
+  // pool spares launched and not yet registered: (node, device) -> (pool, launched at ms)
+  std::map<std::pair<std::string, uint32_t>, std::pair<std::string, uint64_t>> pool_launches;
+  uint64_t pool_warm_ms = 600000;  // a launch not registered within this is tried elsewhere
 
   void event(const std::string& text) {
     std::string eng;
@@ -333,6 +342,11 @@ struct Coordinator {
       e.spares.erase(std::remove_if(e.spares.begin(), e.spares.end(),
                                     [&](const SpareSeat& s) { return s.node == seat.node && s.device == seat.device; }),
                      e.spares.end());
+      e.standing.erase({seat.node, seat.device});
+      e.refused.erase({seat.node, seat.device});
+      // a pool spare stands for every engine of its pool: once one takes it, the others lose it
+      for (auto& [oname, other] : engines)
+        if (&other != &e && other.standing.erase({seat.node, seat.device})) admit(other);
     }
     e.epoch = f.change.epoch;
     coord::Committed c;
@@ -376,9 +390,11 @@ struct Coordinator {
     event("engine " + e.name + ": epoch " + std::to_string(e.epoch) + " committed in " + std::to_string(secs * 1e3) +
           " ms");
     e.in_flight.reset();
+    admit(e);
     update_gauges();
     replan(e);
     replicate(e);
+    reconcile_pools();
     drive(e);  // losses that arrived during the change
   }
 
@@ -401,6 +417,7 @@ struct Coordinator {
     e.in_flight.reset();
     e.pending.clear();
     event("engine " + e.name + ": change abandoned, engine down: " + why);
+    admit(e);
   }
 
   void update_gauges() {
@@ -499,6 +516,211 @@ struct Coordinator {
       m.replicate_targets.targets = targets;
       to_node(h.node, m);
     }
+  }
+
+  // ---- spare admission: identity, cordons, pools and the fit of the spare's device -------------
+  // Why the standing spare `s` may not take a rank of `e` now ("" when it may). A spare for one
+  // rank is held to that rank's device; a spare for any rank to every rank's.
+  std::string verdict(const Engine& e, const SpareSeat& s) const {
+    auto nit = nodes.find(s.node);
+    if (nit != nodes.end() && (nit->second.cordoned || nit->second.drain_by_ms))
+      return "node " + s.node + " is cordoned";
+    if (!e.fingerprint.empty() && !s.fingerprint.empty() && s.fingerprint != e.fingerprint)
+      return "another software identity (build, model, KV format or step configuration)";
+    const Device* dev = topo.device(s.node, s.device);
+    if (!s.pool.empty()) {
+      auto pit = pools.find(s.pool);
+      if (pit == pools.end()) return "pool " + s.pool + " no longer exists";
+      const PoolSpec& pool = pit->second;
+      if (std::find(pool.engines.begin(), pool.engines.end(), e.name) == pool.engines.end())
+        return "pool " + s.pool + " no longer holds spares for this engine";
+      if (dev != nullptr && !pool.device_class.empty() && dev->cls.find(pool.device_class) == std::string::npos)
+        return dev->cls + " is not the pool's class " + pool.device_class;
+      if (dev != nullptr && !pool.domain.empty() && dev->domain != pool.domain)
+        return "domain " + dev->domain + " is not the pool's " + pool.domain;
+    }
+    if (dev == nullptr) return "";  // its node reported no devices: nothing to hold it to
+    std::vector<uint32_t> ranks;
+    if (s.for_rank >= 0) ranks.push_back((uint32_t)s.for_rank);
+    else
+      for (auto& [r, h] : e.workers) ranks.push_back(r);
+    for (uint32_t r : ranks) {
+      auto w = e.workers.find(r);
+      if (w == e.workers.end()) continue;
+      const Device* held = topo.device(w->second.node, w->second.device);
+      if (held == nullptr) continue;
+      Position pos;
+      pos.engine = e.name;
+      pos.rank = r;
+      pos.cls = held->cls;
+      pos.domain = held->domain;
+      const Fit f = fit(pos, *dev);
+      if (!f.ok) return f.why;
+      if (f.same_class) continue;
+      char speed[48];
+      std::snprintf(speed, sizeof speed, " (speed %.2f)", f.speed);
+      if (!policy.spares.allow_mismatched)
+        return f.why + speed + ": the policy admits no mismatched spare";
+      if (!within_degrade(f, policy.spares.max_degrade_percent))
+        return f.why + speed + ": beyond the policy's degrade of " +
+               std::to_string(policy.spares.max_degrade_percent) + "%";
+    }
+    return "";
+  }
+
+  // Derive again which standing spares `e` admits; nothing moves while a change is in flight
+  // (its spares are spoken for).
+  void admit(Engine& e) {
+    if (e.in_flight) return;
+    std::set<std::pair<std::string, uint32_t>> before;
+    for (auto& sp : e.spares) before.insert({sp.node, sp.device});
+    std::vector<SpareSeat> next;
+    std::map<std::pair<std::string, uint32_t>, std::string> refused;
+    for (auto& [key, seat] : e.standing) {
+      const std::string why = verdict(e, seat);
+      const std::string where = seat.node + ":" + std::to_string(seat.device);
+      if (why.empty()) {
+        next.push_back(seat);
+        if (!before.count(key) && e.refused.count(key))
+          event("engine " + e.name + ": spare on " + where + " now qualifies; it stands");
+      } else {
+        refused[key] = why;
+        if (!e.refused.count(key) || e.refused[key] != why) {
+          metrics().inc("everserve_spares_refused_total", {{"engine", e.name}});
+          event("engine " + e.name + ": spare on " + where + " refused: " + why);
+        }
+      }
+    }
+    e.spares = std::move(next);
+    e.refused = std::move(refused);
+  }
+
+  void readmit_all() {
+    for (auto& [name, e] : engines) {
+      const size_t before = e.spares.size();
+      admit(e);
+      if (e.spares.size() != before) {
+        replan(e);
+        replicate(e);
+      }
+    }
+    update_gauges();
+  }
+
+  // ---- pools: spare capacity for engines of one shape ------------------------------------------
+  std::string pool_path(const std::string& name) const { return spec_dir + "/pools/" + name + ".json"; }
+
+  void load_pools() {
+    if (spec_dir.empty()) return;
+    for (auto& f : list_dir(spec_dir + "/pools")) {
+      if (f.size() < 6 || f.compare(f.size() - 5, 5, ".json") != 0) continue;
+      std::string text, err;
+      PoolSpec p;
+      if (read_file(spec_dir + "/pools/" + f, text) && parse_pool(text, p, err) && !p.name.empty()) pools[p.name] = p;
+    }
+  }
+
+  // Refuse a spec naming an engine the policy does not know, or engines of different shapes.
+  std::string check_pool(const PoolSpec& p) const {
+    if (p.name.empty() || p.name.find('/') != std::string::npos || p.name[0] == '.') return "a pool needs a plain name";
+    std::string shape;
+    for (auto& en : p.engines) {
+      auto ep = policy.engines.find(en);
+      if (ep == policy.engines.end()) return "the policy names no engine " + en;
+      const std::string sh = std::to_string(ep->second.tensor) + "x" + std::to_string(ep->second.pipeline) + "x" +
+                             std::to_string(ep->second.data);
+      auto e = engines.find(en);
+      const std::string fp = e != engines.end() ? e->second.fingerprint : "";
+      if (shape.empty()) shape = sh + "|" + fp;
+      else if (shape.substr(0, shape.find('|')) != sh ||
+               (!fp.empty() && shape.size() > sh.size() + 1 && shape.substr(sh.size() + 1) != fp))
+        return "the pool's engines differ in shape (" + en + ")";
+    }
+    return "";
+  }
+
+  struct PoolCount {
+    uint32_t standing = 0, warming = 0;
+  };
+  PoolCount pool_count(const std::string& name) const {
+    PoolCount c;
+    std::set<std::pair<std::string, uint32_t>> seen;
+    for (auto& [en, e] : engines)
+      for (auto& [key, seat] : e.standing)
+        if (seat.pool == name) seen.insert(key);
+    c.standing = (uint32_t)seen.size();
+    for (auto& [key, v] : pool_launches)
+      if (v.first == name) c.warming++;
+    return c;
+  }
+
+  // Launch what each pool is short of on free devices of linked, uncordoned nodes.
+  void reconcile_pools() {
+    const uint64_t now = now_ms();
+    for (auto it = pool_launches.begin(); it != pool_launches.end();)  // launches that never registered
+      it = now - it->second.second > pool_warm_ms ? pool_launches.erase(it) : std::next(it);
+    std::set<std::pair<std::string, uint32_t>> busy;
+    for (auto& [en, e] : engines) {
+      for (auto& [r, h] : e.workers) busy.insert({h.node, h.device});
+      for (auto& [key, seat] : e.standing) busy.insert(key);
+    }
+    for (auto& [key, v] : pool_launches) busy.insert(key);
+    for (auto& [name, ep] : policy.engines)
+      for (auto& slot : ep.spare_slots) busy.insert({slot.node, slot.device});
+    for (auto& [name, pool] : pools) {
+      if (pool.command.empty() || pool.engines.empty()) continue;
+      const PoolCount c = pool_count(name);
+      if (c.standing + c.warming >= pool.wants) continue;
+      std::vector<FreeDevice> free;
+      for (auto& [node, devs] : topo.all()) {
+        auto nit = nodes.find(node);
+        if (nit == nodes.end() || !nit->second.linked || nit->second.cordoned || nit->second.drain_by_ms) continue;
+        for (auto& d : devs)
+          if (!busy.count({node, d.index})) free.push_back({node, d.index, d.cls, d.domain});
+      }
+      for (auto& [node, device] : place_pool_spares(pool, free, pool.wants - c.standing - c.warming)) {
+        coord::CoordToDaemon m;
+        m.has_launch_spare = true;
+        auto& ls = m.launch_spare;
+        ls.pool = name;
+        ls.engines = pool.engines;
+        ls.engine = pool.engines.size() == 1 ? pool.engines[0] : "";
+        ls.device = device;
+        ls.command = pool.command;
+        ls.env = pool.env;
+        to_node(node, m);
+        pool_launches[{node, device}] = {name, now};
+        busy.insert({node, device});
+        event("pool " + name + ": spare launch asked of " + node + ":" + std::to_string(device));
+      }
+    }
+    for (auto& [name, pool] : pools) {
+      const PoolCount c = pool_count(name);
+      metrics().set("everserve_pool_spares", {{"pool", name}, {"state", "standing"}}, c.standing);
+      metrics().set("everserve_pool_spares", {{"pool", name}, {"state", "warming"}}, c.warming);
+    }
+  }
+
+  std::string pool_view_json(const PoolSpec& p) const {
+    const PoolCount c = pool_count(p.name);
+    const uint32_t have = c.standing + c.warming;
+    std::string spares = "[";
+    bool first = true;
+    std::set<std::pair<std::string, uint32_t>> seen;
+    for (auto& [en, e] : engines)
+      for (auto& [key, seat] : e.standing)
+        if (seat.pool == p.name && seen.insert(key).second) {
+          auto r = e.refused.find(key);
+          spares += std::string(first ? "" : ",") + "{\"node\":\"" + json_escape(key.first) + "\",\"device\":" +
+                    std::to_string(key.second) + ",\"refused\":\"" + json_escape(r == e.refused.end() ? "" : r->second) +
+                    "\"}";
+          first = false;
+        }
+    spares += "]";
+    return "{\"metadata\":{\"name\":\"" + json_escape(p.name) + "\",\"generation\":" + std::to_string(p.generation) +
+           "},\"spec\":" + pool_json(p) + ",\"status\":{\"standing\":" + std::to_string(c.standing) +
+           ",\"warming\":" + std::to_string(c.warming) + ",\"short\":" +
+           std::to_string(p.wants > have ? p.wants - have : 0) + ",\"spares\":" + spares + "}}";
   }
 
   // ---- spares the daemons launch ---------------------------------------------------------------
@@ -639,15 +861,16 @@ struct Coordinator {
         s.for_rank = ev.any_rank ? -1 : (int64_t)ev.rank;
         s.pid = ev.pid;
         s.fingerprint = fingerprint_of(ev);
-        // a daemon announces its processes again on every link: one seat per (node, device)
-        e.spares.erase(std::remove_if(e.spares.begin(), e.spares.end(),
-                                      [&](const SpareSeat& x) { return x.node == node && x.device == ev.device; }),
-                       e.spares.end());
-        if (!e.fingerprint.empty() && !s.fingerprint.empty() && s.fingerprint != e.fingerprint) {
+        auto pl = pool_launches.find({node, ev.device});
+        if (pl != pool_launches.end()) s.pool = pl->second.first;
+        for (auto& [pname, pool] : pools)  // a pool spare that outlived a restart of this process
+          if (s.pool.empty() && ev.any_rank &&
+              std::find(pool.engines.begin(), pool.engines.end(), e.name) != pool.engines.end())
+            s.pool = pname;
+        if (!e.fingerprint.empty() && !s.fingerprint.empty() && s.fingerprint != e.fingerprint)
           metrics().inc("everserve_spares_mismatched_total", {{"engine", e.name}});
-          event("engine " + e.name + ": spare on " + node + " has another software identity; it cannot take a rank");
-        }
-        e.spares.push_back(s);
+        // a daemon announces its processes again on every link: one seat per (node, device)
+        e.standing[{node, ev.device}] = s;
         break;
       }
       case K::WorkerEvent_Kind_HEAD_REGISTERED: e.head_nodes.insert(node); break;
@@ -660,6 +883,8 @@ struct Coordinator {
         break;
       }
       case K::WorkerEvent_Kind_SPARE_DEPARTED:
+        e.standing.erase({node, ev.device});
+        e.refused.erase({node, ev.device});
         e.spares.erase(std::remove_if(e.spares.begin(), e.spares.end(),
                                       [&](const SpareSeat& s) { return s.node == node && s.device == ev.device; }),
                        e.spares.end());
@@ -667,9 +892,12 @@ struct Coordinator {
       case K::WorkerEvent_Kind_HEAD_DEPARTED: e.head_nodes.erase(node); break;
       default: break;
     }
+    if (ev.kind == K::WorkerEvent_Kind_SPARE_REGISTERED) pool_launches.erase({node, ev.device});
+    admit(e);
     update_gauges();
     replan(e);
     replicate(e);
+    reconcile_pools();
   }
 
   void from_daemon(Conn& c, const std::string& frame) {
@@ -698,13 +926,26 @@ struct Coordinator {
       n.last_seen_ms = now_ms();
       n.heartbeat_ms = m.hello.heartbeat_ms ? m.hello.heartbeat_ms : 500;
       n.replica_address = m.hello.mirror_replica_address;
+      std::vector<Device> devs;
+      for (auto& d : m.hello.devices) {
+        Device dv;
+        dv.index = d.index;
+        dv.uuid = d.uuid;
+        dv.cls = d.class_;
+        dv.memory_bytes = d.memory_bytes;
+        dv.domain = d.domain;
+        devs.push_back(dv);
+      }
+      topo.set_node(node, std::move(devs));
       for (auto& st : m.hello.engines) {
         Engine& e = engine(st.engine);
         e.epoch = std::max(e.epoch, st.epoch);
       }
-      event("node " + node + " linked");
+      event("node " + node + " linked (" + std::to_string(m.hello.devices.size()) + " device(s))");
+      for (auto& [ename, en] : engines) admit(en);
       update_gauges();
       launch_spares(node);
+      reconcile_pools();
       loop.every(200, [this] {
         for (auto& [name, en] : engines) try_resume(en);
       }, false);
@@ -796,10 +1037,18 @@ struct Coordinator {
         if (h.node == node) ranks.push_back(r);
       e.spares.erase(std::remove_if(e.spares.begin(), e.spares.end(), [&](const SpareSeat& s) { return s.node == node; }),
                      e.spares.end());
+      for (auto it = e.standing.begin(); it != e.standing.end();)
+        it = it->first.first == node ? e.standing.erase(it) : std::next(it);
+      for (auto it = e.refused.begin(); it != e.refused.end();)
+        it = it->first.first == node ? e.refused.erase(it) : std::next(it);
       if (e.in_flight && e.in_flight->waiting.count(node)) abandon(e, "node " + node + " lost during the change");
       if (!ranks.empty()) report_loss(name, ranks, 0, "node lost");
     }
+    for (auto it = pool_launches.begin(); it != pool_launches.end();)
+      it = it->first.first == node ? pool_launches.erase(it) : std::next(it);
+    topo.remove_node(node);
     update_gauges();
+    reconcile_pools();
   }
 
   void check_heartbeats() {
@@ -839,10 +1088,21 @@ struct Coordinator {
     first = true;
     for (auto& sp : e.spares) {
       s += std::string(first ? "" : ",") + "{\"node\":\"" + json_escape(sp.node) + "\",\"device\":" +
-           std::to_string(sp.device) + ",\"forRank\":" + std::to_string(sp.for_rank) + "}";
+           std::to_string(sp.device) + ",\"forRank\":" + std::to_string(sp.for_rank) + ",\"pool\":\"" +
+           json_escape(sp.pool) + "\"}";
       first = false;
     }
     s += "]";
+    std::string refused = "[";
+    first = true;
+    for (auto& [key, why] : e.refused) {
+      const SpareSeat& seat = e.standing.at(key);
+      refused += std::string(first ? "" : ",") + "{\"node\":\"" + json_escape(key.first) + "\",\"device\":" +
+                 std::to_string(key.second) + ",\"forRank\":" + std::to_string(seat.for_rank) + ",\"why\":\"" +
+                 json_escape(why) + "\"}";
+      first = false;
+    }
+    refused += "]";
     // conditions, as an operator reads them
     const uint32_t world = e.world ? e.world : (uint32_t)e.workers.size();
     size_t covered = 0, replacements = 0;
@@ -880,7 +1140,7 @@ struct Coordinator {
     cov += "]}";
     return "{\"metadata\":{\"name\":\"" + json_escape(e.name) + "\"},\"status\":{\"epoch\":" + std::to_string(e.epoch) +
            ",\"worldSize\":" + std::to_string(e.world) + ",\"down\":" + (e.down ? "true" : "false") +
-           ",\"changing\":" + (e.in_flight ? "true" : "false") + ",\"workers\":" + w + ",\"spares\":" + s + ",\"cover\":" + cov + ",\"conditions\":" + conds + "}}";
+           ",\"changing\":" + (e.in_flight ? "true" : "false") + ",\"workers\":" + w + ",\"spares\":" + s + ",\"refusedSpares\":" + refused + ",\"cover\":" + cov + ",\"conditions\":" + conds + "}}";
   }
 
   bool api(const HttpRequest& req, HttpResponse& resp) {
@@ -896,7 +1156,7 @@ struct Coordinator {
       resp.body = o + "]}";
       return true;
     }
-    if (req.method == "GET" && path.rfind("/v1/engines/", 0) == 0) {
+    if (req.method == "GET" && path.rfind("/v1/engines/", 0) == 0 && path.find('/', 12) == std::string::npos) {
       const std::string name = path.substr(12);
       auto it = engines.find(name);
       if (it == engines.end()) return false;
@@ -907,9 +1167,18 @@ struct Coordinator {
       std::string o = "{\"items\":[";
       bool first = true;
       for (auto& [name, n] : nodes) {
+        std::string devs = "[";
+        if (const auto* ds = topo.node(name))
+          for (size_t i = 0; i < ds->size(); i++) {
+            const Device& d = (*ds)[i];
+            devs += std::string(i ? "," : "") + "{\"index\":" + std::to_string(d.index) + ",\"uuid\":\"" +
+                    json_escape(d.uuid) + "\",\"class\":\"" + json_escape(d.cls) + "\",\"memoryBytes\":" +
+                    std::to_string(d.memory_bytes) + ",\"domain\":\"" + json_escape(d.domain) + "\"}";
+          }
+        devs += "]";
         o += std::string(first ? "" : ",") + "{\"metadata\":{\"name\":\"" + json_escape(name) + "\"},\"spec\":{\"unschedulable\":" +
              (n.cordoned ? "true" : "false") + ",\"drainByMs\":" + std::to_string(n.drain_by_ms) + "},\"status\":{\"linked\":" +
-             (n.linked ? "true" : "false") + "}}";
+             (n.linked ? "true" : "false") + ",\"domain\":\"" + json_escape(topo.domain_of(name)) + "\",\"devices\":" + devs + "}}";
         first = false;
       }
       resp.body = o + "]}";
@@ -928,6 +1197,8 @@ struct Coordinator {
         drain(node, 0, "operator");
       } else if (verb == "undrain") n.drain_by_ms = 0;
       else return false;
+      readmit_all();
+      reconcile_pools();
       resp.body = "{\"node\":\"" + json_escape(node) + "\",\"done\":\"" + verb + "\"}";
       return true;
     }
@@ -987,11 +1258,84 @@ struct Coordinator {
       resp.body = "{\"requested\":" + std::to_string(m.stacks.request_id) + "}";
       return true;
     }
+    if (path == "/v1/pools" && req.method == "GET") {
+      std::string o = "{\"items\":[";
+      bool first = true;
+      for (auto& [name, p] : pools) {
+        o += (first ? "" : ",") + pool_view_json(p);
+        first = false;
+      }
+      resp.body = o + "]}";
+      return true;
+    }
+    if (path.rfind("/v1/pools/", 0) == 0) {
+      const std::string name = path.substr(10);
+      auto it = pools.find(name);
+      if (req.method == "GET") {
+        if (it == pools.end()) return false;
+        resp.body = pool_view_json(it->second);
+        return true;
+      }
+      if (req.method == "DELETE") {
+        if (it == pools.end()) return false;
+        pools.erase(it);
+        if (!spec_dir.empty()) ::unlink(pool_path(name).c_str());
+        metrics().inc("everserve_spec_writes_total", {{"kind", "pool"}, {"verdict", "deleted"}});
+        event("pool " + name + " deleted");
+        readmit_all();
+        resp.body = "{\"deleted\":\"" + json_escape(name) + "\"}";
+        return true;
+      }
+      if (req.method == "PUT") {
+        PoolSpec p;
+        std::string err;
+        if (!parse_pool(req.body, p, err)) {
+          resp.status = 400;
+          resp.body = "{\"error\":\"" + json_escape(err) + "\"}";
+          return true;
+        }
+        p.name = name;
+        const uint64_t held = it == pools.end() ? 0 : it->second.generation;
+        const auto q = req.path.find("generation=");
+        if (q != std::string::npos && std::stoull(req.path.substr(q + 11)) != held) {
+          resp.status = 409;
+          resp.body = "{\"error\":\"" + json_escape(name) + ": written against generation " + req.path.substr(q + 11) +
+                      ", and generation " + std::to_string(held) + " is held\"}";
+          return true;
+        }
+        const std::string why = check_pool(p);
+        if (!why.empty()) {
+          resp.status = 400;
+          resp.body = "{\"error\":\"" + json_escape(why) + "\"}";
+          metrics().inc("everserve_spec_writes_total", {{"kind", "pool"}, {"verdict", "refused"}});
+          return true;
+        }
+        p.generation = held + 1;
+        if (!spec_dir.empty()) {
+          mkdirs(spec_dir + "/pools");
+          if (!write_file_atomic(pool_path(name), pool_json(p))) {
+            resp.status = 500;
+            resp.body = "{\"error\":\"the spec store refused the write\"}";
+            return true;
+          }
+        }
+        pools[name] = p;
+        metrics().inc("everserve_spec_writes_total", {{"kind", "pool"}, {"verdict", "written"}});
+        event("pool " + name + " written (generation " + std::to_string(p.generation) + ", wants " +
+              std::to_string(p.wants) + ")");
+        readmit_all();
+        reconcile_pools();
+        resp.body = pool_view_json(p);
+        return true;
+      }
+      return false;
+    }
     if (req.method == "GET" && path == "/v1/openapi") {
       resp.body =
           "{\"openapi\":\"3.0.0\",\"info\":{\"title\":\"everserve coordinator\",\"version\":\"1\"},\"paths\":{"
           "\"/v1/engines\":{\"get\":{}},\"/v1/engines/{name}\":{\"get\":{}},\"/v1/engines/{name}/events\":{\"get\":{}},\"/v1/engines/{name}/stacks\":{\"post\":{}},\"/v1/stacks/{request}\":{\"get\":{}},"
           "\"/v1/nodes\":{\"get\":{}},\"/v1/nodes/{name}/{cordon|uncordon|drain|undrain}\":{\"put\":{}},"
+          "\"/v1/pools\":{\"get\":{}},\"/v1/pools/{name}\":{\"get\":{},\"put\":{},\"delete\":{}},"
           "\"/v1/watch\":{\"get\":{}}}}";
       return true;
     }
@@ -1081,6 +1425,7 @@ int main(int argc, char** argv) {
   }
   co.exit_after_log = env_or("EVERSERVE_COORD_EXIT_AFTER_LOG", "") == "1";
   co.load_spec();
+  co.load_pools();
   metrics().describe("everserve_changes_total", "Membership changes by engine, cause, outcome and verdict", "counter");
   metrics().describe("everserve_change_seconds", "From the first loss report to the commit", "histogram");
   metrics().describe("everserve_change_decision_seconds", "Time to choose an outcome", "histogram");
@@ -1096,6 +1441,8 @@ int main(int argc, char** argv) {
   metrics().describe("everserve_cover_form_seconds", "Time a member took to form a planned group", "histogram");
   metrics().describe("everserve_cover_failures_total", "Planned groups a member failed to form", "counter");
   metrics().describe("everserve_fenced_total", "Reports dropped as older than the engine's epoch", "counter");
+  metrics().describe("everserve_spares_refused_total", "Spares refused admission (identity, cordon, pool, device fit)", "counter");
+  metrics().describe("everserve_pool_spares", "Spares of each pool by state (standing, warming)", "gauge");
   metrics().describe("everserve_unheard_ranks_lost_total", "Loss reports naming ranks the coordinator does not hold", "counter");
   Address a;
   if (!Address::parse(listen, a) || !co.loop.listen(a, [&](Conn& c) {
@@ -1115,6 +1462,7 @@ int main(int argc, char** argv) {
     return 1;
   }
   co.loop.every(100, [&] { co.check_heartbeats(); });
+  co.loop.every(1000, [&] { co.reconcile_pools(); });
   ES_INFO("coordinator term %llu listening on %s", (unsigned long long)co.term, listen.c_str());
   co.loop.run();
   return 0;

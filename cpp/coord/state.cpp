@@ -44,6 +44,14 @@ bool parse_policy(const std::string& json, Policy& out, std::string& err) {
     if (const Json* en = cv->get("enabled")) out.cover_enabled = en->b;
     out.cover_max_groups_per_gpu = u32(cv->get("maxGroupsPerGpu"), 0);
   }
+  if (const Json* sp = j.get("spares")) {
+    out.spares.per_engine = u32(sp->get("perEngine"), 0);
+    if (const Json* l = sp->get("loading"))
+      out.spares.loading = l->kind == Json::Number ? (int32_t)l->num
+                           : l->str == "LOADING_PRELOADED" ? 1 : l->str == "LOADING_ON_NOTICE" ? 2 : 0;
+    if (const Json* am = sp->get("allowMismatched")) out.spares.allow_mismatched = am->b;
+    out.spares.max_degrade_percent = u32(sp->get("maxDegradePercent"), 0);
+  }
   if (const Json* es = j.get("engines")) {
     for (auto& e : es->arr) {
       EnginePolicy ep;
@@ -80,6 +88,70 @@ bool parse_policy(const std::string& json, Policy& out, std::string& err) {
     }
   }
   return true;
+}
+
+bool parse_pool(const std::string& json, PoolSpec& out, std::string& err) {
+  Json j;
+  if (!Json::parse(json, j, &err)) return false;
+  if (j.kind != Json::Object) {
+    err = "a pool spec is a JSON object";
+    return false;
+  }
+  out = PoolSpec{};
+  if (const Json* n = j.get("name")) out.name = n->str;
+  if (const Json* es = j.get("engines"))
+    for (auto& e : es->arr) out.engines.push_back(e.str);
+  out.wants = u32(j.get("wants"), 0);
+  if (const Json* c = j.get("deviceClass")) out.device_class = c->str;
+  if (const Json* d = j.get("domain")) out.domain = d->str;
+  if (const Json* r = j.get("reason")) out.reason = r->str;
+  if (const Json* c = j.get("command"))
+    for (auto& a : c->arr) out.command.push_back(a.str);
+  if (const Json* env = j.get("env"))
+    for (auto& [k, v] : env->obj) out.env[k] = v.str;
+  if (const Json* g = j.get("generation")) out.generation = g->kind == Json::Number ? (uint64_t)g->num : std::stoull(g->str);
+  return true;
+}
+
+std::string pool_json(const PoolSpec& p) {
+  auto list = [](const std::vector<std::string>& v) {
+    std::string o = "[";
+    for (size_t i = 0; i < v.size(); i++) o += (i ? ",\"" : "\"") + json_escape(v[i]) + "\"";
+    return o + "]";
+  };
+  std::string env = "{";
+  bool first = true;
+  for (auto& [k, v] : p.env) {
+    env += std::string(first ? "" : ",") + "\"" + json_escape(k) + "\":\"" + json_escape(v) + "\"";
+    first = false;
+  }
+  env += "}";
+  return "{\"name\":\"" + json_escape(p.name) + "\",\"engines\":" + list(p.engines) + ",\"wants\":" +
+         std::to_string(p.wants) + ",\"deviceClass\":\"" + json_escape(p.device_class) + "\",\"domain\":\"" +
+         json_escape(p.domain) + "\",\"reason\":\"" + json_escape(p.reason) + "\",\"command\":" + list(p.command) +
+         ",\"env\":" + env + ",\"generation\":" + std::to_string(p.generation) + "}";
+}
+
+std::vector<std::pair<std::string, uint32_t>> place_pool_spares(const PoolSpec& pool,
+                                                                 const std::vector<FreeDevice>& free, uint32_t count) {
+  std::map<std::string, std::vector<uint32_t>> by_node;
+  for (auto& d : free) {
+    if (!pool.device_class.empty() && d.cls.find(pool.device_class) == std::string::npos) continue;
+    if (!pool.domain.empty() && d.domain != pool.domain) continue;
+    by_node[d.node].push_back(d.device);
+  }
+  for (auto& [n, devs] : by_node) std::sort(devs.begin(), devs.end());
+  std::vector<std::pair<std::string, uint32_t>> out;
+  for (size_t round = 0; out.size() < count; round++) {
+    bool any = false;
+    for (auto& [n, devs] : by_node) {
+      if (round >= devs.size() || out.size() >= count) continue;
+      out.emplace_back(n, devs[round]);
+      any = true;
+    }
+    if (!any) break;
+  }
+  return out;
 }
 
 Choice choose_outcome(const Policy& p, const std::string& engine, const std::set<uint32_t>& lost,

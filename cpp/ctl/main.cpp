@@ -1,6 +1,7 @@
 // everserve-ctl: the operator's client of the coordinator's REST API.
 //
-//   everserve-ctl [--api host:port] get engines|nodes|engine NAME
+//   everserve-ctl [--api host:port] get engines|nodes|pools|engine NAME|pool NAME
+//   everserve-ctl [--api host:port] pool apply NAME FILE [--generation N] | pool delete NAME
 //   everserve-ctl [--api host:port] watch [--since N] [--once]
 //   everserve-ctl [--api host:port] cordon|uncordon|drain|undrain NODE
 //   everserve-ctl [--api host:port] stacks ENGINE
@@ -25,7 +26,8 @@ using namespace es;
 
 static int usage() {
   fprintf(stderr,
-          "usage: everserve-ctl [--api ADDR] get engines|nodes|engine NAME\n"
+          "usage: everserve-ctl [--api ADDR] get engines|nodes|pools|engine NAME|pool NAME\n"
+          "       everserve-ctl [--api ADDR] pool apply NAME FILE [--generation N] | pool delete NAME\n"
           "       everserve-ctl [--api ADDR] watch [--since N] [--once]\n"
           "       everserve-ctl [--api ADDR] cordon|uncordon|drain|undrain NODE\n"
           "       everserve-ctl [--api ADDR] stacks ENGINE\n"
@@ -36,9 +38,10 @@ static int usage() {
   return 2;
 }
 
-static int call(const std::string& api, const std::string& method, const std::string& path) {
+static int call(const std::string& api, const std::string& method, const std::string& path,
+                const std::string& body = "") {
   std::string out;
-  const int code = http_request(api, method, path, "", out);
+  const int code = http_request(api, method, path, body, out);
   if (code < 0) {
     fprintf(stderr, "cannot reach the coordinator at %s\n", api.c_str());
     return 1;
@@ -64,9 +67,27 @@ int main(int argc, char** argv) {
   }
   if (args.empty()) return usage();
   const std::string& verb = args[0];
+  if (verb == "pool") {
+    // a pool's spec (spec.v1.PoolSpec as proto3 JSON) written over the generation held, or only
+    // over `--generation N` when given
+    if (args.size() >= 3 && args[1] == "delete") return call(api, "DELETE", "/v1/pools/" + args[2]);
+    if (args.size() >= 4 && args[1] == "apply") {
+      std::string body;
+      if (!read_file(args[3], body)) {
+        fprintf(stderr, "cannot read %s\n", args[3].c_str());
+        return 1;
+      }
+      std::string path = "/v1/pools/" + args[2];
+      if (args.size() >= 6 && args[4] == "--generation") path += "?generation=" + args[5];
+      return call(api, "PUT", path, body);
+    }
+    return usage();
+  }
   if (verb == "get") {
-    if (args.size() >= 2 && (args[1] == "engines" || args[1] == "nodes")) return call(api, "GET", "/v1/" + args[1]);
+    if (args.size() >= 2 && (args[1] == "engines" || args[1] == "nodes" || args[1] == "pools"))
+      return call(api, "GET", "/v1/" + args[1]);
     if (args.size() >= 3 && args[1] == "engine") return call(api, "GET", "/v1/engines/" + args[2]);
+    if (args.size() >= 3 && args[1] == "pool") return call(api, "GET", "/v1/pools/" + args[2]);
     return usage();
   }
   if (verb == "cordon" || verb == "uncordon" || verb == "drain" || verb == "undrain") {

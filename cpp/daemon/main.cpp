@@ -2,9 +2,15 @@
 //
 //   everserve-node --node NAME --socket unix:/run/everserve/node.sock --coordinator ADDR
 //                  [--heartbeat-ms 500] [--metrics-addr host:port] [--ack-timeout-ms 120000]
-//                  [--mirror-socket ADDR] [--discovery-dir DIR]
+//                  [--mirror-socket ADDR] [--discovery-dir DIR] [--devices-from nvidia-smi|none|PROGRAM]
+//                  [--domain NAME]
 // Flags also read EVERSERVE_NODE, EVERSERVE_SOCKET, EVERSERVE_COORDINATOR, EVERSERVE_HEARTBEAT_MS,
-// EVERSERVE_METRICS_ADDR, EVERSERVE_MIRROR_SOCKET, EVERSERVE_DISCOVERY_DIR.
+// EVERSERVE_METRICS_ADDR, EVERSERVE_MIRROR_SOCKET, EVERSERVE_DISCOVERY_DIR, EVERSERVE_DEVICES_FROM,
+// EVERSERVE_DOMAIN.
+//
+// The node's GPUs (index, UUID, product name, memory) are listed once at start by
+// `nvidia-smi --query-gpu=...` (or another program answering the same query) and sent in every
+// hello; `--domain` names the NVLink domain they reach at full speed (default: the node).
 //
 // Processes of the node (workers, spares, heads, clients) connect to the Unix socket and speak
 // signals.proto. The daemon:
@@ -23,6 +29,8 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cctype>
+#include <cstring>
 #include <deque>
 #include <map>
 #include <random>
@@ -88,6 +96,47 @@ static bool proc_dying(int pid) {
   return false;
 }
 
+// The node's GPUs from `nvidia-smi --query-gpu=index,uuid,name,memory.total --format=csv,noheader,nounits`
+// (memory in MiB), run as `source` ("nvidia-smi", or another program that answers the same
+// query; "none" lists nothing). A node without the program, or whose listing fails, reports none.
+std::vector<coord::Device> list_devices(const std::string& source, const std::string& domain) {
+  std::vector<coord::Device> out;
+  if (source.empty() || source == "none") return out;
+  std::string text;
+  if (!run_capture({source, "--query-gpu=index,uuid,name,memory.total", "--format=csv,noheader,nounits"}, 20000,
+                   text)) {
+    ES_WARN("device listing by %s failed: this node reports no devices", source.c_str());
+    return out;
+  }
+  size_t start = 0;
+  while (start < text.size()) {
+    size_t end = text.find('\n', start);
+    if (end == std::string::npos) end = text.size();
+    std::string line = text.substr(start, end - start);
+    start = end + 1;
+    std::vector<std::string> f;
+    size_t a = 0;
+    for (;;) {
+      const size_t c = line.find(',', a);
+      std::string x = line.substr(a, c == std::string::npos ? std::string::npos : c - a);
+      while (!x.empty() && (x.front() == ' ' || x.front() == '\t')) x.erase(x.begin());
+      while (!x.empty() && (x.back() == ' ' || x.back() == '\r' || x.back() == '\t')) x.pop_back();
+      f.push_back(x);
+      if (c == std::string::npos) break;
+      a = c + 1;
+    }
+    if (f.size() < 4 || f[0].empty() || !std::isdigit((unsigned char)f[0][0])) continue;
+    coord::Device d;
+    d.index = (uint32_t)std::stoul(f[0]);
+    d.uuid = f[1];
+    d.class_ = f[2];
+    d.memory_bytes = std::isdigit((unsigned char)f[3].c_str()[0]) ? std::stoull(f[3]) << 20 : 0;
+    d.domain = domain;
+    out.push_back(d);
+  }
+  return out;
+}
+
 // A spare this daemon launched for the coordinator (LaunchSpare) and keeps running: a spare that
 // exits before it takes a rank is started again after a backoff (1 s, doubling to 30 s; reset
 // after a minute of running). One that took a rank is a worker and no longer supervised.
@@ -127,7 +176,8 @@ struct Daemon {
   std::string socket;  // this daemon's process socket (handed to the spares it launches)
   std::string replica_address;  // where this node's store takes replicated rows (announced in the hello)
   std::map<std::string, std::vector<std::string>> replicate_sent;  // engine:rank -> targets told to the store
-  std::map<std::string, Supervised> supervised;  // engine:device -> launched spare
+  std::map<std::string, Supervised> supervised;  // engine:device (or pool/<pool>:device) -> launched spare
+  std::vector<coord::Device> devices;            // this node's GPUs, announced in every hello
 
   // ---- up: to the coordinator ------------------------------------------------------------------
   void up(const coord::DaemonToCoord& m) {
@@ -159,6 +209,7 @@ struct Daemon {
     m.hello.protocol_oldest = signals::ProtocolOldest_PROTOCOL_OLDEST;
     m.hello.term = term;
     m.hello.mirror_replica_address = replica_address;
+    m.hello.devices = devices;
     std::set<std::string> engines;
     for (auto& [id, p] : procs)
       if (p.registered) engines.insert(p.engine);
@@ -641,7 +692,7 @@ struct Daemon {
 
   // ---- spares launched for the coordinator -----------------------------------------------------
   void launch_spare(const coord::LaunchSpare& spec) {
-    const std::string key = spec.engine + ":" + std::to_string(spec.device);
+    const std::string key = (spec.pool.empty() ? spec.engine : "pool/" + spec.pool) + ":" + std::to_string(spec.device);
     if (spec.command.empty()) return;
     auto it = supervised.find(key);
     if (it != supervised.end() && !it->second.taken) return;  // already standing (or starting)
@@ -651,11 +702,29 @@ struct Daemon {
     start_spare(supervised[key]);
   }
 
+  // `{pool}`, `{device}`, `{node}`, `{socket}`, `{engines}`, `{engine}` and `{rank}` in a launch's
+  // command and environment.
+  std::string fill(std::string s, const coord::LaunchSpare& spec) const {
+    std::string engines_csv;
+    for (size_t i = 0; i < spec.engines.size(); i++) engines_csv += (i ? "," : "") + spec.engines[i];
+    if (engines_csv.empty()) engines_csv = spec.engine;
+    const std::pair<const char*, std::string> subs[] = {
+        {"{pool}", spec.pool}, {"{device}", std::to_string(spec.device)}, {"{node}", node}, {"{socket}", socket},
+        {"{engines}", engines_csv}, {"{engine}", spec.engine}, {"{rank}", spec.has_rank ? std::to_string(spec.rank) : ""}};
+    for (auto& [k, v] : subs)
+      for (size_t at = s.find(k); at != std::string::npos; at = s.find(k, at + v.size())) s.replace(at, strlen(k), v);
+    return s;
+  }
+
   void start_spare(Supervised& sv) {
     std::vector<std::string> envs;
     for (char** e = environ; *e; e++) envs.emplace_back(*e);
     auto set = [&](const std::string& k, const std::string& v) { envs.push_back(k + "=" + v); };
-    for (auto& [k, v] : sv.spec.env) set(k, v);
+    for (auto& [k, v] : sv.spec.env) set(k, fill(v, sv.spec));
+    std::string engines_csv;
+    for (size_t i = 0; i < sv.spec.engines.size(); i++) engines_csv += (i ? "," : "") + sv.spec.engines[i];
+    set("EVERSERVE_ENGINES", engines_csv.empty() ? sv.spec.engine : engines_csv);
+    if (!sv.spec.pool.empty()) set("EVERSERVE_POOL", sv.spec.pool);
     set("EVERSERVE_ENGINE", sv.spec.engine);
     set("EVERSERVE_SPARE_RANK", sv.spec.has_rank ? std::to_string(sv.spec.rank) : "any");
     set("EVERSERVE_DEVICE", std::to_string(sv.spec.device));
@@ -670,8 +739,10 @@ struct Daemon {
     }
     if (pid == 0) {
       setpgid(0, 0);
+      std::vector<std::string> args;
+      for (auto& a : sv.spec.command) args.push_back(fill(a, sv.spec));
       std::vector<char*> argv, envp;
-      for (auto& a : sv.spec.command) argv.push_back(const_cast<char*>(a.c_str()));
+      for (auto& a : args) argv.push_back(const_cast<char*>(a.c_str()));
       argv.push_back(nullptr);
       for (auto& e : envs) envp.push_back(const_cast<char*>(e.c_str()));
       envp.push_back(nullptr);
@@ -754,6 +825,8 @@ int main(int argc, char** argv) {
   std::string notice_endpoint = env_or("EVERSERVE_NOTICE_ENDPOINT", "");
   uint32_t notice_interval = 1000;
   uint64_t proc_poll_ms = std::stoull(env_or("EVERSERVE_PROC_POLL_MS", "2"));
+  std::string devices_from = env_or("EVERSERVE_DEVICES_FROM", "nvidia-smi");
+  std::string domain = env_or("EVERSERVE_DOMAIN", "");
   for (int i = 1; i + 1 < argc; i += 2) {
     const std::string k = argv[i], v = argv[i + 1];
     if (k == "--node") d.node = v;
@@ -769,6 +842,8 @@ int main(int argc, char** argv) {
     else if (k == "--notice-source") notice_source = v;
     else if (k == "--notice-endpoint") notice_endpoint = v;
     else if (k == "--notice-interval-ms") notice_interval = (uint32_t)std::stoul(v);
+    else if (k == "--devices-from") devices_from = v;
+    else if (k == "--domain") domain = v;
     else {
       fprintf(stderr, "unknown flag %s\n", k.c_str());
       return 2;
@@ -776,6 +851,8 @@ int main(int argc, char** argv) {
   }
   d.instance = (now_us() << 8) ^ (uint64_t)getpid();
   d.socket = socket;
+  d.devices = list_devices(devices_from, domain);
+  ES_INFO("%zu device(s) on %s", d.devices.size(), d.node.c_str());
   metrics().describe("everserve_node_linked", "1 while the daemon is linked to the coordinator", "gauge");
   metrics().describe("everserve_node_workers", "Workers registered on this node", "gauge");
   Address a;

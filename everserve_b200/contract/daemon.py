@@ -228,13 +228,13 @@ class DaemonConnection(HearsEngine):
 
     # ---- the reader ------------------------------------------------------------------------------
     def _serve(self) -> None:
-        p = self.participant
         while not self._link.closed.is_set():
             try:
                 sig = self._link.recv()
             except (ConnectionError, OSError):
                 return
             kind = _kind(sig)
+            p = self.participant  # a spare for any rank hands its link to the rank it became
             try:
                 if kind == "change":
                     ch = sig.change

@@ -86,9 +86,12 @@ class ControlPlane:
     def __init__(self, workdir: str, engines: list[dict] | None = None, node: str = "n0", extra_nodes=(),
                  outcomes=("OUTCOME_REPLACE",), heartbeat_ms: int = 500, store_slots: int = 1 << 16,
                  store_budget: int = 8 << 30, ack_timeout_ms: int = 120000, cover: bool = True,
-                 standby: bool = False, coord_env: dict | None = None, node_args: list[str] | None = None):
+                 standby: bool = False, coord_env: dict | None = None, node_args: list[str] | None = None,
+                 node_extra: dict | None = None, policy_extra: dict | None = None):
         """`standby`: a second coordinator waits for the lease and takes over when the first
-        exits. `coord_env`: extra environment of the first coordinator."""
+        exits. `coord_env`: extra environment of the first coordinator. `node_args`: extra flags
+        of every daemon; `node_extra`: of one daemon, by node. `policy_extra`: more policy fields
+        (e.g. ``{"spares": {"allowMismatched": True}}``)."""
         self.dir = os.path.abspath(workdir)
         os.makedirs(self.dir, exist_ok=True)
         self.node = node
@@ -102,13 +105,15 @@ class ControlPlane:
         self.api = f"127.0.0.1:{free_port()}"
         self.policy_path = os.path.join(self.dir, "policy.json")
         with open(self.policy_path, "w") as f:
-            json.dump({"outcomesInOrder": list(outcomes), "engines": engines or [], "cover": {"enabled": cover}}, f)
+            json.dump({"outcomesInOrder": list(outcomes), "engines": engines or [], "cover": {"enabled": cover},
+                       **(policy_extra or {})}, f)
         self.heartbeat_ms = heartbeat_ms
         self.store_slots = store_slots
         self.store_budget = store_budget
         self.ack_timeout_ms = ack_timeout_ms
         self.standby = standby
         self.node_args = list(node_args or [])
+        self.node_extra = dict(node_extra or {})
         self.coord_env = coord_env or {}
         self.procs: dict[str, subprocess.Popen] = {}
         self._logs = []
@@ -141,7 +146,7 @@ class ControlPlane:
                       [binary("everserve-node"), "--node", n, "--socket", self.daemon_sockets[n],
                        "--coordinator", self.coord_socket, "--heartbeat-ms", str(self.heartbeat_ms),
                        "--ack-timeout-ms", str(self.ack_timeout_ms), "--mirror-socket", self.store_sockets[n],
-                       "--replica-address", self.replica_addrs[n]] + self.node_args)
+                       "--replica-address", self.replica_addrs[n]] + self.node_args + list(self.node_extra.get(n, [])))
         for n in self.nodes:
             wait_listening(self.store_sockets[n])
             wait_listening(self.daemon_sockets[n])
@@ -157,6 +162,19 @@ class ControlPlane:
         body = c.getresponse().read()
         c.close()
         return json.loads(body)
+
+    def request(self, method: str, path: str, body: dict | None = None) -> tuple[int, dict]:
+        """An operator API call: (status, JSON answer)."""
+        import http.client
+
+        host, _, port = self.api.rpartition(":")
+        c = http.client.HTTPConnection(host, int(port), timeout=5)
+        c.request(method, path, body=json.dumps(body) if body is not None else None,
+                  headers={"Content-Type": "application/json"})
+        r = c.getresponse()
+        data = r.read()
+        c.close()
+        return r.status, json.loads(data) if data else {}
 
     def engine_view(self, name: str) -> dict:
         return self.get(f"/v1/engines/{name}")
@@ -190,7 +208,11 @@ class ControlPlane:
             f.close()
 
     def __enter__(self) -> "ControlPlane":
-        return self.start()
+        try:
+            return self.start()
+        except BaseException:
+            self.stop()  # a binary that came up before the failure must not outlive the test
+            raise
 
     def __exit__(self, *exc) -> None:
         self.stop()

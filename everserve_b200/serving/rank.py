@@ -64,21 +64,34 @@ def _store(addr: str, timeout_s: float = 60.0):
     return dist.TCPStore(host, int(port), is_master=False, timeout=datetime.timedelta(seconds=timeout_s))
 
 
+def device_of(a: argparse.Namespace) -> torch.device:
+    dev = torch.device(a.device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    return dev
+
+
+def config_of(a: argparse.Namespace) -> EngineConfig:
+    """The engine configuration a rank process's arguments describe."""
+    return EngineConfig(model=a.model, device=str(device_of(a)), dtype=_DTYPES[a.dtype], seed=a.seed,
+                        block_size=a.block_size, num_blocks=a.num_blocks, max_batch=a.max_batch,
+                        max_model_len=a.max_model_len, tensor_parallel=a.tp, pipeline_parallel=a.pp,
+                        use_cuda_graphs=False, checkpoint=a.checkpoint)
+
+
 class RankProcess:
-    def __init__(self, a: argparse.Namespace):
+    def __init__(self, a: argparse.Namespace, daemon_link=None):
+        """`daemon_link`: the daemon connection of a spare that stood for any rank and was named
+        to take `a.rank`; this process answers on it instead of registering again."""
         self.a = a
+        self._link_device = daemon_link.device if daemon_link is not None else None
         self.engine = a.engine
         self.spare = a.role == "spare"
         self.rank = a.rank
         self.layout = ParallelLayout(a.tp, a.pp)
-        dev = torch.device(a.device)
-        if dev.type == "cuda" and dev.index is None:
-            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        dev = device_of(a)
         self.device = dev
-        self.cfg = EngineConfig(model=a.model, device=str(dev), dtype=_DTYPES[a.dtype], seed=a.seed,
-                                block_size=a.block_size, num_blocks=a.num_blocks, max_batch=a.max_batch,
-                                max_model_len=a.max_model_len, tensor_parallel=a.tp, pipeline_parallel=a.pp,
-                                use_cuda_graphs=False, checkpoint=a.checkpoint)
+        self.cfg = config_of(a)
         self.runtime = Runtime(self.rank)
         self.rdzv = _store(a.rdzv)
         self.groups = SwappableGroups(self.rdzv, self.rank, self.layout, dev, timeout_s=a.group_timeout)
@@ -116,13 +129,17 @@ class RankProcess:
         self.daemon = None
         self.cover = None
         self.key = f"R{self.rank}@{a.node}:{self.identity()[1]}" if self.spare else str(self.rank)
-        if a.daemon and a.pp > 1:
+        if (a.daemon or daemon_link is not None) and a.pp > 1:
             from ..runtime.cover import Cover
 
             self.cover = Cover(self.rdzv, self.key, self.engine, dev,
                                report=lambda r: self.daemon.report(r) if self.daemon is not None else None,
                                timeout_s=a.group_timeout)
-        if a.daemon:
+        if daemon_link is not None:
+            daemon_link.rank = self.rank
+            daemon_link.participant = self
+            self.daemon = daemon_link
+        elif a.daemon:
             from ..contract.identity import identity
 
             self.daemon = DaemonConnection(a.daemon, self.engine, self, role=sp.ROLE_SPARE if self.spare else sp.ROLE_WORKER,
@@ -215,6 +232,8 @@ class RankProcess:
 
     # ---- participant (daemon reader thread) ------------------------------------------------------
     def identity(self) -> tuple[int, int]:
+        if self._link_device is not None:  # the device the adopted link registered
+            return self.rank, self._link_device
         return self.rank, self.device.index or 0 if self.device.type == "cuda" else 0
 
     def on_change(self, change) -> str | None:
