@@ -270,13 +270,11 @@ static std::string dechunk(const std::string& b) {
   return out;
 }
 
-int http_request_ex(const std::string& addr, const std::string& method, const std::string& path,
-                    const std::vector<std::string>& headers, const std::string& body, std::string& out, int timeout_ms) {
-  Address a;
-  if (!Address::parse(addr, a)) return -1;
-  tls::Stream st;
-  if (!tls::connect_stream(a, timeout_ms, st, nullptr)) return -1;
-  std::string req = method + " " + path + " HTTP/1.1\r\nHost: " + a.host + "\r\nContent-Length: " +
+// One request over a connected stream; the answer's status (-1: none) and body.
+static int exchange(tls::Stream& st, const std::string& host, const std::string& method, const std::string& path,
+                    const std::vector<std::string>& headers, const std::string& body, std::string& out,
+                    int timeout_ms) {
+  std::string req = method + " " + path + " HTTP/1.1\r\nHost: " + host + "\r\nContent-Length: " +
                     std::to_string(body.size()) + "\r\nConnection: close\r\n";
   for (auto& h : headers) req += h + "\r\n";
   req += "\r\n" + body;
@@ -306,6 +304,43 @@ int http_request_ex(const std::string& addr, const std::string& method, const st
   out = resp.substr(be + 4);
   if (head.find("transfer-encoding: chunked") != std::string::npos) out = dechunk(out);
   return status;
+}
+
+int http_request_ex(const std::string& addr, const std::string& method, const std::string& path,
+                    const std::vector<std::string>& headers, const std::string& body, std::string& out, int timeout_ms) {
+  Address a;
+  if (!Address::parse(addr, a)) return -1;
+  tls::Stream st;
+  if (!tls::connect_stream(a, timeout_ms, st, nullptr)) return -1;
+  return exchange(st, a.host, method, path, headers, body, out, timeout_ms);
+}
+
+bool parse_url(const std::string& url, bool& https, std::string& hostport, std::string& path) {
+  std::string rest = url;
+  https = false;
+  if (rest.rfind("https://", 0) == 0) {
+    https = true;
+    rest = rest.substr(8);
+  } else if (rest.rfind("http://", 0) == 0) {
+    rest = rest.substr(7);
+  }
+  const auto slash = rest.find('/');
+  hostport = rest.substr(0, slash);
+  path = slash == std::string::npos ? "/" : rest.substr(slash);
+  if (hostport.empty()) return false;
+  if (hostport.find(':') == std::string::npos) hostport += https ? ":443" : ":80";
+  return true;
+}
+
+int http_url(const std::string& url, const std::string& method, const std::vector<std::string>& headers,
+             const std::string& body, std::string& out, int timeout_ms, const std::string& ca_file) {
+  bool https = false;
+  std::string hostport, path;
+  Address a;
+  if (!parse_url(url, https, hostport, path) || !Address::parse(hostport, a)) return -1;
+  tls::Stream st;
+  if (!tls::connect_web(a, https, ca_file, timeout_ms, st, nullptr)) return -1;
+  return exchange(st, a.host, method, path, headers, body, out, timeout_ms);
 }
 
 int http_request(const std::string& addr, const std::string& method, const std::string& path, const std::string& body,

@@ -60,4 +60,12 @@ int http_request_ex(const std::string& addr, const std::string& method, const st
                     const std::vector<std::string>& headers, const std::string& body, std::string& out,
                     int timeout_ms = 2000);
 
+// A request to a web endpoint outside the control plane (cloud metadata, the Kubernetes API):
+// `url` is http://host[:port]/path (plain) or https://... (server verified against `ca_file`,
+// the system's trust store when empty); never the cluster's mutual TLS.
+int http_url(const std::string& url, const std::string& method, const std::vector<std::string>& headers,
+             const std::string& body, std::string& out, int timeout_ms = 5000, const std::string& ca_file = "");
+// "http(s)://host[:port]/path" into its parts (the default port of the scheme when none).
+bool parse_url(const std::string& url, bool& https, std::string& hostport, std::string& path);
+
 }  // namespace es

@@ -11,6 +11,8 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 #include <cstdio>
 #include <cstdlib>
 
@@ -170,6 +172,56 @@ bool connect_stream(const Address& a, int timeout_ms, Stream& out, std::string* 
       out.close();
       return false;
     }
+  }
+  return true;
+}
+
+bool connect_web(const Address& a, bool https, const std::string& ca_file, int timeout_ms, Stream& out,
+                 std::string* err) {
+  out = Stream{};
+  out.fd = connect_to(a, timeout_ms, err);
+  if (out.fd < 0) return false;
+  if (!https) return true;
+  // one client context per CA file (the system's trust store for ""), made on first use
+  static std::mutex mu;
+  static std::map<std::string, SSL_CTX*> ctxs;
+  SSL_CTX* ctx = nullptr;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = ctxs.find(ca_file);
+    if (it != ctxs.end()) {
+      ctx = it->second;
+    } else {
+      ctx = SSL_CTX_new(TLS_client_method());
+      if (ctx) {
+        SSL_CTX_set_min_proto_version(ctx, TLS1_2_VERSION);
+        SSL_CTX_set_mode(ctx, SSL_MODE_ENABLE_PARTIAL_WRITE | SSL_MODE_ACCEPT_MOVING_WRITE_BUFFER);
+        const int ok = ca_file.empty() ? SSL_CTX_set_default_verify_paths(ctx)
+                                       : SSL_CTX_load_verify_locations(ctx, ca_file.c_str(), nullptr);
+        if (ok != 1) {
+          if (err) *err = "CA " + (ca_file.empty() ? std::string("(system)") : ca_file) + ": " + last_error();
+          SSL_CTX_free(ctx);
+          ctx = nullptr;
+        } else {
+          SSL_CTX_set_verify(ctx, SSL_VERIFY_PEER, nullptr);
+          ctxs[ca_file] = ctx;
+        }
+      }
+    }
+  }
+  if (!ctx) {
+    out.close();
+    return false;
+  }
+  SSL* s = SSL_new(ctx);
+  SSL_set_fd(s, out.fd);
+  SSL_set_connect_state(s);
+  SSL_set_tlsext_host_name(s, a.host.c_str());
+  SSL_set1_host(s, a.host.c_str());  // the certificate must name the host asked for
+  out.ssl = s;
+  if (!finish_handshake(out, timeout_ms, err)) {
+    out.close();
+    return false;
   }
   return true;
 }

@@ -52,6 +52,11 @@ struct Stream {
   void close();
 };
 bool connect_stream(const Address& a, int timeout_ms, Stream& out, std::string* err);
+// A client connection to a web endpoint outside the cluster's mutual TLS (a cloud metadata
+// service, the Kubernetes API): plain TCP, or TLS (1.2 or later) verifying the server against
+// `ca_file` (the system's trust store when empty) and the host name asked for.
+bool connect_web(const Address& a, bool https, const std::string& ca_file, int timeout_ms, Stream& out,
+                 std::string* err);
 // The server side of a blocking exchange on an accepted TCP fd (handshake bounded by timeout_ms).
 bool accept_stream(int fd, int timeout_ms, Stream& out, std::string* err);
 

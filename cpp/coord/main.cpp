@@ -3,6 +3,7 @@
 //   everserve-coord --listen unix:/run/everserve/coord.sock --policy policy.json --spec-store DIR
 //                   [--lease FILE] [--api-addr host:port] [--metrics-addr host:port]
 //                   [--node-loss-misses 3] [--delivery-timeout-ms 130000]
+//                   [--lease-holder NAME] [--lease-duration-s 15]   (--lease k8s:NS/NAME: a Kubernetes Lease)
 // Flags also read EVERSERVE_LISTEN, EVERSERVE_POLICY, EVERSERVE_SPEC_STORE, EVERSERVE_LEASE,
 // EVERSERVE_API_ADDR, EVERSERVE_METRICS_ADDR, EVERSERVE_NODE_LOSS_MISSES.
 //
@@ -28,9 +29,11 @@
 #include <deque>
 #include <map>
 #include <set>
+#include <thread>
 
 #include "cover.h"
 #include "everserve_pb.h"
+#include "lease.h"
 #include "topology.h"
 #include "net.h"
 #include "state.h"
@@ -47,6 +50,7 @@ struct Holder {
   uint32_t device = 0;
   uint32_t pid = 0;
   std::string host;
+  signals::CompileCache cache;  // the compile-cache pair its worker registered
 };
 
 struct InFlight {
@@ -395,6 +399,7 @@ struct Coordinator {
     replan(e);
     replicate(e);
     reconcile_pools();
+    send_placement(e);
     drive(e);  // losses that arrived during the change
   }
 
@@ -516,6 +521,48 @@ struct Coordinator {
       m.replicate_targets.targets = targets;
       to_node(h.node, m);
     }
+  }
+
+  // ---- placement: where each rank runs, its compile-cache pair and the stores that hold it -----
+  void send_placement(const Engine& e) {
+    coord::CoordToDaemon m;
+    m.has_engine_placement = true;
+    auto& pl = m.engine_placement;
+    pl.engine = e.name;
+    pl.epoch = e.epoch;
+    for (auto& [r, h] : e.workers) {
+      signals::RankPlacement p;
+      p.rank = r;
+      p.node = h.node;
+      p.device = h.device;
+      p.has_device = true;
+      p.host = h.host;
+      if (!h.cache.key.empty()) {
+        p.compile_cache = h.cache;
+        p.has_compile_cache = true;
+        std::set<std::string> holders;  // every node whose worker registered the same pair
+        for (auto& [r2, h2] : e.workers)
+          if (h2.cache.key == h.cache.key && h2.cache.digest == h.cache.digest) {
+            auto nit = nodes.find(h2.node);
+            if (nit != nodes.end() && !nit->second.replica_address.empty()) holders.insert(nit->second.replica_address);
+          }
+        p.cache_holders.assign(holders.begin(), holders.end());
+      }
+      pl.members.push_back(p);
+    }
+    for (auto& sp : e.spares) {
+      signals::SparePlacement s;
+      if (sp.for_rank >= 0) {
+        s.for_rank = (uint32_t)sp.for_rank;
+        s.has_for_rank = true;
+      }
+      s.node = sp.node;
+      s.device = sp.device;
+      pl.spares.push_back(s);
+    }
+    // every linked node: a spare for the engine may be starting anywhere
+    for (auto& [name, n] : nodes)
+      if (n.linked) to_node(name, m);
   }
 
   // ---- spare admission: identity, cordons, pools and the fit of the spare's device -------------
@@ -845,6 +892,7 @@ struct Coordinator {
         h.device = ev.device;
         h.pid = ev.pid;
         h.host = ev.host;
+        if (ev.has_compile_cache) h.cache = ev.compile_cache;
         e.workers[ev.rank] = h;
         if (e.fingerprint.empty()) e.fingerprint = fingerprint_of(ev);
         e.epoch = std::max(e.epoch, ev.epoch);
@@ -898,6 +946,7 @@ struct Coordinator {
     replan(e);
     replicate(e);
     reconcile_pools();
+    send_placement(e);
   }
 
   void from_daemon(Conn& c, const std::string& frame) {
@@ -946,6 +995,7 @@ struct Coordinator {
       update_gauges();
       launch_spares(node);
       reconcile_pools();
+      for (auto& [ename, en] : engines) send_placement(en);
       loop.every(200, [this] {
         for (auto& [name, en] : engines) try_resume(en);
       }, false);
@@ -1343,37 +1393,6 @@ struct Coordinator {
   }
 };
 
-// A lease on a file: an exclusive lock held for the process's life; the term it records goes up
-// by one with every holder.
-bool take_lease(const std::string& path, uint64_t& term, std::string& err) {
-  const int fd = ::open(path.c_str(), O_RDWR | O_CREAT, 0660);
-  if (fd < 0) {
-    err = "cannot open the lease " + path;
-    return false;
-  }
-  while (flock(fd, LOCK_EX | LOCK_NB) != 0) {
-    ES_INFO("waiting for the lease %s", path.c_str());
-    sleep(1);
-  }
-  std::string data;
-  char buf[4096];
-  ssize_t n;
-  while ((n = ::read(fd, buf, sizeof(buf))) > 0) data.append(buf, size_t(n));
-  coord::LeaseRecord rec;
-  if (!data.empty()) rec.parse(data);
-  rec.term += 1;
-  rec.holder = "pid" + std::to_string(getpid());
-  rec.renewed_at_ms = (int64_t)now_ms();
-  const std::string out = rec.serialize();
-  if (ftruncate(fd, 0) != 0 || pwrite(fd, out.data(), out.size(), 0) != (ssize_t)out.size()) {
-    err = "cannot write the lease";
-    return false;
-  }
-  fsync(fd);
-  term = rec.term;
-  return true;  // the fd stays open (and locked) until exit
-}
-
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -1394,6 +1413,8 @@ int main(int argc, char** argv) {
   std::string api_addr = env_or("EVERSERVE_API_ADDR", "");
   std::string metrics_addr = env_or("EVERSERVE_METRICS_ADDR", "");
   co.loss_misses = (uint32_t)std::stoul(env_or("EVERSERVE_NODE_LOSS_MISSES", "3"));
+  std::string lease_holder = env_or("EVERSERVE_LEASE_HOLDER", "");
+  uint32_t lease_duration_s = (uint32_t)std::stoul(env_or("EVERSERVE_LEASE_DURATION_S", "15"));
   for (int i = 1; i + 1 < argc; i += 2) {
     const std::string k = argv[i], v = argv[i + 1];
     if (k == "--listen") listen = v;
@@ -1404,6 +1425,8 @@ int main(int argc, char** argv) {
     else if (k == "--metrics-addr") metrics_addr = v;
     else if (k == "--node-loss-misses") co.loss_misses = (uint32_t)std::stoul(v);
     else if (k == "--delivery-timeout-ms") co.delivery_timeout_ms = std::stoull(v);
+    else if (k == "--lease-holder") lease_holder = v;
+    else if (k == "--lease-duration-s") lease_duration_s = (uint32_t)std::stoul(v);
     else {
       fprintf(stderr, "unknown flag %s\n", k.c_str());
       return 2;
@@ -1419,9 +1442,32 @@ int main(int argc, char** argv) {
   } else {
     co.policy.outcomes = {signals::Outcome_OUTCOME_REPLACE};
   }
-  if (!lease.empty() && !take_lease(lease, co.term, err)) {
-    ES_ERROR("%s", err.c_str());
-    return 1;
+  std::unique_ptr<Lease> held;
+  if (!lease.empty()) {
+    if (lease_holder.empty()) {
+      char host[256] = {0};
+      gethostname(host, sizeof(host) - 1);
+      lease_holder = std::string(host) + ":" + std::to_string(getpid());
+    }
+    held = make_lease(lease, lease_holder, lease_duration_s);
+    if (!held->acquire(co.term, err)) {
+      ES_ERROR("lease %s: %s", lease.c_str(), err.c_str());
+      return 1;
+    }
+    ES_INFO("lease %s held by %s, term %llu", lease.c_str(), lease_holder.c_str(), (unsigned long long)co.term);
+    if (const uint64_t every = held->renew_every_ms()) {
+      // renewed off the loop; a holder that lost its lease stops at once (a successor may write)
+      std::thread([every, &held, lease] {
+        for (;;) {
+          std::this_thread::sleep_for(std::chrono::milliseconds(every));
+          std::string e;
+          if (!held->renew(e)) {
+            ES_ERROR("lease %s lost: %s; exiting", lease.c_str(), e.c_str());
+            _exit(3);
+          }
+        }
+      }).detach();
+    }
   }
   co.exit_after_log = env_or("EVERSERVE_COORD_EXIT_AFTER_LOG", "") == "1";
   co.load_spec();

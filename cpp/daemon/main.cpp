@@ -3,7 +3,7 @@
 //   everserve-node --node NAME --socket unix:/run/everserve/node.sock --coordinator ADDR
 //                  [--heartbeat-ms 500] [--metrics-addr host:port] [--ack-timeout-ms 120000]
 //                  [--mirror-socket ADDR] [--discovery-dir DIR] [--devices-from nvidia-smi|none|PROGRAM]
-//                  [--domain NAME]
+//                  [--domain NAME] [--cache-wait-ms 600000]
 // Flags also read EVERSERVE_NODE, EVERSERVE_SOCKET, EVERSERVE_COORDINATOR, EVERSERVE_HEARTBEAT_MS,
 // EVERSERVE_METRICS_ADDR, EVERSERVE_MIRROR_SOCKET, EVERSERVE_DISCOVERY_DIR, EVERSERVE_DEVICES_FROM,
 // EVERSERVE_DOMAIN.
@@ -11,6 +11,9 @@
 // The node's GPUs (index, UUID, product name, memory) are listed once at start by
 // `nvidia-smi --query-gpu=...` (or another program answering the same query) and sent in every
 // hello; `--domain` names the NVLink domain they reach at full speed (default: the node).
+// A process's CacheWanted is answered once the coordinator's placement names its rank's
+// compile-cache pair: the node's store fetches the set from the stores holding it (CacheFetch),
+// then CacheReady (or CacheRefused with the reason; no pair within --cache-wait-ms).
 //
 // Processes of the node (workers, spares, heads, clients) connect to the Unix socket and speak
 // signals.proto. The daemon:
@@ -35,6 +38,7 @@
 #include <map>
 #include <random>
 #include <set>
+#include <thread>
 
 #include "everserve_pb.h"
 #include "frame.h"
@@ -178,6 +182,15 @@ struct Daemon {
   std::map<std::string, std::vector<std::string>> replicate_sent;  // engine:rank -> targets told to the store
   std::map<std::string, Supervised> supervised;  // engine:device (or pool/<pool>:device) -> launched spare
   std::vector<coord::Device> devices;            // this node's GPUs, announced in every hello
+  std::map<std::string, signals::EnginePlacement> placements;  // the coordinator's latest, by engine
+  // compile-cache asks waiting for their rank's pair to be placed (answered or refused by deadline)
+  struct CacheWait {
+    uint64_t conn = 0;
+    signals::CacheWanted want;
+    uint64_t deadline_ms = 0;
+  };
+  std::vector<CacheWait> cache_waits;
+  uint64_t cache_wait_ms = 600000;
 
   // ---- up: to the coordinator ------------------------------------------------------------------
   void up(const coord::DaemonToCoord& m) {
@@ -337,6 +350,8 @@ struct Daemon {
       s.engine_policy = m.engine_policy;
       to_engine(m.engine_policy.engine, s);
     } else if (m.has_engine_placement) {
+      placements[m.engine_placement.engine] = m.engine_placement;
+      answer_cache_waits(m.engine_placement.engine);
       signals::Signal s;
       s.has_engine_placement = true;
       s.engine_placement = m.engine_placement;
@@ -605,6 +620,13 @@ struct Daemon {
       m.stacks_sent.answered = true;
       m.stacks_sent.text = s.stacks_dumped.text.substr(0, 1 << 20);
       up(m);
+    } else if (s.has_cache_wanted) {
+      CacheWait w;
+      w.conn = c.id;
+      w.want = s.cache_wanted;
+      w.deadline_ms = now_ms() + cache_wait_ms;
+      cache_waits.push_back(w);
+      answer_cache_waits(w.want.engine);
     } else if (s.has_replay_ask || s.has_replay_offer) {
       coord::DaemonToCoord m;
       if (s.has_replay_ask) {
@@ -688,6 +710,87 @@ struct Daemon {
     if (write_frame(fd, req.serialize()) && read_frame(fd, reply, 2000)) replicate_sent[key] = t.targets;
     ::close(fd);
     ES_INFO("store of %s replicates %s to %zu target(s)", node.c_str(), key.c_str(), t.targets.size());
+  }
+
+  // ---- compile caches: a spare's rank's artifacts, fetched into this node's store ----------------
+  void cache_answer(uint64_t conn, const signals::CacheWanted& want, bool ok, const signals::CompileCache& pair,
+                    const std::string& why) {
+    signals::Signal s;
+    if (ok) {
+      s.has_cache_ready = true;
+      s.cache_ready.engine = want.engine;
+      s.cache_ready.rank = want.rank;
+      s.cache_ready.key = pair.key;
+      s.cache_ready.digest = pair.digest;
+    } else {
+      s.has_cache_refused = true;
+      s.cache_refused.engine = want.engine;
+      s.cache_refused.rank = want.rank;
+      s.cache_refused.reason = why;
+      ES_WARN("%s: rank %u's compile cache: %s", want.engine.c_str(), want.rank, why.c_str());
+    }
+    metrics().inc("everserve_node_cache_asks_total", {{"verdict", ok ? "ready" : "refused"}});
+    loop.send(conn, s.serialize());
+  }
+
+  // Answer the asks of `engine` whose rank's pair is placed (its set fetched by the node's store
+  // from the stores holding it, on a thread of its own), and refuse those past their deadline.
+  void answer_cache_waits(const std::string& engine) {
+    const uint64_t now = now_ms();
+    std::vector<CacheWait> keep;
+    for (auto& w : cache_waits) {
+      if (!procs.count(w.conn)) continue;  // the asker left
+      const signals::RankPlacement* rp = nullptr;
+      auto pit = placements.find(w.want.engine);
+      if (pit != placements.end())
+        for (auto& m : pit->second.members)
+          if (m.rank == w.want.rank && m.has_compile_cache && !m.compile_cache.key.empty()) rp = &m;
+      if (rp == nullptr) {
+        if (now >= w.deadline_ms) cache_answer(w.conn, w.want, false, {}, "no compile-cache pair placed for the rank in time");
+        else keep.push_back(w);
+        continue;
+      }
+      if (w.want.engine != engine && !engine.empty()) {
+        keep.push_back(w);
+        continue;
+      }
+      if (mirror_socket.empty()) {
+        cache_answer(w.conn, w.want, false, {}, "this node has no store to fetch it into");
+        continue;
+      }
+      mirror::MirrorRequest req;
+      req.has_cache_fetch = true;
+      req.cache_fetch.key = rp->compile_cache.key;
+      req.cache_fetch.digest = rp->compile_cache.digest;
+      req.cache_fetch.rank = w.want.rank;
+      req.cache_fetch.dp = w.want.dp;
+      req.cache_fetch.holders = rp->cache_holders;
+      const signals::CompileCache pair = rp->compile_cache;
+      const std::string store = mirror_socket;
+      const uint64_t conn = w.conn;
+      const signals::CacheWanted want = w.want;
+      const int timeout_ms = (int)std::max<int64_t>(1000, (int64_t)w.deadline_ms - (int64_t)now);
+      std::thread([this, req, pair, store, conn, want, timeout_ms] {
+        Address a;
+        std::string err, reply;
+        bool ok = false;
+        const int fd = Address::parse(store, a) ? connect_to(a, 2000, &err) : -1;
+        if (fd >= 0) {
+          mirror::MirrorReply r;
+          if (write_frame(fd, req.serialize()) && read_frame(fd, reply, timeout_ms) && r.parse(reply)) {
+            ok = r.error.empty();
+            err = r.error;
+          } else if (err.empty()) {
+            err = "the store did not answer";
+          }
+          ::close(fd);
+        }
+        loop.post([this, conn, want, ok, pair, err] {
+          if (procs.count(conn)) cache_answer(conn, want, ok, pair, err);
+        });
+      }).detach();
+    }
+    cache_waits = std::move(keep);
   }
 
   // ---- spares launched for the coordinator -----------------------------------------------------
@@ -785,6 +888,7 @@ struct Daemon {
   }
 
   void tick() {
+    if (!cache_waits.empty()) answer_cache_waits("");
     if (coord_conn != 0) {
       coord::DaemonToCoord m;
       m.has_heartbeat = true;
@@ -844,6 +948,7 @@ int main(int argc, char** argv) {
     else if (k == "--notice-interval-ms") notice_interval = (uint32_t)std::stoul(v);
     else if (k == "--devices-from") devices_from = v;
     else if (k == "--domain") domain = v;
+    else if (k == "--cache-wait-ms") d.cache_wait_ms = std::stoull(v);
     else {
       fprintf(stderr, "unknown flag %s\n", k.c_str());
       return 2;

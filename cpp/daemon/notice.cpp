@@ -5,6 +5,7 @@
 #include <chrono>
 #include <vector>
 
+#include "kube.h"
 #include "net.h"
 #include "telemetry.h"
 #include "util.h"
@@ -27,10 +28,21 @@ int64_t parse_time_ms(const std::string& s) {
 NoticeWatcher::NoticeWatcher(std::string source, std::string endpoint, std::string node, uint32_t interval_ms)
     : source_(std::move(source)), endpoint_(std::move(endpoint)), node_(std::move(node)), interval_ms_(interval_ms) {
   if (endpoint_.empty()) {
-    if (source_ == "aws" || source_ == "azure") endpoint_ = "169.254.169.254:80";
-    else if (source_ == "gcp") endpoint_ = "metadata.google.internal:80";
-    else if (source_ == "k8s") endpoint_ = "127.0.0.1:8001";
+    if (source_ == "aws" || source_ == "azure") endpoint_ = "http://169.254.169.254";
+    else if (source_ == "gcp") endpoint_ = "http://metadata.google.internal";
+  } else if (endpoint_.find("://") == std::string::npos) {
+    endpoint_ = "http://" + endpoint_;
   }
+}
+
+// A metadata endpoint is plain HTTP on the link-local network, never the cluster's mutual TLS.
+int NoticeWatcher::get(const std::string& method, const std::string& path, const std::vector<std::string>& headers,
+                       std::string& body) {
+  if (source_ == "k8s") {
+    const KubeClient k = endpoint_.empty() ? KubeClient::from_env() : KubeClient::at(endpoint_);
+    return k.request(method, path, "", body);
+  }
+  return http_url(endpoint_ + path, method, headers, "", body);
 }
 
 NoticeWatcher::~NoticeWatcher() {
@@ -74,11 +86,9 @@ bool NoticeWatcher::poll_once(NodeNoticeEvent& out) {
   out.source = source_;
   if (source_ == "aws") {
     std::string token;
-    if (http_request_ex(endpoint_, "PUT", "/latest/api/token", {"X-aws-ec2-metadata-token-ttl-seconds: 300"}, "",
-                        token) != 200)
+    if (get("PUT", "/latest/api/token", {"X-aws-ec2-metadata-token-ttl-seconds: 300"}, token) != 200)
       return false;
-    const int st = http_request_ex(endpoint_, "GET", "/latest/meta-data/spot/instance-action",
-                                   {"X-aws-ec2-metadata-token: " + token}, "", body);
+    const int st = get("GET", "/latest/meta-data/spot/instance-action", {"X-aws-ec2-metadata-token: " + token}, body);
     if (st != 200) return false;
     Json j;
     if (!Json::parse(body, j)) return false;
@@ -91,13 +101,13 @@ bool NoticeWatcher::poll_once(NodeNoticeEvent& out) {
   }
   if (source_ == "gcp") {
     const std::vector<std::string> h = {"Metadata-Flavor: Google"};
-    if (http_request_ex(endpoint_, "GET", "/computeMetadata/v1/instance/preempted", h, "", body) == 200 &&
+    if (get("GET", "/computeMetadata/v1/instance/preempted", h, body) == 200 &&
         body.find("TRUE") != std::string::npos) {
       out.detail = "preempted";
       out.deadline_ms = wall_ms() + 30000;
       return true;
     }
-    if (http_request_ex(endpoint_, "GET", "/computeMetadata/v1/instance/maintenance-event", h, "", body) == 200 &&
+    if (get("GET", "/computeMetadata/v1/instance/maintenance-event", h, body) == 200 &&
         !body.empty() && body.find("NONE") == std::string::npos) {
       out.detail = "maintenance " + body.substr(0, 64);
       out.deadline_ms = wall_ms() + 60000;
@@ -106,8 +116,7 @@ bool NoticeWatcher::poll_once(NodeNoticeEvent& out) {
     return false;
   }
   if (source_ == "azure") {
-    if (http_request_ex(endpoint_, "GET", "/metadata/scheduledevents?api-version=2020-07-01", {"Metadata: true"}, "",
-                        body) != 200)
+    if (get("GET", "/metadata/scheduledevents?api-version=2020-07-01", {"Metadata: true"}, body) != 200)
       return false;
     Json j;
     if (!Json::parse(body, j)) return false;
@@ -127,7 +136,7 @@ bool NoticeWatcher::poll_once(NodeNoticeEvent& out) {
     return false;
   }
   // k8s: the node object
-  if (http_request_ex(endpoint_, "GET", "/api/v1/nodes/" + node_, {"Accept: application/json"}, "", body) != 200)
+  if (get("GET", "/api/v1/nodes/" + node_, {}, body) != 200)
     return false;
   Json j;
   if (!Json::parse(body, j)) return false;

@@ -2,15 +2,17 @@
 //
 // A watcher polls one source on its own thread (the daemon's loop never blocks on HTTP) and
 // hands the loop each new notice once. Sources, with the endpoints they read (an
-// `--notice-endpoint host:port` replaces the well-known address, e.g. for a local fake):
+// `--notice-endpoint URL` or `host:port` replaces the well-known address, e.g. for a local fake;
+// metadata services are plain HTTP, never the cluster's mutual TLS):
 //   aws    IMDSv2: a session token (PUT /latest/api/token), then
 //          GET /latest/meta-data/spot/instance-action -> {"action": ..., "time": ISO-8601}
 //   gcp    GET /computeMetadata/v1/instance/preempted ("TRUE") and .../maintenance-event
 //          (anything but "NONE"); header Metadata-Flavor: Google; 30 s of notice
 //   azure  GET /metadata/scheduledevents?api-version=2020-07-01 (header Metadata: true):
 //          events of type Preempt, Terminate, Reboot or Redeploy; NotBefore is the deadline
-//   k8s    GET /api/v1/nodes/<node> through a plain-HTTP API endpoint (kubectl proxy): the node
-//          unschedulable, or tainted for deletion / termination
+//   k8s    GET /api/v1/nodes/<node> from the Kubernetes API (kube.h: in-cluster service account,
+//          EVERSERVE_KUBE_API, or kubectl proxy): the node unschedulable, or tainted for deletion /
+//          termination
 #pragma once
 
 #include <atomic>
@@ -18,6 +20,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
 namespace es {
 
@@ -39,6 +42,8 @@ class NoticeWatcher {
   bool poll_once(NodeNoticeEvent& out);
 
  private:
+  int get(const std::string& method, const std::string& path, const std::vector<std::string>& headers,
+          std::string& body);
   void run();
   std::string source_, endpoint_, node_;
   uint32_t interval_ms_;

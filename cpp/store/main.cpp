@@ -2,7 +2,7 @@
 //
 //   everserve-store --socket unix:/run/everserve/mirror.sock --data-dir /dev/shm/everserve/store
 //                   [--slots N] [--budget-bytes B] [--replica-listen host:port]
-//                   [--metrics-addr host:port] [--replication-queue-bytes Q]
+//                   [--metrics-addr host:port] [--replication-queue-bytes Q] [--compile-cache-dir DIR]
 // Every flag also reads an EVERSERVE_STORE_* environment variable.
 //
 // Workers speak mirror.proto over the Unix socket (Open, Prepare, Commit, Restore, Evicted,
@@ -21,11 +21,12 @@
 #include <mutex>
 #include <thread>
 
+#include "cache.h"
 #include "everserve_pb.h"
 #include "net.h"
-#include "tls.h"
 #include "storage.h"
 #include "telemetry.h"
+#include "tls.h"
 #include "util.h"
 
 using namespace es;
@@ -38,6 +39,7 @@ struct Options {
   size_t slots = 1 << 20;
   size_t budget = size_t(64) << 30;
   std::string replica_listen;
+  std::string cache_dir;  // the node's compile cache ("" keeps none)
   std::string metrics_addr;
   size_t queue_bytes = size_t(1) << 30;
 };
@@ -98,7 +100,7 @@ class Carrier {
   std::thread th_;
 };
 
-void handle(Storage& st, Carrier& carrier, Loop& loop, Conn& c, const std::string& frame) {
+void handle(Storage& st, Carrier& carrier, CompileCacheDir& cache, Loop& loop, Conn& c, const std::string& frame) {
   mirror::MirrorRequest req;
   mirror::MirrorReply rep;
   if (!req.parse(frame)) {
@@ -185,6 +187,30 @@ void handle(Storage& st, Carrier& carrier, Loop& loop, Conn& c, const std::strin
     }
   } else if (req.has_expect) {
     rep.has_done = true;
+  } else if (req.has_cache_manifest) {
+    if (cache.manifest(req.cache_manifest.key, req.cache_manifest.digest, rep.cache_manifest, err))
+      rep.has_cache_manifest = true;
+  } else if (req.has_cache_read) {
+    if (cache.read(req.cache_read, rep.cache_chunk.data, err)) rep.has_cache_chunk = true;
+  } else if (req.has_cache_fetch) {
+    // pulled from the holders on a thread of its own; the answer comes when the set is in place
+    const uint64_t conn = c.id;
+    const mirror::CacheFetch f = req.cache_fetch;
+    std::thread([&cache, &loop, conn, f] {
+      std::string e;
+      const uint64_t t = now_us();
+      const bool ok = cache.fetch(f, e);
+      metrics().inc("everserve_store_cache_fetches_total", {{"verdict", ok ? "ok" : "failed"}});
+      if (ok) metrics().observe("everserve_store_cache_fetch_seconds", {}, (now_us() - t) * 1e-6);
+      else ES_WARN("compile cache %s/%s: %s", f.key.c_str(), f.digest.c_str(), e.c_str());
+      loop.post([&loop, conn, ok, e] {
+        mirror::MirrorReply r;
+        if (ok) r.has_done = true;
+        r.error = ok ? "" : e;
+        loop.send(conn, r.serialize());
+      });
+    }).detach();
+    return;
   } else {
     err = "unsupported request";
   }
@@ -212,6 +238,7 @@ int main(int argc, char** argv) {
   o.replica_listen = env_or("EVERSERVE_STORE_REPLICA_LISTEN", "");
   o.metrics_addr = env_or("EVERSERVE_METRICS_ADDR", "");
   o.queue_bytes = std::stoull(env_or("EVERSERVE_STORE_REPLICATION_QUEUE_BYTES", std::to_string(o.queue_bytes)));
+  o.cache_dir = env_or("EVERSERVE_STORE_COMPILE_CACHE_DIR", "");
   for (int i = 1; i + 1 < argc; i += 2) {
     const std::string k = argv[i], v = argv[i + 1];
     if (k == "--socket") o.socket = v;
@@ -221,6 +248,7 @@ int main(int argc, char** argv) {
     else if (k == "--replica-listen") o.replica_listen = v;
     else if (k == "--metrics-addr") o.metrics_addr = v;
     else if (k == "--replication-queue-bytes") o.queue_bytes = std::stoull(v);
+    else if (k == "--compile-cache-dir") o.cache_dir = v;
     else {
       fprintf(stderr, "unknown flag %s\n", k.c_str());
       return 2;
@@ -234,15 +262,19 @@ int main(int argc, char** argv) {
   metrics().describe("everserve_store_replicated_total", "Replication parts a target acknowledged", "counter");
   metrics().describe("everserve_store_replication_dropped_total", "Replication parts dropped by the bounded queue", "counter");
   metrics().describe("everserve_store_replication_link_failures_total", "Failed sends to a replication target", "counter");
+  metrics().describe("everserve_store_cache_fetches_total", "Compile-cache fetches from holder stores, by verdict", "counter");
+  metrics().describe("everserve_store_cache_fetch_seconds", "Time to put a compile cache in place", "histogram");
   metrics().describe("everserve_store_replica_applied_total", "Replication parts applied from a source store", "counter");
   mkdirs(o.data_dir);
   Storage st(o.data_dir, o.slots, o.budget);
   Carrier carrier(o.queue_bytes);
+  CompileCacheDir cache(o.cache_dir);
+  if (cache.enabled()) mkdirs(o.cache_dir);
   Loop loop;
   Address a;
   std::string err;
   if (!Address::parse(o.socket, a) || !loop.listen(a, [&](Conn& c) {
-        c.on_frame = [&](Conn& cc, const std::string& f) { handle(st, carrier, loop, cc, f); };
+        c.on_frame = [&](Conn& cc, const std::string& f) { handle(st, carrier, cache, loop, cc, f); };
       }, &err)) {
     ES_ERROR("listen %s: %s", o.socket.c_str(), err.c_str());
     return 1;
@@ -250,7 +282,7 @@ int main(int argc, char** argv) {
   if (!o.replica_listen.empty()) {
     Address ra;
     if (!Address::parse(o.replica_listen, ra) || !loop.listen(ra, [&](Conn& c) {
-          c.on_frame = [&](Conn& cc, const std::string& f) { handle(st, carrier, loop, cc, f); };
+          c.on_frame = [&](Conn& cc, const std::string& f) { handle(st, carrier, cache, loop, cc, f); };
         }, &err)) {
       ES_ERROR("replica listen %s: %s", o.replica_listen.c_str(), err.c_str());
       return 1;

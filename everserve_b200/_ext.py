@@ -1,6 +1,7 @@
 """Loader of the compiled sm_100a kernels (``everserve_b200._C``).
 
-The extension is built in-tree (``python setup.py build_ext --inplace``). On a machine with a GPU a
+The extension is built in-tree (``python setup.py build_ext --inplace``), or, on a node without
+the build, fetched from another node's compile cache and named by ``ES_EXTENSION_PATH``. On a machine with a GPU a
 missing or broken extension is an error: no op silently runs another implementation on a CUDA
 tensor. CPU tensors use the PyTorch reference ops in :mod:`everserve_b200.ops.ref`, which are the
 CPU engine's arithmetic and the kernels' numerical oracle.
@@ -27,7 +28,18 @@ def load():
     if _ERR is not None:
         raise RuntimeError(f"everserve_b200._C is not available: {_ERR}") from _ERR
     try:
-        _C = importlib.import_module("everserve_b200._C")
+        path = os.environ.get("ES_EXTENSION_PATH", "")
+        if path:  # a build fetched from another node's compile cache
+            import importlib.util
+            import sys
+
+            spec = importlib.util.spec_from_file_location("everserve_b200._C", path)
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            sys.modules["everserve_b200._C"] = mod
+            _C = mod
+        else:
+            _C = importlib.import_module("everserve_b200._C")
     except Exception as e:  # noqa: BLE001 - re-raised with context below
         _ERR = e
         raise RuntimeError(

@@ -169,7 +169,7 @@ class DaemonConnection(HearsEngine):
 
     def __init__(self, path: str, engine: str, participant: Participant, role: int = sp.ROLE_WORKER,
                  any_rank: bool = False, stage: Sequence[int] = (), timeout_s: float = 10.0, node: str = "",
-                 identity=None):
+                 identity=None, compile_cache=None):
         super().__init__()
         self.engine_name = engine
         self.participant = participant
@@ -185,6 +185,8 @@ class DaemonConnection(HearsEngine):
                           stage=list(stage), member=sp.Member(node=self.node, device=device))
         if identity is not None:
             reg.identity.CopyFrom(identity)
+        if compile_cache is not None:  # the pair of the artifacts this process loads (compile_cache.py)
+            reg.compile_cache.CopyFrom(compile_cache)
         self._link.send(sp.Signal(register=reg))
         self._reader = threading.Thread(target=self._serve, name=f"daemon-{engine}-{rank}", daemon=True)
         self._reader.start()

@@ -105,6 +105,18 @@ class LlamaCore:
             if key[1] in set(attn_units):
                 self.kv[key] = rows.clone()
 
+    def mark(self) -> dict:
+        """The KV lengths now (rolled back to by ``rollback`` when an attempt is abandoned)."""
+        return {k: v.shape[0] for k, v in self.kv.items()}
+
+    def rollback(self, mark: dict) -> None:
+        for k in list(self.kv):
+            n = mark.get(k)
+            if n is None:
+                del self.kv[k]
+            elif self.kv[k].shape[0] != n:
+                self.kv[k] = self.kv[k][:n].clone()
+
     # ---- the forward ---------------------------------------------------------------------------
     def _slots_sum(self, parts: dict[int, torch.Tensor], n_units: int, T: int) -> torch.Tensor:
         buf = torch.zeros(n_units, T, self.H)

@@ -1,9 +1,11 @@
 """An exact committed-KV store for the reference tier, over multiprocessing connections.
 
 ``ExactStore`` serves, in a thread, what ranks commit: KV rows keyed by (layer, KV head, sequence)
-with the step and epoch that wrote them. Rows are kept as the exact tensors sent (no conversion).
-A commit from an epoch older than the store has seen for a rank is refused. ``restore`` returns a
-lost rank's rows for the heads a survivor absorbs. ``LoopbackCommittedKV`` is a rank's client.
+and by the step that wrote them. Rows are kept as the exact tensors sent (no conversion). A
+commit of a step the store holds replaces it (a re-run step writes the same rows again, never
+twice); a commit from an epoch older than the store has seen for a rank is refused. ``restore``
+returns a lost rank's rows for the heads a survivor absorbs, up to a step when one is given (a
+step the survivors did not accept is left out). ``LoopbackCommittedKV`` is a rank's client.
 
 Reference parity: core/everserve/reference/store.py:40-246 and committed.py:22-79 (a synchronous
 exact store for the CPU tier; the product path uses the C++ store).
@@ -22,7 +24,8 @@ class ExactStore:
         self._listener = Listener(address, authkey=authkey)
         self.address = self._listener.address
         self.authkey = authkey
-        self.rows: dict[tuple[int, int, int], torch.Tensor] = {}  # (layer, head, seq) -> [n, 2, d]
+        # (layer, head, seq) -> {step: [n, 2, d]}
+        self.rows: dict[tuple[int, int, int], dict[int, torch.Tensor]] = {}
         self.owner: dict[tuple[int, int, int], int] = {}
         self.epochs: dict[int, int] = {}
         self.steps: dict[int, int] = {}
@@ -55,16 +58,22 @@ class ExactStore:
                 raise ValueError(f"stale epoch {epoch} for rank {rank}")
             self.epochs[rank] = epoch
             for key, new in rows.items():
-                old = self.rows.get(key)
-                self.rows[key] = new.clone() if old is None else torch.cat([old, new])
+                self.rows.setdefault(key, {})[step] = new.clone()
                 self.owner[key] = rank
             self.steps[rank] = step
         return step
 
-    def _restore(self, heads: list) -> dict:
+    def _restore(self, heads: list, upto_step: int | None = None) -> dict:
         want = set(heads)
+        out = {}
         with self._lock:
-            return {k: v.clone() for k, v in self.rows.items() if k[1] in want}
+            for k, by_step in self.rows.items():
+                if k[1] not in want:
+                    continue
+                parts = [by_step[s] for s in sorted(by_step) if upto_step is None or s <= upto_step]
+                if parts:
+                    out[k] = torch.cat(parts)
+        return out
 
     def _moved(self, heads: list, rank: int) -> int:
         """The heads now belong to `rank` (its later commits extend their rows)."""
@@ -97,8 +106,8 @@ class LoopbackCommittedKV:
     def commit(self, rank: int, epoch: int, step: int, rows: dict) -> int:
         return self._call("commit", rank, epoch, step, rows)
 
-    def restore(self, heads) -> dict:
-        return self._call("restore", list(heads))
+    def restore(self, heads, upto_step: int | None = None) -> dict:
+        return self._call("restore", list(heads), upto_step)
 
     def close(self) -> None:
         self._conn.close()

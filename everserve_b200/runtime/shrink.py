@@ -49,6 +49,10 @@ class ShrinkableGroup:
         self.pg.allreduce([t]).wait()
         return t
 
+    def all_reduce_async(self, t):
+        """The collective's work handle (``is_completed`` / ``wait``)."""
+        return self.pg.allreduce([t])
+
     def shrink(self, lost, epoch: int) -> None:
         if hasattr(self.pg, "abort"):
             try:

@@ -100,6 +100,7 @@ class ControlPlane:
         self.daemon_sockets = {n: f"unix:{self.dir}/{n}.sock" for n in self.nodes}
         self.store_sockets = {n: f"unix:{self.dir}/store-{n}.sock" for n in self.nodes}
         self.replica_addrs = {n: f"127.0.0.1:{free_port()}" for n in self.nodes}
+        self.cache_dirs = {n: os.path.join(self.dir, f"compile-cache-{n}") for n in self.nodes}
         self.daemon_socket = self.daemon_sockets[node]
         self.store_socket = self.store_sockets[node]
         self.api = f"127.0.0.1:{free_port()}"
@@ -133,7 +134,7 @@ class ControlPlane:
                       [binary("everserve-store"), "--socket", self.store_sockets[n], "--data-dir",
                        os.path.join(self.dir, "store" if n == self.node else f"store-{n}"), "--slots",
                        str(self.store_slots), "--budget-bytes", str(self.store_budget), "--replica-listen",
-                       self.replica_addrs[n]])
+                       self.replica_addrs[n], "--compile-cache-dir", self.cache_dirs[n]])
         coord = [binary("everserve-coord"), "--listen", self.coord_socket, "--policy", self.policy_path,
                  "--spec-store", os.path.join(self.dir, "spec"), "--lease", os.path.join(self.dir, "lease"),
                  "--api-addr", self.api]
@@ -146,7 +147,8 @@ class ControlPlane:
                       [binary("everserve-node"), "--node", n, "--socket", self.daemon_sockets[n],
                        "--coordinator", self.coord_socket, "--heartbeat-ms", str(self.heartbeat_ms),
                        "--ack-timeout-ms", str(self.ack_timeout_ms), "--mirror-socket", self.store_sockets[n],
-                       "--replica-address", self.replica_addrs[n]] + self.node_args + list(self.node_extra.get(n, [])))
+                       "--replica-address", self.replica_addrs[n]] + self.node_args + list(self.node_extra.get(n, [])),
+                      {"EVERSERVE_COMPILE_CACHE": self.cache_dirs[n]})
         for n in self.nodes:
             wait_listening(self.store_sockets[n])
             wait_listening(self.daemon_sockets[n])

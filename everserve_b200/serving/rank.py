@@ -142,9 +142,19 @@ class RankProcess:
         elif a.daemon:
             from ..contract.identity import identity
 
+            pair = None
+            cache_dir = os.environ.get("EVERSERVE_COMPILE_CACHE", "")
+            if cache_dir and not self.spare:
+                # the kernel build this worker loads, published for spares on nodes without it
+                from ..contract.compile_cache import publish
+
+                try:
+                    pair = publish(cache_dir)
+                except OSError as e:
+                    self.runtime.trace("compile cache not published", why=str(e))
             self.daemon = DaemonConnection(a.daemon, self.engine, self, role=sp.ROLE_SPARE if self.spare else sp.ROLE_WORKER,
                                            stage=[self.layout.stage(self.rank)], node=a.node,
-                                           identity=identity(self.cfg, self.engine))
+                                           identity=identity(self.cfg, self.engine), compile_cache=pair)
 
     def _build_worker(self, coll=None, weights=None) -> None:
         a, mc = self.a, self.cfg.model

@@ -82,6 +82,8 @@ class AnyRankStand:
         self.node = os.environ.get("EVERSERVE_NODE", "")
         self.device = int(os.environ.get("EVERSERVE_DEVICE", "0"))
         self.records = {e: fetch_startup(daemon, e, 0, timeout_s) for e in engines}
+        if any(r.get("gpu") for r in self.records.values()):
+            ensure_build(daemon, engines[0], 0)  # every rank of an engine loads the same build
         self.became = None  # the RankProcess it became
         self.error = ""
         self.done = threading.Event()
@@ -147,6 +149,19 @@ class _Seat:
         pass
 
 
+def ensure_build(daemon: str, engine: str, rank: int) -> None:
+    """A spare on a node without the kernel build (or told to fetch it) takes its rank's from the
+    node's compile cache, fetched by the daemon from the stores that hold it."""
+    from .. import _ext
+    from ..contract import compile_cache
+
+    cache_dir = os.environ.get("EVERSERVE_COMPILE_CACHE", "")
+    if not cache_dir or (_ext.available() and os.environ.get("EVERSERVE_FETCH_COMPILE_CACHE") != "1"):
+        return
+    ready = compile_cache.want(daemon, engine, rank)
+    compile_cache.load_from_cache(cache_dir, ready)
+
+
 def main() -> int:
     daemon = os.environ["EVERSERVE_SOCKET"]
     rank_s = os.environ.get("EVERSERVE_SPARE_RANK", "any")
@@ -156,6 +171,8 @@ def main() -> int:
     if rank_s.isdigit():
         rank = int(rank_s)
         rec = fetch_startup(daemon, engines[0], rank)
+        if rec.get("gpu"):
+            ensure_build(daemon, engines[0], rank)
         return rank_main(_rank_argv(rec, rank, daemon))
     stand = AnyRankStand(engines, daemon)
     stand.done.wait()
