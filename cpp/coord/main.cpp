@@ -34,6 +34,7 @@
 #include "cover.h"
 #include "everserve_pb.h"
 #include "lease.h"
+#include "spec_store.h"
 #include "topology.h"
 #include "net.h"
 #include "state.h"
@@ -114,7 +115,8 @@ struct Event {
 struct Coordinator {
   Loop loop;
   Policy policy;
-  std::string spec_dir;
+  std::string spec_dir;               // the --spec-store flag
+  std::unique_ptr<SpecStore> spec;    // nullptr: nothing outlives this process
   uint64_t term = 1;
   uint32_t loss_misses = 3;
   uint64_t delivery_timeout_ms = 130000;
@@ -165,10 +167,8 @@ struct Coordinator {
   }
 
   // ---- spec store ------------------------------------------------------------------------------
-  std::string status_path(const std::string& engine) const { return spec_dir + "/" + engine + ".status"; }
-
   void write_status(const Engine& e, const InFlight* f, const coord::Committed* committed) {
-    if (spec_dir.empty()) return;
+    if (!spec) return;
     spec::EngineStatus st;
     st.engine = e.name;
     for (auto& [r, h] : e.workers) {
@@ -198,10 +198,33 @@ struct Coordinator {
         st.change.has_committed = true;
       }
     }
-    mkdirs(spec_dir);
-    if (!write_file_atomic(status_path(e.name), st.serialize()))
-      ES_ERROR("cannot write the spec store at %s", spec_dir.c_str());
+    if (!spec->put(e.name + ".status", st.serialize()))
+      ES_ERROR("cannot write the spec store at %s", spec->where().c_str());
     metrics().inc("everserve_spec_writes_total");
+  }
+
+  void write_node(const Node& n) {
+    if (!spec) return;
+    const std::string j = "{\"node\":\"" + json_escape(n.name) + "\",\"unschedulable\":" +
+                          (n.cordoned ? "true" : "false") + ",\"drainByMs\":" + std::to_string(n.drain_by_ms) + "}";
+    if (!spec->put("nodes/" + n.name + ".json", j)) ES_ERROR("cannot write node %s's spec", n.name.c_str());
+    metrics().inc("everserve_spec_writes_total", {{"kind", "node"}, {"verdict", "written"}});
+  }
+
+  void load_nodes() {
+    std::map<std::string, std::string> all;
+    if (!spec || !spec->list("nodes/", all)) return;
+    for (auto& [key, text] : all) {
+      Json j;
+      std::string err;
+      if (!Json::parse(text, j, &err)) continue;
+      const Json* name = j.get("node");
+      if (!name || name->str.empty()) continue;
+      Node& n = nodes[name->str];
+      n.name = name->str;
+      if (const Json* u = j.get("unschedulable")) n.cordoned = u->b;
+      if (const Json* d = j.get("drainByMs")) n.drain_by_ms = (int64_t)d->num;
+    }
   }
 
   // ---- the transition machine ------------------------------------------------------------------
@@ -438,13 +461,12 @@ struct Coordinator {
 
   // ---- takeover: views from the spec store and the daemons' announcements ----------------------
   void load_spec() {
-    if (spec_dir.empty()) return;
-    std::vector<std::string> files = list_dir(spec_dir);
-    for (auto& f : files) {
-      if (f.size() < 8 || f.compare(f.size() - 7, 7, ".status") != 0) continue;
-      std::string data;
+    std::map<std::string, std::string> all;
+    if (!spec || !spec->list("", all)) return;
+    for (auto& [f, data] : all) {
+      if (f.find('/') != std::string::npos || f.size() < 8 || f.compare(f.size() - 7, 7, ".status") != 0) continue;
       spec::EngineStatus st;
-      if (!read_file(spec_dir + "/" + f, data) || !st.parse(data) || st.engine.empty()) continue;
+      if (!st.parse(data) || st.engine.empty()) continue;
       Engine& e = engine(st.engine);
       for (auto& a : st.assignments) e.epoch = std::max(e.epoch, a.epoch);
       if (st.has_change && st.change.has_change) {
@@ -655,15 +677,13 @@ struct Coordinator {
   }
 
   // ---- pools: spare capacity for engines of one shape ------------------------------------------
-  std::string pool_path(const std::string& name) const { return spec_dir + "/pools/" + name + ".json"; }
-
   void load_pools() {
-    if (spec_dir.empty()) return;
-    for (auto& f : list_dir(spec_dir + "/pools")) {
-      if (f.size() < 6 || f.compare(f.size() - 5, 5, ".json") != 0) continue;
-      std::string text, err;
+    std::map<std::string, std::string> all;
+    if (!spec || !spec->list("pools/", all)) return;
+    for (auto& [key, text] : all) {
+      std::string err;
       PoolSpec p;
-      if (read_file(spec_dir + "/pools/" + f, text) && parse_pool(text, p, err) && !p.name.empty()) pools[p.name] = p;
+      if (parse_pool(text, p, err) && !p.name.empty()) pools[p.name] = p;
     }
   }
 
@@ -1114,7 +1134,9 @@ struct Coordinator {
 
   void drain(const std::string& node, int64_t deadline_ms, const std::string& why) {
     Node& n = nodes[node];
+    n.name = node;
     n.drain_by_ms = deadline_ms ? deadline_ms : (int64_t)now_ms();
+    write_node(n);
     event("node " + node + " draining (" + why + ")");
     for (auto& [name, e] : engines) {
       std::vector<uint32_t> ranks;
@@ -1247,6 +1269,7 @@ struct Coordinator {
         drain(node, 0, "operator");
       } else if (verb == "undrain") n.drain_by_ms = 0;
       else return false;
+      write_node(n);
       readmit_all();
       reconcile_pools();
       resp.body = "{\"node\":\"" + json_escape(node) + "\",\"done\":\"" + verb + "\"}";
@@ -1329,7 +1352,7 @@ struct Coordinator {
       if (req.method == "DELETE") {
         if (it == pools.end()) return false;
         pools.erase(it);
-        if (!spec_dir.empty()) ::unlink(pool_path(name).c_str());
+        if (spec) spec->remove("pools/" + name + ".json");
         metrics().inc("everserve_spec_writes_total", {{"kind", "pool"}, {"verdict", "deleted"}});
         event("pool " + name + " deleted");
         readmit_all();
@@ -1361,9 +1384,8 @@ struct Coordinator {
           return true;
         }
         p.generation = held + 1;
-        if (!spec_dir.empty()) {
-          mkdirs(spec_dir + "/pools");
-          if (!write_file_atomic(pool_path(name), pool_json(p))) {
+        if (spec) {
+          if (!spec->put("pools/" + name + ".json", pool_json(p))) {
             resp.status = 500;
             resp.body = "{\"error\":\"the spec store refused the write\"}";
             return true;
@@ -1470,8 +1492,10 @@ int main(int argc, char** argv) {
     }
   }
   co.exit_after_log = env_or("EVERSERVE_COORD_EXIT_AFTER_LOG", "") == "1";
+  co.spec = make_spec_store(co.spec_dir);
   co.load_spec();
   co.load_pools();
+  co.load_nodes();
   metrics().describe("everserve_changes_total", "Membership changes by engine, cause, outcome and verdict", "counter");
   metrics().describe("everserve_change_seconds", "From the first loss report to the commit", "histogram");
   metrics().describe("everserve_change_decision_seconds", "Time to choose an outcome", "histogram");

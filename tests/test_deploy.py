@@ -54,3 +54,17 @@ def test_baremetal_smoke():
                        timeout=60)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "smoke: ok" in r.stdout
+
+
+def test_helm_chart_kubernetes_state_backend():
+    """The chart runs the coordinator on a Lease and EverserveState objects by default, ships the
+    CRD, and grants the coordinator exactly those resources."""
+    chart = os.path.join(DEPLOY, "kubernetes", "everserve")
+    crd = yaml.safe_load(open(os.path.join(chart, "crds", "everservestate.yaml")))
+    assert crd["spec"]["group"] == "everserve.ai" and crd["spec"]["names"]["plural"] == "everservestates"
+    values = yaml.safe_load(open(os.path.join(chart, "values.yaml")))
+    assert values["coordinator"]["stateBackend"] == "kubernetes"
+    tpl = open(os.path.join(chart, "templates", "coordinator.yaml")).read()
+    assert '"--spec-store", "k8s:{{ .Release.Namespace }}"' in tpl
+    assert '"--lease", "k8s:{{ .Release.Namespace }}/everserve-coord"' in tpl
+    assert "resources: [leases]" in tpl and "resources: [everservestates]" in tpl

@@ -15,9 +15,12 @@ from everserve_b200.serving.cluster import binary, free_port, wait_listening
 
 
 class FakeKube:
+    """Namespaced objects of any collection (/apis/G/V/namespaces/NS/PLURAL[/NAME]) with
+    resourceVersion conflicts, behind a bearer token."""
+
     def __init__(self, token="tok-1"):
         self.token = token
-        self.leases = {}  # (ns, name) -> object
+        self.objects = {}  # (collection path, name) -> object
         self.rv = 0
         self.lock = threading.Lock()
         self.requests = []
@@ -33,59 +36,68 @@ class FakeKube:
                 self.wfile.write(body)
 
             def _auth(self):
+                fake.requests.append((self.command, self.path))
                 if self.headers.get("Authorization") != f"Bearer {fake.token}":
                     self._send(401, {"kind": "Status", "code": 401})
                     return False
                 return True
 
             def _key(self):
-                parts = self.path.split("/")  # /apis/coordination.k8s.io/v1/namespaces/NS/leases[/NAME]
-                return parts[5], (parts[7] if len(parts) > 7 else None)
+                parts = self.path.split("?")[0].split("/")  # ['', apis, G, V, namespaces, NS, PLURAL, NAME?]
+                return "/".join(parts[:7]), (parts[7] if len(parts) > 7 else None)
 
             def _body(self):
                 n = int(self.headers.get("Content-Length", "0"))
                 return json.loads(self.rfile.read(n)) if n else {}
 
             def do_GET(self):  # noqa: N802
-                fake.requests.append(("GET", self.path))
                 if not self._auth():
                     return
-                ns, name = self._key()
+                coll, name = self._key()
                 with fake.lock:
-                    obj = fake.leases.get((ns, name))
+                    if name is None:
+                        items = [o for (c, _), o in sorted(fake.objects.items()) if c == coll]
+                        return self._send(200, {"kind": "List", "items": items})
+                    obj = fake.objects.get((coll, name))
                 self._send(200, obj) if obj else self._send(404, {"kind": "Status", "code": 404})
 
             def do_POST(self):  # noqa: N802
-                fake.requests.append(("POST", self.path))
                 if not self._auth():
                     return
-                ns, _ = self._key()
+                coll, _ = self._key()
                 obj = self._body()
                 name = obj["metadata"]["name"]
                 with fake.lock:
-                    if (ns, name) in fake.leases:
+                    if (coll, name) in fake.objects:
                         return self._send(409, {"kind": "Status", "code": 409})
                     fake.rv += 1
                     obj["metadata"]["resourceVersion"] = str(fake.rv)
-                    fake.leases[(ns, name)] = obj
+                    fake.objects[(coll, name)] = obj
                 self._send(201, obj)
 
             def do_PUT(self):  # noqa: N802
-                fake.requests.append(("PUT", self.path))
                 if not self._auth():
                     return
-                ns, name = self._key()
+                coll, name = self._key()
                 obj = self._body()
                 with fake.lock:
-                    cur = fake.leases.get((ns, name))
+                    cur = fake.objects.get((coll, name))
                     if cur is None:
                         return self._send(404, {"kind": "Status", "code": 404})
                     if obj["metadata"].get("resourceVersion") != cur["metadata"]["resourceVersion"]:
                         return self._send(409, {"kind": "Status", "code": 409})
                     fake.rv += 1
                     obj["metadata"]["resourceVersion"] = str(fake.rv)
-                    fake.leases[(ns, name)] = obj
+                    fake.objects[(coll, name)] = obj
                 self._send(200, obj)
+
+            def do_DELETE(self):  # noqa: N802
+                if not self._auth():
+                    return
+                coll, name = self._key()
+                with fake.lock:
+                    obj = fake.objects.pop((coll, name), None)
+                self._send(200, obj) if obj else self._send(404, {"kind": "Status", "code": 404})
 
             def log_message(self, *a):
                 pass
@@ -94,14 +106,21 @@ class FakeKube:
         self.url = f"http://127.0.0.1:{self.server.server_address[1]}"
         threading.Thread(target=self.server.serve_forever, daemon=True).start()
 
-    def lease(self, ns="ns1", name="coord"):
-        with self.lock:
-            return json.loads(json.dumps(self.leases.get((ns, name))))
+    LEASES = "/apis/coordination.k8s.io/v1/namespaces/ns1/leases"
+    STATES = "/apis/everserve.ai/v1/namespaces/ns1/everservestates"
 
-    def take_over(self, holder, ns="ns1", name="coord"):
+    def lease(self, name="coord"):
+        with self.lock:
+            return json.loads(json.dumps(self.objects.get((self.LEASES, name))))
+
+    def states(self):
+        with self.lock:
+            return {o["spec"]["key"]: o for (c, _), o in self.objects.items() if c == self.STATES}
+
+    def take_over(self, holder, name="coord"):
         """Another process writes the lease (as if it had won it)."""
         with self.lock:
-            obj = self.leases[(ns, name)]
+            obj = self.objects[(self.LEASES, name)]
             obj["spec"]["holderIdentity"] = holder
             obj["spec"]["leaseTransitions"] += 1
             self.rv += 1
@@ -111,14 +130,26 @@ class FakeKube:
         self.server.shutdown()
 
 
-def _coord(tmp_path, name, fake, token_file):
+def _coord(tmp_path, name, fake, token_file, spec=None):
     env = dict(os.environ, EVERSERVE_KUBE_API=fake.url, EVERSERVE_KUBE_TOKEN_FILE=str(token_file))
     api = f"127.0.0.1:{free_port()}"
     log = open(tmp_path / f"{name}.log", "w")  # noqa: SIM115
     p = subprocess.Popen([binary("everserve-coord"), "--listen", f"unix:{tmp_path}/{name}.sock", "--spec-store",
-                          str(tmp_path / "spec"), "--lease", "k8s:ns1/coord", "--lease-duration-s", "2",
+                          spec or str(tmp_path / "spec"), "--lease", "k8s:ns1/coord", "--lease-duration-s", "2",
                           "--lease-holder", name, "--api-addr", api], stdout=log, stderr=subprocess.STDOUT, env=env)
     return p, api
+
+
+def _call(api, method, path, body=None):
+    import http.client
+
+    host, port = api.rsplit(":", 1)
+    c = http.client.HTTPConnection(host, int(port), timeout=5)
+    c.request(method, path, body=json.dumps(body) if body is not None else None)
+    r = c.getresponse()
+    data = r.read()
+    c.close()
+    return r.status, json.loads(data) if data else {}
 
 
 def test_kubernetes_lease_term_standby_and_loss(tmp_path):
@@ -152,3 +183,56 @@ def test_kubernetes_lease_term_standby_and_loss(tmp_path):
                 p.kill()
                 p.wait()
         fake.close()
+
+
+def test_spec_in_custom_resources_survives_the_coordinator(tmp_path):
+    """Pools and node specs written by one coordinator into EverserveState objects are read back
+    by its successor (the lease's next holder)."""
+    fake = FakeKube()
+    token = tmp_path / "token"
+    token.write_text("tok-1")
+    policy = tmp_path / "policy.json"
+    policy.write_text(json.dumps({"engines": [{"name": "e0", "tensorParallel": 2}]}))
+    a = b = None
+    try:
+        a, api_a = _coord(tmp_path, "coord-a", fake, token, spec="k8s:ns1")
+        wait_listening(api_a)
+        code, _ = _call(api_a, "PUT", "/v1/nodes/n3/cordon")
+        assert code == 200
+        code, _ = _call(api_a, "PUT", "/v1/pools/p0", {"engines": [], "wants": 2, "reason": "warm capacity"})
+        assert code == 200
+        st = fake.states()
+        assert "nodes/n3.json" in st and "pools/p0.json" in st
+        assert all(o["metadata"]["name"].startswith("es-") for o in st.values())
+        a.send_signal(signal.SIGKILL)
+        a.wait()
+        b, api_b = _coord(tmp_path, "coord-b", fake, token, spec="k8s:ns1")
+        wait_listening(api_b, timeout_s=15)
+        nodes = {n["metadata"]["name"]: n for n in _call(api_b, "GET", "/v1/nodes")[1]["items"]}
+        assert nodes["n3"]["spec"]["unschedulable"] is True
+        pool = _call(api_b, "GET", "/v1/pools/p0")[1]
+        assert pool["spec"]["wants"] == 2 and pool["spec"]["reason"] == "warm capacity"
+        assert pool["metadata"]["generation"] == 1
+        code, _ = _call(api_b, "DELETE", "/v1/pools/p0")
+        assert code == 200 and "pools/p0.json" not in fake.states()
+    finally:
+        for p in (a, b):
+            if p is not None and p.poll() is None:
+                p.kill()
+                p.wait()
+        fake.close()
+
+
+def test_file_spec_store_keeps_cordons_across_a_restart(tmp_path):
+    from everserve_b200.serving.cluster import ControlPlane
+
+    with ControlPlane(str(tmp_path / "cp"), engines=[{"name": "e0"}]) as cp:
+        assert cp.request("PUT", "/v1/nodes/n0/cordon")[0] == 200
+        coord = cp.procs["coord"]
+        args = list(coord.args)
+        coord.kill()
+        coord.wait()
+        cp._run("coord", args)  # the same flags: the same spec store
+        wait_listening(cp.api)
+        nodes = {n["metadata"]["name"]: n for n in cp.get("/v1/nodes")["items"]}
+        assert nodes["n0"]["spec"]["unschedulable"] is True
