@@ -113,6 +113,8 @@ std::string Registry::exposition() const {
   return o;
 }
 
+static constexpr size_t kMaxBody = 16u << 20;  // a request body larger than this is refused
+
 static bool read_request(tls::Stream& st, HttpRequest& req) {
   std::string buf;
   char tmp[8192];
@@ -135,11 +137,18 @@ static bool read_request(tls::Stream& st, HttpRequest& req) {
   for (size_t p = 0; p < headers.size();) {
     size_t e = headers.find("\r\n", p);
     if (e == std::string::npos) e = headers.size();
-    std::string h = headers.substr(p, e - p);
-    for (auto& c : h) c = (char)tolower(c);
-    if (h.rfind("content-length:", 0) == 0) content_len = (size_t)atol(h.substr(15).c_str());
+    const std::string h = headers.substr(p, e - p);
+    const auto colon = h.find(':');
+    if (colon != std::string::npos) {
+      std::string name = h.substr(0, colon), value = h.substr(colon + 1);
+      for (auto& c : name) c = (char)tolower(c);
+      while (!value.empty() && (value.front() == ' ' || value.front() == '\t')) value.erase(value.begin());
+      if (name == "content-length") content_len = (size_t)atol(value.c_str());
+      req.headers[name] = value;
+    }
     p = e + 2;
   }
+  if (content_len > kMaxBody) return false;
   req.body = buf.substr(header_end + 4);
   while (req.body.size() < content_len) {
     const long n = st.read_some(tmp, sizeof(tmp), 2000);
@@ -165,10 +174,10 @@ static const char* reason(int s) {
 // One connection: handshake, request, answer. /metrics and /healthz are answered here (the
 // registry has its own lock); a route runs on the loop's thread, since it reads the process's
 // state, and the connection waits for it at most 10 s.
-static void serve_http_conn(Loop* loop, int fd, HttpRoute route) {
+static void serve_http_conn(Loop* loop, int fd, HttpRoute route, HttpOptions opt) {
   tls::Stream st;
   std::string terr;
-  if (!tls::accept_stream(fd, 5000, st, &terr)) return;  // HTTPS when TLS is configured
+  if (!tls::accept_stream(fd, 5000, st, &terr, opt.client_cert)) return;  // HTTPS when TLS is configured
   HttpRequest req;
   HttpResponse resp;
   if (!read_request(st, req)) {
@@ -180,6 +189,11 @@ static void serve_http_conn(Loop* loop, int fd, HttpRoute route) {
     resp.body = metrics().exposition();
   } else if (req.method == "GET" && path == "/healthz") {
     resp.body = "ok\n";
+  } else if (route && !opt.route_on_loop) {
+    if (!route(req, resp)) {
+      resp.status = 404;
+      resp.body = "not found\n";
+    }
   } else if (route) {
     struct Pending {
       std::mutex mu;
@@ -213,12 +227,12 @@ static void serve_http_conn(Loop* loop, int fd, HttpRoute route) {
   }
   std::string out = "HTTP/1.1 " + std::to_string(resp.status) + " " + reason(resp.status) +
                     "\r\nContent-Type: " + resp.content_type + "\r\nContent-Length: " + std::to_string(resp.body.size()) +
-                    "\r\nConnection: close\r\n\r\n" + resp.body;
+                    "\r\nConnection: close\r\n" + resp.extra_headers + "\r\n" + resp.body;
   st.write_all(out, 5000);
   st.close();
 }
 
-bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::string* err) {
+bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::string* err, HttpOptions opt) {
   Address a;
   if (!Address::parse(addr, a)) {
     if (err) *err = "bad address " + addr;
@@ -231,7 +245,7 @@ bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::strin
   const int flags = fcntl(lfd, F_GETFL, 0);
   fcntl(lfd, F_SETFL, flags & ~O_NONBLOCK);
   Loop* lp = &loop;
-  std::thread([lfd, lp, route] {
+  std::thread([lfd, lp, route, opt] {
     static std::atomic<int> active{0};
     for (;;) {
       const int fd = ::accept4(lfd, nullptr, nullptr, SOCK_CLOEXEC);
@@ -243,12 +257,12 @@ bool serve_http(Loop& loop, const std::string& addr, HttpRoute route, std::strin
         return;
       }
       if (active.load() >= 64) {  // bounded: beyond this, connections wait their turn here
-        serve_http_conn(lp, fd, route);
+        serve_http_conn(lp, fd, route, opt);
         continue;
       }
       active++;
-      std::thread([lp, fd, route] {
-        serve_http_conn(lp, fd, route);
+      std::thread([lp, fd, route, opt] {
+        serve_http_conn(lp, fd, route, opt);
         active--;
       }).detach();
     }

@@ -40,17 +40,25 @@ Registry& metrics();
 
 struct HttpRequest {
   std::string method, path, body;
+  std::map<std::string, std::string> headers;  // names in lower case
 };
 struct HttpResponse {
   int status = 200;
   std::string content_type = "text/plain; version=0.0.4";
   std::string body;
+  std::string extra_headers;  // "Name: value\r\n" lines
+};
+struct HttpOptions {
+  bool client_cert = true;    // ask for a client certificate when TLS is configured
+  bool route_on_loop = true;  // the route reads the loop's state: run it there (else on the
+                              // connection's thread, for routes that block, e.g. on another API)
 };
 using HttpRoute = std::function<bool(const HttpRequest&, HttpResponse&)>;  // true: handled
 
 class Loop;
 // Serve HTTP on `addr` ("host:port") from `loop`: /metrics, /healthz, then `route`.
-bool serve_http(Loop& loop, const std::string& addr, HttpRoute route = nullptr, std::string* err = nullptr);
+bool serve_http(Loop& loop, const std::string& addr, HttpRoute route = nullptr, std::string* err = nullptr,
+                HttpOptions opt = {});
 // A blocking HTTP request (used by the CLI); returns the status code, or -1.
 int http_request(const std::string& addr, const std::string& method, const std::string& path, const std::string& body,
                  std::string& out);

@@ -5,6 +5,7 @@
 #include <openssl/pem.h>
 #include <openssl/ssl.h>
 #include <openssl/x509v3.h>
+#include <arpa/inet.h>
 #include <poll.h>
 #include <sys/stat.h>
 #include <sys/socket.h>
@@ -15,6 +16,7 @@
 #include <mutex>
 #include <cstdio>
 #include <cstdlib>
+#include <ctime>
 
 #include "util.h"
 
@@ -24,6 +26,7 @@ namespace {
 
 SSL_CTX* g_server = nullptr;
 SSL_CTX* g_client = nullptr;
+SSL_CTX* g_server_open = nullptr;  // the same identity, no client certificate asked (enrollment)
 
 std::string last_error() {
   char buf[256];
@@ -58,10 +61,23 @@ bool wait_fd(int fd, bool write, int timeout_ms) {
 }  // namespace
 
 bool configure(const Config& c, std::string* err) {
-  g_server = make_ctx(true, c, err);
-  if (!g_server) return false;
-  g_client = make_ctx(false, c, err);
-  return g_client != nullptr;
+  SSL_CTX* server = make_ctx(true, c, err);
+  if (!server) return false;
+  SSL_CTX* client = make_ctx(false, c, err);
+  SSL_CTX* open = make_ctx(true, c, err);
+  if (!client || !open) {
+    SSL_CTX_free(server);
+    if (client) SSL_CTX_free(client);
+    return false;
+  }
+  SSL_CTX_set_verify(open, SSL_VERIFY_NONE, nullptr);
+  // replaced contexts are freed: sessions made from them hold their own references
+  std::swap(g_server, server);
+  std::swap(g_client, client);
+  std::swap(g_server_open, open);
+  for (SSL_CTX* old : {server, client, open})
+    if (old) SSL_CTX_free(old);
+  return true;
 }
 
 bool configure_from_env(std::string* err) {
@@ -216,8 +232,15 @@ bool connect_web(const Address& a, bool https, const std::string& ca_file, int t
   SSL* s = SSL_new(ctx);
   SSL_set_fd(s, out.fd);
   SSL_set_connect_state(s);
-  SSL_set_tlsext_host_name(s, a.host.c_str());
-  SSL_set1_host(s, a.host.c_str());  // the certificate must name the host asked for
+  // the certificate must name the host (or the IP address) asked for
+  in6_addr ip6;
+  in_addr ip4;
+  if (inet_pton(AF_INET, a.host.c_str(), &ip4) == 1 || inet_pton(AF_INET6, a.host.c_str(), &ip6) == 1) {
+    X509_VERIFY_PARAM_set1_ip_asc(SSL_get0_param(s), a.host.c_str());
+  } else {
+    SSL_set_tlsext_host_name(s, a.host.c_str());
+    SSL_set1_host(s, a.host.c_str());
+  }
   out.ssl = s;
   if (!finish_handshake(out, timeout_ms, err)) {
     out.close();
@@ -226,11 +249,18 @@ bool connect_web(const Address& a, bool https, const std::string& ca_file, int t
   return true;
 }
 
-bool accept_stream(int fd, int timeout_ms, Stream& out, std::string* err) {
+bool accept_stream(int fd, int timeout_ms, Stream& out, std::string* err, bool client_cert) {
   out = Stream{};
   out.fd = fd;
   if (enabled()) {
-    out.ssl = new_server(fd);
+    if (client_cert) {
+      out.ssl = new_server(fd);
+    } else {
+      SSL* s = SSL_new(g_server_open);
+      SSL_set_fd(s, fd);
+      SSL_set_accept_state(s);
+      out.ssl = s;
+    }
     if (!finish_handshake(out, timeout_ms, err)) {
       out.close();
       return false;
@@ -395,6 +425,91 @@ bool issue(const std::string& dir, const std::string& name, int days, std::strin
   }
   if (!ok && err) *err = "cannot issue a certificate for " + name;
   EVP_PKEY_free(key);
+  EVP_PKEY_free(ca_key);
+  X509_free(ca);
+  return ok;
+}
+
+static std::string pem_of(EVP_PKEY* key, bool private_part) {
+  BIO* b = BIO_new(BIO_s_mem());
+  const int ok = private_part ? PEM_write_bio_PrivateKey(b, key, nullptr, nullptr, 0, nullptr, nullptr)
+                              : PEM_write_bio_PUBKEY(b, key);
+  std::string out;
+  if (ok == 1) {
+    char* p = nullptr;
+    const long n = BIO_get_mem_data(b, &p);
+    out.assign(p, (size_t)n);
+  }
+  BIO_free(b);
+  return out;
+}
+
+bool make_key(std::string& key_pem, std::string& pub_pem, std::string* err) {
+  EVP_PKEY* key = EVP_EC_gen("P-256");
+  if (!key) {
+    if (err) *err = "key generation failed";
+    return false;
+  }
+  key_pem = pem_of(key, true);
+  pub_pem = pem_of(key, false);
+  EVP_PKEY_free(key);
+  return !key_pem.empty() && !pub_pem.empty();
+}
+
+bool sign_node(const std::string& ca_dir, const std::string& node, const std::string& pub_pem, int hours,
+               std::string& cert_pem, std::string& ca_pem, int64_t& not_after_ms, std::string* err) {
+  FILE* fk = fopen((ca_dir + "/ca.key").c_str(), "r");
+  FILE* fc = fopen((ca_dir + "/ca.crt").c_str(), "r");
+  if (!fk || !fc) {
+    if (fk) fclose(fk);
+    if (fc) fclose(fc);
+    if (err) *err = "this coordinator holds no CA key";
+    return false;
+  }
+  EVP_PKEY* ca_key = PEM_read_PrivateKey(fk, nullptr, nullptr, nullptr);
+  X509* ca = PEM_read_X509(fc, nullptr, nullptr, nullptr);
+  fclose(fk);
+  fclose(fc);
+  BIO* b = BIO_new_mem_buf(pub_pem.data(), (int)pub_pem.size());
+  EVP_PKEY* pub = PEM_read_bio_PUBKEY(b, nullptr, nullptr, nullptr);
+  BIO_free(b);
+  bool ok = ca_key && ca && pub;
+  if (!pub && err) *err = "the public key does not parse";
+  if (ok) {
+    X509* x = X509_new();
+    X509_set_version(x, 2);
+    ASN1_INTEGER_set(X509_get_serialNumber(x), (long)(now_us() & 0x7fffffff));
+    X509_gmtime_adj(X509_getm_notBefore(x), -60);
+    X509_gmtime_adj(X509_getm_notAfter(x), (long)hours * 3600);
+    X509_set_pubkey(x, pub);
+    X509_NAME_add_entry_by_txt(X509_get_subject_name(x), "CN", MBSTRING_ASC,
+                               reinterpret_cast<const unsigned char*>(node.c_str()), -1, -1, 0);
+    X509_set_issuer_name(x, X509_get_subject_name(ca));
+    const std::string san = "DNS:" + node;
+    add_ext(x, ca, NID_subject_alt_name, san.c_str());
+    add_ext(x, ca, NID_basic_constraints, "critical,CA:FALSE");
+    add_ext(x, ca, NID_ext_key_usage, "serverAuth,clientAuth");
+    ok = X509_sign(x, ca_key, EVP_sha256()) > 0;
+    if (ok) {
+      BIO* o = BIO_new(BIO_s_mem());
+      PEM_write_bio_X509(o, x);
+      char* p = nullptr;
+      const long n = BIO_get_mem_data(o, &p);
+      cert_pem.assign(p, (size_t)n);
+      BIO_free(o);
+      BIO* c = BIO_new(BIO_s_mem());
+      PEM_write_bio_X509(c, ca);
+      p = nullptr;
+      const long m = BIO_get_mem_data(c, &p);
+      ca_pem.assign(p, (size_t)m);
+      BIO_free(c);
+      not_after_ms = (int64_t)(std::time(nullptr) + (time_t)hours * 3600) * 1000;
+    } else if (err) {
+      *err = "signing failed";
+    }
+    X509_free(x);
+  }
+  EVP_PKEY_free(pub);
   EVP_PKEY_free(ca_key);
   X509_free(ca);
   return ok;

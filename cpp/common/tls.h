@@ -57,13 +57,22 @@ bool connect_stream(const Address& a, int timeout_ms, Stream& out, std::string* 
 // `ca_file` (the system's trust store when empty) and the host name asked for.
 bool connect_web(const Address& a, bool https, const std::string& ca_file, int timeout_ms, Stream& out,
                  std::string* err);
-// The server side of a blocking exchange on an accepted TCP fd (handshake bounded by timeout_ms).
-bool accept_stream(int fd, int timeout_ms, Stream& out, std::string* err);
+// The server side of a blocking exchange on an accepted TCP fd (handshake bounded by timeout_ms);
+// `client_cert` false: no client certificate is asked (the enrollment endpoint, where a node
+// proves itself another way).
+bool accept_stream(int fd, int timeout_ms, Stream& out, std::string* err, bool client_cert = true);
 
 // Certificates: a CA (ca.key, ca.crt) and leaf certificates signed by it (<name>.key, <name>.crt,
 // CN and DNS name = <name>, IP 127.0.0.1), EC P-256, SHA-256, `days` of validity.
 bool make_ca(const std::string& dir, int days, std::string* err);
 bool issue(const std::string& dir, const std::string& name, int days, std::string* err);
+
+// Enrollment: a key made where it is used (PEM private key and PEM public key), and a node's
+// certificate (CN and DNS name = node, valid `hours`) signed by the CA in `ca_dir` for a public
+// key it was sent; also the CA's certificate and the expiry.
+bool make_key(std::string& key_pem, std::string& pub_pem, std::string* err);
+bool sign_node(const std::string& ca_dir, const std::string& node, const std::string& pub_pem, int hours,
+               std::string& cert_pem, std::string& ca_pem, int64_t& not_after_ms, std::string* err);
 
 }  // namespace tls
 }  // namespace es

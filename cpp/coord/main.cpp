@@ -4,6 +4,7 @@
 //                   [--lease FILE] [--api-addr host:port] [--metrics-addr host:port]
 //                   [--node-loss-misses 3] [--delivery-timeout-ms 130000]
 //                   [--lease-holder NAME] [--lease-duration-s 15]   (--lease k8s:NS/NAME: a Kubernetes Lease)
+//                   [--enroll-addr host:port] [--enroll-ca-dir DIR] [--enroll-hours 12]   (node enrollment, issuer.h)
 // Flags also read EVERSERVE_LISTEN, EVERSERVE_POLICY, EVERSERVE_SPEC_STORE, EVERSERVE_LEASE,
 // EVERSERVE_API_ADDR, EVERSERVE_METRICS_ADDR, EVERSERVE_NODE_LOSS_MISSES.
 //
@@ -33,6 +34,7 @@
 
 #include "cover.h"
 #include "everserve_pb.h"
+#include "issuer.h"
 #include "lease.h"
 #include "spec_store.h"
 #include "topology.h"
@@ -1436,6 +1438,9 @@ int main(int argc, char** argv) {
   std::string metrics_addr = env_or("EVERSERVE_METRICS_ADDR", "");
   co.loss_misses = (uint32_t)std::stoul(env_or("EVERSERVE_NODE_LOSS_MISSES", "3"));
   std::string lease_holder = env_or("EVERSERVE_LEASE_HOLDER", "");
+  std::string enroll_addr = env_or("EVERSERVE_ENROLL_ADDR", "");
+  std::string enroll_ca_dir = env_or("EVERSERVE_ENROLL_CA_DIR", env_or("EVERSERVE_TLS_DIR", ""));
+  int enroll_hours = std::stoi(env_or("EVERSERVE_ENROLL_HOURS", "12"));
   uint32_t lease_duration_s = (uint32_t)std::stoul(env_or("EVERSERVE_LEASE_DURATION_S", "15"));
   for (int i = 1; i + 1 < argc; i += 2) {
     const std::string k = argv[i], v = argv[i + 1];
@@ -1448,6 +1453,9 @@ int main(int argc, char** argv) {
     else if (k == "--node-loss-misses") co.loss_misses = (uint32_t)std::stoul(v);
     else if (k == "--delivery-timeout-ms") co.delivery_timeout_ms = std::stoull(v);
     else if (k == "--lease-holder") lease_holder = v;
+    else if (k == "--enroll-addr") enroll_addr = v;
+    else if (k == "--enroll-ca-dir") enroll_ca_dir = v;
+    else if (k == "--enroll-hours") enroll_hours = std::stoi(v);
     else if (k == "--lease-duration-s") lease_duration_s = (uint32_t)std::stoul(v);
     else {
       fprintf(stderr, "unknown flag %s\n", k.c_str());
@@ -1512,6 +1520,7 @@ int main(int argc, char** argv) {
   metrics().describe("everserve_cover_failures_total", "Planned groups a member failed to form", "counter");
   metrics().describe("everserve_fenced_total", "Reports dropped as older than the engine's epoch", "counter");
   metrics().describe("everserve_spares_refused_total", "Spares refused admission (identity, cordon, pool, device fit)", "counter");
+  metrics().describe("everserve_enrollments_total", "Node certificate requests by verdict (issued, refused)", "counter");
   metrics().describe("everserve_pool_spares", "Spares of each pool by state (standing, warming)", "gauge");
   metrics().describe("everserve_unheard_ranks_lost_total", "Loss reports naming ranks the coordinator does not hold", "counter");
   Address a;
@@ -1526,6 +1535,23 @@ int main(int argc, char** argv) {
       !serve_http(co.loop, api_addr, [&](const HttpRequest& r, HttpResponse& s) { return co.api(r, s); }, &err)) {
     ES_ERROR("api %s: %s", api_addr.c_str(), err.c_str());
     return 1;
+  }
+  std::unique_ptr<Issuer> issuer;
+  if (!enroll_addr.empty()) {
+    if (enroll_ca_dir.empty()) {
+      ES_ERROR("--enroll-addr needs the CA's directory (--enroll-ca-dir or EVERSERVE_TLS_DIR)");
+      return 1;
+    }
+    issuer = std::make_unique<Issuer>(KubeClient::from_env(), enroll_ca_dir, enroll_hours);
+    HttpOptions open;
+    open.client_cert = false;     // the node has no certificate yet: the token proves it
+    open.route_on_loop = false;   // the review waits on the API server
+    Issuer* is = issuer.get();
+    if (!serve_http(co.loop, enroll_addr, [is](const HttpRequest& r, HttpResponse& s) { return is->route(r, s); },
+                    &err, open)) {
+      ES_ERROR("enroll %s: %s", enroll_addr.c_str(), err.c_str());
+      return 1;
+    }
   }
   if (!metrics_addr.empty() && metrics_addr != api_addr && !serve_http(co.loop, metrics_addr, nullptr, &err)) {
     ES_ERROR("metrics %s: %s", metrics_addr.c_str(), err.c_str());

@@ -3,7 +3,7 @@
 //   everserve-node --node NAME --socket unix:/run/everserve/node.sock --coordinator ADDR
 //                  [--heartbeat-ms 500] [--metrics-addr host:port] [--ack-timeout-ms 120000]
 //                  [--mirror-socket ADDR] [--discovery-dir DIR] [--devices-from nvidia-smi|none|PROGRAM]
-//                  [--domain NAME] [--cache-wait-ms 600000]
+//                  [--domain NAME] [--cache-wait-ms 600000] [--enroll URL --tls-dir DIR]
 // Flags also read EVERSERVE_NODE, EVERSERVE_SOCKET, EVERSERVE_COORDINATOR, EVERSERVE_HEARTBEAT_MS,
 // EVERSERVE_METRICS_ADDR, EVERSERVE_MIRROR_SOCKET, EVERSERVE_DISCOVERY_DIR, EVERSERVE_DEVICES_FROM,
 // EVERSERVE_DOMAIN.
@@ -40,8 +40,10 @@
 #include <set>
 #include <thread>
 
+#include "enroll.h"
 #include "everserve_pb.h"
 #include "frame.h"
+#include "kube.h"
 #include "net.h"
 #include "notice.h"
 #include "telemetry.h"
@@ -908,7 +910,13 @@ struct Daemon {
 }  // namespace
 
 int main(int argc, char** argv) {
-  {
+  std::string enroll_url = env_or("EVERSERVE_ENROLL_URL", "");
+  std::string tls_dir = env_or("EVERSERVE_TLS_DIR", "");
+  for (int i = 1; i + 1 < argc; i += 2) {
+    if (std::string(argv[i]) == "--enroll") enroll_url = argv[i + 1];
+    if (std::string(argv[i]) == "--tls-dir") tls_dir = argv[i + 1];
+  }
+  if (enroll_url.empty()) {
     std::string terr;
     if (!es::tls::configure_from_env(&terr)) {
       fprintf(stderr, "TLS: %s\n", terr.c_str());
@@ -949,10 +957,62 @@ int main(int argc, char** argv) {
     else if (k == "--devices-from") devices_from = v;
     else if (k == "--domain") domain = v;
     else if (k == "--cache-wait-ms") d.cache_wait_ms = std::stoull(v);
+    else if (k == "--enroll" || k == "--tls-dir") continue;  // read above
     else {
       fprintf(stderr, "unknown flag %s\n", k.c_str());
       return 2;
     }
+  }
+  if (!enroll_url.empty()) {
+    // the node's certificate from the coordinator's issuer, then mutual TLS with it
+    if (tls_dir.empty()) {
+      ES_ERROR("--enroll needs --tls-dir (holding the bootstrap ca.crt)");
+      return 2;
+    }
+    const std::string token_file = env_or("EVERSERVE_ENROLL_TOKEN_FILE", "/var/run/secrets/everserve/token");
+    Enrolled held;
+    if (!enrolled_in(tls_dir, 600000, held)) {
+      std::string e;
+      bool ok = false;
+      const int attempts = std::stoi(env_or("EVERSERVE_ENROLL_ATTEMPTS", "5"));
+      for (int attempt = 0; attempt < attempts && !(ok = enroll(enroll_url, tls_dir, token_file, held, e)); attempt++) {
+        ES_WARN("enrollment: %s", e.c_str());
+        if (attempt + 1 < attempts) sleep(1u << std::min(attempt, 5));
+      }
+      if (!ok) {
+        ES_ERROR("enrollment at %s failed: %s", enroll_url.c_str(), e.c_str());
+        return 2;
+      }
+    }
+    if (held.node != d.node) ES_WARN("the certificate names node %s, not %s", held.node.c_str(), d.node.c_str());
+    std::string terr;
+    tls::Config tc{tls_dir + "/ca.crt", tls_dir + "/node.crt", tls_dir + "/node.key"};
+    if (!tls::configure(tc, &terr)) {
+      ES_ERROR("TLS: %s", terr.c_str());
+      return 2;
+    }
+    ES_INFO("enrolled as %s until %lld", held.node.c_str(), (long long)held.not_after_ms);
+    // renew at half the certificate's life; the new files are taken on the loop's thread
+    std::thread([enroll_url, tls_dir, token_file, held, &d]() mutable {
+      for (;;) {
+        const int64_t half = held.issued_at_ms + (held.not_after_ms - held.issued_at_ms) / 2;
+        const int64_t wait = std::max<int64_t>(30000, half - wall_clock_ms());
+        std::this_thread::sleep_for(std::chrono::milliseconds(wait));
+        std::string e;
+        if (!enroll(enroll_url, tls_dir, token_file, held, e)) {
+          ES_WARN("renewal: %s", e.c_str());
+          held.issued_at_ms = wall_clock_ms() - (held.not_after_ms - wall_clock_ms());  // again in 30 s
+          continue;
+        }
+        d.loop.post([tls_dir] {
+          std::string terr;
+          if (!tls::configure({tls_dir + "/ca.crt", tls_dir + "/node.crt", tls_dir + "/node.key"}, &terr))
+            ES_ERROR("TLS after renewal: %s", terr.c_str());
+          else
+            ES_INFO("certificate renewed");
+        });
+      }
+    }).detach();
   }
   d.instance = (now_us() << 8) ^ (uint64_t)getpid();
   d.socket = socket;

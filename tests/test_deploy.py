@@ -68,3 +68,15 @@ def test_helm_chart_kubernetes_state_backend():
     assert '"--spec-store", "k8s:{{ .Release.Namespace }}"' in tpl
     assert '"--lease", "k8s:{{ .Release.Namespace }}/everserve-coord"' in tpl
     assert "resources: [leases]" in tpl and "resources: [everservestates]" in tpl
+
+
+def test_helm_chart_node_daemonset_rbac_and_network_policies():
+    chart = os.path.join(DEPLOY, "kubernetes", "everserve")
+    node = open(os.path.join(chart, "templates", "node.yaml")).read()
+    coord = open(os.path.join(chart, "templates", "coordinator.yaml")).read()
+    assert "kind: NetworkPolicy" in node and "resources: [nodes], verbs: [get]" in node
+    assert "audience: everserve" in node and "--enroll https://everserve-coord" in node
+    assert "--compile-cache-dir" in node and "EVERSERVE_COMPILE_CACHE" in node
+    assert "resources: [tokenreviews], verbs: [create]" in coord and "--enroll-addr" in coord
+    values = yaml.safe_load(open(os.path.join(chart, "values.yaml")))
+    assert values["coordinator"]["enrollPort"] == 7682 and values["store"]["replicaPort"] == 7683
