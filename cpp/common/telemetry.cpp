@@ -185,7 +185,9 @@ static void serve_http_conn(Loop* loop, int fd, HttpRoute route, HttpOptions opt
     return;
   }
   const std::string path = req.path.substr(0, req.path.find('?'));
-  if (req.method == "GET" && path == "/metrics") {
+  if (opt.gate && !(path == "/healthz") && !opt.gate(req, resp)) {
+    // refused: the gate set the answer
+  } else if (req.method == "GET" && path == "/metrics") {
     resp.body = metrics().exposition();
   } else if (req.method == "GET" && path == "/healthz") {
     resp.body = "ok\n";

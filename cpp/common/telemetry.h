@@ -52,6 +52,9 @@ struct HttpOptions {
   bool client_cert = true;    // ask for a client certificate when TLS is configured
   bool route_on_loop = true;  // the route reads the loop's state: run it there (else on the
                               // connection's thread, for routes that block, e.g. on another API)
+  // Runs on the connection's thread before the route (it may block, e.g. on a token review):
+  // false refuses the request with the status and body it set.
+  std::function<bool(const HttpRequest&, HttpResponse&)> gate;
 };
 using HttpRoute = std::function<bool(const HttpRequest&, HttpResponse&)>;  // true: handled
 

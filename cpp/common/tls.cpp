@@ -516,4 +516,18 @@ bool sign_node(const std::string& ca_dir, const std::string& node, const std::st
 }
 
 }  // namespace tls
+
+std::string sha256_hex(const std::string& data) {
+  unsigned char md[EVP_MAX_MD_SIZE];
+  unsigned int n = 0;
+  EVP_Digest(data.data(), data.size(), md, &n, EVP_sha256(), nullptr);
+  static const char* d = "0123456789abcdef";
+  std::string out;
+  for (unsigned int i = 0; i < n; i++) {
+    out.push_back(d[md[i] >> 4]);
+    out.push_back(d[md[i] & 15]);
+  }
+  return out;
+}
+
 }  // namespace es

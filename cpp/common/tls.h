@@ -75,4 +75,8 @@ bool sign_node(const std::string& ca_dir, const std::string& node, const std::st
                std::string& cert_pem, std::string& ca_pem, int64_t& not_after_ms, std::string* err);
 
 }  // namespace tls
+
+// sha256 of `data`, lower-case hex.
+std::string sha256_hex(const std::string& data);
+
 }  // namespace es

@@ -5,6 +5,7 @@
 //                   [--node-loss-misses 3] [--delivery-timeout-ms 130000]
 //                   [--lease-holder NAME] [--lease-duration-s 15]   (--lease k8s:NS/NAME: a Kubernetes Lease)
 //                   [--enroll-addr host:port] [--enroll-ca-dir DIR] [--enroll-hours 12]   (node enrollment, issuer.h)
+//                   [--api-auth cert|kube] [--api-namespace NS]   (operator API: client certificates, or api_auth.h)
 // Flags also read EVERSERVE_LISTEN, EVERSERVE_POLICY, EVERSERVE_SPEC_STORE, EVERSERVE_LEASE,
 // EVERSERVE_API_ADDR, EVERSERVE_METRICS_ADDR, EVERSERVE_NODE_LOSS_MISSES.
 //
@@ -34,6 +35,7 @@
 
 #include "cover.h"
 #include "everserve_pb.h"
+#include "api_auth.h"
 #include "issuer.h"
 #include "lease.h"
 #include "spec_store.h"
@@ -1441,6 +1443,8 @@ int main(int argc, char** argv) {
   std::string enroll_addr = env_or("EVERSERVE_ENROLL_ADDR", "");
   std::string enroll_ca_dir = env_or("EVERSERVE_ENROLL_CA_DIR", env_or("EVERSERVE_TLS_DIR", ""));
   int enroll_hours = std::stoi(env_or("EVERSERVE_ENROLL_HOURS", "12"));
+  std::string api_auth = env_or("EVERSERVE_API_AUTH", "cert");
+  std::string api_namespace = env_or("EVERSERVE_API_NAMESPACE", "");
   uint32_t lease_duration_s = (uint32_t)std::stoul(env_or("EVERSERVE_LEASE_DURATION_S", "15"));
   for (int i = 1; i + 1 < argc; i += 2) {
     const std::string k = argv[i], v = argv[i + 1];
@@ -1456,6 +1460,8 @@ int main(int argc, char** argv) {
     else if (k == "--enroll-addr") enroll_addr = v;
     else if (k == "--enroll-ca-dir") enroll_ca_dir = v;
     else if (k == "--enroll-hours") enroll_hours = std::stoi(v);
+    else if (k == "--api-auth") api_auth = v;
+    else if (k == "--api-namespace") api_namespace = v;
     else if (k == "--lease-duration-s") lease_duration_s = (uint32_t)std::stoul(v);
     else {
       fprintf(stderr, "unknown flag %s\n", k.c_str());
@@ -1520,6 +1526,7 @@ int main(int argc, char** argv) {
   metrics().describe("everserve_cover_failures_total", "Planned groups a member failed to form", "counter");
   metrics().describe("everserve_fenced_total", "Reports dropped as older than the engine's epoch", "counter");
   metrics().describe("everserve_spares_refused_total", "Spares refused admission (identity, cordon, pool, device fit)", "counter");
+  metrics().describe("everserve_api_refusals_total", "Operator API requests refused by the token gate, by code", "counter");
   metrics().describe("everserve_enrollments_total", "Node certificate requests by verdict (issued, refused)", "counter");
   metrics().describe("everserve_pool_spares", "Spares of each pool by state (standing, warming)", "gauge");
   metrics().describe("everserve_unheard_ranks_lost_total", "Loss reports naming ranks the coordinator does not hold", "counter");
@@ -1531,8 +1538,23 @@ int main(int argc, char** argv) {
     ES_ERROR("listen %s: %s", listen.c_str(), err.c_str());
     return 1;
   }
+  std::unique_ptr<KubeGate> gate;
+  HttpOptions api_opt;
+  if (api_auth == "kube") {
+    // bearer tokens reviewed by the Kubernetes API server instead of client certificates
+    if (api_namespace.empty() && !read_file("/var/run/secrets/kubernetes.io/serviceaccount/namespace", api_namespace))
+      api_namespace = "default";
+    gate = std::make_unique<KubeGate>(KubeClient::from_env(), api_namespace);
+    KubeGate* g = gate.get();
+    api_opt.client_cert = false;
+    api_opt.gate = [g](const HttpRequest& r, HttpResponse& s) { return g->admit(r, s); };
+  } else if (api_auth != "cert") {
+    ES_ERROR("--api-auth is cert or kube");
+    return 2;
+  }
   if (!api_addr.empty() &&
-      !serve_http(co.loop, api_addr, [&](const HttpRequest& r, HttpResponse& s) { return co.api(r, s); }, &err)) {
+      !serve_http(co.loop, api_addr, [&](const HttpRequest& r, HttpResponse& s) { return co.api(r, s); }, &err,
+                  api_opt)) {
     ES_ERROR("api %s: %s", api_addr.c_str(), err.c_str());
     return 1;
   }

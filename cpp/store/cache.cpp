@@ -106,12 +106,6 @@ bool ask(tls::Stream& st, const mirror::MirrorRequest& req, mirror::MirrorReply&
 
 }  // namespace
 
-std::string sha256_hex(const std::string& data) {
-  Sha256 h;
-  h.update(data.data(), data.size());
-  return h.hex();
-}
-
 std::string CompileCacheDir::base(const std::string& key, const std::string& digest) const {
   return dir_ + "/" + key + "/" + digest;
 }

@@ -17,6 +17,7 @@
 #include <string>
 
 #include "everserve_pb.h"
+#include "tls.h"
 
 namespace es {
 
@@ -39,8 +40,5 @@ class CompileCacheDir {
   std::string dir_;
   std::mutex fetch_mu_;  // one fetch at a time: two asks for a set fetch it once
 };
-
-// sha256 of `data`, lower-case hex.
-std::string sha256_hex(const std::string& data);
 
 }  // namespace es
