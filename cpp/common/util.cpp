@@ -420,3 +420,46 @@ bool run_capture(const std::vector<std::string>& argv, int timeout_ms, std::stri
 }
 
 }  // namespace es
+
+namespace es {
+
+static const char* kB64 = "ABCDEFGHIJKLMNOPQRSTUVWXYZabcdefghijklmnopqrstuvwxyz0123456789+/";
+
+std::string base64_encode(const std::string& in) {
+  std::string out;
+  size_t i = 0;
+  for (; i + 2 < in.size(); i += 3) {
+    const uint32_t v = ((uint8_t)in[i] << 16) | ((uint8_t)in[i + 1] << 8) | (uint8_t)in[i + 2];
+    for (int s = 18; s >= 0; s -= 6) out.push_back(kB64[(v >> s) & 63]);
+  }
+  if (i + 1 == in.size()) {
+    const uint32_t v = (uint8_t)in[i] << 16;
+    out += {kB64[(v >> 18) & 63], kB64[(v >> 12) & 63], '=', '='};
+  } else if (i + 2 == in.size()) {
+    const uint32_t v = ((uint8_t)in[i] << 16) | ((uint8_t)in[i + 1] << 8);
+    out += {kB64[(v >> 18) & 63], kB64[(v >> 12) & 63], kB64[(v >> 6) & 63], '='};
+  }
+  return out;
+}
+
+bool base64_decode(const std::string& in, std::string& out) {
+  int val[256];
+  for (int& v : val) v = -1;
+  for (int k = 0; k < 64; k++) val[(uint8_t)kB64[k]] = k;
+  out.clear();
+  uint32_t acc = 0;
+  int bits = 0;
+  for (char c : in) {
+    if (c == '=' || c == '\n' || c == '\r') continue;
+    if (val[(uint8_t)c] < 0) return false;
+    acc = (acc << 6) | (uint32_t)val[(uint8_t)c];
+    bits += 6;
+    if (bits >= 8) {
+      bits -= 8;
+      out.push_back((char)((acc >> bits) & 0xff));
+    }
+  }
+  return true;
+}
+
+}  // namespace es

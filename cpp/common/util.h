@@ -52,6 +52,9 @@ std::string env_or(const char* name, const std::string& dflt);
 // Run `argv` (PATH searched) and capture its standard output; false if it cannot start, exits
 // non-zero, or runs past `timeout_ms` (then it is killed).
 bool run_capture(const std::vector<std::string>& argv, int timeout_ms, std::string& out);
+// Standard base64 (RFC 4648, padded); decode skips line breaks, false on another character.
+std::string base64_encode(const std::string& in);
+bool base64_decode(const std::string& in, std::string& out);
 
 // ---- processes -----------------------------------------------------------------------------------
 // /proc/<pid>/stat state: 'R','S','D','Z','X',... or 0 when the process does not exist.

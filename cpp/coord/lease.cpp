@@ -4,10 +4,13 @@
 #include <sys/file.h>
 #include <unistd.h>
 
+#include <chrono>
+#include <cstdlib>
 #include <thread>
 
 #include "everserve_pb.h"
 #include "net.h"
+#include "telemetry.h"
 #include "util.h"
 
 namespace es {
@@ -53,6 +56,15 @@ class FileLease : public Lease {
 }  // namespace
 
 std::unique_ptr<Lease> make_lease(const std::string& spec, const std::string& holder, uint32_t duration_s) {
+  if (spec.rfind("etcd:", 0) == 0) {
+    // etcd:http://host:2379/path/of/key
+    const std::string rest = spec.substr(5);
+    const auto scheme = rest.find("://");
+    const auto slash = rest.find('/', scheme == std::string::npos ? 0 : scheme + 3);
+    const std::string url = slash == std::string::npos ? rest : rest.substr(0, slash);
+    const std::string key = slash == std::string::npos ? "/everserve/coordinator" : rest.substr(slash);
+    return std::make_unique<EtcdLease>(url, key, holder, duration_s);
+  }
   if (spec.rfind("k8s:", 0) == 0) {
     const std::string rest = spec.substr(4);
     const auto slash = rest.find('/');
@@ -175,6 +187,82 @@ bool KubeLease::renew(std::string& err) {
     return false;
   }
   return true;  // try again at the next period
+}
+
+EtcdLease::EtcdLease(std::string url, std::string key, std::string holder, uint32_t ttl_s)
+    : url_(std::move(url)), key_(std::move(key)), holder_(std::move(holder)), ca_(env_or("EVERSERVE_ETCD_CA", "")),
+      ttl_s_(ttl_s ? ttl_s : 15) {}
+
+int EtcdLease::post(const std::string& path, const std::string& body, std::string& out) const {
+  return http_url(url_ + path, "POST", {"Content-Type: application/json"}, body, out, 3000, ca_);
+}
+
+// etcd's JSON gateway writes 64-bit numbers as strings
+static uint64_t num_of(const Json* j) {
+  if (!j) return 0;
+  return j->kind == Json::Number ? (uint64_t)j->num : std::strtoull(j->str.c_str(), nullptr, 10);
+}
+
+bool EtcdLease::acquire(uint64_t& term, std::string& err) {
+  bool said_waiting = false;
+  const std::string k64 = base64_encode(key_);
+  for (;;) {
+    std::string out;
+    Json j;
+    if (lease_id_.empty()) {
+      if (post("/v3/lease/grant", "{\"TTL\":" + std::to_string(ttl_s_) + "}", out) != 200 || !Json::parse(out, j)) {
+        ES_WARN("etcd %s: no lease granted", url_.c_str());
+        std::this_thread::sleep_for(std::chrono::milliseconds(1000));
+        continue;
+      }
+      const Json* id = j.get("ID");
+      lease_id_ = id ? (id->kind == Json::Number ? std::to_string((uint64_t)id->num) : id->str) : "";
+      if (lease_id_.empty()) continue;
+    }
+    // the key is ours only if nobody holds it: created with our lease, or held by someone else
+    const std::string txn =
+        "{\"compare\":[{\"key\":\"" + k64 + "\",\"result\":\"EQUAL\",\"target\":\"CREATE\",\"create_revision\":\"0\"}],"
+        "\"success\":[{\"request_put\":{\"key\":\"" + k64 + "\",\"value\":\"" + base64_encode(holder_) +
+        "\",\"lease\":\"" + lease_id_ + "\"}}],\"failure\":[{\"request_range\":{\"key\":\"" + k64 + "\"}}]}";
+    if (post("/v3/kv/txn", txn, out) == 200 && Json::parse(out, j)) {
+      const Json* ok = j.get("succeeded");
+      if (ok && ok->b) {
+        const Json* header = j.get("header");
+        term = num_of(header ? header->get("revision") : nullptr);  // our key's create revision
+        last_renewed_ms_ = wall_clock_ms();
+        return term > 0 || (err = "etcd answered no revision", false);
+      }
+      if (!said_waiting) {
+        ES_INFO("waiting for the etcd lease %s", key_.c_str());
+        said_waiting = true;
+      }
+    } else {
+      ES_WARN("etcd %s: the transaction was not answered", url_.c_str());
+    }
+    // keep our own etcd lease alive while we wait, so it is there when the key frees
+    post("/v3/lease/keepalive", "{\"ID\":\"" + lease_id_ + "\"}", out);
+    std::this_thread::sleep_for(std::chrono::milliseconds(500));
+  }
+}
+
+bool EtcdLease::renew(std::string& err) {
+  std::string out;
+  Json j;
+  const int64_t now = wall_clock_ms();
+  if (post("/v3/lease/keepalive", "{\"ID\":\"" + lease_id_ + "\"}", out) == 200 && Json::parse(out, j)) {
+    const Json* res = j.get("result");
+    if (!res || num_of(res->get("TTL")) == 0) {
+      err = "etcd says the lease expired";
+      return false;
+    }
+    last_renewed_ms_ = now;
+    return true;
+  }
+  if (now - last_renewed_ms_ > (int64_t)ttl_s_ * 1000) {
+    err = "not kept alive for " + std::to_string((now - last_renewed_ms_) / 1000) + " s";
+    return false;
+  }
+  return true;
 }
 
 }  // namespace es

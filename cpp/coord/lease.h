@@ -6,12 +6,16 @@
 //   --lease k8s:NS/NAME     a Kubernetes Lease (coordination.k8s.io/v1): held while renewed every
 //                           quarter of its duration; `leaseTransitions` is the term; a standby
 //                           takes it once the holder's renewTime is older than the duration
+//   --lease etcd:URL/KEY    an etcd v3 key (JSON gateway at URL, e.g. http://etcd:2379) created
+//                           only if absent, bound to an etcd lease kept alive every quarter of
+//                           its TTL; the key's create revision is the term (it grows with every
+//                           holder); a standby takes the key once the holder's lease expires
 //
-// A holder that cannot renew its Kubernetes lease within the duration has lost it and exits: a
+// A holder that cannot renew its Kubernetes or etcd lease within the duration has lost it and exits: a
 // successor may hold it, and two writers of epochs must never overlap.
 //
-// Reference parity: controller/src/lease/{mod,file,kubernetes,renewal}.rs (file lock and
-// Kubernetes Lease with a term, renewal at TTL/4); the etcd backend is not built.
+// Reference parity: controller/src/lease/{mod,file,etcd,kubernetes,renewal}.rs (file lock, etcd
+// and Kubernetes Lease with a term, renewal at TTL/4).
 #pragma once
 
 #include <cstdint>
@@ -49,6 +53,21 @@ class KubeLease : public Lease {
   uint32_t duration_s_;
   uint64_t term_ = 0;
   int64_t acquired_ms_ = 0, last_renewed_ms_ = 0;
+};
+
+class EtcdLease : public Lease {
+ public:
+  EtcdLease(std::string url, std::string key, std::string holder, uint32_t ttl_s);
+  bool acquire(uint64_t& term, std::string& err) override;
+  uint64_t renew_every_ms() const override { return ttl_s_ * 250ull; }
+  bool renew(std::string& err) override;
+
+ private:
+  int post(const std::string& path, const std::string& body, std::string& out) const;
+  std::string url_, key_, holder_, ca_;
+  uint32_t ttl_s_;
+  std::string lease_id_;
+  int64_t last_renewed_ms_ = 0;
 };
 
 }  // namespace es

@@ -37,45 +37,6 @@ class FileSpecStore : public SpecStore {
   std::string dir_;
 };
 
-const char* kB64 = "ABCDEFGHIJKLMNOPQRSTUVWXYZabcdefghijklmnopqrstuvwxyz0123456789+/";
-
-std::string b64(const std::string& in) {
-  std::string out;
-  size_t i = 0;
-  for (; i + 2 < in.size(); i += 3) {
-    const uint32_t v = ((uint8_t)in[i] << 16) | ((uint8_t)in[i + 1] << 8) | (uint8_t)in[i + 2];
-    for (int s = 18; s >= 0; s -= 6) out.push_back(kB64[(v >> s) & 63]);
-  }
-  if (i + 1 == in.size()) {
-    const uint32_t v = (uint8_t)in[i] << 16;
-    out += {kB64[(v >> 18) & 63], kB64[(v >> 12) & 63], '=', '='};
-  } else if (i + 2 == in.size()) {
-    const uint32_t v = ((uint8_t)in[i] << 16) | ((uint8_t)in[i + 1] << 8);
-    out += {kB64[(v >> 18) & 63], kB64[(v >> 12) & 63], kB64[(v >> 6) & 63], '='};
-  }
-  return out;
-}
-
-bool unb64(const std::string& in, std::string& out) {
-  int val[256];
-  for (int& v : val) v = -1;
-  for (int k = 0; k < 64; k++) val[(uint8_t)kB64[k]] = k;
-  out.clear();
-  uint32_t acc = 0;
-  int bits = 0;
-  for (char c : in) {
-    if (c == '=' || c == '\n' || c == '\r') continue;
-    if (val[(uint8_t)c] < 0) return false;
-    acc = (acc << 6) | (uint32_t)val[(uint8_t)c];
-    bits += 6;
-    if (bits >= 8) {
-      bits -= 8;
-      out.push_back((char)((acc >> bits) & 0xff));
-    }
-  }
-  return true;
-}
-
 class KubeSpecStore : public SpecStore {
  public:
   KubeSpecStore(KubeClient k, std::string ns) : k_(std::move(k)), ns_(std::move(ns)) {}
@@ -93,7 +54,7 @@ class KubeSpecStore : public SpecStore {
       const std::string obj = "{\"apiVersion\":\"everserve.ai/v1\",\"kind\":\"EverserveState\",\"metadata\":{\"name\":\"" +
                               name + "\",\"namespace\":\"" + json_escape(ns_) + "\"" +
                               (rv.empty() ? "" : ",\"resourceVersion\":\"" + json_escape(rv) + "\"") +
-                              "},\"spec\":{\"key\":\"" + json_escape(key) + "\",\"data\":\"" + b64(bytes) + "\"}}";
+                              "},\"spec\":{\"key\":\"" + json_escape(key) + "\",\"data\":\"" + base64_encode(bytes) + "\"}}";
       const int w = g == 404 ? k_.request("POST", coll(), obj, out) : k_.request("PUT", coll() + "/" + name, obj, out);
       if (w == 200 || w == 201) return true;
       if (w != 409) {
@@ -122,7 +83,7 @@ class KubeSpecStore : public SpecStore {
         const Json* data = spec ? spec->get("data") : nullptr;
         if (!key || key->str.compare(0, prefix.size(), prefix) != 0) continue;
         std::string bytes;
-        if (data && unb64(data->str, bytes)) out[key->str] = bytes;
+        if (data && base64_decode(data->str, bytes)) out[key->str] = bytes;
       }
     return true;
   }

@@ -139,8 +139,9 @@ class Engine:
         sch.step_id += k - 1
         return [[toks[i][j] for i in range(k)] for j in range(n)]
 
-    def generate(self, prompts: list[list[int]], max_tokens: int = 16) -> list[list[int]]:
-        ids = [self.add_request(p, SamplingParams(max_tokens=max_tokens)) for p in prompts]
+    def generate(self, prompts: list[list[int]], max_tokens: int = 16, **sampling) -> list[list[int]]:
+        """Every prompt to completion; `sampling`: temperature, top_k, top_p, seed (greedy by default)."""
+        ids = [self.add_request(p, SamplingParams(max_tokens=max_tokens, **sampling)) for p in prompts]
         while self.has_work():
             self.step()
         return [self.scheduler.requests[i].outputs for i in ids]

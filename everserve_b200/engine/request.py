@@ -28,9 +28,26 @@ class Status(enum.Enum):
 
 @dataclass
 class SamplingParams:
+    """``temperature`` 0 is greedy; otherwise tokens are drawn with ``top_k`` (0: off) and
+    ``top_p`` (1: off) from a stream keyed by ``seed`` (default: the request id) and the position,
+    so a replayed position draws the same token (everserve_b200.engine.sampling)."""
+
     max_tokens: int = 16
     eos_id: int | None = None
     ignore_eos: bool = True
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    seed: int | None = None
+
+    def sampling_key(self, req_id: str) -> tuple[float, int, float, int] | None:
+        """What a step needs to sample for this request (None: greedy)."""
+        if self.temperature <= 0:
+            return None
+        from .sampling import default_seed
+
+        seed = self.seed if self.seed is not None else default_seed(req_id)
+        return (float(self.temperature), int(self.top_k), float(self.top_p), int(seed) & ((1 << 63) - 1))
 
 
 @dataclass

@@ -9,6 +9,9 @@ kernel skips). Prefill runs eagerly.
 ``decode_loop(k)`` runs k decode steps with no host round trip: after each replay a small kernel
 turns the sampled ids into the next step's inputs (position + 1, the slot from the block table).
 The engine uses it for multi-step decoding when no request can finish inside the window.
+
+A batch with a sampled (temperature > 0) row stages its rows' sampling parameters into static
+buffers too and runs its own graph per bucket; greedy batches keep the greedy graphs.
 """
 
 from __future__ import annotations
@@ -16,6 +19,7 @@ from __future__ import annotations
 import torch
 
 from ..models.llama import DecoderLM, StepInput
+from .sampling import SamplingBatch
 from .scheduler import StepPlan
 
 _BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
@@ -47,8 +51,13 @@ class ModelRunner:
         self.d_bt = torch.zeros(B, self.max_blocks, dtype=torch.int32, device=self.device)
         self.d_ctx32 = torch.zeros(B, dtype=torch.int32, device=self.device)
         self.d_seq = torch.arange(B, dtype=torch.int64, device=self.device)
-        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
-        self.graph_out: dict[int, torch.Tensor] = {}
+        # sampling parameters: rows temperature, top_p (float32) and top_k, seed (int64)
+        self.h_sf = torch.zeros(2, B, dtype=torch.float32, pin_memory=pin)
+        self.h_si = torch.zeros(2, B, dtype=torch.int64, pin_memory=pin)
+        self.d_sf = torch.zeros(2, B, dtype=torch.float32, device=self.device)
+        self.d_si = torch.zeros(2, B, dtype=torch.int64, device=self.device)
+        self.graphs: dict[tuple[int, bool], torch.cuda.CUDAGraph] = {}  # (bucket, sampled)
+        self.graph_out: dict[tuple[int, bool], torch.Tensor] = {}
         self.h_out = torch.zeros(B, dtype=torch.int64, pin_memory=pin)
         self._pool = None
         if self.device.type == "cuda" and model.ops.kind == "kernel":
@@ -61,6 +70,24 @@ class ModelRunner:
             if b >= n:
                 return b
         raise ValueError(f"batch {n} above max_batch {self.max_batch}")
+
+    @staticmethod
+    def sampled(plan: StepPlan) -> bool:
+        return any(r.sampling is not None for r in plan.reqs)
+
+    def _stage_sampling(self, plan: StepPlan, b: int) -> None:
+        hf, hi = self.h_sf.numpy(), self.h_si.numpy()
+        hf[0, :b], hf[1, :b], hi[0, :b], hi[1, :b] = 0.0, 1.0, 0, 0
+        for i, r in enumerate(plan.reqs):
+            if r.sampling is not None:
+                hf[0, i], hi[0, i], hf[1, i], hi[1, i] = r.sampling
+        self.d_sf[:, :b].copy_(self.h_sf[:, :b], non_blocking=True)
+        self.d_si[:, :b].copy_(self.h_si[:, :b], non_blocking=True)
+        self.h2d_bytes += 2 * b * 4 + 2 * b * 8
+
+    def _sampling_batch(self, b: int) -> SamplingBatch:
+        return SamplingBatch(temperature=self.d_sf[0, :b], top_k=self.d_si[0, :b], top_p=self.d_sf[1, :b],
+                             seed=self.d_si[1, :b])
 
     def stage_decode(self, plan: StepPlan) -> int:
         """Copy a decode plan's inputs into the static device buffers; returns the bucket size."""
@@ -82,13 +109,16 @@ class ModelRunner:
         self.d_i64[:, :b].copy_(self.h_i64[:, :b], non_blocking=True)
         self.d_bt[:b].copy_(self.h_bt[:b], non_blocking=True)
         self.h2d_bytes = 4 * b * 8 + b * self.max_blocks * 4
+        if self.sampled(plan):
+            self._stage_sampling(plan, b)
         return b
 
-    def _decode_input(self, b: int) -> StepInput:
+    def _decode_input(self, b: int, sampled: bool = False) -> StepInput:
         self.d_ctx32[:b].copy_(self.d_i64[3, :b])
         return StepInput(ids=self.d_i64[0, :b], positions=self.d_i64[1, :b], slots=self.d_i64[2, :b],
                          block_tables=self.d_bt[:b], ctx_lens=self.d_ctx32[:b], q_seq=self.d_seq[:b],
-                         logits_idx=self.d_seq[:b], is_decode=True, max_model_len=self.max_model_len)
+                         logits_idx=self.d_seq[:b], is_decode=True, max_model_len=self.max_model_len,
+                         sampling=self._sampling_batch(b) if sampled else None)
 
     def prefill_input(self, plan: StepPlan) -> StepInput:
         ids, pos, slots, seq, last, ctx = [], [], [], [], [], []
@@ -106,9 +136,14 @@ class ModelRunner:
             bt[i, : len(r.block_table)] = torch.tensor(r.block_table, dtype=torch.int32)
         dev = self.device
         t = lambda v, dt=torch.int64: torch.tensor(v, dtype=dt).to(dev, non_blocking=True)  # noqa: E731
+        sb = None
+        if self.sampled(plan):
+            ps = [r.sampling or (0.0, 0, 1.0, 0) for r in plan.reqs]
+            sb = SamplingBatch(temperature=t([p[0] for p in ps], torch.float32), top_k=t([p[1] for p in ps]),
+                               top_p=t([p[2] for p in ps], torch.float32), seed=t([p[3] for p in ps]))
         return StepInput(ids=t(ids), positions=t(pos), slots=t(slots), block_tables=bt.to(dev),
                          ctx_lens=t(ctx, torch.int32), q_seq=t(seq), logits_idx=t(last), is_decode=False,
-                         max_model_len=self.max_model_len)
+                         max_model_len=self.max_model_len, sampling=sb)
 
     # ---- forward ---------------------------------------------------------------------------------
     def forward(self, inp: StepInput, hidden=None, residual=None):
@@ -120,26 +155,27 @@ class ModelRunner:
             return self.forward(self.prefill_input(plan), hidden, residual)
         n = len(plan.reqs)
         b = self.stage_decode(plan)
+        key = (b, self.sampled(plan))
         if self.use_graphs and self.model.last and self.model.first:
-            g = self.graphs.get(b)
+            g = self.graphs.get(key)
             if g is None:
-                self._capture(b)
-                g = self.graphs[b]
+                self._capture(*key)
+                g = self.graphs[key]
             g.replay()
-            return self.graph_out[b][:n]
-        out = self.forward(self._decode_input(b), hidden, residual)
+            return self.graph_out[key][:n]
+        out = self.forward(self._decode_input(*key), hidden, residual)
         if isinstance(out, tuple):
             return out[0][:n], out[1][:n]
         return out[:n]
 
-    def _capture(self, b: int) -> None:
+    def _capture(self, b: int, sampled: bool = False) -> None:
         # warm up on a side stream (allocator and lazily configured kernels), then capture
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         saved = self.d_i64[:, :b].clone(), self.d_bt[:b].clone()
         with torch.cuda.stream(s):
             for _ in range(2):
-                self.forward(self._decode_input(b))
+                self.forward(self._decode_input(b, sampled))
         torch.cuda.current_stream(self.device).wait_stream(s)
         self.d_i64[:, :b].copy_(saved[0])
         self.d_bt[:b].copy_(saved[1])
@@ -147,9 +183,9 @@ class ModelRunner:
         if self._pool is None:
             self._pool = torch.cuda.graph_pool_handle()
         with torch.cuda.graph(g, pool=self._pool):
-            out = self.forward(self._decode_input(b))
-        self.graphs[b] = g
-        self.graph_out[b] = out
+            out = self.forward(self._decode_input(b, sampled))
+        self.graphs[(b, sampled)] = g
+        self.graph_out[(b, sampled)] = out
 
     def release_graphs(self) -> None:
         """Drop every captured graph (a graph holding NCCL calls must go before the process group)."""
@@ -163,7 +199,7 @@ class ModelRunner:
         if not self.use_graphs:
             return
         for b in self.buckets:
-            if b not in self.graphs:
+            if (b, False) not in self.graphs:
                 self._capture(b)
 
     # ---- multi-step decode -----------------------------------------------------------------------
@@ -174,16 +210,17 @@ class ModelRunner:
         """
         n = len(plan.reqs)
         b = self.stage_decode(plan)
+        key = (b, self.sampled(plan))
         out = torch.empty(k, n, dtype=torch.int64, device=self.device)
-        if self.use_graphs and b not in self.graphs:
-            self._capture(b)
+        if self.use_graphs and key not in self.graphs:
+            self._capture(*key)
         bs = self.block_size
         for i in range(k):
             if self.use_graphs:
-                self.graphs[b].replay()
-                ids = self.graph_out[b]
+                self.graphs[key].replay()
+                ids = self.graph_out[key]
             else:
-                ids = self.forward(self._decode_input(b))
+                ids = self.forward(self._decode_input(*key))
             out[i] = ids[:n]
             if i + 1 < k:
                 self._advance(b, ids, bs)

@@ -28,6 +28,7 @@ class ScheduledReq:
     block_table: list[int]
     sample: bool  # the last fed position is the request's last token: its sample is a new output
     expect: int | None = None  # replayed position: the output already recorded there
+    sampling: tuple | None = None  # (temperature, top_k, top_p, seed); None: greedy
 
 
 @dataclass
@@ -105,7 +106,8 @@ class Scheduler:
             req.status = Status.RUNNING
             self.running.append(req)
             plan.reqs.append(ScheduledReq(req.req_id, req.tokens[req.num_computed:], req.num_computed,
-                                          list(req.blocks), sample=True))
+                                          list(req.blocks), sample=True,
+                                          sampling=req.params.sampling_key(req.req_id)))
             budget -= n
         return plan if plan.reqs else None
 
@@ -132,7 +134,8 @@ class Scheduler:
             p = req.num_computed
             last = p == req.num_tokens - 1
             plan.reqs.append(ScheduledReq(req.req_id, [req.tokens[p]], p, list(req.blocks), sample=last,
-                                          expect=None if last else req.tokens[p + 1]))
+                                          expect=None if last else req.tokens[p + 1],
+                                          sampling=req.params.sampling_key(req.req_id)))
         return plan
 
     def _preempt(self, req: Request) -> None:

@@ -38,6 +38,7 @@ class StepInput:
     logits_idx: torch.Tensor  # [B] int64: each sequence's last row
     is_decode: bool
     max_model_len: int = 0
+    sampling: object | None = None  # engine.sampling.SamplingBatch of the rows; None: greedy
 
 
 def _seed_of(seed: int, *parts) -> int:
@@ -250,7 +251,19 @@ class DecoderLM:
         h_last = h.index_select(0, inp.logits_idx) if h.shape[0] != inp.logits_idx.shape[0] else h
         head = W["embed"] if c.tie_embeddings else W["lm_head"]
         logits = ops.linear(h_last, head)
+        if inp.sampling is not None:
+            return self._sample(logits, inp)
         return self._greedy(logits)
+
+    def _sample(self, logits: torch.Tensor, inp: StepInput) -> torch.Tensor:
+        """Seeded sampling of every row (engine.sampling); each tensor-parallel rank gathers the
+        full vocabulary and draws the same tokens."""
+        from ..engine.sampling import sample
+
+        full = logits if self.tp.size == 1 else self.tp.all_gather_rows(logits.contiguous())
+        full = full[:, : self.cfg.vocab]
+        pos = inp.positions if inp.positions.shape[0] == full.shape[0] else inp.positions.index_select(0, inp.logits_idx)
+        return sample(full, pos, inp.sampling)
 
     def logits(self, inp: StepInput, caches, hidden=None, residual=None):
         """Full-vocab logits of each sequence's last row (tests and the CPU oracle)."""

@@ -2,7 +2,8 @@
 
     python -m everserve_b200.serving.api --model llama-3-8b --port 8000 [--checkpoint DIR] [--tp 8 ...]
 
-``POST /v1/completions`` with ``{"prompt": [token ids] | "text", "max_tokens": n, "stream": bool}``
+``POST /v1/completions`` with ``{"prompt": [token ids] | "text", "max_tokens": n, "stream": bool,
+"temperature": t, "top_k": k, "top_p": p, "seed": s}`` (temperature 0, the default, is greedy)
 returns ``choices[0].token_ids`` (and ``text`` when a tokenizer is configured); with
 ``"stream": true`` it sends one server-sent event per new token. ``GET /v1/models``, ``GET /live``
 and ``GET /ready`` report the model and health (``/ready`` is 503 while a membership change is
@@ -132,7 +133,11 @@ def build_app(loop: EngineLoop, model_name: str, vocab: int, tokenizer=None):
         prompt = encode(body.get("prompt", ""))
         if not prompt:
             raise HTTPException(400, "empty prompt")
-        params = SamplingParams(max_tokens=int(body.get("max_tokens", 16)))
+        seed = body.get("seed")
+        params = SamplingParams(max_tokens=int(body.get("max_tokens", 16)),
+                                temperature=float(body.get("temperature", 0.0) or 0.0),
+                                top_k=int(body.get("top_k", 0) or 0), top_p=float(body.get("top_p", 1.0) or 1.0),
+                                seed=int(seed) if seed is not None else None)
         p = loop.submit(prompt, params)
         created = int(time.time())
 

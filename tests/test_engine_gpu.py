@@ -52,3 +52,15 @@ def test_graphs_match_eager_and_multistep(cuda):
     while eng.has_work():
         eng.step()
     assert [eng.request(i).outputs for i in ids] == outs[1]
+
+
+def test_sampled_graphs_match_eager_and_replay(cuda):
+    """Seeded sampling in captured decode graphs draws what eager decode draws, run after run."""
+    prompts = [[3, 1, 4, 1, 5, 9, 2, 6], list(range(40, 77)), [7] * 20]
+    kw = dict(max_tokens=24, temperature=0.7, top_p=0.9, top_k=50, seed=2024)
+    eager = Engine(_cfg(TINY_QWEN, graphs=False)).generate(prompts, **kw)
+    graphs = Engine(_cfg(TINY_QWEN, graphs=True)).generate(prompts, **kw)
+    again = Engine(_cfg(TINY_QWEN, graphs=True)).generate(prompts, **kw)
+    greedy = Engine(_cfg(TINY_QWEN, graphs=True)).generate(prompts, max_tokens=24)
+    assert graphs == again and graphs == eager
+    assert graphs != greedy

@@ -33,7 +33,7 @@ def _prompts():
     return [[rng.randrange(vocab) for _ in range(PROMPT)] for _ in range(STREAMS)]
 
 
-def _run(workdir, kill_at=None, spares=(1,)):
+def _run(workdir, kill_at=None, spares=(1,), **sampling):
     cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
                        max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
     with ControlPlane(str(workdir), engines=[{"name": "e0", "pipelineParallel": 2}]) as cp:
@@ -47,7 +47,7 @@ def _run(workdir, kill_at=None, spares=(1,)):
             eng.wrap_step(failover(ex, eng))
             if kill_at is not None:
                 ex.kill_at_decode_step = (kill_at, 1)
-            out = eng.generate(_prompts(), max_tokens=TOKENS)
+            out = eng.generate(_prompts(), max_tokens=TOKENS, **sampling)
             mism = sum(r.replay_mismatches for r in eng.scheduler.requests.values())
             view = cp.engine_view("e0")
             return out, ex.changes, mism, view
@@ -246,3 +246,16 @@ def test_node_agent_starts_remote_ranks(tmp_path):
         finally:
             ex.shutdown()
             assert agent.wait(timeout=60) == 0
+
+
+@pytest.mark.slow
+def test_sampled_streams_replay_exactly_after_sigkill(tmp_path):
+    """Temperature / top-p / top-k sampling with a seed: the resumed streams draw what the lost
+    rank's steps drew (the draw is a function of seed and position), so they finish identical."""
+    kw = dict(temperature=0.8, top_p=0.95, top_k=40, seed=5)
+    base, _, _, _ = _run(tmp_path / "nofault", spares=(), **kw)
+    greedy, _, _, _ = _run(tmp_path / "greedy", spares=())
+    assert base != greedy
+    out, changes, mism, _ = _run(tmp_path / "fault", kill_at=KILL_AT, **kw)
+    assert len(changes) == 1 and mism == 0
+    assert out == base

@@ -3,6 +3,7 @@ resourceVersion conflicts, bearer tokens): the first coordinator holds term 1 an
 standby takes term 2 once the holder is killed and its renewTime runs out; a holder whose lease
 another process took exits rather than write epochs beside it."""
 
+import base64
 import json
 import os
 import signal
@@ -236,3 +237,114 @@ def test_file_spec_store_keeps_cordons_across_a_restart(tmp_path):
         wait_listening(cp.api)
         nodes = {n["metadata"]["name"]: n for n in cp.get("/v1/nodes")["items"]}
         assert nodes["n0"]["spec"]["unschedulable"] is True
+
+
+class FakeEtcd:
+    """etcd v3's JSON gateway, as much as a lease holder uses: lease grant and keepalive, a
+    create-if-absent transaction, keys dropped when their lease expires, a revision counter."""
+
+    def __init__(self):
+        self.lock = threading.Lock()
+        self.rev = 100
+        self.leases = {}  # id -> (ttl, expires_at)
+        self.kv = {}  # key -> (value, create_revision, lease id)
+        self.next_id = 7000
+        fake = self
+
+        class H(BaseHTTPRequestHandler):
+            def _send(self, obj):
+                body = json.dumps(obj).encode()
+                self.send_response(200)
+                self.send_header("Content-Length", str(len(body)))
+                self.end_headers()
+                self.wfile.write(body)
+
+            def do_POST(self):  # noqa: N802
+                req = json.loads(self.rfile.read(int(self.headers.get("Content-Length", "0"))) or b"{}")
+                now = time.monotonic()
+                with fake.lock:
+                    for lid, (ttl, exp) in list(fake.leases.items()):
+                        if exp < now:  # expired: its keys go
+                            del fake.leases[lid]
+                            for k in [k for k, v in fake.kv.items() if v[2] == lid]:
+                                del fake.kv[k]
+                                fake.rev += 1
+                    if self.path == "/v3/lease/grant":
+                        fake.next_id += 1
+                        fake.leases[str(fake.next_id)] = (int(req["TTL"]), now + int(req["TTL"]))
+                        return self._send({"ID": str(fake.next_id), "TTL": str(req["TTL"])})
+                    if self.path == "/v3/lease/keepalive":
+                        lid = str(req["ID"])
+                        if lid not in fake.leases:
+                            return self._send({"result": {"ID": lid}})  # TTL absent: gone
+                        ttl = fake.leases[lid][0]
+                        fake.leases[lid] = (ttl, now + ttl)
+                        return self._send({"result": {"ID": lid, "TTL": str(ttl)}})
+                    if self.path == "/v3/kv/txn":
+                        key = base64.b64decode(req["compare"][0]["key"]).decode()
+                        if key not in fake.kv:
+                            put = req["success"][0]["request_put"]
+                            fake.rev += 1
+                            fake.kv[key] = (base64.b64decode(put["value"]).decode(), fake.rev, str(put["lease"]))
+                            return self._send({"header": {"revision": str(fake.rev)}, "succeeded": True})
+                        return self._send({"header": {"revision": str(fake.rev)}, "succeeded": False})
+                self.send_response(404)
+                self.end_headers()
+
+            def log_message(self, *a):
+                pass
+
+        self.server = ThreadingHTTPServer(("127.0.0.1", 0), H)
+        self.url = f"http://127.0.0.1:{self.server.server_address[1]}"
+        threading.Thread(target=self.server.serve_forever, daemon=True).start()
+
+    def holder(self, key="/everserve/coord"):
+        with self.lock:
+            v = self.kv.get(key)
+            return (v[0], v[1]) if v else None
+
+    def revoke_all(self):
+        with self.lock:
+            self.leases.clear()
+            self.kv.clear()
+
+    def close(self):
+        self.server.shutdown()
+
+
+def test_etcd_lease_term_standby_and_loss(tmp_path):
+    etcd = FakeEtcd()
+    procs = []
+
+    def coord(name):
+        api = f"127.0.0.1:{free_port()}"
+        log = open(tmp_path / f"{name}.log", "w")  # noqa: SIM115
+        p = subprocess.Popen([binary("everserve-coord"), "--listen", f"unix:{tmp_path}/{name}.sock", "--spec-store",
+                              str(tmp_path / "spec"), "--lease", f"etcd:{etcd.url}/everserve/coord",
+                              "--lease-duration-s", "2", "--lease-holder", name, "--api-addr", api],
+                             stdout=log, stderr=subprocess.STDOUT)
+        procs.append(p)
+        return p, api
+
+    try:
+        a, api_a = coord("coord-a")
+        wait_listening(api_a)
+        held = etcd.holder()
+        assert held[0] == "coord-a"
+        b, api_b = coord("coord-b")
+        time.sleep(1.5)
+        assert b.poll() is None and etcd.holder()[0] == "coord-a"  # a keeps its lease alive
+        a.send_signal(signal.SIGKILL)
+        a.wait()
+        wait_listening(api_b, timeout_s=15)  # a's etcd lease expires, its key goes, b creates it
+        held_b = etcd.holder()
+        assert held_b[0] == "coord-b" and held_b[1] > held[1]  # the term (create revision) grew
+        assert f"term {held_b[1]}" in open(tmp_path / "coord-b.log").read()
+        etcd.revoke_all()  # b's lease is gone: it stops
+        assert b.wait(timeout=10) == 3
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+                p.wait()
+        etcd.close()
