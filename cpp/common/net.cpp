@@ -68,7 +68,7 @@ int listen_on(const Address& a, std::string* err) {
     }
     std::strcpy(sa.sun_path, a.path.c_str());
     ::unlink(a.path.c_str());
-    if (::bind(fd, (sockaddr*)&sa, sizeof(sa)) != 0 || ::listen(fd, 128) != 0) {
+    if (::bind(fd, (sockaddr*)&sa, sizeof(sa)) != 0 || ::listen(fd, SOMAXCONN > 4096 ? SOMAXCONN : 4096) != 0) {
       if (err) *err = std::string("bind/listen ") + a.path + ": " + strerror(errno);
       ::close(fd);
       return -1;
@@ -82,7 +82,7 @@ int listen_on(const Address& a, std::string* err) {
     sa.sin_port = htons((uint16_t)a.port);
     if (a.host.empty() || a.host == "0.0.0.0") sa.sin_addr.s_addr = INADDR_ANY;
     else inet_pton(AF_INET, a.host == "localhost" ? "127.0.0.1" : a.host.c_str(), &sa.sin_addr);
-    if (::bind(fd, (sockaddr*)&sa, sizeof(sa)) != 0 || ::listen(fd, 128) != 0) {
+    if (::bind(fd, (sockaddr*)&sa, sizeof(sa)) != 0 || ::listen(fd, SOMAXCONN > 4096 ? SOMAXCONN : 4096) != 0) {
       if (err) *err = std::string("bind/listen ") + a.str() + ": " + strerror(errno);
       ::close(fd);
       return -1;

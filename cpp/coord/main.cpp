@@ -79,6 +79,7 @@ struct Engine {
   std::map<std::pair<std::string, uint32_t>, SpareSeat> standing;
   std::map<std::pair<std::string, uint32_t>, std::string> refused;
   std::set<std::string> head_nodes;
+  std::set<std::string> listeners;  // nodes where a process asked for the engine's start-up record
   std::set<uint32_t> pending;
   std::set<uint32_t> departing;  // planned departures among pending
   uint64_t first_report_us = 0;
@@ -422,7 +423,7 @@ struct Coordinator {
           " ms");
     e.in_flight.reset();
     admit(e);
-    update_gauges();
+    update_gauges(&e);
     replan(e);
     replicate(e);
     reconcile_pools();
@@ -452,15 +453,37 @@ struct Coordinator {
     admit(e);
   }
 
-  void update_gauges() {
+  // The spare gauge of `only` (of every engine when `all`): per-engine gauges are set where that
+  // engine changed, so an event costs O(1) metric writes whatever the fleet's size; the
+  // fleet-wide gauges are refreshed on a timer (fleet_gauges).
+  void update_gauges(const Engine* only = nullptr, bool all = false) {
+    if (all)
+      for (auto& [name, e] : engines)
+        metrics().set("everserve_spares", {{"engine", name}, {"state", "standing"}}, (double)e.spares.size());
+    else if (only != nullptr)
+      metrics().set("everserve_spares", {{"engine", only->name}, {"state", "standing"}}, (double)only->spares.size());
+  }
+
+  void fleet_gauges() {
     uint64_t linked = 0, workers = 0;
     for (auto& [n, node] : nodes) linked += node.linked;
-    for (auto& [name, e] : engines) {
-      workers += e.workers.size();
-      metrics().set("everserve_spares", {{"engine", name}, {"state", "standing"}}, (double)e.spares.size());
-    }
+    for (auto& [name, e] : engines) workers += e.workers.size();
     metrics().set("everserve_daemons_connected", {}, (double)linked);
     metrics().set("everserve_workers_registered", {}, (double)workers);
+  }
+
+  // Whether `node` needs `e`'s placement (placement_nodes, by lookups rather than a full walk).
+  bool needs_placement(const Engine& e, const std::string& node) const {
+    if (e.head_nodes.count(node) || e.listeners.count(node)) return true;
+    for (auto& [r, h] : e.workers)
+      if (h.node == node) return true;
+    auto st = e.standing.lower_bound({node, 0});
+    if (st != e.standing.end() && st->first.first == node) return true;
+    auto ep = policy.engines.find(e.name);
+    if (ep != policy.engines.end())
+      for (auto& slot : ep->second.spare_slots)
+        if (slot.node == node) return true;
+    return false;
   }
 
   // ---- takeover: views from the spec store and the daemons' announcements ----------------------
@@ -550,7 +573,25 @@ struct Coordinator {
   }
 
   // ---- placement: where each rank runs, its compile-cache pair and the stores that hold it -----
-  void send_placement(const Engine& e) {
+  // The nodes that need an engine's placement: its ranks', heads' and spares' nodes, and the
+  // nodes where spares for it are launched (they fetch the engine's compile cache from it).
+  std::set<std::string> placement_nodes(const Engine& e) {
+    std::set<std::string> to = engine_nodes(e);
+    for (auto& [key, seat] : e.standing) to.insert(key.first);
+    to.insert(e.listeners.begin(), e.listeners.end());
+    auto ep = policy.engines.find(e.name);
+    if (ep != policy.engines.end())
+      for (auto& slot : ep->second.spare_slots) to.insert(slot.node);
+    for (auto& [key, launch] : pool_launches) {
+      auto pit = pools.find(launch.first);
+      if (pit != pools.end() &&
+          std::find(pit->second.engines.begin(), pit->second.engines.end(), e.name) != pit->second.engines.end())
+        to.insert(key.first);
+    }
+    return to;
+  }
+
+  void send_placement(const Engine& e, const std::string& only_node = "") {
     coord::CoordToDaemon m;
     m.has_engine_placement = true;
     auto& pl = m.engine_placement;
@@ -586,9 +627,8 @@ struct Coordinator {
       s.device = sp.device;
       pl.spares.push_back(s);
     }
-    // every linked node: a spare for the engine may be starting anywhere
-    for (auto& [name, n] : nodes)
-      if (n.linked) to_node(name, m);
+    for (auto& n : placement_nodes(e))
+      if (only_node.empty() || n == only_node) to_node(n, m);
   }
 
   // ---- spare admission: identity, cordons, pools and the fit of the spare's device -------------
@@ -668,7 +708,7 @@ struct Coordinator {
     e.refused = std::move(refused);
   }
 
-  void readmit_all() {
+  void readmit_all() {  // after a cordon, a pool write: every engine
     for (auto& [name, e] : engines) {
       const size_t before = e.spares.size();
       admit(e);
@@ -677,7 +717,7 @@ struct Coordinator {
         replicate(e);
       }
     }
-    update_gauges();
+    update_gauges(nullptr, true);
   }
 
   // ---- pools: spare capacity for engines of one shape ------------------------------------------
@@ -727,6 +767,7 @@ struct Coordinator {
 
   // Launch what each pool is short of on free devices of linked, uncordoned nodes.
   void reconcile_pools() {
+    if (pools.empty() && pool_launches.empty()) return;
     const uint64_t now = now_ms();
     for (auto it = pool_launches.begin(); it != pool_launches.end();)  // launches that never registered
       it = now - it->second.second > pool_warm_ms ? pool_launches.erase(it) : std::next(it);
@@ -762,6 +803,10 @@ struct Coordinator {
         to_node(node, m);
         pool_launches[{node, device}] = {name, now};
         busy.insert({node, device});
+        for (auto& en : pool.engines) {
+          auto eit = engines.find(en);
+          if (eit != engines.end()) send_placement(eit->second, node);
+        }
         event("pool " + name + ": spare launch asked of " + node + ":" + std::to_string(device));
       }
     }
@@ -769,6 +814,8 @@ struct Coordinator {
       const PoolCount c = pool_count(name);
       metrics().set("everserve_pool_spares", {{"pool", name}, {"state", "standing"}}, c.standing);
       metrics().set("everserve_pool_spares", {{"pool", name}, {"state", "warming"}}, c.warming);
+      metrics().set("everserve_pool_deficit", {{"pool", name}},
+                    pool.wants > c.standing + c.warming ? pool.wants - c.standing - c.warming : 0);
     }
   }
 
@@ -966,7 +1013,7 @@ struct Coordinator {
     }
     if (ev.kind == K::WorkerEvent_Kind_SPARE_REGISTERED) pool_launches.erase({node, ev.device});
     admit(e);
-    update_gauges();
+    update_gauges(&e);
     replan(e);
     replicate(e);
     reconcile_pools();
@@ -1015,11 +1062,14 @@ struct Coordinator {
         e.epoch = std::max(e.epoch, st.epoch);
       }
       event("node " + node + " linked (" + std::to_string(m.hello.devices.size()) + " device(s))");
-      for (auto& [ename, en] : engines) admit(en);
-      update_gauges();
+      // this node's devices change the fit of spares on it and of positions held on it
+      for (auto& [ename, en] : engines)
+        if (needs_placement(en, node)) {
+          admit(en);
+          send_placement(en, node);  // what this node's processes need
+        }
       launch_spares(node);
       reconcile_pools();
-      for (auto& [ename, en] : engines) send_placement(en);
       loop.every(200, [this] {
         for (auto& [name, en] : engines) try_resume(en);
       }, false);
@@ -1079,6 +1129,9 @@ struct Coordinator {
         out.has_replay_ask = true;
         out.replay_ask = m.replay_ask;
         eng = m.replay_ask.engine;
+        // a process starting for the engine on this node (a spare): it will want the placement
+        Engine& le = engine(eng);
+        if (le.listeners.insert(node).second) send_placement(le, node);
       } else {
         // an offer goes back to the node of the process that asked
         out.has_replay_offer = true;
@@ -1121,7 +1174,7 @@ struct Coordinator {
     for (auto it = pool_launches.begin(); it != pool_launches.end();)
       it = it->first.first == node ? pool_launches.erase(it) : std::next(it);
     topo.remove_node(node);
-    update_gauges();
+    update_gauges(nullptr, true);
     reconcile_pools();
   }
 
@@ -1529,6 +1582,7 @@ int main(int argc, char** argv) {
   metrics().describe("everserve_api_refusals_total", "Operator API requests refused by the token gate, by code", "counter");
   metrics().describe("everserve_enrollments_total", "Node certificate requests by verdict (issued, refused)", "counter");
   metrics().describe("everserve_pool_spares", "Spares of each pool by state (standing, warming)", "gauge");
+  metrics().describe("everserve_pool_deficit", "Spares a pool wants beyond those standing or warming", "gauge");
   metrics().describe("everserve_unheard_ranks_lost_total", "Loss reports naming ranks the coordinator does not hold", "counter");
   Address a;
   if (!Address::parse(listen, a) || !co.loop.listen(a, [&](Conn& c) {
@@ -1580,7 +1634,10 @@ int main(int argc, char** argv) {
     return 1;
   }
   co.loop.every(100, [&] { co.check_heartbeats(); });
-  co.loop.every(1000, [&] { co.reconcile_pools(); });
+  co.loop.every(1000, [&] {
+    co.reconcile_pools();
+    co.fleet_gauges();
+  });
   ES_INFO("coordinator term %llu listening on %s", (unsigned long long)co.term, listen.c_str());
   co.loop.run();
   return 0;

@@ -172,6 +172,8 @@ struct Daemon {
   Loop loop;
   std::map<uint64_t, Proc> procs;
   uint64_t coord_conn = 0;
+  bool connecting = false;        // a link attempt is in flight on its helper thread
+  uint64_t unlinked_at_ms = 0;    // when the last link ended (for the relink time)
   uint64_t term = 0;
   std::deque<std::string> held;  // reports made while unlinked
   std::map<uint64_t, PendingDelivery> deliveries;
@@ -185,6 +187,7 @@ struct Daemon {
   std::map<std::string, Supervised> supervised;  // engine:device (or pool/<pool>:device) -> launched spare
   std::vector<coord::Device> devices;            // this node's GPUs, announced in every hello
   std::map<std::string, signals::EnginePlacement> placements;  // the coordinator's latest, by engine
+  std::map<std::string, std::set<uint32_t>> departing;  // per engine: the last change's planned departures
   // compile-cache asks waiting for their rank's pair to be placed (answered or refused by deadline)
   struct CacheWait {
     uint64_t conn = 0;
@@ -232,13 +235,24 @@ struct Daemon {
     loop.send(coord_conn, m.serialize());
   }
 
+  // The coordinator link: connected on a helper thread (a TCP connect to a dead host would hold
+  // the loop for its timeout) and adopted on the loop, with jittered backoff between attempts.
   void link() {
-    if (coordinator.empty() || coord_conn != 0) return;
-    Address a;
-    std::string err;
-    int fd = -1;
-    if (Address::parse(coordinator, a)) fd = connect_to(a, 1000, &err);
+    if (coordinator.empty() || coord_conn != 0 || connecting) return;
+    connecting = true;
+    const std::string addr = coordinator;
+    std::thread([this, addr] {
+      Address a;
+      std::string err;
+      const int fd = Address::parse(addr, a) ? connect_to(a, 1000, &err) : -1;
+      loop.post([this, fd] { linked(fd); });
+    }).detach();
+  }
+
+  void linked(int fd) {
+    connecting = false;
     if (fd < 0) {
+      metrics().inc("everserve_coordinator_unreachable_total");
       std::uniform_int_distribution<uint64_t> jit(0, backoff_ms / 2);
       const uint64_t wait = backoff_ms + jit(rng);
       backoff_ms = std::min<uint64_t>(backoff_ms * 2, 2000);
@@ -252,7 +266,9 @@ struct Daemon {
     c->on_close = [this](Conn&) {
       ES_WARN("coordinator link lost");
       metrics().set("everserve_node_linked", {}, 0);
+      metrics().set("everserve_coordinator_linked", {}, 0);
       coord_conn = 0;
+      unlinked_at_ms = now_ms();
       loop.every(100, [this] { link(); }, false);
     };
     send_hello();
@@ -265,6 +281,11 @@ struct Daemon {
       if (p.registered && registered_kind(p.role) != coord::WorkerEvent_Kind_KIND_UNSPECIFIED)
         worker_event(p, registered_kind(p.role), 0, "");
     metrics().set("everserve_node_linked", {}, 1);
+    metrics().set("everserve_coordinator_linked", {}, 1);
+    if (unlinked_at_ms) {
+      metrics().observe("everserve_coordinator_relink_seconds", {}, (now_ms() - unlinked_at_ms) * 1e-3);
+      unlinked_at_ms = 0;
+    }
     ES_INFO("linked to coordinator %s", coordinator.c_str());
   }
 
@@ -289,6 +310,7 @@ struct Daemon {
     if (m.term < term) return;  // an old coordinator: fenced
     term = std::max(term, m.term);
     if (m.has_deliver) {
+      departing[m.deliver.engine] = std::set<uint32_t>(m.deliver.change.departing.begin(), m.deliver.change.departing.end());
       deliver(m.deliver);
     } else if (m.has_committed) {
       epochs[m.committed.engine] = std::max(epochs[m.committed.engine], m.committed.membership.epoch);
@@ -308,6 +330,7 @@ struct Daemon {
             p.any_rank = false;
             break;
           }
+      fence_displaced(m.committed);
     } else if (m.has_abandon) {
       signals::Signal s;
       s.has_abandoned = true;
@@ -714,6 +737,35 @@ struct Daemon {
     ES_INFO("store of %s replicates %s to %zu target(s)", node.c_str(), key.c_str(), t.targets.size());
   }
 
+  // ---- fencing: a worker of this node whose rank the commit gave away, still running -------------
+  // A lost rank that did not leave by notice and whose process is still connected is hung or cut
+  // off; its position now belongs to another process. It is stopped (SIGTERM, SIGKILL after
+  // 5 s) so it can write nothing more and its GPU is free again. Planned departures finish their
+  // step and are released by the head; they are left alone.
+  void fence_displaced(const coord::Committed& c) {
+    const auto& gone = departing[c.engine];
+    for (uint32_t r : c.lost) {
+      if (gone.count(r)) continue;
+      const signals::Take* take = nullptr;
+      for (auto& t : c.take)
+        if (t.rank == r) take = &t;
+      for (auto& [id, p] : procs) {
+        if (!p.registered || p.engine != c.engine || p.rank != r || p.role != signals::Role_ROLE_WORKER ||
+            p.os_pid <= 0)
+          continue;
+        if (take != nullptr && take->node == node && take->device == p.device) continue;  // the new holder
+        const pid_t pid = (pid_t)p.os_pid;
+        ES_WARN("fencing %s rank %u (process %d): the commit to epoch %llu gave its position away", c.engine.c_str(),
+                r, (int)pid, (unsigned long long)c.membership.epoch);
+        metrics().inc("everserve_node_fenced_total", {{"engine", c.engine}});
+        kill(pid, SIGTERM);
+        loop.every(5000, [pid] {
+          if (kill(pid, 0) == 0) kill(pid, SIGKILL);
+        }, false);
+      }
+    }
+  }
+
   // ---- compile caches: a spare's rank's artifacts, fetched into this node's store ----------------
   void cache_answer(uint64_t conn, const signals::CacheWanted& want, bool ok, const signals::CompileCache& pair,
                     const std::string& why) {
@@ -1019,6 +1071,10 @@ int main(int argc, char** argv) {
   d.devices = list_devices(devices_from, domain);
   ES_INFO("%zu device(s) on %s", d.devices.size(), d.node.c_str());
   metrics().describe("everserve_node_linked", "1 while the daemon is linked to the coordinator", "gauge");
+  metrics().describe("everserve_node_fenced_total", "Displaced workers this daemon stopped after a commit", "counter");
+  metrics().describe("everserve_coordinator_linked", "1 while the daemon is linked to the coordinator", "gauge");
+  metrics().describe("everserve_coordinator_relink_seconds", "From a lost coordinator link to the next one", "histogram");
+  metrics().describe("everserve_coordinator_unreachable_total", "Link attempts the coordinator did not answer", "counter");
   metrics().describe("everserve_node_workers", "Workers registered on this node", "gauge");
   Address a;
   std::string err;

@@ -170,6 +170,7 @@ void handle(Storage& st, Carrier& carrier, CompileCacheDir& cache, Loop& loop, C
     // a new target first gets everything the rank has written (queued ahead of its next commits)
     for (const auto& target : req.replicate.targets) {
       if (std::find(before.begin(), before.end(), target) != before.end()) continue;
+      metrics().inc("everserve_store_snapshots_total");
       for (auto& part : st.snapshot_of(req.replicate.engine, req.replicate.rank, kMaxFrame - 4096)) {
         mirror::MirrorRequest out;
         out.has_replicated = true;
@@ -262,6 +263,7 @@ int main(int argc, char** argv) {
   metrics().describe("everserve_store_replicated_total", "Replication parts a target acknowledged", "counter");
   metrics().describe("everserve_store_replication_dropped_total", "Replication parts dropped by the bounded queue", "counter");
   metrics().describe("everserve_store_replication_link_failures_total", "Failed sends to a replication target", "counter");
+  metrics().describe("everserve_store_snapshots_total", "Snapshots of a rank's rows sent to a new replication target", "counter");
   metrics().describe("everserve_store_cache_fetches_total", "Compile-cache fetches from holder stores, by verdict", "counter");
   metrics().describe("everserve_store_cache_fetch_seconds", "Time to put a compile cache in place", "histogram");
   metrics().describe("everserve_store_replica_applied_total", "Replication parts applied from a source store", "counter");

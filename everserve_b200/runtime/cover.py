@@ -50,6 +50,10 @@ def _form_pg(store, prefix: str, rank: int, size: int, device: torch.device, tim
 class Cover:
     def __init__(self, store, me: str, engine: str, device: torch.device,
                  report: Callable[[object], None] | None = None, timeout_s: float = 30.0):
+        """`store`: the rendezvous store, or a function making a client of it. A store client
+        serves one blocking request at a time, so formations that run beside each other (and
+        beside the boundary's own) each need a client of their own: one formation waiting for a
+        peer's key must not hold up another's writes, or two processes wait on each other."""
         self.store, self.me, self.engine, self.device = store, me, engine, device
         self.report = report
         self.timeout_s = timeout_s
@@ -111,7 +115,8 @@ class Cover:
         t0 = time.monotonic()
         rank = keys.index(self.me)
         try:
-            pg = _form_pg(self.store, f"cover/g{generation}/{key}/", rank, len(keys), self.device, self.timeout_s)
+            store = self.store() if callable(self.store) else self.store
+            pg = _form_pg(store, f"cover/g{generation}/{key}/", rank, len(keys), self.device, self.timeout_s)
             # a first collective, so the group is usable (not only created) when a change adopts it
             t = torch.zeros(1, device=self.device)
             pg.allreduce([t]).wait()

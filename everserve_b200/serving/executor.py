@@ -70,6 +70,20 @@ class ChangeRecord:
     t_fault_wall: float = 0.0  # the same instant on the wall clock (the coordinator's stamps are wall time)
     coordinator: dict = field(default_factory=dict)
 
+    first_steps_ms: list = field(default_factory=list)  # device time of the steps after the resume
+
+    def spans(self) -> dict:
+        """The coordinator's part of the change, claim to commit, in ms: `decide` (loss reported to
+        change delivered: outcome chosen, logged), `acks` (delivered to every node answering),
+        `commit` (acknowledged to committed), and `claim_to_commit` in total.
+
+        Reference parity: spans.claim_to_commit of adapters/vllm/everserve_vllm/spans.py:18."""
+        c = self.coordinator
+        rep, dlv, ack, com = (c.get(k) or 0 for k in ("reported_at_us", "delivered_at_us", "acknowledged_at_us",
+                                                       "committed_at_us"))
+        d = lambda a, b: round((b - a) / 1e3, 3) if a and b else None  # noqa: E731
+        return {"decide": d(rep, dlv), "acks": d(dlv, ack), "commit": d(ack, com), "claim_to_commit": d(rep, com)}
+
     def as_dict(self) -> dict:
         """Milestones in ms from the fault when it is known (else from the head's detection)."""
         t0 = self.t_fault or self.t_detect
@@ -77,7 +91,7 @@ class ChangeRecord:
         return {"epoch": self.epoch, "lost": self.lost, "outcome": self.outcome, "from": "fault" if self.t_fault
                 else "detect", "detected_ms": ms(self.t_detect), "committed_ms": ms(self.t_committed),
                 "joined_ms": ms(self.t_joined), "ready_ms": ms(self.t_ready), "resumed_ms": ms(self.t_resumed),
-                "coordinator": self.coordinator}
+                "coordinator": self.coordinator, "spans": self.spans(), "first_steps_ms": self.first_steps_ms}
 
 
 class MultiprocExecutor:
@@ -202,7 +216,18 @@ class MultiprocExecutor:
         return int(self.links[rank].hello["pid"])
 
     # ---- steps -----------------------------------------------------------------------------------
+    FIRST_STEPS = 3  # steps timed after each resume (ChangeRecord.first_steps_ms)
+
     def execute(self, plan):
+        t_step = time.monotonic()
+        ids = self._execute(plan)
+        if self.changes and len(self.changes[-1].first_steps_ms) < self.FIRST_STEPS and self.changes[-1].t_resumed:
+            # the first steps after a change pay for whatever the change left cold (graphs,
+            # mappings, caches): how long they take is part of what a client of the streams sees
+            self.changes[-1].first_steps_ms.append(round((time.monotonic() - t_step) * 1e3, 3))
+        return ids
+
+    def _execute(self, plan):
         msg = {"op": "step", "epoch": self.epoch, "plan": plan}
         if self._finished:
             self._broadcast({"op": "finished", "ids": self._finished})
@@ -361,7 +386,7 @@ class MultiprocExecutor:
                            if mc.reported_at_us else None, "pause_ms": mc.pause_ms,
                            # the coordinator's wall clock: comparable with time.time() on one host
                            "reported_at_us": mc.reported_at_us, "committed_at_us": mc.committed_at_us,
-                           "delivered_at_us": mc.delivered_at_us,
+                           "delivered_at_us": mc.delivered_at_us, "acknowledged_at_us": mc.acknowledged_at_us,
                            "acks_at_us": {int(a.rank): int(a.received_at_us) for a in mc.acks}}
         lost = [r for r in mc.lost]
         ch = self.client.last_change

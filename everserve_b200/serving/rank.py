@@ -132,7 +132,8 @@ class RankProcess:
         if (a.daemon or daemon_link is not None) and a.pp > 1:
             from ..runtime.cover import Cover
 
-            self.cover = Cover(self.rdzv, self.key, self.engine, dev,
+            # each background formation gets its own store client (Cover's docstring)
+            self.cover = Cover(lambda: _store(a.rdzv), self.key, self.engine, dev,
                                report=lambda r: self.daemon.report(r) if self.daemon is not None else None,
                                timeout_s=a.group_timeout)
         if daemon_link is not None:
@@ -404,8 +405,12 @@ class RankProcess:
         self.carrier.send(reply)
 
     def _boundary(self, msg: dict) -> None:
+        import faulthandler
+
         epoch = int(msg["epoch"])
         t0 = time.monotonic()
+        # a boundary that takes longer than the group timeout leaves every thread's stack in the log
+        faulthandler.dump_traceback_later(self.a.group_timeout + 15, exit=False)
         try:
             if self.spare and self.ckv is not None and self.ckv.restored_step >= 0:
                 # rows the departing (or last) holder committed after the restore
@@ -436,6 +441,8 @@ class RankProcess:
                      "form_s": time.monotonic() - t0, "adopted": g.adopted}
         except Exception as e:  # noqa: BLE001
             reply = {"op": "error", "epoch": epoch, "rank": self.rank, "error": f"{type(e).__name__}: {e}"}
+        finally:
+            faulthandler.cancel_dump_traceback_later()
         self.carrier.send(reply)
 
     def close(self) -> None:
@@ -481,6 +488,12 @@ def parse(argv=None) -> argparse.Namespace:
 
 
 def main(argv=None) -> int:
+    import faulthandler
+    import signal as _signal
+
+    # `kill -USR1 <pid>` writes every thread's stack to this process's log (a hung rank is
+    # inspected without stopping it)
+    faulthandler.register(_signal.SIGUSR1, all_threads=True)
     a = parse(argv)
     if a.threads:
         torch.set_num_threads(a.threads)

@@ -10,6 +10,24 @@
 | ``EVERSERVE_STEP_SAMPLE`` | 16 | steps measured before the bound is set from the step period |
 | ``EVERSERVE_NODE`` | host name | this node's name in the control plane |
 
+Read where they are used (set by the node daemon for the processes it starts, or by the pod):
+
+| variable | meaning |
+|---|---|
+| ``EVERSERVE_SOCKET`` | the node daemon's process socket |
+| ``EVERSERVE_MIRROR_SOCKET`` | the node's KV store socket |
+| ``EVERSERVE_ENGINE`` / ``EVERSERVE_ENGINES`` | the engine (or a pool's engines, comma-separated) a launched spare stands for |
+| ``EVERSERVE_SPARE_RANK`` | the rank a launched spare stands for, or ``any`` |
+| ``EVERSERVE_POOL`` | the pool a launched spare belongs to |
+| ``EVERSERVE_DEVICE`` | the GPU a launched spare runs on |
+| ``EVERSERVE_COMPILE_CACHE`` | the node's compile-cache directory (workers publish their build there) |
+| ``EVERSERVE_FETCH_COMPILE_CACHE`` | ``1``: a spare takes its build from the compile cache even when one is installed |
+| ``EVERSERVE_EVENT_DIR`` | where rank processes write their event logs |
+| ``EVERSERVE_DISCOVERY_DIR`` | where daemons write their discovery records |
+| ``ES_EXTENSION_PATH`` | a kernel extension to load instead of the in-tree build |
+| ``ES_PDL`` | ``0``: launch the decode kernels without programmatic dependent launch |
+| ``ES_AR_TWO_SHOT`` / ``ES_NVLS`` | the fused all-reduce's variant: two-shot, or NVLS multicast (``0`` off) |
+
 Reference parity: adapters/vllm/everserve_vllm/settings.py:54-99 (same defaults: 3 steps, a 30 ms
 floor, 10 s to hung, a 2 ms poll).
 """

@@ -48,7 +48,15 @@ def test_spare_node_fetches_the_ranks_build_from_the_holder(tmp_path):
         pair = cc.publish(cp.cache_dirs["n0"], [art], key="es-test")
         w0 = DaemonConnection(cp.daemon_sockets["n0"], "e0", _P(0), node="n0", compile_cache=pair)
         assert _wait(lambda: cp.engine_view("e0")["status"]["workers"])
+        # a spare starting on n1 first asks for the engine's start-up record (the coordinator then
+        # sends n1 the engine's placement), then for its rank's build
+        from everserve_b200.contract.daemon import _Link
+        from everserve_b200.proto import signals as sp
+
+        ask = _Link(cp.daemon_sockets["n1"])
+        ask.send(sp.Signal(replay_ask=sp.ReplayAsk(engine="e0", rank=0)))
         ready = cc.want(cp.daemon_sockets["n1"], "e0", 0, timeout_s=30)
+        ask.close()
         assert (ready.key, ready.digest) == (pair.key, pair.digest)
         got = cc.locate(cp.cache_dirs["n1"], pair.key, pair.digest)
         assert open(got[os.path.basename(art)], "rb").read() == open(art, "rb").read()

@@ -105,3 +105,57 @@ def test_stale_epoch_loss_report_is_fenced(tmp_path):
                    for line in text.splitlines())
         for conn in (c0, cb):
             conn.close()
+
+
+def test_fleet_harness_commits_every_loss_at_scale():
+    """The control-plane scale harness against the real coordinator: 72 simulated nodes (64 TP8
+    engines, 8 spare nodes); every loss is replaced and committed within the coordinator's
+    stamps."""
+    import asyncio
+
+    from everserve_b200.perf.fleet import run_fleet
+    from everserve_b200.serving.cluster import binary
+
+    r = asyncio.run(run_fleet(binary("everserve-coord"), 72, 8, 8))
+    assert r["losses"] == 8 and r["engines"] == 64
+    assert 0 < r["report_to_commit_ms"]["max"] < 1000
+
+
+def test_daemon_fences_a_displaced_worker(tmp_path):
+    """A worker whose rank the coordinator gave to a spare while the worker still runs (hung, or
+    cut off) is stopped by its node's daemon after the commit."""
+    import subprocess
+    import sys
+
+    from everserve_b200.proto import signals as sp2
+
+    code = (
+        "import time, sys\n"
+        "from everserve_b200.contract.daemon import DaemonConnection\n"
+        "class P:\n"
+        "    def identity(self): return 1, 1\n"
+        "    def on_change(self, ch): return None\n"
+        "    def on_notice(self, *a): pass\n"
+        "    def on_abandoned(self, *a): pass\n"
+        "    def on_committed(self, c): pass\n"
+        "    def on_join(self, j): pass\n"
+        "    def on_displaced(self, *a): pass\n"
+        "c = DaemonConnection({cp_sock!r}, 'e0', P(), node='n0')\n"
+        "print('registered', flush=True)\n"
+        "time.sleep(120)\n"
+    )
+    with ControlPlane(str(tmp_path), engines=[{"name": "e0", "tensorParallel": 2}], extra_nodes=["n1"]) as cp:
+        w0 = DaemonConnection(cp.daemon_sockets["n0"], "e0", _P(0), node="n0")
+        hung = subprocess.Popen([sys.executable, "-c", code.replace("{cp_sock!r}", repr(cp.daemon_sockets["n0"]))],
+                                stdout=subprocess.PIPE, text=True,
+                                env=dict(os.environ, PYTHONPATH=os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+        assert hung.stdout.readline().strip() == "registered"
+        spare = DaemonConnection(cp.daemon_sockets["n1"], "e0", _P(1), node="n1", role=sp2.ROLE_SPARE)
+        assert _wait(lambda: len(cp.engine_view("e0")["status"]["workers"]) == 2 and
+                     cp.engine_view("e0")["status"]["spares"])
+        w0.report_lost([1], "rank 1 is hung", reason=sp2.REASON_FAULT)
+        assert _wait(lambda: cp.engine_view("e0")["status"]["epoch"] == 1, timeout=15)
+        assert hung.wait(timeout=15) != 0  # stopped by its daemon
+        assert "fencing e0 rank 1" in cp.log("node")
+        for c in (w0, spare):
+            c.close()

@@ -72,9 +72,23 @@ def _wait_covered(cp, engine, timeout_s=60.0):
 def test_sigkill_rank1_spare_takes_over_token_identical(tmp_path):
     base, changes0, _, _ = _run(tmp_path / "nofault", spares=())
     assert changes0 == []
-    out, changes, mism, view = _run(tmp_path / "fault", kill_at=KILL_AT)
+    events = tmp_path / "events"
+    os.environ["EVERSERVE_EVENT_DIR"] = str(events)  # the rank processes write their event logs
+    try:
+        out, changes, mism, view = _run(tmp_path / "fault", kill_at=KILL_AT)
+    finally:
+        del os.environ["EVERSERVE_EVENT_DIR"]
     assert len(changes) == 1
     rec = changes[0].as_dict()
+    sp = rec["spans"]
+    assert all(sp[k] is not None and sp[k] >= 0 for k in ("decide", "acks", "commit", "claim_to_commit"))
+    assert abs(sp["decide"] + sp["acks"] + sp["commit"] - sp["claim_to_commit"]) < 0.01
+    assert len(rec["first_steps_ms"]) == 3
+    import json
+
+    trace = [json.loads(line) for line in open(events / "rank0.trace.jsonl")]
+    kinds = [t["kind"] for t in trace]
+    assert "change" in kinds and "boundary" in kinds and all("wall" in t and "thread" in t for t in trace)
     assert rec["lost"] == [1] and rec["epoch"] == 1
     assert rec["from"] == "fault" and rec["resumed_ms"] is not None
     assert rec["coordinator"]["pre_formed_groups"] == [0, 1]  # the cover group was adopted
