@@ -1120,6 +1120,24 @@ struct Coordinator {
       v.emplace_back(node + ":" + std::to_string(m.stacks_sent.pid),
                      m.stacks_sent.answered ? m.stacks_sent.text : "(no answer: " + m.stacks_sent.error + ")");
       while (stacks.size() > 64) stacks.erase(stacks.begin());
+    } else if (m.has_release_leaked) {
+      // a process could not release a refused group within its bound: it holds what a stuck
+      // communicator holds, so it is retired by notice (it finishes its step; a spare takes the
+      // rank at the boundary) when a spare can take its rank, and counted either way
+      const auto& lk = m.release_leaked.leak;
+      metrics().inc("everserve_releases_leaked_total", {{"engine", lk.engine}});
+      event("engine " + lk.engine + ": rank " + std::to_string(lk.rank) + " on " + node + " leaked a release (" +
+            lk.release + ", " + std::to_string(lk.run_ms) + " ms)");
+      auto it = engines.find(lk.engine);
+      if (it != engines.end()) {
+        Engine& e = it->second;
+        auto w = e.workers.find(lk.rank);
+        const bool spare = std::any_of(e.spares.begin(), e.spares.end(), [&](const SpareSeat& s) {
+          return s.for_rank < 0 || s.for_rank == (int64_t)lk.rank;
+        });
+        if (w != e.workers.end() && w->second.node == node && spare)
+          report_loss(lk.engine, {lk.rank}, 0, "release leaked", true);
+      }
     } else if (m.has_cover_report) {
       on_cover_report(m.cover_report);
     } else if (m.has_replay_ask || m.has_replay_offer) {
@@ -1580,6 +1598,7 @@ int main(int argc, char** argv) {
   metrics().describe("everserve_fenced_total", "Reports dropped as older than the engine's epoch", "counter");
   metrics().describe("everserve_spares_refused_total", "Spares refused admission (identity, cordon, pool, device fit)", "counter");
   metrics().describe("everserve_api_refusals_total", "Operator API requests refused by the token gate, by code", "counter");
+  metrics().describe("everserve_releases_leaked_total", "Refused groups a process could not release within its bound", "counter");
   metrics().describe("everserve_enrollments_total", "Node certificate requests by verdict (issued, refused)", "counter");
   metrics().describe("everserve_pool_spares", "Spares of each pool by state (standing, warming)", "gauge");
   metrics().describe("everserve_pool_deficit", "Spares a pool wants beyond those standing or warming", "gauge");

@@ -44,6 +44,9 @@ class LocalExecutor:
     def fetch(self, ids) -> list[int]:
         return self.worker.runner.fetch(ids)
 
+    def logprobs(self, n: int) -> list | None:
+        return self.worker.runner.logprob_rows(n)
+
     def decode_loop(self, plan: StepPlan, k: int):
         return self.worker.runner.decode_loop(plan, k)
 
@@ -99,9 +102,12 @@ class Engine:
             self.connector.begin_step(plan, self.scheduler)
         ids = self.executor.execute(plan)
         tokens = self.executor.fetch(ids)
+        lp = None
+        if any(sr.logprobs is not None for sr in plan.reqs) and hasattr(self.executor, "logprobs"):
+            lp = self.executor.logprobs(len(plan.reqs))
         if self.connector is not None:
             self.connector.end_step(plan, self.scheduler)
-        out = self.scheduler.update(plan, tokens)
+        out = self.scheduler.update(plan, tokens, lp)
         tell = getattr(self.executor, "finished", None)
         for req_id, _, fin in out:
             if fin:

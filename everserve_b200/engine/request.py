@@ -39,6 +39,7 @@ class SamplingParams:
     top_k: int = 0
     top_p: float = 1.0
     seed: int | None = None
+    logprobs: int | None = None  # None: none; k: each output's log-probability and the k most likely
 
     def sampling_key(self, req_id: str) -> tuple[float, int, float, int] | None:
         """What a step needs to sample for this request (None: greedy)."""
@@ -62,6 +63,8 @@ class Request:
     blocks: list[int] = field(default_factory=list)
     arrival: int = 0
     replay_mismatches: int = 0
+    # per output when asked (SamplingParams.logprobs): (log-probability, [(token, log-probability)])
+    logprobs: list = field(default_factory=list)
 
     @property
     def tokens(self) -> list[int]:

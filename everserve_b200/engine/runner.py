@@ -60,6 +60,7 @@ class ModelRunner:
         self.graph_out: dict[tuple[int, bool], torch.Tensor] = {}
         self.h_out = torch.zeros(B, dtype=torch.int64, pin_memory=pin)
         self._pool = None
+        self.last_logprobs = None  # (chosen [B], top ids [B, k], top values [B, k]) of the last step
         if self.device.type == "cuda" and model.ops.kind == "kernel":
             model.ops.reserve_linear(max(max_batch, 1), model.linear_shapes())
             model.ops.reserve_attention(max_batch, model.hq, model.d, max_model_len)
@@ -74,6 +75,19 @@ class ModelRunner:
     @staticmethod
     def sampled(plan: StepPlan) -> bool:
         return any(r.sampling is not None for r in plan.reqs)
+
+    @staticmethod
+    def logprobs_k(plan: StepPlan) -> int | None:
+        ks = [r.logprobs for r in plan.reqs if r.logprobs is not None]
+        return max(ks) if ks else None
+
+    def logprob_rows(self, n: int) -> list | None:
+        """The last step's log-probability records of its first n rows, on the host:
+        [(log-probability, [(token, log-probability), ...]), ...]; None when it made none."""
+        if self.last_logprobs is None:
+            return None
+        chosen, idx, val = (t[:n].cpu() for t in self.last_logprobs)
+        return [(float(chosen[i]), list(zip(idx[i].tolist(), val[i].tolist()))) for i in range(len(chosen))]
 
     def _stage_sampling(self, plan: StepPlan, b: int) -> None:
         hf, hi = self.h_sf.numpy(), self.h_si.numpy()
@@ -150,12 +164,29 @@ class ModelRunner:
         return self.model.forward(inp, self.caches, hidden, residual)
 
     def execute(self, plan: StepPlan, hidden=None, residual=None):
-        """Run one step. Last stage: sampled ids (device int64 [n]); other stages: (hidden, residual)."""
+        """Run one step. Last stage: sampled ids (device int64 [n]); other stages: (hidden, residual).
+
+        A step asked for log-probabilities runs eagerly and leaves them in ``last_logprobs``."""
+        k = self.logprobs_k(plan)
+        self.last_logprobs = None
+        self.model.step_logprobs = None
         if plan.is_prefill:
-            return self.forward(self.prefill_input(plan), hidden, residual)
+            inp = self.prefill_input(plan)
+            inp.logprobs_k = k
+            out = self.forward(inp, hidden, residual)
+            self.last_logprobs = self.model.step_logprobs if k is not None else None
+            return out
         n = len(plan.reqs)
         b = self.stage_decode(plan)
         key = (b, self.sampled(plan))
+        if k is not None:
+            inp = self._decode_input(*key)
+            inp.logprobs_k = k
+            out = self.forward(inp, hidden, residual)
+            self.last_logprobs = self.model.step_logprobs
+            if isinstance(out, tuple):
+                return out[0][:n], out[1][:n]
+            return out[:n]
         if self.use_graphs and self.model.last and self.model.first:
             g = self.graphs.get(key)
             if g is None:

@@ -29,6 +29,7 @@ class ScheduledReq:
     sample: bool  # the last fed position is the request's last token: its sample is a new output
     expect: int | None = None  # replayed position: the output already recorded there
     sampling: tuple | None = None  # (temperature, top_k, top_p, seed); None: greedy
+    logprobs: int | None = None  # how many alternatives' log-probabilities to report (None: none)
 
 
 @dataclass
@@ -107,7 +108,8 @@ class Scheduler:
             self.running.append(req)
             plan.reqs.append(ScheduledReq(req.req_id, req.tokens[req.num_computed:], req.num_computed,
                                           list(req.blocks), sample=True,
-                                          sampling=req.params.sampling_key(req.req_id)))
+                                          sampling=req.params.sampling_key(req.req_id),
+                                          logprobs=req.params.logprobs))
             budget -= n
         return plan if plan.reqs else None
 
@@ -135,7 +137,8 @@ class Scheduler:
             last = p == req.num_tokens - 1
             plan.reqs.append(ScheduledReq(req.req_id, [req.tokens[p]], p, list(req.blocks), sample=last,
                                           expect=None if last else req.tokens[p + 1],
-                                          sampling=req.params.sampling_key(req.req_id)))
+                                          sampling=req.params.sampling_key(req.req_id),
+                                          logprobs=req.params.logprobs if last else None))
         return plan
 
     def _preempt(self, req: Request) -> None:
@@ -147,16 +150,20 @@ class Scheduler:
         self.preemptions.append(req.req_id)
 
     # ---- results ---------------------------------------------------------------------------------
-    def update(self, plan: StepPlan, sampled: list[int]) -> list[tuple[str, int | None, bool]]:
-        """Apply one step's sampled ids; returns (req_id, new token or None, finished) per request."""
+    def update(self, plan: StepPlan, sampled: list[int], logprobs: list | None = None) -> list[tuple[str, int | None, bool]]:
+        """Apply one step's sampled ids (and each row's log-probability record when the step made
+        them); returns (req_id, new token or None, finished) per request."""
         out = []
-        for sr, tok in zip(plan.reqs, sampled):
+        for i, (sr, tok) in enumerate(zip(plan.reqs, sampled)):
             req = self.requests[sr.req_id]
             req.num_computed = sr.start_pos + len(sr.token_ids)
             new = None
             if sr.sample:
                 req.outputs.append(int(tok))
                 new = int(tok)
+                if sr.logprobs is not None and logprobs is not None:
+                    lp, top = logprobs[i]
+                    req.logprobs.append((lp, top[: sr.logprobs]))
             elif sr.expect is not None and int(tok) != sr.expect:
                 req.replay_mismatches += 1
             fin = sr.sample and req.done_generating()

@@ -39,6 +39,7 @@ class StepInput:
     is_decode: bool
     max_model_len: int = 0
     sampling: object | None = None  # engine.sampling.SamplingBatch of the rows; None: greedy
+    logprobs_k: int | None = None  # the step also reports log-probabilities (k alternatives)
 
 
 def _seed_of(seed: int, *parts) -> int:
@@ -85,6 +86,7 @@ class DecoderLM:
         self.device = torch.device(device)
         self.dtype = dtype
         self.seed = seed
+        self.step_logprobs = None  # the last forward's log-probabilities, when it was asked for them
         self.tp = tp or TPGroup()
         self.ops = ops_for(self.device)
         self.l0, self.l1 = layer_range or (0, cfg.layers)
@@ -251,9 +253,19 @@ class DecoderLM:
         h_last = h.index_select(0, inp.logits_idx) if h.shape[0] != inp.logits_idx.shape[0] else h
         head = W["embed"] if c.tie_embeddings else W["lm_head"]
         logits = ops.linear(h_last, head)
-        if inp.sampling is not None:
-            return self._sample(logits, inp)
-        return self._greedy(logits)
+        ids = self._sample(logits, inp) if inp.sampling is not None else self._greedy(logits)
+        if inp.logprobs_k is not None:
+            self.step_logprobs = self._logprobs(logits, ids, inp.logprobs_k)
+        return ids
+
+    def _logprobs(self, logits: torch.Tensor, ids: torch.Tensor, k: int):
+        """Each row's chosen token's log-probability and its k most likely tokens with theirs
+        (the model's distribution, before temperature and filters): ([B], [B, k], [B, k])."""
+        full = logits if self.tp.size == 1 else self.tp.all_gather_rows(logits.contiguous())
+        lsm = torch.log_softmax(full[:, : self.cfg.vocab].float(), dim=-1)
+        chosen = lsm.gather(1, ids.view(-1, 1).long())[:, 0]
+        top = torch.topk(lsm, max(0, min(k, lsm.shape[1])), dim=-1)
+        return chosen, top.indices, top.values
 
     def _sample(self, logits: torch.Tensor, inp: StepInput) -> torch.Tensor:
         """Seeded sampling of every row (engine.sampling); each tensor-parallel rank gathers the

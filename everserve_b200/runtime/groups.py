@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import datetime
 import threading
+import time
 
 import torch
 import torch.distributed as dist
@@ -80,13 +81,40 @@ class EpochGroups:
 
 
 class SwappableGroups:
-    """The live epoch's groups; refused while a change is staged, replaced at the boundary."""
+    """The live epoch's groups; refused while a change is staged, replaced at the boundary.
 
-    def __init__(self, store, rank: int, layout: ParallelLayout, device: torch.device, timeout_s: float = 30.0):
+    A refused epoch's groups are released beside the change, on a thread, within
+    `release_bound_s`: an abort that does not return by then (a communicator stuck on a dead peer)
+    is a leak, reported through `on_leak(release, seconds, leaked_total)`; the process keeps
+    serving, and the control plane retires it by notice at a later boundary."""
+
+    def __init__(self, store, rank: int, layout: ParallelLayout, device: torch.device, timeout_s: float = 30.0,
+                 release_bound_s: float = 10.0, on_leak=None):
         self.store, self.rank, self.layout, self.device, self.timeout_s = store, rank, layout, device, timeout_s
         self.current: EpochGroups | None = None
         self.refused = threading.Event()
         self._lock = threading.Lock()
+        self.release_bound_s = release_bound_s
+        self.on_leak = on_leak
+        self.leaked = 0
+
+    def _release(self, g: "EpochGroups", what: str) -> None:
+        """Abort `g` beside the caller, bounded; a release past the bound is reported as a leak."""
+        done = threading.Event()
+
+        def run():
+            g.abort()
+            done.set()
+
+        def watch():
+            t0 = time.monotonic()
+            if not done.wait(self.release_bound_s):
+                self.leaked += 1
+                if self.on_leak is not None:
+                    self.on_leak(what, time.monotonic() - t0, self.leaked)
+
+        threading.Thread(target=run, name=f"release-e{g.epoch}", daemon=True).start()
+        threading.Thread(target=watch, name=f"release-watch-e{g.epoch}", daemon=True).start()
 
     def form(self, epoch: int, rank: int | None = None, pipe=None) -> EpochGroups:
         """Build the epoch's groups (a rendezvous with every member of the epoch), adopting `pipe`
@@ -98,7 +126,7 @@ class SwappableGroups:
             old, self.current = self.current, g
             self.refused.clear()
         if old is not None:
-            old.abort()
+            self._release(old, f"epoch {old.epoch} groups")
         return g
 
     def refuse(self) -> None:
@@ -107,7 +135,7 @@ class SwappableGroups:
         with self._lock:
             g = self.current
         if g is not None and self.device.type == "cuda":
-            g.abort()
+            self._release(g, f"epoch {g.epoch} groups (refused)")
 
     def live(self) -> EpochGroups:
         if self.refused.is_set() or self.current is None:

@@ -3,7 +3,8 @@
     python -m everserve_b200.serving.api --model llama-3-8b --port 8000 [--checkpoint DIR] [--tp 8 ...]
 
 ``POST /v1/completions`` with ``{"prompt": [token ids] | "text", "max_tokens": n, "stream": bool,
-"temperature": t, "top_k": k, "top_p": p, "seed": s}`` (temperature 0, the default, is greedy)
+"temperature": t, "top_k": k, "top_p": p, "seed": s, "logprobs": n}`` (temperature 0, the default, is greedy;
+``logprobs`` n returns each token's log-probability and the n most likely, at most 20)
 returns ``choices[0].token_ids`` (and ``text`` when a tokenizer is configured); with
 ``"stream": true`` it sends one server-sent event per new token. ``GET /v1/models``, ``GET /live``
 and ``GET /ready`` report the model and health (``/ready`` is 503 while a membership change is
@@ -134,12 +135,25 @@ def build_app(loop: EngineLoop, model_name: str, vocab: int, tokenizer=None):
         if not prompt:
             raise HTTPException(400, "empty prompt")
         seed = body.get("seed")
+        nlp = body.get("logprobs")
         params = SamplingParams(max_tokens=int(body.get("max_tokens", 16)),
                                 temperature=float(body.get("temperature", 0.0) or 0.0),
                                 top_k=int(body.get("top_k", 0) or 0), top_p=float(body.get("top_p", 1.0) or 1.0),
-                                seed=int(seed) if seed is not None else None)
+                                seed=int(seed) if seed is not None else None,
+                                logprobs=min(20, int(nlp)) if nlp is not None else None)
         p = loop.submit(prompt, params)
         created = int(time.time())
+
+        def logprobs_of(ids: list[int], first: int = 0):
+            """The completions API's logprobs object for outputs first .. first + len(ids)."""
+            if params.logprobs is None:
+                return None
+            recs = loop.engine.request(p.req_id).logprobs[first : first + len(ids)]
+            name = lambda t: decode([t]) if decode([t]) is not None else str(t)  # noqa: E731 - ids without a tokenizer
+            names = [name(t) for t in ids]
+            offsets = [sum(len(x) for x in names[:i]) for i in range(len(names))]
+            return {"tokens": names, "token_logprobs": [r[0] for r in recs],
+                    "top_logprobs": [{name(t): v for t, v in r[1]} for r in recs], "text_offset": offsets}
 
         async def tokens():
             while True:
@@ -152,16 +166,20 @@ def build_app(loop: EngineLoop, model_name: str, vocab: int, tokenizer=None):
 
         if body.get("stream"):
             async def events():
+                i = 0
                 async for t in tokens():
                     chunk = {"id": p.req_id, "object": "text_completion", "created": created, "model": model_name,
-                             "choices": [{"index": 0, "token_ids": [t], "text": decode([t]), "finish_reason": None}]}
+                             "choices": [{"index": 0, "token_ids": [t], "text": decode([t]), "finish_reason": None,
+                                          "logprobs": logprobs_of([t], i)}]}
+                    i += 1
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
 
             return StreamingResponse(events(), media_type="text/event-stream")
         ids = [t async for t in tokens()]
         return {"id": p.req_id, "object": "text_completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "token_ids": ids, "text": decode(ids), "finish_reason": "length"}],
+                "choices": [{"index": 0, "token_ids": ids, "text": decode(ids), "finish_reason": "length",
+                             "logprobs": logprobs_of(ids)}],
                 "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(ids),
                           "total_tokens": len(prompt) + len(ids)}}
 

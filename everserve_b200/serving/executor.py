@@ -275,6 +275,7 @@ class MultiprocExecutor:
                 errors[r] = reply["error"]
             elif "ids" in reply:
                 ids = reply["ids"]
+                self._logprobs = reply.get("logprobs")
         if lost or errors:
             raise RankLost(lost or set(errors), "; ".join(f"rank {r}: {e}" for r, e in errors.items()) or "link ended")
         return ids
@@ -288,6 +289,10 @@ class MultiprocExecutor:
 
     def fetch(self, ids):
         return ids
+
+    def logprobs(self, n: int):
+        """The last step's log-probability records (from the last stage's first column)."""
+        return getattr(self, "_logprobs", None)
 
     def finished(self, req_id: str) -> None:
         self._finished.append(req_id)

@@ -94,7 +94,10 @@ class RankProcess:
         self.cfg = config_of(a)
         self.runtime = Runtime(self.rank)
         self.rdzv = _store(a.rdzv)
-        self.groups = SwappableGroups(self.rdzv, self.rank, self.layout, dev, timeout_s=a.group_timeout)
+        from ..settings import load as load_settings
+
+        self.groups = SwappableGroups(self.rdzv, self.rank, self.layout, dev, timeout_s=a.group_timeout,
+                                      release_bound_s=load_settings().release_bound_ms / 1e3, on_leak=self._leaked)
         mc = self.cfg.model
         self.exchange = Exchange(self.groups, mc.hidden, self.cfg.dtype) if a.pp > 1 else None
         self.row = a.row if a.row is not None else self.rank
@@ -240,6 +243,17 @@ class RankProcess:
         self.watch = SlotWatch(self.region, self.row, lost, rank_of_row=lambda row: by_row.get(row, row),
                                members=members, poll_s=self.settings.poll_ms / 1e3,
                                hang_s=self.settings.hang_s).start()
+
+    def _leaked(self, release: str, seconds: float, total: int) -> None:
+        """A refused group's release outlived its bound: tell the control plane, which retires this
+        process by notice (a spare takes the rank at a later boundary)."""
+        self.runtime.trace("release leaked", release=release, seconds=seconds, total=total)
+        daemon = getattr(self, "daemon", None)
+        if daemon is not None:
+            try:
+                daemon.report_leak(release, seconds, total)
+            except OSError:
+                pass
 
     # ---- participant (daemon reader thread) ------------------------------------------------------
     def identity(self) -> tuple[int, int]:
@@ -400,6 +414,9 @@ class RankProcess:
             reply = {"op": "done", "step": plan.step, "rank": self.rank}
             if out is not None and self.layout.column(self.rank) == 0:
                 reply["ids"] = out.tolist() if isinstance(out, torch.Tensor) else list(out)
+                rows = self.worker.runner.logprob_rows(len(plan.reqs))
+                if rows is not None:
+                    reply["logprobs"] = rows
         except Exception as e:  # noqa: BLE001 - the head decides what a failed step means
             reply = {"op": "error", "step": plan.step, "rank": self.rank, "error": f"{type(e).__name__}: {e}"}
         self.carrier.send(reply)

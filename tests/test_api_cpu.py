@@ -33,3 +33,24 @@ def test_completions_match_generate():
         assert len(r["choices"][0]["token_ids"]) == 2
     finally:
         loop.close()
+
+
+def test_completions_sampling_and_logprobs():
+    loop = EngineLoop(Engine(_cfg()))
+    try:
+        c = TestClient(build_app(loop, "tiny-llama", 512))
+        body = {"prompt": [5, 6, 7], "max_tokens": 6, "temperature": 0.8, "top_p": 0.9, "seed": 7, "logprobs": 2}
+        a = c.post("/v1/completions", json=body).json()["choices"][0]
+        b = c.post("/v1/completions", json=body).json()["choices"][0]
+        assert a["token_ids"] == b["token_ids"]  # the same seed draws the same tokens
+        lp = a["logprobs"]
+        assert len(lp["token_logprobs"]) == 6 and all(v <= 0 for v in lp["token_logprobs"])
+        assert all(len(t) <= 2 for t in lp["top_logprobs"])
+        with c.stream("POST", "/v1/completions", json=dict(body, stream=True)) as s:
+            chunks = [json.loads(ln[6:]) for ln in s.iter_lines() if ln.startswith("data: {")]
+        assert [ch["choices"][0]["token_ids"][0] for ch in chunks] == a["token_ids"]
+        assert [ch["choices"][0]["logprobs"]["token_logprobs"][0] for ch in chunks] == lp["token_logprobs"]
+        g = c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 6}).json()["choices"][0]
+        assert g["logprobs"] is None
+    finally:
+        loop.close()

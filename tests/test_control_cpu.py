@@ -159,3 +159,28 @@ def test_daemon_fences_a_displaced_worker(tmp_path):
         assert "fencing e0 rank 1" in cp.log("node")
         for c in (w0, spare):
             c.close()
+
+
+def test_leaked_release_retires_the_rank_by_notice(tmp_path):
+    """A worker that reports a leaked release is retired by notice when a spare can take its rank:
+    the change names it as departing, so it finishes its step before the spare takes over."""
+    from everserve_b200.proto import signals as sp2
+
+    class Rec(_P):
+        def on_change(self, ch):
+            self.changes.append(ch)
+            return None
+
+    with ControlPlane(str(tmp_path), engines=[{"name": "e0", "tensorParallel": 2}], extra_nodes=["n1"]) as cp:
+        r0, r1 = Rec(0), Rec(1)
+        w0 = DaemonConnection(cp.daemon_sockets["n0"], "e0", r0, node="n0")
+        w1 = DaemonConnection(cp.daemon_sockets["n0"], "e0", r1, node="n0")
+        spare = DaemonConnection(cp.daemon_sockets["n1"], "e0", Rec(1), node="n1", role=sp2.ROLE_SPARE)
+        assert _wait(lambda: len(cp.engine_view("e0")["status"]["workers"]) == 2 and
+                     cp.engine_view("e0")["status"]["spares"])
+        w1.report_leak("epoch 0 groups", 12.5, 1)
+        assert _wait(lambda: cp.engine_view("e0")["status"]["epoch"] == 1, timeout=15)
+        assert r1.changes and list(r1.changes[-1].departing) == [1]
+        assert any("leaked a release" in e["text"] for e in cp.get("/v1/engines/e0/events")["events"])
+        for c in (w0, w1, spare):
+            c.close()

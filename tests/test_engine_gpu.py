@@ -64,3 +64,17 @@ def test_sampled_graphs_match_eager_and_replay(cuda):
     greedy = Engine(_cfg(TINY_QWEN, graphs=True)).generate(prompts, max_tokens=24)
     assert graphs == again and graphs == eager
     assert graphs != greedy
+
+
+def test_logprobs_on_the_device(cuda):
+    """A request asking for log-probabilities runs its steps eagerly; the greedy token is the most
+    likely one and its log-probability matches the top entry."""
+    eng = Engine(_cfg(TINY_QWEN, graphs=True))
+    rid = eng.add_request([3, 1, 4, 1, 5, 9], SamplingParams(max_tokens=6, logprobs=4))
+    other = eng.add_request([2, 7, 1, 8], SamplingParams(max_tokens=6))
+    while eng.has_work():
+        eng.step()
+    r = eng.request(rid)
+    assert len(r.logprobs) == 6 and eng.request(other).logprobs == []
+    for tok, (lp, top) in zip(r.outputs, r.logprobs):
+        assert top[0][0] == tok and abs(lp - top[0][1]) < 1e-5 and len(top) == 4

@@ -273,3 +273,33 @@ def test_sampled_streams_replay_exactly_after_sigkill(tmp_path):
     out, changes, mism, _ = _run(tmp_path / "fault", kill_at=KILL_AT, **kw)
     assert len(changes) == 1 and mism == 0
     assert out == base
+
+
+def test_logprobs_through_the_multiprocess_engine(tmp_path):
+    """Log-probabilities come back from the last stage's ranks and match a single process's."""
+    from everserve_b200.engine.request import SamplingParams
+
+    cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
+                       max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
+    prompts = _prompts()[:2]
+    sp = SamplingParams(max_tokens=4, logprobs=2)
+    one = Engine(EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
+                              max_model_len=PROMPT + TOKENS + 16, use_cuda_graphs=False))
+    ids1 = [one.add_request(p, sp) for p in prompts]
+    while one.has_work():
+        one.step()
+    with ControlPlane(str(tmp_path / "cp"), engines=[{"name": "e0", "pipelineParallel": 2}]) as cp:
+        ex = MultiprocExecutor(cfg, engine="e0", daemon=cp.daemon_socket, store=cp.store_socket, spares=(),
+                               node="n0", log_dir=str(tmp_path / "logs"), threads=2)
+        try:
+            eng = Engine(cfg, executor=ex)
+            ids = [eng.add_request(p, sp) for p in prompts]
+            while eng.has_work():
+                eng.step()
+            for a, b in zip(ids, ids1):
+                ra, rb = eng.request(a), one.request(b)
+                assert ra.outputs == rb.outputs and len(ra.logprobs) == 4
+                for (la, ta), (lb, tb) in zip(ra.logprobs, rb.logprobs):
+                    assert abs(la - lb) < 1e-4 and [t for t, _ in ta] == [t for t, _ in tb]
+        finally:
+            ex.shutdown()

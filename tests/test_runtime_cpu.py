@@ -136,3 +136,33 @@ def test_discovery_file_backend(tmp_path, monkeypatch):
     assert discovery.local_daemon("n0", tmp_path).pid == 42
     monkeypatch.setenv(discovery.DAEMON_SOCKET_ENV, "unix:/x.sock")
     assert discovery.local_daemon("n0").address == "unix:/x.sock"
+
+
+def test_a_release_past_its_bound_is_reported_as_a_leak():
+    import threading
+    import time
+
+    import torch
+
+    from everserve_b200.runtime.groups import SwappableGroups
+    from everserve_b200.runtime.layout import ParallelLayout
+
+    class Stuck:
+        epoch = 3
+
+        def __init__(self, seconds):
+            self.seconds = seconds
+
+        def abort(self):
+            time.sleep(self.seconds)
+
+    leaks = []
+    got = threading.Event()
+    g = SwappableGroups(None, 0, ParallelLayout(1, 1), torch.device("cpu"), release_bound_s=0.2,
+                        on_leak=lambda what, s, n: (leaks.append((what, s, n)), got.set()))
+    g._release(Stuck(0.0), "fast")
+    g._release(Stuck(2.0), "epoch 3 groups")
+    assert got.wait(5)
+    assert leaks[0][0] == "epoch 3 groups" and leaks[0][1] >= 0.2 and leaks[0][2] == 1
+    time.sleep(0.3)
+    assert len(leaks) == 1  # the fast release was no leak

@@ -78,3 +78,28 @@ def test_engine_sampling_is_reproducible_and_replays_exactly():
         eng2.step()
     assert [eng2.request(i).outputs for i in ids] == a
     assert all(eng2.request(i).replay_mismatches == 0 for i in ids)
+
+
+def test_logprobs_match_the_models_distribution():
+    cfg = EngineConfig(model="tiny-qwen", device="cpu", dtype=torch.float32, num_blocks=64, max_batch=4,
+                       max_model_len=128, use_cuda_graphs=False)
+    eng = Engine(cfg)
+    prompt = [3, 1, 4, 1, 5]
+    a = eng.add_request(prompt, SamplingParams(max_tokens=5, logprobs=3))
+    b = eng.add_request([9, 9, 9], SamplingParams(max_tokens=5))  # no logprobs asked: none recorded
+    while eng.has_work():
+        eng.step()
+    ra, rb = eng.request(a), eng.request(b)
+    assert len(ra.logprobs) == 5 and rb.logprobs == []
+    for tok, (lp, top) in zip(ra.outputs, ra.logprobs):
+        assert len(top) == 3 and top[0][0] == tok  # greedy: the chosen token is the most likely
+        assert abs(lp - top[0][1]) < 1e-6 and top[0][1] >= top[1][1] >= top[2][1]
+    # the first output's log-probability against the model's own logits
+    worker = Engine(cfg).executor.worker
+    from everserve_b200.engine.scheduler import ScheduledReq, StepPlan
+
+    plan = StepPlan(0, True, [ScheduledReq("x", prompt, 0, list(range(1)), True)])
+    inp = worker.runner.prefill_input(plan)
+    lg = worker.model.logits(inp, worker.runner.caches)
+    want = torch.log_softmax(lg.float(), -1)[0, ra.outputs[0]]
+    assert abs(float(want) - ra.logprobs[0][0]) < 1e-4
