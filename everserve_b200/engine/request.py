@@ -40,6 +40,7 @@ class SamplingParams:
     top_p: float = 1.0
     seed: int | None = None
     logprobs: int | None = None  # None: none; k: each output's log-probability and the k most likely
+    stop_ids: tuple = ()  # token ids that end the request (the token is kept as its last output)
 
     def sampling_key(self, req_id: str) -> tuple[float, int, float, int] | None:
         """What a step needs to sample for this request (None: greedy)."""
@@ -82,11 +83,19 @@ class Request:
         return self.num_computed == 0 and len(self.prompt) > 1
 
     def done_generating(self) -> bool:
+        return self.finish_reason() is not None
+
+    def finish_reason(self) -> str | None:
+        """"stop" (an end-of-sequence or stop token), "length" (max_tokens), or None (not done)."""
+        if self.outputs:
+            last = self.outputs[-1]
+            if last in self.params.stop_ids:
+                return "stop"
+            if not self.params.ignore_eos and self.params.eos_id is not None and last == self.params.eos_id:
+                return "stop"
         if len(self.outputs) >= self.params.max_tokens:
-            return True
-        if not self.params.ignore_eos and self.params.eos_id is not None and self.outputs:
-            return self.outputs[-1] == self.params.eos_id
-        return False
+            return "length"
+        return None
 
     def resume_point(self) -> int:
         """Where computation restarts after a loss: the committed count, at most the last token."""

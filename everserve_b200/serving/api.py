@@ -4,7 +4,8 @@
 
 ``POST /v1/completions`` with ``{"prompt": [token ids] | "text", "max_tokens": n, "stream": bool,
 "temperature": t, "top_k": k, "top_p": p, "seed": s, "logprobs": n}`` (temperature 0, the default, is greedy;
-``logprobs`` n returns each token's log-probability and the n most likely, at most 20)
+``logprobs`` n returns each token's log-probability and the n most likely, at most 20;
+``stop_token_ids`` end a completion, as the tokenizer's end-of-sequence id does unless ``ignore_eos``)
 returns ``choices[0].token_ids`` (and ``text`` when a tokenizer is configured); with
 ``"stream": true`` it sends one server-sent event per new token. ``GET /v1/models``, ``GET /live``
 and ``GET /ready`` report the model and health (``/ready`` is 503 while a membership change is
@@ -112,6 +113,8 @@ def build_app(loop: EngineLoop, model_name: str, vocab: int, tokenizer=None):
     def decode(ids: list[int]) -> str | None:
         return tokenizer.decode(ids) if tokenizer is not None else None
 
+    eos_id = getattr(tokenizer, "eos_token_id", None) if tokenizer is not None else None
+
     @app.get("/live")
     def live():
         return {"live": True}
@@ -140,7 +143,9 @@ def build_app(loop: EngineLoop, model_name: str, vocab: int, tokenizer=None):
                                 temperature=float(body.get("temperature", 0.0) or 0.0),
                                 top_k=int(body.get("top_k", 0) or 0), top_p=float(body.get("top_p", 1.0) or 1.0),
                                 seed=int(seed) if seed is not None else None,
-                                logprobs=min(20, int(nlp)) if nlp is not None else None)
+                                logprobs=min(20, int(nlp)) if nlp is not None else None,
+                                stop_ids=tuple(int(t) for t in body.get("stop_token_ids") or ()),
+                                eos_id=eos_id, ignore_eos=bool(body.get("ignore_eos", eos_id is None)))
         p = loop.submit(prompt, params)
         created = int(time.time())
 
@@ -173,12 +178,17 @@ def build_app(loop: EngineLoop, model_name: str, vocab: int, tokenizer=None):
                                           "logprobs": logprobs_of([t], i)}]}
                     i += 1
                     yield f"data: {json.dumps(chunk)}\n\n"
+                final = {"id": p.req_id, "object": "text_completion", "created": created, "model": model_name,
+                         "choices": [{"index": 0, "token_ids": [], "text": "",
+                                      "finish_reason": loop.engine.request(p.req_id).finish_reason() or "length"}]}
+                yield f"data: {json.dumps(final)}\n\n"
                 yield "data: [DONE]\n\n"
 
             return StreamingResponse(events(), media_type="text/event-stream")
         ids = [t async for t in tokens()]
+        finish = loop.engine.request(p.req_id).finish_reason() or "length"
         return {"id": p.req_id, "object": "text_completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "token_ids": ids, "text": decode(ids), "finish_reason": "length",
+                "choices": [{"index": 0, "token_ids": ids, "text": decode(ids), "finish_reason": finish,
                              "logprobs": logprobs_of(ids)}],
                 "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(ids),
                           "total_tokens": len(prompt) + len(ids)}}
