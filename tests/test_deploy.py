@@ -80,3 +80,11 @@ def test_helm_chart_node_daemonset_rbac_and_network_policies():
     assert "resources: [tokenreviews], verbs: [create]" in coord and "--enroll-addr" in coord
     values = yaml.safe_load(open(os.path.join(chart, "values.yaml")))
     assert values["coordinator"]["enrollPort"] == 7682 and values["store"]["replicaPort"] == 7683
+
+
+def test_every_alert_has_a_runbook_entry():
+    rules = yaml.safe_load(open(os.path.join(DEPLOY, "grafana", "alerts.yml")))
+    runbook = open(os.path.join(ROOT, "docs", "RUNBOOK.md")).read()
+    missing = [r["alert"] for g in rules["groups"] for r in g["rules"] if f"`{r['alert']}`" not in runbook
+               and r["alert"].replace("Everserve", "`...") not in runbook]
+    assert not missing, missing
