@@ -140,7 +140,8 @@ class Engine:
             if i > 0:
                 for sr in plan.reqs:
                     sr.start_pos += 1
-                    sr.token_ids = [sch.requests[sr.req_id].tokens[-1]]
+                    r = sch.requests[sr.req_id]
+                    sr.token_ids = [r.token_at(r.num_tokens - 1)]
             sch.update(plan, toks[i])
         sch.step_id += k - 1
         return [[toks[i][j] for i in range(k)] for j in range(n)]

@@ -62,6 +62,7 @@ class Request:
     num_computed: int = 0
     committed: int = 0  # tokens whose K/V the committed-KV store holds
     blocks: list[int] = field(default_factory=list)
+    blocks_version: int = 0  # raised whenever the blocks are given back (a new table follows)
     arrival: int = 0
     replay_mismatches: int = 0
     # per output when asked (SamplingParams.logprobs): (log-probability, [(token, log-probability)])
@@ -70,6 +71,11 @@ class Request:
     @property
     def tokens(self) -> list[int]:
         return self.prompt + self.outputs
+
+    def token_at(self, i: int) -> int:
+        """tokens[i] without building the list (the decode loop's per-step access)."""
+        n = len(self.prompt)
+        return self.prompt[i] if i < n else self.outputs[i - n]
 
     @property
     def num_tokens(self) -> int:

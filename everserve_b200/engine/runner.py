@@ -46,6 +46,7 @@ class ModelRunner:
         self.h_bt = torch.zeros(B, self.max_blocks, dtype=torch.int32, pin_memory=pin)
         self.h_i64_np = self.h_i64.numpy()
         self.h_bt_np = self.h_bt.numpy()
+        self._bt_rows = [(None, 0)] * B  # per staging row: ((request, table version), entries written)
         self.h2d_bytes = 0
         self.d_i64 = torch.zeros(4, B, dtype=torch.int64, device=self.device)
         self.d_bt = torch.zeros(B, self.max_blocks, dtype=torch.int32, device=self.device)
@@ -108,18 +109,32 @@ class ModelRunner:
         n = len(plan.reqs)
         b = self._bucket(n)
         h = self.h_i64_np
-        h[:, :b] = 0
-        h[2, :b] = -1
         bs = self.block_size
         hbt = self.h_bt_np
+        ids, pos, slots = [], [], []
+        rows = self._bt_rows
         for i, r in enumerate(plan.reqs):
             p = r.start_pos
             bt = r.block_table
-            h[0, i] = r.token_ids[0]
-            h[1, i] = p
-            h[2, i] = bt[p // bs] * bs + p % bs
-            h[3, i] = p + 1
-            hbt[i, : len(bt)] = bt
+            ids.append(r.token_ids[0])
+            pos.append(p)
+            slots.append(bt[p // bs] * bs + p % bs)
+            # a row's block table is written only where it changed (a request keeps its row while
+            # it runs; its table grows by appending)
+            key = (r.req_id, r.bt_version)
+            done = rows[i][1] if rows[i][0] == key else 0
+            if len(bt) > done:
+                hbt[i, done : len(bt)] = bt[done:]
+            rows[i] = (key, len(bt))
+        for i in range(n, b):
+            rows[i] = (None, 0)
+        h[:, n:b] = 0
+        h[2, n:b] = -1
+        if n:
+            h[0, :n] = ids
+            h[1, :n] = pos
+            h[2, :n] = slots
+            h[3, :n] = h[1, :n] + 1
         self.d_i64[:, :b].copy_(self.h_i64[:, :b], non_blocking=True)
         self.d_bt[:b].copy_(self.h_bt[:b], non_blocking=True)
         self.h2d_bytes = 4 * b * 8 + b * self.max_blocks * 4

@@ -29,6 +29,7 @@ class ScheduledReq:
     sample: bool  # the last fed position is the request's last token: its sample is a new output
     expect: int | None = None  # replayed position: the output already recorded there
     sampling: tuple | None = None  # (temperature, top_k, top_p, seed); None: greedy
+    bt_version: int = 0  # the request's blocks_version: a staged table is valid while it holds
     logprobs: int | None = None  # how many alternatives' log-probabilities to report (None: none)
 
 
@@ -119,8 +120,12 @@ class Scheduler:
         # every running request feeds position num_computed; make sure its block exists
         self.running.sort(key=lambda r: r.arrival)
         i = 0
+        bs = self.bm.block_size
         while i < len(self.running):
             req = self.running[i]
+            if req.num_computed < len(req.blocks) * bs:  # its next position is in a block it holds
+                i += 1
+                continue
             if self.bm.can_grow(req.blocks, req.num_computed + 1):
                 self.bm.grow(req.blocks, req.num_computed + 1)
                 i += 1
@@ -135,14 +140,18 @@ class Scheduler:
         for req in self.running[: self.max_batch]:
             p = req.num_computed
             last = p == req.num_tokens - 1
-            plan.reqs.append(ScheduledReq(req.req_id, [req.tokens[p]], p, list(req.blocks), sample=last,
-                                          expect=None if last else req.tokens[p + 1],
+            # the block list is handed over, not copied: a plan is staged before the next schedule
+            # grows it, and growth only appends
+            plan.reqs.append(ScheduledReq(req.req_id, [req.token_at(p)], p, req.blocks, sample=last,
+                                          bt_version=req.blocks_version,
+                                          expect=None if last else req.token_at(p + 1),
                                           sampling=req.params.sampling_key(req.req_id),
                                           logprobs=req.params.logprobs if last else None))
         return plan
 
     def _preempt(self, req: Request) -> None:
         self.bm.free(req.blocks)
+        req.blocks_version += 1
         req.num_computed = 0
         req.committed = 0
         req.status = Status.WAITING
@@ -171,6 +180,7 @@ class Scheduler:
                 req.status = Status.FINISHED
                 self.running.remove(req)
                 self.bm.free(req.blocks)
+                req.blocks_version += 1
             out.append((sr.req_id, new, fin))
         if self.one_token_replay and all(r.num_computed >= r.num_tokens - 1 for r in self.running):
             self.one_token_replay = False
@@ -187,6 +197,7 @@ class Scheduler:
         for req in sorted([r for r in self.running if r.committed == 0], key=lambda r: -r.arrival):
             self.running.remove(req)
             self.bm.free(req.blocks)
+            req.blocks_version += 1
             req.num_computed = 0
             req.status = Status.WAITING
             self.waiting.appendleft(req)
