@@ -27,6 +27,17 @@ namespace {
 SSL_CTX* g_server = nullptr;
 SSL_CTX* g_client = nullptr;
 SSL_CTX* g_server_open = nullptr;  // the same identity, no client certificate asked (enrollment)
+// the contexts are replaced when the files change (reload_if_changed): a session is made under
+// this lock, and holds its own reference to its context from then on
+std::mutex g_mu;
+Config g_config;
+std::map<std::string, long long> g_mtimes;
+
+long long mtime_of(const std::string& path) {
+  struct stat st;
+  if (stat(path.c_str(), &st) != 0) return -1;
+  return (long long)st.st_mtim.tv_sec * 1000000000ll + st.st_mtim.tv_nsec;
+}
 
 std::string last_error() {
   char buf[256];
@@ -72,11 +83,37 @@ bool configure(const Config& c, std::string* err) {
   }
   SSL_CTX_set_verify(open, SSL_VERIFY_NONE, nullptr);
   // replaced contexts are freed: sessions made from them hold their own references
-  std::swap(g_server, server);
-  std::swap(g_client, client);
-  std::swap(g_server_open, open);
+  {
+    std::lock_guard<std::mutex> g(g_mu);
+    std::swap(g_server, server);
+    std::swap(g_client, client);
+    std::swap(g_server_open, open);
+    g_config = c;
+    g_mtimes.clear();
+    for (auto* f : {&c.ca, &c.cert, &c.key}) g_mtimes[*f] = mtime_of(*f);
+  }
   for (SSL_CTX* old : {server, client, open})
     if (old) SSL_CTX_free(old);
+  return true;
+}
+
+uint64_t reload_period_ms() {
+  static const uint64_t ms = std::strtoull(env_or("EVERSERVE_TLS_RELOAD_MS", "30000").c_str(), nullptr, 10);
+  return ms ? ms : 30000;
+}
+
+bool reload_if_changed(std::string* err) {
+  Config c;
+  bool changed = false;
+  {
+    std::lock_guard<std::mutex> g(g_mu);
+    if (g_server == nullptr) return true;
+    c = g_config;
+    for (auto& [f, t] : g_mtimes) changed |= mtime_of(f) != t;
+  }
+  if (!changed) return true;
+  if (!configure(c, err)) return false;
+  ES_INFO("TLS files changed: certificates reloaded");
   return true;
 }
 
@@ -104,6 +141,7 @@ bool configure_from_env(std::string* err) {
 bool enabled() { return g_server != nullptr && g_client != nullptr; }
 
 void* new_server(int fd) {
+  std::lock_guard<std::mutex> g(g_mu);
   SSL* s = SSL_new(g_server);
   SSL_set_fd(s, fd);
   SSL_set_accept_state(s);
@@ -111,6 +149,7 @@ void* new_server(int fd) {
 }
 
 void* new_client(int fd) {
+  std::lock_guard<std::mutex> g(g_mu);
   SSL* s = SSL_new(g_client);
   SSL_set_fd(s, fd);
   SSL_set_connect_state(s);
@@ -256,6 +295,7 @@ bool accept_stream(int fd, int timeout_ms, Stream& out, std::string* err, bool c
     if (client_cert) {
       out.ssl = new_server(fd);
     } else {
+      std::lock_guard<std::mutex> g(g_mu);
       SSL* s = SSL_new(g_server_open);
       SSL_set_fd(s, fd);
       SSL_set_accept_state(s);

@@ -11,6 +11,7 @@
 // `everserve-ctl certs init|issue` makes the CA and the per-process certificates.
 #pragma once
 
+#include <cstdint>
 #include <string>
 
 #include "net.h"
@@ -25,6 +26,11 @@ struct Config {
 bool configure(const Config& c, std::string* err);
 // From the environment; true (and TLS off) when nothing is configured.
 bool configure_from_env(std::string* err);
+// Configure again if a configured file changed since (renewed certificates are taken without a
+// restart); false only when the new files do not load (the old ones stay in use).
+bool reload_if_changed(std::string* err);
+// How often binaries look for changed TLS files: EVERSERVE_TLS_RELOAD_MS, default 30000.
+uint64_t reload_period_ms();
 bool enabled();
 
 // Non-blocking sessions for the loop (opaque SSL* as void*).

@@ -55,3 +55,35 @@ def test_mtls_control_plane(tmp_path):
         for n in nodes:
             n.stop()
         coord.stop()
+
+
+def test_renewed_certificate_is_taken_without_a_restart(tmp_path):
+    certs = str(tmp_path / "certs")
+    assert _ctl("certs", "init", certs).returncode == 0
+    assert _ctl("certs", "issue", certs, "coord").returncode == 0
+    listen, api = f"127.0.0.1:{free_port()}", f"127.0.0.1:{free_port()}"
+    env = dict(os.environ, EVERSERVE_TLS_DIR=certs, EVERSERVE_TLS_NAME="coord", EVERSERVE_TLS_RELOAD_MS="200")
+    coord = Proc([binary("everserve-coord"), "--listen", listen, "--api-addr", api, "--spec-store",
+                  str(tmp_path / "spec")], env=env)
+
+    def serial():
+        ctx = ssl.create_default_context(cafile=os.path.join(certs, "ca.crt"))
+        ctx.check_hostname = False
+        ctx.load_cert_chain(os.path.join(certs, "coord.crt"), os.path.join(certs, "coord.key"))
+        host, port = api.rsplit(":", 1)
+        with socket.create_connection((host, int(port)), timeout=5) as raw, ctx.wrap_socket(raw) as s:
+            return s.getpeercert()["serialNumber"]
+
+    try:
+        wait_socket(api)
+        before = serial()
+        time.sleep(1.1)  # a new serial (it is taken from the clock)
+        assert _ctl("certs", "issue", certs, "coord").returncode == 0
+        deadline = time.monotonic() + 10
+        after = before
+        while time.monotonic() < deadline and after == before:
+            time.sleep(0.2)
+            after = serial()
+        assert after != before
+    finally:
+        coord.stop()

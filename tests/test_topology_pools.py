@@ -168,3 +168,28 @@ def test_pool_spare_for_any_rank_takes_over_token_identical(tmp_path):
             assert _wait(lambda: cp.get("/v1/pools/p0")["status"]["short"] == 1)
         finally:
             ex.shutdown()
+
+
+def test_node_reclaimable_and_expected_pause(tmp_path):
+    with ControlPlane(str(tmp_path / "cp"), engines=[{"name": "e0", "tensorParallel": 2}], extra_nodes=["n1"]) as cp:
+        w0 = DaemonConnection(cp.daemon_sockets["n0"], "e0", _Dev(0, 0), node="n0")
+        w1 = DaemonConnection(cp.daemon_sockets["n0"], "e0", _Dev(1, 1), node="n0")
+        assert _wait(lambda: len(cp.engine_view("e0")["status"]["workers"]) == 2)
+        nodes = {n["metadata"]["name"]: n["status"] for n in cp.get("/v1/nodes")["items"]}
+        assert nodes["n0"]["reclaimable"] is False and "rank 0" in nodes["n0"]["reclaimBlocker"]
+        assert nodes["n1"]["reclaimable"] is True  # holds nothing
+        assert cp.engine_view("e0")["status"]["expectedPauseMs"] is None
+        # one spare for any rank on n1: n0 holds two ranks, so it is still not reclaimable
+        s1 = DaemonConnection(cp.daemon_sockets["n1"], "e0", _Dev(0, 0), node="n1", role=sp.ROLE_SPARE, any_rank=True)
+        assert _wait(lambda: cp.engine_view("e0")["status"]["spares"])
+        nodes = {n["metadata"]["name"]: n["status"] for n in cp.get("/v1/nodes")["items"]}
+        assert nodes["n0"]["reclaimable"] is False and "rank 1" in nodes["n0"]["reclaimBlocker"]
+        s2 = DaemonConnection(cp.daemon_sockets["n1"], "e0", _Dev(1, 1), node="n1", role=sp.ROLE_SPARE)
+        assert _wait(lambda: {n["metadata"]["name"]: n["status"] for n in cp.get("/v1/nodes")["items"]}["n0"]["reclaimable"])
+        # a change gives the engine an observed pause (rank 1's connection ends: a departure; a
+        # reported loss of a rank whose process still runs would have its daemon fence it, and
+        # here that process is this test's)
+        w1.close(sp.STOP_CAUSE_LOST)
+        assert _wait(lambda: cp.engine_view("e0")["status"]["expectedPauseMs"] is not None, timeout=15)
+        for c in (w0, s1, s2):
+            c.close()
