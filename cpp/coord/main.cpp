@@ -2,7 +2,7 @@
 //
 //   everserve-coord --listen unix:/run/everserve/coord.sock --policy policy.json --spec-store DIR
 //                   [--lease FILE] [--api-addr host:port] [--metrics-addr host:port]
-//                   [--node-loss-misses 3] [--delivery-timeout-ms 130000]
+//                   [--node-loss-misses 3] [--delivery-timeout-ms 130000] [--fold-ms 3]
 //                   [--lease-holder NAME] [--lease-duration-s 15]   (--lease k8s:NS/NAME: a Kubernetes Lease)
 //                   [--enroll-addr host:port] [--enroll-ca-dir DIR] [--enroll-hours 12]   (node enrollment, issuer.h)
 //                   [--api-auth cert|kube] [--api-namespace NS]   (operator API: client certificates, or api_auth.h)
@@ -80,6 +80,8 @@ struct Engine {
   std::map<std::pair<std::string, uint32_t>, std::string> refused;
   std::set<std::string> head_nodes;
   std::set<std::string> listeners;  // nodes where a process asked for the engine's start-up record
+  std::deque<double> pauses_ms;     // the last changes' pauses (report to commit), newest last
+  bool drive_posted = false;        // a drive is queued behind the reports now being read
   std::set<uint32_t> pending;
   std::set<uint32_t> departing;  // planned departures among pending
   uint64_t first_report_us = 0;
@@ -125,6 +127,7 @@ struct Coordinator {
   uint64_t term = 1;
   uint32_t loss_misses = 3;
   uint64_t delivery_timeout_ms = 130000;
+  uint64_t fold_ms = 3;  // how long a first loss report waits for others to fold into its change
   bool exit_after_log = false;  // host-side fault injection for tests: the coordinator dies mid-change
   std::map<std::string, Engine> engines;
   std::map<std::string, Node> nodes;
@@ -253,7 +256,19 @@ struct Coordinator {
     if (e.first_report_us == 0) e.first_report_us = now_us();
     e.cause = cause;
     event("engine " + name + ": lost ranks reported (" + cause + ")");
-    drive(e);
+    // the change starts `fold_ms` after the first report: losses that arrive together (processes
+    // of one node dying within a scan or two of its daemon's watcher) fold into one change rather
+    // than one change meeting the next loss in flight
+    if (!e.drive_posted) {
+      e.drive_posted = true;
+      auto go = [this, name] {
+        Engine& en = engine(name);
+        en.drive_posted = false;
+        drive(en);
+      };
+      if (fold_ms == 0) loop.post(go);
+      else loop.every(fold_ms, go, false);
+    }
   }
 
   void drive(Engine& e) {
@@ -407,6 +422,8 @@ struct Coordinator {
     mc.committed_at_us = now_us();
     mc.acks = f.acks;
     mc.pause_ms = (uint32_t)((mc.committed_at_us - (f.reported_us ? f.reported_us : f.delivered_us)) / 1000);
+    e.pauses_ms.push_back((mc.committed_at_us - (f.reported_us ? f.reported_us : f.delivered_us)) / 1e3);
+    if (e.pauses_ms.size() > 16) e.pauses_ms.pop_front();
     write_status(e, &f, &c);
     coord::CoordToDaemon m;
     m.has_committed = true;
@@ -1221,6 +1238,43 @@ struct Coordinator {
     }
   }
 
+  // ---- readiness -------------------------------------------------------------------------------
+  // Whether `node` can be drained now without an engine going down: every rank it holds has an
+  // admitted spare on another node (distinct spares; a spare for one rank only takes that rank).
+  std::string reclaim_blocker(const std::string& node) const {
+    for (auto& [name, e] : engines) {
+      std::vector<uint32_t> ranks;
+      for (auto& [r, h] : e.workers)
+        if (h.node == node) ranks.push_back(r);
+      if (ranks.empty()) continue;
+      std::vector<SpareSeat> seats;
+      for (auto& sp : e.spares)
+        if (sp.node != node) seats.push_back(sp);
+      std::vector<bool> used(seats.size(), false);
+      for (uint32_t r : ranks) {
+        int pick = -1;
+        for (size_t i = 0; i < seats.size() && pick < 0; i++)
+          if (!used[i] && seats[i].for_rank == (int64_t)r) pick = (int)i;
+        for (size_t i = 0; i < seats.size() && pick < 0; i++)
+          if (!used[i] && seats[i].for_rank < 0) pick = (int)i;
+        if (pick < 0) return "engine " + name + " rank " + std::to_string(r) + " has no spare on another node";
+        used[(size_t)pick] = true;
+      }
+    }
+    return "";
+  }
+
+  // The pause a loss is expected to cost now: the median of the engine's recent changes (null
+  // before its first).
+  std::string expected_pause_json(const Engine& e) const {
+    if (e.pauses_ms.empty()) return "null";
+    std::vector<double> v(e.pauses_ms.begin(), e.pauses_ms.end());
+    std::sort(v.begin(), v.end());
+    char buf[32];
+    std::snprintf(buf, sizeof buf, "%.3f", v[v.size() / 2]);
+    return buf;
+  }
+
   // ---- operator API ----------------------------------------------------------------------------
   std::string engine_json(const Engine& e) {
     std::string w = "[";
@@ -1287,7 +1341,8 @@ struct Coordinator {
     cov += "]}";
     return "{\"metadata\":{\"name\":\"" + json_escape(e.name) + "\"},\"status\":{\"epoch\":" + std::to_string(e.epoch) +
            ",\"worldSize\":" + std::to_string(e.world) + ",\"down\":" + (e.down ? "true" : "false") +
-           ",\"changing\":" + (e.in_flight ? "true" : "false") + ",\"workers\":" + w + ",\"spares\":" + s + ",\"refusedSpares\":" + refused + ",\"cover\":" + cov + ",\"conditions\":" + conds + "}}";
+           ",\"changing\":" + (e.in_flight ? "true" : "false") + ",\"workers\":" + w + ",\"spares\":" + s + ",\"refusedSpares\":" + refused + ",\"expectedPauseMs\":" +
+           expected_pause_json(e) + ",\"cover\":" + cov + ",\"conditions\":" + conds + "}}";
   }
 
   bool api(const HttpRequest& req, HttpResponse& resp) {
@@ -1325,7 +1380,9 @@ struct Coordinator {
         devs += "]";
         o += std::string(first ? "" : ",") + "{\"metadata\":{\"name\":\"" + json_escape(name) + "\"},\"spec\":{\"unschedulable\":" +
              (n.cordoned ? "true" : "false") + ",\"drainByMs\":" + std::to_string(n.drain_by_ms) + "},\"status\":{\"linked\":" +
-             (n.linked ? "true" : "false") + ",\"domain\":\"" + json_escape(topo.domain_of(name)) + "\",\"devices\":" + devs + "}}";
+             (n.linked ? "true" : "false") + ",\"domain\":\"" + json_escape(topo.domain_of(name)) + "\",\"devices\":" + devs +
+             ",\"reclaimable\":" + (reclaim_blocker(name).empty() ? "true" : "false") + ",\"reclaimBlocker\":\"" +
+             json_escape(reclaim_blocker(name)) + "\"}}";
         first = false;
       }
       resp.body = o + "]}";
@@ -1510,6 +1567,7 @@ int main(int argc, char** argv) {
   std::string api_addr = env_or("EVERSERVE_API_ADDR", "");
   std::string metrics_addr = env_or("EVERSERVE_METRICS_ADDR", "");
   co.loss_misses = (uint32_t)std::stoul(env_or("EVERSERVE_NODE_LOSS_MISSES", "3"));
+  co.fold_ms = std::stoull(env_or("EVERSERVE_FOLD_MS", "3"));
   std::string lease_holder = env_or("EVERSERVE_LEASE_HOLDER", "");
   std::string enroll_addr = env_or("EVERSERVE_ENROLL_ADDR", "");
   std::string enroll_ca_dir = env_or("EVERSERVE_ENROLL_CA_DIR", env_or("EVERSERVE_TLS_DIR", ""));
@@ -1527,6 +1585,7 @@ int main(int argc, char** argv) {
     else if (k == "--metrics-addr") metrics_addr = v;
     else if (k == "--node-loss-misses") co.loss_misses = (uint32_t)std::stoul(v);
     else if (k == "--delivery-timeout-ms") co.delivery_timeout_ms = std::stoull(v);
+    else if (k == "--fold-ms") co.fold_ms = std::stoull(v);
     else if (k == "--lease-holder") lease_holder = v;
     else if (k == "--enroll-addr") enroll_addr = v;
     else if (k == "--enroll-ca-dir") enroll_ca_dir = v;
@@ -1652,6 +1711,10 @@ int main(int argc, char** argv) {
     ES_ERROR("metrics %s: %s", metrics_addr.c_str(), err.c_str());
     return 1;
   }
+  co.loop.every(tls::reload_period_ms(), [] {  // renewed certificates, taken without a restart
+    std::string terr;
+    if (!tls::reload_if_changed(&terr)) ES_WARN("TLS reload: %s", terr.c_str());
+  });
   co.loop.every(100, [&] { co.check_heartbeats(); });
   co.loop.every(1000, [&] {
     co.reconcile_pools();

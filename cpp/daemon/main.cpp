@@ -1098,6 +1098,10 @@ int main(int argc, char** argv) {
     ES_ERROR("metrics %s: %s", metrics_addr.c_str(), err.c_str());
     return 1;
   }
+  d.loop.every(tls::reload_period_ms(), [] {  // renewed certificates, taken without a restart
+    std::string terr;
+    if (!tls::reload_if_changed(&terr)) ES_WARN("TLS reload: %s", terr.c_str());
+  });
   d.link();
   d.loop.every(d.heartbeat_ms, [&] { d.tick(); });
   d.loop.every(100, [&] { d.supervise(); });

@@ -294,6 +294,10 @@ int main(int argc, char** argv) {
     ES_ERROR("metrics %s: %s", o.metrics_addr.c_str(), err.c_str());
     return 1;
   }
+  loop.every(tls::reload_period_ms(), [] {  // renewed certificates, taken without a restart
+    std::string terr;
+    if (!tls::reload_if_changed(&terr)) ES_WARN("TLS reload: %s", terr.c_str());
+  });
   ES_INFO("serving %s (data %s, %zu slots, budget %zu bytes)", o.socket.c_str(), o.data_dir.c_str(), o.slots, o.budget);
   loop.run();
   return 0;

@@ -100,6 +100,7 @@ class CarrierServer:
         self.address = f"{host}:{self.sock.getsockname()[1]}"
         self.links: dict[int, Link] = {}
         self.arrivals: queue.Queue[Link] = queue.Queue()
+        self._unclaimed: list[Link] = []  # links that arrived while another was awaited
         self._stop = threading.Event()
         self._accept = threading.Thread(target=self._accept_loop, name="carrier-accept", daemon=True)
         self._accept.start()
@@ -134,7 +135,12 @@ class CarrierServer:
                 return
 
     def wait_link(self, timeout: float, want=None) -> Link:
-        """The next arriving link (optionally one whose hello satisfies `want`)."""
+        """The next arriving link (optionally one whose hello satisfies `want`). A link that
+        arrives while another is wanted is kept for a later call (two spares taking two ranks
+        link in either order)."""
+        for i, link in enumerate(self._unclaimed):
+            if want is None or want(link.hello):
+                return self._unclaimed.pop(i)
         deadline = time.monotonic() + timeout
         while True:
             left = deadline - time.monotonic()
@@ -146,6 +152,7 @@ class CarrierServer:
                 raise TimeoutError("no rank linked in time") from None
             if want is None or want(link.hello):
                 return link
+            self._unclaimed.append(link)
 
     def close(self) -> None:
         self._stop.set()

@@ -193,7 +193,10 @@ class MultiprocExecutor:
         self._boundary(0)
         self.changes: list[ChangeRecord] = []
         self.decode_steps_run = 0
-        self.kill_at_decode_step: tuple[int, int] | None = None  # (decode step, rank): host-side fault injection
+        # host-side fault injection: (decode step, rank or ranks), or (prefill step, rank or ranks)
+        self.kill_at_decode_step: tuple | None = None
+        self.kill_at_prefill_step: tuple | None = None
+        self.prefill_steps_run = 0
         self.notice_at_decode_step: tuple[int, int] | None = None  # (decode step, rank): a planned departure
         self.t_kill = self.t_kill_wall = 0.0
         self._finished: list[str] = []
@@ -233,6 +236,11 @@ class MultiprocExecutor:
             self._broadcast({"op": "finished", "ids": self._finished})
             self._finished = []
         victim = None
+        if plan.is_prefill:
+            self.prefill_steps_run += 1
+            if self.kill_at_prefill_step and self.prefill_steps_run == self.kill_at_prefill_step[0]:
+                victim = self.kill_at_prefill_step[1]
+                self.kill_at_prefill_step = None
         if not plan.is_prefill:
             self.decode_steps_run += 1
             if self.kill_at_decode_step and self.decode_steps_run == self.kill_at_decode_step[0]:
@@ -242,9 +250,11 @@ class MultiprocExecutor:
                 self.t_kill = time.monotonic()
                 self.notice(self.notice_at_decode_step[1])
                 self.notice_at_decode_step = None
+        if victim is not None and not isinstance(victim, (list, tuple)):
+            victim = [victim]
         if victim is not None and self.gpu:
             # on GPUs a rank leaves between steps (its kernels done), never mid-kernel
-            msg = dict(msg, fail_at=plan.step, fail_rank=victim)
+            msg = dict(msg, fail_at=plan.step, fail_rank=list(victim))
             self.t_kill, self.t_kill_wall = time.monotonic(), time.time()
             victim = None
         lost, errors = set(), {}
@@ -255,7 +265,8 @@ class MultiprocExecutor:
                 lost.add(r)
         if victim is not None:
             self.t_kill, self.t_kill_wall = time.monotonic(), time.time()
-            os.kill(self.pid_of(victim), signal.SIGKILL)  # the fault: SIGKILL mid-step
+            for v in victim:
+                os.kill(self.pid_of(v), signal.SIGKILL)  # the fault: SIGKILL mid-step
         ids = None
         for r, link in self.links.items():
             if r in lost:

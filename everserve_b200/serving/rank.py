@@ -259,7 +259,11 @@ class RankProcess:
     def identity(self) -> tuple[int, int]:
         if self._link_device is not None:  # the device the adopted link registered
             return self.rank, self._link_device
-        return self.rank, self.device.index or 0 if self.device.type == "cuda" else 0
+        if self.device.type == "cuda":
+            return self.rank, self.device.index or 0
+        # a CPU process has no device of its own: its row (one per process) stands in, so two
+        # spares on one node are two seats
+        return self.rank, self.row
 
     def on_change(self, change) -> str | None:
         self.runtime.trace("change", epoch=change.epoch)
@@ -384,7 +388,8 @@ class RankProcess:
 
     def _step(self, msg: dict) -> None:
         plan = msg["plan"]
-        if msg.get("fail_at") == plan.step and self.rank == msg.get("fail_rank"):
+        fail = msg.get("fail_rank")
+        if msg.get("fail_at") == plan.step and (self.rank in fail if isinstance(fail, list) else self.rank == fail):
             # host-side fault injection: the process dies between steps, nothing of it in flight
             if self.device.type == "cuda":
                 torch.cuda.synchronize(self.device)

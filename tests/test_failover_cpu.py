@@ -33,7 +33,7 @@ def _prompts():
     return [[rng.randrange(vocab) for _ in range(PROMPT)] for _ in range(STREAMS)]
 
 
-def _run(workdir, kill_at=None, spares=(1,), **sampling):
+def _run(workdir, kill_at=None, spares=(1,), kill_prefill=None, **sampling):
     cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
                        max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
     with ControlPlane(str(workdir), engines=[{"name": "e0", "pipelineParallel": 2}]) as cp:
@@ -46,7 +46,9 @@ def _run(workdir, kill_at=None, spares=(1,), **sampling):
             eng = Engine(cfg, executor=ex)
             eng.wrap_step(failover(ex, eng))
             if kill_at is not None:
-                ex.kill_at_decode_step = (kill_at, 1)
+                ex.kill_at_decode_step = kill_at if isinstance(kill_at, tuple) else (kill_at, 1)
+            if kill_prefill is not None:
+                ex.kill_at_prefill_step = kill_prefill
             out = eng.generate(_prompts(), max_tokens=TOKENS, **sampling)
             mism = sum(r.replay_mismatches for r in eng.scheduler.requests.values())
             view = cp.engine_view("e0")
@@ -303,3 +305,24 @@ def test_logprobs_through_the_multiprocess_engine(tmp_path):
                     assert abs(la - lb) < 1e-4 and [t for t, _ in ta] == [t for t, _ in tb]
         finally:
             ex.shutdown()
+
+
+@pytest.mark.slow
+def test_rank_killed_during_prefill_is_replaced_and_prefill_runs_again(tmp_path):
+    """Nothing is committed when a rank dies in the middle of the first prefill: every request
+    goes back to the queue and is prefilled again on the new membership."""
+    base, _, _, _ = _run(tmp_path / "nofault", spares=())
+    out, changes, mism, _ = _run(tmp_path / "fault", kill_prefill=(1, 1))
+    assert len(changes) == 1 and changes[0].lost == [1]
+    assert mism == 0 and out == base
+
+
+@pytest.mark.slow
+def test_two_ranks_killed_at_once_both_replaced(tmp_path):
+    """Both stages lose their process in the same step; a spare stands for each and both take
+    their ranks in one change."""
+    base, _, _, _ = _run(tmp_path / "nofault", spares=())
+    out, changes, mism, view = _run(tmp_path / "fault", kill_at=(KILL_AT, [0, 1]), spares=(0, 1))
+    assert len(changes) == 1 and sorted(changes[0].lost) == [0, 1]
+    assert mism == 0 and out == base
+    assert view["status"]["epoch"] == 1

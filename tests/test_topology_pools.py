@@ -142,7 +142,7 @@ def test_pool_spare_for_any_rank_takes_over_token_identical(tmp_path):
     base, _, _, _ = _run(tmp_path / "nofault", spares=())
     cfg = EngineConfig(model=MODEL, device="cpu", dtype=torch.float32, num_blocks=128, max_batch=STREAMS,
                        max_model_len=PROMPT + TOKENS + 16, pipeline_parallel=2, use_cuda_graphs=False)
-    smi = _fake_smi(str(tmp_path / "smi"), [("NVIDIA B200", 183359)] * 2)
+    smi = _fake_smi(str(tmp_path / "smi"), [("NVIDIA B200", 183359)] * 3)  # ranks 0 and 1 hold devices 0, 1
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     with ControlPlane(str(tmp_path / "pool"), engines=[{"name": "e0", "pipelineParallel": 2}],
                       node_args=["--devices-from", smi]) as cp:
@@ -156,16 +156,16 @@ def test_pool_spare_for_any_rank_takes_over_token_identical(tmp_path):
             assert code == 200
             cp.wait_spares("e0", 1, timeout_s=300)
             spare = cp.engine_view("e0")["status"]["spares"][0]
-            assert spare["forRank"] == -1 and spare["pool"] == "p0" and spare["device"] == 1
+            assert spare["forRank"] == -1 and spare["pool"] == "p0" and spare["device"] == 2
             eng = Engine(cfg, executor=ex)
             eng.wrap_step(failover(ex, eng))
             ex.kill_at_decode_step = (KILL_AT, 1)
             out = eng.generate(_prompts(), max_tokens=TOKENS)
             assert len(ex.changes) == 1 and out == base
             workers = {w["rank"]: w for w in cp.engine_view("e0")["status"]["workers"]}
-            assert workers[1]["device"] == 1  # the pool's device holds rank 1 now
-            # its spare is spent and no B200 is free: the pool is short of one
-            assert _wait(lambda: cp.get("/v1/pools/p0")["status"]["short"] == 1)
+            assert workers[1]["device"] == 2  # the pool's device holds rank 1 now
+            # its spare is spent; the lost rank's device is free again, and the pool launches there
+            assert _wait(lambda: cp.get("/v1/pools/p0")["status"]["short"] == 0, timeout=30)
         finally:
             ex.shutdown()
 
