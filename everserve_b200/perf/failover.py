@@ -105,6 +105,7 @@ def main() -> None:
                 "detect_ms": (rep_us / 1e3 - t_fault * 1e3) if rep_us else None,
                 "commit_ms": d["committed_ms"], "resumed_ms": d["resumed_ms"],
                 "pause_ms": max(gaps) * 1e3 if gaps else None,
+                "spans": d["spans"], "acks_at_us": rec.coordinator.get("acks_at_us"),
             })
         summary = {"metric": "failover pause p99; dead-rank detect ms", "model": model, "device": a.device,
                    "trials": len(rows), "token_identical": all(r["identical"] for r in rows)}
