@@ -57,6 +57,12 @@ struct GemmArgs {
   const void* pre = nullptr;
   int64_t ldp = 0;
   int two_shot = 0;  // fused all-reduce: 1 = reduce-scatter to tile owners, then all-gather
+  // grouped rows (an expert over what each sender dispatched to it): rows [s*valid_cap, s*valid_cap
+  // + valid[s]) of each of the valid_segs segments are live; token tiles holding no live row are
+  // skipped and their output rows left unwritten (plain GEMM only)
+  const uint32_t* valid = nullptr;
+  int64_t valid_cap = 0;
+  int valid_segs = 0;
 };
 int64_t gemm_pick_bn(int64_t M);
 int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms);
@@ -66,11 +72,36 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t s);
 // Mixture routing: per token softmax over E logits (bf16 rows of `stride`), top k (ties to the
 // lowest index), renormalised; scale[e, t] for this rank's experts e0 .. e0 + el - 1 (0 when not
 // chosen). E <= 64, el <= 32.
+// `ids`/`weights` (nullable, [T, k]): each token's chosen experts in rank order and their
+// renormalised probabilities; `scale` (nullable when el = 0).
 cudaError_t launch_moe_route(const void* logits, int64_t stride, int T, int E, int k, int e0, int el, float* scale,
-                             cudaStream_t s);
+                             int32_t* ids, float* weights, cudaStream_t s);
 // out = sum over the group's members (member order) of x_r . w_r^T (+ residual): the row-parallel
 // GEMM with its all-reduce fused into the epilogue (decode sizes, M <= 64).
 cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStream_t s);
+
+// ---- moe.cu (expert-parallel all-to-all over peer memory; layout in moe.cu) -----------------------
+struct MoeArgs {
+  const uint64_t* peers;   // device [8]: each row's MoE buffer (0 = unmapped)
+  const int32_t* members;  // device [1 + 8]: member count W, then the row holding each position
+  uint32_t* call;          // device [2 * nz]: call counter and CTAs done, per emulated member
+  void* ctrl;              // control words (comm Ctrl) of the first member; nz of them in a row
+  int pos;                 // this member's position (the first of the nz it plays)
+  int nz;                  // members this launch plays (1 with a GPU each)
+  int E, el, k, H;         // experts, experts per member, experts per token, hidden size
+  int64_t cap;             // rows of one (expert, sender) segment: at least a sender's token count
+  int splits;              // dispatch CTAs per expert
+};
+int64_t moe_header_bytes();
+int64_t moe_counts_offset();
+int64_t moe_counts_stride();
+int64_t moe_buffer_bytes(int64_t el, int64_t W, int64_t cap, int64_t H);
+// x [nz][T, H] (member stride x_member elements), ids [nz][T, k]; writes place [nz][T, k]
+cudaError_t launch_moe_dispatch(const void* x, int64_t x_member, const int32_t* ids, int32_t* place, int T,
+                                const MoeArgs& a, cudaStream_t s);
+cudaError_t launch_moe_ready(const MoeArgs& a, cudaStream_t s);
+cudaError_t launch_moe_combine(const int32_t* ids, const float* weights, const int32_t* place, void* out,
+                               int64_t out_member, int T, int num_sms, const MoeArgs& a, cudaStream_t s);
 
 // ---- attention.cu --------------------------------------------------------------------------------
 struct DecodeArgs {

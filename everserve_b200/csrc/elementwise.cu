@@ -243,7 +243,8 @@ __global__ void argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t*
 // probabilities renormalised, and for this rank's experts [e0, e0 + el) the weight of each token
 // (0 where the expert is not among the token's top k). One warp per token, E <= 64.
 __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, int64_t stride, int T, int E, int k,
-                                 int e0, int el, float* __restrict__ scale) {
+                                 int e0, int el, float* __restrict__ scale, int32_t* __restrict__ ids,
+                                 float* __restrict__ weights) {
   pdl_wait();
   pdl_launch();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -278,7 +279,13 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, int64
     if (bi == lane) s0 = true;
     if (bi == lane + 32) s1 = true;
     chosen += bv;
+    if (lane == 0 && ids) {
+      ids[(size_t)t * k + r] = bi;
+      weights[(size_t)t * k + r] = bv;
+    }
   }
+  if (lane == 0 && ids)
+    for (int r = 0; r < k; r++) weights[(size_t)t * k + r] /= chosen;
   for (int e = 0; e < el; e++) {  // the same trip count on every lane: the shuffles take the warp
     const int g = e0 + e;
     const float v0 = __shfl_sync(0xffffffffu, s0 ? p0 : 0.f, g & 31);
@@ -290,12 +297,13 @@ __global__ void moe_route_kernel(const __nv_bfloat16* __restrict__ logits, int64
 }  // namespace
 
 cudaError_t launch_moe_route(const void* logits, int64_t stride, int T, int E, int k, int e0, int el, float* scale,
-                             cudaStream_t stream) {
+                             int32_t* ids, float* weights, cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   if (E > 64 || k < 1 || k > E || el > 32 || e0 < 0 || e0 + el > E) return cudaErrorInvalidValue;
+  if ((el > 0 && !scale) || (!ids != !weights)) return cudaErrorInvalidValue;
   constexpr int kWarps = 4;
   return launch_ex(moe_route_kernel, dim3((unsigned)((T + kWarps - 1) / kWarps)), dim3(32 * kWarps), 0, stream, 0,
-                   static_cast<const __nv_bfloat16*>(logits), stride, T, E, k, e0, el, scale);
+                   static_cast<const __nv_bfloat16*>(logits), stride, T, E, k, e0, el, scale, ids, weights);
 }
 
 cudaError_t launch_decode_advance(int64_t* st, const int64_t* sampled, const int* bt, int64_t bt_stride, int b, int B,

@@ -60,7 +60,20 @@ struct Params {
   const __nv_bfloat16* pre;    // added to the (scaled) product before any reduction (nullable)
   int ldp;
   int two_shot;                // fused all-reduce as reduce-scatter to tile owners + all-gather
+  const uint32_t* valid;       // grouped rows: valid[s] rows of segment s (rows [s*cap, (s+1)*cap)) are live
+  int valid_cap, valid_segs;
 };
+
+// A token tile [m0, m0 + BN) of a grouped GEMM holds a live row: some segment it overlaps has a
+// count reaching into it. Tiles without one are skipped whole (their output rows are padding).
+ES_DEVICE bool tile_live(const Params& p, int m0, int BN) {
+  const int last = min(p.M, m0 + BN) - 1;
+  for (int seg = m0 / p.valid_cap; seg <= last / p.valid_cap && seg < p.valid_segs; seg++) {
+    const int lo = max(m0, seg * p.valid_cap) - seg * p.valid_cap;
+    if (lo < (int)p.valid[seg]) return true;
+  }
+  return false;
+}
 
 // the product's epilogue terms before a reduction over members: acc * scale[m] + pre[m, n]
 ES_DEVICE float pre_terms(const Params& p, float acc, size_t m, int n) {
@@ -98,6 +111,12 @@ __global__ void __launch_bounds__(kThreads, CPS)
   const int kb0 = split * kps;
   const int nkb = max(0, min(p.kb, kb0 + kps) - kb0);
 
+  if (!kAR && p.valid != nullptr) {
+    // the counts come from the kernel before; every CTA of a cluster shares the token tile, so a
+    // skipped tile's cluster leaves together, before any barrier, TMEM allocation or copy
+    pdl_wait();
+    if (!tile_live(p, m0, BN)) return;
+  }
   if (threadIdx.x == 0) {
     s_fail = 0;
     ptx::prefetch_tmap(&tmap_w);
@@ -474,6 +493,12 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.scale = a.scale;
   p.pre = static_cast<const __nv_bfloat16*>(a.pre);
   p.ldp = (int)a.ldp;
+  if (a.valid != nullptr) {
+    if (a.valid_cap <= 0 || a.valid_segs <= 0 || a.valid_cap * a.valid_segs < a.M) return cudaErrorInvalidValue;
+    p.valid = a.valid;
+    p.valid_cap = (int)a.valid_cap;
+    p.valid_segs = a.valid_segs;
+  }
   int cps = 1;
   gemm_plan(a.M, a.N, a.K, a.num_sms, &p.splits, &cps);
   const unsigned tiles_n = (unsigned)((a.N + gemm::BM - 1) / gemm::BM);

@@ -129,7 +129,8 @@ void mixture_terms(es::GemmArgs& a, const c10::optional<torch::Tensor>& scale, c
 
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
                torch::Tensor ws, torch::Tensor sync, torch::Tensor status, int64_t num_sms,
-               c10::optional<torch::Tensor> scale, c10::optional<torch::Tensor> pre) {
+               c10::optional<torch::Tensor> scale, c10::optional<torch::Tensor> pre,
+               c10::optional<torch::Tensor> valid, int64_t valid_cap) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
@@ -162,6 +163,14 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
     a.ldr = residual->stride(0);
   }
   mixture_terms(a, scale, pre);
+  if (valid.has_value() && valid->defined()) {
+    TORCH_CHECK(valid->is_cuda() && valid->scalar_type() == at::kInt && valid->is_contiguous(),
+                "valid: int32 counts on the device");
+    TORCH_CHECK(valid_cap > 0 && valid_cap * valid->numel() >= M, "valid: segments of valid_cap rows cover M");
+    a.valid = reinterpret_cast<const uint32_t*>(valid->data_ptr<int32_t>());
+    a.valid_cap = valid_cap;
+    a.valid_segs = (int)valid->numel();
+  }
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
 }
@@ -173,8 +182,95 @@ torch::Tensor moe_route(torch::Tensor logits, int64_t k, int64_t e0, int64_t el)
   auto scale = torch::empty({el, T}, logits.options().dtype(at::kFloat));
   const c10::cuda::CUDAGuard g(logits.device());
   ES_CHECK_CUDA(es::launch_moe_route(logits.data_ptr(), logits.stride(0), (int)T, (int)E, (int)k, (int)e0, (int)el,
-                                     scale.data_ptr<float>(), cur()));
+                                     scale.data_ptr<float>(), nullptr, nullptr, cur()));
   return scale;
+}
+
+// Each token's top k experts (rank order) and their renormalised probabilities: (ids [T, k] int32,
+// weights [T, k] fp32).
+std::vector<torch::Tensor> moe_topk(torch::Tensor logits, int64_t k) {
+  check_bf16(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits: [T, E] rows");
+  const int64_t T = logits.size(0), E = logits.size(1);
+  auto ids = torch::empty({T, k}, logits.options().dtype(at::kInt));
+  auto w = torch::empty({T, k}, logits.options().dtype(at::kFloat));
+  const c10::cuda::CUDAGuard g(logits.device());
+  ES_CHECK_CUDA(es::launch_moe_route(logits.data_ptr(), logits.stride(0), (int)T, (int)E, (int)k, 0, 0, nullptr,
+                                     ids.data_ptr<int32_t>(), w.data_ptr<float>(), cur()));
+  return {ids, w};
+}
+
+// A uint8 tensor over `nbytes` of device memory at `ptr` that the caller keeps alive (a mapped
+// symmetric buffer): lets the GEMMs read and write regions of it.
+torch::Tensor device_view(int64_t ptr, int64_t nbytes, int64_t device) {
+  TORCH_CHECK(ptr != 0 && nbytes > 0, "an address and a size");
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {nbytes},
+                          torch::TensorOptions().dtype(at::kByte).device(at::kCUDA, (c10::DeviceIndex)device));
+}
+
+// The expert-parallel all-to-all's tables: peers int64[8] (buffer of each row), members int32[9]
+// (count, row of each position), call int32[2 * nz], ctrl (device address of nz control words).
+es::MoeArgs moe_args(torch::Tensor peers, torch::Tensor members, torch::Tensor call, int64_t ctrl, int64_t pos,
+                     int64_t nz, int64_t E, int64_t el, int64_t k, int64_t H, int64_t cap, int64_t splits) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong && peers.numel() >= 8, "peers: int64[8] on the device");
+  TORCH_CHECK(members.is_cuda() && members.scalar_type() == at::kInt && members.numel() >= 9,
+              "members: int32[9] on the device");
+  TORCH_CHECK(call.is_cuda() && call.scalar_type() == at::kInt && call.numel() >= 2 * nz,
+              "call: int32[2 * nz] on the device");
+  TORCH_CHECK(ctrl != 0 && nz >= 1 && pos >= 0 && pos + nz <= 8, "control words, position and members played");
+  es::MoeArgs a{};
+  a.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  a.members = members.data_ptr<int32_t>();
+  a.call = reinterpret_cast<uint32_t*>(call.data_ptr<int32_t>());
+  a.ctrl = reinterpret_cast<void*>(ctrl);
+  a.pos = (int)pos;
+  a.nz = (int)nz;
+  a.E = (int)E;
+  a.el = (int)el;
+  a.k = (int)k;
+  a.H = (int)H;
+  a.cap = cap;
+  a.splits = (int)splits;
+  return a;
+}
+
+void moe_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor place, torch::Tensor peers, torch::Tensor members,
+                  torch::Tensor call, int64_t ctrl, int64_t pos, int64_t E, int64_t el, int64_t cap, int64_t splits) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 3 && x.is_contiguous(), "x: [members played, T, H] contiguous");
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == at::kInt && ids.is_contiguous() && ids.dim() == 3 &&
+                  ids.size(0) == x.size(0) && ids.size(1) == x.size(1), "ids: int32 [members played, T, k]");
+  TORCH_CHECK(place.is_cuda() && place.scalar_type() == at::kInt && place.is_contiguous() &&
+                  place.sizes() == ids.sizes(), "place: int32 like ids");
+  const auto a = moe_args(peers, members, call, ctrl, pos, x.size(0), E, el, ids.size(2), x.size(2), cap, splits);
+  const c10::cuda::CUDAGuard g(x.device());
+  ES_CHECK_CUDA(es::launch_moe_dispatch(x.data_ptr(), x.size(1) * x.size(2), ids.data_ptr<int32_t>(),
+                                        place.data_ptr<int32_t>(), (int)x.size(1), a, cur()));
+}
+
+void moe_ready(torch::Tensor peers, torch::Tensor members, torch::Tensor call, int64_t ctrl, int64_t pos, int64_t nz,
+               int64_t E, int64_t el, int64_t k, int64_t H, int64_t cap) {
+  const auto a = moe_args(peers, members, call, ctrl, pos, nz, E, el, k, H, cap, 1);
+  const c10::cuda::CUDAGuard g(peers.device());
+  ES_CHECK_CUDA(es::launch_moe_ready(a, cur()));
+}
+
+void moe_combine(torch::Tensor ids, torch::Tensor weights, torch::Tensor place, torch::Tensor out, torch::Tensor peers,
+                 torch::Tensor members, torch::Tensor call, int64_t ctrl, int64_t pos, int64_t E, int64_t el,
+                 int64_t cap, int64_t num_sms) {
+  check_bf16(out, "out");
+  TORCH_CHECK(out.dim() == 3 && out.is_contiguous(), "out: [members played, T, H] contiguous");
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == at::kInt && ids.is_contiguous() && ids.dim() == 3 &&
+                  ids.size(0) == out.size(0) && ids.size(1) == out.size(1), "ids: int32 [members played, T, k]");
+  TORCH_CHECK(weights.is_cuda() && weights.scalar_type() == at::kFloat && weights.is_contiguous() &&
+                  weights.sizes() == ids.sizes(), "weights: fp32 like ids");
+  TORCH_CHECK(place.is_cuda() && place.scalar_type() == at::kInt && place.is_contiguous() &&
+                  place.sizes() == ids.sizes(), "place: int32 like ids");
+  const auto a = moe_args(peers, members, call, ctrl, pos, out.size(0), E, el, ids.size(2), out.size(2), cap, 1);
+  const c10::cuda::CUDAGuard g(out.device());
+  ES_CHECK_CUDA(es::launch_moe_combine(ids.data_ptr<int32_t>(), weights.data_ptr<float>(), place.data_ptr<int32_t>(),
+                                       out.data_ptr(), out.size(1) * out.size(2), (int)out.size(1), (int)num_sms, a,
+                                       cur()));
 }
 
 es::CommArgs comm_args(torch::Tensor peers, torch::Tensor order, torch::Tensor call, int64_t ctrl, int64_t row,
@@ -398,13 +494,23 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM out = x . w^T * scale + pre (+ residual)", pybind11::arg("x"),
         pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("residual"), pybind11::arg("ws"), pybind11::arg("sync"),
         pybind11::arg("status"), pybind11::arg("num_sms"), pybind11::arg("scale") = pybind11::none(),
-        pybind11::arg("pre") = pybind11::none());
+        pybind11::arg("pre") = pybind11::none(), pybind11::arg("valid") = pybind11::none(),
+        pybind11::arg("valid_cap") = 0);
   m.def("gemm_pick_bn", &es::gemm_pick_bn);
   m.def("gemm_pick_splits", &es::gemm_pick_splits);
   m.def("gemm_ws_floats", &es::gemm_ws_floats);
   m.def("gemm_sync_words", &es::gemm_sync_words);
   m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
   m.def("moe_route", &moe_route, "mixture routing: per-token weights of this rank's experts [el, T]");
+  m.def("moe_topk", &moe_topk, "mixture routing: each token's top k experts and their weights");
+  m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch of tokens to their experts' owners (peer stores)");
+  m.def("moe_ready", &moe_ready, "expert-parallel: this member's expert outputs are written");
+  m.def("moe_combine", &moe_combine, "expert-parallel combine: each token's weighted expert outputs (peer loads)");
+  m.def("moe_buffer_bytes", &es::moe_buffer_bytes);
+  m.def("device_view", &device_view, "uint8 tensor over caller-owned device memory");
+  m.def("moe_header_bytes", &es::moe_header_bytes);
+  m.def("moe_counts_offset", &es::moe_counts_offset);
+  m.def("moe_counts_stride", &es::moe_counts_stride);
   m.def("fdar", &fdar, "failure-detecting all-reduce over peer memory (member order)");
   m.def("gemm_allreduce", &gemm_allreduce, "row-parallel GEMM with the all-reduce fused into its epilogue",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("residual"), pybind11::arg("status"),

@@ -2,6 +2,7 @@
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -25,6 +26,9 @@ class EngineConfig:
     pipeline_parallel: int = 1
     use_cuda_graphs: bool = True
     checkpoint: str | None = None  # a Hugging Face safetensors directory; None: random-init from `seed`
+    # mixture models on a peer-memory TP group: route tokens to their experts' owners (all-to-all)
+    # instead of running every local expert on every token; ES_MOE_ROUTED=1 sets it
+    moe_routed: bool = field(default_factory=lambda: os.environ.get("ES_MOE_ROUTED", "0") == "1")
     extra: dict = field(default_factory=dict)
 
     def __post_init__(self):

@@ -46,6 +46,8 @@ class Worker:
             from ..models.weights import load_hf_checkpoint
 
             load_hf_checkpoint(self.model, cfg.checkpoint)
+        if cfg.moe_routed:
+            self.model.enable_routed_experts(max(cfg.max_prefill_tokens, cfg.max_batch))
         self.num_blocks = cfg.num_blocks or self._auto_blocks()
         self.runner = ModelRunner(self.model, self.num_blocks, cfg.block_size, cfg.max_batch, cfg.max_model_len,
                                   cfg.use_cuda_graphs and pp == 1)

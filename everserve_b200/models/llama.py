@@ -87,6 +87,7 @@ class DecoderLM:
         self.dtype = dtype
         self.seed = seed
         self.step_logprobs = None  # the last forward's log-probabilities, when it was asked for them
+        self.a2a = None  # routed experts (parallel.moe_a2a), when enabled
         self.tp = tp or TPGroup()
         self.ops = ops_for(self.device)
         self.l0, self.l1 = layer_range or (0, cfg.layers)
@@ -311,6 +312,40 @@ class DecoderLM:
         return allp[torch.arange(pair.shape[0], device=pair.device), best, 1].long()
 
     # ---- MoE -----------------------------------------------------------------------------------
+    def enable_routed_experts(self, max_tokens: int) -> bool:
+        """Route each token to its experts' owners instead of running every local expert on every
+        token (``parallel.moe_a2a``): rank r takes the r-th slice of the step's (replicated) tokens,
+        the all-to-all carries each row to the ranks owning its top k experts, the experts run
+        grouped GEMMs over what they received (tiles no token reached are skipped: unchosen experts
+        read no weights, and prefill does the routed FLOPs instead of E/k times them), the combine
+        brings the weighted outputs back, and an all-gather of the slices replicates the result.
+        Needs the GPU kernels and a peer-memory collective; False (nothing changes) otherwise."""
+        coll = self.tp.collective
+        if (not self.cfg.is_moe or self.tp.size == 1 or self.ops.kind != "kernel" or coll is None
+                or not hasattr(coll, "region") or getattr(coll, "nvls", False)):
+            return False
+        from ..parallel.moe_a2a import ExpertAllToAll, default_cap
+
+        per = -(-max_tokens // self.tp.size)
+        self.a2a = ExpertAllToAll.over(coll, experts=self.cfg.num_experts, top_k=self.cfg.top_k,
+                                       hidden=self.cfg.hidden, cap=default_cap(per))
+        return True
+
+    def _moe_routed(self, h: torch.Tensor, p: str) -> torch.Tensor:
+        ops, c, W = self.ops, self.cfg, self.weights
+        T, R = h.shape[0], self.tp.size
+        per = -(-T // R)
+        lo = min(T, self.tp.rank * per)
+        hi = min(T, lo + per)
+        mine = h[lo:hi].contiguous()
+        logits = (mine.float() @ W[p + "router"].float().t()).to(h.dtype)
+        ids, weights = ops.moe_topk(logits, c.top_k)
+        out = self.a2a(ops, mine[None], ids[None], weights[None], lambda e: W[p + f"e{e}.gate_up"],
+                       lambda e: W[p + f"e{e}.down"])[0]
+        full = torch.zeros(R * per, h.shape[1], dtype=h.dtype, device=h.device)
+        full[lo:hi] = out
+        return self.tp.all_reduce(full)[:T]  # disjoint slices: the sum is the gather, exactly
+
     def _moe(self, h: torch.Tensor, p: str) -> torch.Tensor:
         """Top-k softmax mixture over this rank's experts, combined over the ranks.
 
@@ -324,6 +359,8 @@ class DecoderLM:
         synchronisation, so the layer is captured in CUDA graphs; fixed orders, so results are
         deterministic.
         """
+        if self.a2a is not None:
+            return self._moe_routed(h, p)
         ops, c, W = self.ops, self.cfg, self.weights
         # the router's product is a few experts wide: a plain matmul, not a weight-streaming GEMM
         logits = (h.float() @ W[p + "router"].float().t()).to(h.dtype)

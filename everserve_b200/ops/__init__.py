@@ -33,11 +33,19 @@ class RefOps:
     def rmsnorm(self, x, w, eps, residual=None):
         return ref.rmsnorm(x, w, eps, residual)
 
-    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None):
-        return ref.linear(x, w, bias, residual, scale, pre)
+    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None, valid=None, valid_cap=0):
+        # rows a grouped GEMM would skip are padding nobody reads: computing them changes nothing
+        y = ref.linear(x, w, bias, residual, scale, pre)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
     def moe_route(self, logits, k, e0, el):
         return ref.moe_route(logits, k, e0, el)
+
+    def moe_topk(self, logits, k):
+        return ref.moe_topk(logits, k)
 
     def rope_kv_write(self, qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size):
         return ref.rope_kv_write(qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size)
@@ -115,7 +123,9 @@ class KernelOps:
         self.C.rmsnorm(x, residual, w, y, eps)
         return y
 
-    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None):
+    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None, valid=None, valid_cap=0):
+        """`valid` (int32 counts of segments of `valid_cap` rows) makes it a grouped GEMM whose
+        token tiles holding no counted row are skipped and left unwritten."""
         M, K = x.shape
         N = w.shape[0]
         if out is None:
@@ -125,11 +135,16 @@ class KernelOps:
             # bias folds into the residual input of the epilogue
             b = bias.expand(M, N) if residual is None else residual + bias
             residual = b.contiguous()
-        self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, self.num_sms, scale, pre)
+        self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, self.num_sms, scale, pre, valid,
+                         valid_cap)
         return out
 
     def moe_route(self, logits, k, e0, el):
         return self.C.moe_route(logits.contiguous(), k, e0, el)
+
+    def moe_topk(self, logits, k):
+        ids, w = self.C.moe_topk(logits.contiguous(), k)
+        return ids, w
 
     def rope_kv_write(self, qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size):
         T = qkv.shape[0]

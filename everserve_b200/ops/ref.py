@@ -160,6 +160,38 @@ def moe_route(logits: torch.Tensor, k: int, e0: int, el: int) -> torch.Tensor:
     return w[:, e0 : e0 + el].t().contiguous()
 
 
+def moe_topk(logits: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Each token's top k experts by softmax probability (ties to the lowest index), in rank
+    order, and their probabilities renormalised over the k: (int32 [T, k], fp32 [T, k])."""
+    p = torch.softmax(logits.float(), dim=-1)
+    ids = torch.argsort(-p, dim=-1, stable=True)[:, :k]
+    w = p.gather(1, ids)
+    return ids.to(torch.int32), w / w.sum(-1, keepdim=True)
+
+
+def expert_places(ids: torch.Tensor, num_experts: int) -> torch.Tensor:
+    """Where each (token, slot) row goes in its expert's segment from this sender: its rank among
+    the sender's rows for the same expert in (token, slot) order. int32 like `ids`."""
+    flat = ids.reshape(-1).long()
+    onehot = torch.nn.functional.one_hot(flat, num_experts)
+    before = onehot.cumsum(0) - onehot  # rows of each expert strictly before this one
+    return before.gather(1, flat[:, None]).reshape(ids.shape).to(torch.int32)
+
+
+def moe_a2a(xs: list[torch.Tensor], ids: list[torch.Tensor], weights: list[torch.Tensor], expert) -> list[torch.Tensor]:
+    """Oracle of the expert-parallel all-to-all: for each member's tokens x [T, H], the sum over
+    slots (in order, fp32) of weight * expert(e, x[t]); `expert(e, rows)` gives fp32 outputs."""
+    outs = []
+    for x, i, w in zip(xs, ids, weights):
+        acc = torch.zeros(x.shape, dtype=torch.float32, device=x.device)
+        for j in range(i.shape[1]):
+            for e in i[:, j].unique().tolist():
+                rows = (i[:, j] == e).nonzero().flatten()
+                acc[rows] += w[rows, j, None].float() * expert(int(e), x[rows]).float()
+        outs.append(acc.to(x.dtype))
+    return outs
+
+
 def argmax(logits: torch.Tensor) -> torch.Tensor:
     return torch.argmax(logits.float(), dim=-1)
 

@@ -115,6 +115,9 @@ class FusedTPCollective:
             self._open(self.members)
         self._write_order()
         self._counting = None
+        # objects on this group's members and control words (the routed experts' all-to-all) that
+        # follow its membership changes: set_members(rows), resume(), close()
+        self.attached: list = []
         if self.nvls:
             self.variant = "nvls"
         else:
@@ -246,6 +249,8 @@ class FusedTPCollective:
             self.rank = self.members.index(self.row)
         self._open(self.members)
         self._write_order()
+        for a in self.attached:
+            a.set_members(self.members)
 
     def abort(self) -> None:
         self.region.set_abort([self.row], 1)
@@ -261,6 +266,8 @@ class FusedTPCollective:
             else:
                 self.C.memset_async(self.own, int(self.C.comm_buffer_bytes()))
             torch.cuda.synchronize(self.device)
+        for a in self.attached:
+            a.resume()
         self.region.clear_late(self.row)
         self.region.set_u32(self.row, 16, 0)  # status
         self.region.set_abort([self.row], 0)
@@ -298,6 +305,9 @@ class FusedTPCollective:
         self.C = Counting()
 
     def close(self) -> None:
+        for a in self.attached:
+            a.close()
+        self.attached = []
         for m in self._opened.values():
             try:
                 m.close()

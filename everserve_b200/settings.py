@@ -27,6 +27,7 @@ Read where they are used (set by the node daemon for the processes it starts, or
 | ``ES_EXTENSION_PATH`` | a kernel extension to load instead of the in-tree build |
 | ``ES_PDL`` | ``0``: launch the decode kernels without programmatic dependent launch |
 | ``ES_AR_TWO_SHOT`` / ``ES_NVLS`` | the fused all-reduce's variant: two-shot, or NVLS multicast (``0`` off) |
+| ``ES_MOE_ROUTED`` | ``1``: mixture layers route tokens to their experts' owners (the peer-memory all-to-all) |
 
 Reference parity: adapters/vllm/everserve_vllm/settings.py:54-99 (same defaults: 3 steps, a 30 ms
 floor, 10 s to hung, a 2 ms poll).
