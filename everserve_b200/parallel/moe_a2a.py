@@ -88,7 +88,10 @@ class ExpertAllToAll:
         C = tp.C
         el = experts // len(tp.members)
         nbytes = int(C.moe_buffer_bytes(el, len(tp.members), cap, hidden))
-        path = lambda r: f"{tp.region.path}.r{r}.moe.fd"  # noqa: E731
+        # one descriptor socket per row and instance (every member attaches its instances in the
+        # same order, so the n-th names agree)
+        n = sum(isinstance(a, ExpertAllToAll) for a in getattr(tp, "attached", []))
+        path = lambda r: f"{tp.region.path}.r{r}.moe{n}.fd"  # noqa: E731
         with torch.cuda.device(tp.device):
             buf = SymmetricBuffer(C, nbytes, path(tp.row))
             C.memset_async(buf.ptr, buf.size)
