@@ -14,7 +14,9 @@ Reference parity: the reference's loader builds its extension with
 from __future__ import annotations
 
 import importlib
+import importlib.util
 import os
+import sys
 
 _C = None
 _ERR: Exception | None = None
@@ -28,11 +30,10 @@ def load():
     if _ERR is not None:
         raise RuntimeError(f"everserve_b200._C is not available: {_ERR}") from _ERR
     try:
+        import torch  # noqa: F401 - the extension links against torch's libraries, loaded by this import
+
         path = os.environ.get("ES_EXTENSION_PATH", "")
         if path:  # a build fetched from another node's compile cache
-            import importlib.util
-            import sys
-
             spec = importlib.util.spec_from_file_location("everserve_b200._C", path)
             mod = importlib.util.module_from_spec(spec)
             spec.loader.exec_module(mod)
