@@ -83,10 +83,11 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
 // ---- moe.cu (expert-parallel all-to-all over peer memory; layout in moe.cu) -----------------------
 struct MoeArgs {
   const uint64_t* peers;   // device [8]: each row's MoE buffer (0 = unmapped)
-  const int32_t* members;  // device [1 + 8]: member count W, then the row holding each position
+  const int32_t* members;  // device [1 + 8 + 1]: member count W, the row holding each position, then
+                           // the first position this process plays (-1: none, a spare before its take)
   uint32_t* call;          // device [2 * nz]: call counter and CTAs done, per emulated member
   void* ctrl;              // control words (comm Ctrl) of the first member; nz of them in a row
-  int pos;                 // this member's position (the first of the nz it plays)
+  int pos;                 // the host's view of the first position played (the kernels read the table's)
   int nz;                  // members this launch plays (1 with a GPU each)
   int E, el, k, H;         // experts, experts per member, experts per token, hidden size
   int64_t cap;             // rows of one (expert, sender) segment: at least a sender's token count

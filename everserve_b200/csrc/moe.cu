@@ -71,11 +71,13 @@ struct Member {
   comm::Ctrl* ctrl;
 };
 
+// The position comes from the device table (entry 1 + kMaxRows), so captured graphs follow a
+// spare's takeover; a process holding no position (a spare before its take) has row -1.
 ES_DEVICE Member member_of(const MoeArgs& a) {
   Member m;
-  m.pos = a.pos + (int)blockIdx.z;
+  m.pos = a.members[1 + comm::kMaxRows] + (int)blockIdx.z;
   m.W = a.members[0];
-  m.row = a.members[1 + m.pos];
+  m.row = (m.pos >= 0 && m.pos < m.W && m.W <= comm::kMaxRows) ? a.members[1 + m.pos] : -1;
   m.call = a.call + 2 * blockIdx.z;
   m.ctrl = reinterpret_cast<comm::Ctrl*>(a.ctrl) + blockIdx.z;
   return m;
@@ -117,6 +119,7 @@ __global__ void __launch_bounds__(kThreads) dispatch_kernel(const __nv_bfloat16*
   pdl_wait();  // the tokens and their routing come from the kernels before
   pdl_launch();
   const Member m = member_of(a);
+  if (m.row < 0) return;  // no position: nothing to send or receive
   const uint32_t seq = *reinterpret_cast<volatile uint32_t*>(m.call) + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t H = a.H;
@@ -207,6 +210,7 @@ __global__ void ready_kernel(MoeArgs a) {
   pdl_wait();  // the expert GEMMs that wrote y
   pdl_launch();
   const Member m = member_of(a);
+  if (m.row < 0) return;
   const uint32_t seq = *reinterpret_cast<volatile uint32_t*>(m.call) + 1;
   const int p = threadIdx.x;
   if (p >= m.W) return;
@@ -227,6 +231,7 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(const int32_t* __rest
   pdl_wait();
   pdl_launch();
   const Member m = member_of(a);
+  if (m.row < 0) return;  // uniform over the CTA: no barrier below is reached by only some threads
   const uint32_t seq = *reinterpret_cast<volatile uint32_t*>(m.call) + 1;
   const uint64_t own = a.peers[m.row];
   const int tid = threadIdx.x;
@@ -284,8 +289,8 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(const int32_t* __rest
 
 bool valid_args(const MoeArgs& a, int T) {
   return a.E > 0 && a.el > 0 && a.el <= kMaxLocal && a.E % a.el == 0 && a.k > 0 && a.k <= a.E && a.H > 0 &&
-         a.H % 8 == 0 && a.splits > 0 && a.splits <= kMaxSplits && a.nz > 0 && a.cap >= T && a.pos >= 0 &&
-         a.pos + a.nz <= comm::kMaxRows && a.E / a.el <= comm::kMaxRows && a.peers && a.members && a.call && a.ctrl;
+         a.H % 8 == 0 && a.splits > 0 && a.splits <= kMaxSplits && a.nz > 0 && a.cap >= T &&
+         a.nz <= comm::kMaxRows && a.E / a.el <= comm::kMaxRows && a.peers && a.members && a.call && a.ctrl;
 }
 
 }  // namespace moe

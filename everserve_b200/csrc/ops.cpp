@@ -208,16 +208,17 @@ torch::Tensor device_view(int64_t ptr, int64_t nbytes, int64_t device) {
                           torch::TensorOptions().dtype(at::kByte).device(at::kCUDA, (c10::DeviceIndex)device));
 }
 
-// The expert-parallel all-to-all's tables: peers int64[8] (buffer of each row), members int32[9]
-// (count, row of each position), call int32[2 * nz], ctrl (device address of nz control words).
+// The expert-parallel all-to-all's tables: peers int64[8] (buffer of each row), members int32[10]
+// (count, row of each position, this process's first position), call int32[2 * nz], ctrl (device
+// address of nz control words).
 es::MoeArgs moe_args(torch::Tensor peers, torch::Tensor members, torch::Tensor call, int64_t ctrl, int64_t pos,
                      int64_t nz, int64_t E, int64_t el, int64_t k, int64_t H, int64_t cap, int64_t splits) {
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong && peers.numel() >= 8, "peers: int64[8] on the device");
-  TORCH_CHECK(members.is_cuda() && members.scalar_type() == at::kInt && members.numel() >= 9,
-              "members: int32[9] on the device");
+  TORCH_CHECK(members.is_cuda() && members.scalar_type() == at::kInt && members.numel() >= 10,
+              "members: int32[10] on the device (count, rows of the positions, this process's position)");
   TORCH_CHECK(call.is_cuda() && call.scalar_type() == at::kInt && call.numel() >= 2 * nz,
               "call: int32[2 * nz] on the device");
-  TORCH_CHECK(ctrl != 0 && nz >= 1 && pos >= 0 && pos + nz <= 8, "control words, position and members played");
+  TORCH_CHECK(ctrl != 0 && nz >= 1 && nz <= 8 && pos + nz <= 8, "control words and members played");
   es::MoeArgs a{};
   a.peers = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
   a.members = members.data_ptr<int32_t>();

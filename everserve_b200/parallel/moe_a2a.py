@@ -39,7 +39,7 @@ CTRL_BYTES = 32  # one member's control words: abort, late, bound_ns, status, pa
 
 class ExpertAllToAll:
     def __init__(self, C, device, *, experts: int, top_k: int, hidden: int, cap: int, addrs: list[int],
-                 members: list[int], pos: int, nz: int, ctrl: int, splits: int | None = None):
+                 members: list[int], own_rows: list[int], pos: int, ctrl: int, splits: int | None = None):
         self.C = C
         self.device = torch.device(device)
         self.E, self.k, self.H, self.cap = int(experts), int(top_k), int(hidden), int(cap)
@@ -49,7 +49,8 @@ class ExpertAllToAll:
         if self.H % 8:
             raise ValueError("the hidden size must be a multiple of 8 (16-byte rows)")
         self.el = self.E // self.W
-        self.pos, self.nz = int(pos), int(nz)
+        self.own_rows = [int(r) for r in own_rows]  # the buffers this process owns, one per member played
+        self.pos, self.nz = int(pos), len(self.own_rows)
         self.members = [int(r) for r in members]
         self.splits = int(splits or max(1, min(32, 148 // max(1, self.E))))
         self.bytes = int(C.moe_buffer_bytes(self.el, self.W, self.cap, self.H))
@@ -57,6 +58,8 @@ class ExpertAllToAll:
         self.ctrl = int(ctrl)
         with torch.cuda.device(self.device):
             self.peers = torch.tensor(self._addrs, dtype=torch.int64, device=self.device)
+            # count, the row of each position, then the first position this process plays (the
+            # kernels read it here, so captured graphs follow a spare's take)
             self.members_t = torch.tensor(self._member_rows(), dtype=torch.int32, device=self.device)
             self.call = torch.zeros(2 * self.nz, dtype=torch.int32, device=self.device)
         self._views: dict[int, torch.Tensor] = {}
@@ -72,8 +75,8 @@ class ExpertAllToAll:
         bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=device) for _ in range(members)]
         ctrl = torch.zeros(members * CTRL_BYTES, dtype=torch.uint8, device=device)
         self = cls(C, device, experts=experts, top_k=top_k, hidden=hidden, cap=cap,
-                   addrs=[b.data_ptr() for b in bufs], members=list(range(members)), pos=0, nz=members,
-                   ctrl=ctrl.data_ptr(), splits=splits)
+                   addrs=[b.data_ptr() for b in bufs], members=list(range(members)),
+                   own_rows=list(range(members)), pos=0, ctrl=ctrl.data_ptr(), splits=splits)
         self._keep = (bufs, ctrl)
         return self
 
@@ -100,24 +103,26 @@ class ExpertAllToAll:
         addrs = [0] * MAX_ROWS
         addrs[tp.row] = buf.ptr
         opened = {}
+        member = tp.row in tp.members  # a spare holds no position until it takes one
         with torch.cuda.device(tp.device):
-            for r in tp.members:
+            for r in tp.members if member else ():
                 if r != tp.row:
                     opened[r] = PeerMapping(C, path(r))
                     addrs[r] = opened[r].ptr
         self = cls(C, tp.device, experts=experts, top_k=top_k, hidden=hidden, cap=cap, addrs=addrs,
-                   members=tp.members, pos=tp.members.index(tp.row), nz=1, ctrl=int(tp.ctrl), splits=splits)
+                   members=tp.members, own_rows=[tp.row], pos=tp.members.index(tp.row) if member else -1,
+                   ctrl=int(tp.ctrl), splits=splits)
         self._buf, self._opened, self._path, self._tp = buf, opened, path, tp
         if hasattr(tp, "attached"):
             tp.attached.append(self)  # membership changes and resumes of the group reach this too
         return self
 
     def _member_rows(self) -> list[int]:
-        return [self.W, *self.members] + [0] * (MAX_ROWS - self.W)
+        return [self.W, *self.members] + [0] * (MAX_ROWS - self.W) + [self.pos]
 
     # ---- views of a member's own buffer --------------------------------------------------------
     def _own(self, z: int) -> torch.Tensor:
-        row = self.members[self.pos + z]
+        row = self.own_rows[z]
         if row not in self._views:
             keep = getattr(self, "_keep", None)
             if keep is not None:
@@ -170,6 +175,8 @@ class ExpertAllToAll:
     def run_experts(self, ops, gate_up, down) -> None:
         """Each local expert of each member played over what it received: `gate_up(e)` [2I, H] and
         `down(e)` [H, I] give global expert e's weights."""
+        if self.pos < 0:
+            return  # no position: no experts
         for z in range(self.nz):
             for el in range(self.el):
                 e = (self.pos + z) * self.el + el
@@ -199,13 +206,14 @@ class ExpertAllToAll:
             raise RuntimeError("an emulated group has fixed members")
         if len(members) != self.W:
             raise ValueError("the group keeps its size; a spare takes a position")
-        me = self.members[self.pos]
+        me = self.own_rows[0]
         with torch.cuda.device(self.device):
             for r in members:
                 if r != me and r not in self._opened:
                     self._opened[r] = PeerMapping(self.C, self._path(r))
                     self._addrs[r] = self._opened[r].ptr
             self.members = [int(r) for r in members]
+            self.pos = self.members.index(me) if me in self.members else -1
             self.peers.copy_(torch.tensor(self._addrs, dtype=torch.int64))
             self.members_t.copy_(torch.tensor(self._member_rows(), dtype=torch.int32))
 
