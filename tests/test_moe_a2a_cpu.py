@@ -101,3 +101,43 @@ def test_routed_experts_need_the_kernels_and_a_peer_group(monkeypatch):
     assert EngineConfig(TINY_MIXTRAL, device="cpu").moe_routed
     monkeypatch.setenv("ES_MOE_ROUTED", "0")
     assert not EngineConfig(TINY_MIXTRAL, device="cpu").moe_routed
+
+
+class _OracleA2A:
+    """Stands in for the all-to-all on the CPU: the dense oracle over every expert's weights."""
+
+    def __init__(self, weights):
+        self.W = weights
+
+    def __call__(self, ops, x, ids, weights, gate_up, down):
+        def expert(e, rows):
+            return ops.linear(ops.silu_mul(ops.linear(rows, self.W[f"l0.e{e}.gate_up"])), self.W[f"l0.e{e}.down"])
+        return torch.stack(ref.moe_a2a(list(x), list(ids), list(weights), expert))
+
+
+class _Identity:
+    def all_reduce(self, t):
+        return t
+
+
+def test_routed_layer_slices_tokens_and_gathers_them_back():
+    """The model's routed path (token slices per rank, top-k, the all-to-all, the slices'
+    all-gather) equals its every-expert path, at TP 1 and at TP 2 played rank by rank."""
+    from everserve_b200.models.config import TINY_MIXTRAL
+    from everserve_b200.models.llama import DecoderLM, TPGroup
+
+    full = DecoderLM(TINY_MIXTRAL, "cpu", torch.float32)
+    g = torch.Generator().manual_seed(5)
+    for T in (1, 2, 7):
+        h = torch.randn(T, TINY_MIXTRAL.hidden, generator=g)
+        dense = full._moe(h, "l0.")
+        full.a2a = _OracleA2A(full.weights)
+        assert torch.allclose(full._moe(h, "l0."), dense, atol=1e-4)
+        full.a2a = None
+        # TP 2: each rank contributes its slice's rows; the all-gather is a sum of disjoint rows
+        parts = []
+        for r in range(2):
+            m = DecoderLM(TINY_MIXTRAL, "cpu", torch.float32, tp=TPGroup(r, 2, _Identity()))
+            m.a2a = _OracleA2A(full.weights)
+            parts.append(m._moe(h, "l0."))
+        assert torch.allclose(parts[0] + parts[1], dense, atol=1e-4)
