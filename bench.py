@@ -107,12 +107,114 @@ def reference_arm(args) -> None:
         print(json.dumps({"impl": "reference", "unavailable": why}))
 
 
+def stock_arm(args) -> None:
+    """The stock arm: vLLM (the engine the reference plugs into, unmodified, with none of this
+    framework's code) serving the same architecture with dummy random weights, the same 64
+    streams of uniform-random 1024-token prompts and greedy decoding, TP over the same GPUs
+    (``external_launcher``: one vLLM engine per torchrun rank, in this process). Decode tok/s is
+    counted through vLLM's public engine API (``LLMEngine.step``): output tokens gained over K
+    steps after W warm-up steps, wall clock between device synchronisations, max over ranks."""
+    import tempfile
+
+    os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")  # engine core in this process
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    _watchdog(args.deadline, rank)
+    import torch
+
+    torch.cuda.set_device(local)
+    from transformers import LlamaConfig
+
+    model_dir = tempfile.mkdtemp(prefix="es-stock-")
+    LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=500000.0,
+                max_position_embeddings=8192, rms_norm_eps=1e-5, tie_word_embeddings=False,
+                torch_dtype="bfloat16", architectures=["LlamaForCausalLM"]).save_pretrained(model_dir)
+    from vllm import LLM
+    from vllm import SamplingParams as VSP
+    from vllm.inputs import TokensPrompt
+
+    kw = dict(model=model_dir, load_format="dummy", skip_tokenizer_init=True, tensor_parallel_size=world,
+              dtype="bfloat16", max_num_seqs=args.batch, max_model_len=args.prompt_len + args.max_tokens + 16,
+              gpu_memory_utilization=0.85, seed=args.seed, enable_prefix_caching=False)
+    if world > 1:
+        kw["distributed_executor_backend"] = "external_launcher"
+    llm = LLM(**kw)
+    eng = llm.llm_engine
+    g = torch.Generator().manual_seed(args.seed)
+    prompts = torch.randint(0, 128256, (args.batch, args.prompt_len), generator=g).tolist()
+    sp = VSP(max_tokens=args.max_tokens, temperature=0.0, ignore_eos=True, detokenize=False)
+    for i, p in enumerate(prompts):
+        eng.add_request(f"s{i}", TokensPrompt(prompt_token_ids=p), sp)
+    got: dict[str, int] = {}
+
+    def step() -> None:
+        for o in eng.step():
+            got[o.request_id] = len(o.outputs[0].token_ids)
+
+    t_pf = time.perf_counter()
+    while len(got) < args.batch or min(got.values()) < 1:
+        step()
+    print(f"[bench stock] prefill of {args.batch}x{args.prompt_len} tokens: {time.perf_counter() - t_pf:.2f} s",
+          file=sys.stderr)
+    for _ in range(args.warmup):
+        step()
+    import torch.distributed as dist
+
+    def sync():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    sync()
+    before = sum(got.values())
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    gained = sum(got.values()) - before
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([dt], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    value = gained / dt
+    out = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 4), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": 1.0, "dtype": "bf16",
+           "data": "synthetic: uniform-random 1024-token prompts (seed 0), vLLM dummy random weights",
+           "config": {"model": "Llama-3-8B architecture (32 layers, hidden 4096, 32/8 heads, d 128, ffn 14336, "
+                               "vocab 128256)", "global_batch": args.batch, "seq_len": args.prompt_len,
+                      "parallelism": f"tp{world}", "engine": f"vLLM {_vllm_version()} (stock, CUDA graphs)",
+                      "timing": "wall clock over K LLMEngine.step() calls, output tokens gained"},
+           "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": None,
+                   "d2h_bytes_per_step": None},
+           "gpu_launches": None, "clocks": clk, "impl": "stock"}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    os._exit(0)  # vLLM's engine and its process group are torn down by the exit
+
+
+def _vllm_version() -> str:
+    try:
+        import vllm
+
+        return vllm.__version__
+    except Exception:  # noqa: BLE001
+        return "?"
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "stock"])
     ap.add_argument("--model", default="llama-3-8b")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--prompt-len", type=int, default=1024)
@@ -124,6 +226,9 @@ def main() -> None:
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.impl == "stock":
+        stock_arm(args)
         return
     assert args.warmup >= 3, "at least 3 warm-up steps"
     assert 4 + args.warmup + 2 * args.steps <= args.max_tokens, "steps exceed the 512-token generation"

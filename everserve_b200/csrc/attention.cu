@@ -270,12 +270,11 @@ __global__ void decode_merge_kernel(const float* __restrict__ part_o, const floa
 template <int D, int BS, int S>
 cudaError_t launch_decode(const CUtensorMap& map, const DecodeParams& p, int B, cudaStream_t stream) {
   using C = DecodeCfg<D, BS, S>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<D, BS, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(decode_kernel<D, BS, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  });
+  if (e != cudaSuccess) return e;
   dim3 grid(B, p.hkv, p.max_splits);
   return launch_ex(decode_kernel<D, BS, S>, grid, dim3(kThreads), C::kSmem, stream, 0, map, p);
 }

@@ -1,7 +1,9 @@
 // Peer-memory collectives of a tensor-parallel group over NVLink (one process per GPU).
 //
-// Every member owns one symmetric buffer in its device memory, exported by CUDA IPC and mapped by
-// the others:
+// Every member owns one symmetric buffer in its device memory: a driver VMM allocation whose
+// descriptor is passed to the other members over a Unix socket, each of which maps it for its own
+// device (vmm.cpp). Its memory lives until every mapping is released, so a member that dies leaves
+// it valid under the survivors' bounded waits. Layout:
 //   flags: uint32 [2 parity][kMaxRows sender][kFlagSlots]
 //   data : bytes  [2 parity][kMaxRows sender][kDataBytes]
 // A call pushes this member's contribution into every member's buffer at its own sender row

@@ -30,6 +30,10 @@
  * [batch, *] int32 (rows of bt_stride), ctx_lens [batch] int32, out [batch, q_heads * head_dim]
  * bf16 (rows of out_stride). Positions are split into runs of 256 (the regular default), so the
  * result matches the regular entry point's bit for bit when that one uses the same split length.
+ *
+ * Limits of the inputs: every ctx_lens[b] must be at most max_model_len (the scratch and the grid
+ * are sized from max_model_len, so positions past it would be left out of the result), and each
+ * row of block_tables must hold at least ceil(ctx_lens[b] / block_size) valid block indices.
  */
 #ifndef ES_NOALLOC_H_
 #define ES_NOALLOC_H_

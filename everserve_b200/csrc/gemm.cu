@@ -382,15 +382,14 @@ template <int BN, int CPS = (BN <= 64 ? 2 : 1), bool kAR = false>
 cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, dim3 grid, cudaStream_t stream,
                    const comm::View& cv = comm::View{}) {
   using C = Cfg<BN, CPS>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e =
+  static std::atomic<uint64_t> configured{0};
+  cudaError_t e = once_per_device(configured, [] {
+    cudaError_t r =
         cudaFuncSetAttribute(gemm_kernel<BN, CPS, kAR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(gemm_kernel<BN, CPS, kAR>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+    if (r != cudaSuccess) return r;
+    return cudaFuncSetAttribute(gemm_kernel<BN, CPS, kAR>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  });
+  if (e != cudaSuccess) return e;
   return launch_ex(gemm_kernel<BN, CPS, kAR>, grid, dim3(kThreads), C::kSmem, stream, p.splits, mw, mx, p, cv);
 }
 

@@ -7,6 +7,8 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdint>
 #include <cstdlib>
 #include <utility>
 
@@ -18,6 +20,21 @@ inline bool pdl_enabled() {
     return !(v && v[0] == '0');
   }();
   return on;
+}
+
+// Kernel attributes (shared-memory size, cluster permissions) are set per device: `done` keeps one
+// bit per device index, and `set_up` runs on the current device until it has succeeded there.
+// Two threads may both run it for one device; setting an attribute twice is harmless.
+template <typename F>
+cudaError_t once_per_device(std::atomic<uint64_t>& done, F&& set_up) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t(1) << dev) : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+  e = set_up();
+  if (e == cudaSuccess && bit != 0) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
 }
 
 template <typename... KArgs, typename... Args>

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import os
 import socket
+import time
 import threading
 
 
@@ -69,13 +70,22 @@ class PeerMapping:
 
     def __init__(self, C, sock_path: str, timeout_s: float = 30.0):
         self.C = C
-        s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
-        s.settimeout(timeout_s)
-        try:
-            s.connect(sock_path)
-            msg, fds, _, _ = socket.recv_fds(s, 8, 1)
-        finally:
-            s.close()
+        # the peer may still be creating its buffer (loading weights, say): its socket appears
+        # when it is ready, so a missing or refusing socket is retried until the timeout
+        deadline = time.monotonic() + timeout_s
+        while True:
+            s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+            s.settimeout(timeout_s)
+            try:
+                s.connect(sock_path)
+                msg, fds, _, _ = socket.recv_fds(s, 8, 1)
+                break
+            except (FileNotFoundError, ConnectionRefusedError):
+                if time.monotonic() > deadline:
+                    raise
+                time.sleep(0.01)
+            finally:
+                s.close()
         if not fds or len(msg) != 8:
             raise RuntimeError(f"no buffer descriptor from {sock_path}")
         size = int.from_bytes(msg, "little")

@@ -181,19 +181,27 @@ def member_sets(world: int, losses: Sequence[Sequence[int]] | None = None,
 
 
 def sets_to_preform(policy: Policy, engine: Engine, spare_ranks: Sequence[int] = ()) -> list[tuple[Member, ...]]:
+    """The member sets an engine forms groups for before any loss, in one order every process
+    derives alike: the survivor sets of each single loss when the policy can shrink, then, when it
+    can replace, the set in which each standing spare holds its rank. Spares the policy could never
+    use, or for ranks the engine does not have, are a configuration error."""
     world = engine.world_size
-    out: list[tuple[Member, ...]] = []
-    if Outcome.SHRINK in policy.outcomes_in_order:
-        out.extend(member_sets(world))
-    spares = sorted(set(spare_ranks))
-    if spares and Outcome.REPLACE not in policy.outcomes_in_order:
-        raise ValueError(f"spares for ranks {spares} under a policy without REPLACE")
-    bad = [r for r in spares if not 0 <= r < world]
-    if bad:
-        raise ValueError(f"spare ranks {bad} outside the engine's world of {world}")
-    for r in spares:
-        out.extend(member_sets(world, replacements=[(r,)]))
-    return out
+    standing = sorted({int(r) for r in spare_ranks})
+    enabled = set(policy.outcomes_in_order)
+    errors = []
+    if standing and Outcome.REPLACE not in enabled:
+        errors.append(f"standing spares {standing} would never be used: the policy has no REPLACE outcome")
+    stray = [r for r in standing if r < 0 or r >= world]
+    if stray:
+        errors.append(f"standing spares name ranks {stray}, but the engine has ranks 0..{world - 1}")
+    if errors:
+        raise ValueError("; ".join(errors))
+    planned: list[tuple[Member, ...]] = []
+    if Outcome.SHRINK in enabled:
+        planned += member_sets(world)
+    if Outcome.REPLACE in enabled and standing:
+        planned += member_sets(world, replacements=[(r,) for r in standing])
+    return planned
 
 
 def loss_sets(world: int, max_losses: int) -> list[tuple[int, ...]]:

@@ -22,7 +22,8 @@ def main(argv=None) -> int:
     from ..engine.config import EngineConfig
     from ..engine.engine import Engine
     from .api import EngineLoop, build_app
-    from .executor import MultiprocExecutor, failover
+    from ..plugin import register
+    from .executor import MultiprocExecutor
 
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--engine", required=True)
@@ -51,7 +52,7 @@ def main(argv=None) -> int:
     ex = MultiprocExecutor(cfg, engine=a.engine, daemon=a.daemon, store=a.store, spares=spares, node=a.node,
                            device="cuda" if gpu else "cpu", dtype="bfloat16" if gpu else "float32", local_ranks=local)
     eng = Engine(cfg, executor=ex)
-    eng.wrap_step(failover(ex, eng))
+    register(eng)  # the failover step hook for the multi-process executor
     loop = EngineLoop(eng)
     try:
         uvicorn.run(build_app(loop, cfg.model.name, cfg.model.vocab), host=a.host, port=a.port, log_level="warning")
