@@ -221,6 +221,9 @@ def main() -> None:
     ap.add_argument("--max-tokens", type=int, default=512)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--collective", default="fused", choices=["fused", "nccl"])
+    ap.add_argument("--commit", default="store", choices=["store", "off"],
+                    help="store: every step's KV rows and counts are committed to everserve-store (the "
+                         "serving configuration); off: no commit (for comparison)")
     ap.add_argument("--deadline", type=float, default=300.0,
                     help="seconds after which a run that has not finished reports a failure and exits")
     args = ap.parse_args()
@@ -256,11 +259,19 @@ def main() -> None:
 
         collective = make_tp_collective(dev, kind=args.collective)
 
-    cfg = EngineConfig(args.model, device=str(dev), max_batch=args.batch,
-                       max_model_len=args.prompt_len + args.max_tokens + 16, max_prefill_tokens=8192,
-                       tensor_parallel=world, seed=args.seed)
+    max_len = args.prompt_len + args.max_tokens + 16
+    block_size = 16
+    num_blocks = args.batch * (-(-max_len // block_size)) + 64
+    cfg = EngineConfig(args.model, device=str(dev), max_batch=args.batch, max_model_len=max_len,
+                       max_prefill_tokens=8192, tensor_parallel=world, seed=args.seed, num_blocks=num_blocks,
+                       block_size=block_size)
     ex = LocalExecutor(cfg, rank=rank, collective=collective)
-    eng = Engine(cfg, executor=ex)
+    connector = None
+    store = None
+    if args.commit == "store":
+        store, connector = _store_connector(ex, rank, local, num_blocks * block_size, block_size,
+                                            os.environ.get("MASTER_PORT", "0"), world)
+    eng = Engine(cfg, executor=ex, connector=connector)
     g = torch.Generator().manual_seed(args.seed)
     vocab = cfg.model.vocab
     prompts = torch.randint(0, vocab, (args.batch, args.prompt_len), generator=g).tolist()
@@ -302,6 +313,8 @@ def main() -> None:
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     eng.decode_steps(args.steps)
+    if connector is not None:
+        connector.ckv.join_stream()  # the timed region covers every step's KV gather
     end.record()
     torch.cuda.synchronize()
     barrier()
@@ -313,6 +326,8 @@ def main() -> None:
     t0 = time.perf_counter()
     for _ in range(args.steps):
         eng.step()
+    if connector is not None:
+        connector.drain()  # every commit of the region acknowledged by the store
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
@@ -344,6 +359,7 @@ def main() -> None:
                    "l2": "inputs larger than L2 (16 GB of weights / TP and the KV history read every step)"},
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": runner.h2d_bytes,
                 "d2h_bytes_per_step": args.batch * 8},
+        "commit": _commit_summary(connector, args),
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk,
         "impl": "ours",
@@ -356,10 +372,56 @@ def main() -> None:
     if world > 1:
         dist.barrier(device_ids=[local])
     eng.shutdown()
+    if connector is not None:
+        connector.close()
+    if store is not None:
+        store.terminate()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def _store_connector(ex, rank: int, local: int, slots: int, block_size: int, tag: str, world: int):
+    """Start the node's everserve-store (the first process of the node) and give this rank a KV
+    connector committing to it, as a serving rank does."""
+    import shutil
+
+    from everserve_b200.state.connector import StoreConnector
+    from everserve_b200.state.kvcopy import PagedKV
+    from everserve_b200.state.mirror import MirrorClient, MirrorCommittedKV
+
+    base = "/dev/shm" if shutil.disk_usage("/dev/shm").free > (64 << 30) else "/tmp"
+    root = os.path.join(base, f"es-bench-{tag}")
+    sock = os.path.join(root, "store.sock")
+    proc = None
+    if local == 0:
+        shutil.rmtree(root, ignore_errors=True)
+        os.makedirs(os.path.join(root, "data"), exist_ok=True)
+        binary = os.path.join(HERE, "cpp", "bin", "everserve-store")
+        if not os.path.exists(binary):
+            subprocess.run(["make", "-C", os.path.join(HERE, "cpp"), f"-j{os.cpu_count() or 8}"], check=True,
+                           stdout=subprocess.DEVNULL)
+        proc = subprocess.Popen([binary, "--socket", f"unix:{sock}", "--data-dir", os.path.join(root, "data"),
+                                 "--slots", str(slots), "--budget-bytes", str(256 << 30)],
+                                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+    t0 = time.monotonic()
+    while not os.path.exists(sock):
+        if time.monotonic() - t0 > 60:
+            raise RuntimeError(f"everserve-store did not come up at {sock}")
+        time.sleep(0.05)
+    w = ex.worker
+    kv = PagedKV("heads_blocked", w.num_blocks, block_size, w.model.hkv, w.model.d)
+    ckv = MirrorCommittedKV(MirrorClient(f"unix:{sock}"), "bench", rank, w.runner.caches, kv, store_slots=slots)
+    return proc, StoreConnector(ckv, block_size)
+
+
+def _commit_summary(connector, args) -> dict:
+    if connector is None:
+        return {"mode": "off"}
+    st = connector.ckv.stats()
+    return {"mode": "everserve-store, every step (gather on a side stream, fence 2 steps back)",
+            "commits": connector.commits, "bytes": st.get("bytes", 0), "fence_waits": st.get("fence_waits", 0)}
 
 
 def _fail(rank: int, why: str, code: int) -> None:

@@ -60,12 +60,40 @@ static bool g_crc_init = [] {
   return true;
 }();
 
-uint32_t crc32c(const void* data, size_t n, uint32_t crc) {
+static uint32_t crc32c_table(const uint8_t* p, size_t n, uint32_t crc) {
   (void)g_crc_init;
-  const auto* p = static_cast<const uint8_t*>(data);
-  crc = ~crc;
   for (size_t i = 0; i < n; i++) crc = g_crc_table[(crc ^ p[i]) & 0xFF] ^ (crc >> 8);
-  return ~crc;
+  return crc;
+}
+
+#if defined(__x86_64__)
+// The same polynomial through the SSE4.2 crc32 instruction, eight bytes at a time (about an order
+// of magnitude faster than the table: the store checksums every row it is sent).
+__attribute__((target("sse4.2"))) static uint32_t crc32c_hw(const uint8_t* p, size_t n, uint32_t crc) {
+  uint64_t c = crc;
+  while (n >= 8) {
+    uint64_t v;
+    memcpy(&v, p, 8);
+    c = __builtin_ia32_crc32di(c, v);
+    p += 8;
+    n -= 8;
+  }
+  uint32_t c32 = (uint32_t)c;
+  while (n > 0) {
+    c32 = __builtin_ia32_crc32qi(c32, *p++);
+    n--;
+  }
+  return c32;
+}
+static const bool g_crc_hw = __builtin_cpu_supports("sse4.2");
+#endif
+
+uint32_t crc32c(const void* data, size_t n, uint32_t crc) {
+  const auto* p = static_cast<const uint8_t*>(data);
+#if defined(__x86_64__)
+  if (g_crc_hw) return ~crc32c_hw(p, n, ~crc);
+#endif
+  return ~crc32c_table(p, n, ~crc);
 }
 
 // ---- JSON ----------------------------------------------------------------------------------------

@@ -2,9 +2,87 @@
 
 #include <unistd.h>
 
+#include <algorithm>
+#include <atomic>
+#include <condition_variable>
 #include <cstring>
+#include <functional>
+#include <mutex>
+#include <thread>
 
 namespace es {
+
+// A fixed pool of commit workers (at most 8, one less than the cores). `parallel_for(n, fn)` runs
+// fn(0..n-1) over the pool and the calling thread and returns when every call has finished; calls
+// are serialised (the store's loop makes one at a time).
+namespace {
+class CommitPool {
+ public:
+  CommitPool() {
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const unsigned n = std::min(8u, hw > 1 ? hw - 1 : 0u);
+    for (unsigned i = 0; i < n; i++) threads_.emplace_back([this] { loop(); });
+  }
+  ~CommitPool() {
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : threads_) t.join();
+  }
+  void run(size_t n, const std::function<void(size_t)>& fn) {
+    if (threads_.empty() || n < 2) {
+      for (size_t i = 0; i < n; i++) fn(i);
+      return;
+    }
+    std::unique_lock<std::mutex> g(mu_);
+    fn_ = &fn;
+    n_ = n;
+    next_.store(0);
+    busy_ = threads_.size();
+    gen_++;
+    g.unlock();
+    cv_.notify_all();
+    work();
+    g.lock();
+    done_cv_.wait(g, [this] { return busy_ == 0; });
+    fn_ = nullptr;
+  }
+
+ private:
+  void work() {
+    for (size_t i = next_.fetch_add(1); i < n_; i = next_.fetch_add(1)) (*fn_)(i);
+  }
+  void loop() {
+    uint64_t seen = 0;
+    std::unique_lock<std::mutex> g(mu_);
+    while (true) {
+      cv_.wait(g, [&] { return stop_ || gen_ != seen; });
+      if (stop_) return;
+      seen = gen_;
+      g.unlock();
+      work();
+      g.lock();
+      if (--busy_ == 0) done_cv_.notify_all();
+    }
+  }
+  std::vector<std::thread> threads_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_cv_;
+  const std::function<void(size_t)>* fn_ = nullptr;
+  size_t n_ = 0;
+  std::atomic<size_t> next_{0};
+  size_t busy_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
+
+void parallel_for(size_t n, const std::function<void(size_t)>& fn) {
+  static CommitPool pool;
+  pool.run(n, fn);
+}
+}  // namespace
 
 size_t dtype_bytes(const std::string& d) {
   if (d == "float8_e4m3fn" || d == "float8_e5m2" || d == "int8" || d == "uint8") return 1;
@@ -151,7 +229,10 @@ bool Storage::commit(const mirror::Commit& c, std::string& err) {
       }
     }
     const uint64_t stamp = c.step == 0 ? 1 : c.step;
-    for (auto& [t, off] : plan) {
+    // tables are independent: their copies and checksums run on the commit workers
+    parallel_for(plan.size(), [&](size_t pi) {
+      Table* t = plan[pi].first;
+      const uint64_t off = plan[pi].second;
       char* rows = static_cast<char*>(t->rows->addr);
       for (size_t i = 0; i < b.slots.size();) {
         const int64_t s0 = b.slots[i];
@@ -170,7 +251,7 @@ bool Storage::commit(const mirror::Commit& c, std::string& err) {
         }
         i += n;
       }
-    }
+    });
   }
   r.epoch = c.epoch;
   r.step = c.step;

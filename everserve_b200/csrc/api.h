@@ -125,6 +125,25 @@ struct DecodeArgs {
 };
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t s);
 
+// ---- prefill.cu ----------------------------------------------------------------------------------
+struct PrefillArgs {
+  const void* q;        // [T, Hq, D] rows of q_stride (= Hq * D) elements
+  int64_t q_stride;
+  const void* cache;    // [nb, 2, Hkv, bs, D] contiguous
+  int64_t num_blocks;
+  const int* block_tables;
+  int64_t bt_stride;
+  const int* tiles;     // [n_tiles, 4] int32: sequence, first row, rows (<= 128), first position
+  int n_tiles;
+  void* out;            // [T, Hq * D] rows of out_stride
+  int64_t out_stride;
+  int* status;
+  int64_t T;
+  int hq, hkv, d, block_size;
+  float scale;
+};
+cudaError_t launch_paged_prefill(const PrefillArgs& a, cudaStream_t s);
+
 // ---- kvcopy.cu -----------------------------------------------------------------------------------
 struct KvCopyArgs {
   const int64_t* layer_ptrs;  // device array of per-layer cache addresses

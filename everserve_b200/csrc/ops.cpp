@@ -384,6 +384,41 @@ void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tabl
   ES_CHECK_CUDA(es::launch_paged_decode(a, cur()));
 }
 
+void paged_prefill(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor tiles,
+                   torch::Tensor out, torch::Tensor status, double scale) {
+  check_bf16(q, "q");
+  check_bf16(cache, "cache");
+  check_bf16(out, "out");
+  TORCH_CHECK(cache.dim() == 5 && cache.is_contiguous(), "cache must be contiguous [nb, 2, Hkv, bs, D]");
+  TORCH_CHECK(q.dim() == 3 && q.is_contiguous() && q.size(2) == cache.size(4), "q must be contiguous [T, Hq, D]");
+  TORCH_CHECK(out.sizes() == q.sizes() && out.is_contiguous(), "out must be [T, Hq, D] like q");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2, "int32 block tables");
+  TORCH_CHECK(tiles.scalar_type() == at::kInt && tiles.dim() == 2 && tiles.size(1) == 4 && tiles.is_contiguous() &&
+                  reinterpret_cast<uintptr_t>(tiles.data_ptr()) % 16 == 0,
+              "tiles must be a contiguous, 16-byte aligned int32 [n, 4]");
+  TORCH_CHECK(status.scalar_type() == at::kInt, "int32 status word");
+  es::PrefillArgs a{};
+  a.q = q.data_ptr();
+  a.q_stride = q.stride(0);
+  a.cache = cache.data_ptr();
+  a.num_blocks = cache.size(0);
+  a.block_tables = block_tables.data_ptr<int>();
+  a.bt_stride = block_tables.stride(0);
+  a.tiles = tiles.data_ptr<int>();
+  a.n_tiles = (int)tiles.size(0);
+  a.out = out.data_ptr();
+  a.out_stride = out.stride(0);
+  a.status = status.data_ptr<int>();
+  a.T = q.size(0);
+  a.hq = (int)q.size(1);
+  a.hkv = (int)cache.size(2);
+  a.d = (int)cache.size(4);
+  a.block_size = (int)cache.size(3);
+  a.scale = (float)scale;
+  const c10::cuda::CUDAGuard g(q.device());
+  ES_CHECK_CUDA(es::launch_paged_prefill(a, cur()));
+}
+
 void kv_copy(bool gather, torch::Tensor layer_ptrs, torch::Tensor slots, torch::Tensor heads, int64_t staging_ptr,
              int64_t cap, int64_t d, int64_t block_size, std::vector<int64_t> strides, int64_t elem) {
   TORCH_CHECK(layer_ptrs.is_cuda() && slots.is_cuda() && heads.is_cuda(), "device index tensors");
@@ -502,6 +537,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ws_floats", &es::gemm_ws_floats);
   m.def("gemm_sync_words", &es::gemm_sync_words);
   m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
+  m.def("paged_prefill", &paged_prefill, "paged causal prefill attention (tcgen05: S and P.V in TMEM, TMA K/V tiles)");
   m.def("moe_route", &moe_route, "mixture routing: per-token weights of this rank's experts [el, T]");
   m.def("moe_topk", &moe_topk, "mixture routing: each token's top k experts and their weights");
   m.def("moe_dispatch", &moe_dispatch, "expert-parallel dispatch of tokens to their experts' owners (peer stores)");

@@ -198,6 +198,35 @@ ES_DEVICE uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand (the MN dimension contiguous) written
+// by TMA with 128-byte swizzle: 64-element MN chunks of 8 K-rows x 128 bytes (one swizzle atom per
+// 8 K-rows), `mn_chunk_bytes` between consecutive 64-element MN chunks (leading byte offset) and
+// 1024 bytes between consecutive 8-row K groups (stride byte offset). Base 1024-byte aligned.
+ES_DEVICE uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint32_t mn_chunk_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((mn_chunk_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Named barrier over `count` threads that also ORs a predicate across them: every thread gets
+// true when any thread passed true (so a group of warps can leave a loop together).
+ES_DEVICE bool named_bar_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 // Instruction descriptor of tcgen05.mma kind::f16: bf16 A and B, both K-major, fp32 D, M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
   return (1u << 4)                       // D format: f32
@@ -206,6 +235,8 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
          | ((uint32_t)(n >> 3) << 17)    // N / 8
          | ((uint32_t)(m >> 4) << 24);   // M / 16
 }
+// The same with B MN-major (bit 16: B transposed), e.g. V [keys, d] as the B operand of P.V.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int m, int n) { return idesc_bf16_f32(m, n) | (1u << 16); }
 
 }  // namespace ptx
 }  // namespace es

@@ -47,8 +47,8 @@ class LocalExecutor:
     def logprobs(self, n: int) -> list | None:
         return self.worker.runner.logprob_rows(n)
 
-    def decode_loop(self, plan: StepPlan, k: int):
-        return self.worker.runner.decode_loop(plan, k)
+    def decode_loop(self, plan: StepPlan, k: int, after_step=None):
+        return self.worker.runner.decode_loop(plan, k, after_step)
 
     def shutdown(self):
         """Release the graphs, then the collective's peer mappings and buffers."""
@@ -132,7 +132,10 @@ class Engine:
             assert sr.sample and len(req.outputs) + k <= req.params.max_tokens
             self.blocks.grow(req.blocks, req.num_computed + k)
             sr.block_table = list(req.blocks)
-        ids = self.executor.decode_loop(plan, k)
+        hook = None
+        if self.connector is not None and hasattr(self.connector, "decode_hook"):
+            hook = self.connector.decode_hook(plan, k)  # every device step's rows are committed
+        ids = self.executor.decode_loop(plan, k, hook) if hook is not None else self.executor.decode_loop(plan, k)
         rows = self.executor.fetch(ids)
         n = len(plan.reqs)
         toks = [rows[i * n : (i + 1) * n] for i in range(k)]

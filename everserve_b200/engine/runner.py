@@ -19,6 +19,7 @@ from __future__ import annotations
 import torch
 
 from ..models.llama import DecoderLM, StepInput
+from ..ops import prefill_tiles
 from .sampling import SamplingBatch
 from .scheduler import StepPlan
 
@@ -170,9 +171,10 @@ class ModelRunner:
             ps = [r.sampling or (0.0, 0, 1.0, 0) for r in plan.reqs]
             sb = SamplingBatch(temperature=t([p[0] for p in ps], torch.float32), top_k=t([p[1] for p in ps]),
                                top_p=t([p[2] for p in ps], torch.float32), seed=t([p[3] for p in ps]))
+        tiles = prefill_tiles(seq, pos, device=dev) if self.model.ops.kind == "kernel" else None
         return StepInput(ids=t(ids), positions=t(pos), slots=t(slots), block_tables=bt.to(dev),
                          ctx_lens=t(ctx, torch.int32), q_seq=t(seq), logits_idx=t(last), is_decode=False,
-                         max_model_len=self.max_model_len, sampling=sb)
+                         max_model_len=self.max_model_len, sampling=sb, prefill_tiles=tiles)
 
     # ---- forward ---------------------------------------------------------------------------------
     def forward(self, inp: StepInput, hidden=None, residual=None):
@@ -249,10 +251,12 @@ class ModelRunner:
                 self._capture(b)
 
     # ---- multi-step decode -----------------------------------------------------------------------
-    def decode_loop(self, plan: StepPlan, k: int) -> torch.Tensor:
+    def decode_loop(self, plan: StepPlan, k: int, after_step=None) -> torch.Tensor:
         """k decode steps from `plan` without host round trips; returns device ids [k, n].
 
         Every request's block table must already cover positions start_pos .. start_pos + k - 1.
+        ``after_step(i)`` is called on the host once step i's kernels are enqueued (the KV
+        connector enqueues that step's commit behind them).
         """
         n = len(plan.reqs)
         b = self.stage_decode(plan)
@@ -268,6 +272,8 @@ class ModelRunner:
             else:
                 ids = self.forward(self._decode_input(*key))
             out[i] = ids[:n]
+            if after_step is not None:
+                after_step(i)
             if i + 1 < k:
                 self._advance(b, ids, bs)
         return out

@@ -40,6 +40,7 @@ class StepInput:
     max_model_len: int = 0
     sampling: object | None = None  # engine.sampling.SamplingBatch of the rows; None: greedy
     logprobs_k: int | None = None  # the step also reports log-probabilities (k alternatives)
+    prefill_tiles: torch.Tensor | None = None  # prefill kernel work list (ops.prefill_tiles), device
 
 
 def _seed_of(seed: int, *parts) -> int:
@@ -233,7 +234,7 @@ class DecoderLM:
                     a = ops.decode_attention(q, cache, inp.block_tables, inp.ctx_lens, self.scale)
             else:
                 a = ops.prefill_attention(q, cache, inp.block_tables, inp.ctx_lens, inp.q_seq, inp.positions,
-                                          self.scale)
+                                          self.scale, inp.prefill_tiles)
             a = a.reshape(a.shape[0], self.hq * self.d)
             o = self.tp.linear_allreduce(ops, a, W[p + "o"])
             h = ops.rmsnorm(o, W[p + "post_norm"], c.rms_eps, residual)

@@ -16,7 +16,7 @@ import torch
 from . import ref
 from .. import _ext
 
-__all__ = ["KernelOps", "RefOps", "ops_for", "ref"]
+__all__ = ["KernelOps", "RefOps", "ops_for", "prefill_tiles", "ref"]
 
 
 class RefOps:
@@ -55,7 +55,7 @@ class RefOps:
         seq = torch.arange(B, device=q.device)
         return ref.paged_attention(q, cache, block_tables, ctx_lens, seq, ctx_lens.long() - 1, scale)
 
-    def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale):
+    def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale, tiles=None):
         return ref.paged_attention(q, cache, block_tables, ctx_lens, q_seq, q_pos, scale)
 
     def silu_mul(self, gu):
@@ -166,9 +166,17 @@ class KernelOps:
                             ms, self.PART_TOKENS, scale, self.ATTN_STAGES)
         return out
 
-    def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale):
-        # prefill runs once per request and is outside the decode loop; reference math on device
-        return ref.paged_attention(q, cache, block_tables, ctx_lens, q_seq, q_pos, scale)
+    def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale, tiles=None):
+        """Causal attention of the step's new rows over their sequences' paged history (the tcgen05
+        prefill kernel). `tiles` ([n, 4] int32 on the device: sequence, first row, rows, first
+        position) comes with the step's inputs; without it the tiles are derived here, which reads
+        q_seq and q_pos back to the host."""
+        if tiles is None:
+            tiles = prefill_tiles(q_seq.tolist(), q_pos.tolist(), device=q.device)
+        qc = q.contiguous()
+        out = torch.empty_like(qc)
+        self.C.paged_prefill(qc, cache, block_tables, tiles, out, self.status, scale)
+        return out
 
     def silu_mul(self, gu):
         out = torch.empty(*gu.shape[:-1], gu.shape[-1] // 2, dtype=gu.dtype, device=gu.device)
@@ -186,6 +194,30 @@ class KernelOps:
         if v:
             self.status.zero_()
         return v
+
+
+PREFILL_ROWS = 128  # query rows per tile of the prefill kernel
+
+
+def prefill_tiles(q_seq, q_pos, device=None, rows: int = PREFILL_ROWS) -> torch.Tensor:
+    """The prefill kernel's work list from each row's sequence index and position (rows of one
+    sequence consecutive, positions increasing by one): tiles of at most `rows` rows, as int32
+    [n, 4] (sequence, first row, rows, first position), the longest history first so the causal
+    tail of long sequences starts early."""
+    tiles = []
+    t, T = 0, len(q_seq)
+    while t < T:
+        s = q_seq[t]
+        e = t
+        while e < T and q_seq[e] == s:
+            e += 1
+        for r0 in range(t, e, rows):
+            n = min(rows, e - r0)
+            tiles.append((int(s), r0, n, int(q_pos[r0])))
+        t = e
+    tiles.sort(key=lambda x: -(x[3] + x[2]))
+    out = torch.tensor(tiles or [(0, 0, 0, 0)], dtype=torch.int32)[: len(tiles)]
+    return out.to(device, non_blocking=True) if device is not None else out
 
 
 _CACHE: dict[str, object] = {}

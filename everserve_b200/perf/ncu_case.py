@@ -2,6 +2,7 @@
 
     python -m everserve_b200.perf.ncu_case --kernel gemm [--n 28672 --k 4096 --m 64]
     python -m everserve_b200.perf.ncu_case --kernel attn [--batch 64 --ctx 1024]
+    python -m everserve_b200.perf.ncu_case --kernel prefill [--batch 16 --ctx 1024]
     python -m everserve_b200.perf.ncu_case --kernel norm|rope|silu|argmax|kvgather
 
 Each case allocates a few hundred MB at most (operands larger than the 126 MB L2 where the kernel
@@ -23,13 +24,14 @@ from ..ops import KernelOps
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
-                    choices=["gemm", "attn", "norm", "rope", "silu", "argmax", "kvgather"])
+                    choices=["gemm", "attn", "prefill", "norm", "rope", "silu", "argmax", "kvgather"])
     ap.add_argument("--m", type=int, default=64)
     ap.add_argument("--n", type=int, default=28672)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx", type=int, default=1024)
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--time", action="store_true", help="also print the CUDA-event time per launch")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     ops = KernelOps(dev)
@@ -50,6 +52,21 @@ def main() -> None:
         q = torch.randn(a.batch, hq, d, device=dev, generator=g).bfloat16()
         ops.reserve_attention(a.batch, hq, d, mb * bs)
         run = lambda: ops.decode_attention(q, cache, bt, cl, 1 / math.sqrt(d), mb * bs)  # noqa: E731
+    elif a.kernel == "prefill":
+        # `batch` prompts of `ctx` tokens prefilled at once (each sees its own causal history)
+        from ..ops import prefill_tiles
+
+        hq, hkv, d, bs = 32, 8, 128, 16
+        mb = (a.ctx + bs - 1) // bs
+        cache = torch.randn(a.batch * mb, 2, hkv, bs, d, device=dev, generator=g).bfloat16()
+        bt = torch.arange(a.batch * mb, device=dev, dtype=torch.int32).view(a.batch, mb)
+        cl = torch.full((a.batch,), a.ctx, device=dev, dtype=torch.int32)
+        q = torch.randn(a.batch * a.ctx, hq, d, device=dev, generator=g).bfloat16()
+        seq = [i for i in range(a.batch) for _ in range(a.ctx)]
+        pos = [p for _ in range(a.batch) for p in range(a.ctx)]
+        tiles = prefill_tiles(seq, pos, device=dev)
+        qs, ps = torch.tensor(seq, device=dev), torch.tensor(pos, device=dev)
+        run = lambda: ops.prefill_attention(q, cache, bt, cl, qs, ps, 1 / math.sqrt(d), tiles)  # noqa: E731
     elif a.kernel == "norm":
         x = torch.randn(a.batch * 64, 4096, device=dev, generator=g).bfloat16()
         r = torch.randn_like(x)
@@ -89,6 +106,20 @@ def main() -> None:
         run()
     torch.cuda.synchronize()
     print(f"{a.kernel}: {a.launches} launches done")
+    if a.time:
+        # CUDA-event time per launch after the launches above (warm); never read under a profiler
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        ts = []
+        for _ in range(10):
+            flush.zero_()  # the operands leave L2 between launches
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            run()
+            e.record()
+            torch.cuda.synchronize()
+            ts.append(s.elapsed_time(e) * 1e3)
+        ts.sort()
+        print(f"{a.kernel}: median {ts[len(ts) // 2]:.1f} us, min {ts[0]:.1f} us per launch (L2 flushed)")
 
 
 if __name__ == "__main__":

@@ -219,6 +219,7 @@ class MirrorCommittedKV:
                     done = torch.cuda.Event()
                     done.record(self._side)
                 job.event = done
+                self._last_gather = done
             else:
                 sl = torch.tensor(slot_list, dtype=torch.int64)
                 heads = torch.tensor(self.heads, dtype=torch.int64)
@@ -277,6 +278,13 @@ class MirrorCommittedKV:
             self.stats_record["fence_wait_s"] += waited
         if self._error is not None:
             raise MirrorError(f"the store link failed: {self._error}")
+
+    def join_stream(self, stream=None) -> None:
+        """Make `stream` (default: the current one) wait for the last gather launched, so work
+        recorded after it on that stream also covers the commits' device copies."""
+        ev = getattr(self, "_last_gather", None)
+        if ev is not None:
+            (stream or torch.cuda.current_stream(self.device)).wait_event(ev)
 
     def flush(self, timeout_s: float = 30.0) -> None:
         """Wait for every commit issued so far."""

@@ -38,10 +38,14 @@ class _P:
 
 
 def _wait(pred, timeout=10.0):
+    """Poll `pred` until it holds; a view the coordinator has not made yet (404) counts as not yet."""
     t0 = time.monotonic()
     while time.monotonic() - t0 < timeout:
-        if pred():
-            return True
+        try:
+            if pred():
+                return True
+        except (ValueError, KeyError):
+            pass
         time.sleep(0.02)
     return False
 
