@@ -38,6 +38,10 @@ if HERE not in sys.path:
 
 METRIC = "decode tok/s at TP8 (1/2/4/8 GPU); failover pause p99; dead-rank detect ms"
 
+# The baseline: stock vLLM 0.22 (the engine the reference plugs into, unmodified) on the same
+# workload, measured by `bench.py --impl stock` on this pool's B200s (tokens/s by GPU count).
+STOCK_TOK_S = {1: 12701.7}
+
 
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons while the timed region runs."""
@@ -350,7 +354,7 @@ def main() -> None:
         "ms_per_step": round(dev_ms / args.steps, 4),
         "higher_is_better": True,
         "scaling": "strong",
-        "vs_baseline": None,
+        "vs_baseline": round(value / STOCK_TOK_S[world], 4) if world in STOCK_TOK_S else None,
         "dtype": "bf16",
         "data": "synthetic: uniform-random 1024-token prompts (seed 0), random-init weights",
         "config": {"model": "Llama-3-8B architecture (32 layers, hidden 4096, 32/8 heads, d 128, ffn 14336, "

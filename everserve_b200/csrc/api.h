@@ -16,7 +16,7 @@ cudaError_t launch_rmsnorm(const void* x, void* residual, const void* w, void* y
 cudaError_t launch_rope_kv(const void* qkv, const void* bias, const int64_t* positions, const float* cos_sin,
                            const int64_t* slots, void* q_out, void* cache, int64_t T, int hq, int hkv, int d,
                            int block_size, const int64_t* strides5, cudaStream_t s);
-cudaError_t launch_silu_mul(const void* gu, void* out, int64_t rows, int inter, cudaStream_t s);
+cudaError_t launch_silu_mul(const void* gu, void* out, int64_t rows, int inter, bool interleaved, cudaStream_t s);
 cudaError_t launch_embed(const int64_t* ids, const void* table, void* out, int64_t T, int hidden, int64_t vocab,
                          cudaStream_t s);
 cudaError_t launch_decode_advance(int64_t* st, const int64_t* sampled, const int* bt, int64_t bt_stride, int b, int B,
@@ -63,12 +63,20 @@ struct GemmArgs {
   const uint32_t* valid = nullptr;
   int64_t valid_cap = 0;
   int valid_segs = 0;
+  // gate/up rows interleaved by 64 (tile t: gate rows 64t.., then their up rows): out[M, N/2] =
+  // silu(gate) * up of the bf16-rounded products (no residual, scale, pre or valid)
+  int silu = 0;
 };
 int64_t gemm_pick_bn(int64_t M);
 int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms);
 int64_t gemm_ws_floats(int64_t num_sms);
 int64_t gemm_sync_words(int64_t num_sms);
 cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t s);
+// gemm_stream.cu: the stream-K decode GEMM (M <= 64; `ws`/`sync` sized by gemm_sk_*). With `silu`
+// the weight rows are gate/up interleaved by 64 and out[M, N/2] = silu(gate) * up.
+int64_t gemm_sk_ws_floats(int64_t num_sms);
+int64_t gemm_sk_sync_words(int64_t num_sms);
+cudaError_t launch_gemm_stream(const GemmArgs& a, bool silu, cudaStream_t s);
 // Mixture routing: per token softmax over E logits (bf16 rows of `stride`), top k (ties to the
 // lowest index), renormalised; scale[e, t] for this rank's experts e0 .. e0 + el - 1 (0 when not
 // chosen). E <= 64, el <= 32.

@@ -121,9 +121,10 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv
 }
 
 // ---------------------------------------------------------------------------------------------
-// out[t, i] = silu(g[t, i]) * u[t, i], g and u the two halves of gate_up's row.
+// out[t, i] = silu(g[t, i]) * u[t, i], g and u the two halves of gate_up's row, or (interleaved)
+// alternating runs of 64: g[i] at (i / 64) * 128 + i % 64 and u 64 further.
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int inter,
-                                int64_t rows) {
+                                int64_t rows, int interleaved) {
   pdl_wait();
   pdl_launch();
   const int nvec = inter >> 3;
@@ -134,8 +135,9 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloa
     const int i = (int)(idx % nvec);
     const uint4* row = reinterpret_cast<const uint4*>(gu + t * 2 * inter);
     float g[8], u[8], o[8];
-    unpack8(row[i], g);
-    unpack8(row[nvec + i], u);
+    const int gi = interleaved ? (i >> 3) * 16 + (i & 7) : i;  // 8 vectors = 64 elements per run
+    unpack8(row[gi], g);
+    unpack8(row[interleaved ? gi + 8 : nvec + i], u);
 #pragma unroll
     for (int e = 0; e < 8; e++) o[e] = g[e] / (1.f + __expf(-g[e])) * u[e];
     reinterpret_cast<uint4*>(out + t * inter)[i] = pack8(o);
@@ -352,14 +354,16 @@ cudaError_t launch_rope_kv(const void* qkv, const void* bias, const int64_t* pos
                    st[0], st[1], st[2], st[3]);
 }
 
-cudaError_t launch_silu_mul(const void* gu, void* out, int64_t rows, int inter, cudaStream_t stream) {
-  if (inter % 8 != 0) return cudaErrorInvalidValue;
+cudaError_t launch_silu_mul(const void* gu, void* out, int64_t rows, int inter, bool interleaved,
+                            cudaStream_t stream) {
+  if (inter % 8 != 0 || (interleaved && inter % 64 != 0)) return cudaErrorInvalidValue;
   if (rows == 0) return cudaSuccess;
   const int64_t total = rows * (inter / 8);
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
   return launch_ex(silu_mul_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, 0,
-                   static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(out), inter, rows);
+                   static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(out), inter, rows,
+                   interleaved ? 1 : 0);
 }
 
 cudaError_t launch_embed(const int64_t* ids, const void* table, void* out, int64_t T, int hidden, int64_t vocab,

@@ -18,6 +18,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <mutex>
 #include <unordered_map>
@@ -62,6 +63,7 @@ struct Params {
   int two_shot;                // fused all-reduce as reduce-scatter to tile owners + all-gather
   const uint32_t* valid;       // grouped rows: valid[s] rows of segment s (rows [s*cap, (s+1)*cap)) are live
   int valid_cap, valid_segs;
+  int silu;                    // rows gate/up interleaved by 64: out[m, N/2] = silu(gate) * up
 };
 
 // A token tile [m0, m0 + BN) of a grouped GEMM holds a live row: some segment it overlaps has a
@@ -80,6 +82,37 @@ ES_DEVICE float pre_terms(const Params& p, float acc, size_t m, int n) {
   if (p.scale) acc *= p.scale[m];
   if (p.pre) acc += bf2f(p.pre[m * p.ldp + n]);
   return acc;
+}
+
+// The partials of a cluster at byte offset `off` of each CTA's partial tile, loaded, and their sum
+// in rank order. Loads are issued for one element while the previous element is summed (software
+// pipelined): a distributed-shared-memory load has a long latency, and with in-order issue an add
+// right after each load would make every load wait for the one before it.
+struct ClusterRow {
+  float4 v[8];
+};
+ES_DEVICE void cluster_load(ClusterRow& r, uint32_t local, uint32_t off, int S) {
+#pragma unroll
+  for (int k = 0; k < 8; k++)
+    if (k < S) r.v[k] = ptx::ld_cluster_v4(ptx::map_cluster(local + off, (uint32_t)k));
+}
+ES_DEVICE float4 cluster_total(const ClusterRow& r, int S) {
+  float4 acc = r.v[0];
+#pragma unroll
+  for (int k = 1; k < 8; k++) {
+    if (k < S) {
+      acc.x += r.v[k].x;
+      acc.y += r.v[k].y;
+      acc.z += r.v[k].z;
+      acc.w += r.v[k].w;
+    }
+  }
+  return acc;
+}
+ES_DEVICE float4 cluster_sum(uint32_t local, uint32_t off, int S) {
+  ClusterRow r;
+  cluster_load(r, local, off, S);
+  return cluster_total(r, S);
 }
 
 // kAR: the row-parallel variant whose epilogue sums the tile over the group's members (comm.cuh)
@@ -145,16 +178,22 @@ __global__ void __launch_bounds__(kThreads, CPS)
   }
 
   if (producer) {
+    // Every CTA reads the same small activation matrix: walking the k-blocks from the same start,
+    // the CTAs of all weight tiles would ask the same L2 lines for the same block at once. Each
+    // tile starts its walk at its own offset instead (a fixed order per tile, so a row's sum does
+    // not depend on the batch).
+    const int rot = nkb > 0 ? (int)(blockIdx.x % (unsigned)nkb) : 0;
+    auto kblk = [&](int i) { return kb0 + (i + rot) % nkb; };
     // the weight tiles of the first stages depend on no kernel of the step: stream them while the
     // previous kernel finishes, then the activation tiles once it has
     const int pre = min(nkb, C::kStages);
     for (int i = 0; i < pre; i++) {
       ptx::mbar_arrive_expect_tx(&full[i], C::kStageBytes);
-      ptx::tma_load_2d(a_tiles + i * C::kABytes, &tmap_w, (kb0 + i) * BK, n0, &full[i]);
+      ptx::tma_load_2d(a_tiles + i * C::kABytes, &tmap_w, kblk(i) * BK, n0, &full[i]);
     }
     pdl_wait();
     pdl_launch();
-    for (int i = 0; i < pre; i++) ptx::tma_load_2d(b_tiles + i * C::kBBytes, &tmap_x, (kb0 + i) * BK, m0, &full[i]);
+    for (int i = 0; i < pre; i++) ptx::tma_load_2d(b_tiles + i * C::kBBytes, &tmap_x, kblk(i) * BK, m0, &full[i]);
     for (int i = pre; i < nkb; i++) {
       const int s = i % C::kStages;
       if (i >= C::kStages && !ptx::mbar_wait(&empty[s], ((i / C::kStages) - 1) & 1)) {
@@ -162,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
         break;
       }
       ptx::mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-      const int kx = (kb0 + i) * BK;
+      const int kx = kblk(i) * BK;
       ptx::tma_load_2d(a_tiles + s * C::kABytes, &tmap_w, kx, n0, &full[s]);
       ptx::tma_load_2d(b_tiles + s * C::kBBytes, &tmap_x, kx, m0, &full[s]);
     }
@@ -202,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
 #pragma unroll
         for (int j = 0; j < 16; j++) v[j] = 0.f;
       }
-      if (S > 1 || kAR) {
+      if (S > 1 || kAR || p.silu) {
         // the ring is drained (all MMAs completed before `done`), so its smem holds the partial
 #pragma unroll
         for (int j = 0; j < 16; j++) partial[(c0 + j) * BM + r] = v[j];
@@ -219,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
       }
     }
   }
-  if (S > 1 || kAR) {
+  if (S > 1 || kAR || p.silu) {
     // publish the partials to the cluster, then reduce this CTA's row slice over all of them
     ptx::cluster_sync();
     const uint32_t rank = ptx::cluster_rank();
@@ -241,17 +280,43 @@ __global__ void __launch_bounds__(kThreads, CPS)
       __syncthreads();
     }
     const uint32_t seq = kAR ? s_seq : 0u, parity = seq & 1u;
-    for (int e = threadIdx.x; e < total; e += kThreads) {
-      const int col = e / span4, row = r0 + (e % span4) * 4;
-      const uint32_t off = (uint32_t)((col * BM + row) * 4);
-      float4 acc = ptx::ld_cluster_v4(ptx::map_cluster(local + off, 0));
-      for (int k = 1; k < S; k++) {
-        const float4 v = ptx::ld_cluster_v4(ptx::map_cluster(local + off, (uint32_t)k));
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+    if (!kAR && p.silu) {
+      // SiLU-mul epilogue: this rank sums gate rows [g0, g1) of the tile and their up rows 64
+      // further over the partials (rank order, as the plain reduction), rounds both to bf16 as the
+      // plain GEMM's output would be, and applies the SiLU-mul kernel's arithmetic
+      const int rows64 = ((64 / S) + 3) & ~3;
+      const int g0 = min(64, (int)rank * rows64);
+      const int g1 = (int)rank + 1 == S ? 64 : min(64, g0 + rows64);
+      const int gspan4 = (g1 - g0) >> 2;
+      for (int e = threadIdx.x; e < gspan4 * mcount; e += kThreads) {
+        const int col = e / gspan4, row = g0 + (e % gspan4) * 4;
+        const uint32_t offg = (uint32_t)((col * BM + row) * 4), offu = offg + 64 * 4;
+        const float4 g = cluster_sum(local, offg, S);
+        const float4 u = cluster_sum(local, offu, S);
+        const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+        const size_t m = (size_t)(m0 + col);
+#pragma unroll
+        for (int z = 0; z < 4; z++) {
+          const int n = n0 / 2 + row + z;
+          if (n < p.N / 2) {
+            const float gq = bf2f(f2bf(gv[z])), uq = bf2f(f2bf(uv[z]));
+            p.out[m * p.ldo + n] = f2bf(gq / (1.f + __expf(-gq)) * uq);
+          }
+        }
       }
+    }
+    const int ptotal = p.silu ? 0 : total;
+    ClusterRow cur, nxt;
+    if ((int)threadIdx.x < ptotal) {
+      const int e = threadIdx.x;
+      cluster_load(cur, local, (uint32_t)(((e / span4) * BM + r0 + (e % span4) * 4) * 4), S);
+    }
+    for (int e = threadIdx.x; e < ptotal; e += kThreads) {
+      const int col = e / span4, row = r0 + (e % span4) * 4;
+      const int en = e + kThreads;
+      if (en < ptotal) cluster_load(nxt, local, (uint32_t)(((en / span4) * BM + r0 + (en % span4) * 4) * 4), S);
+      float4 acc = cluster_total(cur, S);
+      cur = nxt;
       if (p.scale || p.pre) {
         const size_t mm = (size_t)(m0 + col);
         const int nn = n0 + row;
@@ -436,18 +501,33 @@ int64_t gemm_pick_bn(int64_t M) {
 }
 
 // Cluster split for an N x K weight at decode sizes: as many CTAs per tile as the SM slots allow,
-// at most 8 (the portable cluster size) and at least 4 k-blocks each. One CTA per SM with a
-// deep ring when that still splits each tile 4 ways (or as far as two per SM would, with no more
-// tiles than SMs); otherwise two per SM. A function of (N, K, #SMs) only.
-static int64_t split_for(int64_t tiles, int64_t kb, int64_t slots) {
-  int64_t s = std::max<int64_t>(1, slots / tiles);
-  s = std::min<int64_t>(s, 8);  // portable cluster size: a cluster of 16 needs 16 free SMs in one GPC
-  s = std::min<int64_t>(s, std::max<int64_t>(1, kb / 4));
+// at most 8 (the portable cluster size), each with at least 16 k-blocks (each CTA pays a fixed
+// start-up and reduction cost, so fewer longer CTAs stream faster: measured on B200, the 6144 x
+// 4096 projection takes 18 us at 4 splits against 25 us at 6), relaxed to 8 and then 4 k-blocks
+// when that would leave fewer CTAs than half the SMs. A function of (N, K, #SMs) only.
+static int64_t split_for(int64_t tiles, int64_t kb, int64_t slots, int64_t num_sms) {
+  int64_t s = 1;
+  for (int64_t min_kb : {16, 8, 4}) {
+    s = std::max<int64_t>(1, slots / tiles);
+    s = std::min<int64_t>(s, 8);  // portable cluster size: a cluster of 16 needs 16 free SMs in one GPC
+    s = std::min<int64_t>(s, std::max<int64_t>(1, kb / min_kb));
+    if (tiles * s >= num_sms / 2) break;
+  }
   while (s > 1 && (kb + s - 1) / s * (s - 1) >= kb) s--;  // every split holds k-blocks
   return s;
 }
 
 void gemm_plan(int64_t M, int64_t N, int64_t K, int64_t num_sms, int* splits, int* cps) {
+  // tuning override for measurements: ES_GEMM_PLAN="<splits>,<ctas per SM>" for decode sizes
+  static const char* forced = std::getenv("ES_GEMM_PLAN");
+  if (forced != nullptr && M <= 64) {
+    int s = 0, c = 0;
+    if (sscanf(forced, "%d,%d", &s, &c) == 2 && s >= 1 && s <= 8 && (c == 1 || c == 2)) {
+      *splits = s;
+      *cps = c;
+      return;
+    }
+  }
   if (M > 64) {
     *splits = 1;
     *cps = 1;
@@ -455,7 +535,7 @@ void gemm_plan(int64_t M, int64_t N, int64_t K, int64_t num_sms, int* splits, in
   }
   const int64_t tiles = (N + gemm::BM - 1) / gemm::BM;
   const int64_t kb = (K + gemm::BK - 1) / gemm::BK;
-  const int64_t s1 = split_for(tiles, kb, num_sms), s2 = split_for(tiles, kb, 2 * num_sms);
+  const int64_t s1 = split_for(tiles, kb, num_sms, num_sms), s2 = split_for(tiles, kb, 2 * num_sms, num_sms);
   if (s1 >= 4 || (s1 == s2 && tiles <= num_sms)) {
     *splits = (int)s1;
     *cps = 1;
@@ -471,11 +551,30 @@ int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms) {
   return s;
 }
 
-int64_t gemm_ws_floats(int64_t) { return 1; }
-int64_t gemm_sync_words(int64_t) { return 1; }
+int64_t gemm_ws_floats(int64_t num_sms) { return gemm_sk_ws_floats(num_sms); }
+int64_t gemm_sync_words(int64_t num_sms) { return gemm_sk_sync_words(num_sms); }
+
+// Decode-size plain GEMMs with several waves of weight tiles (the vocabulary projection: 1002 tiles
+// on 296 CTA slots, a last wave 40 % full) take the stream-K kernel (gemm_stream.cu), about 5 %
+// faster there; the others stay on the cluster split-K kernel below, which is as fast or faster on
+// the shapes measured. ES_GEMM_STREAM=1 sends every decode-size plain GEMM to stream-K.
+static bool stream_k_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("ES_GEMM_STREAM");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
 
 cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return cudaSuccess;
+  const int64_t n_tiles = (a.N + gemm::BM - 1) / gemm::BM;
+  if (a.M <= 64 && a.valid == nullptr && a.ws != nullptr && a.sync != nullptr &&
+      (stream_k_enabled() || n_tiles > 4 * (int64_t)a.num_sms))
+    return launch_gemm_stream(a, a.silu != 0, stream);
+  if (a.silu && (a.N % gemm::BM != 0 || a.residual != nullptr || a.scale != nullptr || a.pre != nullptr ||
+                 a.valid != nullptr))
+    return cudaErrorInvalidValue;
   if (a.K % 8 != 0 || (a.ldx * 2) % 16 != 0 || (a.ldw * 2) % 16 != 0) return cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || reinterpret_cast<uintptr_t>(a.w) % 16 != 0)
     return cudaErrorInvalidValue;
@@ -492,6 +591,7 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.scale = a.scale;
   p.pre = static_cast<const __nv_bfloat16*>(a.pre);
   p.ldp = (int)a.ldp;
+  p.silu = a.silu;
   if (a.valid != nullptr) {
     if (a.valid_cap <= 0 || a.valid_segs <= 0 || a.valid_cap * a.valid_segs < a.M) return cudaErrorInvalidValue;
     p.valid = a.valid;

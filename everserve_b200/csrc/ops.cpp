@@ -74,14 +74,15 @@ void rope_kv_write(torch::Tensor qkv, c10::optional<torch::Tensor> bias, torch::
                                    (int)hkv, d, (int)block_size, strides.data(), cur()));
 }
 
-void silu_mul(torch::Tensor gu, torch::Tensor out) {
+void silu_mul(torch::Tensor gu, torch::Tensor out, bool interleaved) {
   check_bf16(gu, "gate_up");
   check_bf16(out, "out");
   TORCH_CHECK(gu.is_contiguous() && out.is_contiguous(), "contiguous");
   const int inter = (int)out.size(-1);
   TORCH_CHECK(gu.size(-1) == 2 * inter, "gate_up width");
+  TORCH_CHECK(!interleaved || inter % 64 == 0, "interleaved gate_up needs runs of 64");
   const c10::cuda::CUDAGuard g(gu.device());
-  ES_CHECK_CUDA(es::launch_silu_mul(gu.data_ptr(), out.data_ptr(), out.numel() / inter, inter, cur()));
+  ES_CHECK_CUDA(es::launch_silu_mul(gu.data_ptr(), out.data_ptr(), out.numel() / inter, inter, interleaved, cur()));
 }
 
 void embed(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
@@ -171,6 +172,38 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
     a.valid_cap = valid_cap;
     a.valid_segs = (int)valid->numel();
   }
+  const c10::cuda::CUDAGuard g(x.device());
+  ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
+}
+
+// out[M, N/2] = silu(gate) * up of x . w^T, w's rows gate/up interleaved by 64 (decode sizes)
+void gemm_silu(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor ws, torch::Tensor sync,
+               torch::Tensor status, int64_t num_sms) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D operands");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "K-contiguous operands");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && N % 128 == 0, "w: [N, K] with N a multiple of 128");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N / 2, "out: [M, N / 2]");
+  TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= es::gemm_ws_floats(num_sms), "stream-K workspace too small");
+  TORCH_CHECK(sync.scalar_type() == at::kInt && sync.numel() >= es::gemm_sync_words(num_sms), "sync words too small");
+  es::GemmArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.out = out.data_ptr();
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ldx = x.stride(0);
+  a.ldw = w.stride(0);
+  a.ldo = out.stride(0);
+  a.status = status.data_ptr<int>();
+  a.ws = ws.data_ptr<float>();
+  a.sync = reinterpret_cast<uint32_t*>(sync.data_ptr<int>());
+  a.num_sms = (int)num_sms;
+  a.silu = 1;
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
 }
@@ -523,7 +556,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "everserve_b200 sm_100a kernels";
   m.def("rmsnorm", &rmsnorm, "RMSNorm, optionally fused with the residual add");
   m.def("rope_kv_write", &rope_kv_write, "RoPE on q/k and the paged-KV write of k/v");
-  m.def("silu_mul", &silu_mul, "silu(gate) * up");
+  m.def("silu_mul", &silu_mul, "silu(gate) * up (halves, or runs of 64 interleaved)", pybind11::arg("gu"),
+        pybind11::arg("out"), pybind11::arg("interleaved") = false);
   m.def("embed", &embed, "embedding gather");
   m.def("argmax", &argmax, "greedy argmax per row");
   m.def("decode_advance", &decode_advance, "next decode step's inputs from the sampled ids");
@@ -537,6 +571,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ws_floats", &es::gemm_ws_floats);
   m.def("gemm_sync_words", &es::gemm_sync_words);
   m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
+  m.def("gemm_silu", &gemm_silu, "GEMM with SiLU-mul fused into its epilogue (gate/up rows interleaved by 64)");
   m.def("paged_prefill", &paged_prefill, "paged causal prefill attention (tcgen05: S and P.V in TMEM, TMA K/V tiles)");
   m.def("moe_route", &moe_route, "mixture routing: per-token weights of this rank's experts [el, T]");
   m.def("moe_topk", &moe_topk, "mixture routing: each token's top k experts and their weights");

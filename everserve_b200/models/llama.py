@@ -17,11 +17,12 @@ group, which is the fused GEMM + all-reduce when the group has one.
 from __future__ import annotations
 
 import hashlib
+import os
 from dataclasses import dataclass
 
 import torch
 
-from ..ops import ops_for, ref, softmax_scale
+from ..ops import interleave_gate_up, ops_for, ref, softmax_scale
 from .config import ModelConfig
 
 
@@ -117,6 +118,10 @@ class DecoderLM:
             self.inter = cfg.intermediate // T
         self.vocab_local = (cfg.vocab + T - 1) // T
         self.vocab0 = r * self.vocab_local
+        # dense gate_up weights on the kernels are stored interleaved by 64 rows, so the decode GEMM
+        # computes SiLU-mul in its epilogue (ops.linear_silu); the reference ops keep gate then up
+        self.fused_silu = (not cfg.is_moe and self.ops.kind == "kernel" and self.inter % 64 == 0
+                           and os.environ.get("ES_FUSED_SILU", "1") != "0")
         self.cos_sin = ref.cos_sin_table(cfg.head_dim, cfg.max_position, cfg.rope_theta, cfg.rope_scaling).to(self.device)
         self.weights: dict[str, torch.Tensor] = {}
         if init == "random":
@@ -131,6 +136,8 @@ class DecoderLM:
         return t
 
     def _put(self, key: str, t: torch.Tensor):
+        if self.fused_silu and key.endswith(".gate_up") and ".e" not in key:
+            t = interleave_gate_up(t)
         self.weights[key] = t.to(device=self.device, dtype=self.dtype).contiguous()
 
     def _init_random(self):
@@ -241,8 +248,10 @@ class DecoderLM:
             if c.is_moe:
                 m = self._moe(h, p)
             else:
-                gu = ops.linear(h, W[p + "gate_up"])
-                act = ops.silu_mul(gu)
+                if self.fused_silu:
+                    act = ops.linear_silu(h, W[p + "gate_up"])
+                else:
+                    act = ops.silu_mul(ops.linear(h, W[p + "gate_up"]))
                 m = self.tp.linear_allreduce(ops, act, W[p + "down"])
             nxt = f"l{l + 1}.in_norm" if l + 1 < self.l1 else None
             if nxt is not None:

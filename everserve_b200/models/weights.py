@@ -18,6 +18,7 @@ import os
 
 import torch
 
+from ..ops import deinterleave_gate_up
 from .llama import DecoderLM
 
 
@@ -126,6 +127,8 @@ def to_hf_state_dict(model: DecoderLM) -> dict[str, torch.Tensor]:
                 out[m + f"experts.{e}.w2.weight"] = W[p + f"e{e}.down"]
         else:
             gu = W[p + "gate_up"]
+            if getattr(model, "fused_silu", False):
+                gu = deinterleave_gate_up(gu)
             out[hf + "mlp.gate_proj.weight"], out[hf + "mlp.up_proj.weight"] = gu[: c.intermediate], gu[c.intermediate :]
             out[hf + "mlp.down_proj.weight"] = W[p + "down"]
     return {k: v.clone().contiguous() for k, v in out.items()}

@@ -16,7 +16,7 @@ import torch
 from . import ref
 from .. import _ext
 
-__all__ = ["KernelOps", "RefOps", "ops_for", "prefill_tiles", "ref"]
+__all__ = ["KernelOps", "RefOps", "deinterleave_gate_up", "interleave_gate_up", "ops_for", "prefill_tiles", "ref"]
 
 
 class RefOps:
@@ -58,8 +58,13 @@ class RefOps:
     def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale, tiles=None):
         return ref.paged_attention(q, cache, block_tables, ctx_lens, q_seq, q_pos, scale)
 
-    def silu_mul(self, gu):
+    def silu_mul(self, gu, interleaved: bool = False):
+        if interleaved:
+            gu = deinterleave_gate_up(gu.t()).t()
         return ref.silu_mul(gu)
+
+    def linear_silu(self, x, w):
+        return self.silu_mul(self.linear(x, w), interleaved=True)
 
     def argmax(self, logits):
         return ref.argmax(logits)
@@ -178,9 +183,19 @@ class KernelOps:
         self.C.paged_prefill(qc, cache, block_tables, tiles, out, self.status, scale)
         return out
 
-    def silu_mul(self, gu):
+    def silu_mul(self, gu, interleaved: bool = False):
         out = torch.empty(*gu.shape[:-1], gu.shape[-1] // 2, dtype=gu.dtype, device=gu.device)
-        self.C.silu_mul(gu, out)
+        self.C.silu_mul(gu, out, interleaved)
+        return out
+
+    def linear_silu(self, x, w):
+        """silu(gate) * up of x . w^T for a gate/up weight interleaved by 64 rows
+        (``interleave_gate_up``): one GEMM with the SiLU-mul in its epilogue (each 128-row tile
+        holds 64 gates and their up rows)."""
+        M = x.shape[0]
+        self.reserve_linear()
+        out = torch.empty(M, w.shape[0] // 2, dtype=x.dtype, device=x.device)
+        self.C.gemm_silu(x, w, out, self._ws, self._ctr, self.status, self.num_sms)
         return out
 
     def argmax(self, logits):
@@ -194,6 +209,21 @@ class KernelOps:
         if v:
             self.status.zero_()
         return v
+
+
+def interleave_gate_up(gu: torch.Tensor, run: int = 64) -> torch.Tensor:
+    """[2I, H] gate rows then up rows -> runs of `run` gate rows each followed by the matching up
+    rows: the layout whose 128-row GEMM tiles hold a gate and its up projection together."""
+    inter = gu.shape[0] // 2
+    g, u = gu[:inter], gu[inter:]
+    return torch.stack([g.reshape(inter // run, run, -1), u.reshape(inter // run, run, -1)], 1).reshape(gu.shape)
+
+
+def deinterleave_gate_up(w: torch.Tensor, run: int = 64) -> torch.Tensor:
+    """The inverse of ``interleave_gate_up``."""
+    inter = w.shape[0] // 2
+    v = w.reshape(inter // run, 2, run, -1)
+    return torch.cat([v[:, 0].reshape(inter, -1), v[:, 1].reshape(inter, -1)], 0)
 
 
 PREFILL_ROWS = 128  # query rows per tile of the prefill kernel

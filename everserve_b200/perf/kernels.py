@@ -75,6 +75,12 @@ def main() -> None:
             rows.append({"kernel": "gemm", "name": name, "M": M, "N": N, "K": K,
                          "us": round(ms * 1e3, 2), "gb_s": round(byts / ms / 1e6, 1),
                          "cublas_us": round(cub * 1e3, 2), "cublas_gb_s": round(byts / cub / 1e6, 1)})
+            if name == "gate_up" and M <= 64:
+                # the same weights with SiLU-mul in the GEMM epilogue (rows interleaved by 64)
+                sms = _time(lambda: k.linear_silu(x, w), flush=flush)
+                byts_s = (N * K + M * K + M * N // 2) * 2
+                rows.append({"kernel": "gemm_silu", "name": name, "M": M, "N": N, "K": K,
+                             "us": round(sms * 1e3, 2), "gb_s": round(byts_s / sms / 1e6, 1)})
     if a.only in (None, "attn"):
         hq, hkv, d, bs = 32 // tp, max(1, 8 // tp), 128, 16
         B, ctx = M, a.ctx

@@ -228,3 +228,38 @@ def test_kv_gather_to_mapped_host(kops):
         assert torch.equal(view[1, 1, 1, 0], caches[1][33 // bs, 0, 1, 33 % bs].cpu())
     finally:
         C.host_unregister(host.data_ptr())
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 28672, 4096), (5, 3584, 4096), (1, 256, 512), (33, 9728, 896), (200, 3584, 4096)])
+def test_gemm_silu_fused(kops, M, N, K):
+    """SiLU-mul in the GEMM epilogue (gate/up rows interleaved by 64) equals the GEMM followed by the
+    SiLU-mul kernel bit for bit, and the fp32 oracle within bf16 tolerance."""
+    from everserve_b200.ops import interleave_gate_up
+
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    gu = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
+    w = interleave_gate_up(gu).contiguous()
+    fused = kops.linear_silu(x, w)
+    unfused = kops.silu_mul(kops.linear(x, w), interleaved=True)
+    assert torch.equal(fused, unfused)
+    # (the plain layout puts a row in another tile, so its k-blocks split differently: close, not equal)
+    close(unfused, kops.silu_mul(kops.linear(x, gu)))
+    gate, up = (x.float() @ gu.float().t()).chunk(2, dim=1)
+    close(fused, torch.nn.functional.silu(gate) * up)
+    assert kops.check_status() == 0
+
+
+def test_gemm_stream_k_repeats_and_tail(kops):
+    """Stream-K: runs that end inside a tile park partials for the CTA that finishes the tile; the
+    result does not change over repeated launches (epoch flags) or with the token count."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    for N, K in ((128256 // 8, 4096), (4096, 14336), (1000, 1792), (128, 64), (6144, 4096)):
+        w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
+        x = torch.randn(64, K, device="cuda", generator=g).bfloat16()
+        first = kops.linear(x, w)
+        for _ in range(3):
+            assert torch.equal(kops.linear(x, w), first)
+        assert torch.equal(kops.linear(x[:7].contiguous(), w), first[:7])
+        close(first, x.float() @ w.float().t())
+    assert kops.check_status() == 0
