@@ -93,6 +93,7 @@ struct Engine {
   std::string cover_sig;
   signals::CoverPlan cover;
   std::vector<std::vector<uint32_t>> cover_covers;
+  std::vector<Uncovered> cover_uncovered;  // losses the plan leaves unanswered, with the reason
   std::map<std::string, std::set<std::string>> cover_formed;
   std::map<std::string, std::string> cover_failed;
   // a change an earlier lease holder logged but did not commit: finished once its nodes link
@@ -900,8 +901,15 @@ struct Coordinator {
     for (auto& [r, h] : e.workers) in.holders[r] = {h.node, h.device};
     in.spares = e.spares;
     in.max_groups_per_gpu = policy.cover_max_groups_per_gpu;
+    auto allows = [&](int32_t o) {
+      return std::find(policy.outcomes.begin(), policy.outcomes.end(), o) != policy.outcomes.end();
+    };
+    in.replace = allows(signals::Outcome_OUTCOME_REPLACE);
+    in.shrink = allows(signals::Outcome_OUTCOME_SHRINK) && ep != policy.engines.end() && ep->second.placement_independent;
     std::vector<std::vector<uint32_t>> covers;
-    signals::CoverPlan plan = plan_cover(in, &covers);
+    std::vector<Uncovered> uncovered;
+    signals::CoverPlan plan = plan_cover(in, &covers, &uncovered);
+    e.cover_uncovered = uncovered;
     const std::string sig = plan.serialize();
     if (sig == e.cover_sig) return;
     e.cover_sig = sig;
@@ -1337,6 +1345,13 @@ struct Coordinator {
           ranks += (k ? "," : "") + std::to_string(e.cover_covers[i][k]);
       cov += std::string(i ? "," : "") + "{\"purpose\":\"" + json_escape(e.cover.sets[i].purpose) + "\",\"covers\":" +
              ranks + "],\"covered\":" + (set_covered(e, i) ? "true" : "false") + "}";
+    }
+    cov += "],\"uncovered\":[";
+    for (size_t i = 0; i < e.cover_uncovered.size(); i++) {
+      const auto& u = e.cover_uncovered[i];
+      std::string ranks = "[";
+      for (size_t k = 0; k < u.lost.size(); k++) ranks += (k ? "," : "") + std::to_string(u.lost[k]);
+      cov += std::string(i ? "," : "") + "{\"lost\":" + ranks + "],\"why\":\"" + json_escape(u.why) + "\"}";
     }
     cov += "]}";
     return "{\"metadata\":{\"name\":\"" + json_escape(e.name) + "\"},\"status\":{\"epoch\":" + std::to_string(e.epoch) +

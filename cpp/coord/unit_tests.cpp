@@ -155,7 +155,113 @@ static void test_policy_and_outcome() {
   CHECK(c.outcome == signals::Outcome_OUTCOME_SHRINK);
 }
 
+// ---- cover planning --------------------------------------------------------------------------
+static SpareSeat seat(const std::string& node, uint32_t device, int64_t for_rank) {
+  SpareSeat s;
+  s.node = node;
+  s.device = device;
+  s.for_rank = for_rank;
+  return s;
+}
+
+static CoverInput cover_in(uint32_t tp, uint32_t pp, const std::vector<std::pair<std::string, std::vector<uint32_t>>>& nodes) {
+  CoverInput in;
+  in.engine = "e0";
+  in.tp = tp;
+  in.pp = pp;
+  for (auto& [node, ranks] : nodes)
+    for (uint32_t r : ranks) in.holders[r] = {node, r};
+  return in;
+}
+
+static std::vector<std::string> purposes(const signals::CoverPlan& p) {
+  std::vector<std::string> out;
+  for (auto& s : p.sets) out.push_back(s.purpose);
+  return out;
+}
+
+static void test_cover() {
+  // TP1 PP2 over two nodes with one any-rank spare on a third node
+  CoverInput in = cover_in(1, 2, {{"a", {0}}, {"b", {1}}});
+  in.spares = {seat("c", 0, -1)};
+  std::vector<std::vector<uint32_t>> covers;
+  std::vector<Uncovered> unc;
+  auto plan = plan_cover(in, &covers, &unc);
+  auto ps = purposes(plan);
+  // the current set, then each node's loss (each node holds one rank here, so no position losses)
+  CHECK(ps.size() == 3 && ps[0] == "current" && ps[1] == "REPLACE of ranks [0]" && ps[2] == "REPLACE of ranks [1]");
+  CHECK(covers.size() == 3 && covers[0].empty() && covers[1] == std::vector<uint32_t>{0});
+  CHECK(unc.empty());
+  CHECK(plan.sets[1].members[0].has_spare && plan.sets[1].members[0].spare.node == "c" && !plan.sets[1].members[1].has_spare);
+  // one pipeline group per set, the current set's group first and shared by no other set
+  CHECK(plan.groups.size() == 3 && plan.sets[0].groups.size() == 1);
+
+  // TP2 PP1 on one node with two any-rank spares on another: the node's loss needs both spares,
+  // then each position's loss; second spares after every first cover
+  in = cover_in(2, 1, {{"a", {0, 1}}});
+  in.spares = {seat("s", 0, -1), seat("s", 1, -1)};
+  covers.clear();
+  unc.clear();
+  plan = plan_cover(in, &covers, &unc);
+  ps = purposes(plan);
+  CHECK(ps.size() == 6);
+  CHECK(ps[1] == "REPLACE of ranks [0, 1]" && ps[2] == "REPLACE of ranks [0]" && ps[3] == "REPLACE of ranks [1]");
+  CHECK(ps[4] == "REPLACE of ranks [0] through a second spare" && ps[5] == "REPLACE of ranks [1] through a second spare");
+  CHECK(answers(plan.sets[1].members, {0, 1}) && answers(plan.sets[2].members, {0}) && !answers(plan.sets[2].members, {1}));
+  // the second spare is another seat than the first
+  CHECK(plan.sets[4].members[0].spare.device != plan.sets[2].members[0].spare.device);
+  CHECK(unc.empty());
+
+  // a spare on the lost node dies with it: the node's loss is uncovered, its positions are not
+  in = cover_in(2, 1, {{"a", {0, 1}}});
+  in.spares = {seat("a", 5, -1)};
+  unc.clear();
+  plan = plan_cover(in, nullptr, &unc);
+  CHECK(unc.size() == 1 && unc[0].lost == (std::vector<uint32_t>{0, 1}) && unc[0].why.find("no spare") != std::string::npos);
+
+  // SHRINK allowed: every loss also gets its survivors' set
+  in = cover_in(2, 1, {{"a", {0}}, {"b", {1}}});
+  in.replace = false;
+  in.shrink = true;
+  plan = plan_cover(in);
+  ps = purposes(plan);
+  CHECK(ps.size() == 3 && ps[1] == "SHRINK of ranks [0]" && plan.sets[1].members.size() == 1);
+
+  // neither outcome: every loss uncovered with the policy as the reason
+  in.shrink = false;
+  unc.clear();
+  plan_cover(in, nullptr, &unc);
+  CHECK(unc.size() == 2 && unc[0].why.find("neither") != std::string::npos);
+
+  // the budget bounds the groups a process holds (TP1 PP2: each set needs one group over both
+  // members); the sets it refuses are reported as over the budget
+  in = cover_in(1, 2, {{"a", {0}}, {"b", {1}}});
+  in.spares = {seat("c", 0, -1)};
+  in.max_groups_per_gpu = 2;  // the current group plus one more each: both replacement sets fit
+  unc.clear();
+  plan = plan_cover(in, nullptr, &unc);
+  CHECK(plan.sets.size() == 3 && unc.empty());
+  in.max_groups_per_gpu = 1;  // the current group only
+  unc.clear();
+  plan = plan_cover(in, nullptr, &unc);
+  CHECK(plan.sets.size() == 1 && unc.size() == 2 && unc[0].why.find("budget of 1") != std::string::npos);
+  // groups other engines' plans put on the spare count too
+  in.max_groups_per_gpu = 3;
+  in.elsewhere[{"c", 0}] = 3;
+  unc.clear();
+  plan = plan_cover(in, nullptr, &unc);
+  CHECK(plan.sets.size() == 1 && unc.size() == 2);
+
+  // a spare for rank 1 takes rank 1 ahead of an any-rank spare
+  in = cover_in(2, 1, {{"a", {0}}, {"b", {1}}});
+  in.spares = {seat("x", 0, -1), seat("y", 0, 1)};
+  plan = plan_cover(in);
+  for (auto& st : plan.sets)
+    if (st.purpose == "REPLACE of ranks [1]") CHECK(st.members[1].spare.node == "y");
+}
+
 int main() {
+  test_cover();
   test_fit();
   test_degrade();
   test_topology();

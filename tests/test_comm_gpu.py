@@ -66,6 +66,15 @@ def _worker(rank: int, world: int, port: int, results, nvls: bool = False):
         dist.all_gather(parts, part)
         expect = (ref.member_sum(parts).float() + res.float())
         out["gemm_ar_close"] = bool(torch.allclose(fused.float(), expect, rtol=2e-2, atol=2e-2))
+        # the fp32 oracle straight from the operands: every member's x_r . w_r^T, summed in rank order
+        oracle = torch.zeros(M, N)
+        for r in range(world):
+            gr = torch.Generator(device="cpu").manual_seed(7 + r)
+            xr = torch.randn(M, K, generator=gr).bfloat16()
+            wr = (torch.randn(N, K, generator=gr) / 64).bfloat16()
+            oracle += xr.float() @ wr.float().t()
+        oracle += res.float().cpu()
+        out["gemm_ar_oracle"] = bool(torch.allclose(fused.float().cpu(), oracle, rtol=2e-2, atol=3e-2))
         allf = [torch.empty_like(fused) for _ in range(world)]
         dist.all_gather(allf, fused)
         out["gemm_ar_same_on_ranks"] = all(torch.equal(allf[0], f) for f in allf)
@@ -147,7 +156,7 @@ def test_peer_collectives(nvls):
     for r in range(world):
         o = res[r]
         assert o["fdar_exact"], o
-        assert o["gemm_ar_close"] and o["gemm_ar_same_on_ranks"], o
+        assert o["gemm_ar_close"] and o["gemm_ar_same_on_ranks"] and o["gemm_ar_oracle"], o
         assert o["alternating_splits_close"], o
         assert o["status"] == 0, o
         if not nvls:
