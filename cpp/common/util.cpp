@@ -241,6 +241,20 @@ const Json* Json::get(const std::string& k) const {
   return nullptr;
 }
 
+const Json* Json::field(const std::string& camel) const {
+  if (const Json* v = get(camel)) return v;
+  std::string snake;
+  for (char c : camel) {
+    if (c >= 'A' && c <= 'Z') {
+      snake.push_back('_');
+      snake.push_back((char)(c - 'A' + 'a'));
+    } else {
+      snake.push_back(c);
+    }
+  }
+  return snake == camel ? nullptr : get(snake);
+}
+
 bool Json::parse(const std::string& text, Json& out, std::string* err) {
   JP p{text, 0, {}};
   if (!p.value(out)) {

@@ -29,6 +29,9 @@ struct Json {
   std::vector<Json> arr;
   std::vector<std::pair<std::string, Json>> obj;
   const Json* get(const std::string& k) const;
+  // A proto3 JSON field by its lowerCamelCase name, or by the proto field name it came from
+  // ("outcomesInOrder" or "outcomes_in_order"): proto3 JSON readers accept both.
+  const Json* field(const std::string& camel) const;
   static bool parse(const std::string& text, Json& out, std::string* err = nullptr);
   std::string dump() const;
 };

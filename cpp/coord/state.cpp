@@ -35,53 +35,53 @@ bool parse_policy(const std::string& json, Policy& out, std::string& err) {
     return false;
   }
   out = Policy{};
-  if (const Json* o = j.get("outcomesInOrder"))
+  if (const Json* o = j.field("outcomesInOrder"))
     for (auto& v : o->arr) out.outcomes.push_back(outcome_of(v));
   if (out.outcomes.empty()) out.outcomes = {signals::Outcome_OUTCOME_REPLACE};
-  out.max_concurrent_losses = u32(j.get("maxConcurrentLosses"), 0);
-  out.notice_min_ms = u32(j.get("noticeMinMs"), 0);
-  if (const Json* cv = j.get("cover")) {
-    if (const Json* en = cv->get("enabled")) out.cover_enabled = en->b;
-    out.cover_max_groups_per_gpu = u32(cv->get("maxGroupsPerGpu"), 0);
+  out.max_concurrent_losses = u32(j.field("maxConcurrentLosses"), 0);
+  out.notice_min_ms = u32(j.field("noticeMinMs"), 0);
+  if (const Json* cv = j.field("cover")) {
+    if (const Json* en = cv->field("enabled")) out.cover_enabled = en->b;
+    out.cover_max_groups_per_gpu = u32(cv->field("maxGroupsPerGpu"), 0);
   }
-  if (const Json* sp = j.get("spares")) {
-    out.spares.per_engine = u32(sp->get("perEngine"), 0);
-    if (const Json* l = sp->get("loading"))
+  if (const Json* sp = j.field("spares")) {
+    out.spares.per_engine = u32(sp->field("perEngine"), 0);
+    if (const Json* l = sp->field("loading"))
       out.spares.loading = l->kind == Json::Number ? (int32_t)l->num
                            : l->str == "LOADING_PRELOADED" ? 1 : l->str == "LOADING_ON_NOTICE" ? 2 : 0;
-    if (const Json* am = sp->get("allowMismatched")) out.spares.allow_mismatched = am->b;
-    out.spares.max_degrade_percent = u32(sp->get("maxDegradePercent"), 0);
+    if (const Json* am = sp->field("allowMismatched")) out.spares.allow_mismatched = am->b;
+    out.spares.max_degrade_percent = u32(sp->field("maxDegradePercent"), 0);
   }
-  if (const Json* es = j.get("engines")) {
+  if (const Json* es = j.field("engines")) {
     for (auto& e : es->arr) {
       EnginePolicy ep;
-      if (const Json* n = e.get("name")) ep.name = n->str;
+      if (const Json* n = e.field("name")) ep.name = n->str;
       if (ep.name.empty()) {
         err = "an engine without a name";
         return false;
       }
-      ep.tensor = std::max<uint32_t>(1, u32(e.get("tensorParallel"), 1));
-      ep.pipeline = std::max<uint32_t>(1, u32(e.get("pipelineParallel"), 1));
-      ep.data = std::max<uint32_t>(1, u32(e.get("dataParallel"), 1));
-      ep.expert = std::max<uint32_t>(1, u32(e.get("expertParallel"), 1));
-      if (const Json* pi = e.get("placementIndependentModel")) ep.placement_independent = pi->b;
-      if (const Json* sn = e.get("spareNodes"))
+      ep.tensor = std::max<uint32_t>(1, u32(e.field("tensorParallel"), 1));
+      ep.pipeline = std::max<uint32_t>(1, u32(e.field("pipelineParallel"), 1));
+      ep.data = std::max<uint32_t>(1, u32(e.field("dataParallel"), 1));
+      ep.expert = std::max<uint32_t>(1, u32(e.field("expertParallel"), 1));
+      if (const Json* pi = e.field("placementIndependentModel")) ep.placement_independent = pi->b;
+      if (const Json* sn = e.field("spareNodes"))
         for (auto& s : sn->arr) ep.spare_nodes.push_back(s.str);
-      if (const Json* rb = e.get("releaseBoundMs")) ep.release_bound_ms = (int64_t)u32(rb, 0);
-      if (const Json* rn = e.get("replicaNodes"))
+      if (const Json* rb = e.field("releaseBoundMs")) ep.release_bound_ms = (int64_t)u32(rb, 0);
+      if (const Json* rn = e.field("replicaNodes"))
         for (auto& n : rn->arr) ep.replica_nodes.push_back(n.str);
-      if (const Json* sl = e.get("spares"))
+      if (const Json* sl = e.field("spares"))
         for (auto& x : sl->arr) {
           SpareSlotPolicy slot;
-          if (const Json* n = x.get("node")) slot.node = n->str;
-          slot.device = u32(x.get("device"), 0);
-          if (const Json* r = x.get("rank")) slot.rank = (int64_t)u32(r, 0);
+          if (const Json* n = x.field("node")) slot.node = n->str;
+          slot.device = u32(x.field("device"), 0);
+          if (const Json* r = x.field("rank")) slot.rank = (int64_t)u32(r, 0);
           ep.spare_slots.push_back(slot);
         }
-      if (const Json* sl = e.get("spareLaunch")) {
-        if (const Json* c = sl->get("command"))
+      if (const Json* sl = e.field("spareLaunch")) {
+        if (const Json* c = sl->field("command"))
           for (auto& a : c->arr) ep.launch_command.push_back(a.str);
-        if (const Json* env = sl->get("env"))
+        if (const Json* env = sl->field("env"))
           for (auto& [k, v] : env->obj) ep.launch_env[k] = v.str;
       }
       out.engines[ep.name] = ep;

@@ -468,6 +468,16 @@ def emit_cpp(files: dict[str, ProtoFile]) -> str:
         w("  }")
         w("  return true;")
         w("}")
+    # decode then encode by full message name: the codec's check against other encoders
+    w("\nnamespace pbgen {")
+    w("// Decode `in` as the message `full` names (\"everserve.signals.v1.Change\") and encode it again;")
+    w("// false for an unknown name or bytes the codec refuses.")
+    w("inline bool roundtrip(const std::string& full, const std::string& in, std::string& out) {")
+    for name in sorted(msgs):
+        w(f'  if (full == "{name}") {{ {_cpp_name(name)} m; if (!m.parse(in)) return false; out = m.serialize(); return true; }}')
+    w("  return false;")
+    w("}")
+    w("}  // namespace pbgen")
     return "\n".join(out) + "\n"
 
 
