@@ -6,7 +6,8 @@ import subprocess
 import time
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-BIN = os.path.join(ROOT, "cpp", "bin")
+# EVERSERVE_CPP_BIN points the tests at another build of the binaries (the sanitizer builds)
+BIN = os.environ.get("EVERSERVE_CPP_BIN") or os.path.join(ROOT, "cpp", "bin")
 
 
 def build() -> None:
