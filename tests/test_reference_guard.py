@@ -33,9 +33,9 @@ DIE_STEP, DIE_AT_CALL = 3, 2
 def _guarded_rank(rank, cfg, port, store_addr, conn, fault_q, die):
     torch.set_num_threads(1)
     tcp = dist.TCPStore("127.0.0.1", port, is_master=False, timeout=datetime.timedelta(seconds=60))
-    from everserve_b200.reference.world import join_world, leave_world
+    from everserve_b200.reference.world import form_group, shrink_world
 
-    group = join_world(tcp, list(range(WORLD)), rank, timeout_s=20)
+    group = form_group(tcp, list(range(WORLD)), rank, timeout_s=20)
     place = {"attn": P.even_units(cfg.kv_heads, WORLD), "mlp": P.even_units(MLP_UNITS, WORLD)}
     kv = LoopbackCommittedKV(store_addr)
     faults = FaultListener()
@@ -52,7 +52,7 @@ def _guarded_rank(rank, cfg, port, store_addr, conn, fault_q, die):
     core = LlamaCore(cfg, rank, place["attn"][rank], place["mlp"][rank], MLP_UNITS, reduce=reduce)
 
     def leave(f):
-        leave_world(group, f["lost"], f["epoch"])
+        shrink_world(group, f["lost"], f["epoch"])
 
     def absorb(f, upto):
         a1, m1 = P.after_loss(place["attn"], f["lost"]), P.after_loss(place["mlp"], f["lost"])
@@ -129,9 +129,9 @@ def test_rank_dies_mid_step_survivors_rerun_bit_identical(cfg):
 def _reconcile_rank(rank, port, conn):
     torch.set_num_threads(1)
     tcp = dist.TCPStore("127.0.0.1", port, is_master=False, timeout=datetime.timedelta(seconds=60))
-    from everserve_b200.reference.world import join_world
+    from everserve_b200.reference.world import form_group
 
-    group = join_world(tcp, [0, 1, 2], rank, timeout_s=20)
+    group = form_group(tcp, [0, 1, 2], rank, timeout_s=20)
     state = {"x": torch.zeros(4)}
     marks = {}
     guard = StepGuard(group, leave=lambda f: None, absorb=lambda f, upto: None)

@@ -66,9 +66,9 @@ def _oracle(cfg):
 def _rank(rank, cfg, port, store_addr, conn, fault_addr_q):
     torch.set_num_threads(1)
     tcp = dist.TCPStore("127.0.0.1", port, is_master=False, timeout=datetime.timedelta(seconds=30))
-    from everserve_b200.reference.world import join_world, leave_world
+    from everserve_b200.reference.world import form_group, shrink_world
 
-    group = join_world(tcp, list(range(WORLD)), rank)
+    group = form_group(tcp, list(range(WORLD)), rank)
     attn0, mlp0 = P.even_units(cfg.kv_heads, WORLD), P.even_units(MLP_UNITS, WORLD)
     core = LlamaCore(cfg, rank, attn0[rank], mlp0[rank], MLP_UNITS, reduce=group.all_reduce)
     kv = LoopbackCommittedKV(store_addr)
@@ -82,7 +82,7 @@ def _rank(rank, cfg, port, store_addr, conn, fault_addr_q):
         if cmd == "check-fault":
             f = faults.next(timeout=30)
             lost, epoch = f["lost"], f["epoch"]
-            leave_world(group, lost, epoch)
+            shrink_world(group, lost, epoch)
             a1, m1 = P.after_loss(attn0, lost), P.after_loss(mlp0, lost)
             gained_a, gained_m = P.moved(attn0, a1)[rank], P.moved(mlp0, m1)[rank]
             core.absorb(gained_a, gained_m, kv.restore(gained_a))
