@@ -34,7 +34,7 @@ struct CommArgs {
   int row;                // this member's row
 };
 int64_t comm_buffer_bytes();
-int64_t comm_max_elems();
+int64_t comm_max_elems(int64_t members);
 int64_t comm_ll_max_elems();
 cudaError_t launch_fdar(const void* inp, void* out, int64_t n, const CommArgs& c, cudaStream_t s);
 
@@ -68,6 +68,8 @@ struct GemmArgs {
   int silu = 0;
 };
 int64_t gemm_pick_bn(int64_t M);
+// the decode split plan (cluster split-K and CTAs per SM) for an N x K bf16 weight at M tokens
+void gemm_plan(int64_t M, int64_t N, int64_t K, int64_t num_sms, int* splits, int* cps);
 int64_t gemm_pick_splits(int64_t M, int64_t N, int64_t K, int64_t num_sms);
 int64_t gemm_ws_floats(int64_t num_sms);
 int64_t gemm_sync_words(int64_t num_sms);
@@ -132,6 +134,24 @@ struct DecodeArgs {
   float scale;
 };
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t s);
+
+// ---- gemm_fp8.cu: block-scaled fp8 (e4m3) GEMM ------------------------------------------------------
+struct Fp8GemmArgs {
+  const void* x;        // [M, K] e4m3, row stride ldx bytes
+  const void* w;        // [N, K] e4m3, row stride ldw bytes
+  const float* x_scale; // [M, K / 128], row stride xs_ld
+  const float* w_scale; // [ceil(N / 128), K / 128], row stride ws_ld
+  void* out;            // [M, N] bf16 (or [M, N / 2] with silu), row stride ldo
+  const void* residual; // optional [M, N] bf16, row stride ldr
+  int* status;
+  int64_t M, N, K, ldx, ldw, ldo, ldr, xs_ld, ws_ld;
+  int num_sms;
+  int silu = 0;         // gate/up rows interleaved by 64: out = silu(gate) * up
+};
+cudaError_t launch_gemm_fp8(const Fp8GemmArgs& a, cudaStream_t s);
+// per token and 128-wide block: x8 = e4m3(x / scale), scale = amax / 448
+cudaError_t launch_quant_fp8(const void* x, int64_t ldx, void* x8, int64_t ld8, float* scale, int64_t lds, int64_t M,
+                             int64_t K, cudaStream_t s);
 
 // ---- prefill.cu ----------------------------------------------------------------------------------
 struct PrefillArgs {

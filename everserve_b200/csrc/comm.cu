@@ -1,11 +1,12 @@
 // Failure-detecting all-reduce ("fdar"): sum a bf16 vector over the members of a tensor-parallel
 // group through peer memory, in member order, with bounded waits (see comm.cuh for the protocol).
 //
-// One CTA per chunk of kChunk elements: it pushes its chunk into every member's buffer at its own
-// sender row with 16-byte stores over NVLink, publishes one flag per member (system-scope release
-// after a system fence), waits on its own buffer for every member's flag of the chunk, then sums
-// the members' chunks in member order in fp32 (one rounding) into `out`. Decode-size tensors (up
-// to 1 Mi elements, the data region of one sender) take this path; larger ones go to NCCL.
+// Decode-size tensors (up to 512 Ki elements) take the LL kernel: every 8-byte word carries two
+// bf16 and the call number, pushed to every member, so one round trip and no flags. Larger ones take
+// the two-shot kernel (a reduce-scatter to chunk owners, then the owners' sums to every member),
+// up to 1 Mi elements per member per call; the host splits bigger tensors into calls.
+#include <algorithm>
+
 #include "api.h"
 #include "launch.h"
 #include "comm.cuh"
@@ -15,8 +16,17 @@ namespace comm {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kChunk = 4096;  // elements per CTA and flag slot
+constexpr int kChunk = kChunkElems;
 
+// Two-shot all-reduce (tensors above the LL path): a persistent grid, CTA b taking chunks b,
+// b + grid, ... in the same order on every member. For chunk c (owner: member c % count):
+//   1. every member writes its part of c into the owner's data row for it (at the owner's local
+//      index c / count), a system fence, then raises the owner's flag for (its row, local index);
+//   2. the owner waits for every member's flag, sums the parts in member order in fp32 (one
+//      rounding) into `out`, writes the sum into every other member's gather area and raises the
+//      chunk's gather flag there; the others wait for that flag and copy the sum out.
+// Each member sends about twice (count - 1) / count of the vector and receives as much, against
+// count - 1 times the vector for pushing every part to every member. Every wait is bounded.
 __global__ void __launch_bounds__(kThreads) fdar_kernel(const __nv_bfloat16* __restrict__ inp,
                                                         __nv_bfloat16* __restrict__ out, int n, View v) {
   pdl_wait();
@@ -35,58 +45,75 @@ __global__ void __launch_bounds__(kThreads) fdar_kernel(const __nv_bfloat16* __r
   __syncthreads();
   const uint32_t seq = s_seq, parity = seq & 1u;
   const int count = s_count;
-  const int c = blockIdx.x;
-  const int e0 = c * kChunk, e1 = min(n, e0 + kChunk);
-  const int nvec = (e1 - e0) / 8;  // whole 16-byte vectors; the tail goes element by element
   const uint64_t my_base = v.peers[v.row];
-  // push this member's chunk to every member
-  const uint4* src = reinterpret_cast<const uint4*>(inp + e0);
-  if (v.mc) {
-    // NVLS: one multicast store per vector reaches every member (the tail in whole words too)
-    uint4* dst = reinterpret_cast<uint4*>(data_ptr(v.mc, parity, v.row) + (size_t)e0 * 2);
-    for (int i = threadIdx.x; i < nvec; i += kThreads) mc_st_v4(dst + i, src[i]);
-    if (threadIdx.x == 0 && e1 > e0 + nvec * 8) {
-      uint4 t = make_uint4(0, 0, 0, 0);
-      __nv_bfloat16* tb = reinterpret_cast<__nv_bfloat16*>(&t);
-      for (int i = e0 + nvec * 8; i < e1; i++) tb[i - e0 - nvec * 8] = inp[i];
-      mc_st_v4(dst + nvec, t);
-    }
-  } else {
-    for (int k = 0; k < count; k++) {
-      uint4* dst = reinterpret_cast<uint4*>(data_ptr(v.peers[s_order[k]], parity, v.row) + (size_t)e0 * 2);
+  const int nchunks = (n + kChunk - 1) / kChunk;
+  // an owner's chunks must fit one data row of each sender: at most kDataBytes / chunk per member
+  if (nchunks > (int)(kDataBytes / (kChunk * 2)) * count) {
+    if (threadIdx.x == 0) finish_call(v, seq, kBadShape);
+    return;
+  }
+  for (int c = blockIdx.x; count > 0 && c < nchunks; c += gridDim.x) {
+    const int owner = s_order[c % count];
+    const size_t local = (size_t)(c / count) * kChunk * 2;  // byte offset in the owner's rows
+    const int e0 = c * kChunk, e1 = min(n, e0 + kChunk);
+    const int nvec = (e1 - e0) / 8;  // whole 16-byte vectors; the tail goes element by element
+    // 1. this member's part of the chunk, into the owner's row for this member
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(inp + e0);
+      uint4* dst = reinterpret_cast<uint4*>(data_ptr(v.peers[owner], parity, v.row) + local);
       for (int i = threadIdx.x; i < nvec; i += kThreads) dst[i] = src[i];
       __nv_bfloat16* dt = reinterpret_cast<__nv_bfloat16*>(dst);
       for (int i = e0 + nvec * 8 + threadIdx.x; i < e1; i += kThreads) dt[i - e0] = inp[i];
     }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) __threadfence_system();
-  __syncthreads();
-  if (v.mc) {
-    if (threadIdx.x == 0) mc_st_release_u32(flag_ptr(v.mc, parity, v.row, c), seq);
-  } else if (threadIdx.x < count) {
-    st_release_sys(flag_ptr(v.peers[s_order[threadIdx.x]], parity, v.row, c), seq);
-  }
-  if (threadIdx.x == 0) s_fail = wait_members(v, my_base, parity, c, seq, s_order, count);
-  __syncthreads();
-  if (s_fail == kOk) {
-    for (int i = threadIdx.x; i < nvec; i += kThreads) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int k = 0; k < count; k++) {
-        const uint4 w = reinterpret_cast<const uint4*>(data_ptr(my_base, parity, s_order[k]) + (size_t)e0 * 2)[i];
-        float f[8];
-        unpack8(w, f);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      st_release_sys(flag_ptr(v.peers[owner], parity, v.row, c / count), seq);
+    }
+    if (owner == v.row) {
+      // 2. the owner: every part, summed in member order, to `out` and every member's gather area
+      if (threadIdx.x == 0) s_fail = wait_members(v, my_base, parity, c / count, seq, s_order, count);
+      __syncthreads();
+      if (s_fail != kOk) break;
+      for (int i = threadIdx.x; i < nvec; i += kThreads) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int k = 0; k < count; k++) {
+          const uint4 w = reinterpret_cast<const uint4*>(data_ptr(my_base, parity, s_order[k]) + local)[i];
+          float f[8];
+          unpack8(w, f);
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[j] += f[j];
+          for (int j = 0; j < 8; j++) acc[j] += f[j];
+        }
+        const uint4 r = pack8(acc);
+        reinterpret_cast<uint4*>(out + e0)[i] = r;
+        for (int k = 0; k < count; k++)
+          if (s_order[k] != v.row) reinterpret_cast<uint4*>(ag_ptr(v.peers[s_order[k]], parity) + (size_t)e0 * 2)[i] = r;
       }
-      reinterpret_cast<uint4*>(out + e0)[i] = pack8(acc);
+      for (int i = e0 + nvec * 8 + threadIdx.x; i < e1; i += kThreads) {
+        float acc = 0.f;
+        for (int k = 0; k < count; k++)
+          acc += bf2f(reinterpret_cast<const __nv_bfloat16*>(data_ptr(my_base, parity, s_order[k]) + local)[i - e0]);
+        const __nv_bfloat16 r = f2bf(acc);
+        out[i] = r;
+        for (int k = 0; k < count; k++)
+          if (s_order[k] != v.row) reinterpret_cast<__nv_bfloat16*>(ag_ptr(v.peers[s_order[k]], parity))[i] = r;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) __threadfence_system();
+      __syncthreads();
+      if (threadIdx.x < count && s_order[threadIdx.x] != v.row)
+        st_release_sys(ag_flag_ptr(v.peers[s_order[threadIdx.x]], parity, c), seq);
+    } else {
+      // the others: the owner's sum, from this member's gather area
+      if (threadIdx.x == 0) s_fail = wait_flag(v, ag_flag_ptr(my_base, parity, c), seq, owner);
+      __syncthreads();
+      if (s_fail != kOk) break;
+      const uint4* src = reinterpret_cast<const uint4*>(ag_ptr(my_base, parity) + (size_t)e0 * 2);
+      for (int i = threadIdx.x; i < nvec; i += kThreads) reinterpret_cast<uint4*>(out + e0)[i] = src[i];
+      for (int i = e0 + nvec * 8 + threadIdx.x; i < e1; i += kThreads)
+        out[i] = reinterpret_cast<const __nv_bfloat16*>(ag_ptr(my_base, parity))[i];
     }
-    for (int i = e0 + nvec * 8 + threadIdx.x; i < e1; i += kThreads) {
-      float acc = 0.f;
-      for (int k = 0; k < count; k++)
-        acc += bf2f(reinterpret_cast<const __nv_bfloat16*>(data_ptr(my_base, parity, s_order[k]))[i]);
-      out[i] = f2bf(acc);
-    }
+    __syncthreads();
   }
   __syncthreads();
   if (threadIdx.x == 0) finish_call(v, seq, s_fail);
@@ -153,12 +180,14 @@ __global__ void __launch_bounds__(kLLThreads) fdar_ll_kernel(const __nv_bfloat16
 int64_t comm_ll_max_elems() { return (int64_t)(comm::kLLSmallBytes / 8 * 2); }
 
 int64_t comm_buffer_bytes() { return (int64_t)comm::kBufferBytes; }
-int64_t comm_max_elems() { return (int64_t)(comm::kDataBytes / 2); }
+// elements one all-reduce call takes: each member owns at most a data row's worth of chunks
+int64_t comm_max_elems(int64_t members) {
+  return std::max<int64_t>(1, std::min<int64_t>(members, comm::kMaxRows)) * (int64_t)(comm::kDataBytes / 2);
+}
 
 cudaError_t launch_fdar(const void* inp, void* out, int64_t n, const CommArgs& c, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
-  if (n > comm_max_elems() || reinterpret_cast<uintptr_t>(inp) % 16 != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0 ||
-      c.seqs == nullptr)
+  if (reinterpret_cast<uintptr_t>(inp) % 16 != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0 || c.seqs == nullptr)
     return cudaErrorInvalidValue;
   comm::View v{};
   v.seqs = c.seqs;
@@ -174,7 +203,17 @@ cudaError_t launch_fdar(const void* inp, void* out, int64_t n, const CommArgs& c
     return launch_ex(comm::fdar_ll_kernel, dim3(grid), dim3(comm::kLLThreads), 0, stream, 0,
                      static_cast<const __nv_bfloat16*>(inp), static_cast<__nv_bfloat16*>(out), (int)n, v);
   }
-  const int grid = (int)((n + comm::kChunk - 1) / comm::kChunk);
+  // the two-shot path: the member count is a device table (it changes with membership), so the
+  // call's size is checked against the largest group; the caller keeps calls within its own count
+  if (n > (int64_t)comm::kMaxChunks * comm::kChunk) return cudaErrorInvalidValue;
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (sms[dev] == 0 && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return cudaErrorInvalidDevice;
+  // persistent: every CTA resident at once (they wait on peers' CTAs of the same index)
+  const int chunks = (int)((n + comm::kChunk - 1) / comm::kChunk);
+  const int grid = std::min(chunks, 2 * sms[dev]);
   return launch_ex(comm::fdar_kernel, dim3(grid), dim3(comm::kThreads), 0, stream, 0,
                    static_cast<const __nv_bfloat16*>(inp), static_cast<__nv_bfloat16*>(out), (int)n, v);
 }

@@ -21,6 +21,12 @@
 // ORs the rows it still waits for into the host-visible late mask and keeps waiting; the host's
 // abort word (polled every 1024 spins) or a hard limit ends the wait, the call returns garbage and
 // the status word says why. Nothing here traps or spins without a bound.
+//
+// Heartbeats: every member's process advances a beat word in its row of the slot region from a
+// native thread (about every 0.5 ms, whatever its Python thread is doing). A wait that sees the
+// beat of the member it waits for stand still for `beat_limit_us` (host-written, 0 = off) names
+// that member late and leaves with kDead: a member whose process died is named in milliseconds,
+// by the kernel itself, instead of after the bound and the host's checks.
 #pragma once
 
 #include <stdint.h>
@@ -41,18 +47,32 @@ constexpr size_t kLLGemmOff = kFlagBytes + (size_t)2 * kMaxRows * kDataBytes;
 constexpr size_t kLLSmallOff = kLLGemmOff + (size_t)2 * kMaxRows * kLLGemmBytes;
 constexpr size_t kLLResOff = kLLSmallOff + (size_t)2 * kMaxRows * kLLSmallBytes;
 // the two-shot fused GEMM's results: [2 parity][kLLGemmBytes], each word written by its tile's owner
-constexpr size_t kBufferBytes = kLLResOff + (size_t)2 * kLLGemmBytes;
+// Two-shot all-reduce of large tensors (comm.cu): chunks of kChunkElems, chunk c owned by member
+// c % count; senders write their part of an owned chunk into the owner's data rows (at the owner's
+// local chunk index), the owner sums and writes the result into every member's gather area, then
+// raises the chunk's gather flag there.
+constexpr int kChunkElems = 4096;
+constexpr int kMaxChunks = kMaxRows * (int)(kDataBytes / (kChunkElems * 2));  // 2048: 8 Mi elements
+constexpr size_t kAGFlagOff = kLLResOff + (size_t)2 * kLLGemmBytes;
+constexpr size_t kAGFlagBytes = (size_t)2 * kMaxChunks * 4;                     // [2 parity][chunk] u32
+constexpr size_t kAGOff = kAGFlagOff + ((kAGFlagBytes + 4095) & ~(size_t)4095);
+constexpr size_t kAGBytes = (size_t)kMaxRows * kDataBytes;                      // per parity: a whole call
+constexpr size_t kBufferBytes = kAGOff + (size_t)2 * kAGBytes;
 constexpr int kSeqSlots = 4096;  // per-slot LL call counters (this member's device memory)
 constexpr uint64_t kHardLimitNs = 5000000000ull;  // a wait never outlives 5 s
 
-// Host-mapped control words of one member (pinned host memory the device reads and writes).
+// Host-mapped control words of one member (pinned host memory the device reads and writes); the
+// members' rows lie kRowBytes apart in the slot region, so a kernel finds a peer's row from its own.
 struct Ctrl {
-  uint32_t abort;      // host: non-zero makes waiting kernels leave
-  uint32_t late;       // device: mask of rows a wait has been waiting for past bound_ns
-  uint64_t bound_ns;   // host: 0 = never name late members
-  uint32_t status;     // device: last failure (kTimeout / kAborted)
-  uint32_t pad[3];
+  uint32_t abort;          // host: non-zero makes waiting kernels leave
+  uint32_t late;           // device: mask of rows a wait has been waiting for past bound_ns
+  uint64_t bound_ns;       // host: 0 = never name late members
+  uint32_t status;         // device: last failure (kTimeout / kAborted / kDead)
+  uint32_t beat;           // the member's process: its heartbeat counter
+  uint32_t beat_limit_us;  // host: a beat standing still this long means the member is dead (0 = off)
+  uint32_t pad;
 };
+constexpr int kRowBytes = 256;  // slot region row stride (parallel/slot.py ROW_BYTES)
 
 // Device view of a member's place in the group (kernel parameter, by value).
 struct View {
@@ -107,17 +127,46 @@ ES_DEVICE void mc_st_u64(void* mc_addr, uint64_t v) {
                : "memory");
 }
 
+// The control words of row `row` (a member's row of the slot region, found from this member's).
+ES_DEVICE volatile Ctrl* ctrl_of(const View& v, int row) {
+  return reinterpret_cast<volatile Ctrl*>(reinterpret_cast<char*>(v.ctrl) + (ptrdiff_t)(row - v.row) * kRowBytes);
+}
+
+// Heartbeat watch of one awaited member: true once its beat has stood still past the limit.
+struct BeatWatch {
+  uint32_t last = 0;
+  uint64_t since = 0;
+  ES_DEVICE bool stopped(const View& v, int sender, uint64_t now) {
+    const uint32_t lim = v.ctrl->beat_limit_us;
+    if (lim == 0) return false;
+    const uint32_t b = ctrl_of(v, sender)->beat;
+    if (since == 0 || b != last) {
+      last = b;
+      since = now;
+      return false;
+    }
+    return now - since > (uint64_t)lim * 1000ull;
+  }
+};
+
 // Poll one LL word of `sender` until it carries `seq`; returns its two bf16 (as bits) or reports
-// a failure through `fail` (aborted / hard limit). `t0`, `named` and `spins` persist per thread.
+// a failure through `fail` (aborted / dead / hard limit). `t0`, `named` and `spins` persist per
+// thread.
 ES_DEVICE uint32_t ll_wait(const View& v, const uint64_t* w, uint32_t seq, int sender, uint64_t& t0, bool& named,
                            uint32_t& spins, int& fail) {
   uint64_t x = ld_u64_relaxed(w);
+  BeatWatch beat;
   while ((uint32_t)(x >> 32) != seq) {
     if ((++spins & 1023u) == 0) {
       volatile Ctrl* c = v.ctrl;
       if (t0 == 0) t0 = global_ns();
       if (c->abort) {
         fail = kAborted;
+        return 0;
+      }
+      if (beat.stopped(v, sender, global_ns())) {
+        c->late = c->late | (1u << sender);
+        fail = kDead;
         return 0;
       }
       const uint64_t now = global_ns() - t0;
@@ -134,6 +183,42 @@ ES_DEVICE uint32_t ll_wait(const View& v, const uint64_t* w, uint32_t seq, int s
     x = ld_u64_relaxed(w);
   }
   return (uint32_t)x;
+}
+
+ES_DEVICE uint32_t* ag_flag_ptr(uint64_t base, uint32_t parity, int chunk) {
+  return reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(base) + kAGFlagOff) + (size_t)parity * kMaxChunks + chunk;
+}
+ES_DEVICE char* ag_ptr(uint64_t base, uint32_t parity) {
+  return reinterpret_cast<char*>(base) + kAGOff + (size_t)parity * kAGBytes;
+}
+
+// Wait until the flag at `f` (in this member's own buffer) equals `seq`, raised by member `sender`:
+// bounded like every wait (abort word, the sender's heartbeat, the bound naming it late, the hard
+// limit). Called by one thread; returns kOk or the failure.
+ES_DEVICE int wait_flag(const View& v, const uint32_t* f, uint32_t seq, int sender) {
+  const uint64_t t0 = global_ns();
+  uint64_t bound = 0;
+  bool named = false;
+  uint32_t spins = 0;
+  BeatWatch beat;
+  while (ld_acquire_sys(f) != seq) {
+    if ((++spins & 1023u) == 0) {
+      volatile Ctrl* c = v.ctrl;
+      if (c->abort) return kAborted;
+      const uint64_t t = global_ns();
+      if (beat.stopped(v, sender, t)) {
+        c->late = c->late | (1u << sender);
+        return kDead;
+      }
+      if (bound == 0) bound = c->bound_ns;
+      if (!named && bound != 0 && t - t0 > bound) {
+        c->late = c->late | (1u << sender);
+        named = true;
+      }
+      if (t - t0 > kHardLimitNs) return kTimeout;
+    }
+  }
+  return kOk;
 }
 
 ES_DEVICE uint32_t* flag_ptr(uint64_t base, uint32_t parity, int sender, int slot) {
@@ -154,10 +239,15 @@ ES_DEVICE int wait_members(const View& v, uint64_t my_base, uint32_t parity, int
   for (int i = 0; i < count; i++) {
     const int sender = order[i];
     const uint32_t* f = flag_ptr(my_base, parity, sender, slot);
+    BeatWatch beat;
     while (ld_acquire_sys(f) != seq) {
       if ((++spins & 1023u) == 0) {
         volatile Ctrl* c = v.ctrl;
         if (c->abort) return kAborted;
+        if (beat.stopped(v, sender, global_ns())) {
+          c->late = c->late | (1u << sender);
+          return kDead;
+        }
         const uint64_t now = global_ns() - t0;
         if (bound == 0) bound = c->bound_ns;
         if (!named && bound != 0 && now > bound) {

@@ -19,6 +19,7 @@ enum Status : int32_t {
   kTimeout = 1,      // a bounded wait ran out (peer flag, mbarrier)
   kAborted = 2,      // the host raised the abort word
   kBadShape = 3,     // a launch-time check failed on the device side
+  kDead = 4,         // a member awaited stopped its heartbeat (its process is gone)
 };
 
 ES_DEVICE uint64_t global_ns() {

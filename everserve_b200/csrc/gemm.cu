@@ -439,7 +439,8 @@ __global__ void __launch_bounds__(kThreads, CPS)
   __syncthreads();
   if (warp == 1) ptx::tmem_dealloc(tmem, C::kTmemCols);
   if (threadIdx.x == 0) {
-    if (s_fail && p.status) atomicExch(p.status, s_fail == kAborted ? (int)kAborted : (int)kTimeout);
+    if (s_fail && p.status)
+      atomicExch(p.status, (s_fail == kAborted || s_fail == kDead) ? s_fail : (int)kTimeout);
   }
 }
 

@@ -7,8 +7,14 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <atomic>
+#include <chrono>
 #include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "api.h"
@@ -206,6 +212,60 @@ void gemm_silu(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tenso
   a.silu = 1;
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
+}
+
+// ---- block-scaled fp8 ---------------------------------------------------------------------------
+void quant_fp8(torch::Tensor x, torch::Tensor x8, torch::Tensor scale) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x8.dim() == 2 && x8.stride(1) == 1, "2-D row-major operands");
+  TORCH_CHECK(x8.element_size() == 1 && x8.sizes() == x.sizes(), "x8: one byte per element, x's shape");
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && scale.dim() == 2 && scale.size(0) == x.size(0) &&
+                  scale.size(1) == x.size(1) / 128 && scale.stride(1) == 1,
+              "scale: fp32 [M, K / 128]");
+  const c10::cuda::CUDAGuard g(x.device());
+  ES_CHECK_CUDA(es::launch_quant_fp8(x.data_ptr(), x.stride(0), x8.data_ptr(), x8.stride(0), scale.data_ptr<float>(),
+                                     scale.stride(0), x.size(0), x.size(1), cur()));
+}
+
+void gemm_fp8(torch::Tensor x8, torch::Tensor x_scale, torch::Tensor w8, torch::Tensor w_scale, torch::Tensor out,
+              c10::optional<torch::Tensor> residual, torch::Tensor status, int64_t num_sms, bool silu) {
+  TORCH_CHECK(x8.element_size() == 1 && w8.element_size() == 1, "fp8 operands (one byte per element)");
+  TORCH_CHECK(x8.dim() == 2 && w8.dim() == 2 && x8.stride(1) == 1 && w8.stride(1) == 1, "2-D K-contiguous operands");
+  check_bf16(out, "out");
+  const int64_t M = x8.size(0), K = x8.size(1), N = w8.size(0);
+  TORCH_CHECK(w8.size(1) == K && K % 128 == 0, "K mismatch or not a multiple of 128");
+  TORCH_CHECK(x_scale.scalar_type() == at::kFloat && x_scale.size(0) == M && x_scale.size(1) == K / 128 &&
+                  x_scale.stride(1) == 1,
+              "x_scale: fp32 [M, K / 128]");
+  TORCH_CHECK(w_scale.scalar_type() == at::kFloat && w_scale.size(0) == (N + 127) / 128 && w_scale.size(1) == K / 128 &&
+                  w_scale.stride(1) == 1,
+              "w_scale: fp32 [ceil(N / 128), K / 128]");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == (silu ? N / 2 : N) && out.stride(1) == 1, "out shape");
+  es::Fp8GemmArgs a{};
+  a.x = x8.data_ptr();
+  a.w = w8.data_ptr();
+  a.x_scale = x_scale.data_ptr<float>();
+  a.w_scale = w_scale.data_ptr<float>();
+  a.out = out.data_ptr();
+  a.status = status.data_ptr<int>();
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ldx = x8.stride(0);
+  a.ldw = w8.stride(0);
+  a.ldo = out.stride(0);
+  a.xs_ld = x_scale.stride(0);
+  a.ws_ld = w_scale.stride(0);
+  a.num_sms = (int)num_sms;
+  a.silu = silu ? 1 : 0;
+  if (residual.has_value() && residual->defined()) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N && residual->stride(1) == 1, "residual shape");
+    a.residual = residual->data_ptr();
+    a.ldr = residual->stride(0);
+  }
+  const c10::cuda::CUDAGuard g(x8.device());
+  ES_CHECK_CUDA(es::launch_gemm_fp8(a, cur()));
 }
 
 torch::Tensor moe_route(torch::Tensor logits, int64_t k, int64_t e0, int64_t el) {
@@ -478,6 +538,50 @@ void kv_copy(bool gather, torch::Tensor layer_ptrs, torch::Tensor slots, torch::
 
 // ---- host helpers ---------------------------------------------------------------------------------
 
+// ---- heartbeats ------------------------------------------------------------------------------
+// A native thread that advances a 32-bit counter (a member's beat word in the slot region's shared,
+// device-mapped pages) every `period_us`, independent of the Python interpreter: the beat stops only
+// when the process does. The kernels' peer waits read it (comm.cuh).
+namespace {
+struct Beater {
+  std::atomic<bool> stop{false};
+  std::thread t;
+};
+std::mutex g_beat_mu;
+std::map<int64_t, std::unique_ptr<Beater>> g_beaters;
+int64_t g_beat_next = 1;
+}  // namespace
+
+int64_t heartbeat_start(int64_t addr, int64_t period_us) {
+  TORCH_CHECK(addr != 0 && addr % 4 == 0 && period_us > 0, "heartbeat: a 4-byte aligned word and a period");
+  auto b = std::make_unique<Beater>();
+  Beater* raw = b.get();
+  uint32_t* word = reinterpret_cast<uint32_t*>(addr);
+  raw->t = std::thread([raw, word, period_us] {
+    while (!raw->stop.load(std::memory_order_relaxed)) {
+      __atomic_fetch_add(word, 1u, __ATOMIC_RELEASE);
+      std::this_thread::sleep_for(std::chrono::microseconds(period_us));
+    }
+  });
+  std::lock_guard<std::mutex> g(g_beat_mu);
+  const int64_t id = g_beat_next++;
+  g_beaters.emplace(id, std::move(b));
+  return id;
+}
+
+void heartbeat_stop(int64_t id) {
+  std::unique_ptr<Beater> b;
+  {
+    std::lock_guard<std::mutex> g(g_beat_mu);
+    auto it = g_beaters.find(id);
+    if (it == g_beaters.end()) return;
+    b = std::move(it->second);
+    g_beaters.erase(it);
+  }
+  b->stop.store(true);
+  if (b->t.joinable()) b->t.join();
+}
+
 int64_t host_register_mapped(int64_t ptr, int64_t bytes) {
   ES_CHECK_CUDA(cudaHostRegister(reinterpret_cast<void*>(ptr), (size_t)bytes,
                                  cudaHostRegisterMapped | cudaHostRegisterPortable));
@@ -572,6 +676,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_sync_words", &es::gemm_sync_words);
   m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
   m.def("gemm_silu", &gemm_silu, "GEMM with SiLU-mul fused into its epilogue (gate/up rows interleaved by 64)");
+  m.def("quant_fp8", &quant_fp8, "x -> e4m3 with a scale per token and 128-wide block");
+  m.def("gemm_fp8", &gemm_fp8, "block-scaled fp8 GEMM (tcgen05 kind::f8f6f4, scales per 128-wide K block)");
   m.def("paged_prefill", &paged_prefill, "paged causal prefill attention (tcgen05: S and P.V in TMEM, TMA K/V tiles)");
   m.def("moe_route", &moe_route, "mixture routing: per-token weights of this rank's experts [el, T]");
   m.def("moe_topk", &moe_topk, "mixture routing: each token's top k experts and their weights");
@@ -591,7 +697,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("scale") = pybind11::none(), pybind11::arg("pre") = pybind11::none(),
         pybind11::arg("two_shot") = 0);
   m.def("comm_buffer_bytes", &es::comm_buffer_bytes);
-  m.def("comm_max_elems", &es::comm_max_elems);
+  m.def("comm_max_elems", &es::comm_max_elems, "elements one all-reduce call takes for a group of `members`",
+        pybind11::arg("members") = 1);
   m.def("comm_ll_max_elems", &es::comm_ll_max_elems);
   m.def("kv_gather", [](torch::Tensor lp, torch::Tensor s, torch::Tensor h, int64_t st, int64_t cap, int64_t d,
                         int64_t bs, std::vector<int64_t> str, int64_t el) { kv_copy(true, lp, s, h, st, cap, d, bs, str, el); },
@@ -600,6 +707,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                          int64_t bs, std::vector<int64_t> str, int64_t el) { kv_copy(false, lp, s, h, st, cap, d, bs, str, el); },
         "staging rows -> paged cache");
   m.def("host_register_mapped", &host_register_mapped);
+  m.def("heartbeat_start", &heartbeat_start, "advance a beat word every period_us from a native thread; returns its id");
+  m.def("heartbeat_stop", &heartbeat_stop, "stop a heartbeat thread");
   m.def("host_unregister", &host_unregister);
   m.def("device_alloc", &device_alloc);
   m.def("device_free", &device_free);

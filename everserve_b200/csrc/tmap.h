@@ -85,5 +85,23 @@ inline cudaError_t bf16_2d(CUtensorMap* out, void* base, int64_t rows, int64_t c
   return cudaSuccess;
 }
 
+// A 2-D map of one-byte elements (fp8 tensors) over a row-major [rows, cols] matrix with row stride
+// `ld` bytes; the box is [box_rows, box_cols] with box_cols == 128 (one 128-byte swizzle row),
+// swizzled 128B. Not cached: callers encode it per launch (a few microseconds on the host).
+inline cudaError_t u8_2d(CUtensorMap* out, void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                         int box_cols) {
+  if (box_cols != 128 || reinterpret_cast<uintptr_t>(base) % 16 != 0 || ld % 16 != 0) return cudaErrorInvalidValue;
+  EncodeFn enc = encoder();
+  if (enc == nullptr) return cudaErrorNotSupported;
+  std::memset(out, 0, sizeof(*out));
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace tmap
 }  // namespace es

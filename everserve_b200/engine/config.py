@@ -26,6 +26,9 @@ class EngineConfig:
     pipeline_parallel: int = 1
     use_cuda_graphs: bool = True
     checkpoint: str | None = None  # a Hugging Face safetensors directory; None: random-init from `seed`
+    # "fp8": the dense projections' weights in e4m3 with one scale per 128 x 128 block, activations
+    # quantized per token and 128-wide block (the block-scaled fp8 GEMM); None: bf16
+    quant: str | None = None
     # mixture models on a peer-memory TP group: route tokens to their experts' owners (all-to-all)
     # instead of running every local expert on every token; ES_MOE_ROUTED=1 sets it
     moe_routed: bool = field(default_factory=lambda: os.environ.get("ES_MOE_ROUTED", "0") == "1")
@@ -36,6 +39,8 @@ class EngineConfig:
             self.model = get_config(self.model)
         if self.block_size not in (16, 32):
             raise ValueError("block_size must be 16 or 32")
+        if self.quant not in (None, "fp8"):
+            raise ValueError(f"unknown quantization {self.quant!r}")
 
     @property
     def world_size(self) -> int:

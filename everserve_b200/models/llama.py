@@ -22,7 +22,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ..ops import interleave_gate_up, ops_for, ref, softmax_scale
+from ..ops import interleave_gate_up, ops_for, quantize_weight_fp8, ref, softmax_scale
 from .config import ModelConfig
 
 
@@ -81,10 +81,17 @@ class TPGroup:
 
 
 class DecoderLM:
+    # the dense projections that take block-scaled fp8 weights in the fp8 configuration
+    FP8_LINEARS = ("qkv", "o", "gate_up", "down")
+
     def __init__(self, cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0,
                  tp: TPGroup | None = None, layer_range: tuple[int, int] | None = None,
-                 init: str = "random"):
+                 init: str = "random", quant: str | None = None):
         self.cfg = cfg
+        # fp8: those weights stored as e4m3 with 128 x 128 block scales (key.q8, key.s8)
+        self.fp8 = quant == "fp8"
+        if self.fp8 and cfg.is_moe:
+            raise ValueError("the fp8 configuration covers dense models")
         self.device = torch.device(device)
         self.dtype = dtype
         self.seed = seed
@@ -138,7 +145,26 @@ class DecoderLM:
     def _put(self, key: str, t: torch.Tensor):
         if self.fused_silu and key.endswith(".gate_up") and ".e" not in key:
             t = interleave_gate_up(t)
+        if self.fp8 and key.rsplit(".", 1)[-1] in self.FP8_LINEARS:
+            q, s = quantize_weight_fp8(t.to(device=self.device, dtype=torch.float32))
+            self.weights[key + ".q8"], self.weights[key + ".s8"] = q.contiguous(), s.contiguous()
+            return
         self.weights[key] = t.to(device=self.device, dtype=self.dtype).contiguous()
+
+    def _linear(self, ops, x, key: str, residual=None):
+        """x . W[key]^T (+ residual) for a bf16 or a block-scaled fp8 weight."""
+        if self.fp8:
+            return ops.linear_fp8(x, self.weights[key + ".q8"], self.weights[key + ".s8"], residual)
+        return ops.linear(x, self.weights[key], residual=residual)
+
+    def _row_parallel(self, ops, x, key: str, residual=None):
+        """A row-parallel projection summed over the tensor-parallel ranks, then the residual."""
+        if not self.fp8:
+            return self.tp.linear_allreduce(ops, x, self.weights[key], residual)
+        if self.tp.size == 1:
+            return self._linear(ops, x, key, residual)
+        y = self.tp.all_reduce(self._linear(ops, x, key))
+        return y if residual is None else (y.float() + residual.float()).to(y.dtype)
 
     def _init_random(self):
         c, d = self.cfg, self.cfg.head_dim
@@ -230,7 +256,7 @@ class DecoderLM:
         for i, l in enumerate(range(self.l0, self.l1)):
             p = f"l{l}."
             cache = caches[i]
-            qkv = ops.linear(h, W[p + "qkv"])
+            qkv = self._linear(ops, h, p + "qkv")
             q = ops.rope_kv_write(qkv, W.get(p + "qkv_bias"), inp.positions, self.cos_sin, inp.slots, cache,
                                   self.hq, self.hkv, bs)
             if inp.is_decode:
@@ -243,16 +269,20 @@ class DecoderLM:
                 a = ops.prefill_attention(q, cache, inp.block_tables, inp.ctx_lens, inp.q_seq, inp.positions,
                                           self.scale, inp.prefill_tiles)
             a = a.reshape(a.shape[0], self.hq * self.d)
-            o = self.tp.linear_allreduce(ops, a, W[p + "o"])
+            o = self._row_parallel(ops, a, p + "o")
             h = ops.rmsnorm(o, W[p + "post_norm"], c.rms_eps, residual)
             if c.is_moe:
                 m = self._moe(h, p)
             else:
-                if self.fused_silu:
+                if self.fp8:
+                    act = ops.linear_fp8(h, W[p + "gate_up.q8"], W[p + "gate_up.s8"], silu=self.fused_silu)
+                    if not self.fused_silu:
+                        act = ops.silu_mul(act)
+                elif self.fused_silu:
                     act = ops.linear_silu(h, W[p + "gate_up"])
                 else:
                     act = ops.silu_mul(ops.linear(h, W[p + "gate_up"]))
-                m = self.tp.linear_allreduce(ops, act, W[p + "down"])
+                m = self._row_parallel(ops, act, p + "down")
             nxt = f"l{l + 1}.in_norm" if l + 1 < self.l1 else None
             if nxt is not None:
                 h = ops.rmsnorm(m, W[nxt], c.rms_eps, residual)

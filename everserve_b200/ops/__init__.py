@@ -16,7 +16,8 @@ import torch
 from . import ref
 from .. import _ext
 
-__all__ = ["KernelOps", "RefOps", "deinterleave_gate_up", "interleave_gate_up", "ops_for", "prefill_tiles", "ref"]
+__all__ = ["KernelOps", "RefOps", "deinterleave_gate_up", "dequantize_fp8", "interleave_gate_up", "ops_for",
+           "prefill_tiles", "quantize_act_fp8", "quantize_weight_fp8", "ref"]
 
 
 class RefOps:
@@ -65,6 +66,16 @@ class RefOps:
 
     def linear_silu(self, x, w):
         return self.silu_mul(self.linear(x, w), interleaved=True)
+
+    def linear_fp8(self, x, w8, w_scale, residual=None, silu: bool = False):
+        """The fp8 GEMM's arithmetic in fp32: activations quantized by the kernel's rule, both
+        operands dequantized, one product (its rounding differs from the kernel's per-block sums)."""
+        q, sc = quantize_act_fp8(x)
+        y = dequantize_fp8(q, sc, 1) @ dequantize_fp8(w8, w_scale, 128).t()
+        if residual is not None:
+            y = y + residual.float()
+        y = y.to(x.dtype)
+        return self.silu_mul(y, interleaved=True) if silu else y
 
     def argmax(self, logits):
         return ref.argmax(logits)
@@ -144,6 +155,24 @@ class KernelOps:
                          valid_cap)
         return out
 
+    def quant_fp8(self, x):
+        """x [M, K] bf16 -> (e4m3 [M, K], fp32 scales [M, K/128]) on the device."""
+        M, K = x.shape
+        q = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
+        sc = torch.empty(M, K // 128, dtype=torch.float32, device=x.device)
+        self.C.quant_fp8(x.contiguous(), q, sc)
+        return q, sc
+
+    def linear_fp8(self, x, w8, w_scale, residual=None, silu: bool = False):
+        """x . w^T for block-scaled e4m3 weights (``quantize_weight_fp8``): the activations quantized
+        per token and 128-wide block, then the tcgen05 fp8 GEMM; `silu` for gate/up interleaved
+        weights (out [M, N/2])."""
+        q, sc = self.quant_fp8(x)
+        N = w8.shape[0]
+        out = torch.empty(x.shape[0], N // 2 if silu else N, dtype=torch.bfloat16, device=x.device)
+        self.C.gemm_fp8(q, sc, w8, w_scale, out, residual, self.status, self.num_sms, silu)
+        return out
+
     def moe_route(self, logits, k, e0, el):
         return self.C.moe_route(logits.contiguous(), k, e0, el)
 
@@ -209,6 +238,42 @@ class KernelOps:
         if v:
             self.status.zero_()
         return v
+
+
+FP8_MAX = 448.0  # largest finite e4m3
+
+
+def quantize_weight_fp8(w: torch.Tensor, block: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+    """[N, K] weight -> (e4m3 [N, K], fp32 scales [ceil(N/128), K/128]): each 128 x 128 block's
+    scale maps its largest magnitude to the e4m3 maximum."""
+    N, K = w.shape
+    assert K % block == 0, "K must be a multiple of 128"
+    nb = (N + block - 1) // block
+    wf = w.float()
+    if N % block:
+        wf = torch.cat([wf, torch.zeros(nb * block - N, K, dtype=wf.dtype, device=wf.device)])
+    blocks = wf.view(nb, block, K // block, block)
+    amax = blocks.abs().amax(dim=(1, 3))
+    scale = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
+    q = (blocks / scale[:, None, :, None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    return q.view(nb * block, K)[:N].contiguous(), scale.contiguous()
+
+
+def dequantize_fp8(q: torch.Tensor, scale: torch.Tensor, rows_per_scale: int, block: int = 128) -> torch.Tensor:
+    """The fp32 values of e4m3 data [R, K] with one scale per (rows_per_scale rows, 128 columns)."""
+    R, K = q.shape
+    s = scale.repeat_interleave(rows_per_scale, dim=0)[:R].repeat_interleave(block, dim=1)
+    return q.float() * s
+
+
+def quantize_act_fp8(x: torch.Tensor, block: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per token and 128-wide block (the kernel's rule, restated): (e4m3 [M, K], fp32 [M, K/128])."""
+    M, K = x.shape
+    xb = x.float().view(M, K // block, block)
+    amax = xb.abs().amax(dim=2)
+    scale = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
+    q = (xb * (1.0 / scale)[:, :, None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    return q.view(M, K), scale
 
 
 def interleave_gate_up(gu: torch.Tensor, run: int = 64) -> torch.Tensor:

@@ -27,6 +27,9 @@ from .slot import HANDLE_BYTES, MAX_ROWS, SlotRegion
 from .symm import PeerMapping, SymmetricBuffer
 
 
+BEAT_PERIOD_US = 500  # how often a member's heartbeat thread advances its beat word
+
+
 class FusedTPCollective:
     """``nvls=True`` pushes through an NVSwitch multicast mapping of the members' buffers (one copy
     leaves each GPU); the buffers then come from torch's symmetric-memory rendezvous and the
@@ -68,7 +71,7 @@ class FusedTPCollective:
             if self.rank != 0:
                 region = SlotRegion.open(name)
         self.region = region
-        self.max_elems = int(self.C.comm_max_elems())
+        self.max_elems = int(self.C.comm_max_elems(len(members) if members is not None else self.size))
         self.two_shot = 1 if os.environ.get("ES_AR_TWO_SHOT", "0") == "1" else 0
         self.nvls = bool(nvls)
         self.mc = 0
@@ -103,6 +106,8 @@ class FusedTPCollective:
                 self.own = self._buf.ptr
                 self._addrs[self.row] = self.own
         self.region.set_pid(self.row, os.getpid())
+        # this member's heartbeat (a native thread): peers' kernels name it dead when it stops
+        self._beat = int(self.C.heartbeat_start(self.region.beat_address(self.row), BEAT_PERIOD_US))
         if not self.nvls:
             name = os.path.basename(self._sock_path(self.row)).encode()
             self.region.publish(self.row, name + bytes(HANDLE_BYTES - len(name)))
@@ -181,17 +186,25 @@ class FusedTPCollective:
         if self.can_take(inp) and out.is_contiguous() and out.data_ptr() % 16 == 0:
             self.C.fdar(inp, out, *self._comm())
             return out
-        if self.nccl is None:
+        if self.nccl is None or inp.dtype == torch.bfloat16:
+            # above one call's size: several calls of the same failure-detecting kernels
             return self._chunked_all_reduce(inp, out)
         if out.data_ptr() != inp.data_ptr():
             out.copy_(inp)
         return self.nccl.all_reduce(out)
 
     def _chunked_all_reduce(self, inp: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        """A tensor above one call's size (or not bf16) in calls the kernels take."""
+        """A tensor above one call's size (or not bf16) in calls the kernels take (in place when
+        both are contiguous bf16: a call reads each chunk of its input before it writes it)."""
+        step = self.max_elems - self.max_elems % 8
+        if (inp.dtype == out.dtype == torch.bfloat16 and inp.is_contiguous() and out.is_contiguous()
+                and inp.data_ptr() % 16 == 0 and out.data_ptr() % 16 == 0):
+            src, dst = inp.reshape(-1), out.reshape(-1)
+            for i in range(0, src.numel(), step):
+                self.C.fdar(src[i : i + step], dst[i : i + step], *self._comm())
+            return out
         src = inp.reshape(-1).to(torch.bfloat16).contiguous()
         dst = torch.empty_like(src)
-        step = self.max_elems - self.max_elems % 8
         for i in range(0, src.numel(), step):
             self.C.fdar(src[i : i + step], dst[i : i + step], *self._comm())
         out.copy_(dst.view(out.shape).to(out.dtype))
@@ -210,7 +223,38 @@ class FusedTPCollective:
             self.C.gemm_allreduce(x, w, out, residual, ops.status, ops.num_sms, *self._comm(), scale, pre,
                                   self.two_shot)
             return out
+        if x.dtype == torch.bfloat16 and not torch.cuda.is_current_stream_capturing():
+            return self._linear_allreduce_overlapped(ops, x, w, residual, scale, pre)
         y = self.all_reduce(ops.linear(x, w, scale=scale, pre=pre))
+        if residual is not None:
+            y = (y.float() + residual.float()).to(y.dtype)
+        return y
+
+    ROW_BLOCK = 512  # rows per GEMM block of an overlapped row-parallel linear
+
+    def _linear_allreduce_overlapped(self, ops, x, w, residual, scale, pre) -> torch.Tensor:
+        """Prefill sizes: the GEMM in blocks of rows, each block's all-reduce on a second stream
+        while the next block's GEMM runs (the same failure-detecting kernels; every member runs
+        the blocks in the same order), then the residual."""
+        M = x.shape[0]
+        y = torch.empty(M, w.shape[0], dtype=x.dtype, device=x.device)
+        main = torch.cuda.current_stream(self.device)
+        if getattr(self, "_comm_stream", None) is None:
+            self._comm_stream = torch.cuda.Stream(self.device)
+        side = self._comm_stream
+        side.wait_stream(main)
+        for r0 in range(0, M, self.ROW_BLOCK):
+            r1 = min(M, r0 + self.ROW_BLOCK)
+            ops.linear(x[r0:r1], w, out=y[r0:r1], scale=None if scale is None else scale[r0:r1],
+                       pre=None if pre is None else pre[r0:r1])
+            ev = torch.cuda.Event()
+            ev.record(main)
+            side.wait_event(ev)
+            with torch.cuda.stream(side):
+                blk = y[r0:r1]
+                self.all_reduce_into(blk, blk)
+        main.wait_stream(side)
+        y.record_stream(side)
         if residual is not None:
             y = (y.float() + residual.float()).to(y.dtype)
         return y
@@ -304,7 +348,15 @@ class FusedTPCollective:
 
         self.C = Counting()
 
+    def set_beat_limit_us(self, us: int) -> None:
+        """Kernels of this member name a peer dead once its beat stands still `us` microseconds
+        (0: off; the bound and the host's checks still apply)."""
+        self.region.set_beat_limit_us([self.row], int(us))
+
     def close(self) -> None:
+        if getattr(self, "_beat", 0):
+            self.C.heartbeat_stop(self._beat)
+            self._beat = 0
         for a in self.attached:
             a.close()
         self.attached = []

@@ -8,7 +8,9 @@ the watchdog and the members exchange on the host:
       +0   abort    u32  host -> device: non-zero makes a kernel waiting on peers leave
       +4   late     u32  device -> host: rows a wait has waited for past `bound` (a bit mask)
       +8   bound_ns u64  host -> device: wait after which late members are named (0: off)
-      +16  status   u32  device -> host: last failure of a collective (1 timeout, 2 aborted)
+      +16  status   u32  device -> host: last failure of a collective (1 timeout, 2 aborted, 4 dead)
+      +20  beat     u32  the member's process: heartbeat counter (a native thread, ~0.5 ms)
+      +24  beat_limit_us u32 host -> device: a peer's beat standing still this long is a death
       +32  pid      i64  the member's process
       +40  step     i64  the step in flight (0: idle) -- the step word the watchdog reads
       +48  lost     u32  set by a watcher that found the member dead
@@ -35,7 +37,7 @@ ROW0 = 4096
 ROW_BYTES = 256
 SIZE = 8192
 
-OFF_ABORT, OFF_LATE, OFF_BOUND, OFF_STATUS = 0, 4, 8, 16
+OFF_ABORT, OFF_LATE, OFF_BOUND, OFF_STATUS, OFF_BEAT, OFF_BEAT_LIMIT = 0, 4, 8, 16, 20, 24
 OFF_PID, OFF_STEP, OFF_LOST, OFF_PUBLISHED = 32, 40, 48, 52
 OFF_ORDER, OFF_HANDLE = 64, 128
 HANDLE_BYTES = 64
@@ -120,6 +122,19 @@ class SlotRegion:
 
     def status(self, row: int) -> int:
         return self.u32(row, OFF_STATUS)
+
+    def beat(self, row: int) -> int:
+        return self.u32(row, OFF_BEAT)
+
+    def beat_address(self, row: int) -> int:
+        """Host address of the row's beat word (what the native heartbeat thread advances)."""
+        import ctypes
+
+        return ctypes.addressof(ctypes.c_char.from_buffer(self.mm)) + self._off(row, OFF_BEAT)
+
+    def set_beat_limit_us(self, rows, us: int) -> None:
+        for r in rows:
+            self.set_u32(r, OFF_BEAT_LIMIT, us)
 
     def set_pid(self, row: int, pid: int) -> None:
         self.set_i64(row, OFF_PID, pid)

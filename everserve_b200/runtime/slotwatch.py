@@ -66,12 +66,14 @@ class SlotWatch:
 
     def __init__(self, region: SlotRegion, row: int, on_lost: Callable[[list[int], str], None],
                  rank_of_row: Callable[[int], int] | None = None, members: Sequence[int] | None = None,
-                 poll_s: float = 0.002, hang_s: float = 10.0, stall_s: float = 5.0):
+                 poll_s: float = 0.002, hang_s: float = 10.0, stall_s: float = 5.0, beat_limit_s: float = 0.0):
         self.region, self.row = region, row
         self.on_lost = on_lost
         self.rank_of_row = rank_of_row or (lambda r: r)
         self.members = list(members) if members is not None else None
         self.poll_s, self.hang_s, self.stall_s = poll_s, hang_s, stall_s
+        self.beat_limit_s = beat_limit_s  # 0: heartbeats not watched
+        self._beats: dict[int, tuple[int, float]] = {}  # row -> (last beat, when it changed)
         self.reported: set[int] = set()
         self.events: list[tuple[float, str, int]] = []
         self._late_since: dict[int, float] = {}
@@ -92,6 +94,7 @@ class SlotWatch:
         self.members = list(rows)
         self.reported &= set(rows)
         self._late_since.clear()
+        self._beats.clear()
 
     def _lost(self, rows: list[int], why: str) -> None:
         rows = [r for r in rows if r not in self.reported]
@@ -123,6 +126,18 @@ class SlotWatch:
         for r in list(self._late_since):
             if r not in rows:
                 del self._late_since[r]
+        # a member whose heartbeat stopped is dead, late or not (its native beat thread ends only
+        # with its process)
+        if self.beat_limit_s > 0 and self.members is not None:
+            for r in self.members:
+                if r == self.row or r in dead or r in self.reported or self.region.pid(r) <= 0:
+                    continue
+                b = self.region.beat(r)
+                last = self._beats.get(r)
+                if last is None or last[0] != b:
+                    self._beats[r] = (b, now)
+                elif now - last[1] > self.beat_limit_s:
+                    dead.append(r)
         if dead:
             self._lost(dead, "dead")
         # a step in flight too long: look at every member's process

@@ -204,6 +204,7 @@ class RankProcess:
             barrier = lambda: self._store_barrier("tp/e0", members)  # noqa: E731
         coll = FusedTPCollective(dev, region=self.region, row=self.row, members=members, barrier=barrier)
         coll.set_bound_ns(self.settings.bound_ns(0.0))
+        coll.set_beat_limit_us(int(self.settings.beat_limit_ms * 1000))
         if not self.spare:
             self._start_watch(coll, members)
             threading.Thread(target=self._premap_spares, args=(coll,), name="premap", daemon=True).start()
@@ -242,7 +243,7 @@ class RankProcess:
         by_row = {row: r for r, row in self.rows.items()}
         self.watch = SlotWatch(self.region, self.row, lost, rank_of_row=lambda row: by_row.get(row, row),
                                members=members, poll_s=self.settings.poll_ms / 1e3,
-                               hang_s=self.settings.hang_s).start()
+                               hang_s=self.settings.hang_s, beat_limit_s=self.settings.beat_limit_ms / 1e3).start()
 
     def _leaked(self, release: str, seconds: float, total: int) -> None:
         """A refused group's release outlived its bound: tell the control plane, which retires this

@@ -5,6 +5,7 @@
 | ``EVERSERVE_DETECT_STEPS`` | 3 | a collective waits this many measured step periods before it names late members |
 | ``EVERSERVE_DETECT_FLOOR_MS`` | 30 | ... but never less than this |
 | ``EVERSERVE_HANG_S`` | 10 | a late member that is alive is hung after this long |
+| ``EVERSERVE_BEAT_LIMIT_MS`` | 20 | a member whose heartbeat stands still this long is dead (kernels and detector; 0 off) |
 | ``EVERSERVE_POLL_MS`` | 2 | the failure detector's poll period |
 | ``EVERSERVE_RELEASE_BOUND_MS`` | 10000 | how long a boundary waits for a refused group's release |
 | ``EVERSERVE_STEP_SAMPLE`` | 16 | steps measured before the bound is set from the step period |
@@ -53,6 +54,7 @@ class Settings:
     detect_steps: float = 3.0
     detect_floor_ms: float = 30.0
     hang_s: float = 10.0
+    beat_limit_ms: float = 20.0
     poll_ms: float = 2.0
     release_bound_ms: float = 10000.0
     step_sample: int = 16
@@ -67,5 +69,6 @@ def load() -> Settings:
     return Settings(
         detect_steps=_f("EVERSERVE_DETECT_STEPS", 3.0), detect_floor_ms=_f("EVERSERVE_DETECT_FLOOR_MS", 30.0),
         hang_s=_f("EVERSERVE_HANG_S", 10.0), poll_ms=_f("EVERSERVE_POLL_MS", 2.0),
+        beat_limit_ms=_f("EVERSERVE_BEAT_LIMIT_MS", 20.0),
         release_bound_ms=_f("EVERSERVE_RELEASE_BOUND_MS", 10000.0), step_sample=int(_f("EVERSERVE_STEP_SAMPLE", 16)),
         node=os.environ.get("EVERSERVE_NODE", socket.gethostname()))

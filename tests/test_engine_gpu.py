@@ -78,3 +78,31 @@ def test_logprobs_on_the_device(cuda):
     assert len(r.logprobs) == 6 and eng.request(other).logprobs == []
     for tok, (lp, top) in zip(r.outputs, r.logprobs):
         assert top[0][0] == tok and abs(lp - top[0][1]) < 1e-5 and len(top) == 4
+
+
+def test_fp8_forward_matches_reference_and_graphs(cuda):
+    """The fp8 configuration on the kernels: block-scaled fp8 GEMMs (SiLU fused) against the same
+    model through the reference ops, and decode graphs against eager steps."""
+    cfg = EngineConfig(TINY_LLAMA, device="cuda", max_batch=8, max_model_len=512, num_blocks=256, quant="fp8",
+                       use_cuda_graphs=False)
+    eng = Engine(cfg)
+    worker = eng.executor.worker
+    eng.add_request([3, 1, 4, 1, 5, 9, 2, 6], SamplingParams(max_tokens=4))
+    plan = eng.scheduler.schedule()
+    runner = worker.runner
+    inp = runner.prefill_input(plan)
+    m = worker.model
+    logits_k = m.logits(inp, runner.caches)
+    kops = m.ops
+    m.ops = RefOps("cuda")
+    try:
+        logits_r = m.logits(inp, [torch.zeros_like(c) for c in runner.caches])
+    finally:
+        m.ops = kops
+    torch.testing.assert_close(logits_k.float(), logits_r.float(), rtol=5e-2, atol=5e-2)
+    outs = []
+    for graphs in (False, True):
+        e = Engine(EngineConfig(TINY_LLAMA, device="cuda", max_batch=8, max_model_len=512, num_blocks=256,
+                                quant="fp8", use_cuda_graphs=graphs))
+        outs.append(e.generate([[1, 2, 3], [7, 7, 7, 7]], max_tokens=6))
+    assert outs[0] == outs[1]

@@ -166,3 +166,29 @@ def test_a_release_past_its_bound_is_reported_as_a_leak():
     assert leaks[0][0] == "epoch 3 groups" and leaks[0][1] >= 0.2 and leaks[0][2] == 1
     time.sleep(0.3)
     assert len(leaks) == 1  # the fast release was no leak
+
+
+def test_slotwatch_names_a_member_whose_heartbeat_stopped(tmp_path, monkeypatch):
+    """A member's beat word that stands still past the limit is a death, even when no kernel has
+    named it late (its process may look alive to /proc for a moment: a zombie, a frozen host)."""
+    import os
+    import time
+
+    from everserve_b200.parallel.slot import OFF_BEAT, SlotRegion
+    from everserve_b200.runtime import slotwatch as sw
+
+    monkeypatch.setenv("EVERSERVE_SHM_DIR", str(tmp_path))
+    region = SlotRegion.create("beats")
+    for row in (0, 1, 2):
+        region.set_pid(row, os.getpid())  # every member "alive" to the /proc check
+    lost = []
+    w = sw.SlotWatch(region, 0, lambda ranks, why: lost.append((ranks, why)), members=[0, 1, 2],
+                     beat_limit_s=0.05)
+    t0 = time.monotonic()
+    while time.monotonic() - t0 < 1.0 and not lost:
+        region.set_u32(2, OFF_BEAT, region.beat(2) + 1)  # row 2 beats, row 1 does not
+        w.check()
+        time.sleep(0.005)
+    assert lost == [([1], "dead")]
+    assert time.monotonic() - t0 < 0.5
+    region.close(unlink=True)
