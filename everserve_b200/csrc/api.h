@@ -66,6 +66,9 @@ struct GemmArgs {
   // gate/up rows interleaved by 64 (tile t: gate rows 64t.., then their up rows): out[M, N/2] =
   // silu(gate) * up of the bf16-rounded products (no residual, scale, pre or valid)
   int silu = 0;
+  // fused reduce-scatter (gemm_allreduce only): the member at position j of the order keeps tokens
+  // [j * rs_per, (j + 1) * rs_per) of the sum, in out/residual rows from 0
+  int64_t rs_per = 0;
 };
 int64_t gemm_pick_bn(int64_t M);
 // the decode split plan (cluster split-K and CTAs per SM) for an N x K bf16 weight at M tokens
@@ -89,6 +92,11 @@ cudaError_t launch_moe_route(const void* logits, int64_t stride, int T, int E, i
 // out = sum over the group's members (member order) of x_r . w_r^T (+ residual): the row-parallel
 // GEMM with its all-reduce fused into the epilogue (decode sizes, M <= 64).
 cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStream_t s);
+// out[M, N] = X . w^T with X the member-order concatenation of every member's [ag_per, K] rows
+// (a.x: this member's), gathered into each member's own buffer (own_base) by the kernel itself:
+// the column-parallel GEMM with its all-gather fused (M = ag_per * members <= 64).
+cudaError_t launch_gemm_allgather(const GemmArgs& a, const CommArgs& c, int64_t ag_per, int64_t members,
+                                  uint64_t own_base, cudaStream_t s);
 
 // ---- moe.cu (expert-parallel all-to-all over peer memory; layout in moe.cu) -----------------------
 struct MoeArgs {

@@ -57,7 +57,17 @@ constexpr size_t kAGFlagOff = kLLResOff + (size_t)2 * kLLGemmBytes;
 constexpr size_t kAGFlagBytes = (size_t)2 * kMaxChunks * 4;                     // [2 parity][chunk] u32
 constexpr size_t kAGOff = kAGFlagOff + ((kAGFlagBytes + 4095) & ~(size_t)4095);
 constexpr size_t kAGBytes = (size_t)kMaxRows * kDataBytes;                      // per parity: a whole call
-constexpr size_t kBufferBytes = kAGOff + (size_t)2 * kAGBytes;
+// All-gather into a GEMM (gemm.cu, kAG): every member's token slice lands, by peer stores of a few
+// pusher CTAs, in every member's gather rows [2 parity][kAGGemmBytes] (rows in member order), and
+// each pusher raises a flag per (parity, sender, pusher) there; the GEMM reads the rows with TMA.
+constexpr int kAGPushers = 16;
+constexpr size_t kAGGemmFlagOff = kAGOff + (size_t)2 * kAGBytes;
+constexpr size_t kAGGemmFlagBytes = 4096;  // [2][kMaxRows][kAGPushers] u32
+constexpr size_t kAGGemmOff = kAGGemmFlagOff + kAGGemmFlagBytes;
+constexpr size_t kAGGemmBytes = (size_t)4 << 20;  // per parity: e.g. 64 rows of K = 16384 bf16 x 2
+constexpr int kAGSeqSlot = 4095;                  // the gathering GEMM's call counter in `seqs` ...
+constexpr int kAGDoneSlot = 4094;                 // ... and its CTAs-done counter
+constexpr size_t kBufferBytes = kAGGemmOff + (size_t)2 * kAGGemmBytes;
 constexpr int kSeqSlots = 4096;  // per-slot LL call counters (this member's device memory)
 constexpr uint64_t kHardLimitNs = 5000000000ull;  // a wait never outlives 5 s
 
@@ -219,6 +229,14 @@ ES_DEVICE int wait_flag(const View& v, const uint32_t* f, uint32_t seq, int send
     }
   }
   return kOk;
+}
+
+ES_DEVICE uint32_t* ag_gemm_flag_ptr(uint64_t base, uint32_t parity, int sender, int pusher) {
+  return reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(base) + kAGGemmFlagOff) +
+         ((size_t)parity * kMaxRows + sender) * kAGPushers + pusher;
+}
+ES_DEVICE char* ag_gemm_ptr(uint64_t base, uint32_t parity) {
+  return reinterpret_cast<char*>(base) + kAGGemmOff + (size_t)parity * kAGGemmBytes;
 }
 
 ES_DEVICE uint32_t* flag_ptr(uint64_t base, uint32_t parity, int sender, int slot) {

@@ -64,7 +64,46 @@ struct Params {
   const uint32_t* valid;       // grouped rows: valid[s] rows of segment s (rows [s*cap, (s+1)*cap)) are live
   int valid_cap, valid_segs;
   int silu;                    // rows gate/up interleaved by 64: out[m, N/2] = silu(gate) * up
+  int rs_per;                  // fused reduce-scatter: member at position j keeps tokens [j*rs_per, (j+1)*rs_per)
+  // fused all-gather: this member's ag_per token rows (ag_x, row stride ag_ldx) go to every member's
+  // gather rows at its position; the GEMM's activations are those rows (K = ag_k)
+  const __nv_bfloat16* ag_x;
+  int ag_per, ag_ldx, ag_k;
 };
+
+// The fused all-gather's wait: every member's pushers have raised their flags for this call in this
+// member's buffer. One thread; `pushers` flags per member, read together (independent loads). Bounded
+// like every peer wait (abort word, the sender's heartbeat, the hard limit).
+ES_DEVICE int wait_gather(const comm::View& cv, uint32_t parity, uint32_t seq, const int* order, int count,
+                          int pushers) {
+  const uint64_t base = cv.peers[cv.row];
+  const uint64_t t0 = global_ns();
+  for (int k = 0; k < count; k++) {
+    const uint32_t* f = comm::ag_gemm_flag_ptr(base, parity, order[k], 0);
+    comm::BeatWatch beat;
+    uint32_t spins = 0;
+    while (true) {
+      uint32_t v[comm::kAGPushers];
+#pragma unroll
+      for (int i = 0; i < comm::kAGPushers; i++) v[i] = i < pushers ? ptx::ld_acquire_gpu(f + i) : seq;
+      bool all = true;
+#pragma unroll
+      for (int i = 0; i < comm::kAGPushers; i++) all = all && v[i] == seq;
+      if (all) break;
+      if ((++spins & 63u) == 0) {
+        volatile comm::Ctrl* c = cv.ctrl;
+        if (c->abort) return kAborted;
+        const uint64_t now = global_ns();
+        if (beat.stopped(cv, order[k], now)) {
+          c->late = c->late | (1u << order[k]);
+          return kDead;
+        }
+        if (now - t0 > comm::kHardLimitNs) return kTimeout;
+      }
+    }
+  }
+  return kOk;
+}
 
 // A token tile [m0, m0 + BN) of a grouped GEMM holds a live row: some segment it overlaps has a
 // count reaching into it. Tiles without one are skipped whole (their output rows are padding).
@@ -118,8 +157,8 @@ ES_DEVICE float4 cluster_sum(uint32_t local, uint32_t off, int S) {
 // kAR: the row-parallel variant whose epilogue sums the tile over the group's members (comm.cuh)
 template <int BN, int CPS, bool kAR>
 __global__ void __launch_bounds__(kThreads, CPS)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, Params p,
-                comm::View cv) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                const __grid_constant__ CUtensorMap tmap_x1, Params p, comm::View cv) {
   using C = Cfg<BN, CPS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -134,6 +173,8 @@ __global__ void __launch_bounds__(kThreads, CPS)
   __shared__ uint32_t s_seq;
   __shared__ int s_order[comm::kMaxRows];
   __shared__ int s_count;
+  __shared__ int s_pos;  // this member's position in the member order (reduce-scatter, all-gather)
+  __shared__ uint32_t s_agseq;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BM;
@@ -171,10 +212,41 @@ __global__ void __launch_bounds__(kThreads, CPS)
     pdl_wait();  // everything below reads what the previous kernel wrote, or writes global memory
     pdl_launch();
   }
-  if (kAR && threadIdx.x == 64) {
+  if ((kAR || p.ag_per) && threadIdx.x == 64) {
     const int cnt = cv.order[0];
     s_count = cnt < 0 ? 0 : (cnt > comm::kMaxRows ? comm::kMaxRows : cnt);
-    for (int i = 0; i < s_count; i++) s_order[i] = cv.order[1 + i];
+    s_pos = -1;
+    for (int i = 0; i < s_count; i++) {
+      s_order[i] = cv.order[1 + i];
+      if (s_order[i] == cv.row) s_pos = i;
+    }
+    if (p.ag_per) s_agseq = cv.seqs[comm::kAGSeqSlot] + 1;
+  }
+  const int n_ctas = (int)(gridDim.x * gridDim.y * gridDim.z);
+  const int pushers = min(comm::kAGPushers, n_ctas);
+  if (p.ag_per) {
+    __syncthreads();  // the order, position and call number above
+    // the first CTAs push this member's rows to every member (its rows at its position), then
+    // raise their flag there; every CTA's producer waits for all of them before its activations
+    const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+    if (lin < pushers && threadIdx.x >= 64 && s_pos >= 0) {
+      const uint32_t parity = s_agseq & 1u;
+      const int vrow = p.ag_k / 8;  // 16-byte vectors per row
+      const int total_v = p.ag_per * vrow;
+      const int v0 = (int)((long long)total_v * lin / pushers), v1 = (int)((long long)total_v * (lin + 1) / pushers);
+      for (int k = 0; k < s_count; k++) {
+        char* dst = comm::ag_gemm_ptr(cv.peers[s_order[k]], parity) + (size_t)s_pos * p.ag_per * p.ag_k * 2;
+        for (int i = v0 + (int)threadIdx.x - 64; i < v1; i += kThreads - 64) {
+          const int r = i / vrow, c = i % vrow;
+          reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(p.ag_x + (size_t)r * p.ag_ldx)[c];
+        }
+      }
+      __threadfence_system();
+      ptx::named_bar(2, kThreads - 64);
+      if (threadIdx.x == 64)
+        for (int k = 0; k < s_count; k++)
+          st_release_sys(comm::ag_gemm_flag_ptr(cv.peers[s_order[k]], parity, cv.row, lin), s_agseq);
+    }
   }
 
   if (producer) {
@@ -193,7 +265,18 @@ __global__ void __launch_bounds__(kThreads, CPS)
     }
     pdl_wait();
     pdl_launch();
-    for (int i = 0; i < pre; i++) ptx::tma_load_2d(b_tiles + i * C::kBBytes, &tmap_x, kblk(i) * BK, m0, &full[i]);
+    const CUtensorMap* xmap = &tmap_x;
+    if (p.ag_per) {
+      // the gathered rows of this call's parity, once every member's pushers have landed them
+      const int r = wait_gather(cv, s_agseq & 1u, s_agseq, s_order, s_count, pushers);
+      if (r != kOk) {
+        s_fail = r;
+        volatile comm::Ctrl* cw = cv.ctrl;
+        cw->status = (uint32_t)r;
+      }
+      if (s_agseq & 1u) xmap = &tmap_x1;
+    }
+    for (int i = 0; i < pre; i++) ptx::tma_load_2d(b_tiles + i * C::kBBytes, xmap, kblk(i) * BK, m0, &full[i]);
     for (int i = pre; i < nkb; i++) {
       const int s = i % C::kStages;
       if (i >= C::kStages && !ptx::mbar_wait(&empty[s], ((i / C::kStages) - 1) & 1)) {
@@ -203,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
       ptx::mbar_arrive_expect_tx(&full[s], C::kStageBytes);
       const int kx = kblk(i) * BK;
       ptx::tma_load_2d(a_tiles + s * C::kABytes, &tmap_w, kx, n0, &full[s]);
-      ptx::tma_load_2d(b_tiles + s * C::kBBytes, &tmap_x, kx, m0, &full[s]);
+      ptx::tma_load_2d(b_tiles + s * C::kBBytes, xmap, kx, m0, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = ptx::idesc_bf16_f32(BM, BN);
@@ -331,7 +414,15 @@ __global__ void __launch_bounds__(kThreads, CPS)
         const size_t widx = ((size_t)(blockIdx.x * BN + col) * BM + row) / 2;
         const uint64_t w0 = ((uint64_t)seq << 32) | ptx::pack_bf16x2(acc.x, acc.y);
         const uint64_t w1 = ((uint64_t)seq << 32) | ptx::pack_bf16x2(acc.z, acc.w);
-        if (p.two_shot) {
+        if (p.rs_per) {
+          // reduce-scatter by tokens: the words of token `col` go to the member keeping it only
+          const int op = col / p.rs_per;
+          if (op < s_count) {
+            uint64_t* d = comm::ll_gemm_ptr(cv.peers[s_order[op]], parity, cv.row) + widx;
+            comm::st_u64_relaxed(d, w0);
+            comm::st_u64_relaxed(d + 1, w1);
+          }
+        } else if (p.two_shot) {
           // reduce-scatter: only the tile's owner takes the partials (1/count of the words a
           // one-shot push sends)
           uint64_t* d = comm::ll_gemm_ptr(cv.peers[s_order[blockIdx.x % s_count]], parity, cv.row) + widx;
@@ -366,13 +457,14 @@ __global__ void __launch_bounds__(kThreads, CPS)
       // the tile's owner sums, then pushes the sums to the others, who poll for them instead.
       const uint64_t my_base = cv.peers[cv.row];
       const int owner_row = s_count > 0 ? s_order[blockIdx.x % s_count] : cv.row;
-      const bool owner = !p.two_shot || owner_row == cv.row;
+      const bool owner = p.rs_per || !p.two_shot || owner_row == cv.row;
       uint64_t t0 = 0;
       bool named = false;
       uint32_t spins = 0;
       int fail = kOk;
       for (int e = threadIdx.x; e < total && fail == kOk; e += kThreads) {
         const int col = e / span4, row = r0 + (e % span4) * 4;
+        if (p.rs_per && col / p.rs_per != s_pos) continue;  // another member keeps this token
         const size_t widx = ((size_t)(blockIdx.x * BN + col) * BM + row) / 2;
         float o[4] = {0.f, 0.f, 0.f, 0.f};
         if (!owner) {
@@ -399,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
           o[3] += hi.y;
         }
         if (fail != kOk) break;
-        if (p.two_shot && owner) {
+        if (p.two_shot && !p.rs_per && owner) {
           // all-gather: the reduced words (rounded to bf16 once, as every member will use them)
           const uint64_t r0w = ((uint64_t)seq << 32) | ptx::pack_bf16x2(o[0], o[1]);
           const uint64_t r1w = ((uint64_t)seq << 32) | ptx::pack_bf16x2(o[2], o[3]);
@@ -416,7 +508,8 @@ __global__ void __launch_bounds__(kThreads, CPS)
           o[2] = hi.x;
           o[3] = hi.y;
         }
-        const size_t m = (size_t)(m0 + col);
+        // reduce-scatter: this member's slice starts at its first token (out and residual rows)
+        const size_t m = (size_t)(m0 + col - (p.rs_per ? s_pos * p.rs_per : 0));
 #pragma unroll
         for (int z = 0; z < 4; z++) {
           const int n = n0 + row + z;
@@ -441,12 +534,22 @@ __global__ void __launch_bounds__(kThreads, CPS)
   if (threadIdx.x == 0) {
     if (s_fail && p.status)
       atomicExch(p.status, (s_fail == kAborted || s_fail == kDead) ? s_fail : (int)kTimeout);
+    if (p.ag_per) {
+      // the last CTA of the call advances the gathering GEMM's call number (every CTA has read it)
+      __threadfence();
+      if (atomicAdd(cv.seqs + comm::kAGDoneSlot, 1u) == (uint32_t)n_ctas - 1) {
+        cv.seqs[comm::kAGDoneSlot] = 0;
+        __threadfence();
+        ptx::st_release_gpu(cv.seqs + comm::kAGSeqSlot, s_agseq);
+      }
+    }
   }
 }
 
 template <int BN, int CPS = (BN <= 64 ? 2 : 1), bool kAR = false>
 cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p, dim3 grid, cudaStream_t stream,
-                   const comm::View& cv = comm::View{}) {
+                   const comm::View& cv = comm::View{}, const CUtensorMap* mx_odd = nullptr) {
+  const CUtensorMap& mx1 = mx_odd ? *mx_odd : mx;  // the gathered rows of odd calls (all-gather GEMM)
   using C = Cfg<BN, CPS>;
   static std::atomic<uint64_t> configured{0};
   cudaError_t e = once_per_device(configured, [] {
@@ -456,7 +559,7 @@ cudaError_t launch(const CUtensorMap& mw, const CUtensorMap& mx, const Params& p
     return cudaFuncSetAttribute(gemm_kernel<BN, CPS, kAR>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   });
   if (e != cudaSuccess) return e;
-  return launch_ex(gemm_kernel<BN, CPS, kAR>, grid, dim3(kThreads), C::kSmem, stream, p.splits, mw, mx, p, cv);
+  return launch_ex(gemm_kernel<BN, CPS, kAR>, grid, dim3(kThreads), C::kSmem, stream, p.splits, mw, mx, mx1, p, cv);
 }
 
 // The largest split whose clusters all fit on the device at once (the fused all-reduce waits on
@@ -644,6 +747,8 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
   p.pre = static_cast<const __nv_bfloat16*>(a.pre);
   p.ldp = (int)a.ldp;
   p.two_shot = c.mc ? 0 : a.two_shot;  // the multicast variant pushes once already
+  p.rs_per = (int)a.rs_per;
+  if (a.rs_per < 0 || (a.rs_per > 0 && c.mc)) return cudaErrorInvalidValue;  // reduce-scatter pushes to one member
   int cps = 1;
   gemm_plan(BN, a.N, a.K, a.num_sms, &p.splits, &cps);
   // every CTA waits on peers: the whole grid must be resident at once
@@ -663,7 +768,7 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
   }
   if (s_fit <= 0) return cudaErrorInvalidConfiguration;
   p.splits = s_fit;
-  if (tiles * p.splits > comm::kSeqSlots) return cudaErrorInvalidValue;
+  if (tiles > comm::kAGDoneSlot) return cudaErrorInvalidValue;  // per-tile call numbers below the gather's
   comm::View v{};
   v.seqs = c.seqs;
   v.peers = c.peers;
@@ -680,6 +785,65 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
   dim3 grid((unsigned)tiles, 1, (unsigned)p.splits);
   return cps == 1 ? gemm::launch<BN, 1, true>(mw, mx, p, grid, stream, v)
                   : gemm::launch<BN, 2, true>(mw, mx, p, grid, stream, v);
+}
+
+}  // namespace es
+
+namespace es {
+
+cudaError_t launch_gemm_allgather(const GemmArgs& a, const CommArgs& c, int64_t ag_per, int64_t members,
+                                  uint64_t own_base, cudaStream_t stream) {
+  constexpr int BN = 64;
+  const int64_t M = ag_per * members;  // the gathered rows, in member order
+  if (ag_per <= 0 || members <= 0 || members > comm::kMaxRows || M > BN || a.N == 0) return cudaErrorInvalidValue;
+  if (a.K % 8 != 0 || (a.ldx * 2) % 16 != 0 || (a.ldw * 2) % 16 != 0 || a.silu || a.valid != nullptr)
+    return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || own_base % 16 != 0 ||
+      c.seqs == nullptr)
+    return cudaErrorInvalidValue;
+  if ((size_t)M * a.K * 2 > comm::kAGGemmBytes) return cudaErrorInvalidValue;
+  const int tiles = (int)((a.N + gemm::BM - 1) / gemm::BM);
+  gemm::Params p{};
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.residual = static_cast<const __nv_bfloat16*>(a.residual);
+  p.status = a.status;
+  p.M = (int)M;
+  p.N = (int)a.N;
+  p.ldo = (int)a.ldo;
+  p.ldr = (int)a.ldr;
+  p.kb = (int)((a.K + gemm::BK - 1) / gemm::BK);
+  p.scale = a.scale;
+  p.pre = static_cast<const __nv_bfloat16*>(a.pre);
+  p.ldp = (int)a.ldp;
+  p.ag_x = static_cast<const __nv_bfloat16*>(a.x);
+  p.ag_per = (int)ag_per;
+  p.ag_ldx = (int)a.ldx;
+  p.ag_k = (int)a.K;
+  int cps = 1;
+  gemm_plan(BN, a.N, a.K, a.num_sms, &p.splits, &cps);
+  // every CTA waits for the pushers of every member: the whole grid must be resident at once
+  const int s_fit = cps == 1 ? gemm::resident_split<BN, 1>(tiles, p.splits) : gemm::resident_split<BN, 2>(tiles, p.splits);
+  if (s_fit <= 0) return cudaErrorInvalidConfiguration;
+  p.splits = s_fit;
+  comm::View v{};
+  v.seqs = c.seqs;
+  v.peers = c.peers;
+  v.order = c.order;
+  v.call = c.call;
+  v.ctrl = reinterpret_cast<comm::Ctrl*>(c.ctrl);
+  v.row = c.row;
+  // the gathered rows live in this member's own buffer, one region per call parity
+  CUtensorMap mw, mx0, mx1;
+  cudaError_t e = tmap::bf16_2d(&mw, const_cast<void*>(a.w), a.N, a.K, a.ldw, gemm::BM, gemm::BK);
+  if (e != cudaSuccess) return e;
+  char* rows = reinterpret_cast<char*>(own_base) + comm::kAGGemmOff;
+  e = tmap::bf16_2d(&mx0, rows, M, a.K, a.K, BN, gemm::BK);
+  if (e != cudaSuccess) return e;
+  e = tmap::bf16_2d(&mx1, rows + comm::kAGGemmBytes, M, a.K, a.K, BN, gemm::BK);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)tiles, 1, (unsigned)p.splits);
+  return cps == 1 ? gemm::launch<BN, 1, false>(mw, mx0, p, grid, stream, v, &mx1)
+                  : gemm::launch<BN, 2, false>(mw, mx0, p, grid, stream, v, &mx1);
 }
 
 }  // namespace es

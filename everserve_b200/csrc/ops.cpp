@@ -398,14 +398,14 @@ void fdar(torch::Tensor inp, torch::Tensor out, torch::Tensor peers, torch::Tens
 void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
                     torch::Tensor status, int64_t num_sms, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
                     int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs, c10::optional<torch::Tensor> scale,
-                    c10::optional<torch::Tensor> pre, int64_t two_shot) {
+                    c10::optional<torch::Tensor> pre, int64_t two_shot, int64_t rs_per) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D operands");
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "K-contiguous operands");
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
-  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N, "shapes");
+  TORCH_CHECK(w.size(1) == K && out.size(1) == N && out.size(0) == (rs_per > 0 ? rs_per : M), "shapes");
   TORCH_CHECK(M <= 64, "the fused all-reduce GEMM takes decode batches (M <= 64)");
   es::GemmArgs a{};
   a.x = x.data_ptr();
@@ -421,15 +421,51 @@ void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::op
   a.num_sms = (int)num_sms;
   if (residual.has_value()) {
     check_bf16(*residual, "residual");
-    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N && residual->stride(1) == 1, "residual shape");
+    TORCH_CHECK(residual->size(0) == out.size(0) && residual->size(1) == N && residual->stride(1) == 1,
+                "residual shape (out's rows)");
     a.residual = residual->data_ptr();
     a.ldr = residual->stride(0);
   }
   mixture_terms(a, scale, pre);
   a.two_shot = (int)two_shot;
+  a.rs_per = rs_per;
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_allreduce(a, comm_args(peers, order, call, ctrl, row, mc, seqs), cur()));
 }
+
+void gemm_allgather(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
+                    torch::Tensor status, int64_t num_sms, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
+                    int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs, int64_t members, int64_t own_base) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(out, "out");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D operands");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "K-contiguous operands");
+  const int64_t per = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && out.size(0) == per * members && out.size(1) == N, "shapes: out is [per * members, N]");
+  es::GemmArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.out = out.data_ptr();
+  a.M = per * members;
+  a.N = N;
+  a.K = K;
+  a.ldx = x.stride(0);
+  a.ldw = w.stride(0);
+  a.ldo = out.stride(0);
+  a.status = status.data_ptr<int>();
+  a.num_sms = (int)num_sms;
+  if (residual.has_value() && residual->defined()) {
+    check_bf16(*residual, "residual");
+    TORCH_CHECK(residual->size(0) == a.M && residual->size(1) == N && residual->stride(1) == 1, "residual shape");
+    a.residual = residual->data_ptr();
+    a.ldr = residual->stride(0);
+  }
+  const c10::cuda::CUDAGuard g(x.device());
+  ES_CHECK_CUDA(es::launch_gemm_allgather(a, comm_args(peers, order, call, ctrl, row, mc, seqs), per, members,
+                                          (uint64_t)own_base, cur()));
+}
+
 
 void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
                   torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor status,
@@ -695,7 +731,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("num_sms"), pybind11::arg("peers"), pybind11::arg("order"), pybind11::arg("call"),
         pybind11::arg("ctrl"), pybind11::arg("row"), pybind11::arg("mc"), pybind11::arg("seqs"),
         pybind11::arg("scale") = pybind11::none(), pybind11::arg("pre") = pybind11::none(),
-        pybind11::arg("two_shot") = 0);
+        pybind11::arg("two_shot") = 0, pybind11::arg("rs_per") = 0);
+  m.def("gemm_allgather", &gemm_allgather,
+        "column-parallel GEMM with the all-gather of its token rows fused (peer stores into each member's buffer)");
   m.def("comm_buffer_bytes", &es::comm_buffer_bytes);
   m.def("comm_max_elems", &es::comm_max_elems, "elements one all-reduce call takes for a group of `members`",
         pybind11::arg("members") = 1);

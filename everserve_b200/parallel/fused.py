@@ -230,6 +230,42 @@ class FusedTPCollective:
             y = (y.float() + residual.float()).to(y.dtype)
         return y
 
+    def linear_reduce_scatter(self, ops, x: torch.Tensor, w: torch.Tensor, residual=None) -> torch.Tensor:
+        """Row-parallel linear whose sum over the members is reduce-scattered by tokens: the member at
+        position j keeps tokens [j * per, (j + 1) * per), per = ceil(M / members), as [per, N] (rows
+        past M are padding), plus `residual` (its own [per, N] slice). One fused kernel at decode
+        sizes (the sum's words go to the member keeping the token only)."""
+        M, n = x.shape[0], len(self.members)
+        per = -(-M // n)
+        pos = self.members.index(self.row)
+        out = torch.empty(per, w.shape[0], dtype=x.dtype, device=x.device)
+        if M <= 64 and x.dtype == torch.bfloat16 and not self.nvls:
+            self.C.gemm_allreduce(x, w, out, residual, ops.status, ops.num_sms, *self._comm(), None, None, 0, per)
+            return out
+        full = self.linear_allreduce(ops, x, w)
+        out.zero_()
+        lo, hi = min(M, pos * per), min(M, (pos + 1) * per)
+        out[: hi - lo] = full[lo:hi]
+        if residual is not None:
+            out = (out.float() + residual.float()).to(out.dtype)
+        return out
+
+    def gather_linear(self, ops, x: torch.Tensor, w: torch.Tensor, residual=None) -> torch.Tensor:
+        """Column-parallel linear over the member-order concatenation of every member's token rows
+        ([per, K] here, the same per on every member): [per * members, N]. One fused kernel at
+        decode sizes (the rows reach every member's own buffer by peer stores inside the GEMM, whose
+        activation tiles then come from local memory)."""
+        per, n = x.shape[0], len(self.members)
+        out = torch.empty(per * n, w.shape[0], dtype=x.dtype, device=x.device)
+        if per * n <= 64 and x.dtype == torch.bfloat16 and not self.nvls and x.stride(1) == 1:
+            self.C.gemm_allgather(x, w, out, residual, ops.status, ops.num_sms, *self._comm(), n, self.own)
+            return out
+        rows = torch.zeros(per * n, x.shape[1], dtype=x.dtype, device=x.device)
+        pos = self.members.index(self.row)
+        rows[pos * per : (pos + 1) * per] = x
+        self.all_reduce_into(rows, rows)  # disjoint rows: the sum is the gather, exactly
+        return ops.linear(rows, w, residual=residual)
+
     ROW_BLOCK = 512  # rows per GEMM block of an overlapped row-parallel linear
 
     def _linear_allreduce_overlapped(self, ops, x, w, residual, scale, pre) -> torch.Tensor:

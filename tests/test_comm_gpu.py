@@ -94,6 +94,27 @@ def _worker(rank: int, world: int, port: int, results, nvls: bool = False):
                 ok &= bool(torch.allclose(f2.float(), ref.member_sum(ps2).float(), rtol=2e-2, atol=2e-2))
         out["alternating_splits_close"] = ok
         out["status"] += coll.status() + kops.check_status()
+        # 2c. the fused reduce-scatter and all-gather GEMMs (the sequence-parallel pair) against fp32
+        ok_rs = ok_ag = True
+        for it, M in enumerate((64, 37, 8)):
+            K, N = 1024, 2048
+            xs_r = [torch.randn(M, K, generator=torch.Generator().manual_seed(300 + 7 * it + r)).bfloat16()
+                    for r in range(world)]
+            ws_r = [(torch.randn(N, K, generator=torch.Generator().manual_seed(400 + 7 * it + r)) / 32).bfloat16()
+                    for r in range(world)]
+            per = -(-M // world)
+            rs = coll.linear_reduce_scatter(kops, xs_r[rank].to(dev), ws_r[rank].to(dev))
+            full = sum(x.float() @ wr.float().t() for x, wr in zip(xs_r, ws_r))
+            lo, hi = min(M, rank * per), min(M, (rank + 1) * per)
+            ok_rs &= bool(torch.allclose(rs[: hi - lo].float().cpu(), full[lo:hi], rtol=2e-2, atol=3e-2))
+            # every member's own rows, gathered in member order, times this member's weight
+            mine = [torch.randn(per, K, generator=torch.Generator().manual_seed(500 + 7 * it + r)).bfloat16()
+                    for r in range(world)]
+            ag = coll.gather_linear(kops, mine[rank].to(dev), ws_r[rank].to(dev))
+            want = torch.cat(mine).float() @ ws_r[rank].float().t()
+            ok_ag &= bool(torch.allclose(ag.float().cpu(), want, rtol=2e-2, atol=3e-2))
+        out["rs_close"], out["ag_close"] = ok_rs, ok_ag
+        out["status"] += coll.status() + kops.check_status()
         # 3. a member that never enters the call: named late, released by the abort word (P2P only:
         # no member of an NVLS group is ever left behind on this pool)
         torch.cuda.synchronize()
@@ -158,6 +179,8 @@ def test_peer_collectives(nvls):
         assert o["fdar_exact"], o
         assert o["gemm_ar_close"] and o["gemm_ar_same_on_ranks"] and o["gemm_ar_oracle"], o
         assert o["alternating_splits_close"], o
+        if not nvls:
+            assert o["rs_close"] and o["ag_close"], o
         assert o["status"] == 0, o
         if not nvls:
             assert o["after_resume"], o

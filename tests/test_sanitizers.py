@@ -4,6 +4,7 @@ and with ThreadSanitizer (`make -C cpp asan tsan`), run through the same tests a
 A sanitizer report ends the binary with an error, which fails the tests it serves."""
 
 import os
+import shutil
 import subprocess
 import sys
 
@@ -23,7 +24,12 @@ def test_control_plane_under_sanitizer(kind):
     assert unit.returncode == 0, unit.stderr[-2000:]
     env = dict(os.environ, EVERSERVE_CPP_BIN=bindir, ASAN_OPTIONS="detect_leaks=0:abort_on_error=0",
                TSAN_OPTIONS="halt_on_error=1:exitcode=66", UBSAN_OPTIONS="halt_on_error=1")
-    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-p", "no:cacheprovider",
-                        "tests/test_wire_golden.py", "tests/test_store.py", "tests/test_compile_cache.py"],
-                       cwd=ROOT, env=env, capture_output=True, text=True, timeout=1200)
+    try:
+        r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-p", "no:cacheprovider",
+                            "tests/test_wire_golden.py", "tests/test_store.py", "tests/test_compile_cache.py"],
+                           cwd=ROOT, env=env, capture_output=True, text=True, timeout=1200)
+    finally:
+        # the sanitizer builds are large; the plain build is the one the tree keeps
+        for d in (bindir, os.path.join(ROOT, "cpp", f"build-{kind}")):
+            shutil.rmtree(d, ignore_errors=True)
     assert r.returncode == 0, (r.stdout[-3000:], r.stderr[-3000:])
