@@ -270,7 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // x [M, K] bf16 -> x8 [M, K] e4m3 and x_scale [M, K / 128]: per token and 128-wide block, the scale
-// maps the block's largest magnitude to the e4m3 maximum (448). One warp per (token, block).
+// maps the block's largest magnitude to the e4m3 maximum (scale = amax * (1/448), values multiplied
+// by 1/scale). One warp per (token, block).
 __global__ void quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, uint8_t* __restrict__ x8,
                              int64_t ld8, float* __restrict__ scale, int64_t lds, int M, int K) {
   pdl_wait();
@@ -289,7 +290,7 @@ __global__ void quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, u
     amax = fmaxf(amax, fabsf(f[i]));
   }
   amax = warp_max(amax);
-  const float s = amax > 0.f ? amax / 448.f : 1.f;
+  const float s = amax > 0.f ? amax * (1.f / 448.f) : 1.f;
   const float inv = 1.f / s;
   uint32_t packed = 0;
 #pragma unroll

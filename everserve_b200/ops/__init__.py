@@ -271,7 +271,7 @@ def quantize_act_fp8(x: torch.Tensor, block: int = 128) -> tuple[torch.Tensor, t
     M, K = x.shape
     xb = x.float().view(M, K // block, block)
     amax = xb.abs().amax(dim=2)
-    scale = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
+    scale = torch.where(amax > 0, amax * (1.0 / FP8_MAX), torch.ones_like(amax))
     q = (xb * (1.0 / scale)[:, :, None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
     return q.view(M, K), scale
 
