@@ -225,6 +225,8 @@ def main() -> None:
     ap.add_argument("--max-tokens", type=int, default=512)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--collective", default="fused", choices=["fused", "nccl"])
+    ap.add_argument("--sp", action="store_true",
+                    help="sequence-parallel decode (token-sliced norms; reduce-scatter and all-gather GEMMs)")
     ap.add_argument("--commit", default="store", choices=["store", "off"],
                     help="store: every step's KV rows and counts are committed to everserve-store (the "
                          "serving configuration); off: no commit (for comparison)")
@@ -268,7 +270,7 @@ def main() -> None:
     num_blocks = args.batch * (-(-max_len // block_size)) + 64
     cfg = EngineConfig(args.model, device=str(dev), max_batch=args.batch, max_model_len=max_len,
                        max_prefill_tokens=8192, tensor_parallel=world, seed=args.seed, num_blocks=num_blocks,
-                       block_size=block_size)
+                       block_size=block_size, sequence_parallel=args.sp and world > 1)
     ex = LocalExecutor(cfg, rank=rank, collective=collective)
     connector = None
     store = None
@@ -359,7 +361,8 @@ def main() -> None:
         "data": "synthetic: uniform-random 1024-token prompts (seed 0), random-init weights",
         "config": {"model": "Llama-3-8B architecture (32 layers, hidden 4096, 32/8 heads, d 128, ffn 14336, "
                             "vocab 128256)", "global_batch": args.batch, "seq_len": args.prompt_len,
-                   "parallelism": f"tp{world}", "collective": args.collective if world > 1 else "none",
+                   "parallelism": f"tp{world}" + ("-sp" if args.sp and world > 1 else ""),
+                   "collective": args.collective if world > 1 else "none",
                    "l2": "inputs larger than L2 (16 GB of weights / TP and the KV history read every step)"},
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": runner.h2d_bytes,
                 "d2h_bytes_per_step": args.batch * 8},

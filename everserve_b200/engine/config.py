@@ -29,6 +29,9 @@ class EngineConfig:
     # "fp8": the dense projections' weights in e4m3 with one scale per 128 x 128 block, activations
     # quantized per token and 128-wide block (the block-scaled fp8 GEMM); None: bf16
     quant: str | None = None
+    # tensor-parallel ranks keep the residual stream of their token slice (norms on the slice,
+    # reduce-scatter GEMMs for o/down, all-gather GEMMs for qkv/gate_up/vocabulary); ES_SP=1 sets it
+    sequence_parallel: bool = field(default_factory=lambda: os.environ.get("ES_SP", "0") == "1")
     # mixture models on a peer-memory TP group: route tokens to their experts' owners (all-to-all)
     # instead of running every local expert on every token; ES_MOE_ROUTED=1 sets it
     moe_routed: bool = field(default_factory=lambda: os.environ.get("ES_MOE_ROUTED", "0") == "1")

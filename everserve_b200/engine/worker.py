@@ -39,7 +39,8 @@ class Worker:
         layers = stage_layers(cfg.model.layers, pp, self.stage)
         init = "none" if (cfg.checkpoint or weights is not None) else "random"
         self.model = DecoderLM(cfg.model, self.device, cfg.dtype, cfg.seed, self.tp, layers, init=init,
-                               quant=getattr(cfg, "quant", None))
+                               quant=getattr(cfg, "quant", None),
+                               sequence_parallel=getattr(cfg, "sequence_parallel", False))
         if weights is not None:  # a resident copy (pinned host memory): copied in, no init
             for k, t in weights.items():
                 self.model._put(k, t)

@@ -79,6 +79,43 @@ class TPGroup:
             return t
         return self.collective.all_gather(t)
 
+    # ---- the sequence-parallel pair: token slices between the projections ----------------------
+    def token_slice(self, M: int) -> tuple[int, int, int]:
+        """(per, first, last): this rank keeps tokens [first, last) of M, per = ceil(M / size)."""
+        per = -(-M // self.size)
+        return per, min(M, self.rank * per), min(M, (self.rank + 1) * per)
+
+    def gather_rows(self, t: torch.Tensor) -> torch.Tensor:
+        """Every rank's [per, K] rows, in rank order: [per * size, K]."""
+        if self.size == 1:
+            return t
+        flat = self.collective.all_gather(t.reshape(1, -1).contiguous())
+        return flat.reshape(self.size * t.shape[0], t.shape[1])
+
+    def gather_linear(self, ops, x_local, w):
+        """Column-parallel linear over every rank's token rows (rank order): [per * size, N]; the
+        all-gather fused into the GEMM when the collective has it."""
+        if self.size == 1:
+            return ops.linear(x_local, w)
+        fused = getattr(self.collective, "gather_linear", None)
+        if fused is not None and ops.kind == "kernel":
+            return fused(ops, x_local, w)
+        return ops.linear(self.gather_rows(x_local), w)
+
+    def reduce_scatter_linear(self, ops, x, w):
+        """Row-parallel linear whose sum over the ranks this rank keeps for its token slice only:
+        [per, N] (rows past the tokens are padding); fused into the GEMM when the collective has it."""
+        if self.size == 1:
+            return ops.linear(x, w)
+        fused = getattr(self.collective, "linear_reduce_scatter", None)
+        if fused is not None and ops.kind == "kernel":
+            return fused(ops, x, w)
+        y = self.collective.all_reduce(ops.linear(x, w))
+        per, lo, hi = self.token_slice(x.shape[0])
+        out = torch.zeros(per, y.shape[1], dtype=y.dtype, device=y.device)
+        out[: hi - lo] = y[lo:hi]
+        return out
+
 
 class DecoderLM:
     # the dense projections that take block-scaled fp8 weights in the fp8 configuration
@@ -86,7 +123,7 @@ class DecoderLM:
 
     def __init__(self, cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0,
                  tp: TPGroup | None = None, layer_range: tuple[int, int] | None = None,
-                 init: str = "random", quant: str | None = None):
+                 init: str = "random", quant: str | None = None, sequence_parallel: bool = False):
         self.cfg = cfg
         # fp8: those weights stored as e4m3 with 128 x 128 block scales (key.q8, key.s8)
         self.fp8 = quant == "fp8"
@@ -102,6 +139,10 @@ class DecoderLM:
         self.l0, self.l1 = layer_range or (0, cfg.layers)
         self.first = self.l0 == 0
         self.last = self.l1 == cfg.layers
+        # token-sliced residual stream between the projections (one stage, dense, bf16 weights)
+        self.sequence_parallel = bool(sequence_parallel) and self.tp.size > 1
+        if self.sequence_parallel and (cfg.is_moe or quant or not (self.first and self.last)):
+            raise ValueError("sequence parallelism covers single-stage dense bf16 models")
         T, r = self.tp.size, self.tp.rank
         assert cfg.heads % T == 0, "query heads must divide by the tensor-parallel size"
         self.hq = cfg.heads // T
@@ -245,6 +286,8 @@ class DecoderLM:
     def forward(self, inp: StepInput, caches: list[torch.Tensor], hidden: torch.Tensor | None = None,
                 residual: torch.Tensor | None = None):
         """Run this stage. Returns (hidden, residual) for a middle stage, next-token ids for the last."""
+        if self.sequence_parallel:
+            return self._forward_sp(inp, caches)
         ops, c, W = self.ops, self.cfg, self.weights
         if self.first:
             x = self.embed(inp.ids)
@@ -294,6 +337,60 @@ class DecoderLM:
         h_last = h.index_select(0, inp.logits_idx) if h.shape[0] != inp.logits_idx.shape[0] else h
         head = W["embed"] if c.tie_embeddings else W["lm_head"]
         logits = ops.linear(h_last, head)
+        ids = self._sample(logits, inp) if inp.sampling is not None else self._greedy(logits)
+        if inp.logprobs_k is not None:
+            self.step_logprobs = self._logprobs(logits, ids, inp.logprobs_k)
+        return ids
+
+    def _forward_sp(self, inp: StepInput, caches: list[torch.Tensor]):
+        """The sequence-parallel forward: each rank keeps the residual stream of its slice of the
+        step's tokens and runs the norms there; the column-parallel projections (qkv, gate_up, the
+        vocabulary) take every rank's normalised rows through the all-gather fused into their GEMM,
+        the row-parallel ones (o, down) reduce-scatter their sums by tokens in their GEMM's epilogue.
+        Attention still sees every token of the rank's heads. The bytes on the links equal the
+        all-reduce forward's; the norms and residual adds run on a 1/size slice, and each collective
+        overlaps its own GEMM's weight streaming."""
+        ops, c, W = self.ops, self.cfg, self.weights
+        M = inp.ids.shape[0]
+        per, lo, hi = self.tp.token_slice(M)
+        x = self.embed(inp.ids)
+        residual = torch.zeros(per, c.hidden, dtype=x.dtype, device=x.device)
+        residual[: hi - lo] = x[lo:hi]
+        h = ops.rmsnorm(residual, W[f"l{self.l0}.in_norm"], c.rms_eps)
+        bs = caches[0].shape[3] if caches else 16
+        hidden = None
+        for i, l in enumerate(range(self.l0, self.l1)):
+            p = f"l{l}."
+            cache = caches[i]
+            qkv = self.tp.gather_linear(ops, h, W[p + "qkv"])[:M]  # the first M rows: contiguous
+            q = ops.rope_kv_write(qkv, W.get(p + "qkv_bias"), inp.positions, self.cos_sin, inp.slots, cache,
+                                  self.hq, self.hkv, bs)
+            if inp.is_decode:
+                if ops.kind == "kernel":
+                    a = ops.decode_attention(q, cache, inp.block_tables, inp.ctx_lens, self.scale,
+                                             inp.max_model_len or None)
+                else:
+                    a = ops.decode_attention(q, cache, inp.block_tables, inp.ctx_lens, self.scale)
+            else:
+                a = ops.prefill_attention(q, cache, inp.block_tables, inp.ctx_lens, inp.q_seq, inp.positions,
+                                          self.scale, inp.prefill_tiles)
+            a = a.reshape(M, self.hq * self.d)
+            o = self.tp.reduce_scatter_linear(ops, a, W[p + "o"])
+            h = ops.rmsnorm(o, W[p + "post_norm"], c.rms_eps, residual)
+            gu = self.tp.gather_linear(ops, h, W[p + "gate_up"])[:M].contiguous()
+            act = ops.silu_mul(gu, interleaved=self.fused_silu)
+            m = self.tp.reduce_scatter_linear(ops, act, W[p + "down"])
+            if l + 1 < self.l1:
+                h = ops.rmsnorm(m, W[f"l{l + 1}.in_norm"], c.rms_eps, residual)
+            else:
+                hidden = m
+        h = ops.rmsnorm(hidden, W["final_norm"], c.rms_eps, residual)
+        head = W["embed"] if c.tie_embeddings else W["lm_head"]
+        if inp.is_decode and M <= 64 and inp.logits_idx.shape[0] == M:
+            logits = self.tp.gather_linear(ops, h, head)[:M]
+        else:
+            rows = self.tp.gather_rows(h)[:M]
+            logits = ops.linear(rows.index_select(0, inp.logits_idx), head)
         ids = self._sample(logits, inp) if inp.sampling is not None else self._greedy(logits)
         if inp.logprobs_k is not None:
             self.step_logprobs = self._logprobs(logits, ids, inp.logprobs_k)

@@ -3,6 +3,8 @@
     python -m everserve_b200.perf.ncu_case --kernel gemm [--n 28672 --k 4096 --m 64]
     python -m everserve_b200.perf.ncu_case --kernel attn [--batch 64 --ctx 1024]
     python -m everserve_b200.perf.ncu_case --kernel prefill [--batch 16 --ctx 1024]
+    python -m everserve_b200.perf.ncu_case --kernel gemm_ar|fdar [--n 4096 --k 512 --m 64]  (a one-member group)
+    python -m everserve_b200.perf.ncu_case --kernel fp8 [--n 28672 --k 4096 --m 64]
     python -m everserve_b200.perf.ncu_case --kernel norm|rope|silu|argmax|kvgather
 
 Each case allocates a few hundred MB at most (operands larger than the 126 MB L2 where the kernel
@@ -24,7 +26,8 @@ from ..ops import KernelOps
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
-                    choices=["gemm", "attn", "prefill", "norm", "rope", "silu", "argmax", "kvgather"])
+                    choices=["gemm", "attn", "prefill", "norm", "rope", "silu", "argmax", "kvgather", "gemm_ar", "fdar",
+                             "fp8"])
     ap.add_argument("--m", type=int, default=64)
     ap.add_argument("--n", type=int, default=28672)
     ap.add_argument("--k", type=int, default=4096)
@@ -67,6 +70,36 @@ def main() -> None:
         tiles = prefill_tiles(seq, pos, device=dev)
         qs, ps = torch.tensor(seq, device=dev), torch.tensor(pos, device=dev)
         run = lambda: ops.prefill_attention(q, cache, bt, cl, qs, ps, 1 / math.sqrt(d), tiles)  # noqa: E731
+    elif a.kernel in ("gemm_ar", "fdar"):
+        # the fused GEMM + all-reduce (or the all-reduce alone) in a group of one member on this GPU:
+        # the kernel's full code path, its pushes going to this member's own buffer
+        import os
+        import socket
+
+        import torch.distributed as dist
+
+        from ..parallel.fused import FusedTPCollective
+
+        sk = socket.socket()
+        sk.bind(("127.0.0.1", 0))
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(sk.getsockname()[1]))
+        sk.close()
+        dist.init_process_group("gloo", rank=0, world_size=1)
+        coll = FusedTPCollective(dev)
+        if a.kernel == "gemm_ar":
+            w = torch.randn(a.n, a.k, device=dev, generator=g).bfloat16()
+            x = torch.randn(a.m, a.k, device=dev, generator=g).bfloat16()
+            run = lambda: coll.linear_allreduce(ops, x, w)  # noqa: E731
+        else:
+            v = torch.randn(a.m * a.n, device=dev, generator=g).bfloat16()
+            run = lambda: coll.all_reduce_into(v, v)  # noqa: E731
+    elif a.kernel == "fp8":
+        from ..ops import quantize_weight_fp8
+
+        w8, ws = quantize_weight_fp8(torch.randn(a.n, a.k, device=dev, generator=g) / 64)
+        x = torch.randn(a.m, a.k, device=dev, generator=g).bfloat16()
+        run = lambda: ops.linear_fp8(x, w8, ws)  # noqa: E731
     elif a.kernel == "norm":
         x = torch.randn(a.batch * 64, 4096, device=dev, generator=g).bfloat16()
         r = torch.randn_like(x)
