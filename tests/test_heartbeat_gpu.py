@@ -7,6 +7,7 @@ still), or on the host's abort word when it is not. Both are bounded waits that 
 nothing traps and the context stays usable.
 """
 
+import os
 import threading
 import time
 
@@ -22,13 +23,13 @@ DEAD, ABORTED = 4, 2
 
 
 @pytest.fixture
-def pair(tmp_path, monkeypatch):
+def pair():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    monkeypatch.setenv("EVERSERVE_SHM_DIR", str(tmp_path))
     C = _ext.load()
     dev = torch.device("cuda:0")
-    region = SlotRegion.create("hb")
+    # the region must live in shared memory (the device maps its pages)
+    region = SlotRegion.create(f"es_hb_test_{os.getpid()}")
     region.map_device(C)
     nbytes = int(C.comm_buffer_bytes())
     bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=dev) for _ in range(2)]
