@@ -21,6 +21,22 @@ cudaError_t launch_embed(const int64_t* ids, const void* table, void* out, int64
                          cudaStream_t s);
 cudaError_t launch_decode_advance(int64_t* st, const int64_t* sampled, const int* bt, int64_t bt_stride, int b, int B,
                                   int bs, cudaStream_t s);
+// Seeded temperature / top-k / top-p sampling of each row (sampling.cu).
+struct SampleArgs {
+  const void* logits = nullptr;  // [rows, >= vocab] bf16 (or fp32 when fp32), rows `stride` apart
+  bool fp32 = false;
+  int64_t stride = 0;
+  int vocab = 0;
+  int64_t rows = 0;
+  const int64_t* positions = nullptr;
+  const float* temperature = nullptr;  // <= 0: greedy
+  const int64_t* top_k = nullptr;      // <= 0: off
+  const float* top_p = nullptr;        // >= 1: off
+  const int64_t* seeds = nullptr;
+  int64_t* out = nullptr;
+};
+cudaError_t launch_sample(const SampleArgs& a, cudaStream_t stream);
+
 cudaError_t launch_argmax(const void* logits, int64_t* out, int64_t rows, int vocab, int64_t stride, cudaStream_t s);
 
 // ---- comm.cu (peer-memory collectives; layout in comm.cuh) ----------------------------------
@@ -69,6 +85,8 @@ struct GemmArgs {
   // fused reduce-scatter (gemm_allreduce only): the member at position j of the order keeps tokens
   // [j * rs_per, (j + 1) * rs_per) of the sum, in out/residual rows from 0
   int64_t rs_per = 0;
+  // the weight pre-packed by (128-row tile, 64-wide k-block) into swizzled 16 KB blocks (nullable)
+  const void* w_packed = nullptr;
 };
 int64_t gemm_pick_bn(int64_t M);
 // the decode split plan (cluster split-K and CTAs per SM) for an N x K bf16 weight at M tokens

@@ -69,6 +69,9 @@ struct Params {
   // gather rows at its position; the GEMM's activations are those rows (K = ag_k)
   const __nv_bfloat16* ag_x;
   int ag_per, ag_ldx, ag_k;
+  // weights pre-packed per (tile, k-block) as 16 KB blocks already in the swizzled shared-memory
+  // layout (pack_weight): one bulk copy per stage reads them sequentially (nullable)
+  const uint8_t* w_packed;
 };
 
 // The fused all-gather's wait: every member's pushers have raised their flags for this call in this
@@ -259,9 +262,16 @@ __global__ void __launch_bounds__(kThreads, CPS)
     // the weight tiles of the first stages depend on no kernel of the step: stream them while the
     // previous kernel finishes, then the activation tiles once it has
     const int pre = min(nkb, C::kStages);
+    auto load_w = [&](int stage, int kb) {
+      if (p.w_packed)
+        ptx::bulk_g2s(a_tiles + stage * C::kABytes, p.w_packed + ((size_t)blockIdx.x * p.kb + kb) * C::kABytes,
+                      C::kABytes, &full[stage]);
+      else
+        ptx::tma_load_2d(a_tiles + stage * C::kABytes, &tmap_w, kb * BK, n0, &full[stage]);
+    };
     for (int i = 0; i < pre; i++) {
       ptx::mbar_arrive_expect_tx(&full[i], C::kStageBytes);
-      ptx::tma_load_2d(a_tiles + i * C::kABytes, &tmap_w, kblk(i) * BK, n0, &full[i]);
+      load_w(i, kblk(i));
     }
     pdl_wait();
     pdl_launch();
@@ -285,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
       }
       ptx::mbar_arrive_expect_tx(&full[s], C::kStageBytes);
       const int kx = kblk(i) * BK;
-      ptx::tma_load_2d(a_tiles + s * C::kABytes, &tmap_w, kx, n0, &full[s]);
+      load_w(s, kblk(i));
       ptx::tma_load_2d(b_tiles + s * C::kBBytes, xmap, kx, m0, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
@@ -696,6 +706,8 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.pre = static_cast<const __nv_bfloat16*>(a.pre);
   p.ldp = (int)a.ldp;
   p.silu = a.silu;
+  p.w_packed = static_cast<const uint8_t*>(a.w_packed);
+  if (p.w_packed && reinterpret_cast<uintptr_t>(p.w_packed) % 16 != 0) return cudaErrorInvalidValue;
   if (a.valid != nullptr) {
     if (a.valid_cap <= 0 || a.valid_segs <= 0 || a.valid_cap * a.valid_segs < a.M) return cudaErrorInvalidValue;
     p.valid = a.valid;

@@ -110,6 +110,37 @@ void argmax(torch::Tensor logits, torch::Tensor out) {
                                   logits.stride(0), cur()));
 }
 
+void sample(torch::Tensor logits, torch::Tensor positions, torch::Tensor temperature, torch::Tensor top_k,
+            torch::Tensor top_p, torch::Tensor seeds, torch::Tensor out) {
+  TORCH_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "logits [rows, vocab] on the device");
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 || logits.scalar_type() == at::kFloat, "logits bf16 or fp32");
+  const int64_t B = logits.size(0);
+  auto vec = [&](const torch::Tensor& t, at::ScalarType st, const char* n) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == st && t.is_contiguous() && t.numel() == B, n,
+                ": one contiguous value per row on the device");
+  };
+  vec(positions, at::kLong, "positions");
+  vec(temperature, at::kFloat, "temperature");
+  vec(top_k, at::kLong, "top_k");
+  vec(top_p, at::kFloat, "top_p");
+  vec(seeds, at::kLong, "seeds");
+  vec(out, at::kLong, "out");
+  es::SampleArgs a;
+  a.logits = logits.data_ptr();
+  a.fp32 = logits.scalar_type() == at::kFloat;
+  a.stride = logits.stride(0);
+  a.vocab = (int)logits.size(1);
+  a.rows = B;
+  a.positions = positions.data_ptr<int64_t>();
+  a.temperature = temperature.data_ptr<float>();
+  a.top_k = top_k.data_ptr<int64_t>();
+  a.top_p = top_p.data_ptr<float>();
+  a.seeds = seeds.data_ptr<int64_t>();
+  a.out = out.data_ptr<int64_t>();
+  const c10::cuda::CUDAGuard g(logits.device());
+  ES_CHECK_CUDA(es::launch_sample(a, cur()));
+}
+
 void decode_advance(torch::Tensor st, torch::Tensor sampled, torch::Tensor bt, int64_t b, int64_t bs) {
   TORCH_CHECK(st.scalar_type() == at::kLong && st.dim() == 2 && st.size(0) == 4 && st.is_contiguous(), "state [4, B]");
   TORCH_CHECK(sampled.scalar_type() == at::kLong && bt.scalar_type() == at::kInt && bt.stride(1) == 1, "dtypes");
@@ -137,7 +168,7 @@ void mixture_terms(es::GemmArgs& a, const c10::optional<torch::Tensor>& scale, c
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
                torch::Tensor ws, torch::Tensor sync, torch::Tensor status, int64_t num_sms,
                c10::optional<torch::Tensor> scale, c10::optional<torch::Tensor> pre,
-               c10::optional<torch::Tensor> valid, int64_t valid_cap) {
+               c10::optional<torch::Tensor> valid, int64_t valid_cap, c10::optional<torch::Tensor> w_packed) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
@@ -177,6 +208,13 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
     a.valid = reinterpret_cast<const uint32_t*>(valid->data_ptr<int32_t>());
     a.valid_cap = valid_cap;
     a.valid_segs = (int)valid->numel();
+  }
+  if (w_packed.has_value() && w_packed->defined()) {
+    const int64_t blocks = ((N + 127) / 128) * ((K + 63) / 64);
+    TORCH_CHECK(w_packed->is_cuda() && w_packed->is_contiguous() && w_packed->numel() * w_packed->element_size() ==
+                    blocks * 16384,
+                "w_packed: the weight packed into (tile, k-block) blocks of 16 KB");
+    a.w_packed = w_packed->data_ptr();
   }
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
@@ -700,12 +738,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("out"), pybind11::arg("interleaved") = false);
   m.def("embed", &embed, "embedding gather");
   m.def("argmax", &argmax, "greedy argmax per row");
+  m.def("sample", &sample, "seeded temperature / top-k / top-p sampling per row (Gumbel-max)");
   m.def("decode_advance", &decode_advance, "next decode step's inputs from the sampled ids");
   m.def("gemm_bf16", &gemm_bf16, "tcgen05 GEMM out = x . w^T * scale + pre (+ residual)", pybind11::arg("x"),
         pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("residual"), pybind11::arg("ws"), pybind11::arg("sync"),
         pybind11::arg("status"), pybind11::arg("num_sms"), pybind11::arg("scale") = pybind11::none(),
         pybind11::arg("pre") = pybind11::none(), pybind11::arg("valid") = pybind11::none(),
-        pybind11::arg("valid_cap") = 0);
+        pybind11::arg("valid_cap") = 0, pybind11::arg("w_packed") = pybind11::none());
   m.def("gemm_pick_bn", &es::gemm_pick_bn);
   m.def("gemm_pick_splits", &es::gemm_pick_splits);
   m.def("gemm_ws_floats", &es::gemm_ws_floats);

@@ -81,7 +81,8 @@ def sample(logits: torch.Tensor, positions: torch.Tensor, sb: SamplingBatch) -> 
     keep_sorted = rank < k[:, None]
     probs = torch.softmax(sz, dim=1)
     before = torch.cumsum(probs, dim=1) - probs  # mass of the tokens ranked above
-    keep_sorted &= before < sb.top_p[:, None]  # the top token is always kept
+    # the top token is always kept; top_p >= 1 keeps every token (no rounding of the running sum)
+    keep_sorted &= (before < sb.top_p[:, None]) | (rank == 0) | (sb.top_p[:, None] >= 1)
     keep = torch.zeros_like(keep_sorted).scatter(1, order, keep_sorted)
     g = -torch.log(-torch.log(uniforms(sb.seed, positions, V)))
     s = torch.where(keep, z.double() + g, torch.full_like(g, float("-inf")))

@@ -408,12 +408,10 @@ class DecoderLM:
     def _sample(self, logits: torch.Tensor, inp: StepInput) -> torch.Tensor:
         """Seeded sampling of every row (engine.sampling); each tensor-parallel rank gathers the
         full vocabulary and draws the same tokens."""
-        from ..engine.sampling import sample
-
         full = logits if self.tp.size == 1 else self.tp.all_gather_rows(logits.contiguous())
         full = full[:, : self.cfg.vocab]
         pos = inp.positions if inp.positions.shape[0] == full.shape[0] else inp.positions.index_select(0, inp.logits_idx)
-        return sample(full, pos, inp.sampling)
+        return self.ops.sample(full, pos, inp.sampling)
 
     def logits(self, inp: StepInput, caches, hidden=None, residual=None):
         """Full-vocab logits of each sequence's last row (tests and the CPU oracle)."""

@@ -80,6 +80,12 @@ class RefOps:
     def argmax(self, logits):
         return ref.argmax(logits)
 
+    def sample(self, logits, positions, sb):
+        """Seeded temperature / top-k / top-p draw of each row (engine.sampling.sample)."""
+        from ..engine.sampling import sample
+
+        return sample(logits, positions, sb)
+
     def check_status(self):
         return 0
 
@@ -139,9 +145,11 @@ class KernelOps:
         self.C.rmsnorm(x, residual, w, y, eps)
         return y
 
-    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None, valid=None, valid_cap=0):
+    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None, valid=None, valid_cap=0,
+               w_packed=None):
         """`valid` (int32 counts of segments of `valid_cap` rows) makes it a grouped GEMM whose
-        token tiles holding no counted row are skipped and left unwritten."""
+        token tiles holding no counted row are skipped and left unwritten. `w_packed`
+        (``pack_weight(w)``) streams the weight as contiguous swizzled blocks instead of tiles."""
         M, K = x.shape
         N = w.shape[0]
         if out is None:
@@ -152,7 +160,7 @@ class KernelOps:
             b = bias.expand(M, N) if residual is None else residual + bias
             residual = b.contiguous()
         self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, self.num_sms, scale, pre, valid,
-                         valid_cap)
+                         valid_cap, w_packed)
         return out
 
     def quant_fp8(self, x):
@@ -232,6 +240,20 @@ class KernelOps:
         self.C.argmax(logits, out)
         return out
 
+    def sample(self, logits, positions, sb):
+        """The sampling kernel: the same Gumbel-max draw over the same kept tokens as
+        engine.sampling.sample, with the top-p mass summed exactly in fixed point (the host
+        sampler's float running sum can differ at the cut-off by a rounding)."""
+        out = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+        if logits.dtype not in (torch.bfloat16, torch.float32):
+            logits = logits.float()
+        if logits.stride(1) != 1:
+            logits = logits.contiguous()
+        self.C.sample(logits, positions.to(torch.int64).contiguous(), sb.temperature.float().contiguous(),
+                      sb.top_k.to(torch.int64).contiguous(), sb.top_p.float().contiguous(),
+                      sb.seed.to(torch.int64).contiguous(), out)
+        return out
+
     def check_status(self) -> int:
         """Read (and clear) the status word that bounded waits set; non-zero means a timeout."""
         v = int(self.status.item())
@@ -241,6 +263,22 @@ class KernelOps:
 
 
 FP8_MAX = 448.0  # largest finite e4m3
+
+
+def pack_weight(w: torch.Tensor) -> torch.Tensor:
+    """A [N, K] bf16 weight laid out as the GEMM's shared-memory stages: per 128-row tile and 64-wide
+    k-block (tile-major), one 16 KB block of 128 rows of 128 bytes whose 16-byte chunk c of row r sits
+    at chunk c ^ (r % 8) (the 128-byte swizzle the MMA descriptors name). Rows past N and columns past
+    K are zero. One bulk copy per stage then reads the weight front to back."""
+    N, K = w.shape
+    T, KB = (N + 127) // 128, (K + 63) // 64
+    pad = torch.zeros(T * 128, KB * 64, dtype=w.dtype, device=w.device)
+    pad[:N, :K] = w
+    blocks = pad.view(T, 128, KB, 8, 8).permute(0, 2, 1, 3, 4)  # [T, KB, row, chunk, 8]
+    r = torch.arange(128, device=w.device).view(128, 1)
+    src = torch.arange(8, device=w.device).view(1, 8) ^ (r % 8)  # stored chunk c' holds logical c' ^ (r % 8)
+    out = blocks[:, :, torch.arange(128, device=w.device).view(128, 1), src]
+    return out.contiguous().view(torch.uint8).view(-1)
 
 
 def quantize_weight_fp8(w: torch.Tensor, block: int = 128) -> tuple[torch.Tensor, torch.Tensor]:

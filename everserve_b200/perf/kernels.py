@@ -15,7 +15,7 @@ import math
 
 import torch
 
-from ..ops import KernelOps, ref
+from ..ops import KernelOps, pack_weight, ref
 
 
 def _graph_ms(body, iters):
@@ -75,6 +75,14 @@ def main() -> None:
             rows.append({"kernel": "gemm", "name": name, "M": M, "N": N, "K": K,
                          "us": round(ms * 1e3, 2), "gb_s": round(byts / ms / 1e6, 1),
                          "cublas_us": round(cub * 1e3, 2), "cublas_gb_s": round(byts / cub / 1e6, 1)})
+            # the same weights pre-packed into swizzled 16 KB blocks (one bulk copy per stage)
+            wp = pack_weight(w)
+            ref_out = k.linear(x, w).clone()
+            pms = _time(lambda: k.linear(x, w, out=out, w_packed=wp), flush=flush)
+            same = bool(torch.equal(k.linear(x, w, w_packed=wp), ref_out))
+            rows.append({"kernel": "gemm_packed", "name": name, "M": M, "N": N, "K": K,
+                         "us": round(pms * 1e3, 2), "gb_s": round(byts / pms / 1e6, 1), "equal_to_tiled": same})
+            del wp
             if name == "gate_up" and M <= 64:
                 # the same weights with SiLU-mul in the GEMM epilogue (rows interleaved by 64)
                 sms = _time(lambda: k.linear_silu(x, w), flush=flush)
@@ -98,6 +106,23 @@ def main() -> None:
                 rows.append({"kernel": "paged_decode", "B": B, "ctx": ctx, "hq": hq, "hkv": hkv, "part": part,
                              "stages": stages, "us": round(ms * 1e3, 2), "gb_s": round(byts / ms / 1e6, 1)})
         _ = ref
+    if a.only in (None, "sample"):
+        # seeded top-k / top-p sampling of the batch's rows over the 8B vocabulary: the kernel
+        # against the host sampler (tensor ops: sort, softmax, cumsum, scatter)
+        from ..engine.sampling import SamplingBatch, sample
+
+        V = 128256
+        logits = (torch.randn(M, V, device=dev) * 2.5).bfloat16()
+        pos = torch.arange(M, device=dev, dtype=torch.int64)
+        for name, tk, tp in (("temperature", 0, 1.0), ("top_k50", 50, 1.0), ("top_p0.9", 0, 0.9),
+                             ("top_k50_p0.9", 50, 0.9)):
+            sb = SamplingBatch(temperature=torch.full((M,), 0.8, device=dev),
+                               top_k=torch.full((M,), tk, dtype=torch.int64, device=dev),
+                               top_p=torch.full((M,), tp, device=dev), seed=torch.arange(M, device=dev) + 7)
+            ms = _time(lambda: k.sample(logits, pos, sb), flush=flush)
+            hms = _time(lambda: sample(logits, pos, sb), iters=5)
+            rows.append({"kernel": "sample", "name": name, "B": M, "V": V, "us": round(ms * 1e3, 2),
+                         "host_sampler_us": round(hms * 1e3, 2)})
     for r in rows:
         print(json.dumps(r))
 
