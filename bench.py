@@ -40,7 +40,7 @@ METRIC = "decode tok/s at TP8 (1/2/4/8 GPU); failover pause p99; dead-rank detec
 
 # The baseline: stock vLLM 0.22 (the engine the reference plugs into, unmodified) on the same
 # workload, measured by `bench.py --impl stock` on this pool's B200s (tokens/s by GPU count).
-STOCK_TOK_S = {1: 12701.7}
+STOCK_TOK_S = {1: 12701.7, 2: 18094.9}
 
 
 class ClockSampler:
@@ -176,11 +176,16 @@ def stock_arm(args) -> None:
     time.sleep(0.3)
     sync()
     before = sum(got.values())
+    nvtx = os.environ.get("ES_NVTX") == "1"  # a named range for kernel-list captures of the timed steps
+    if nvtx:
+        torch.cuda.nvtx.range_push("es_timed")
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
+    if nvtx:
+        torch.cuda.nvtx.range_pop()
     gained = sum(got.values()) - before
     clk = clocks.stop()
     if world > 1:
@@ -317,11 +322,16 @@ def main() -> None:
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    nvtx = os.environ.get("ES_NVTX") == "1"  # a named range for kernel-list captures of the timed steps
+    if nvtx:
+        torch.cuda.nvtx.range_push("es_timed")
     start.record()
     eng.decode_steps(args.steps)
     if connector is not None:
         connector.ckv.join_stream()  # the timed region covers every step's KV gather
     end.record()
+    if nvtx:
+        torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier()
     dev_ms = max_over_ranks(start.elapsed_time(end))

@@ -19,14 +19,26 @@ constexpr int kThreads = 256;
 constexpr int kChunk = kChunkElems;
 
 // Two-shot all-reduce (tensors above the LL path): a persistent grid, CTA b taking chunks b,
-// b + grid, ... in the same order on every member. For chunk c (owner: member c % count):
-//   1. every member writes its part of c into the owner's data row for it (at the owner's local
-//      index c / count), a system fence, then raises the owner's flag for (its row, local index);
-//   2. the owner waits for every member's flag, sums the parts in member order in fp32 (one
-//      rounding) into `out`, writes the sum into every other member's gather area and raises the
-//      chunk's gather flag there; the others wait for that flag and copy the sum out.
-// Each member sends about twice (count - 1) / count of the vector and receives as much, against
-// count - 1 times the vector for pushing every part to every member. Every wait is bounded.
+// b + grid, ... in the same order on every member (chunk c's owner: member c % count).
+//   1. the CTA writes this member's part of every one of its chunks into the owner's data row for
+//      this member (at the owner's local index c / count), then one release fence and a flag per
+//      chunk at its owner;
+//   2. for the chunks this member owns: wait for every member's flag, sum the parts in member
+//      order in fp32 (one rounding) into `out` and into every other member's gather area; then one
+//      fence and the chunks' gather flags at every other member;
+//   3. for the chunks others own: wait for the owner's gather flag, copy the sum out.
+// A CTA's chunks travel together and it fences twice per call, not per chunk, so the bytes of all
+// of them are on the links at once. Each member sends about twice (count - 1) / count of the
+// vector and receives as much. Every wait is bounded.
+ES_DEVICE void fence_release_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+ES_DEVICE void copy_part(const __nv_bfloat16* __restrict__ src, char* dst, int len) {
+  const int nvec = len / 8;  // whole 16-byte vectors; the tail element by element
+  for (int i = threadIdx.x; i < nvec; i += kThreads)
+    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+  for (int i = nvec * 8 + threadIdx.x; i < len; i += kThreads) reinterpret_cast<__nv_bfloat16*>(dst)[i] = src[i];
+}
+
 __global__ void __launch_bounds__(kThreads) fdar_kernel(const __nv_bfloat16* __restrict__ inp,
                                                         __nv_bfloat16* __restrict__ out, int n, View v) {
   pdl_wait();
@@ -52,26 +64,27 @@ __global__ void __launch_bounds__(kThreads) fdar_kernel(const __nv_bfloat16* __r
     if (threadIdx.x == 0) finish_call(v, seq, kBadShape);
     return;
   }
-  for (int c = blockIdx.x; count > 0 && c < nchunks; c += gridDim.x) {
-    const int owner = s_order[c % count];
-    const size_t local = (size_t)(c / count) * kChunk * 2;  // byte offset in the owner's rows
-    const int e0 = c * kChunk, e1 = min(n, e0 + kChunk);
-    const int nvec = (e1 - e0) / 8;  // whole 16-byte vectors; the tail goes element by element
-    // 1. this member's part of the chunk, into the owner's row for this member
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(inp + e0);
-      uint4* dst = reinterpret_cast<uint4*>(data_ptr(v.peers[owner], parity, v.row) + local);
-      for (int i = threadIdx.x; i < nvec; i += kThreads) dst[i] = src[i];
-      __nv_bfloat16* dt = reinterpret_cast<__nv_bfloat16*>(dst);
-      for (int i = e0 + nvec * 8 + threadIdx.x; i < e1; i += kThreads) dt[i - e0] = inp[i];
+  if (count > 0) {
+    // 1. this member's parts, to their owners
+    for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+      const int owner = s_order[c % count];
+      const int e0 = c * kChunk, e1 = min(n, e0 + kChunk);
+      copy_part(inp + e0, data_ptr(v.peers[owner], parity, v.row) + (size_t)(c / count) * kChunk * 2, e1 - e0);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      __threadfence_system();
-      st_release_sys(flag_ptr(v.peers[owner], parity, v.row, c / count), seq);
+      fence_release_sys();
+      for (int c = blockIdx.x; c < nchunks; c += gridDim.x)
+        st_release_sys(flag_ptr(v.peers[s_order[c % count]], parity, v.row, c / count), seq);
     }
-    if (owner == v.row) {
-      // 2. the owner: every part, summed in member order, to `out` and every member's gather area
+    // 2. the chunks this member owns: summed in member order, to `out` and every member
+    bool owns = false;
+    for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+      if (s_order[c % count] != v.row) continue;
+      owns = true;
+      const size_t local = (size_t)(c / count) * kChunk * 2;
+      const int e0 = c * kChunk, e1 = min(n, e0 + kChunk);
+      const int nvec = (e1 - e0) / 8;
       if (threadIdx.x == 0) s_fail = wait_members(v, my_base, parity, c / count, seq, s_order, count);
       __syncthreads();
       if (s_fail != kOk) break;
@@ -98,22 +111,29 @@ __global__ void __launch_bounds__(kThreads) fdar_kernel(const __nv_bfloat16* __r
         for (int k = 0; k < count; k++)
           if (s_order[k] != v.row) reinterpret_cast<__nv_bfloat16*>(ag_ptr(v.peers[s_order[k]], parity))[i] = r;
       }
-      __syncthreads();
-      if (threadIdx.x == 0) __threadfence_system();
-      __syncthreads();
-      if (threadIdx.x < count && s_order[threadIdx.x] != v.row)
-        st_release_sys(ag_flag_ptr(v.peers[s_order[threadIdx.x]], parity, c), seq);
-    } else {
-      // the others: the owner's sum, from this member's gather area
+      __syncthreads();  // s_fail is rewritten by the next chunk's wait
+    }
+    __syncthreads();
+    if (owns && s_fail == kOk && threadIdx.x == 0) {
+      fence_release_sys();
+      for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        if (s_order[c % count] != v.row) continue;
+        for (int k = 0; k < count; k++)
+          if (s_order[k] != v.row) st_release_sys(ag_flag_ptr(v.peers[s_order[k]], parity, c), seq);
+      }
+    }
+    // 3. the chunks others own: the owner's sum, from this member's gather area
+    for (int c = blockIdx.x; s_fail == kOk && c < nchunks; c += gridDim.x) {
+      const int owner = s_order[c % count];
+      if (owner == v.row) continue;
+      const int e0 = c * kChunk, e1 = min(n, e0 + kChunk);
       if (threadIdx.x == 0) s_fail = wait_flag(v, ag_flag_ptr(my_base, parity, c), seq, owner);
       __syncthreads();
       if (s_fail != kOk) break;
-      const uint4* src = reinterpret_cast<const uint4*>(ag_ptr(my_base, parity) + (size_t)e0 * 2);
-      for (int i = threadIdx.x; i < nvec; i += kThreads) reinterpret_cast<uint4*>(out + e0)[i] = src[i];
-      for (int i = e0 + nvec * 8 + threadIdx.x; i < e1; i += kThreads)
-        out[i] = reinterpret_cast<const __nv_bfloat16*>(ag_ptr(my_base, parity))[i];
+      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(ag_ptr(my_base, parity) + (size_t)e0 * 2);
+      copy_part(src, reinterpret_cast<char*>(out + e0), e1 - e0);
+      __syncthreads();
     }
-    __syncthreads();
   }
   __syncthreads();
   if (threadIdx.x == 0) finish_call(v, seq, s_fail);
