@@ -153,6 +153,7 @@ struct DecodeArgs {
   int64_t out_stride;
   float* part_o;
   float* part_ml;
+  int* tickets;  // [B, Hkv] int32, zero before the first launch (each launch leaves it zero)
   int* status;
   int B, hq, hkv, d, block_size, max_splits, part_tokens;
   int64_t num_blocks;

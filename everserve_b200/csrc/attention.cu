@@ -8,9 +8,10 @@
 // each of the 4 warps takes one block of every stage and computes S = q.K^T and O += P.V with
 // mma.sync m16n8k16 (the G query heads padded to 16 rows: decode attention is memory-bound, the
 // tensor cores only remove the SIMT arithmetic from the critical path), keeping its own online
-// softmax state. The warps merge at the end, each split writes (o / l, m, l), and a second kernel
-// merges the splits in split order. The split length is fixed per engine, so a sequence's result
-// never depends on the batch around it.
+// softmax state. The warps merge at the end and each split writes (o / l, m, l); the last split of
+// a (sequence, kv head) to finish (a ticket per pair, counted with one atomic) merges the splits in
+// split order and writes the bf16 output, so there is no second launch. The split length is fixed
+// per engine, so a sequence's result never depends on the batch around it.
 #include <cuda.h>
 
 #include <cstring>
@@ -36,6 +37,9 @@ struct DecodeParams {
   const int* ctx_lens;
   float* part_o;   // [B, Hq, max_splits, D]
   float* part_ml;  // [B, Hq, max_splits, 2]
+  int* tickets;    // [B, Hkv] zero between launches: splits of the pair done so far
+  __nv_bfloat16* out;  // [B, Hq * D] rows of out_stride
+  int64_t out_stride;
   int hq, hkv, max_splits, part_tokens;
   float scale_log2;  // softmax scale * log2(e)
   int* status;
@@ -71,13 +75,18 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int ctx = p.ctx_lens[b];
   const int s0 = split * p.part_tokens;
-  if (s0 >= ctx) return;
+  const int G = p.hq / p.hkv;
+  if (s0 >= ctx) {
+    if (split == 0)  // an empty history: the output is zero
+      for (int i = threadIdx.x; i < G * D; i += kThreads)
+        p.out[(size_t)b * p.out_stride + (size_t)kvh * G * D + i] = f2bf(0.f);
+    return;
+  }
   const int s1 = min(ctx, s0 + p.part_tokens);
   const int blk0 = s0 / BS, blk1 = (s1 + BS - 1) / BS;
   const int nchunks = (blk1 - blk0 + kWarps - 1) / kWarps;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  const int G = p.hq / p.hkv;
   const int* bt = p.block_tables + (size_t)b * p.bt_stride;
 
   if (tid == 0) {
@@ -201,16 +210,14 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     }
     __syncthreads();  // the stage is free for the next issue
   }
-  if (failed) {
-    if (tid == 0 && p.status) atomicExch(p.status, (int)kTimeout);
-    return;
-  }
-  // merge the warps: row gid's (m, l, o) of each warp, then combine in warp order
+  if (failed && tid == 0 && p.status) atomicExch(p.status, (int)kTimeout);
+  // merge the warps: row gid's (m, l, o) of each warp, then combine in warp order (a failed split
+  // writes nothing but still takes its ticket, so the pair's count stays whole)
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
   float* red_o = reinterpret_cast<float*>(ring);  // [warp][8][D]
   float* red_ml = red_o + kWarps * 8 * D;         // [warp][8][2]
-  if (gid < G) {
+  if (!failed && gid < G) {
 #pragma unroll
     for (int i = 0; i < NT; i++) {
       red_o[(warp * 8 + gid) * D + i * 8 + tig * 2] = o[i][0];
@@ -222,7 +229,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     }
   }
   __syncthreads();
-  for (int i = tid; i < G * D; i += kThreads) {
+  for (int i = tid; !failed && i < G * D; i += kThreads) {
     const int g = i / D, e = i % D;
     float M = -INFINITY;
 #pragma unroll
@@ -242,28 +249,31 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
       p.part_ml[row * 2 + 1] = den;
     }
   }
-}
-
-// Merge the splits of every (sequence, head) in split order; out rows of out_stride elements.
-__global__ void decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                                    const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out,
-                                    int64_t out_stride, int hq, int max_splits, int part_tokens, int d) {
-  pdl_wait();
-  pdl_launch();
-  const int b = blockIdx.x, h = blockIdx.y;
-  const int ctx = ctx_lens[b];
-  const int ns = min(max_splits, (ctx + part_tokens - 1) / part_tokens);
-  const size_t row0 = ((size_t)b * hq + h) * max_splits;
-  float m = -INFINITY;
-  for (int s = 0; s < ns; s++) m = fmaxf(m, part_ml[(row0 + s) * 2]);
-  for (int e = threadIdx.x; e < d; e += blockDim.x) {
+  // the last split of the pair merges every split's (o, m, l) in split order
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  const int ns = min(p.max_splits, (ctx + p.part_tokens - 1) / p.part_tokens);
+  if (tid == 0) {
+    int* tk = p.tickets + (size_t)b * p.hkv + kvh;
+    s_last = atomicAdd(tk, 1) == ns - 1;
+    if (s_last) *tk = 0;  // every split of this launch has counted: the next launch starts at zero
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = tid; i < G * D; i += kThreads) {
+    const int g = i / D, e = i % D;
+    const size_t row0 = ((size_t)b * p.hq + kvh * G + g) * p.max_splits;
+    float m = -INFINITY;
+    for (int sp = 0; sp < ns; sp++) m = fmaxf(m, __ldcg(p.part_ml + (row0 + sp) * 2));
     float num = 0.f, den = 0.f;
-    for (int s = 0; s < ns; s++) {
-      const float w = part_ml[(row0 + s) * 2 + 1] * exp2f(part_ml[(row0 + s) * 2] - m);
-      num += w * part_o[(row0 + s) * d + e];
+    for (int sp = 0; sp < ns; sp++) {
+      const float w = __ldcg(p.part_ml + (row0 + sp) * 2 + 1) * exp2f(__ldcg(p.part_ml + (row0 + sp) * 2) - m);
+      num += w * __ldcg(p.part_o + (row0 + sp) * D + e);
       den += w;
     }
-    out[(size_t)b * out_stride + (size_t)h * d + e] = f2bf(ns > 0 ? num / den : 0.f);
+    p.out[(size_t)b * p.out_stride + (size_t)(kvh * G + g) * D + e] = f2bf(num / den);
   }
 }
 
@@ -309,6 +319,10 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   p.part_tokens = a.part_tokens;
   p.scale_log2 = a.scale * attn::kLog2e;
   p.status = a.status;
+  p.tickets = a.tickets;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.out_stride = a.out_stride;
+  if (p.tickets == nullptr) return cudaErrorInvalidValue;
   // the layer's cache as rows of 64 elements (128 bytes); one box = one (block, kv head) tile
   const int64_t rows = a.num_blocks * 2 * a.hkv * a.block_size * (a.d / 64);
   const int box_rows = a.block_size * (a.d / 64);
@@ -320,11 +334,7 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   else if (a.d == 128 && a.block_size == 32) e = attn::launch_stages<128, 32>(a.stages, map, p, a.B, stream);
   else if (a.d == 64 && a.block_size == 32) e = attn::launch_stages<64, 32>(a.stages, map, p, a.B, stream);
   else return cudaErrorInvalidValue;
-  if (e != cudaSuccess) return e;
-  dim3 mgrid(a.B, a.hq);
-  return launch_ex(attn::decode_merge_kernel, mgrid, dim3(a.d), 0, stream, 0, (const float*)a.part_o,
-                   (const float*)a.part_ml, a.ctx_lens, static_cast<__nv_bfloat16*>(a.out), a.out_stride, a.hq,
-                   a.max_splits, a.part_tokens, a.d);
+  return e;
 }
 
 }  // namespace es
@@ -338,7 +348,8 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
 
 namespace {
 
-constexpr size_t kNoAllocFloats = (size_t)ES_NOALLOC_PART_FLOATS + ES_NOALLOC_ML_FLOATS + 64;  // + status word
+// + the status word (and padding), then the split tickets of every (sequence, kv head) pair
+constexpr size_t kNoAllocFloats = (size_t)ES_NOALLOC_PART_FLOATS + ES_NOALLOC_ML_FLOATS + 64 + ES_NOALLOC_TICKETS;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats];
 
 constexpr int kNoAllocMaxDevices = 64;
@@ -411,6 +422,10 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
     g_noalloc_err = "batch * q_heads * ceil(max_model_len / 256) * head_dim exceeds the fixed scratch (2^21 floats)";
     return (int)cudaErrorInvalidValue;
   }
+  if ((int64_t)batch * kv_heads > ES_NOALLOC_TICKETS) {
+    g_noalloc_err = "batch * kv_heads exceeds the fixed split tickets (4096)";
+    return (int)cudaErrorInvalidValue;
+  }
   float* base = nullptr;
   cudaError_t e = noalloc_scratch(&base);
   if (e != cudaSuccess) return (int)e;
@@ -432,6 +447,10 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   p.part_tokens = kPart;
   p.scale_log2 = scale * attn::kLog2e;
   p.status = status;
+  // zero when the library loads; each launch leaves them at zero again
+  p.tickets = reinterpret_cast<int*>(base + ES_NOALLOC_PART_FLOATS + ES_NOALLOC_ML_FLOATS + 64);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride = out_stride;
   // tensor map encoded on the stack (no cache: nothing is allocated, not even on the host heap)
   tmap::EncodeFn enc = tmap::encoder();
   if (enc == nullptr) {
@@ -456,9 +475,5 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   else if (head_dim == 64 && block_size == 16) e = attn::launch_stages<64, 16>(3, map, p, batch, s);
   else if (head_dim == 128 && block_size == 32) e = attn::launch_stages<128, 32>(3, map, p, batch, s);
   else e = attn::launch_stages<64, 32>(3, map, p, batch, s);
-  if (e != cudaSuccess) return (int)e;
-  dim3 mgrid(batch, q_heads);
-  attn::decode_merge_kernel<<<mgrid, head_dim, 0, s>>>(p.part_o, p.part_ml, ctx_lens, static_cast<__nv_bfloat16*>(out),
-                                                       out_stride, q_heads, (int)splits, kPart, head_dim);
-  return (int)cudaGetLastError();
+  return (int)e;
 }

@@ -6,6 +6,7 @@
 // the two-shot kernel (a reduce-scatter to chunk owners, then the owners' sums to every member),
 // up to 1 Mi elements per member per call; the host splits bigger tensors into calls.
 #include <algorithm>
+#include <cstdlib>
 
 #include "api.h"
 #include "launch.h"
@@ -233,7 +234,13 @@ cudaError_t launch_fdar(const void* inp, void* out, int64_t n, const CommArgs& c
     return cudaErrorInvalidDevice;
   // persistent: every CTA resident at once (they wait on peers' CTAs of the same index)
   const int chunks = (int)((n + comm::kChunk - 1) / comm::kChunk);
-  const int grid = std::min(chunks, 2 * sms[dev]);
+  // ES_FDAR_CTAS_PER_SM (tuning): CTAs per SM of the persistent grid (default 2)
+  static const int per_sm = [] {
+    const char* e = std::getenv("ES_FDAR_CTAS_PER_SM");
+    const int v = e ? std::atoi(e) : 2;
+    return v >= 1 && v <= 8 ? v : 2;
+  }();
+  const int grid = std::min(chunks, per_sm * sms[dev]);
   return launch_ex(comm::fdar_kernel, dim3(grid), dim3(comm::kThreads), 0, stream, 0,
                    static_cast<const __nv_bfloat16*>(inp), static_cast<__nv_bfloat16*>(out), (int)n, v);
 }

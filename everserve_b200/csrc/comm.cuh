@@ -211,7 +211,7 @@ ES_DEVICE int wait_flag(const View& v, const uint32_t* f, uint32_t seq, int send
   bool named = false;
   uint32_t spins = 0;
   BeatWatch beat;
-  while (ld_acquire_sys(f) != seq) {
+  while (ld_relaxed_sys(f) != seq) {
     if ((++spins & 1023u) == 0) {
       volatile Ctrl* c = v.ctrl;
       if (c->abort) return kAborted;
@@ -228,6 +228,7 @@ ES_DEVICE int wait_flag(const View& v, const uint32_t* f, uint32_t seq, int send
       if (t - t0 > kHardLimitNs) return kTimeout;
     }
   }
+  fence_acquire_sys();
   return kOk;
 }
 
@@ -258,7 +259,7 @@ ES_DEVICE int wait_members(const View& v, uint64_t my_base, uint32_t parity, int
     const int sender = order[i];
     const uint32_t* f = flag_ptr(my_base, parity, sender, slot);
     BeatWatch beat;
-    while (ld_acquire_sys(f) != seq) {
+    while (ld_relaxed_sys(f) != seq) {
       if ((++spins & 1023u) == 0) {
         volatile Ctrl* c = v.ctrl;
         if (c->abort) return kAborted;
@@ -282,6 +283,7 @@ ES_DEVICE int wait_members(const View& v, uint64_t my_base, uint32_t parity, int
       }
     }
   }
+  fence_acquire_sys();
   if (v.mc) fence_alias();
   return kOk;
 }

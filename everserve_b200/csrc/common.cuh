@@ -93,6 +93,14 @@ ES_DEVICE uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Spin loads: relaxed (no ordering per iteration); the waiter orders what follows with one
+// fence_acquire_sys once the value it waits for has arrived.
+ES_DEVICE uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+ES_DEVICE void fence_acquire_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 ES_DEVICE void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

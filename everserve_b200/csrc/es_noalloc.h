@@ -12,7 +12,8 @@
  * part of the library itself.
  *
  * Scratch: a file-scope `static __device__` array of ES_NOALLOC_SCRATCH_BYTES bytes (8.25 MiB plus
- * a status word) in attention.cu. Every GPU that loads the library holds that array until the
+ * a status word and 16 KiB of split tickets, which start at zero and which every call leaves at
+ * zero) in attention.cu. Every GPU that loads the library holds that array until the
  * process exits. Requests whose split-KV partials do not fit are rejected (return value
  * cudaErrorInvalidValue, and es_noalloc_last_error() says why); nothing is allocated to make them
  * fit. The caller still passes every input and output buffer.
@@ -31,7 +32,8 @@
  * bf16 (rows of out_stride). Positions are split into runs of 256 (the regular default), so the
  * result matches the regular entry point's bit for bit when that one uses the same split length.
  *
- * Limits of the inputs: every ctx_lens[b] must be at most max_model_len (the scratch and the grid
+ * Limits of the inputs: batch * kv_heads at most ES_NOALLOC_TICKETS; every ctx_lens[b] must be at
+ * most max_model_len (the scratch and the grid
  * are sized from max_model_len, so positions past it would be left out of the result), and each
  * row of block_tables must hold at least ceil(ctx_lens[b] / block_size) valid block indices.
  */
@@ -46,6 +48,7 @@ extern "C" {
 
 #define ES_NOALLOC_PART_FLOATS (1 << 21) /* split partial outputs: batch * q_heads * splits * head_dim */
 #define ES_NOALLOC_ML_FLOATS (1 << 16)   /* split maxima and sums: batch * q_heads * splits * 2 */
+#define ES_NOALLOC_TICKETS 4096          /* split tickets, one per (sequence, kv head): batch * kv_heads */
 
 /* Look up the scratch array's address on the current device (idempotent). Returns a cudaError_t. */
 int es_noalloc_setup(void);

@@ -91,7 +91,7 @@ ES_DEVICE void set_status(comm::Ctrl* ctrl, int failure) {
 // Wait until *f == seq; past the bound name `late_row`; kOk, kAborted or kTimeout.
 ES_DEVICE int wait_flag(const uint32_t* f, uint32_t seq, comm::Ctrl* ctrl, int late_row, uint64_t t0, bool& named) {
   uint32_t spins = 0;
-  while (ld_acquire_sys(f) != seq) {
+  while (ld_relaxed_sys(f) != seq) {
     if ((++spins & 1023u) == 0) {
       volatile comm::Ctrl* c = ctrl;
       if (c->abort) return kAborted;
@@ -104,6 +104,7 @@ ES_DEVICE int wait_flag(const uint32_t* f, uint32_t seq, comm::Ctrl* ctrl, int l
       if (now > comm::kHardLimitNs) return kTimeout;
     }
   }
+  fence_acquire_sys();
   return kOk;
 }
 

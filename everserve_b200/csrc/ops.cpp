@@ -506,8 +506,8 @@ void gemm_allgather(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::op
 
 
 void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
-                  torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor status,
-                  int64_t max_splits, int64_t part_tokens, double scale, int64_t stages) {
+                  torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor tickets,
+                  torch::Tensor status, int64_t max_splits, int64_t part_tokens, double scale, int64_t stages) {
   check_bf16(q, "q");
   check_bf16(cache, "cache");
   check_bf16(out, "out");
@@ -536,6 +536,10 @@ void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tabl
   a.out_stride = out.stride(0);
   a.part_o = part_o.data_ptr<float>();
   a.part_ml = part_ml.data_ptr<float>();
+  TORCH_CHECK(tickets.is_cuda() && tickets.scalar_type() == at::kInt && tickets.is_contiguous() &&
+                  tickets.numel() >= (int64_t)B * hkv,
+              "tickets: int32 [B * kv_heads] on the device, zero before the first call");
+  a.tickets = tickets.data_ptr<int>();
   a.status = status.data_ptr<int>();
   a.B = B;
   a.hq = hq;

@@ -9,6 +9,7 @@ status word that bounded waits set. :class:`RefOps` is the CPU engine's arithmet
 from __future__ import annotations
 
 import math
+import os
 import threading
 
 import torch
@@ -95,7 +96,7 @@ class KernelOps:
 
     kind = "kernel"
     PART_TOKENS = 256  # positions per decode-attention split (fixed: batch-invariant results)
-    ATTN_STAGES = 3
+    ATTN_STAGES = int(os.environ.get("ES_ATTN_STAGES", "3"))  # K/V ring depth of decode attention
 
     def __init__(self, device: torch.device | str):
         self.device = torch.device(device)
@@ -108,6 +109,7 @@ class KernelOps:
         self._ctr = torch.zeros(0, dtype=torch.int32, device=self.device)
         self._part_o = torch.empty(0, dtype=torch.float32, device=self.device)
         self._part_ml = torch.empty(0, dtype=torch.float32, device=self.device)
+        self._tickets = torch.zeros(0, dtype=torch.int32, device=self.device)
         self._lock = threading.Lock()
 
     # ---- scratch ------------------------------------------------------------------------------
@@ -133,6 +135,8 @@ class KernelOps:
         ms = self.max_splits(max_model_len)
         self._ensure("_part_o", max_batch * hq * ms * d, torch.float32)
         self._ensure("_part_ml", max_batch * hq * ms * 2, torch.float32)
+        # one split ticket per (sequence, kv head); every launch leaves them at zero
+        self._ensure("_tickets", max_batch * hq, torch.int32, zero=True)
 
     # ---- ops ----------------------------------------------------------------------------------
     def embed(self, ids, table):
@@ -204,8 +208,8 @@ class KernelOps:
         ms = self.max_splits(max_model_len)
         self.reserve_attention(B, hq, d, max_model_len)
         out = torch.empty(B, hq, d, dtype=q.dtype, device=q.device)
-        self.C.paged_decode(q, cache, block_tables, ctx_lens, out, self._part_o, self._part_ml, self.status,
-                            ms, self.PART_TOKENS, scale, self.ATTN_STAGES)
+        self.C.paged_decode(q, cache, block_tables, ctx_lens, out, self._part_o, self._part_ml, self._tickets,
+                            self.status, ms, self.PART_TOKENS, scale, self.ATTN_STAGES)
         return out
 
     def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale, tiles=None):

@@ -257,7 +257,10 @@ class FusedTPCollective:
         activation tiles then come from local memory)."""
         per, n = x.shape[0], len(self.members)
         out = torch.empty(per * n, w.shape[0], dtype=x.dtype, device=x.device)
-        if per * n <= 64 and x.dtype == torch.bfloat16 and not self.nvls and x.stride(1) == 1:
+        # the fused kernel's CTAs all wait for every member's pushers, so its grid must be resident
+        # at once: at most one 128-row weight tile per SM (the lm_head's vocabulary slice is not)
+        fits = (w.shape[0] + 127) // 128 <= ops.num_sms
+        if per * n <= 64 and fits and x.dtype == torch.bfloat16 and not self.nvls and x.stride(1) == 1:
             self.C.gemm_allgather(x, w, out, residual, ops.status, ops.num_sms, *self._comm(), n, self.own)
             return out
         rows = torch.zeros(per * n, x.shape[1], dtype=x.dtype, device=x.device)

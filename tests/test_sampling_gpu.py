@@ -33,7 +33,8 @@ def _oracle(logits, positions, sb):
     before = torch.cumsum(p, dim=1) - p
     tp = sb.top_p.double()[:, None]
     keep &= (before < tp) | (rank == 0) | (tp >= 1)
-    margin = torch.where((tp > 0) & (tp < 1), (before - tp).abs().min(dim=1).values,
+    active = ((tp > 0) & (tp < 1))[:, 0]
+    margin = torch.where(active, (before - tp).abs().min(dim=1).values,
                          torch.full((B,), 1.0, dtype=torch.float64, device=x.device))
     kept = torch.zeros_like(keep).scatter(1, order, keep)
     g = -torch.log(-torch.log(uniforms(sb.seed, positions, Vv)))
