@@ -5,6 +5,7 @@
 // (cudaErrorInvalidValue for a shape it refuses), so the .cu files stay free of torch headers.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -161,6 +162,12 @@ struct DecodeArgs {
   float scale;
 };
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t s);
+// the tcgen05 persistent variant (decode_tc.cu): head dim 128, G <= 16, splits of 256 positions
+bool decode_tc_supported(const DecodeArgs& a);
+cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s);
+// the same with the tensor maps given: q as [B * Hq, D] with a box of (G rows, 64 columns), the
+// cache as [num_blocks * 2 * Hkv * BS, D] with a box of (BS rows, 64 columns), both 128-byte swizzled
+cudaError_t launch_decode_tc_maps(const DecodeArgs& a, const CUtensorMap& qm, const CUtensorMap& cm, cudaStream_t s);
 
 // ---- gemm_fp8.cu: block-scaled fp8 (e4m3) GEMM ------------------------------------------------------
 struct Fp8GemmArgs {

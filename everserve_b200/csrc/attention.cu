@@ -14,6 +14,7 @@
 // per engine, so a sequence's result never depends on the batch around it.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "api.h"
@@ -302,6 +303,12 @@ cudaError_t launch_stages(int stages, const CUtensorMap& map, const DecodeParams
 
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (a.B == 0) return cudaSuccess;
+  // the tcgen05 kernel where it applies (ES_ATTN_TC=0: always this file's mma.sync kernel)
+  static const bool tc = [] {
+    const char* v = std::getenv("ES_ATTN_TC");
+    return !(v && v[0] == '0');
+  }();
+  if (tc && decode_tc_supported(a)) return launch_decode_tc(a, stream);
   if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.hq / a.hkv > 8 || a.part_tokens % 64 != 0 || a.max_splits <= 0)
     return cudaErrorInvalidValue;
   if (a.s_kv != (int64_t)a.hkv * a.block_size * a.d || a.s_block != 2 * a.s_kv) return cudaErrorInvalidValue;
@@ -470,6 +477,54 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
     g_noalloc_err = "the cache cannot be described by a TMA map (alignment or size)";
     return (int)cudaErrorInvalidValue;
+  }
+  // the tcgen05 kernel where it applies, as the regular entry point (the same result bit for bit);
+  // its maps too are encoded here, on the stack
+  DecodeArgs da{};
+  da.q = q;
+  da.q_stride = q_stride;
+  da.cache = cache;
+  da.block_tables = block_tables;
+  da.bt_stride = bt_stride;
+  da.ctx_lens = ctx_lens;
+  da.out = out;
+  da.out_stride = out_stride;
+  da.part_o = p.part_o;
+  da.part_ml = p.part_ml;
+  da.tickets = p.tickets;
+  da.status = status;
+  da.B = batch;
+  da.hq = q_heads;
+  da.hkv = kv_heads;
+  da.d = head_dim;
+  da.block_size = block_size;
+  da.max_splits = (int)splits;
+  da.part_tokens = kPart;
+  da.num_blocks = num_blocks;
+  da.scale = scale;
+  const char* tc_env = std::getenv("ES_ATTN_TC");
+  if (!(tc_env && tc_env[0] == '0') && decode_tc_supported(da)) {
+    CUtensorMap qm;
+    std::memset(&qm, 0, sizeof(qm));
+    const cuuint64_t qdims[2] = {(cuuint64_t)head_dim, (cuuint64_t)batch * q_heads};
+    const cuuint64_t qstrides[1] = {(cuuint64_t)head_dim * 2};
+    const cuuint32_t qbox[2] = {64, (cuuint32_t)(q_heads / kv_heads)};
+    const cuuint64_t cdims[2] = {(cuuint64_t)head_dim, (cuuint64_t)(num_blocks * 2 * kv_heads * block_size)};
+    const cuuint64_t cstrides[1] = {(cuuint64_t)head_dim * 2};
+    const cuuint32_t cbox[2] = {64, (cuuint32_t)block_size};
+    CUtensorMap cm;
+    std::memset(&cm, 0, sizeof(cm));
+    if (reinterpret_cast<uintptr_t>(q) % 16 != 0 ||
+        enc(&qm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(q), qdims, qstrides, qbox, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&cm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(cache), cdims, cstrides, cbox, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      g_noalloc_err = "q or the cache cannot be described by a TMA map (alignment or size)";
+      return (int)cudaErrorInvalidValue;
+    }
+    return (int)launch_decode_tc_maps(da, qm, cm, s);
   }
   if (head_dim == 128 && block_size == 16) e = attn::launch_stages<128, 16>(3, map, p, batch, s);
   else if (head_dim == 64 && block_size == 16) e = attn::launch_stages<64, 16>(3, map, p, batch, s);

@@ -20,6 +20,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -196,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
   }
   if (threadIdx.x == 0) {
     s_fail = 0;
-    ptx::prefetch_tmap(&tmap_w);
+    if (p.w_packed == nullptr) ptx::prefetch_tmap(&tmap_w);
     ptx::prefetch_tmap(&tmap_x);
     for (int s = 0; s < C::kStages; s++) {
       ptx::mbar_init(&full[s], 1);
@@ -680,18 +681,29 @@ static bool stream_k_enabled() {
   return on;
 }
 
+// The weight's operand: a tensor map of the row-major weight, or (pre-packed weight) nothing, the
+// kernel reading the packed blocks by bulk copies. Checks the alignment either needs.
+static cudaError_t weight_map(const GemmArgs& a, CUtensorMap* mw) {
+  if (a.w_packed != nullptr) {
+    if (reinterpret_cast<uintptr_t>(a.w_packed) % 16 != 0) return cudaErrorInvalidValue;
+    std::memset(mw, 0, sizeof(*mw));
+    return cudaSuccess;
+  }
+  if ((a.ldw * 2) % 16 != 0 || reinterpret_cast<uintptr_t>(a.w) % 16 != 0) return cudaErrorInvalidValue;
+  return tmap::bf16_2d(mw, const_cast<void*>(a.w), a.N, a.K, a.ldw, gemm::BM, gemm::BK);
+}
+
 cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return cudaSuccess;
   const int64_t n_tiles = (a.N + gemm::BM - 1) / gemm::BM;
-  if (a.M <= 64 && a.valid == nullptr && a.ws != nullptr && a.sync != nullptr &&
+  if (a.M <= 64 && a.valid == nullptr && a.ws != nullptr && a.sync != nullptr && a.w_packed == nullptr &&
       (stream_k_enabled() || n_tiles > 4 * (int64_t)a.num_sms))
     return launch_gemm_stream(a, a.silu != 0, stream);
   if (a.silu && (a.N % gemm::BM != 0 || a.residual != nullptr || a.scale != nullptr || a.pre != nullptr ||
                  a.valid != nullptr))
     return cudaErrorInvalidValue;
-  if (a.K % 8 != 0 || (a.ldx * 2) % 16 != 0 || (a.ldw * 2) % 16 != 0) return cudaErrorInvalidValue;
-  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || reinterpret_cast<uintptr_t>(a.w) % 16 != 0)
-    return cudaErrorInvalidValue;
+  if (a.K % 8 != 0 || (a.ldx * 2) % 16 != 0) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0) return cudaErrorInvalidValue;
   const int BN = (int)gemm_pick_bn(a.M);
   gemm::Params p{};
   p.out = static_cast<__nv_bfloat16*>(a.out);
@@ -707,7 +719,6 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.ldp = (int)a.ldp;
   p.silu = a.silu;
   p.w_packed = static_cast<const uint8_t*>(a.w_packed);
-  if (p.w_packed && reinterpret_cast<uintptr_t>(p.w_packed) % 16 != 0) return cudaErrorInvalidValue;
   if (a.valid != nullptr) {
     if (a.valid_cap <= 0 || a.valid_segs <= 0 || a.valid_cap * a.valid_segs < a.M) return cudaErrorInvalidValue;
     p.valid = a.valid;
@@ -721,7 +732,7 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (tiles_m > 65535) return cudaErrorInvalidValue;
   dim3 grid(tiles_n, tiles_m, (unsigned)p.splits);
   CUtensorMap mw, mx;
-  cudaError_t e = tmap::bf16_2d(&mw, const_cast<void*>(a.w), a.N, a.K, a.ldw, gemm::BM, gemm::BK);
+  cudaError_t e = weight_map(a, &mw);
   if (e != cudaSuccess) return e;
   e = tmap::bf16_2d(&mx, const_cast<void*>(a.x), a.M, a.K, a.ldx, BN, gemm::BK);
   if (e != cudaSuccess) return e;
@@ -740,9 +751,8 @@ namespace es {
 
 cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return cudaSuccess;
-  if (a.M > 64 || a.K % 8 != 0 || (a.ldx * 2) % 16 != 0 || (a.ldw * 2) % 16 != 0) return cudaErrorInvalidValue;
-  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || reinterpret_cast<uintptr_t>(a.w) % 16 != 0)
-    return cudaErrorInvalidValue;
+  if (a.M > 64 || a.K % 8 != 0 || (a.ldx * 2) % 16 != 0) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0) return cudaErrorInvalidValue;
   constexpr int BN = 64;  // one token tile for every decode batch: the plan never depends on M
   const int tiles = (int)((a.N + gemm::BM - 1) / gemm::BM);
   if ((size_t)tiles * BN * gemm::BM * 4 > comm::kLLGemmBytes || c.seqs == nullptr) return cudaErrorInvalidValue;
@@ -756,6 +766,7 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
   p.ldr = (int)a.ldr;
   p.kb = (int)((a.K + gemm::BK - 1) / gemm::BK);
   p.scale = a.scale;
+  p.w_packed = static_cast<const uint8_t*>(a.w_packed);
   p.pre = static_cast<const __nv_bfloat16*>(a.pre);
   p.ldp = (int)a.ldp;
   p.two_shot = c.mc ? 0 : a.two_shot;  // the multicast variant pushes once already
@@ -790,7 +801,7 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
   v.ctrl = reinterpret_cast<comm::Ctrl*>(c.ctrl);
   v.row = c.row;
   CUtensorMap mw, mx;
-  cudaError_t e = tmap::bf16_2d(&mw, const_cast<void*>(a.w), a.N, a.K, a.ldw, gemm::BM, gemm::BK);
+  cudaError_t e = weight_map(a, &mw);
   if (e != cudaSuccess) return e;
   e = tmap::bf16_2d(&mx, const_cast<void*>(a.x), a.M, a.K, a.ldx, BN, gemm::BK);
   if (e != cudaSuccess) return e;
@@ -808,10 +819,8 @@ cudaError_t launch_gemm_allgather(const GemmArgs& a, const CommArgs& c, int64_t 
   constexpr int BN = 64;
   const int64_t M = ag_per * members;  // the gathered rows, in member order
   if (ag_per <= 0 || members <= 0 || members > comm::kMaxRows || M > BN || a.N == 0) return cudaErrorInvalidValue;
-  if (a.K % 8 != 0 || (a.ldx * 2) % 16 != 0 || (a.ldw * 2) % 16 != 0 || a.silu || a.valid != nullptr)
-    return cudaErrorInvalidValue;
-  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || reinterpret_cast<uintptr_t>(a.w) % 16 != 0 || own_base % 16 != 0 ||
-      c.seqs == nullptr)
+  if (a.K % 8 != 0 || (a.ldx * 2) % 16 != 0 || a.silu || a.valid != nullptr) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || own_base % 16 != 0 || c.seqs == nullptr)
     return cudaErrorInvalidValue;
   if ((size_t)M * a.K * 2 > comm::kAGGemmBytes) return cudaErrorInvalidValue;
   const int tiles = (int)((a.N + gemm::BM - 1) / gemm::BM);
@@ -831,6 +840,7 @@ cudaError_t launch_gemm_allgather(const GemmArgs& a, const CommArgs& c, int64_t 
   p.ag_per = (int)ag_per;
   p.ag_ldx = (int)a.ldx;
   p.ag_k = (int)a.K;
+  p.w_packed = static_cast<const uint8_t*>(a.w_packed);
   int cps = 1;
   gemm_plan(BN, a.N, a.K, a.num_sms, &p.splits, &cps);
   // every CTA waits for the pushers of every member: the whole grid must be resident at once
@@ -846,7 +856,7 @@ cudaError_t launch_gemm_allgather(const GemmArgs& a, const CommArgs& c, int64_t 
   v.row = c.row;
   // the gathered rows live in this member's own buffer, one region per call parity
   CUtensorMap mw, mx0, mx1;
-  cudaError_t e = tmap::bf16_2d(&mw, const_cast<void*>(a.w), a.N, a.K, a.ldw, gemm::BM, gemm::BK);
+  cudaError_t e = weight_map(a, &mw);
   if (e != cudaSuccess) return e;
   char* rows = reinterpret_cast<char*>(own_base) + comm::kAGGemmOff;
   e = tmap::bf16_2d(&mx0, rows, M, a.K, a.K, BN, gemm::BK);

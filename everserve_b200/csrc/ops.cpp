@@ -35,6 +35,18 @@ void check_bf16(const torch::Tensor& t, const char* name) {
 
 cudaStream_t cur() { return at::cuda::getCurrentCUDAStream(); }
 
+// A weight pre-packed by ops.pack_weight: 16 KB blocks per (128-row tile, 64-wide k-block). `w`
+// then only carries the shape [N, K] (a stride-0 view); the kernels read the blocks.
+bool packed_weight(es::GemmArgs& a, const c10::optional<torch::Tensor>& w_packed, int64_t N, int64_t K) {
+  if (!w_packed.has_value() || !w_packed->defined()) return false;
+  const int64_t blocks = ((N + 127) / 128) * ((K + 63) / 64);
+  TORCH_CHECK(w_packed->is_cuda() && w_packed->is_contiguous() &&
+                  w_packed->numel() * w_packed->element_size() == blocks * 16384,
+              "w_packed: the weight packed into (tile, k-block) blocks of 16 KB");
+  a.w_packed = w_packed->data_ptr();
+  return true;
+}
+
 void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w, torch::Tensor y, double eps) {
   check_bf16(x, "x");
   check_bf16(w, "w");
@@ -173,14 +185,15 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
   check_bf16(w, "w");
   check_bf16(out, "out");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D operands");
-  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "K-contiguous operands");
+  es::GemmArgs a{};
+  const bool packed = packed_weight(a, w_packed, w.size(0), w.size(1));
+  TORCH_CHECK(x.stride(1) == 1 && (packed || w.stride(1) == 1) && out.stride(1) == 1, "K-contiguous operands");
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K, "K mismatch: x has ", K, ", w has ", w.size(1));
   TORCH_CHECK(out.size(0) == M && out.size(1) == N, "out shape");
   TORCH_CHECK(status.scalar_type() == at::kInt && status.is_cuda(), "status must be int32 on the device");
   TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= es::gemm_ws_floats(num_sms), "stream-K workspace too small");
   TORCH_CHECK(sync.scalar_type() == at::kInt && sync.numel() >= es::gemm_sync_words(num_sms), "sync words too small");
-  es::GemmArgs a{};
   a.x = x.data_ptr();
   a.w = w.data_ptr();
   a.out = out.data_ptr();
@@ -209,31 +222,25 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
     a.valid_cap = valid_cap;
     a.valid_segs = (int)valid->numel();
   }
-  if (w_packed.has_value() && w_packed->defined()) {
-    const int64_t blocks = ((N + 127) / 128) * ((K + 63) / 64);
-    TORCH_CHECK(w_packed->is_cuda() && w_packed->is_contiguous() && w_packed->numel() * w_packed->element_size() ==
-                    blocks * 16384,
-                "w_packed: the weight packed into (tile, k-block) blocks of 16 KB");
-    a.w_packed = w_packed->data_ptr();
-  }
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
 }
 
 // out[M, N/2] = silu(gate) * up of x . w^T, w's rows gate/up interleaved by 64 (decode sizes)
 void gemm_silu(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor ws, torch::Tensor sync,
-               torch::Tensor status, int64_t num_sms) {
+               torch::Tensor status, int64_t num_sms, c10::optional<torch::Tensor> w_packed) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D operands");
-  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "K-contiguous operands");
+  es::GemmArgs a{};
+  const bool packed = packed_weight(a, w_packed, w.size(0), w.size(1));
+  TORCH_CHECK(x.stride(1) == 1 && (packed || w.stride(1) == 1) && out.stride(1) == 1, "K-contiguous operands");
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && N % 128 == 0, "w: [N, K] with N a multiple of 128");
   TORCH_CHECK(out.size(0) == M && out.size(1) == N / 2, "out: [M, N / 2]");
   TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= es::gemm_ws_floats(num_sms), "stream-K workspace too small");
   TORCH_CHECK(sync.scalar_type() == at::kInt && sync.numel() >= es::gemm_sync_words(num_sms), "sync words too small");
-  es::GemmArgs a{};
   a.x = x.data_ptr();
   a.w = w.data_ptr();
   a.out = out.data_ptr();
@@ -436,16 +443,18 @@ void fdar(torch::Tensor inp, torch::Tensor out, torch::Tensor peers, torch::Tens
 void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
                     torch::Tensor status, int64_t num_sms, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
                     int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs, c10::optional<torch::Tensor> scale,
-                    c10::optional<torch::Tensor> pre, int64_t two_shot, int64_t rs_per) {
+                    c10::optional<torch::Tensor> pre, int64_t two_shot, int64_t rs_per,
+                    c10::optional<torch::Tensor> w_packed) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D operands");
-  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "K-contiguous operands");
+  es::GemmArgs a{};
+  const bool packed = packed_weight(a, w_packed, w.size(0), w.size(1));
+  TORCH_CHECK(x.stride(1) == 1 && (packed || w.stride(1) == 1) && out.stride(1) == 1, "K-contiguous operands");
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && out.size(1) == N && out.size(0) == (rs_per > 0 ? rs_per : M), "shapes");
   TORCH_CHECK(M <= 64, "the fused all-reduce GEMM takes decode batches (M <= 64)");
-  es::GemmArgs a{};
   a.x = x.data_ptr();
   a.w = w.data_ptr();
   a.out = out.data_ptr();
@@ -473,15 +482,17 @@ void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::op
 
 void gemm_allgather(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
                     torch::Tensor status, int64_t num_sms, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
-                    int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs, int64_t members, int64_t own_base) {
+                    int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs, int64_t members, int64_t own_base,
+                    c10::optional<torch::Tensor> w_packed) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "2-D operands");
-  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "K-contiguous operands");
+  es::GemmArgs a{};
+  const bool packed = packed_weight(a, w_packed, w.size(0), w.size(1));
+  TORCH_CHECK(x.stride(1) == 1 && (packed || w.stride(1) == 1) && out.stride(1) == 1, "K-contiguous operands");
   const int64_t per = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && out.size(0) == per * members && out.size(1) == N, "shapes: out is [per * members, N]");
-  es::GemmArgs a{};
   a.x = x.data_ptr();
   a.w = w.data_ptr();
   a.out = out.data_ptr();
@@ -754,7 +765,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ws_floats", &es::gemm_ws_floats);
   m.def("gemm_sync_words", &es::gemm_sync_words);
   m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
-  m.def("gemm_silu", &gemm_silu, "GEMM with SiLU-mul fused into its epilogue (gate/up rows interleaved by 64)");
+  m.def("gemm_silu", &gemm_silu, "GEMM with SiLU-mul fused into its epilogue (gate/up rows interleaved by 64)",
+        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("ws"), pybind11::arg("sync"),
+        pybind11::arg("status"), pybind11::arg("num_sms"), pybind11::arg("w_packed") = pybind11::none());
   m.def("quant_fp8", &quant_fp8, "x -> e4m3 with a scale per token and 128-wide block");
   m.def("gemm_fp8", &gemm_fp8, "block-scaled fp8 GEMM (tcgen05 kind::f8f6f4, scales per 128-wide K block)");
   m.def("paged_prefill", &paged_prefill, "paged causal prefill attention (tcgen05: S and P.V in TMEM, TMA K/V tiles)");
@@ -774,9 +787,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("num_sms"), pybind11::arg("peers"), pybind11::arg("order"), pybind11::arg("call"),
         pybind11::arg("ctrl"), pybind11::arg("row"), pybind11::arg("mc"), pybind11::arg("seqs"),
         pybind11::arg("scale") = pybind11::none(), pybind11::arg("pre") = pybind11::none(),
-        pybind11::arg("two_shot") = 0, pybind11::arg("rs_per") = 0);
+        pybind11::arg("two_shot") = 0, pybind11::arg("rs_per") = 0, pybind11::arg("w_packed") = pybind11::none());
   m.def("gemm_allgather", &gemm_allgather,
-        "column-parallel GEMM with the all-gather of its token rows fused (peer stores into each member's buffer)");
+        "column-parallel GEMM with the all-gather of its token rows fused (peer stores into each member's buffer)",
+        pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("residual"), pybind11::arg("status"),
+        pybind11::arg("num_sms"), pybind11::arg("peers"), pybind11::arg("order"), pybind11::arg("call"),
+        pybind11::arg("ctrl"), pybind11::arg("row"), pybind11::arg("mc"), pybind11::arg("seqs"),
+        pybind11::arg("members"), pybind11::arg("own_base"), pybind11::arg("w_packed") = pybind11::none());
   m.def("comm_buffer_bytes", &es::comm_buffer_bytes);
   m.def("comm_max_elems", &es::comm_max_elems, "elements one all-reduce call takes for a group of `members`",
         pybind11::arg("members") = 1);

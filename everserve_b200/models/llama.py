@@ -22,7 +22,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ..ops import interleave_gate_up, ops_for, quantize_weight_fp8, ref, softmax_scale
+from ..ops import PackedWeight, interleave_gate_up, ops_for, quantize_weight_fp8, ref, softmax_scale
 from .config import ModelConfig
 
 
@@ -120,6 +120,9 @@ class TPGroup:
 class DecoderLM:
     # the dense projections that take block-scaled fp8 weights in the fp8 configuration
     FP8_LINEARS = ("qkv", "o", "gate_up", "down")
+    # the dense projections whose weights the kernels keep packed in stage blocks (one bulk copy per
+    # stage streams them front to back; measured faster for the large MLP matrices at decode)
+    PACKED_LINEARS = ("gate_up", "down")
 
     def __init__(self, cfg: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0,
                  tp: TPGroup | None = None, layer_range: tuple[int, int] | None = None,
@@ -170,6 +173,8 @@ class DecoderLM:
         # computes SiLU-mul in its epilogue (ops.linear_silu); the reference ops keep gate then up
         self.fused_silu = (not cfg.is_moe and self.ops.kind == "kernel" and self.inter % 64 == 0
                            and os.environ.get("ES_FUSED_SILU", "1") != "0")
+        self.packed_weights = (self.ops.kind == "kernel" and not cfg.is_moe
+                               and os.environ.get("ES_PACK_WEIGHTS", "1") != "0")
         self.cos_sin = ref.cos_sin_table(cfg.head_dim, cfg.max_position, cfg.rope_theta, cfg.rope_scaling).to(self.device)
         self.weights: dict[str, torch.Tensor] = {}
         if init == "random":
@@ -190,7 +195,11 @@ class DecoderLM:
             q, s = quantize_weight_fp8(t.to(device=self.device, dtype=torch.float32))
             self.weights[key + ".q8"], self.weights[key + ".s8"] = q.contiguous(), s.contiguous()
             return
-        self.weights[key] = t.to(device=self.device, dtype=self.dtype).contiguous()
+        t = t.to(device=self.device, dtype=self.dtype).contiguous()
+        if self.packed_weights and key.rsplit(".", 1)[-1] in self.PACKED_LINEARS and ".e" not in key:
+            self.weights[key] = PackedWeight(t)  # the packed blocks only; ops.dense(w) unpacks
+            return
+        self.weights[key] = t
 
     def _linear(self, ops, x, key: str, residual=None):
         """x . W[key]^T (+ residual) for a bf16 or a block-scaled fp8 weight."""

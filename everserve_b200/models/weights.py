@@ -18,7 +18,7 @@ import os
 
 import torch
 
-from ..ops import deinterleave_gate_up
+from ..ops import deinterleave_gate_up, dense
 from .llama import DecoderLM
 
 
@@ -100,7 +100,7 @@ def to_hf_state_dict(model: DecoderLM) -> dict[str, torch.Tensor]:
     if model.tp.size != 1 or not (model.first and model.last):
         raise ValueError("export needs the whole model in one shard")
     c, d = model.cfg, model.cfg.head_dim
-    W = {k: v.detach().float().cpu() for k, v in model.weights.items()}
+    W = {k: dense(v).detach().float().cpu() for k, v in model.weights.items()}
     out = {"model.embed_tokens.weight": W["embed"][: c.vocab], "model.norm.weight": W["final_norm"]}
     if not c.tie_embeddings:
         out["lm_head.weight"] = W["lm_head"][: c.vocab]

@@ -37,7 +37,7 @@ class RefOps:
 
     def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None, valid=None, valid_cap=0):
         # rows a grouped GEMM would skip are padding nobody reads: computing them changes nothing
-        y = ref.linear(x, w, bias, residual, scale, pre)
+        y = ref.linear(x, dense(w), bias, residual, scale, pre)
         if out is not None:
             out.copy_(y)
             return out
@@ -163,6 +163,8 @@ class KernelOps:
             # bias folds into the residual input of the epilogue
             b = bias.expand(M, N) if residual is None else residual + bias
             residual = b.contiguous()
+        if isinstance(w, PackedWeight):
+            w, w_packed = w.carrier, w.packed
         self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, self.num_sms, scale, pre, valid,
                          valid_cap, w_packed)
         return out
@@ -236,7 +238,8 @@ class KernelOps:
         M = x.shape[0]
         self.reserve_linear()
         out = torch.empty(M, w.shape[0] // 2, dtype=x.dtype, device=x.device)
-        self.C.gemm_silu(x, w, out, self._ws, self._ctr, self.status, self.num_sms)
+        wt, wp = weight_args(w)
+        self.C.gemm_silu(x, wt, out, self._ws, self._ctr, self.status, self.num_sms, wp)
         return out
 
     def argmax(self, logits):
@@ -283,6 +286,54 @@ def pack_weight(w: torch.Tensor) -> torch.Tensor:
     src = torch.arange(8, device=w.device).view(1, 8) ^ (r % 8)  # stored chunk c' holds logical c' ^ (r % 8)
     out = blocks[:, :, torch.arange(128, device=w.device).view(128, 1), src]
     return out.contiguous().view(torch.uint8).view(-1)
+
+
+def unpack_weight(packed: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    """The [n, k] bf16 weight of ``pack_weight`` (the chunk swizzle is its own inverse)."""
+    T, KB = (n + 127) // 128, (k + 63) // 64
+    blocks = packed.view(torch.bfloat16).view(T, KB, 128, 8, 8)
+    r = torch.arange(128, device=packed.device).view(128, 1)
+    src = torch.arange(8, device=packed.device).view(1, 8) ^ (r % 8)
+    rows = blocks[:, :, r, src].permute(0, 2, 1, 3, 4).reshape(T * 128, KB * 64)
+    return rows[:n, :k].contiguous()
+
+
+class PackedWeight:
+    """A bf16 [N, K] weight kept only as ``pack_weight(w)``, which the GEMM streams by one bulk copy
+    per stage. ``carrier`` is a stride-0 [N, K] view of one element: it carries the shape through
+    the bindings, whose kernels then read ``packed`` alone."""
+
+    __slots__ = ("packed", "n", "k", "carrier")
+
+    def __init__(self, w: torch.Tensor):
+        self.n, self.k = (int(v) for v in w.shape)
+        self.packed = pack_weight(w)
+        self.carrier = torch.zeros(1, dtype=w.dtype, device=w.device).expand(self.n, self.k)
+
+    @property
+    def shape(self) -> torch.Size:
+        return torch.Size((self.n, self.k))
+
+    @property
+    def dtype(self):
+        return self.carrier.dtype
+
+    @property
+    def device(self):
+        return self.carrier.device
+
+    def unpack(self) -> torch.Tensor:
+        return unpack_weight(self.packed, self.n, self.k)
+
+
+def weight_args(w):
+    """(the tensor a binding takes as `w`, the packed blocks or None)."""
+    return (w.carrier, w.packed) if isinstance(w, PackedWeight) else (w, None)
+
+
+def dense(w) -> torch.Tensor:
+    """The [N, K] tensor of a weight, packed or not."""
+    return w.unpack() if isinstance(w, PackedWeight) else w
 
 
 def quantize_weight_fp8(w: torch.Tensor, block: int = 128) -> tuple[torch.Tensor, torch.Tensor]:

@@ -22,6 +22,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _ext
+from ..ops import weight_args
 from .nccl import GroupCollective
 from .slot import HANDLE_BYTES, MAX_ROWS, SlotRegion
 from .symm import PeerMapping, SymmetricBuffer
@@ -220,8 +221,9 @@ class FusedTPCollective:
         each tile's owner and an all-gather (a quarter of the one-shot push's NVLink bytes at 8)."""
         if x.shape[0] <= 64 and x.dtype == torch.bfloat16:
             out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
-            self.C.gemm_allreduce(x, w, out, residual, ops.status, ops.num_sms, *self._comm(), scale, pre,
-                                  self.two_shot)
+            wt, wp = weight_args(w)
+            self.C.gemm_allreduce(x, wt, out, residual, ops.status, ops.num_sms, *self._comm(), scale, pre,
+                                  self.two_shot, 0, wp)
             return out
         if x.dtype == torch.bfloat16 and not torch.cuda.is_current_stream_capturing():
             return self._linear_allreduce_overlapped(ops, x, w, residual, scale, pre)
@@ -240,7 +242,9 @@ class FusedTPCollective:
         pos = self.members.index(self.row)
         out = torch.empty(per, w.shape[0], dtype=x.dtype, device=x.device)
         if M <= 64 and x.dtype == torch.bfloat16 and not self.nvls:
-            self.C.gemm_allreduce(x, w, out, residual, ops.status, ops.num_sms, *self._comm(), None, None, 0, per)
+            wt, wp = weight_args(w)
+            self.C.gemm_allreduce(x, wt, out, residual, ops.status, ops.num_sms, *self._comm(), None, None, 0, per,
+                                  wp)
             return out
         full = self.linear_allreduce(ops, x, w)
         out.zero_()
@@ -261,7 +265,8 @@ class FusedTPCollective:
         # at once: at most one 128-row weight tile per SM (the lm_head's vocabulary slice is not)
         fits = (w.shape[0] + 127) // 128 <= ops.num_sms
         if per * n <= 64 and fits and x.dtype == torch.bfloat16 and not self.nvls and x.stride(1) == 1:
-            self.C.gemm_allgather(x, w, out, residual, ops.status, ops.num_sms, *self._comm(), n, self.own)
+            wt, wp = weight_args(w)
+            self.C.gemm_allgather(x, wt, out, residual, ops.status, ops.num_sms, *self._comm(), n, self.own, wp)
             return out
         rows = torch.zeros(per * n, x.shape[1], dtype=x.dtype, device=x.device)
         pos = self.members.index(self.row)

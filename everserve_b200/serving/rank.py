@@ -48,6 +48,7 @@ from ..contract import join as joinfmt
 from ..contract.daemon import DaemonConnection
 from ..engine.config import EngineConfig
 from ..engine.worker import Worker
+from ..ops import dense
 from ..proto import signals as sp
 from ..runtime.groups import Exchange, GroupCollective, SwappableGroups
 from ..runtime.layout import ParallelLayout
@@ -174,7 +175,7 @@ class RankProcess:
     def _host_shard(self, coll) -> dict:
         """The rank's weights in pinned host memory (made on the device, then moved off it)."""
         w = Worker(self.cfg, rank=self.rank, collective=coll, pipe=self.exchange, device=str(self.device))
-        host = {k: t.to("cpu").pin_memory() for k, t in w.model.weights.items()}
+        host = {k: dense(t).to("cpu").pin_memory() for k, t in w.model.weights.items()}
         del w
         torch.cuda.empty_cache()
         return host

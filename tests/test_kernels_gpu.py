@@ -263,3 +263,26 @@ def test_gemm_stream_k_repeats_and_tail(kops):
         assert torch.equal(kops.linear(x[:7].contiguous(), w), first[:7])
         close(first, x.float() @ w.float().t())
     assert kops.check_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 28672, 4096), (64, 4096, 14336), (7, 1000, 1792), (200, 3584, 4096),
+                                   (64, 128, 64)])
+def test_gemm_packed_weights(kops, M, N, K):
+    """A weight kept as its packed stage blocks (one bulk copy per stage) gives the tiled weight's
+    result bit for bit: the same tiles, k-blocks and order, only the loads differ. The packed
+    blocks round-trip to the weight; the fused SiLU-mul and residual epilogues take them too."""
+    from everserve_b200.ops import PackedWeight, interleave_gate_up
+
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
+    pw = PackedWeight(w)
+    assert torch.equal(pw.unpack(), w)
+    assert torch.equal(kops.linear(x, pw), kops.linear(x, w))
+    r = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    assert torch.equal(kops.linear(x, pw, residual=r), kops.linear(x, w, residual=r))
+    close(kops.linear(x, pw), x.float() @ w.float().t())
+    if N % 128 == 0 and M <= 64:
+        wi = interleave_gate_up(w).contiguous()
+        assert torch.equal(kops.linear_silu(x, PackedWeight(wi)), kops.linear_silu(x, wi))
+    assert kops.check_status() == 0
