@@ -16,8 +16,9 @@ Each member of the expert-parallel group owns ``el = E / W`` experts (position p
 Every wait is bounded and reports through the member's control words (the abort word, the late
 mask and the status word of the tensor-parallel collective's slot region), so a dead owner makes
 the call end with a status instead of a hang. Buffers are driver VMM allocations that outlive a
-member that dies. Member positions map to buffer rows through a device table, so a spare that
-takes a position serves its experts in captured graphs without recapture.
+member that dies. Member positions map to buffer rows through a device table, so the members'
+traffic follows a membership change inside captured graphs; which experts a member runs is fixed
+when its graph is captured, so a spare captures its graphs after it has taken its position.
 
 ``ExpertAllToAll.emulated`` plays the whole group on one GPU: one kernel launch carries every
 member's traffic between local buffers (the single-GPU numerics test).
@@ -176,7 +177,9 @@ class ExpertAllToAll:
         """Each local expert of each member played over what it received: `gate_up(e)` [2I, H] and
         `down(e)` [H, I] give global expert e's weights."""
         if self.pos < 0:
-            return  # no position: no experts
+            # no position: no experts; a graph captured now would keep running none after a take
+            assert not torch.cuda.is_current_stream_capturing(), "capture the expert graph after the take"
+            return
         for z in range(self.nz):
             for el in range(self.el):
                 e = (self.pos + z) * self.el + el

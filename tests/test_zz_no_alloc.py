@@ -83,6 +83,25 @@ def test_noalloc_matches_regular_entry_point(lib):
         assert torch.equal(out.view_as(expect), expect)
 
 
+def test_noalloc_on_a_second_device(lib):
+    """Kernel attributes and the scratch address are set up per device: the first call on another
+    device works and matches that device's regular entry point."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with torch.cuda.device(1):
+        assert lib.es_noalloc_setup() == 0
+        kops = KernelOps("cuda:1")
+        q, cache, bt, lens, max_len = _case(21)
+        assert q.device.index == 1
+        out = torch.empty(q.shape[0], q.shape[1] * q.shape[2], device="cuda", dtype=torch.bfloat16)
+        rc = _call(lib, q, cache, bt, lens, max_len, out)
+        assert rc == 0, lib.es_noalloc_last_error()
+        torch.cuda.synchronize()
+        kops.PART_TOKENS = 256
+        expect = kops.decode_attention(q, cache, bt, lens, 1.0 / math.sqrt(q.shape[2]), max_len)
+        assert torch.equal(out.view_as(expect), expect)
+
+
 def test_noalloc_rejects_oversized(lib):
     q, cache, bt, lens, _ = _case(13, B=4)
     out = torch.empty(q.shape[0], q.shape[1] * q.shape[2], device="cuda", dtype=torch.bfloat16)
