@@ -8,10 +8,11 @@
 // each of the 4 warps takes one block of every stage and computes S = q.K^T and O += P.V with
 // mma.sync m16n8k16 (the G query heads padded to 16 rows: decode attention is memory-bound, the
 // tensor cores only remove the SIMT arithmetic from the critical path), keeping its own online
-// softmax state. The warps merge at the end and each split writes (o / l, m, l); the last split of
-// a (sequence, kv head) to finish (a ticket per pair, counted with one atomic) merges the splits in
-// split order and writes the bf16 output, so there is no second launch. The split length is fixed
-// per engine, so a sequence's result never depends on the batch around it.
+// softmax state. The warps merge at the end and each split writes (o / l, m, l); a small kernel
+// then merges the splits in split order (or, with ES_ATTN_MERGE=fused, the last split of a
+// (sequence, kv head) to finish merges them, one atomic ticket per pair, and there is no second
+// launch). The split length is fixed per engine, so a sequence's result never depends on the
+// batch around it.
 #include <cuda.h>
 
 #include <cstdlib>
@@ -250,7 +251,9 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
       p.part_ml[row * 2 + 1] = den;
     }
   }
-  // the last split of the pair merges every split's (o, m, l) in split order
+  // without tickets the merge kernel merges the splits; with them the last split of the pair
+  // merges every split's (o, m, l) in split order
+  if (p.tickets == nullptr) return;
   __shared__ int s_last;
   __threadfence();
   __syncthreads();
@@ -278,6 +281,30 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   }
 }
 
+// Merge the splits of every (sequence, head) in split order; out rows of out_stride elements. The
+// same arithmetic, in the same order, as the in-kernel merge of the last split.
+__global__ void decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                                    const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out,
+                                    int64_t out_stride, int hq, int max_splits, int part_tokens, int d) {
+  pdl_wait();
+  pdl_launch();
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int ctx = ctx_lens[b];
+  const int ns = min(max_splits, (ctx + part_tokens - 1) / part_tokens);
+  const size_t row0 = ((size_t)b * hq + h) * max_splits;
+  float m = -INFINITY;
+  for (int s = 0; s < ns; s++) m = fmaxf(m, part_ml[(row0 + s) * 2]);
+  for (int e = threadIdx.x; e < d; e += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < ns; s++) {
+      const float w = part_ml[(row0 + s) * 2 + 1] * exp2f(part_ml[(row0 + s) * 2] - m);
+      num += w * part_o[(row0 + s) * d + e];
+      den += w;
+    }
+    out[(size_t)b * out_stride + (size_t)h * d + e] = f2bf(ns > 0 ? num / den : 0.f);
+  }
+}
+
 template <int D, int BS, int S>
 cudaError_t launch_decode(const CUtensorMap& map, const DecodeParams& p, int B, cudaStream_t stream) {
   using C = DecodeCfg<D, BS, S>;
@@ -299,16 +326,29 @@ cudaError_t launch_stages(int stages, const CUtensorMap& map, const DecodeParams
   }
 }
 
+// Kernel choices read once per process: ES_ATTN_TC=1 takes the tcgen05 kernel where it applies;
+// ES_ATTN_MERGE=fused has the mma.sync kernel's last split merge (tickets) instead of the merge
+// kernel. Both entry points (the binding and the allocation-free one) follow the same choices.
+bool use_tc() {
+  static const bool on = [] {
+    const char* v = std::getenv("ES_ATTN_TC");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+bool fused_merge() {
+  static const bool on = [] {
+    const char* v = std::getenv("ES_ATTN_MERGE");
+    return v && std::strcmp(v, "fused") == 0;
+  }();
+  return on;
+}
+
 }  // namespace attn
 
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (a.B == 0) return cudaSuccess;
-  // the tcgen05 kernel where it applies (ES_ATTN_TC=0: always this file's mma.sync kernel)
-  static const bool tc = [] {
-    const char* v = std::getenv("ES_ATTN_TC");
-    return !(v && v[0] == '0');
-  }();
-  if (tc && decode_tc_supported(a)) return launch_decode_tc(a, stream);
+  if (attn::use_tc() && decode_tc_supported(a)) return launch_decode_tc(a, stream);
   if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.hq / a.hkv > 8 || a.part_tokens % 64 != 0 || a.max_splits <= 0)
     return cudaErrorInvalidValue;
   if (a.s_kv != (int64_t)a.hkv * a.block_size * a.d || a.s_block != 2 * a.s_kv) return cudaErrorInvalidValue;
@@ -326,10 +366,10 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   p.part_tokens = a.part_tokens;
   p.scale_log2 = a.scale * attn::kLog2e;
   p.status = a.status;
-  p.tickets = a.tickets;
+  p.tickets = attn::fused_merge() ? a.tickets : nullptr;
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.out_stride = a.out_stride;
-  if (p.tickets == nullptr) return cudaErrorInvalidValue;
+  if (attn::fused_merge() && p.tickets == nullptr) return cudaErrorInvalidValue;
   // the layer's cache as rows of 64 elements (128 bytes); one box = one (block, kv head) tile
   const int64_t rows = a.num_blocks * 2 * a.hkv * a.block_size * (a.d / 64);
   const int box_rows = a.block_size * (a.d / 64);
@@ -341,7 +381,11 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   else if (a.d == 128 && a.block_size == 32) e = attn::launch_stages<128, 32>(a.stages, map, p, a.B, stream);
   else if (a.d == 64 && a.block_size == 32) e = attn::launch_stages<64, 32>(a.stages, map, p, a.B, stream);
   else return cudaErrorInvalidValue;
-  return e;
+  if (e != cudaSuccess || p.tickets != nullptr) return e;
+  dim3 mgrid(a.B, a.hq);
+  return launch_ex(attn::decode_merge_kernel, mgrid, dim3(a.d), 0, stream, 0, (const float*)a.part_o,
+                   (const float*)a.part_ml, a.ctx_lens, static_cast<__nv_bfloat16*>(a.out), a.out_stride, a.hq,
+                   a.max_splits, a.part_tokens, a.d);
 }
 
 }  // namespace es
@@ -455,7 +499,8 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   p.scale_log2 = scale * attn::kLog2e;
   p.status = status;
   // zero when the library loads; each launch leaves them at zero again
-  p.tickets = reinterpret_cast<int*>(base + ES_NOALLOC_PART_FLOATS + ES_NOALLOC_ML_FLOATS + 64);
+  int* tickets = reinterpret_cast<int*>(base + ES_NOALLOC_PART_FLOATS + ES_NOALLOC_ML_FLOATS + 64);
+  p.tickets = attn::fused_merge() ? tickets : nullptr;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride = out_stride;
   // tensor map encoded on the stack (no cache: nothing is allocated, not even on the host heap)
@@ -491,7 +536,7 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   da.out_stride = out_stride;
   da.part_o = p.part_o;
   da.part_ml = p.part_ml;
-  da.tickets = p.tickets;
+  da.tickets = tickets;
   da.status = status;
   da.B = batch;
   da.hq = q_heads;
@@ -502,8 +547,7 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   da.part_tokens = kPart;
   da.num_blocks = num_blocks;
   da.scale = scale;
-  const char* tc_env = std::getenv("ES_ATTN_TC");
-  if (!(tc_env && tc_env[0] == '0') && decode_tc_supported(da)) {
+  if (attn::use_tc() && decode_tc_supported(da)) {
     CUtensorMap qm;
     std::memset(&qm, 0, sizeof(qm));
     const cuuint64_t qdims[2] = {(cuuint64_t)head_dim, (cuuint64_t)batch * q_heads};
@@ -530,5 +574,11 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   else if (head_dim == 64 && block_size == 16) e = attn::launch_stages<64, 16>(3, map, p, batch, s);
   else if (head_dim == 128 && block_size == 32) e = attn::launch_stages<128, 32>(3, map, p, batch, s);
   else e = attn::launch_stages<64, 32>(3, map, p, batch, s);
+  if (e == cudaSuccess && p.tickets == nullptr) {
+    dim3 mgrid(batch, q_heads);
+    attn::decode_merge_kernel<<<mgrid, head_dim, 0, s>>>(p.part_o, p.part_ml, ctx_lens, static_cast<__nv_bfloat16*>(out),
+                                                         out_stride, q_heads, (int)splits, kPart, head_dim);
+    e = cudaGetLastError();
+  }
   return (int)e;
 }

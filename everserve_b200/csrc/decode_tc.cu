@@ -3,23 +3,26 @@
 // One query token per sequence; its G = Hq / Hkv query heads share a kv head (GQA). The work is
 // split into items (sequence, kv head, split of 256 positions). A CTA per SM walks the items
 // b + k * grid, and per item:
-//   * warp 4 lane 0 (producer): TMA of the item's G query rows (two 64-column halves, rows padded
+//   * warp 8 lane 0 (producer): TMA of the item's G query rows (two 64-column halves, rows padded
 //     to 16 with zeros), then its keys and values in 128-position chunks: per cache block one box
-//     per 64-column half, into a ring of 32 KB stages (K0, K1, V0, V1 per item), running up to the
-//     ring's depth ahead of the consumers, across items;
-//   * warp 5 lane 0 (MMA issuer): S^T = K . Q^T for each chunk (M = 128 positions on the TMEM
+//     per 64-column half, into 32 KB stages: a key ring of two (the item's two chunks, free again
+//     once the score MMAs have read them) and a value ring of four (two items: values wait for
+//     the softmax), so the next item's keys load while this item's values are still held;
+//   * warp 9 lane 0 (MMA issuer): S^T = K . Q^T for each chunk (M = 128 positions on the TMEM
 //     lanes, N = 16 head columns), then, once P is written, O^T = V^T . P^T over the item's 256
 //     positions (M = 128 head dims, V read straight from the cache tile as an MN-major operand);
 //     the scores of item n + 1 are computed while the softmax warps finish item n;
-//   * warps 0-3 (softmax): thread t owns TMEM lane t: position t of each chunk for the scores,
-//     head dim t for the output. Per head the maximum and the sum over the 256 positions are block
+//   * warps 0-7 (softmax, two groups of four taking alternate items, each with its own TMEM
+//     columns, P buffer and barriers, so one group's reductions, ticket and merge overlap the
+//     other's item): thread t of a group owns TMEM lane t: position t of each chunk for the
+//     scores, head dim t for the output. Per head the maximum and the sum over the 256 positions are block
 //     reductions; P goes to shared memory as bf16 in the MMA's swizzled layout. The item's
 //     normalized output, maximum and sum go to the split scratch, and the last split of a
 //     (sequence, kv head) to finish (one atomic ticket per pair) merges the splits in split order
 //     and writes the bf16 output, as the mma.sync kernel does, so both produce the same partials'
 //     format and merge.
 // Decode attention is bound by the K/V bytes; the tensor core takes the arithmetic off the warps,
-// which keep only the reductions, and the producer keeps up to six stages in flight per SM. Every
+// which keep only the reductions, and the producer keeps up to six stages loaded per SM. Every
 // wait is bounded; a wait that runs out sets the status word and the roles leave.
 #include <cuda.h>
 
@@ -40,16 +43,20 @@ constexpr int D = 128;                 // head dim (two 64-column halves)
 constexpr int kChunk = 128;            // positions per chunk (MMA M of S, K of a PV half)
 constexpr int kPart = 256;             // positions per item (two chunks)
 constexpr int kN = 16;                 // head columns of the MMAs (G <= 16, zero rows above G)
-constexpr int kStages = 6;
+constexpr int kKStages = 2;               // the key ring: one item's two chunks (freed by the S MMAs)
+constexpr int kVStages = 4;               // the value ring: two items (freed by the PV MMAs, later)
+constexpr int kStages = kKStages + kVStages;
 constexpr int kStageBytes = 2 * kChunk * 128;  // [half][128 rows][128 B]
 constexpr int kHalfBytes = kChunk * 128;
 constexpr int kQBytes = 2 * kN * 128;          // [half][16 rows][128 B]
 constexpr int kPBytes = (kPart / 64) * kN * 128;  // [64-position chunk][16 rows][128 B]
-constexpr int kSoftmax = 128;
-constexpr int kThreads = kSoftmax + 64;
-constexpr int kTmemCols = 128;  // S0 [0, 32), S1 [32, 64), O [64, 80)
+constexpr int kGroup = 128;               // softmax threads of one group (one per TMEM lane)
+constexpr int kGroups = 2;                 // items alternate between the groups
+constexpr int kThreads = kGroups * kGroup + 64;  // + producer warp + MMA warp
+constexpr int kProducerWarp = kGroups * 4, kMmaWarp = kProducerWarp + 1;
+constexpr int kTmemCols = 128;  // group g: S at [32 g, 32 g + 32), O at [64 + 16 g, 64 + 16 g + 16)
 constexpr int kOCol = 64;
-constexpr int kSmem = 1024 + kStages * kStageBytes + 2 * kQBytes + kPBytes + 512;
+constexpr int kSmem = 1024 + kStages * kStageBytes + 2 * kQBytes + kGroups * kPBytes + 512;
 static_assert(kSmem <= 227 * 1024, "shared memory");
 
 struct Params {
@@ -95,20 +102,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
   uint8_t* q_s = ring + kStages * kStageBytes;  // [2 buffers]
-  uint8_t* p_s = q_s + 2 * kQBytes;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(p_s + kPBytes);
-  uint64_t* kv_full = bar;                 // [kStages]
+  uint8_t* p_s = q_s + 2 * kQBytes;           // [group]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(p_s + kGroups * kPBytes);
+  uint64_t* kv_full = bar;                 // [kStages]: keys [0, kKStages), values after
   uint64_t* kv_empty = bar + kStages;      // [kStages]
   uint64_t* q_full = bar + 2 * kStages;    // [2]
   uint64_t* q_empty = q_full + 2;          // [2]
-  uint64_t* s_full = q_empty + 2;          // [2]
-  uint64_t* s_free = s_full + 2;           // [2]
-  uint64_t* p_full = s_free + 2;
-  uint64_t* o_full = p_full + 1;
-  uint64_t* mma_done = o_full + 1;
+  uint64_t* s_full = q_empty + 2;          // [group]
+  uint64_t* s_free = s_full + kGroups;     // [group]
+  uint64_t* p_full = s_free + kGroups;     // [group]
+  uint64_t* o_full = p_full + kGroups;     // [group]
+  uint64_t* mma_done = o_full + kGroups;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-  __shared__ float red_m[4][kN], red_l[4][kN];
-  __shared__ int s_fail, s_last;
+  __shared__ float red_m[kGroups][4][kN], red_l[kGroups][4][kN];
+  __shared__ int s_fail, s_last[kGroups];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.hq / p.hkv;
@@ -124,20 +131,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 2; s++) {
       ptx::mbar_init(&q_full[s], 1);
       ptx::mbar_init(&q_empty[s], 1);
-      ptx::mbar_init(&s_full[s], 1);
-      ptx::mbar_init(&s_free[s], kSoftmax);
     }
-    ptx::mbar_init(p_full, kSoftmax);
-    ptx::mbar_init(o_full, 1);
+    for (int g = 0; g < kGroups; g++) {
+      ptx::mbar_init(&s_full[g], 1);
+      ptx::mbar_init(&s_free[g], kGroup);
+      ptx::mbar_init(&p_full[g], kGroup);
+      ptx::mbar_init(&o_full[g], 1);
+    }
     ptx::mbar_init(mma_done, 1);
     ptx::fence_mbar_init();
   }
   // stale shared memory must be finite (a masked position's P is 0, and 0 * NaN is not), and the
   // query rows above G must stay zero: clear the ring, Q and P once
-  for (int i = threadIdx.x; i < (kStages * kStageBytes + 2 * kQBytes + kPBytes) / 16; i += kThreads)
+  for (int i = threadIdx.x; i < (kStages * kStageBytes + 2 * kQBytes + kGroups * kPBytes) / 16; i += kThreads)
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0u, 0u, 0u, 0u);
   ptx::fence_proxy_async();
-  if (warp == 5) ptx::tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == kMmaWarp) ptx::tmem_alloc(tmem_slot, kTmemCols);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -145,66 +154,78 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();  // q, the cache rows and the context lengths come from the kernels before
   pdl_launch();
 
-  if (warp == 4) {
-    // ---- producer -----------------------------------------------------------------------------
-    if (lane == 0) {
-      int n = 0;  // non-empty items so far
-      uint32_t q = 0;  // stages issued so far
-      bool ok = true;
-      for (int it = blockIdx.x; ok && it < p.n_items; it += gridDim.x) {
-        const Item x = item_of(p, it);
-        if (x.s0 >= x.ctx) continue;
-        const int qb = n & 1;
-        if (n >= 2 && !ptx::mbar_wait(&q_empty[qb], ((n >> 1) - 1) & 1)) {
-          ok = false;
-          break;
+  if (warp == kProducerWarp) {
+    // ---- producer: the whole warp; lane 0 waits and arms the barriers, the lanes issue the
+    // copies (one block-table entry per lane, loaded together once per item) --------------------
+    int n = 0;  // non-empty items so far
+    bool ok = true;
+    for (int it = blockIdx.x; ok && it < p.n_items; it += gridDim.x) {
+      const Item x = item_of(p, it);
+      if (x.s0 >= x.ctx) continue;
+      const int qb = n & 1;
+      const int nblk_item = (x.s1 - x.s0 + BS - 1) / BS;  // blocks of the item (<= kPart / BS <= 32)
+      const int* bt = p.block_tables + (size_t)x.b * p.bt_stride;
+      const int my_blk = lane < nblk_item ? bt[x.s0 / BS + lane] : 0;
+      if (lane == 0) {
+        ok = n < 2 || ptx::mbar_wait(&q_empty[qb], ((n >> 1) - 1) & 1);
+        if (ok) {
+          ptx::mbar_arrive_expect_tx(&q_full[qb], 2 * G * 128);
+          const int qrow = x.b * p.hq + x.kvh * G;
+          ptx::tma_load_2d(q_s + qb * kQBytes, &qmap, 0, qrow, &q_full[qb]);
+          ptx::tma_load_2d(q_s + qb * kQBytes + kN * 128, &qmap, 64, qrow, &q_full[qb]);
         }
-        ptx::mbar_arrive_expect_tx(&q_full[qb], 2 * G * 128);
-        const int qrow = x.b * p.hq + x.kvh * G;
-        ptx::tma_load_2d(q_s + qb * kQBytes, &qmap, 0, qrow, &q_full[qb]);
-        ptx::tma_load_2d(q_s + qb * kQBytes + kN * 128, &qmap, 64, qrow, &q_full[qb]);
-        const int* bt = p.block_tables + (size_t)x.b * p.bt_stride;
-        for (int part = 0; part < 4; part++, q++) {
-          const int st = (int)(q % kStages);
-          if (q >= (uint32_t)kStages && !ptx::mbar_wait(&kv_empty[st], ((q / kStages) - 1) & 1)) {
-            ok = false;
-            break;
-          }
-          const int kv = part >> 1, c = part & 1;
-          const int first = x.s0 + c * kChunk;
-          const int nblk = first >= x.s1 ? 0 : min(kChunk / BS, (x.s1 - first + BS - 1) / BS);
-          ptx::mbar_arrive_expect_tx(&kv_full[st], (uint32_t)nblk * BS * 256);
-          uint8_t* dst = ring + st * kStageBytes;
-          for (int j = 0; j < nblk; j++) {
-            const int blk = bt[first / BS + j];
-            const int row = ((blk * 2 + kv) * p.hkv + x.kvh) * BS;
-            ptx::tma_load_2d(dst + j * BS * 128, &cmap, 0, row, &kv_full[st]);
-            ptx::tma_load_2d(dst + kHalfBytes + j * BS * 128, &cmap, 64, row, &kv_full[st]);
-          }
-        }
-        n++;
       }
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      for (int part = 0; ok && part < 4; part++) {
+        const int kv = part >> 1, c = part & 1;
+        // the item's c-th chunk of keys (values): the ring's (2 n + c)-th use
+        const uint32_t u = 2u * n + c;
+        const int nst = kv ? kVStages : kKStages;
+        const int st = (kv ? kKStages : 0) + (int)(u % nst);
+        const int first = x.s0 + c * kChunk;
+        const int nblk = first >= x.s1 ? 0 : min(kChunk / BS, (x.s1 - first + BS - 1) / BS);
+        if (lane == 0) {
+          ok = u < (uint32_t)nst || ptx::mbar_wait(&kv_empty[st], ((u / nst) - 1) & 1);
+          if (ok) ptx::mbar_arrive_expect_tx(&kv_full[st], (uint32_t)nblk * BS * 256);
+        }
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);  // the stage is armed before any copy to it
+        // lane 2 j + h copies block j's half h (at most 2 * kChunk / BS <= 16 copies per chunk)
+        const int j = lane >> 1, half = lane & 1;
+        const int blk = __shfl_sync(0xFFFFFFFFu, my_blk, (c * (kChunk / BS) + j) & 31);
+        if (ok && j < nblk) {
+          const int row = ((blk * 2 + kv) * p.hkv + x.kvh) * BS;
+          ptx::tma_load_2d(ring + st * kStageBytes + half * kHalfBytes + j * BS * 128, &cmap, half * 64, row,
+                           &kv_full[st]);
+        }
+      }
+      if (ok) n++;
+    }
+    if (lane == 0) {
       if (!ok) s_fail = 1;
-      // no copy of this CTA may land after it leaves: wait for the stages still in flight
-      for (uint32_t r = q > (uint32_t)kStages ? q - kStages : 0; r < q; r++)
-        ptx::mbar_wait(&kv_full[r % kStages], (r / kStages) & 1);
+      // no copy of this CTA may land after it leaves: wait for the last uses of every stage
+      const uint32_t uses = 2u * n;
+      for (uint32_t u = uses > (uint32_t)kKStages ? uses - kKStages : 0; u < uses; u++)
+        ptx::mbar_wait(&kv_full[u % kKStages], (u / kKStages) & 1);
+      for (uint32_t u = uses > (uint32_t)kVStages ? uses - kVStages : 0; u < uses; u++)
+        ptx::mbar_wait(&kv_full[kKStages + u % kVStages], (u / kVStages) & 1);
       for (int r = max(0, n - 2); r < n; r++) ptx::mbar_wait(&q_full[r & 1], (r >> 1) & 1);
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---- MMA issuer ---------------------------------------------------------------------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(kChunk, kN);
       constexpr uint32_t idesc_o = ptx::idesc_bf16_f32(D, kN) | (1u << 15);  // A (V^T) MN-major
       bool ok = true;
       int n = 0;
+      // item m goes to softmax group m & 1: its S and O columns, its P buffer, its barriers
       auto issue_s = [&](int m) -> bool {
         const int qb = m & 1, sb = m & 1;
         if (!ptx::mbar_wait(&q_full[qb], (m >> 1) & 1)) return false;
-        if (m >= 2 && !ptx::mbar_wait(&s_free[sb], ((m >> 1) - 1) & 1)) return false;
+        if (m >= kGroups && !ptx::mbar_wait(&s_free[sb], ((m >> 1) - 1) & 1)) return false;
         for (int c = 0; c < 2; c++) {
-          const uint32_t qi = 4u * m + c;
-          const int st = (int)(qi % kStages);
-          if (!ptx::mbar_wait(&kv_full[st], (qi / kStages) & 1)) return false;
+          const uint32_t u = 2u * m + c;
+          const int st = (int)(u % kKStages);
+          if (!ptx::mbar_wait(&kv_full[st], (u / kKStages) & 1)) return false;
           ptx::tc_fence_after();
           const uint8_t* kt = ring + st * kStageBytes;
 #pragma unroll
@@ -221,23 +242,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       auto issue_pv = [&](int m) -> bool {
-        if (!ptx::mbar_wait(p_full, m & 1)) return false;
+        const int g = m & 1;
+        if (!ptx::mbar_wait(&p_full[g], (m >> 1) & 1)) return false;
         for (int c = 0; c < 2; c++) {
-          const uint32_t qi = 4u * m + 2 + c;
-          const int st = (int)(qi % kStages);
-          if (!ptx::mbar_wait(&kv_full[st], (qi / kStages) & 1)) return false;
+          const uint32_t u = 2u * m + c;
+          const int st = kKStages + (int)(u % kVStages);
+          if (!ptx::mbar_wait(&kv_full[st], (u / kVStages) & 1)) return false;
           ptx::tc_fence_after();
           const uint8_t* vt = ring + st * kStageBytes;
 #pragma unroll
           for (int ks = 0; ks < kChunk / 16; ks++) {
             const uint64_t ad = ptx::sw128_mnmajor_desc(ptx::smem_u32(vt + ks * 16 * 128), kHalfBytes);
             const int k = c * kChunk + ks * 16;
-            const uint64_t bd = ptx::sw128_kmajor_desc(ptx::smem_u32(p_s + (k >> 6) * kN * 128)) + 2 * ((k >> 4) & 3);
-            ptx::mma_f16_ss(tmem + kOCol, ad, bd, idesc_o, (c > 0 || ks > 0) ? 1u : 0u);
+            const uint64_t bd =
+                ptx::sw128_kmajor_desc(ptx::smem_u32(p_s + g * kPBytes + (k >> 6) * kN * 128)) + 2 * ((k >> 4) & 3);
+            ptx::mma_f16_ss(tmem + kOCol + g * kN, ad, bd, idesc_o, (c > 0 || ks > 0) ? 1u : 0u);
           }
           ptx::mma_commit(&kv_empty[st]);
         }
-        ptx::mma_commit(o_full);
+        ptx::mma_commit(&o_full[g]);
         return true;
       };
       for (int it = blockIdx.x; ok && it < p.n_items; it += gridDim.x) {
@@ -253,28 +276,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_wait(mma_done, 0);
     }
   } else {
-    // ---- softmax warps ------------------------------------------------------------------------
-    const int t = threadIdx.x;  // TMEM lane: a position of each chunk, then a head dim
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    // ---- softmax groups: group g takes the CTA's non-empty items n with n % 2 == g -------------
+    const int g = warp >> 2, wq = warp & 3;
+    const int t = (warp & 3) * 32 + lane;  // TMEM lane: a position of each chunk, then a head dim
+    const uint32_t lane_addr = tmem + ((uint32_t)(wq * 32) << 16);
+    const int bar_id = 1 + g;
+    uint8_t* pg = p_s + g * kPBytes;
     const float c = p.scale_log2;
     bool ok = true;
     int n = 0;
     for (int it = blockIdx.x; it < p.n_items; it += gridDim.x) {
       const Item x = item_of(p, it);
       if (x.s0 >= x.ctx) {
-        if (x.split == 0)  // an empty history: the output is zero
-          for (int i = t; i < G * D; i += kSoftmax)
+        if (x.split == 0 && g == 0)  // an empty history: the output is zero
+          for (int i = t; i < G * D; i += kGroup)
             p.out[(size_t)x.b * p.out_stride + (size_t)x.kvh * G * D + i] = f2bf(0.f);
         continue;
       }
-      const int sb = n & 1;
-      ok = ptx::mbar_wait(&s_full[sb], (n >> 1) & 1) && ok;
+      const int mine = n & 1, jj = n >> 1;
+      n++;
+      if (mine != g) continue;
+      ok = ptx::mbar_wait(&s_full[g], jj & 1) && ok;
       ptx::tc_fence_after();
       float s0[kN], s1[kN];
-      ptx::tmem_ld16(lane_addr + sb * 32, s0);
-      ptx::tmem_ld16(lane_addr + sb * 32 + kN, s1);
+      ptx::tmem_ld16(lane_addr + g * 32, s0);
+      ptx::tmem_ld16(lane_addr + g * 32 + kN, s1);
       ptx::tc_fence_before();
-      ptx::mbar_arrive(&s_free[sb]);
+      ptx::mbar_arrive(&s_free[g]);
       const bool v0 = x.s0 + t < x.s1, v1 = x.s0 + kChunk + t < x.s1;
       // per head: the maximum over the item's positions
 #pragma unroll
@@ -285,35 +313,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           float m = fmaxf(s0[h], s1[h]);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-          if (lane == 0) red_m[warp][h] = m;
+          if (lane == 0) red_m[g][wq][h] = m;
         }
       }
-      if (ptx::named_bar_or(1, kSoftmax, !ok)) break;  // the four warps leave together
+      if (ptx::named_bar_or(bar_id, kGroup, !ok)) break;  // the group's four warps leave together
       float mh[kN], lh[kN];
 #pragma unroll
       for (int h = 0; h < kN; h++) {
         if (h < G) {
-          mh[h] = fmaxf(fmaxf(red_m[0][h], red_m[1][h]), fmaxf(red_m[2][h], red_m[3][h]));
+          mh[h] = fmaxf(fmaxf(red_m[g][0][h], red_m[g][1][h]), fmaxf(red_m[g][2][h], red_m[g][3][h]));
           const float p0 = exp2f(s0[h] - mh[h]), p1 = exp2f(s1[h] - mh[h]);
-          *reinterpret_cast<__nv_bfloat16*>(p_s + p_off(h, t)) = __float2bfloat16(p0);
-          *reinterpret_cast<__nv_bfloat16*>(p_s + p_off(h, kChunk + t)) = __float2bfloat16(p1);
+          *reinterpret_cast<__nv_bfloat16*>(pg + p_off(h, t)) = __float2bfloat16(p0);
+          *reinterpret_cast<__nv_bfloat16*>(pg + p_off(h, kChunk + t)) = __float2bfloat16(p1);
           float l = p0 + p1;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
-          if (lane == 0) red_l[warp][h] = l;
+          if (lane == 0) red_l[g][wq][h] = l;
         }
       }
       ptx::fence_proxy_async();  // the tensor core reads P through the async proxy
       ptx::tc_fence_before();
-      ptx::mbar_arrive(p_full);
-      ptx::named_bar(1, kSoftmax);
+      ptx::mbar_arrive(&p_full[g]);
+      ptx::named_bar(bar_id, kGroup);
 #pragma unroll
       for (int h = 0; h < kN; h++)
-        if (h < G) lh[h] = (red_l[0][h] + red_l[1][h]) + (red_l[2][h] + red_l[3][h]);
-      ok = ptx::mbar_wait(o_full, n & 1) && ok;
+        if (h < G) lh[h] = (red_l[g][0][h] + red_l[g][1][h]) + (red_l[g][2][h] + red_l[g][3][h]);
+      ok = ptx::mbar_wait(&o_full[g], jj & 1) && ok;
       ptx::tc_fence_after();
       float o[kN];
-      ptx::tmem_ld16(lane_addr + kOCol, o);
+      ptx::tmem_ld16(lane_addr + kOCol + g * kN, o);
       ptx::tc_fence_before();
       // this split's normalized output, maximum and sum (the merge's input format)
 #pragma unroll
@@ -327,30 +355,53 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      n++;
-      // the last split of the pair merges every split's (o, m, l) in split order
-      __threadfence();
-      ptx::named_bar(1, kSoftmax);
+      // the last split of the pair merges every split's (o, m, l) in split order; the group's
+      // writes are ordered before its ticket by the barrier and one fence
+      ptx::named_bar(bar_id, kGroup);
       const int ns = min(p.max_splits, (x.ctx + kPart - 1) / kPart);
       if (t == 0) {
-        int* tk = p.tickets + (size_t)x.b * p.hkv + x.kvh;
-        s_last = atomicAdd(tk, 1) == ns - 1;
-        if (s_last) *tk = 0;  // every split of this launch has counted: the next launch starts at zero
-      }
-      ptx::named_bar(1, kSoftmax);
-      if (s_last) {
         __threadfence();
-        for (int g = 0; g < G; g++) {
-          const size_t row0 = ((size_t)x.b * p.hq + x.kvh * G + g) * p.max_splits;
+        int* tk = p.tickets + (size_t)x.b * p.hkv + x.kvh;
+        const bool last = atomicAdd(tk, 1) == ns - 1;
+        if (last) *tk = 0;  // every split of this launch has counted: the next launch starts at zero
+        s_last[g] = last;
+      }
+      ptx::named_bar(bar_id, kGroup);
+      if (s_last[g]) {
+        __threadfence();
+        for (int hh = 0; hh < G; hh++) {
+          const size_t row0 = ((size_t)x.b * p.hq + x.kvh * G + hh) * p.max_splits;
+          const float* ml = p.part_ml + row0 * 2;
+          const float* po = p.part_o + row0 * D + t;
+          // the splits' values in batches of eight independent loads, combined in split order
           float m = -INFINITY;
-          for (int sp = 0; sp < ns; sp++) m = fmaxf(m, __ldcg(p.part_ml + (row0 + sp) * 2));
-          float num = 0.f, den = 0.f;
-          for (int sp = 0; sp < ns; sp++) {
-            const float w = __ldcg(p.part_ml + (row0 + sp) * 2 + 1) * exp2f(__ldcg(p.part_ml + (row0 + sp) * 2) - m);
-            num += w * __ldcg(p.part_o + (row0 + sp) * D + t);
-            den += w;
+          for (int b0 = 0; b0 < ns; b0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = b0 + u < ns ? __ldcg(ml + (b0 + u) * 2) : -INFINITY;
+#pragma unroll
+            for (int u = 0; u < 8; u++) m = fmaxf(m, v[u]);
           }
-          p.out[(size_t)x.b * p.out_stride + (size_t)(x.kvh * G + g) * D + t] = f2bf(num / den);
+          float num = 0.f, den = 0.f;
+          for (int b0 = 0; b0 < ns; b0 += 8) {
+            float mm[8], ll[8], oo[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+              const bool in = b0 + u < ns;
+              mm[u] = in ? __ldcg(ml + (b0 + u) * 2) : 0.f;
+              ll[u] = in ? __ldcg(ml + (b0 + u) * 2 + 1) : 0.f;
+              oo[u] = in ? __ldcg(po + (size_t)(b0 + u) * D) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+              if (b0 + u < ns) {
+                const float w = ll[u] * exp2f(mm[u] - m);
+                num += w * oo[u];
+                den += w;
+              }
+            }
+          }
+          p.out[(size_t)x.b * p.out_stride + (size_t)(x.kvh * G + hh) * D + t] = f2bf(num / den);
         }
       }
     }
@@ -359,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 5) ptx::tmem_dealloc(tmem, kTmemCols);
+  if (warp == kMmaWarp) ptx::tmem_dealloc(tmem, kTmemCols);
   if (threadIdx.x == 0 && s_fail && p.status) atomicExch(p.status, (int)kTimeout);
 }
 

@@ -322,6 +322,15 @@ class PackedWeight:
     def device(self):
         return self.carrier.device
 
+    def dim(self) -> int:
+        return 2
+
+    def numel(self) -> int:
+        return self.n * self.k
+
+    def element_size(self) -> int:
+        return self.carrier.element_size()
+
     def unpack(self) -> torch.Tensor:
         return unpack_weight(self.packed, self.n, self.k)
 
