@@ -88,6 +88,23 @@ struct GemmArgs {
   int64_t rs_per = 0;
   // the weight pre-packed by (128-row tile, 64-wide k-block) into swizzled 16 KB blocks (nullable)
   const void* w_packed = nullptr;
+  // memory the next kernel reads, fetched into L2 while this GEMM runs (nullable; 16-byte aligned)
+  const void* prefetch = nullptr;
+  int64_t prefetch_bytes = 0;
+  // RoPE + paged-KV write epilogue of the qkv projection (nullable): the weight's 128-row tiles are
+  // the q heads, then the k heads, then the v heads (head dim 128); the bf16-rounded product is
+  // rotated (q, k) and written to q_out [M, hq * 128] and to the cache rows of slots[m] (k, v), the
+  // rope_kv_write kernel's arithmetic; `out` is not written
+  const struct RopeOut* rope = nullptr;
+};
+struct RopeOut {
+  const int64_t* positions;  // [M]
+  const float* cos_sin;      // [max_position, 128]: cos of dims 0..63, then sin
+  const int64_t* slots;      // [M] cache slot (block * block_size + offset), < 0: not written
+  void* q_out;               // [M, hq * 128] bf16
+  void* cache;               // the layer's paged cache, bf16
+  int64_t s_block, s_off, s_head, s_kv;  // element strides: block, offset in block, kv head, k -> v
+  int hq, hkv, block_size;
 };
 int64_t gemm_pick_bn(int64_t M);
 // the decode split plan (cluster split-K and CTAs per SM) for an N x K bf16 weight at M tokens
@@ -160,6 +177,9 @@ struct DecodeArgs {
   int64_t num_blocks;
   int stages;  // K/V ring depth (2..4)
   float scale;
+  // memory the next kernel reads, fetched into L2 while this one runs (nullable; 16-byte aligned)
+  const void* prefetch = nullptr;
+  int64_t prefetch_bytes = 0;
 };
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t s);
 // the tcgen05 persistent variant (decode_tc.cu): head dim 128, G <= 16, splits of 256 positions

@@ -39,7 +39,9 @@ struct DecodeParams {
   const int* ctx_lens;
   float* part_o;   // [B, Hq, max_splits, D]
   float* part_ml;  // [B, Hq, max_splits, 2]
-  int* tickets;    // [B, Hkv] zero between launches: splits of the pair done so far
+  int* tickets;    // [B, Hkv] zero between launches: splits of the pair done so far (nullable)
+  const uint8_t* pf;  // memory the next kernel reads, fetched into L2 meanwhile (nullable)
+  int64_t pf_bytes;
   __nv_bfloat16* out;  // [B, Hq * D] rows of out_stride
   int64_t out_stride;
   int hq, hkv, max_splits, part_tokens;
@@ -98,6 +100,8 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   }
   __syncthreads();
 
+  // the history is read once per step: its lines go first, ahead of what later kernels keep
+  const uint64_t pol = ptx::policy_evict_first();
   auto issue = [&](int c) {
     const int st = c % kStages;
     const int first = blk0 + c * kWarps;
@@ -108,12 +112,14 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
       const int row_k = (int)(((phys * 2 + 0) * p.hkv + kvh) * BS * C::kRowsPerTok);
       const int row_v = (int)(((phys * 2 + 1) * p.hkv + kvh) * BS * C::kRowsPerTok);
       uint8_t* dst = ring + st * C::kStageBytes + i * 2 * C::kTileBytes;
-      ptx::tma_load_2d(dst, &cmap, 0, row_k, &full[st]);
-      ptx::tma_load_2d(dst + C::kTileBytes, &cmap, 0, row_v, &full[st]);
+      ptx::tma_load_2d_hint(dst, &cmap, 0, row_k, &full[st], pol);
+      ptx::tma_load_2d_hint(dst + C::kTileBytes, &cmap, 0, row_v, &full[st], pol);
     }
   };
   if (tid == 0) {
     for (int c = 0; c < kStages - 1 && c < nchunks; c++) issue(c);
+    ptx::l2_prefetch_share(p.pf, p.pf_bytes, (int)(b + gridDim.x * (kvh + gridDim.y * split)),
+                           (int)(gridDim.x * gridDim.y * gridDim.z));
   }
 
   // q fragments (rows = the G heads, zero above G; rows 8..15 are always zero)
@@ -367,6 +373,8 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   p.scale_log2 = a.scale * attn::kLog2e;
   p.status = a.status;
   p.tickets = attn::fused_merge() ? a.tickets : nullptr;
+  p.pf = static_cast<const uint8_t*>(a.prefetch);
+  p.pf_bytes = a.prefetch_bytes;
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.out_stride = a.out_stride;
   if (attn::fused_merge() && p.tickets == nullptr) return cudaErrorInvalidValue;

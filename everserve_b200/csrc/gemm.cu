@@ -73,6 +73,10 @@ struct Params {
   // weights pre-packed per (tile, k-block) as 16 KB blocks already in the swizzled shared-memory
   // layout (pack_weight): one bulk copy per stage reads them sequentially (nullable)
   const uint8_t* w_packed;
+  // bytes the next kernel will read (its weights), fetched into L2 while this one runs (nullable)
+  const uint8_t* pf;
+  int64_t pf_bytes;
+  RopeOut rope;  // the qkv projection's RoPE + paged-KV write epilogue when rope.q_out is set
 };
 
 // The fused all-gather's wait: every member's pushers have raised their flags for this call in this
@@ -263,17 +267,28 @@ __global__ void __launch_bounds__(kThreads, CPS)
     // the weight tiles of the first stages depend on no kernel of the step: stream them while the
     // previous kernel finishes, then the activation tiles once it has
     const int pre = min(nkb, C::kStages);
+    // a decode GEMM (one token tile) reads each weight byte once: mark its lines first to go, so
+    // streaming them does not evict what is kept in L2 for later kernels
+    const bool once = gridDim.y == 1;
+    const uint64_t pol = ptx::policy_evict_first();
     auto load_w = [&](int stage, int kb) {
-      if (p.w_packed)
-        ptx::bulk_g2s(a_tiles + stage * C::kABytes, p.w_packed + ((size_t)blockIdx.x * p.kb + kb) * C::kABytes,
-                      C::kABytes, &full[stage]);
-      else
-        ptx::tma_load_2d(a_tiles + stage * C::kABytes, &tmap_w, kb * BK, n0, &full[stage]);
+      uint8_t* dst = a_tiles + stage * C::kABytes;
+      if (p.w_packed) {
+        const uint8_t* src = p.w_packed + ((size_t)blockIdx.x * p.kb + kb) * C::kABytes;
+        if (once) ptx::bulk_g2s_hint(dst, src, C::kABytes, &full[stage], pol);
+        else ptx::bulk_g2s(dst, src, C::kABytes, &full[stage]);
+      } else if (once) {
+        ptx::tma_load_2d_hint(dst, &tmap_w, kb * BK, n0, &full[stage], pol);
+      } else {
+        ptx::tma_load_2d(dst, &tmap_w, kb * BK, n0, &full[stage]);
+      }
     };
     for (int i = 0; i < pre; i++) {
       ptx::mbar_arrive_expect_tx(&full[i], C::kStageBytes);
       load_w(i, kblk(i));
     }
+    ptx::l2_prefetch_share(p.pf, p.pf_bytes, (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)),
+                           (int)(gridDim.x * gridDim.y * gridDim.z));
     pdl_wait();
     pdl_launch();
     const CUtensorMap* xmap = &tmap_x;
@@ -335,7 +350,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
 #pragma unroll
         for (int j = 0; j < 16; j++) v[j] = 0.f;
       }
-      if (S > 1 || kAR || p.silu) {
+      if (S > 1 || kAR || p.silu || p.rope.q_out) {
         // the ring is drained (all MMAs completed before `done`), so its smem holds the partial
 #pragma unroll
         for (int j = 0; j < 16; j++) partial[(c0 + j) * BM + r] = v[j];
@@ -352,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
       }
     }
   }
-  if (S > 1 || kAR || p.silu) {
+  if (S > 1 || kAR || p.silu || p.rope.q_out) {
     // publish the partials to the cluster, then reduce this CTA's row slice over all of them
     ptx::cluster_sync();
     const uint32_t rank = ptx::cluster_rank();
@@ -399,7 +414,59 @@ __global__ void __launch_bounds__(kThreads, CPS)
         }
       }
     }
-    const int ptotal = p.silu ? 0 : total;
+    if (!kAR && p.rope.q_out) {
+      // RoPE + KV-write epilogue: tile = one head of 128 dims (q heads, then k, then v). This rank
+      // sums dims [g0, g1) of the first half and their partners 64 further (rank order), rounds
+      // them to bf16 as the qkv output would be, rotates q and k by the token's position and
+      // writes q to q_out and k, v to the token's cache slot (the rope_kv_write arithmetic)
+      const RopeOut& R = p.rope;
+      const int head = blockIdx.x;
+      const int rows64 = ((64 / S) + 3) & ~3;
+      const int g0 = min(64, (int)rank * rows64);
+      const int g1 = (int)rank + 1 == S ? 64 : min(64, g0 + rows64);
+      const int gspan4 = (g1 - g0) >> 2;
+      for (int e = threadIdx.x; e < gspan4 * mcount; e += kThreads) {
+        const int col = e / gspan4, i = g0 + (e % gspan4) * 4;
+        const uint32_t off_a = (uint32_t)((col * BM + i) * 4), off_b = off_a + 64 * 4;
+        const float4 fa = cluster_sum(local, off_a, S);
+        const float4 fb = cluster_sum(local, off_b, S);
+        const float av[4] = {fa.x, fa.y, fa.z, fa.w}, bv[4] = {fb.x, fb.y, fb.z, fb.w};
+        const size_t m = (size_t)(m0 + col);
+        float ra[4], rb[4];
+        if (head < R.hq + R.hkv) {
+          const float* cs = R.cos_sin + R.positions[m] * 128;
+#pragma unroll
+          for (int z = 0; z < 4; z++) {
+            const float a = bf2f(f2bf(av[z])), b = bf2f(f2bf(bv[z]));
+            const float c = cs[i + z], sn = cs[64 + i + z];
+            ra[z] = a * c - b * sn;
+            rb[z] = b * c + a * sn;
+          }
+        } else {
+#pragma unroll
+          for (int z = 0; z < 4; z++) {
+            ra[z] = av[z];
+            rb[z] = bv[z];
+          }
+        }
+        const uint2 wa = make_uint2(ptx::pack_bf16x2(ra[0], ra[1]), ptx::pack_bf16x2(ra[2], ra[3]));
+        const uint2 wb = make_uint2(ptx::pack_bf16x2(rb[0], rb[1]), ptx::pack_bf16x2(rb[2], rb[3]));
+        __nv_bfloat16* dst;
+        if (head < R.hq) {
+          dst = static_cast<__nv_bfloat16*>(R.q_out) + m * (size_t)R.hq * 128 + (size_t)head * 128;
+        } else {
+          const int64_t slot = R.slots[m];
+          if (slot < 0) continue;
+          const int64_t blk = slot / R.block_size, off = slot % R.block_size;
+          dst = static_cast<__nv_bfloat16*>(R.cache) + blk * R.s_block + off * R.s_off +
+                (head < R.hq + R.hkv ? (int64_t)(head - R.hq) * R.s_head
+                                     : R.s_kv + (int64_t)(head - R.hq - R.hkv) * R.s_head);
+        }
+        *reinterpret_cast<uint2*>(dst + i) = wa;
+        *reinterpret_cast<uint2*>(dst + i + 64) = wb;
+      }
+    }
+    const int ptotal = (p.silu || p.rope.q_out) ? 0 : total;
     ClusterRow cur, nxt;
     if ((int)threadIdx.x < ptotal) {
       const int e = threadIdx.x;
@@ -697,7 +764,7 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.M == 0 || a.N == 0) return cudaSuccess;
   const int64_t n_tiles = (a.N + gemm::BM - 1) / gemm::BM;
   if (a.M <= 64 && a.valid == nullptr && a.ws != nullptr && a.sync != nullptr && a.w_packed == nullptr &&
-      (stream_k_enabled() || n_tiles > 4 * (int64_t)a.num_sms))
+      a.rope == nullptr && (stream_k_enabled() || n_tiles > 4 * (int64_t)a.num_sms))
     return launch_gemm_stream(a, a.silu != 0, stream);
   if (a.silu && (a.N % gemm::BM != 0 || a.residual != nullptr || a.scale != nullptr || a.pre != nullptr ||
                  a.valid != nullptr))
@@ -719,6 +786,17 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.ldp = (int)a.ldp;
   p.silu = a.silu;
   p.w_packed = static_cast<const uint8_t*>(a.w_packed);
+  p.pf = static_cast<const uint8_t*>(a.prefetch);
+  p.pf_bytes = a.prefetch_bytes;
+  if (a.rope != nullptr) {
+    const RopeOut& R = *a.rope;
+    if (a.N != (int64_t)(R.hq + 2 * R.hkv) * 128 || a.silu || a.residual != nullptr || a.scale != nullptr ||
+        a.pre != nullptr || a.valid != nullptr || R.q_out == nullptr || R.cache == nullptr || R.block_size <= 0 ||
+        reinterpret_cast<uintptr_t>(R.q_out) % 8 != 0 || reinterpret_cast<uintptr_t>(R.cache) % 8 != 0 ||
+        R.s_off % 4 != 0 || R.s_head % 4 != 0 || R.s_kv % 4 != 0 || R.s_block % 4 != 0)
+      return cudaErrorInvalidValue;
+    p.rope = R;
+  }
   if (a.valid != nullptr) {
     if (a.valid_cap <= 0 || a.valid_segs <= 0 || a.valid_cap * a.valid_segs < a.M) return cudaErrorInvalidValue;
     p.valid = a.valid;
@@ -767,6 +845,8 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
   p.kb = (int)((a.K + gemm::BK - 1) / gemm::BK);
   p.scale = a.scale;
   p.w_packed = static_cast<const uint8_t*>(a.w_packed);
+  p.pf = static_cast<const uint8_t*>(a.prefetch);
+  p.pf_bytes = a.prefetch_bytes;
   p.pre = static_cast<const __nv_bfloat16*>(a.pre);
   p.ldp = (int)a.ldp;
   p.two_shot = c.mc ? 0 : a.two_shot;  // the multicast variant pushes once already
@@ -841,6 +921,8 @@ cudaError_t launch_gemm_allgather(const GemmArgs& a, const CommArgs& c, int64_t 
   p.ag_ldx = (int)a.ldx;
   p.ag_k = (int)a.K;
   p.w_packed = static_cast<const uint8_t*>(a.w_packed);
+  p.pf = static_cast<const uint8_t*>(a.prefetch);
+  p.pf_bytes = a.prefetch_bytes;
   int cps = 1;
   gemm_plan(BN, a.N, a.K, a.num_sms, &p.splits, &cps);
   // every CTA waits for the pushers of every member: the whole grid must be resident at once

@@ -117,12 +117,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   if (warp == 0) {
     // ---- producer: the run's units in order (weights of the first stages before the wait) ----
     if (lane == 0) {
+      const uint64_t pol = ptx::policy_evict_first();  // the weights are read once per step
       const int pre = min(n_units, kStages);
       for (int i = 0; i < pre; i++) {
         const long long u = u0 + i;
         const int t = (int)(u / p.kb), k = (int)(u % p.kb);
         ptx::mbar_arrive_expect_tx(&full[i], kStageBytes);
-        ptx::tma_load_2d(a_tiles + i * kABytes, &tmap_w, k * BK, t * BM, &full[i]);
+        ptx::tma_load_2d_hint(a_tiles + i * kABytes, &tmap_w, k * BK, t * BM, &full[i], pol);
       }
       pdl_wait();
       pdl_launch();
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const long long u = u0 + i;
         const int t = (int)(u / p.kb), k = (int)(u % p.kb);
         ptx::mbar_arrive_expect_tx(&full[s], kStageBytes);
-        ptx::tma_load_2d(a_tiles + s * kABytes, &tmap_w, k * BK, t * BM, &full[s]);
+        ptx::tma_load_2d_hint(a_tiles + s * kABytes, &tmap_w, k * BK, t * BM, &full[s], pol);
         ptx::tma_load_2d(b_tiles + s * kBBytes, &tmap_x, k * BK, 0, &full[s]);
       }
     }

@@ -35,6 +35,16 @@ void check_bf16(const torch::Tensor& t, const char* name) {
 
 cudaStream_t cur() { return at::cuda::getCurrentCUDAStream(); }
 
+// Memory the next kernel reads, which this kernel fetches into L2 while it runs (nullable).
+template <typename A>
+void set_prefetch(A& a, const c10::optional<torch::Tensor>& t) {
+  if (!t.has_value() || !t->defined()) return;
+  TORCH_CHECK(t->is_cuda() && t->is_contiguous() && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+              "prefetch: a contiguous, 16-byte aligned device tensor");
+  a.prefetch = t->data_ptr();
+  a.prefetch_bytes = t->numel() * t->element_size();
+}
+
 // A weight pre-packed by ops.pack_weight: 16 KB blocks per (128-row tile, 64-wide k-block). `w`
 // then only carries the shape [N, K] (a stride-0 view); the kernels read the blocks.
 bool packed_weight(es::GemmArgs& a, const c10::optional<torch::Tensor>& w_packed, int64_t N, int64_t K) {
@@ -180,7 +190,8 @@ void mixture_terms(es::GemmArgs& a, const c10::optional<torch::Tensor>& scale, c
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optional<torch::Tensor> residual,
                torch::Tensor ws, torch::Tensor sync, torch::Tensor status, int64_t num_sms,
                c10::optional<torch::Tensor> scale, c10::optional<torch::Tensor> pre,
-               c10::optional<torch::Tensor> valid, int64_t valid_cap, c10::optional<torch::Tensor> w_packed) {
+               c10::optional<torch::Tensor> valid, int64_t valid_cap, c10::optional<torch::Tensor> w_packed,
+               c10::optional<torch::Tensor> prefetch) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
@@ -222,13 +233,15 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::optiona
     a.valid_cap = valid_cap;
     a.valid_segs = (int)valid->numel();
   }
+  set_prefetch(a, prefetch);
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
 }
 
 // out[M, N/2] = silu(gate) * up of x . w^T, w's rows gate/up interleaved by 64 (decode sizes)
 void gemm_silu(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor ws, torch::Tensor sync,
-               torch::Tensor status, int64_t num_sms, c10::optional<torch::Tensor> w_packed) {
+               torch::Tensor status, int64_t num_sms, c10::optional<torch::Tensor> w_packed,
+               c10::optional<torch::Tensor> prefetch) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
@@ -255,6 +268,64 @@ void gemm_silu(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tenso
   a.sync = reinterpret_cast<uint32_t*>(sync.data_ptr<int>());
   a.num_sms = (int)num_sms;
   a.silu = 1;
+  set_prefetch(a, prefetch);
+  const c10::cuda::CUDAGuard g(x.device());
+  ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
+}
+
+// q_out[M, hq * 128] and the cache rows of the step's tokens from x . w^T (the qkv projection),
+// RoPE and the paged-KV write in the GEMM's epilogue
+void gemm_rope(torch::Tensor x, torch::Tensor w, torch::Tensor positions, torch::Tensor cos_sin, torch::Tensor slots,
+               torch::Tensor q_out, torch::Tensor cache, int64_t hq, int64_t hkv, int64_t block_size,
+               std::vector<int64_t> strides, torch::Tensor ws, torch::Tensor sync, torch::Tensor status,
+               int64_t num_sms, c10::optional<torch::Tensor> w_packed, c10::optional<torch::Tensor> prefetch) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(q_out, "q_out");
+  check_bf16(cache, "cache");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1, "2-D operands, x K-contiguous");
+  es::GemmArgs a{};
+  const bool packed = packed_weight(a, w_packed, w.size(0), w.size(1));
+  TORCH_CHECK(packed || w.stride(1) == 1, "w K-contiguous");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && N == (hq + 2 * hkv) * 128, "w: [(hq + 2 hkv) * 128, K]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) == 128,
+              "cos_sin: fp32 [positions, 128]");
+  TORCH_CHECK(positions.scalar_type() == at::kLong && slots.scalar_type() == at::kLong &&
+                  positions.numel() >= M && slots.numel() >= M && positions.is_cuda() && slots.is_cuda(),
+              "int64 positions and slots on the device, one per row");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == M * hq * 128, "q_out: [M, hq, 128] contiguous");
+  TORCH_CHECK(strides.size() == 5 && strides[4] == 1, "five cache strides, head dim contiguous");
+  TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.numel() >= es::gemm_ws_floats(num_sms), "stream-K workspace too small");
+  TORCH_CHECK(sync.scalar_type() == at::kInt && sync.numel() >= es::gemm_sync_words(num_sms), "sync words too small");
+  es::RopeOut r{};
+  r.positions = positions.data_ptr<int64_t>();
+  r.cos_sin = cos_sin.data_ptr<float>();
+  r.slots = slots.data_ptr<int64_t>();
+  r.q_out = q_out.data_ptr();
+  r.cache = cache.data_ptr();
+  r.s_block = strides[0];
+  r.s_off = strides[1];
+  r.s_head = strides[2];
+  r.s_kv = strides[3];
+  r.hq = (int)hq;
+  r.hkv = (int)hkv;
+  r.block_size = (int)block_size;
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.out = q_out.data_ptr();  // not written: the epilogue writes q_out and the cache
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ldx = x.stride(0);
+  a.ldw = w.stride(0);
+  a.ldo = N;
+  a.status = status.data_ptr<int>();
+  a.ws = ws.data_ptr<float>();
+  a.sync = reinterpret_cast<uint32_t*>(sync.data_ptr<int>());
+  a.num_sms = (int)num_sms;
+  a.rope = &r;
+  set_prefetch(a, prefetch);
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_bf16(a, cur()));
 }
@@ -444,7 +515,7 @@ void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::op
                     torch::Tensor status, int64_t num_sms, torch::Tensor peers, torch::Tensor order, torch::Tensor call,
                     int64_t ctrl, int64_t row, int64_t mc, torch::Tensor seqs, c10::optional<torch::Tensor> scale,
                     c10::optional<torch::Tensor> pre, int64_t two_shot, int64_t rs_per,
-                    c10::optional<torch::Tensor> w_packed) {
+                    c10::optional<torch::Tensor> w_packed, c10::optional<torch::Tensor> prefetch) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   check_bf16(out, "out");
@@ -476,6 +547,7 @@ void gemm_allreduce(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::op
   mixture_terms(a, scale, pre);
   a.two_shot = (int)two_shot;
   a.rs_per = rs_per;
+  set_prefetch(a, prefetch);
   const c10::cuda::CUDAGuard g(x.device());
   ES_CHECK_CUDA(es::launch_gemm_allreduce(a, comm_args(peers, order, call, ctrl, row, mc, seqs), cur()));
 }
@@ -518,7 +590,8 @@ void gemm_allgather(torch::Tensor x, torch::Tensor w, torch::Tensor out, c10::op
 
 void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
                   torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor tickets,
-                  torch::Tensor status, int64_t max_splits, int64_t part_tokens, double scale, int64_t stages) {
+                  torch::Tensor status, int64_t max_splits, int64_t part_tokens, double scale, int64_t stages,
+                  c10::optional<torch::Tensor> prefetch) {
   check_bf16(q, "q");
   check_bf16(cache, "cache");
   check_bf16(out, "out");
@@ -562,6 +635,7 @@ void paged_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tabl
   a.max_splits = (int)max_splits;
   a.part_tokens = (int)part_tokens;
   a.scale = (float)scale;
+  set_prefetch(a, prefetch);
   const c10::cuda::CUDAGuard g(q.device());
   ES_CHECK_CUDA(es::launch_paged_decode(a, cur()));
 }
@@ -759,15 +833,27 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("residual"), pybind11::arg("ws"), pybind11::arg("sync"),
         pybind11::arg("status"), pybind11::arg("num_sms"), pybind11::arg("scale") = pybind11::none(),
         pybind11::arg("pre") = pybind11::none(), pybind11::arg("valid") = pybind11::none(),
-        pybind11::arg("valid_cap") = 0, pybind11::arg("w_packed") = pybind11::none());
+        pybind11::arg("valid_cap") = 0, pybind11::arg("w_packed") = pybind11::none(),
+        pybind11::arg("prefetch") = pybind11::none());
   m.def("gemm_pick_bn", &es::gemm_pick_bn);
   m.def("gemm_pick_splits", &es::gemm_pick_splits);
   m.def("gemm_ws_floats", &es::gemm_ws_floats);
   m.def("gemm_sync_words", &es::gemm_sync_words);
-  m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)");
+  m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)", pybind11::arg("q"),
+        pybind11::arg("cache"), pybind11::arg("block_tables"), pybind11::arg("ctx_lens"), pybind11::arg("out"),
+        pybind11::arg("part_o"), pybind11::arg("part_ml"), pybind11::arg("tickets"), pybind11::arg("status"),
+        pybind11::arg("max_splits"), pybind11::arg("part_tokens"), pybind11::arg("scale"), pybind11::arg("stages"),
+        pybind11::arg("prefetch") = pybind11::none());
   m.def("gemm_silu", &gemm_silu, "GEMM with SiLU-mul fused into its epilogue (gate/up rows interleaved by 64)",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("ws"), pybind11::arg("sync"),
-        pybind11::arg("status"), pybind11::arg("num_sms"), pybind11::arg("w_packed") = pybind11::none());
+        pybind11::arg("status"), pybind11::arg("num_sms"), pybind11::arg("w_packed") = pybind11::none(),
+        pybind11::arg("prefetch") = pybind11::none());
+  m.def("gemm_rope", &gemm_rope, "qkv GEMM with RoPE and the paged-KV write in its epilogue", pybind11::arg("x"),
+        pybind11::arg("w"), pybind11::arg("positions"), pybind11::arg("cos_sin"), pybind11::arg("slots"),
+        pybind11::arg("q_out"), pybind11::arg("cache"), pybind11::arg("hq"), pybind11::arg("hkv"),
+        pybind11::arg("block_size"), pybind11::arg("strides"), pybind11::arg("ws"), pybind11::arg("sync"),
+        pybind11::arg("status"), pybind11::arg("num_sms"), pybind11::arg("w_packed") = pybind11::none(),
+        pybind11::arg("prefetch") = pybind11::none());
   m.def("quant_fp8", &quant_fp8, "x -> e4m3 with a scale per token and 128-wide block");
   m.def("gemm_fp8", &gemm_fp8, "block-scaled fp8 GEMM (tcgen05 kind::f8f6f4, scales per 128-wide K block)");
   m.def("paged_prefill", &paged_prefill, "paged causal prefill attention (tcgen05: S and P.V in TMEM, TMA K/V tiles)");
@@ -787,7 +873,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("num_sms"), pybind11::arg("peers"), pybind11::arg("order"), pybind11::arg("call"),
         pybind11::arg("ctrl"), pybind11::arg("row"), pybind11::arg("mc"), pybind11::arg("seqs"),
         pybind11::arg("scale") = pybind11::none(), pybind11::arg("pre") = pybind11::none(),
-        pybind11::arg("two_shot") = 0, pybind11::arg("rs_per") = 0, pybind11::arg("w_packed") = pybind11::none());
+        pybind11::arg("two_shot") = 0, pybind11::arg("rs_per") = 0, pybind11::arg("w_packed") = pybind11::none(),
+        pybind11::arg("prefetch") = pybind11::none());
   m.def("gemm_allgather", &gemm_allgather,
         "column-parallel GEMM with the all-gather of its token rows fused (peer stores into each member's buffer)",
         pybind11::arg("x"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("residual"), pybind11::arg("status"),

@@ -64,6 +64,51 @@ ES_DEVICE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* ba
       : "memory");
 }
 
+// An L2 policy for data read once per step (weights, the K/V history): its lines are the first
+// candidates for eviction, so streaming them does not push out lines fetched ahead for later use.
+ES_DEVICE uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0;" : "=l"(p));
+  return p;
+}
+
+// Fetch [src, src + bytes) into L2 ahead of its use (16-byte aligned, size % 16 == 0). No wait.
+ES_DEVICE void l2_prefetch(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// This CTA's share of a prefetch of [base, base + bytes) spread over `n` CTAs (index `i`).
+ES_DEVICE void l2_prefetch_share(const uint8_t* base, int64_t bytes, int i, int n) {
+  if (base == nullptr || bytes <= 0 || n <= 0) return;
+  const int64_t per = ((bytes + n - 1) / n + 15) & ~int64_t(15);
+  const int64_t lo = per * i;
+  if (lo >= bytes) return;
+  int64_t len = bytes - lo < per ? bytes - lo : per;
+  len &= ~int64_t(15);
+  constexpr int64_t kPiece = (int64_t)1 << 20;
+  for (int64_t off = 0; off < len; off += kPiece)
+    l2_prefetch(base + lo + off, (uint32_t)(len - off < kPiece ? len - off : kPiece));
+}
+
+// One-dimensional bulk copy global -> shared with an L2 cache policy.
+ES_DEVICE void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Two-dimensional tiled tensor copy global -> shared (TMA) with an L2 cache policy.
+ES_DEVICE void tma_load_2d_hint(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar,
+                                uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Two-dimensional tiled tensor copy global -> shared (TMA). x is the innermost coordinate.
 ES_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar) {
   asm volatile(

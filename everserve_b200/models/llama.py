@@ -60,13 +60,16 @@ class TPGroup:
             return t
         return self.collective.all_reduce(t)
 
-    def linear_allreduce(self, ops, x, w, residual=None, scale=None, pre=None):
+    def linear_allreduce(self, ops, x, w, residual=None, scale=None, pre=None, prefetch=None):
         """Row-parallel linear (x . w^T * scale + pre) followed by the sum over ranks, then the
-        residual; one fused kernel when the collective has it."""
+        residual; one fused kernel when the collective has it. `prefetch`: what the next kernel
+        reads, fetched into L2 meanwhile (kernels only)."""
         if self.size == 1:
-            return ops.linear(x, w, residual=residual, scale=scale, pre=pre)
+            return ops.linear(x, w, residual=residual, scale=scale, pre=pre, prefetch=prefetch)
         fused = getattr(self.collective, "linear_allreduce", None)
         if fused is not None and ops.kind == "kernel":
+            if getattr(self.collective, "region", None) is not None:  # the peer-memory collective
+                return fused(ops, x, w, residual, scale=scale, pre=pre, prefetch=prefetch)
             return fused(ops, x, w, residual, scale=scale, pre=pre)
         y = self.collective.all_reduce(ops.linear(x, w, scale=scale, pre=pre))
         if residual is not None:
@@ -173,6 +176,9 @@ class DecoderLM:
         # computes SiLU-mul in its epilogue (ops.linear_silu); the reference ops keep gate then up
         self.fused_silu = (not cfg.is_moe and self.ops.kind == "kernel" and self.inter % 64 == 0
                            and os.environ.get("ES_FUSED_SILU", "1") != "0")
+        # the qkv GEMM's RoPE + KV-write epilogue (kernels, bf16, head dim 128, no qkv bias)
+        self.fused_rope = (self.ops.kind == "kernel" and not self.fp8 and cfg.head_dim == 128
+                           and not cfg.qkv_bias and os.environ.get("ES_FUSED_ROPE", "1") != "0")
         self.packed_weights = (self.ops.kind == "kernel" and not cfg.is_moe
                                and os.environ.get("ES_PACK_WEIGHTS", "1") != "0")
         self.cos_sin = ref.cos_sin_table(cfg.head_dim, cfg.max_position, cfg.rope_theta, cfg.rope_scaling).to(self.device)
@@ -207,10 +213,10 @@ class DecoderLM:
             return ops.linear_fp8(x, self.weights[key + ".q8"], self.weights[key + ".s8"], residual)
         return ops.linear(x, self.weights[key], residual=residual)
 
-    def _row_parallel(self, ops, x, key: str, residual=None):
+    def _row_parallel(self, ops, x, key: str, residual=None, prefetch=None):
         """A row-parallel projection summed over the tensor-parallel ranks, then the residual."""
         if not self.fp8:
-            return self.tp.linear_allreduce(ops, x, self.weights[key], residual)
+            return self.tp.linear_allreduce(ops, x, self.weights[key], residual, prefetch=prefetch)
         if self.tp.size == 1:
             return self._linear(ops, x, key, residual)
         y = self.tp.all_reduce(self._linear(ops, x, key))
@@ -308,13 +314,19 @@ class DecoderLM:
         for i, l in enumerate(range(self.l0, self.l1)):
             p = f"l{l}."
             cache = caches[i]
-            qkv = self._linear(ops, h, p + "qkv")
-            q = ops.rope_kv_write(qkv, W.get(p + "qkv_bias"), inp.positions, self.cos_sin, inp.slots, cache,
-                                  self.hq, self.hkv, bs)
+            if self.fused_rope:
+                # one kernel: the qkv GEMM rotates q and k and writes k and v to the cache
+                q = ops.linear_rope_kv(h, W[p + "qkv"], inp.positions, self.cos_sin, inp.slots, cache,
+                                       self.hq, self.hkv, bs)
+            else:
+                qkv = self._linear(ops, h, p + "qkv")
+                q = ops.rope_kv_write(qkv, W.get(p + "qkv_bias"), inp.positions, self.cos_sin, inp.slots, cache,
+                                      self.hq, self.hkv, bs)
             if inp.is_decode:
                 if ops.kind == "kernel":
+                    # the attention streams the history; meanwhile it brings o_proj's weights into L2
                     a = ops.decode_attention(q, cache, inp.block_tables, inp.ctx_lens, self.scale,
-                                             inp.max_model_len or None)
+                                             inp.max_model_len or None, prefetch=W.get(p + "o"))
                 else:
                     a = ops.decode_attention(q, cache, inp.block_tables, inp.ctx_lens, self.scale)
             else:
@@ -334,7 +346,9 @@ class DecoderLM:
                     act = ops.linear_silu(h, W[p + "gate_up"])
                 else:
                     act = ops.silu_mul(ops.linear(h, W[p + "gate_up"]))
-                m = self._row_parallel(ops, act, p + "down")
+                # decode: the down projection brings the next layer's qkv weights into L2
+                pf = W.get(f"l{l + 1}.qkv") if inp.is_decode and l + 1 < self.l1 else None
+                m = self._row_parallel(ops, act, p + "down", prefetch=pf)
             nxt = f"l{l + 1}.in_norm" if l + 1 < self.l1 else None
             if nxt is not None:
                 h = ops.rmsnorm(m, W[nxt], c.rms_eps, residual)
@@ -376,8 +390,9 @@ class DecoderLM:
                                   self.hq, self.hkv, bs)
             if inp.is_decode:
                 if ops.kind == "kernel":
+                    # the attention streams the history; meanwhile it brings o_proj's weights into L2
                     a = ops.decode_attention(q, cache, inp.block_tables, inp.ctx_lens, self.scale,
-                                             inp.max_model_len or None)
+                                             inp.max_model_len or None, prefetch=W.get(p + "o"))
                 else:
                     a = ops.decode_attention(q, cache, inp.block_tables, inp.ctx_lens, self.scale)
             else:

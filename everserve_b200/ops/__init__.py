@@ -35,7 +35,8 @@ class RefOps:
     def rmsnorm(self, x, w, eps, residual=None):
         return ref.rmsnorm(x, w, eps, residual)
 
-    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None, valid=None, valid_cap=0):
+    def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None, valid=None, valid_cap=0,
+               prefetch=None):
         # rows a grouped GEMM would skip are padding nobody reads: computing them changes nothing
         y = ref.linear(x, dense(w), bias, residual, scale, pre)
         if out is not None:
@@ -52,7 +53,10 @@ class RefOps:
     def rope_kv_write(self, qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size):
         return ref.rope_kv_write(qkv, bias, positions, cos_sin, slots, cache, hq, hkv, block_size)
 
-    def decode_attention(self, q, cache, block_tables, ctx_lens, scale):
+    def linear_rope_kv(self, x, w, positions, cos_sin, slots, cache, hq, hkv, block_size, prefetch=None):
+        return self.rope_kv_write(self.linear(x, w), None, positions, cos_sin, slots, cache, hq, hkv, block_size)
+
+    def decode_attention(self, q, cache, block_tables, ctx_lens, scale, max_model_len=None, prefetch=None):
         B = q.shape[0]
         seq = torch.arange(B, device=q.device)
         return ref.paged_attention(q, cache, block_tables, ctx_lens, seq, ctx_lens.long() - 1, scale)
@@ -65,7 +69,7 @@ class RefOps:
             gu = deinterleave_gate_up(gu.t()).t()
         return ref.silu_mul(gu)
 
-    def linear_silu(self, x, w):
+    def linear_silu(self, x, w, prefetch=None):
         return self.silu_mul(self.linear(x, w), interleaved=True)
 
     def linear_fp8(self, x, w8, w_scale, residual=None, silu: bool = False):
@@ -150,7 +154,7 @@ class KernelOps:
         return y
 
     def linear(self, x, w, bias=None, residual=None, out=None, scale=None, pre=None, valid=None, valid_cap=0,
-               w_packed=None):
+               w_packed=None, prefetch=None):
         """`valid` (int32 counts of segments of `valid_cap` rows) makes it a grouped GEMM whose
         token tiles holding no counted row are skipped and left unwritten. `w_packed`
         (``pack_weight(w)``) streams the weight as contiguous swizzled blocks instead of tiles."""
@@ -166,7 +170,7 @@ class KernelOps:
         if isinstance(w, PackedWeight):
             w, w_packed = w.carrier, w.packed
         self.C.gemm_bf16(x, w, out, residual, self._ws, self._ctr, self.status, self.num_sms, scale, pre, valid,
-                         valid_cap, w_packed)
+                         valid_cap, w_packed, prefetch_target(prefetch))
         return out
 
     def quant_fp8(self, x):
@@ -202,7 +206,22 @@ class KernelOps:
                              list(cache.stride()[i] for i in (0, 3, 2, 1, 4)))
         return q
 
-    def decode_attention(self, q, cache, block_tables, ctx_lens, scale, max_model_len=None):
+    def linear_rope_kv(self, x, w, positions, cos_sin, slots, cache, hq, hkv, block_size, prefetch=None):
+        """The qkv projection with RoPE and the paged-KV write in the GEMM's epilogue: q [T, hq, 128]
+        and the cache rows of `slots`, as ``rope_kv_write(linear(x, w), ...)`` computes them (the
+        product rounded to bf16 before the rotation). Head dim 128, no qkv bias."""
+        T = x.shape[0]
+        q = torch.empty(T, hq, 128, dtype=x.dtype, device=x.device)
+        self.reserve_linear()
+        wt, wp = weight_args(w)
+        self.C.gemm_rope(x, wt, positions, cos_sin, slots, q, cache, hq, hkv, block_size,
+                         list(cache.stride()[i] for i in (0, 3, 2, 1, 4)), self._ws, self._ctr, self.status,
+                         self.num_sms, wp, prefetch_target(prefetch))
+        return q
+
+    def decode_attention(self, q, cache, block_tables, ctx_lens, scale, max_model_len=None, prefetch=None):
+        """`prefetch` (a tensor or packed weight the next kernel reads) is fetched into L2 while the
+        attention streams the history, which it marks first to be evicted."""
         B, hq, d = q.shape
         bs = cache.shape[3]
         if max_model_len is None:
@@ -211,7 +230,7 @@ class KernelOps:
         self.reserve_attention(B, hq, d, max_model_len)
         out = torch.empty(B, hq, d, dtype=q.dtype, device=q.device)
         self.C.paged_decode(q, cache, block_tables, ctx_lens, out, self._part_o, self._part_ml, self._tickets,
-                            self.status, ms, self.PART_TOKENS, scale, self.ATTN_STAGES)
+                            self.status, ms, self.PART_TOKENS, scale, self.ATTN_STAGES, prefetch_target(prefetch))
         return out
 
     def prefill_attention(self, q, cache, block_tables, ctx_lens, q_seq, q_pos, scale, tiles=None):
@@ -231,7 +250,7 @@ class KernelOps:
         self.C.silu_mul(gu, out, interleaved)
         return out
 
-    def linear_silu(self, x, w):
+    def linear_silu(self, x, w, prefetch=None):
         """silu(gate) * up of x . w^T for a gate/up weight interleaved by 64 rows
         (``interleave_gate_up``): one GEMM with the SiLU-mul in its epilogue (each 128-row tile
         holds 64 gates and their up rows)."""
@@ -239,7 +258,7 @@ class KernelOps:
         self.reserve_linear()
         out = torch.empty(M, w.shape[0] // 2, dtype=x.dtype, device=x.device)
         wt, wp = weight_args(w)
-        self.C.gemm_silu(x, wt, out, self._ws, self._ctr, self.status, self.num_sms, wp)
+        self.C.gemm_silu(x, wt, out, self._ws, self._ctr, self.status, self.num_sms, wp, prefetch_target(prefetch))
         return out
 
     def argmax(self, logits):
@@ -338,6 +357,17 @@ class PackedWeight:
 def weight_args(w):
     """(the tensor a binding takes as `w`, the packed blocks or None)."""
     return (w.carrier, w.packed) if isinstance(w, PackedWeight) else (w, None)
+
+
+L2_PREFETCH = os.environ.get("ES_L2_PREFETCH", "1") != "0"
+
+
+def prefetch_target(t):
+    """The tensor whose bytes a kernel fetches into L2 for the next kernel (None: nothing), from a
+    tensor or a packed weight; ES_L2_PREFETCH=0 turns the prefetches off."""
+    if t is None or not L2_PREFETCH:
+        return None
+    return t.packed if isinstance(t, PackedWeight) else t
 
 
 def dense(w) -> torch.Tensor:

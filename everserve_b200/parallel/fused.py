@@ -22,7 +22,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _ext
-from ..ops import weight_args
+from ..ops import prefetch_target, weight_args
 from .nccl import GroupCollective
 from .slot import HANDLE_BYTES, MAX_ROWS, SlotRegion
 from .symm import PeerMapping, SymmetricBuffer
@@ -215,7 +215,7 @@ class FusedTPCollective:
         return self.all_reduce_into(t, t)
 
     def linear_allreduce(self, ops, x: torch.Tensor, w: torch.Tensor, residual=None, scale=None,
-                         pre=None) -> torch.Tensor:
+                         pre=None, prefetch=None) -> torch.Tensor:
         """Row-parallel linear (x . w^T * scale + pre) summed over the members, then the residual;
         one fused kernel at decode sizes. ES_AR_TWO_SHOT=1 makes the fused sum a reduce-scatter to
         each tile's owner and an all-gather (a quarter of the one-shot push's NVLink bytes at 8)."""
@@ -223,7 +223,7 @@ class FusedTPCollective:
             out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
             wt, wp = weight_args(w)
             self.C.gemm_allreduce(x, wt, out, residual, ops.status, ops.num_sms, *self._comm(), scale, pre,
-                                  self.two_shot, 0, wp)
+                                  self.two_shot, 0, wp, prefetch_target(prefetch))
             return out
         if x.dtype == torch.bfloat16 and not torch.cuda.is_current_stream_capturing():
             return self._linear_allreduce_overlapped(ops, x, w, residual, scale, pre)

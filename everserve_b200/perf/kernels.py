@@ -72,9 +72,13 @@ def main() -> None:
             ms = _time(lambda: k.linear(x, w, out=out), flush=flush)
             cub = _time(lambda: torch.matmul(x, w.t(), out=out), flush=flush)
             byts = (N * K + M * K + M * N) * 2
+            # the same launch with the weights still in L2 from the launch before (no flush): what
+            # the GEMM would take if its weights were fetched into L2 while the kernel before ran
+            hot = _time(lambda: k.linear(x, w, out=out))
             rows.append({"kernel": "gemm", "name": name, "M": M, "N": N, "K": K,
                          "us": round(ms * 1e3, 2), "gb_s": round(byts / ms / 1e6, 1),
-                         "cublas_us": round(cub * 1e3, 2), "cublas_gb_s": round(byts / cub / 1e6, 1)})
+                         "cublas_us": round(cub * 1e3, 2), "cublas_gb_s": round(byts / cub / 1e6, 1),
+                         "l2_resident_us": round(hot * 1e3, 2)})
             # the same weights pre-packed into swizzled 16 KB blocks (one bulk copy per stage)
             wp = pack_weight(w)
             ref_out = k.linear(x, w).clone()

@@ -286,3 +286,40 @@ def test_gemm_packed_weights(kops, M, N, K):
         wi = interleave_gate_up(w).contiguous()
         assert torch.equal(kops.linear_silu(x, PackedWeight(wi)), kops.linear_silu(x, wi))
     assert kops.check_status() == 0
+
+
+@pytest.mark.parametrize("T,hq,hkv,packed", [(64, 32, 8, False), (7, 8, 2, True), (130, 16, 4, False)])
+def test_gemm_rope_kv_epilogue(kops, T, hq, hkv, packed):
+    """The qkv GEMM with RoPE and the paged-KV write in its epilogue gives q and the cache rows of
+    the separate GEMM + rope_kv_write kernels (the same bf16-rounded product, rotated by the same
+    table) to within one bf16 rounding, and leaves every other cache row untouched."""
+    from everserve_b200.ops import PackedWeight, ref
+
+    g = torch.Generator(device="cuda").manual_seed(T + hq)
+    d, bs, K = 128, 16, 1024
+    x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn((hq + 2 * hkv) * d, K, device="cuda", generator=g) / math.sqrt(K)).bfloat16()
+    pos = torch.randint(0, 4000, (T,), device="cuda", generator=g)
+    cs = ref.cos_sin_table(d, 4096, 5e5).cuda()
+    nb = T // bs + 8
+    slots = torch.randperm(nb * bs, device="cuda", generator=g)[:T]
+    slots[0] = -1  # a padding row: q only
+    c_fused = torch.randn(nb, 2, hkv, bs, d, device="cuda", generator=g).bfloat16()
+    c_plain = c_fused.clone()
+    q_fused = kops.linear_rope_kv(x, PackedWeight(w) if packed else w, pos, cs, slots, c_fused, hq, hkv, bs)
+    q_plain = kops.rope_kv_write(kops.linear(x, w), None, pos, cs, slots, c_plain, hq, hkv, bs)
+    torch.cuda.synchronize()
+    assert kops.check_status() == 0
+
+    def ulps(a, b):  # distance in bf16 steps
+        ia = a.contiguous().view(torch.int16).int()
+        ib = b.contiguous().view(torch.int16).int()
+        return (ia - ib).abs().max().item()
+
+    assert ulps(q_fused, q_plain) <= 1
+    assert ulps(c_fused, c_plain) <= 1
+    # untouched rows are bit-identical (the padding row's slot included)
+    written = torch.zeros(nb * bs, dtype=torch.bool, device="cuda")
+    written[slots[slots >= 0]] = True
+    keep = ~written.view(nb, bs)
+    assert torch.equal(c_fused.permute(0, 3, 1, 2, 4)[keep], c_plain.permute(0, 3, 1, 2, 4)[keep])
