@@ -578,10 +578,10 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
     }
     return (int)launch_decode_tc_maps(da, qm, cm, s);
   }
-  if (head_dim == 128 && block_size == 16) e = attn::launch_stages<128, 16>(3, map, p, batch, s);
-  else if (head_dim == 64 && block_size == 16) e = attn::launch_stages<64, 16>(3, map, p, batch, s);
-  else if (head_dim == 128 && block_size == 32) e = attn::launch_stages<128, 32>(3, map, p, batch, s);
-  else e = attn::launch_stages<64, 32>(3, map, p, batch, s);
+  if (head_dim == 128 && block_size == 16) e = attn::launch_stages<128, 16>(2, map, p, batch, s);
+  else if (head_dim == 64 && block_size == 16) e = attn::launch_stages<64, 16>(2, map, p, batch, s);
+  else if (head_dim == 128 && block_size == 32) e = attn::launch_stages<128, 32>(2, map, p, batch, s);
+  else e = attn::launch_stages<64, 32>(2, map, p, batch, s);
   if (e == cudaSuccess && p.tickets == nullptr) {
     dim3 mgrid(batch, q_heads);
     attn::decode_merge_kernel<<<mgrid, head_dim, 0, s>>>(p.part_o, p.part_ml, ctx_lens, static_cast<__nv_bfloat16*>(out),

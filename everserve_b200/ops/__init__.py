@@ -100,7 +100,9 @@ class KernelOps:
 
     kind = "kernel"
     PART_TOKENS = 256  # positions per decode-attention split (fixed: batch-invariant results)
-    ATTN_STAGES = int(os.environ.get("ES_ATTN_STAGES", "3"))  # K/V ring depth of decode attention
+    # K/V ring depth of decode attention: two stages leave room for three CTAs per SM, which
+    # measured faster in the decode step than a deeper ring with two
+    ATTN_STAGES = int(os.environ.get("ES_ATTN_STAGES", "2"))
 
     def __init__(self, device: torch.device | str):
         self.device = torch.device(device)
@@ -359,12 +361,14 @@ def weight_args(w):
     return (w.carrier, w.packed) if isinstance(w, PackedWeight) else (w, None)
 
 
-L2_PREFETCH = os.environ.get("ES_L2_PREFETCH", "1") != "0"
+# off by default: with the weights' and the history's lines marked evict-first, fetching the next
+# kernel's weights into L2 during the kernel before measured slower in the decode step
+L2_PREFETCH = os.environ.get("ES_L2_PREFETCH", "0") == "1"
 
 
 def prefetch_target(t):
     """The tensor whose bytes a kernel fetches into L2 for the next kernel (None: nothing), from a
-    tensor or a packed weight; ES_L2_PREFETCH=0 turns the prefetches off."""
+    tensor or a packed weight; ES_L2_PREFETCH=1 turns the prefetches on."""
     if t is None or not L2_PREFETCH:
         return None
     return t.packed if isinstance(t, PackedWeight) else t
