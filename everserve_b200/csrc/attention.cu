@@ -42,6 +42,7 @@ struct DecodeParams {
   int* tickets;    // [B, Hkv] zero between launches: splits of the pair done so far (nullable)
   const uint8_t* pf;  // memory the next kernel reads, fetched into L2 meanwhile (nullable)
   int64_t pf_bytes;
+  int cluster;  // the splits of a (sequence, kv head) form one cluster and merge through DSMEM
   __nv_bfloat16* out;  // [B, Hq * D] rows of out_stride
   int64_t out_stride;
   int hq, hkv, max_splits, part_tokens;
@@ -55,7 +56,8 @@ struct DecodeCfg {
   static constexpr int kStageBytes = kWarps * 2 * kTileBytes;
   static constexpr int kRowsPerTok = D / 64;                 // 128-byte TMA rows per position
   static constexpr int kSmem = kStages * kStageBytes + 1024 + 128;
-  static_assert(kWarps * 8 * D * 4 + kWarps * 8 * 2 * 4 <= kStages * kStageBytes, "merge buffer fits the ring");
+  static_assert(kWarps * 8 * D * 4 + kWarps * 8 * 2 * 4 + 8 * D * 4 + 8 * 2 * 4 <= kStages * kStageBytes,
+                "the warp and cluster merge buffers fit the ring");
 };
 
 // byte offset of element (t, d) of a K/V tile written by TMA with 128-byte swizzle
@@ -80,15 +82,17 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   const int ctx = p.ctx_lens[b];
   const int s0 = split * p.part_tokens;
   const int G = p.hq / p.hkv;
-  if (s0 >= ctx) {
+  const bool empty = s0 >= ctx;
+  if (empty && !p.cluster) {
     if (split == 0)  // an empty history: the output is zero
       for (int i = threadIdx.x; i < G * D; i += kThreads)
         p.out[(size_t)b * p.out_stride + (size_t)kvh * G * D + i] = f2bf(0.f);
     return;
   }
-  const int s1 = min(ctx, s0 + p.part_tokens);
+  // (an empty split of a cluster stays for the cluster's barriers and contributes nothing)
+  const int s1 = empty ? s0 : min(ctx, s0 + p.part_tokens);
   const int blk0 = s0 / BS, blk1 = (s1 + BS - 1) / BS;
-  const int nchunks = (blk1 - blk0 + kWarps - 1) / kWarps;
+  const int nchunks = empty ? 0 : (blk1 - blk0 + kWarps - 1) / kWarps;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gid = lane >> 2, tig = lane & 3;
   const int* bt = p.block_tables + (size_t)b * p.bt_stride;
@@ -237,6 +241,8 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     }
   }
   __syncthreads();
+  float* cl_o = red_ml + kWarps * 8 * 2;  // cluster mode: this split's [G][D] output, then [G][2]
+  float* cl_ml = cl_o + G * D;
   for (int i = tid; !failed && i < G * D; i += kThreads) {
     const int g = i / D, e = i % D;
     float M = -INFINITY;
@@ -250,12 +256,45 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
       num += red_o[(w * 8 + g) * D + e] * f;
       den += red_ml[(w * 8 + g) * 2 + 1] * f;
     }
+    if (p.cluster) {
+      cl_o[g * D + e] = num / den;
+      if (e == 0) {
+        cl_ml[g * 2] = M;
+        cl_ml[g * 2 + 1] = den;
+      }
+      continue;
+    }
     const size_t row = ((size_t)b * p.hq + kvh * G + g) * p.max_splits + split;
     p.part_o[row * D + e] = num / den;
     if (e == 0) {
       p.part_ml[row * 2] = M;
       p.part_ml[row * 2 + 1] = den;
     }
+  }
+  if (p.cluster) {
+    // the pair's splits are this cluster (rank = split): each CTA merges a share of the G x D
+    // outputs over the splits' partials in their shared memory, in split order (the merge
+    // kernel's arithmetic), then waits until every CTA has read its partials
+    ptx::cluster_sync();
+    const int ns = min(p.max_splits, (ctx + p.part_tokens - 1) / p.part_tokens);
+    const uint32_t o_local = ptx::smem_u32(cl_o), ml_local = ptx::smem_u32(cl_ml);
+    for (int i = split * kThreads + tid; i < G * D; i += (int)gridDim.z * kThreads) {
+      const int g = i / D, e = i % D;
+      float m = -INFINITY;
+      for (int sp = 0; sp < ns; sp++)
+        m = fmaxf(m, ptx::ld_cluster_f32(ptx::map_cluster(ml_local + g * 8, (uint32_t)sp)));
+      float num = 0.f, den = 0.f;
+      for (int sp = 0; sp < ns; sp++) {
+        const float ms = ptx::ld_cluster_f32(ptx::map_cluster(ml_local + g * 8, (uint32_t)sp));
+        const float ls = ptx::ld_cluster_f32(ptx::map_cluster(ml_local + g * 8 + 4, (uint32_t)sp));
+        const float w = ls * exp2f(ms - m);
+        num += w * ptx::ld_cluster_f32(ptx::map_cluster(o_local + (g * D + e) * 4, (uint32_t)sp));
+        den += w;
+      }
+      p.out[(size_t)b * p.out_stride + (size_t)(kvh * G + g) * D + e] = f2bf(ns > 0 ? num / den : 0.f);
+    }
+    ptx::cluster_sync();
+    return;
   }
   // without tickets the merge kernel merges the splits; with them the last split of the pair
   // merges every split's (o, m, l) in split order
@@ -320,7 +359,8 @@ cudaError_t launch_decode(const CUtensorMap& map, const DecodeParams& p, int B, 
   });
   if (e != cudaSuccess) return e;
   dim3 grid(B, p.hkv, p.max_splits);
-  return launch_ex(decode_kernel<D, BS, S>, grid, dim3(kThreads), C::kSmem, stream, 0, map, p);
+  return launch_ex(decode_kernel<D, BS, S>, grid, dim3(kThreads), C::kSmem, stream, p.cluster ? p.max_splits : 0,
+                   map, p);
 }
 
 template <int D, int BS>
@@ -334,7 +374,7 @@ cudaError_t launch_stages(int stages, const CUtensorMap& map, const DecodeParams
 
 // Kernel choices read once per process: ES_ATTN_TC=1 takes the tcgen05 kernel where it applies;
 // ES_ATTN_MERGE=fused has the mma.sync kernel's last split merge (tickets) instead of the merge
-// kernel. Both entry points (the binding and the allocation-free one) follow the same choices.
+// kernel; ES_ATTN_MERGE=cluster merges through distributed shared memory. Both entry points (the binding and the allocation-free one) follow the same choices.
 bool use_tc() {
   static const bool on = [] {
     const char* v = std::getenv("ES_ATTN_TC");
@@ -348,6 +388,15 @@ bool fused_merge() {
     return v && std::strcmp(v, "fused") == 0;
   }();
   return on;
+}
+// ES_ATTN_MERGE=cluster: the splits of a pair form a thread-block cluster (up to 8) and merge
+// through distributed shared memory; no partials in global memory, no second launch
+bool cluster_merge(int max_splits) {
+  static const bool on = [] {
+    const char* v = std::getenv("ES_ATTN_MERGE");
+    return v && std::strcmp(v, "cluster") == 0;
+  }();
+  return on && max_splits >= 1 && max_splits <= 8;
 }
 
 }  // namespace attn
@@ -373,6 +422,8 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   p.scale_log2 = a.scale * attn::kLog2e;
   p.status = a.status;
   p.tickets = attn::fused_merge() ? a.tickets : nullptr;
+  p.cluster = attn::cluster_merge(a.max_splits) ? 1 : 0;
+  if (p.cluster) p.tickets = nullptr;
   p.pf = static_cast<const uint8_t*>(a.prefetch);
   p.pf_bytes = a.prefetch_bytes;
   p.out = static_cast<__nv_bfloat16*>(a.out);
@@ -389,7 +440,7 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   else if (a.d == 128 && a.block_size == 32) e = attn::launch_stages<128, 32>(a.stages, map, p, a.B, stream);
   else if (a.d == 64 && a.block_size == 32) e = attn::launch_stages<64, 32>(a.stages, map, p, a.B, stream);
   else return cudaErrorInvalidValue;
-  if (e != cudaSuccess || p.tickets != nullptr) return e;
+  if (e != cudaSuccess || p.tickets != nullptr || p.cluster) return e;
   dim3 mgrid(a.B, a.hq);
   return launch_ex(attn::decode_merge_kernel, mgrid, dim3(a.d), 0, stream, 0, (const float*)a.part_o,
                    (const float*)a.part_ml, a.ctx_lens, static_cast<__nv_bfloat16*>(a.out), a.out_stride, a.hq,
@@ -509,6 +560,8 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   // zero when the library loads; each launch leaves them at zero again
   int* tickets = reinterpret_cast<int*>(base + ES_NOALLOC_PART_FLOATS + ES_NOALLOC_ML_FLOATS + 64);
   p.tickets = attn::fused_merge() ? tickets : nullptr;
+  p.cluster = attn::cluster_merge((int)splits) ? 1 : 0;
+  if (p.cluster) p.tickets = nullptr;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride = out_stride;
   // tensor map encoded on the stack (no cache: nothing is allocated, not even on the host heap)
@@ -582,7 +635,7 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   else if (head_dim == 64 && block_size == 16) e = attn::launch_stages<64, 16>(2, map, p, batch, s);
   else if (head_dim == 128 && block_size == 32) e = attn::launch_stages<128, 32>(2, map, p, batch, s);
   else e = attn::launch_stages<64, 32>(2, map, p, batch, s);
-  if (e == cudaSuccess && p.tickets == nullptr) {
+  if (e == cudaSuccess && p.tickets == nullptr && !p.cluster) {
     dim3 mgrid(batch, q_heads);
     attn::decode_merge_kernel<<<mgrid, head_dim, 0, s>>>(p.part_o, p.part_ml, ctx_lens, static_cast<__nv_bfloat16*>(out),
                                                          out_stride, q_heads, (int)splits, kPart, head_dim);

@@ -32,9 +32,10 @@ class EngineConfig:
     # tensor-parallel ranks keep the residual stream of their token slice (norms on the slice,
     # reduce-scatter GEMMs for o/down, all-gather GEMMs for qkv/gate_up/vocabulary); ES_SP=1 sets it
     sequence_parallel: bool = field(default_factory=lambda: os.environ.get("ES_SP", "0") == "1")
-    # mixture models on a peer-memory TP group: route tokens to their experts' owners (all-to-all)
-    # instead of running every local expert on every token; ES_MOE_ROUTED=1 sets it
-    moe_routed: bool = field(default_factory=lambda: os.environ.get("ES_MOE_ROUTED", "0") == "1")
+    # mixture models on the GPU kernels: prefill-size steps route tokens to their experts (within
+    # the GPU, or to the experts' owners over a peer-memory TP group) instead of running every
+    # local expert on every token; ES_MOE_ROUTED=0 turns it off
+    moe_routed: bool = field(default_factory=lambda: os.environ.get("ES_MOE_ROUTED", "1") != "0")
     extra: dict = field(default_factory=dict)
 
     def __post_init__(self):

@@ -478,21 +478,38 @@ class DecoderLM:
         grouped GEMMs over what they received (tiles no token reached are skipped: unchosen experts
         read no weights, and prefill does the routed FLOPs instead of E/k times them), the combine
         brings the weighted outputs back, and an all-gather of the slices replicates the result.
-        Needs the GPU kernels and a peer-memory collective; False (nothing changes) otherwise."""
-        coll = self.tp.collective
-        if (not self.cfg.is_moe or self.tp.size == 1 or self.ops.kind != "kernel" or coll is None
-                or not hasattr(coll, "region") or getattr(coll, "nvls", False)):
+        On one GPU the same kernels route within the GPU (a group of one, buffers in its own
+        memory). Needs the GPU kernels and, across GPUs, a peer-memory collective; False (nothing
+        changes) otherwise. Steps of at least ROUTED_MIN_TOKENS tokens (prefill) take the routed
+        path; smaller ones (decode) keep running every local expert, which reads the same weight
+        bytes and has no dispatch or combine."""
+        if not self.cfg.is_moe or self.ops.kind != "kernel":
             return False
         from ..parallel.moe_a2a import ExpertAllToAll, default_cap
 
+        if self.tp.size == 1:
+            self.a2a = ExpertAllToAll.emulated(self.device, 1, experts=self.cfg.num_experts, top_k=self.cfg.top_k,
+                                               hidden=self.cfg.hidden, cap=default_cap(max_tokens))
+            return True
+        coll = self.tp.collective
+        if coll is None or not hasattr(coll, "region") or getattr(coll, "nvls", False):
+            return False
         per = -(-max_tokens // self.tp.size)
         self.a2a = ExpertAllToAll.over(coll, experts=self.cfg.num_experts, top_k=self.cfg.top_k,
                                        hidden=self.cfg.hidden, cap=default_cap(per))
         return True
 
+    # tokens from which a step routes them to their experts (prefill); ES_MOE_ROUTED_MIN overrides
+    ROUTED_MIN_TOKENS = int(os.environ.get("ES_MOE_ROUTED_MIN", "512"))
+
     def _moe_routed(self, h: torch.Tensor, p: str) -> torch.Tensor:
         ops, c, W = self.ops, self.cfg, self.weights
         T, R = h.shape[0], self.tp.size
+        if R == 1:
+            logits = (h.float() @ W[p + "router"].float().t()).to(h.dtype)
+            ids, weights = ops.moe_topk(logits, c.top_k)
+            return self.a2a(ops, h.contiguous()[None], ids[None], weights[None], lambda e: W[p + f"e{e}.gate_up"],
+                            lambda e: W[p + f"e{e}.down"])[0]
         per = -(-T // R)
         lo = min(T, self.tp.rank * per)
         hi = min(T, lo + per)
@@ -518,7 +535,7 @@ class DecoderLM:
         synchronisation, so the layer is captured in CUDA graphs; fixed orders, so results are
         deterministic.
         """
-        if self.a2a is not None:
+        if self.a2a is not None and h.shape[0] >= self.ROUTED_MIN_TOKENS:
             return self._moe_routed(h, p)
         ops, c, W = self.ops, self.cfg, self.weights
         # the router's product is a few experts wide: a plain matmul, not a weight-streaming GEMM

@@ -194,7 +194,9 @@ def _worker(rank, world, port, results):
                     assert model.enable_routed_experts(128)
                     routed_a2a = model.a2a
                 model.a2a = routed_a2a
+                model.ROUTED_MIN_TOKENS = 1  # route every step size under test
                 routed = model._moe(h, "l0.")
+                model.ROUTED_MIN_TOKENS = 1 << 30
                 torch.cuda.synchronize()
                 layer_errs.append(_close(routed, dense))
             out["layer_err"] = max(layer_errs)
@@ -227,3 +229,32 @@ def test_all_to_all_across_gpus():
     for r in range(world):
         assert results[r]["err"] < 2e-2 and results[r]["status"] == 0, (r, results[r])
         assert results[r].get("layer_err", 0.0) < 3e-2, (r, results[r])
+
+
+def test_routed_experts_on_one_gpu():
+    """On one GPU a prefill-size mixture step routes its tokens within the GPU (a group of one)
+    and agrees with running every expert on every token; a decode-size step keeps the latter."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from everserve_b200.models.config import get_config
+    from everserve_b200.models.llama import DecoderLM
+
+    dev = torch.device("cuda", 0)
+    cfg = get_config("tiny-mixtral")
+    model = DecoderLM(cfg, dev, torch.bfloat16, 0)
+    g = torch.Generator().manual_seed(3)
+    for T in (600, 1037):
+        h = torch.randn(T, cfg.hidden, generator=g).bfloat16().to(dev)
+        model.a2a = None
+        dense = model._moe(h, "l0.")
+        assert model.enable_routed_experts(2048)
+        routed = model._moe(h, "l0.")
+        torch.cuda.synchronize()
+        assert _close(routed, dense) < 3e-2
+        assert model.a2a.status() == 0
+    small = torch.randn(64, cfg.hidden, generator=g).bfloat16().to(dev)
+    a2a, model.a2a = model.a2a, None
+    ref_small = model._moe(small, "l0.")
+    model.a2a = a2a
+    assert torch.equal(model._moe(small, "l0."), ref_small)  # below the threshold: the same path
+
