@@ -14,6 +14,7 @@ Implements the reference's slot-collective protocol (core/everserve/comm/slot.py
 
 from __future__ import annotations
 
+import atexit
 import os
 import threading
 import uuid
@@ -107,8 +108,11 @@ class FusedTPCollective:
                 self.own = self._buf.ptr
                 self._addrs[self.row] = self.own
         self.region.set_pid(self.row, os.getpid())
-        # this member's heartbeat (a native thread): peers' kernels name it dead when it stops
+        # this member's heartbeat (a native thread): peers' kernels name it dead when it stops. It
+        # writes into the slot region's mapping, so it stops before the process unmaps it, also when
+        # the owner never calls close()
         self._beat = int(self.C.heartbeat_start(self.region.beat_address(self.row), BEAT_PERIOD_US))
+        atexit.register(self._stop_beat)
         if not self.nvls:
             name = os.path.basename(self._sock_path(self.row)).encode()
             self.region.publish(self.row, name + bytes(HANDLE_BYTES - len(name)))
@@ -397,10 +401,13 @@ class FusedTPCollective:
         (0: off; the bound and the host's checks still apply)."""
         self.region.set_beat_limit_us([self.row], int(us))
 
-    def close(self) -> None:
+    def _stop_beat(self) -> None:
         if getattr(self, "_beat", 0):
             self.C.heartbeat_stop(self._beat)
             self._beat = 0
+
+    def close(self) -> None:
+        self._stop_beat()
         for a in self.attached:
             a.close()
         self.attached = []

@@ -38,6 +38,7 @@ def main() -> None:
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     ops = KernelOps(dev)
+    coll = None
     C = ops.C
     g = torch.Generator(device=dev).manual_seed(0)
     if a.kernel == "gemm":
@@ -153,6 +154,13 @@ def main() -> None:
             ts.append(s.elapsed_time(e) * 1e3)
         ts.sort()
         print(f"{a.kernel}: median {ts[len(ts) // 2]:.1f} us, min {ts[0]:.1f} us per launch (L2 flushed)")
+    if coll is not None:
+        # the collective's heartbeat thread and peer mappings go before the interpreter does
+        torch.cuda.synchronize()
+        coll.close()
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
