@@ -1,10 +1,11 @@
 // Failure-detecting all-reduce ("fdar"): sum a bf16 vector over the members of a tensor-parallel
 // group through peer memory, in member order, with bounded waits (see comm.cuh for the protocol).
 //
-// Decode-size tensors (up to 512 Ki elements) take the LL kernel: every 8-byte word carries two
-// bf16 and the call number, pushed to every member, so one round trip and no flags. Larger ones take
-// the two-shot kernel (a reduce-scatter to chunk owners, then the owners' sums to every member),
-// up to 1 Mi elements per member per call; the host splits bigger tensors into calls.
+// Decode-size tensors (up to 512 Ki elements) take the one-shot LL kernel: every 8-byte word
+// carries two bf16 and the call number, pushed to every member, so one round trip and no flags.
+// Larger ones take the two-shot kernel on the same LL words (a reduce-scatter to chunk owners,
+// then the owners' sums to every member), up to 512 Ki elements per member per call; the host
+// splits bigger tensors into calls.
 #include <algorithm>
 #include <cstdlib>
 
@@ -19,26 +20,20 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kChunk = kChunkElems;
 
-// Two-shot all-reduce (tensors above the LL path): a persistent grid, CTA b taking chunks b,
-// b + grid, ... in the same order on every member (chunk c's owner: member c % count).
-//   1. the CTA writes this member's part of every one of its chunks into the owner's data row for
-//      this member (at the owner's local index c / count), then one release fence and a flag per
-//      chunk at its owner;
-//   2. for the chunks this member owns: wait for every member's flag, sum the parts in member
-//      order in fp32 (one rounding) into `out` and into every other member's gather area; then one
-//      fence and the chunks' gather flags at every other member;
-//   3. for the chunks others own: wait for the owner's gather flag, copy the sum out.
-// A CTA's chunks travel together and it fences twice per call, not per chunk, so the bytes of all
-// of them are on the links at once. Each member sends about twice (count - 1) / count of the
-// vector and receives as much. Every wait is bounded.
-ES_DEVICE void fence_release_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
-ES_DEVICE void copy_part(const __nv_bfloat16* __restrict__ src, char* dst, int len) {
-  const int nvec = len / 8;  // whole 16-byte vectors; the tail element by element
-  for (int i = threadIdx.x; i < nvec; i += kThreads)
-    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
-  for (int i = nvec * 8 + threadIdx.x; i < len; i += kThreads) reinterpret_cast<__nv_bfloat16*>(dst)[i] = src[i];
-}
+// Two-shot all-reduce (tensors above the one-shot LL path), on LL words: every 8-byte word
+// carries two bf16 and the call number, so a word is its own arrival flag and the kernel needs no
+// fence and no flag round trip (system-scope fences measured several microseconds each here,
+// which made a fenced two-shot latency-bound). A persistent grid, CTA b taking chunks b,
+// b + grid, ... in the same order on every member; chunk c's owner is member c % count:
+//   1. the CTA writes this member's part of each of its chunks, as LL words, into the owner's
+//      data row for this member (at the owner's local index c / count);
+//   2. for the chunks this member owns: each thread polls its words from every member in member
+//      order, sums them in fp32 (one rounding), writes the sum to `out` and, as LL words, into
+//      every other member's gather area;
+//   3. for the chunks others own: each thread polls its words in this member's gather area.
+// Each member sends about twice (count - 1) / count of the vector (in words of twice its bytes)
+// and receives as much. Every wait is bounded (abort word, the sender's heartbeat, hard limit).
+constexpr int kWordsPerChunk = kChunk / 2;
 
 __global__ void __launch_bounds__(kThreads) fdar_kernel(const __nv_bfloat16* __restrict__ inp,
                                                         __nv_bfloat16* __restrict__ out, int n, View v) {
@@ -60,82 +55,68 @@ __global__ void __launch_bounds__(kThreads) fdar_kernel(const __nv_bfloat16* __r
   const int count = s_count;
   const uint64_t my_base = v.peers[v.row];
   const int nchunks = (n + kChunk - 1) / kChunk;
-  // an owner's chunks must fit one data row of each sender: at most kDataBytes / chunk per member
-  if (nchunks > (int)(kDataBytes / (kChunk * 2)) * count) {
+  const int nw = (n + 1) / 2;  // words of the whole vector
+  // an owner's chunks must fit one data row of each sender (in words)
+  if (nchunks > (int)(kDataBytes / 8 / kWordsPerChunk) * count) {
     if (threadIdx.x == 0) finish_call(v, seq, kBadShape);
     return;
   }
+  auto word_of = [&](const __nv_bfloat16* src, int w) -> uint64_t {
+    const uint32_t lo = __bfloat16_as_ushort(src[2 * w]);
+    const uint32_t hi = 2 * w + 1 < n ? __bfloat16_as_ushort(src[2 * w + 1]) : 0u;
+    return ((uint64_t)seq << 32) | (hi << 16) | lo;
+  };
+  int fail = kOk;
   if (count > 0) {
     // 1. this member's parts, to their owners
     for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
       const int owner = s_order[c % count];
-      const int e0 = c * kChunk, e1 = min(n, e0 + kChunk);
-      copy_part(inp + e0, data_ptr(v.peers[owner], parity, v.row) + (size_t)(c / count) * kChunk * 2, e1 - e0);
+      uint64_t* dst = reinterpret_cast<uint64_t*>(data_ptr(v.peers[owner], parity, v.row)) +
+                      (size_t)(c / count) * kWordsPerChunk;
+      const int w0 = c * kWordsPerChunk, w1 = min(nw, w0 + kWordsPerChunk);
+      for (int w = w0 + threadIdx.x; w < w1; w += kThreads) st_u64_relaxed(dst + (w - w0), word_of(inp, w));
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      fence_release_sys();
-      for (int c = blockIdx.x; c < nchunks; c += gridDim.x)
-        st_release_sys(flag_ptr(v.peers[s_order[c % count]], parity, v.row, c / count), seq);
-    }
-    // 2. the chunks this member owns: summed in member order, to `out` and every member
-    bool owns = false;
-    for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    uint64_t t0 = 0;
+    bool named = false;
+    uint32_t spins = 0;
+    // 2. the chunks this member owns: every member's words, summed in member order
+    for (int c = blockIdx.x; fail == kOk && c < nchunks; c += gridDim.x) {
       if (s_order[c % count] != v.row) continue;
-      owns = true;
-      const size_t local = (size_t)(c / count) * kChunk * 2;
-      const int e0 = c * kChunk, e1 = min(n, e0 + kChunk);
-      const int nvec = (e1 - e0) / 8;
-      if (threadIdx.x == 0) s_fail = wait_members(v, my_base, parity, c / count, seq, s_order, count);
-      __syncthreads();
-      if (s_fail != kOk) break;
-      for (int i = threadIdx.x; i < nvec; i += kThreads) {
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int k = 0; k < count; k++) {
-          const uint4 w = reinterpret_cast<const uint4*>(data_ptr(my_base, parity, s_order[k]) + local)[i];
-          float f[8];
-          unpack8(w, f);
-#pragma unroll
-          for (int j = 0; j < 8; j++) acc[j] += f[j];
+      const size_t local = (size_t)(c / count) * kWordsPerChunk;
+      const int w0 = c * kWordsPerChunk, w1 = min(nw, w0 + kWordsPerChunk);
+      for (int w = w0 + threadIdx.x; fail == kOk && w < w1; w += kThreads) {
+        float a0 = 0.f, a1 = 0.f;
+        for (int k = 0; k < count && fail == kOk; k++) {
+          const uint64_t* src = reinterpret_cast<const uint64_t*>(data_ptr(my_base, parity, s_order[k])) + local;
+          const uint32_t bits = ll_wait(v, src + (w - w0), seq, s_order[k], t0, named, spins, fail);
+          a0 += __bfloat162float(__ushort_as_bfloat16((unsigned short)(bits & 0xFFFFu)));
+          a1 += __bfloat162float(__ushort_as_bfloat16((unsigned short)(bits >> 16)));
         }
-        const uint4 r = pack8(acc);
-        reinterpret_cast<uint4*>(out + e0)[i] = r;
+        if (fail != kOk) break;
+        const __nv_bfloat16 r0 = f2bf(a0), r1 = f2bf(a1);
+        out[2 * w] = r0;
+        if (2 * w + 1 < n) out[2 * w + 1] = r1;
+        const uint64_t word = ((uint64_t)seq << 32) | ((uint32_t)__bfloat16_as_ushort(r1) << 16) |
+                              (uint32_t)__bfloat16_as_ushort(r0);
         for (int k = 0; k < count; k++)
-          if (s_order[k] != v.row) reinterpret_cast<uint4*>(ag_ptr(v.peers[s_order[k]], parity) + (size_t)e0 * 2)[i] = r;
-      }
-      for (int i = e0 + nvec * 8 + threadIdx.x; i < e1; i += kThreads) {
-        float acc = 0.f;
-        for (int k = 0; k < count; k++)
-          acc += bf2f(reinterpret_cast<const __nv_bfloat16*>(data_ptr(my_base, parity, s_order[k]) + local)[i - e0]);
-        const __nv_bfloat16 r = f2bf(acc);
-        out[i] = r;
-        for (int k = 0; k < count; k++)
-          if (s_order[k] != v.row) reinterpret_cast<__nv_bfloat16*>(ag_ptr(v.peers[s_order[k]], parity))[i] = r;
-      }
-      __syncthreads();  // s_fail is rewritten by the next chunk's wait
-    }
-    __syncthreads();
-    if (owns && s_fail == kOk && threadIdx.x == 0) {
-      fence_release_sys();
-      for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
-        if (s_order[c % count] != v.row) continue;
-        for (int k = 0; k < count; k++)
-          if (s_order[k] != v.row) st_release_sys(ag_flag_ptr(v.peers[s_order[k]], parity, c), seq);
+          if (s_order[k] != v.row) st_u64_relaxed(reinterpret_cast<uint64_t*>(ag_ptr(v.peers[s_order[k]], parity)) + w, word);
       }
     }
-    // 3. the chunks others own: the owner's sum, from this member's gather area
-    for (int c = blockIdx.x; s_fail == kOk && c < nchunks; c += gridDim.x) {
+    // 3. the chunks others own: the owner's sums, from this member's gather area
+    const uint64_t* gather = reinterpret_cast<const uint64_t*>(ag_ptr(my_base, parity));
+    for (int c = blockIdx.x; fail == kOk && c < nchunks; c += gridDim.x) {
       const int owner = s_order[c % count];
       if (owner == v.row) continue;
-      const int e0 = c * kChunk, e1 = min(n, e0 + kChunk);
-      if (threadIdx.x == 0) s_fail = wait_flag(v, ag_flag_ptr(my_base, parity, c), seq, owner);
-      __syncthreads();
-      if (s_fail != kOk) break;
-      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(ag_ptr(my_base, parity) + (size_t)e0 * 2);
-      copy_part(src, reinterpret_cast<char*>(out + e0), e1 - e0);
-      __syncthreads();
+      const int w0 = c * kWordsPerChunk, w1 = min(nw, w0 + kWordsPerChunk);
+      for (int w = w0 + threadIdx.x; fail == kOk && w < w1; w += kThreads) {
+        const uint32_t bits = ll_wait(v, gather + w, seq, owner, t0, named, spins, fail);
+        if (fail != kOk) break;
+        out[2 * w] = __ushort_as_bfloat16((unsigned short)(bits & 0xFFFFu));
+        if (2 * w + 1 < n) out[2 * w + 1] = __ushort_as_bfloat16((unsigned short)(bits >> 16));
+      }
     }
   }
+  if (fail != kOk) atomicCAS(&s_fail, kOk, fail);
   __syncthreads();
   if (threadIdx.x == 0) finish_call(v, seq, s_fail);
 }
@@ -203,7 +184,8 @@ int64_t comm_ll_max_elems() { return (int64_t)(comm::kLLSmallBytes / 8 * 2); }
 int64_t comm_buffer_bytes() { return (int64_t)comm::kBufferBytes; }
 // elements one all-reduce call takes: each member owns at most a data row's worth of chunks
 int64_t comm_max_elems(int64_t members) {
-  return std::max<int64_t>(1, std::min<int64_t>(members, comm::kMaxRows)) * (int64_t)(comm::kDataBytes / 2);
+  // an owner's chunks fill at most one data row of LL words (two elements per 8-byte word) per sender
+  return std::max<int64_t>(1, std::min<int64_t>(members, comm::kMaxRows)) * (int64_t)(comm::kDataBytes / 8 * 2);
 }
 
 cudaError_t launch_fdar(const void* inp, void* out, int64_t n, const CommArgs& c, cudaStream_t stream) {
@@ -226,7 +208,7 @@ cudaError_t launch_fdar(const void* inp, void* out, int64_t n, const CommArgs& c
   }
   // the two-shot path: the member count is a device table (it changes with membership), so the
   // call's size is checked against the largest group; the caller keeps calls within its own count
-  if (n > (int64_t)comm::kMaxChunks * comm::kChunk) return cudaErrorInvalidValue;
+  if (n > comm_max_elems(comm::kMaxRows)) return cudaErrorInvalidValue;
   static int sms[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;

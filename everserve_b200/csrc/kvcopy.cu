@@ -9,6 +9,8 @@
 // Each cache is addressed through five element strides (block, offset, head, kv, element), so
 // any of the supported cache layouts works. A negative slot is a padding row: gather writes
 // zeros for it, scatter skips it.
+#include <algorithm>
+
 #include "api.h"
 #include "common.cuh"
 
@@ -25,11 +27,8 @@ struct KvCopyParams {
   int elem;                               // bytes per element
 };
 
-// grid (n, L); threads cover (head, kv, 16-byte vector). d * elem must be a multiple of 16.
 template <bool kGather>
-__global__ void kv_copy_kernel(KvCopyParams p) {
-  const int64_t t = blockIdx.x;
-  const int l = blockIdx.y;
+__device__ __forceinline__ void copy_row(const KvCopyParams& p, int64_t t, int l) {
   const int64_t slot = p.slots[t];
   const int vec_per_row = (int)(p.d * p.elem / 16);
   const int per_head = 2 * vec_per_row;
@@ -55,6 +54,17 @@ __global__ void kv_copy_kernel(KvCopyParams p) {
   }
 }
 
+// CTAs walk the (row, layer) pairs; threads cover (head, kv, 16-byte vector). d * elem must be a
+// multiple of 16.
+template <bool kGather>
+__global__ void kv_copy_kernel(KvCopyParams p, int64_t L) {
+  for (int64_t item = blockIdx.x; item < p.n * L; item += gridDim.x) {
+    const int64_t t = item % p.n;
+    const int l = (int)(item / p.n);
+    copy_row<kGather>(p, t, l);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_kv_copy(const KvCopyArgs& a, bool gather, cudaStream_t stream) {
@@ -77,11 +87,16 @@ cudaError_t launch_kv_copy(const KvCopyArgs& a, bool gather, cudaStream_t stream
   p.s_head = a.strides[2];
   p.s_kv = a.strides[3];
   p.elem = a.elem;
-  dim3 grid((unsigned)a.n, (unsigned)a.L);
+  // the per-step gather writes a few MB into host-mapped staging over PCIe, on a side stream next
+  // to the step's kernels: a few CTAs keep up with the link and leave the SMs to the step; the
+  // scatter of a restore takes the whole device
+  const int64_t items = a.n * a.L;
+  const int64_t cap = gather ? std::max<int64_t>(32, items / 64) : ((int64_t)1 << 20);
+  const unsigned grid = (unsigned)std::min<int64_t>(items, cap);
   if (gather)
-    kv_copy_kernel<true><<<grid, 128, 0, stream>>>(p);
+    kv_copy_kernel<true><<<grid, 128, 0, stream>>>(p, a.L);
   else
-    kv_copy_kernel<false><<<grid, 128, 0, stream>>>(p);
+    kv_copy_kernel<false><<<grid, 128, 0, stream>>>(p, a.L);
   return cudaGetLastError();
 }
 

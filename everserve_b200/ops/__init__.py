@@ -99,7 +99,9 @@ class KernelOps:
     """The sm_100a kernels on one CUDA device, with their scratch memory."""
 
     kind = "kernel"
-    PART_TOKENS = 256  # positions per decode-attention split (fixed: batch-invariant results)
+    # positions per decode-attention split (fixed per process: batch-invariant results); a multiple
+    # of 64, ES_ATTN_PART overrides
+    PART_TOKENS = int(os.environ.get("ES_ATTN_PART", "256"))
     # K/V ring depth of decode attention: two stages leave room for three CTAs per SM, which
     # measured faster in the decode step than a deeper ring with two
     ATTN_STAGES = int(os.environ.get("ES_ATTN_STAGES", "2"))
