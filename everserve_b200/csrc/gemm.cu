@@ -77,6 +77,7 @@ struct Params {
   const uint8_t* pf;
   int64_t pf_bytes;
   RopeOut rope;  // the qkv projection's RoPE + paged-KV write epilogue when rope.q_out is set
+  int ahead;     // weight k-blocks fetched into L2 beyond the ring (decode GEMMs), 0: none
 };
 
 // The fused all-gather's wait: every member's pushers have raised their flags for this call in this
@@ -283,10 +284,19 @@ __global__ void __launch_bounds__(kThreads, CPS)
         ptx::tma_load_2d(dst, &tmap_w, kb * BK, n0, &full[stage]);
       }
     };
+    // beyond the ring, the next `ahead` weight k-blocks are fetched into L2, so more of the
+    // stream is in flight from DRAM than the ring's shared memory holds
+    auto ahead_w = [&](int i) {
+      if (!once || i >= nkb) return;
+      const int kb = kblk(i);
+      if (p.w_packed) ptx::l2_prefetch(p.w_packed + ((size_t)blockIdx.x * p.kb + kb) * C::kABytes, C::kABytes);
+      else ptx::tma_prefetch_2d(&tmap_w, kb * BK, n0);
+    };
     for (int i = 0; i < pre; i++) {
       ptx::mbar_arrive_expect_tx(&full[i], C::kStageBytes);
       load_w(i, kblk(i));
     }
+    for (int i = pre; i < pre + p.ahead; i++) ahead_w(i);
     ptx::l2_prefetch_share(p.pf, p.pf_bytes, (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)),
                            (int)(gridDim.x * gridDim.y * gridDim.z));
     pdl_wait();
@@ -312,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
       ptx::mbar_arrive_expect_tx(&full[s], C::kStageBytes);
       const int kx = kblk(i) * BK;
       load_w(s, kblk(i));
+      ahead_w(i + p.ahead);
       ptx::tma_load_2d(b_tiles + s * C::kBBytes, xmap, kx, m0, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
@@ -748,6 +759,16 @@ static bool stream_k_enabled() {
   return on;
 }
 
+// Weight k-blocks a decode GEMM fetches into L2 ahead of its ring (ES_GEMM_L2AHEAD, default 4).
+static int l2_ahead() {
+  static const int v = [] {
+    const char* e = std::getenv("ES_GEMM_L2AHEAD");
+    const int x = e ? std::atoi(e) : 4;
+    return x < 0 ? 0 : (x > 16 ? 16 : x);
+  }();
+  return v;
+}
+
 // The weight's operand: a tensor map of the row-major weight, or (pre-packed weight) nothing, the
 // kernel reading the packed blocks by bulk copies. Checks the alignment either needs.
 static cudaError_t weight_map(const GemmArgs& a, CUtensorMap* mw) {
@@ -788,6 +809,7 @@ cudaError_t launch_gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.w_packed = static_cast<const uint8_t*>(a.w_packed);
   p.pf = static_cast<const uint8_t*>(a.prefetch);
   p.pf_bytes = a.prefetch_bytes;
+  p.ahead = l2_ahead();
   if (a.rope != nullptr) {
     const RopeOut& R = *a.rope;
     if (a.N != (int64_t)(R.hq + 2 * R.hkv) * 128 || a.silu || a.residual != nullptr || a.scale != nullptr ||
@@ -847,6 +869,7 @@ cudaError_t launch_gemm_allreduce(const GemmArgs& a, const CommArgs& c, cudaStre
   p.w_packed = static_cast<const uint8_t*>(a.w_packed);
   p.pf = static_cast<const uint8_t*>(a.prefetch);
   p.pf_bytes = a.prefetch_bytes;
+  p.ahead = l2_ahead();
   p.pre = static_cast<const __nv_bfloat16*>(a.pre);
   p.ldp = (int)a.ldp;
   p.two_shot = c.mc ? 0 : a.two_shot;  // the multicast variant pushes once already
@@ -923,6 +946,7 @@ cudaError_t launch_gemm_allgather(const GemmArgs& a, const CommArgs& c, int64_t 
   p.w_packed = static_cast<const uint8_t*>(a.w_packed);
   p.pf = static_cast<const uint8_t*>(a.prefetch);
   p.pf_bytes = a.prefetch_bytes;
+  p.ahead = l2_ahead();
   int cps = 1;
   gemm_plan(BN, a.N, a.K, a.num_sms, &p.splits, &cps);
   // every CTA waits for the pushers of every member: the whole grid must be resident at once

@@ -90,6 +90,15 @@ ES_DEVICE void l2_prefetch_share(const uint8_t* base, int64_t bytes, int i, int 
     l2_prefetch(base + lo + off, (uint32_t)(len - off < kPiece ? len - off : kPiece));
 }
 
+// Fetch one tensor-map tile into L2 (no shared memory, no barrier): the load of it that follows
+// hits L2. x is the innermost coordinate.
+ES_DEVICE void tma_prefetch_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // One-dimensional bulk copy global -> shared with an L2 cache policy.
 ES_DEVICE void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
   asm volatile(
