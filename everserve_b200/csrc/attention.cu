@@ -300,10 +300,10 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   // merges every split's (o, m, l) in split order
   if (p.tickets == nullptr) return;
   __shared__ int s_last;
-  __threadfence();
-  __syncthreads();
+  __syncthreads();  // every thread's partials are written before the one fence and the ticket
   const int ns = min(p.max_splits, (ctx + p.part_tokens - 1) / p.part_tokens);
   if (tid == 0) {
+    __threadfence();
     int* tk = p.tickets + (size_t)b * p.hkv + kvh;
     s_last = atomicAdd(tk, 1) == ns - 1;
     if (s_last) *tk = 0;  // every split of this launch has counted: the next launch starts at zero
@@ -314,13 +314,35 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   for (int i = tid; i < G * D; i += kThreads) {
     const int g = i / D, e = i % D;
     const size_t row0 = ((size_t)b * p.hq + kvh * G + g) * p.max_splits;
+    const float* ml = p.part_ml + row0 * 2;
+    const float* po = p.part_o + row0 * D + e;
+    // the splits' values in batches of eight independent loads, combined in split order
     float m = -INFINITY;
-    for (int sp = 0; sp < ns; sp++) m = fmaxf(m, __ldcg(p.part_ml + (row0 + sp) * 2));
+    for (int b0 = 0; b0 < ns; b0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = b0 + u < ns ? __ldcg(ml + (b0 + u) * 2) : -INFINITY;
+#pragma unroll
+      for (int u = 0; u < 8; u++) m = fmaxf(m, v[u]);
+    }
     float num = 0.f, den = 0.f;
-    for (int sp = 0; sp < ns; sp++) {
-      const float w = __ldcg(p.part_ml + (row0 + sp) * 2 + 1) * exp2f(__ldcg(p.part_ml + (row0 + sp) * 2) - m);
-      num += w * __ldcg(p.part_o + (row0 + sp) * D + e);
-      den += w;
+    for (int b0 = 0; b0 < ns; b0 += 8) {
+      float mm[8], ll[8], oo[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const bool in = b0 + u < ns;
+        mm[u] = in ? __ldcg(ml + (b0 + u) * 2) : 0.f;
+        ll[u] = in ? __ldcg(ml + (b0 + u) * 2 + 1) : 0.f;
+        oo[u] = in ? __ldcg(po + (size_t)(b0 + u) * D) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        if (b0 + u < ns) {
+          const float w = ll[u] * exp2f(mm[u] - m);
+          num += w * oo[u];
+          den += w;
+        }
+      }
     }
     p.out[(size_t)b * p.out_stride + (size_t)(kvh * G + g) * D + e] = f2bf(num / den);
   }
@@ -517,7 +539,7 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   using namespace es;
   g_noalloc_err = "";
   if (batch == 0) return (int)cudaSuccess;
-  constexpr int kPart = 256;  // positions per split, the regular entry point's default
+  constexpr int kPart = 256;  // positions per split (the regular entry point takes its split length as given)
   if (batch < 0 || kv_heads <= 0 || q_heads % kv_heads != 0 || q_heads / kv_heads > 8 || max_model_len <= 0) {
     g_noalloc_err = "bad shape: q_heads must be 1..8 times kv_heads and max_model_len positive";
     return (int)cudaErrorInvalidValue;

@@ -29,8 +29,8 @@
  * Layouts are those of the regular binding: q [batch, q_heads, head_dim] bf16 (rows of q_stride
  * elements), cache [num_blocks, 2, kv_heads, block_size, head_dim] bf16 contiguous, block_tables
  * [batch, *] int32 (rows of bt_stride), ctx_lens [batch] int32, out [batch, q_heads * head_dim]
- * bf16 (rows of out_stride). Positions are split into runs of 256 (the regular default), so the
- * result matches the regular entry point's bit for bit when that one uses the same split length.
+ * bf16 (rows of out_stride). Positions are split into runs of 256, so the result matches the
+ * regular entry point's bit for bit when that one is given the same split length.
  *
  * Limits of the inputs: batch * kv_heads at most ES_NOALLOC_TICKETS; every ctx_lens[b] must be at
  * most max_model_len (the scratch and the grid

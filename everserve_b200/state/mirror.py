@@ -124,6 +124,7 @@ class _Job:
     slots: list[int]
     event: object = None
     times: dict = field(default_factory=dict)
+    keep: object = None
 
 
 class MirrorCommittedKV:
@@ -211,14 +212,18 @@ class MirrorCommittedKV:
             if self._C is not None:
                 ev = torch.cuda.Event()
                 ev.record(torch.cuda.current_stream(self.device))
+                # the slots go up from pinned memory without blocking the host: a pageable copy
+                # would wait for the side stream, i.e. for the step, before the next step launches
+                host_sl = torch.tensor(slot_list, dtype=torch.int64).pin_memory()
                 with torch.cuda.stream(self._side):
                     self._side.wait_event(ev)
-                    sl = torch.tensor(slot_list, dtype=torch.int64, device=self.device)
+                    sl = host_sl.to(self.device, non_blocking=True)
                     self._C.kv_gather(self._layer_ptrs, sl, self._heads_dev, st.dev_ptr, st.capacity, self.kv.head_dim,
                                       self.kv.block_size, self.kv.strides(), st.tensor.element_size())
                     done = torch.cuda.Event()
                     done.record(self._side)
                 job.event = done
+                job.keep = (host_sl, sl)  # alive until the gather has run (the sender waits on `done`)
                 self._last_gather = done
             else:
                 sl = torch.tensor(slot_list, dtype=torch.int64)
