@@ -182,6 +182,16 @@ struct DecodeArgs {
   int64_t prefetch_bytes = 0;
 };
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t s);
+// the persistent variant (decode_persist.cu; opt-in: ES_ATTN_PERSIST=1, or set_decode_persist, which
+// returns the previous setting): one CTA per SM over an equal share of the (sequence, kv head,
+// split) items, head dim 64 or 128, G <= 8, block size a multiple of 16, q rows 16-byte aligned;
+// tickets required
+int set_decode_persist(int on);
+bool decode_persist_supported(const DecodeArgs& a);
+cudaError_t launch_decode_persist(const DecodeArgs& a, cudaStream_t s);
+// the same with the cache's map given: [num_blocks * 2 * Hkv * BS * D / 64, 64] with a box of
+// (16 * D / 64 rows, 64 columns), 128-byte swizzled
+cudaError_t launch_decode_persist_map(const DecodeArgs& a, const CUtensorMap& cache_map, cudaStream_t s);
 // the tcgen05 persistent variant (decode_tc.cu): head dim 128, G <= 16, splits of 256 positions
 bool decode_tc_supported(const DecodeArgs& a);
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s);

@@ -395,8 +395,10 @@ cudaError_t launch_stages(int stages, const CUtensorMap& map, const DecodeParams
 }
 
 // Kernel choices read once per process: ES_ATTN_TC=1 takes the tcgen05 kernel where it applies;
-// ES_ATTN_MERGE=fused has the mma.sync kernel's last split merge (tickets) instead of the merge
-// kernel; ES_ATTN_MERGE=cluster merges through distributed shared memory. Both entry points (the binding and the allocation-free one) follow the same choices.
+// otherwise the persistent kernel (decode_persist.cu) where it applies, unless ES_ATTN_PERSIST=0;
+// otherwise this file's kernel, whose splits the merge kernel merges, or with ES_ATTN_MERGE=fused
+// the last split (tickets), or with ES_ATTN_MERGE=cluster the cluster through distributed shared
+// memory. Both entry points (the binding and the allocation-free one) follow the same choices.
 bool use_tc() {
   static const bool on = [] {
     const char* v = std::getenv("ES_ATTN_TC");
@@ -426,6 +428,8 @@ bool cluster_merge(int max_splits) {
 cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (a.B == 0) return cudaSuccess;
   if (attn::use_tc() && decode_tc_supported(a)) return launch_decode_tc(a, stream);
+  if (!attn::fused_merge() && !attn::cluster_merge(a.max_splits) && decode_persist_supported(a))
+    return launch_decode_persist(a, stream);
   if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.hq / a.hkv > 8 || a.part_tokens % 64 != 0 || a.max_splits <= 0)
     return cudaErrorInvalidValue;
   if (a.s_kv != (int64_t)a.hkv * a.block_size * a.d || a.s_block != 2 * a.s_kv) return cudaErrorInvalidValue;
@@ -629,6 +633,8 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   da.max_splits = (int)splits;
   da.part_tokens = kPart;
   da.num_blocks = num_blocks;
+  da.s_kv = (int64_t)kv_heads * block_size * head_dim;
+  da.s_block = 2 * da.s_kv;
   da.scale = scale;
   if (attn::use_tc() && decode_tc_supported(da)) {
     CUtensorMap qm;
@@ -652,6 +658,19 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
       return (int)cudaErrorInvalidValue;
     }
     return (int)launch_decode_tc_maps(da, qm, cm, s);
+  }
+  if (!attn::fused_merge() && !p.cluster && decode_persist_supported(da)) {
+    // the persistent kernel, as the regular entry point takes it; its map has 16 positions a box
+    CUtensorMap pm;
+    std::memset(&pm, 0, sizeof(pm));
+    const cuuint32_t pbox[2] = {64, (cuuint32_t)(16 * (head_dim / 64))};
+    if (enc(&pm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(cache), dims, strides, pbox, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      g_noalloc_err = "the cache cannot be described by a TMA map (alignment or size)";
+      return (int)cudaErrorInvalidValue;
+    }
+    return (int)launch_decode_persist_map(da, pm, s);
   }
   if (head_dim == 128 && block_size == 16) e = attn::launch_stages<128, 16>(2, map, p, batch, s);
   else if (head_dim == 64 && block_size == 16) e = attn::launch_stages<64, 16>(2, map, p, batch, s);

@@ -839,6 +839,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pick_splits", &es::gemm_pick_splits);
   m.def("gemm_ws_floats", &es::gemm_ws_floats);
   m.def("gemm_sync_words", &es::gemm_sync_words);
+  m.def("set_decode_persist", [](int64_t on) { return (int64_t)es::set_decode_persist((int)on); },
+        "decode attention on the persistent kernel (1) or the split kernel (0); returns the previous setting",
+        pybind11::arg("on"));
   m.def("paged_decode", &paged_decode, "paged decode attention (split-KV, merged)", pybind11::arg("q"),
         pybind11::arg("cache"), pybind11::arg("block_tables"), pybind11::arg("ctx_lens"), pybind11::arg("out"),
         pybind11::arg("part_o"), pybind11::arg("part_ml"), pybind11::arg("tickets"), pybind11::arg("status"),

@@ -44,6 +44,19 @@ ES_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Whether phase `parity` of `bar` has completed, without waiting (mbarrier.test_wait).
+ES_DEVICE bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` for at most `bound_ns` nanoseconds of the global timer.
 ES_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t bound_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;

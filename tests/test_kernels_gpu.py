@@ -156,7 +156,7 @@ def test_gemm_batch_invariant(kops):
 
 @pytest.mark.parametrize("hq,hkv,d,bs", [(32, 8, 128, 16), (4, 1, 128, 16), (14, 2, 64, 16), (64, 8, 128, 32),
                                          (8, 8, 64, 32)])
-def test_paged_decode(kops, hq, hkv, d, bs):
+def test_paged_decode(kops, decode_kernel, hq, hkv, d, bs):
     g = torch.Generator(device="cuda").manual_seed(5)
     lens = [1, 15, 16, 17, 64, 255, 256, 257, 700, 1029]
     B = len(lens)
@@ -177,6 +177,60 @@ def test_paged_decode(kops, hq, hkv, d, bs):
     one = kops.decode_attention(q[7:8].contiguous(), cache, perm[7:8].contiguous(), ctx[7:8].contiguous(), scale,
                                 max_len)
     assert torch.equal(one, out[7:8])
+
+
+@pytest.fixture(params=[0, 1], ids=["split", "persistent"])
+def decode_kernel(request, kops):
+    """Each decode-attention kernel in turn (the persistent one by its run-time switch)."""
+    prev = kops.C.set_decode_persist(request.param)
+    yield request.param
+    kops.C.set_decode_persist(prev)
+
+
+@pytest.mark.parametrize("hq,hkv,d,bs", [(32, 8, 128, 16), (64, 8, 64, 32), (8, 1, 128, 16)])
+def test_paged_decode_ranges(kops, decode_kernel, hq, hkv, d, bs):
+    """Many more (sequence, kv head, split) items than SMs, so the persistent kernel's ranges cut
+    pairs (merged by the last range, one ticket per pair) as well as hold whole ones (merged in
+    place): every output matches the fp32 oracle, sub-batches give the same bits, and a second call
+    (tickets left at zero by the first) gives the same bits again. One history spans several
+    ranges; empty histories give zero. The split kernel passes the same checks."""
+    g = torch.Generator(device="cpu").manual_seed(11)
+    B = 96
+    lens = torch.randint(1, 3000, (B,), generator=g)
+    lens[3] = 0
+    lens[40] = 0
+    lens[50] = 24000
+    lens[51] = 1
+    max_len = 24064
+    mb = (max_len + bs - 1) // bs
+    need = [int((n + bs - 1) // bs) for n in lens.tolist()]
+    nb = sum(need) + 8
+    cache = torch.randn(nb, 2, hkv, bs, d, generator=g).bfloat16().cuda()
+    perm = torch.randperm(nb, generator=g)
+    bt = torch.zeros(B, mb, dtype=torch.int32)
+    used = 0
+    for b, k in enumerate(need):
+        bt[b, :k] = perm[used:used + k].int()
+        used += k
+    bt = bt.cuda()
+    ctx = lens.int().cuda()
+    q = torch.randn(B, hq, d, generator=g).bfloat16().cuda()
+    scale = 1 / math.sqrt(d)
+    out = kops.decode_attention(q, cache, bt, ctx, scale, max_len)
+    assert kops.check_status() == 0
+    live = [b for b in range(B) if lens[b] > 0]
+    idx = torch.tensor(live, device="cuda")
+    expect = ref.paged_attention(q[idx].float(), cache.float(), bt[idx], ctx[idx], torch.arange(len(live), device="cuda"),
+                                 ctx[idx].long() - 1, scale)
+    close(out[idx], expect, rtol=2e-2, atol=2e-2)
+    assert torch.count_nonzero(out[3]) == 0 and torch.count_nonzero(out[40]) == 0
+    again = kops.decode_attention(q, cache, bt, ctx, scale, max_len)
+    assert torch.equal(again, out)
+    for lo, hi in ((50, 51), (0, 7), (45, 60), (90, 96)):
+        part = kops.decode_attention(q[lo:hi].contiguous(), cache, bt[lo:hi].contiguous(), ctx[lo:hi].contiguous(),
+                                     scale, max_len)
+        assert torch.equal(part, out[lo:hi]), f"rows {lo}:{hi} depend on the batch"
+    assert kops.check_status() == 0
 
 
 def test_kv_gather_scatter(kops):

@@ -68,7 +68,12 @@ def _call(lib, q, cache, bt, lens, max_len, out):
 def test_noalloc_matches_regular_entry_point(lib):
     assert lib.es_noalloc_setup() == 0
     kops = KernelOps("cuda:0")
-    for seed in (11, 12):  # two calls in a row; the second reuses the scratch the first left behind
+    # both decode kernels (the persistent one by its run-time switch, which both entry points
+    # follow); two calls each, the second reusing the scratch the first left behind
+    cases = [(persist, seed) for persist in (0, 1) for seed in (11, 12)]
+    prev = kops.C.set_decode_persist(0)
+    for persist, seed in cases:
+        kops.C.set_decode_persist(persist)
         q, cache, bt, lens, max_len = _case(seed)
         out = torch.empty(q.shape[0], q.shape[1] * q.shape[2], device="cuda", dtype=torch.bfloat16)
         rc = _call(lib, q, cache, bt, lens, max_len, out)
@@ -81,6 +86,7 @@ def test_noalloc_matches_regular_entry_point(lib):
         expect = kops.decode_attention(q, cache, bt, lens, 1.0 / math.sqrt(q.shape[2]), max_len)
         # the same kernels on the same split length: the outputs are identical bit for bit
         assert torch.equal(out.view_as(expect), expect)
+    kops.C.set_decode_persist(prev)
 
 
 def test_noalloc_on_a_second_device(lib):
