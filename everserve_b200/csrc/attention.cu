@@ -162,12 +162,16 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
       for (int tb = 0; tb < BS / 16; tb++) {
         const int tok0 = blk * BS + tb * 16;  // global position of the step's first row
         // S = q . K^T for 16 positions (two n-tiles of 8)
-        float s[2][4];
+        // the even and odd k-steps accumulate apart (four independent chains), then add
+        float s[2][4], s_odd[2][4];
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
-          s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+        for (int j = 0; j < 2; j++)
 #pragma unroll
-          for (int kp = 0; kp < D / 32; kp++) {
+          for (int e = 0; e < 4; e++) s[j][e] = s_odd[j][e] = 0.f;
+#pragma unroll
+        for (int kp = 0; kp < D / 32; kp++) {
+#pragma unroll
+          for (int j = 0; j < 2; j++) {
             uint32_t b0, b1, b2, b3;
             const int t = tb * 16 + j * 8 + (lane & 7);
             const int d = kp * 32 + (lane >> 3) * 8;
@@ -175,9 +179,13 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
             const uint32_t a0[4] = {qa[2 * kp][0], 0u, qa[2 * kp][1], 0u};
             const uint32_t a1[4] = {qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u};
             ptx::mma_bf16_16816(s[j], a0, b0, b1);
-            ptx::mma_bf16_16816(s[j], a1, b2, b3);
+            ptx::mma_bf16_16816(s_odd[j], a1, b2, b3);
           }
         }
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+          for (int e = 0; e < 4; e++) s[j][e] += s_odd[j][e];
         // online softmax on row gid (this thread: positions tig*2+{0,1} of each n-tile)
         float v[4];
         float mx = -INFINITY;

@@ -363,12 +363,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kbase = ptx::smem_u32(ring + (size_t)(warp * p.ws + slot) * 2 * kTile);
       const uint32_t vbase = kbase + kTile;
       const int tok0 = s0 + j * 16;
-      float s[2][4];
+      // S = q . K^T over the 16 positions: the even and odd k-steps accumulate apart (four
+      // independent chains of D / 32 instead of two of D / 16), then add
+      float s[2][4], s_odd[2][4];
 #pragma unroll
-      for (int jn = 0; jn < 2; jn++) {
-        s[jn][0] = s[jn][1] = s[jn][2] = s[jn][3] = 0.f;
+      for (int jn = 0; jn < 2; jn++)
 #pragma unroll
-        for (int kp = 0; kp < D / 32; kp++) {
+        for (int e = 0; e < 4; e++) s[jn][e] = s_odd[jn][e] = 0.f;
+#pragma unroll
+      for (int kp = 0; kp < D / 32; kp++) {
+#pragma unroll
+        for (int jn = 0; jn < 2; jn++) {
           uint32_t b0, b1, b2, b3;
           const int t = jn * 8 + (lane & 7);
           const int d = kp * 32 + (lane >> 3) * 8;
@@ -376,9 +381,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a0[4] = {qa[2 * kp][0], 0u, qa[2 * kp][1], 0u};
           const uint32_t a1[4] = {qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u};
           ptx::mma_bf16_16816(s[jn], a0, b0, b1);
-          ptx::mma_bf16_16816(s[jn], a1, b2, b3);
+          ptx::mma_bf16_16816(s_odd[jn], a1, b2, b3);
         }
       }
+#pragma unroll
+      for (int jn = 0; jn < 2; jn++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) s[jn][e] += s_odd[jn][e];
       float v[4];
       float mx = -INFINITY;
 #pragma unroll

@@ -15,7 +15,7 @@ import math
 
 import torch
 
-from ..ops import KernelOps, pack_weight, ref
+from ..ops import KernelOps, PackedWeight, pack_weight, ref
 
 
 def _graph_ms(body, iters):
@@ -93,6 +93,12 @@ def main() -> None:
                 byts_s = (N * K + M * K + M * N // 2) * 2
                 rows.append({"kernel": "gemm_silu", "name": name, "M": M, "N": N, "K": K,
                              "us": round(sms * 1e3, 2), "gb_s": round(byts_s / sms / 1e6, 1)})
+                # and pre-packed, as the decode step runs it
+                pw = PackedWeight(w)
+                pss = _time(lambda: k.linear_silu(x, pw), flush=flush)
+                rows.append({"kernel": "gemm_silu_packed", "name": name, "M": M, "N": N, "K": K,
+                             "us": round(pss * 1e3, 2), "gb_s": round(byts_s / pss / 1e6, 1)})
+                del pw
     if a.only in (None, "attn"):
         hq, hkv, d, bs = 32 // tp, max(1, 8 // tp), 128, 16
         B, ctx = M, a.ctx
