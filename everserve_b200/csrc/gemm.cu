@@ -24,6 +24,8 @@
 #include <mutex>
 #include <unordered_map>
 
+#include <unistd.h>  // environ
+
 #include "api.h"
 #include "comm.cuh"
 #include "common.cuh"
@@ -711,11 +713,20 @@ static int64_t split_for(int64_t tiles, int64_t kb, int64_t slots, int64_t num_s
 }
 
 void gemm_plan(int64_t M, int64_t N, int64_t K, int64_t num_sms, int* splits, int* cps) {
-  // tuning override for measurements: ES_GEMM_PLAN="<splits>,<ctas per SM>" for decode sizes
-  static const char* forced = std::getenv("ES_GEMM_PLAN");
-  if (forced != nullptr && M <= 64) {
+  // tuning overrides for measurements, decode sizes: ES_GEMM_PLAN_<N>x<K>="<splits>,<ctas per SM>"
+  // for one weight shape, ES_GEMM_PLAN for every shape
+  static const bool any_forced = [] {  // read the environment per launch only when it has any
+    for (char** e = environ; e != nullptr && *e != nullptr; e++)
+      if (std::strncmp(*e, "ES_GEMM_PLAN", 12) == 0) return true;
+    return false;
+  }();
+  if (any_forced && M <= 64) {
+    char name[64];
+    snprintf(name, sizeof(name), "ES_GEMM_PLAN_%lldx%lld", (long long)N, (long long)K);
+    const char* forced = std::getenv(name);
+    if (forced == nullptr) forced = std::getenv("ES_GEMM_PLAN");
     int s = 0, c = 0;
-    if (sscanf(forced, "%d,%d", &s, &c) == 2 && s >= 1 && s <= 8 && (c == 1 || c == 2)) {
+    if (forced != nullptr && sscanf(forced, "%d,%d", &s, &c) == 2 && s >= 1 && s <= 8 && (c == 1 || c == 2)) {
       *splits = s;
       *cps = c;
       return;
