@@ -36,6 +36,10 @@ class EngineConfig:
     # the GPU, or to the experts' owners over a peer-memory TP group) instead of running every
     # local expert on every token; ES_MOE_ROUTED=0 turns it off
     moe_routed: bool = field(default_factory=lambda: os.environ.get("ES_MOE_ROUTED", "1") != "0")
+    # Engine.step keeps one decode step in flight: step N+1 is enqueued (its token fed from step N's
+    # sampled id on the device) before step N's ids are read back, so the host's bookkeeping overlaps
+    # the device; ES_ASYNC_DECODE=0 turns it off
+    async_decode: bool = field(default_factory=lambda: os.environ.get("ES_ASYNC_DECODE", "1") != "0")
     extra: dict = field(default_factory=dict)
 
     def __post_init__(self):

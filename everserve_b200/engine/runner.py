@@ -61,6 +61,12 @@ class ModelRunner:
         self.graphs: dict[tuple[int, bool], torch.cuda.CUDAGraph] = {}  # (bucket, sampled)
         self.graph_out: dict[tuple[int, bool], torch.Tensor] = {}
         self.h_out = torch.zeros(B, dtype=torch.int64, pin_memory=pin)
+        # pipelined steps: two pinned result buffers (a step's ids are read while the next runs), and
+        # the event after the last staged host -> device copies (the pinned staging buffers are
+        # rewritten only once those copies have run)
+        self.h_ids = [torch.zeros(B, dtype=torch.int64, pin_memory=pin) for _ in range(2)]
+        self._ids_slot = 0
+        self._staged = None
         self._pool = None
         self.last_logprobs = None  # (chosen [B], top ids [B, k], top values [B, k]) of the last step
         if self.device.type == "cuda" and model.ops.kind == "kernel":
@@ -107,6 +113,9 @@ class ModelRunner:
 
     def stage_decode(self, plan: StepPlan) -> int:
         """Copy a decode plan's inputs into the static device buffers; returns the bucket size."""
+        if self._staged is not None:
+            self._staged.synchronize()  # the previous step's copies have read the staging buffers
+            self._staged = None
         n = len(plan.reqs)
         b = self._bucket(n)
         h = self.h_i64_np
@@ -141,6 +150,9 @@ class ModelRunner:
         self.h2d_bytes = 4 * b * 8 + b * self.max_blocks * 4
         if self.sampled(plan):
             self._stage_sampling(plan, b)
+        if self.device.type == "cuda":
+            self._staged = torch.cuda.Event()
+            self._staged.record(torch.cuda.current_stream(self.device))
         return b
 
     def _decode_input(self, b: int, sampled: bool = False) -> StepInput:
@@ -291,6 +303,47 @@ class ModelRunner:
         pos = d[1, :b]
         blk = self.d_bt[:b].gather(1, (pos // bs).clamp(max=self.max_blocks - 1)[:, None].to(torch.int64))[:, 0]
         d[2, :b] = torch.where(live, blk.long() * bs + pos % bs, torch.full_like(pos, -1))
+
+    # ---- pipelined decode -------------------------------------------------------------------------
+    def launch_next(self, plan: StepPlan, prev_ids: torch.Tensor) -> torch.Tensor:
+        """Enqueue the decode step `plan` whose fed token of row i is the previous step's sampled id
+        `prev_ids[i]`, still on the device; returns its sampled ids (device [n]). Positions, slots,
+        context lengths, block tables and sampling parameters go from the host as in `execute`; only
+        the ids row is taken on the device, so the step can be enqueued before the previous step's
+        ids reach the host."""
+        n = len(plan.reqs)
+        b = self.stage_decode(plan)
+        self.d_i64[0, :n].copy_(prev_ids[:n])
+        key = (b, self.sampled(plan))
+        if self.use_graphs and self.model.last and self.model.first:
+            if key not in self.graphs:
+                self._capture(*key)
+            self.graphs[key].replay()
+            return self.graph_out[key][:n]
+        return self.forward(self._decode_input(*key))[:n]
+
+    def start_fetch(self, ids: torch.Tensor):
+        """Start the device -> pinned host copy of a step's sampled ids (behind the work enqueued so
+        far); `collect` waits for that copy alone. Two buffers alternate, so a step's ids can be in
+        flight while the previous step's are read."""
+        n = ids.numel()
+        self._ids_slot ^= 1
+        buf = self.h_ids[self._ids_slot]
+        if n > buf.numel():
+            buf = self.h_ids[self._ids_slot] = torch.zeros(n, dtype=torch.int64, pin_memory=self.device.type == "cuda")
+        buf[:n].copy_(ids.reshape(-1), non_blocking=True)
+        ev = None
+        if self.device.type == "cuda":
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+        return buf, n, ev
+
+    @staticmethod
+    def collect(handle) -> list[int]:
+        buf, n, ev = handle
+        if ev is not None:
+            ev.synchronize()
+        return buf[:n].tolist()
 
     def fetch(self, ids: torch.Tensor) -> list[int]:
         """Device -> pinned host copy of sampled ids, synchronised on the copy's stream."""

@@ -85,3 +85,62 @@ def test_scheduler_rejects_long():
     except ValueError:
         return
     raise AssertionError("expected ValueError")
+
+
+def test_async_decode_matches_sync():
+    """Engine.step with one decode step in flight (the next step enqueued before the last step's
+    ids are read) gives the same tokens as the synchronous loop: greedy and seeded sampling,
+    requests ending on their length at different steps and on an end-of-sequence token, requests
+    joining mid-run, and the KV connector sees the same commits."""
+
+    class Log:
+        def __init__(self):
+            self.commits, self.done = [], []
+
+        def begin_step(self, plan, scheduler):
+            pass
+
+        def end_step(self, plan, scheduler):
+            self.commits.append(sorted((r.req_id, r.start_pos + len(r.token_ids)) for r in plan.reqs))
+
+        def finished(self, req_id):
+            self.done.append(req_id)
+
+    def run(async_decode, eos=None):
+        eng = _engine(max_batch=4, async_decode=async_decode)
+        log = Log()
+        eng.connector = log
+        sp = [SamplingParams(max_tokens=9), SamplingParams(max_tokens=4, temperature=0.8, seed=3),
+              SamplingParams(max_tokens=12, temperature=1.1, top_k=5, seed=7)]
+        if eos is not None:
+            sp[0] = SamplingParams(max_tokens=30, eos_id=eos, ignore_eos=False)
+        ids = [eng.add_request([3 + i, 9, 4 + 2 * i], p) for i, p in enumerate(sp)]
+        steps = 0
+        while eng.has_work():
+            eng.step()
+            steps += 1
+            if steps == 5:  # a request joins while the others decode
+                ids.append(eng.add_request([11, 12], SamplingParams(max_tokens=6)))
+        outs = [eng.request(r).outputs for r in ids]
+        # requests by their index (ids differ between engines); commits per request, in order
+        index = {r: i for i, r in enumerate(ids)}
+        per = {}
+        for c in log.commits:
+            for rid, n in c:
+                per.setdefault(index[rid], []).append(n)
+        return outs, per, sorted(index[r] for r in log.done), eng
+
+    sync_out, sync_commits, sync_done, _ = run(False)
+    async_out, async_commits, async_done, eng = run(True)
+    assert async_out == sync_out
+    assert async_done == sync_done
+    for rid, ns in sync_commits.items():
+        # the asynchronous loop may commit one row past a request's end (computed, then dropped)
+        got = async_commits[rid]
+        assert got[: len(ns)] == ns and len(got) <= len(ns) + 1
+    assert eng.async_decode
+    # an end-of-sequence token: the step already in flight for that request is dropped
+    eos = sync_out[0][2]
+    s_out, _, _, _ = run(False, eos=eos)
+    a_out, _, _, _ = run(True, eos=eos)
+    assert a_out == s_out and s_out[0][-1] == eos and len(s_out[0]) <= 3
