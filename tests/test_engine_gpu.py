@@ -106,3 +106,28 @@ def test_fp8_forward_matches_reference_and_graphs(cuda):
                                 quant="fp8", use_cuda_graphs=graphs))
         outs.append(e.generate([[1, 2, 3], [7, 7, 7, 7]], max_tokens=6))
     assert outs[0] == outs[1]
+
+
+def test_async_decode_matches_sync_on_graphs(cuda):
+    """One decode step in flight (the next step's token fed from the last sample on the device, its
+    graph replayed before the last ids are read) gives the synchronous loop's tokens: greedy and
+    seeded sampling, requests of different lengths, one joining mid-run."""
+    prompts = [[i, i + 1, i + 2, 7] for i in range(1, 6)]
+    params = [SamplingParams(max_tokens=12), SamplingParams(max_tokens=5, temperature=0.9, seed=4),
+              SamplingParams(max_tokens=16, temperature=1.2, top_k=7, top_p=0.9, seed=5),
+              SamplingParams(max_tokens=9), SamplingParams(max_tokens=3)]
+    outs = []
+    for async_decode in (False, True):
+        cfg = _cfg(TINY_LLAMA, True)
+        cfg.async_decode = async_decode
+        eng = Engine(cfg)
+        assert eng.async_decode == async_decode
+        ids = [eng.add_request(p, sp) for p, sp in zip(prompts, params)]
+        n = 0
+        while eng.has_work():
+            eng.step()
+            n += 1
+            if n == 4:
+                ids.append(eng.add_request([9, 8, 7], SamplingParams(max_tokens=7)))
+        outs.append([eng.request(r).outputs for r in ids])
+    assert outs[0] == outs[1]
