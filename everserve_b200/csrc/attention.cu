@@ -2,7 +2,7 @@
 //
 // Cache layout (one layer): [num_blocks, 2 (k, v), kv_heads, block_size, head_dim] bf16, so the
 // K (or V) rows of one (block, kv head) are one contiguous tile of block_size * head_dim * 2 bytes.
-// A CTA owns one (sequence, kv head, split of part_tokens positions) and serves the G <= 8 query
+// A CTA owns one (sequence, kv head, split of at most part_tokens positions) and serves the G <= 8 query
 // heads that share the kv head (GQA). Thread 0 streams whole K and V tiles into a 3-stage shared
 // ring with TMA (128-byte swizzle, so the tensor-core fragment loads below are bank-conflict free);
 // each of the 4 warps takes one block of every stage and computes S = q.K^T and O += P.V with
@@ -80,7 +80,12 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
 
   const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int ctx = p.ctx_lens[b];
-  const int s0 = split * p.part_tokens;
+  // a sequence's splits are equal to a block (at most part_tokens each), not part_tokens and a
+  // short rest: the CTAs of a step are closer in length; the count is ceil(ctx / part_tokens) as
+  // the merges assume, and no split is empty (ns - 1 splits of at most part_tokens are below ctx)
+  const int ns_b = max(1, min(p.max_splits, (ctx + p.part_tokens - 1) / p.part_tokens));
+  const int plen = ((ctx + ns_b - 1) / ns_b + BS - 1) / BS * BS;
+  const int s0 = split * plen;
   const int G = p.hq / p.hkv;
   const bool empty = s0 >= ctx;
   if (empty && !p.cluster) {
@@ -90,7 +95,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     return;
   }
   // (an empty split of a cluster stays for the cluster's barriers and contributes nothing)
-  const int s1 = empty ? s0 : min(ctx, s0 + p.part_tokens);
+  const int s1 = empty ? s0 : min(ctx, s0 + plen);
   const int blk0 = s0 / BS, blk1 = (s1 + BS - 1) / BS;
   const int nchunks = empty ? 0 : (blk1 - blk0 + kWarps - 1) / kWarps;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -357,28 +362,41 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
 }
 
 // Merge the splits of every (sequence, head) in split order; out rows of out_stride elements. The
-// same arithmetic, in the same order, as the in-kernel merge of the last split.
-__global__ void decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                                    const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out,
-                                    int64_t out_stride, int hq, int max_splits, int part_tokens, int d) {
+// same arithmetic, in the same order, as the in-kernel merge of the last split. One warp per
+// (sequence, head), eight to a CTA (a CTA per pair would be thousands of tiny CTAs); each lane
+// merges four consecutive elements of the row with 16-byte loads.
+constexpr int kMergeWarps = 8;
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                        const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out, int64_t out_stride,
+                        int B, int hq, int max_splits, int part_tokens, int d) {
   pdl_wait();
   pdl_launch();
-  const int b = blockIdx.x, h = blockIdx.y;
+  const int pair = blockIdx.x * kMergeWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (pair >= B * hq) return;
+  const int b = pair / hq, h = pair % hq;
   const int ctx = ctx_lens[b];
   const int ns = min(max_splits, (ctx + part_tokens - 1) / part_tokens);
   const size_t row0 = ((size_t)b * hq + h) * max_splits;
   float m = -INFINITY;
   for (int s = 0; s < ns; s++) m = fmaxf(m, part_ml[(row0 + s) * 2]);
-  for (int e = threadIdx.x; e < d; e += blockDim.x) {
-    float num = 0.f, den = 0.f;
+  for (int e4 = lane; e4 < d / 4; e4 += 32) {
+    float num[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.f;
     for (int s = 0; s < ns; s++) {
       const float w = part_ml[(row0 + s) * 2 + 1] * exp2f(part_ml[(row0 + s) * 2] - m);
-      num += w * part_o[(row0 + s) * d + e];
+      const float4 o = *reinterpret_cast<const float4*>(part_o + (row0 + s) * d + e4 * 4);
+      num[0] += w * o.x;
+      num[1] += w * o.y;
+      num[2] += w * o.z;
+      num[3] += w * o.w;
       den += w;
     }
-    out[(size_t)b * out_stride + (size_t)h * d + e] = f2bf(ns > 0 ? num / den : 0.f);
+    __nv_bfloat16* dst = out + (size_t)b * out_stride + (size_t)h * d + e4 * 4;
+#pragma unroll
+    for (int j = 0; j < 4; j++) dst[j] = f2bf(ns > 0 ? num[j] / den : 0.f);
   }
 }
+inline dim3 merge_grid(int B, int hq) { return dim3((unsigned)((B * hq + kMergeWarps - 1) / kMergeWarps)); }
 
 template <int D, int BS, int S>
 cudaError_t launch_decode(const CUtensorMap& map, const DecodeParams& p, int B, cudaStream_t stream) {
@@ -475,10 +493,9 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   else if (a.d == 64 && a.block_size == 32) e = attn::launch_stages<64, 32>(a.stages, map, p, a.B, stream);
   else return cudaErrorInvalidValue;
   if (e != cudaSuccess || p.tickets != nullptr || p.cluster) return e;
-  dim3 mgrid(a.B, a.hq);
-  return launch_ex(attn::decode_merge_kernel, mgrid, dim3(a.d), 0, stream, 0, (const float*)a.part_o,
-                   (const float*)a.part_ml, a.ctx_lens, static_cast<__nv_bfloat16*>(a.out), a.out_stride, a.hq,
-                   a.max_splits, a.part_tokens, a.d);
+  return launch_ex(attn::decode_merge_kernel, attn::merge_grid(a.B, a.hq), dim3(attn::kMergeWarps * 32), 0, stream,
+                   0, (const float*)a.part_o, (const float*)a.part_ml, a.ctx_lens, static_cast<__nv_bfloat16*>(a.out),
+                   a.out_stride, a.B, a.hq, a.max_splits, a.part_tokens, a.d);
 }
 
 }  // namespace es
@@ -685,9 +702,9 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   else if (head_dim == 128 && block_size == 32) e = attn::launch_stages<128, 32>(2, map, p, batch, s);
   else e = attn::launch_stages<64, 32>(2, map, p, batch, s);
   if (e == cudaSuccess && p.tickets == nullptr && !p.cluster) {
-    dim3 mgrid(batch, q_heads);
-    attn::decode_merge_kernel<<<mgrid, head_dim, 0, s>>>(p.part_o, p.part_ml, ctx_lens, static_cast<__nv_bfloat16*>(out),
-                                                         out_stride, q_heads, (int)splits, kPart, head_dim);
+    attn::decode_merge_kernel<<<attn::merge_grid(batch, q_heads), attn::kMergeWarps * 32, 0, s>>>(
+        p.part_o, p.part_ml, ctx_lens, static_cast<__nv_bfloat16*>(out), out_stride, batch, q_heads, (int)splits, kPart,
+        head_dim);
     e = cudaGetLastError();
   }
   return (int)e;
