@@ -43,6 +43,7 @@ struct DecodeParams {
   const uint8_t* pf;  // memory the next kernel reads, fetched into L2 meanwhile (nullable)
   int64_t pf_bytes;
   int cluster;  // the splits of a (sequence, kv head) form one cluster and merge through DSMEM
+  int early;    // issue the K/V chunks that need no output of the kernel before ahead of the wait
   __nv_bfloat16* out;  // [B, Hq * D] rows of out_stride
   int64_t out_stride;
   int hq, hkv, max_splits, part_tokens;
@@ -70,16 +71,23 @@ ES_DEVICE uint32_t swz(int t, int d) {
 
 template <int D, int BS, int kStages>
 __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ CUtensorMap cmap, DecodeParams p) {
-  pdl_wait();
-  pdl_launch();
+  // Before the wait for the kernel before (the qkv projection, which writes q and each sequence's
+  // newest K/V row) only what earlier kernels and earlier steps wrote is read: the context lengths,
+  // the block tables (read past L1) and, with `early`, the K/V rows of blocks before a sequence's
+  // last one, so the first stage of the history can stream while the projection finishes.
   using C = DecodeCfg<D, BS, kStages>;
   constexpr int NT = D / 8;  // n-tiles of the output
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * C::kStageBytes);
 
-  const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-  const int ctx = p.ctx_lens[b];
+  // grid (splits, sequences, kv heads): the splits of a pair are neighbours, so the CTAs of splits
+  // a short history does not reach leave among the busy ones, not as a wave at the end; a cluster
+  // launch keeps (sequences, kv heads, splits) with the splits along z, its cluster dimension
+  const int split = p.cluster ? blockIdx.z : blockIdx.x;
+  const int b = p.cluster ? blockIdx.x : blockIdx.y;
+  const int kvh = p.cluster ? blockIdx.y : blockIdx.z;
+  const int ctx = __ldcg(p.ctx_lens + b);
   // a sequence's splits are equal to a block (at most part_tokens each), not part_tokens and a
   // short rest: the CTAs of a step are closer in length; the count is ceil(ctx / part_tokens) as
   // the merges assume, and no split is empty (ns - 1 splits of at most part_tokens are below ctx)
@@ -89,6 +97,8 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   const int G = p.hq / p.hkv;
   const bool empty = s0 >= ctx;
   if (empty && !p.cluster) {
+    pdl_wait();
+    pdl_launch();
     if (split == 0)  // an empty history: the output is zero
       for (int i = threadIdx.x; i < G * D; i += kThreads)
         p.out[(size_t)b * p.out_stride + (size_t)kvh * G * D + i] = f2bf(0.f);
@@ -117,7 +127,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     const int n = min(kWarps, blk1 - first);
     ptx::mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * C::kTileBytes * n));
     for (int i = 0; i < n; i++) {
-      const int64_t phys = bt[first + i];
+      const int64_t phys = __ldcg(bt + first + i);
       const int row_k = (int)(((phys * 2 + 0) * p.hkv + kvh) * BS * C::kRowsPerTok);
       const int row_v = (int)(((phys * 2 + 1) * p.hkv + kvh) * BS * C::kRowsPerTok);
       uint8_t* dst = ring + st * C::kStageBytes + i * 2 * C::kTileBytes;
@@ -125,9 +135,16 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
       ptx::tma_load_2d_hint(dst + C::kTileBytes, &cmap, 0, row_v, &full[st], pol);
     }
   };
+  // chunks holding none of the sequence's last block go before the wait; the rest after it
+  const int last_blk = (ctx - 1) / BS;
+  int early = 0;
+  if (tid == 0 && p.early)
+    for (; early < kStages - 1 && early < nchunks && blk0 + (early + 1) * kWarps - 1 < last_blk; early++) issue(early);
+  pdl_wait();
+  pdl_launch();
   if (tid == 0) {
-    for (int c = 0; c < kStages - 1 && c < nchunks; c++) issue(c);
-    ptx::l2_prefetch_share(p.pf, p.pf_bytes, (int)(b + gridDim.x * (kvh + gridDim.y * split)),
+    for (int c = early; c < kStages - 1 && c < nchunks; c++) issue(c);
+    ptx::l2_prefetch_share(p.pf, p.pf_bytes, (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)),
                            (int)(gridDim.x * gridDim.y * gridDim.z));
   }
 
@@ -406,7 +423,7 @@ cudaError_t launch_decode(const CUtensorMap& map, const DecodeParams& p, int B, 
     return cudaFuncSetAttribute(decode_kernel<D, BS, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
   });
   if (e != cudaSuccess) return e;
-  dim3 grid(B, p.hkv, p.max_splits);
+  const dim3 grid = p.cluster ? dim3(B, p.hkv, p.max_splits) : dim3(p.max_splits, B, p.hkv);
   return launch_ex(decode_kernel<D, BS, S>, grid, dim3(kThreads), C::kSmem, stream, p.cluster ? p.max_splits : 0,
                    map, p);
 }
@@ -428,6 +445,15 @@ cudaError_t launch_stages(int stages, const CUtensorMap& map, const DecodeParams
 bool use_tc() {
   static const bool on = [] {
     const char* v = std::getenv("ES_ATTN_TC");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+// ES_ATTN_EARLY=1: the K/V copies that need no output of the kernel before go ahead of the wait
+// for it (measured level with issuing them after it, so off by default)
+bool early_loads() {
+  static const bool on = [] {
+    const char* v = std::getenv("ES_ATTN_EARLY");
     return v && v[0] == '1';
   }();
   return on;
@@ -456,7 +482,8 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   if (attn::use_tc() && decode_tc_supported(a)) return launch_decode_tc(a, stream);
   if (!attn::fused_merge() && !attn::cluster_merge(a.max_splits) && decode_persist_supported(a))
     return launch_decode_persist(a, stream);
-  if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.hq / a.hkv > 8 || a.part_tokens % 64 != 0 || a.max_splits <= 0)
+  if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.hq / a.hkv > 8 || a.part_tokens % 64 != 0 || a.max_splits <= 0 ||
+      a.B > 65535)
     return cudaErrorInvalidValue;
   if (a.s_kv != (int64_t)a.hkv * a.block_size * a.d || a.s_block != 2 * a.s_kv) return cudaErrorInvalidValue;
   attn::DecodeParams p{};
@@ -476,6 +503,7 @@ cudaError_t launch_paged_decode(const DecodeArgs& a, cudaStream_t stream) {
   p.tickets = attn::fused_merge() ? a.tickets : nullptr;
   p.cluster = attn::cluster_merge(a.max_splits) ? 1 : 0;
   if (p.cluster) p.tickets = nullptr;
+  p.early = attn::early_loads() ? 1 : 0;
   p.pf = static_cast<const uint8_t*>(a.prefetch);
   p.pf_bytes = a.prefetch_bytes;
   p.out = static_cast<__nv_bfloat16*>(a.out);
@@ -613,6 +641,7 @@ extern "C" __attribute__((visibility("default"))) int es_paged_decode_noalloc(
   p.tickets = attn::fused_merge() ? tickets : nullptr;
   p.cluster = attn::cluster_merge((int)splits) ? 1 : 0;
   if (p.cluster) p.tickets = nullptr;
+  p.early = attn::early_loads() ? 1 : 0;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride = out_stride;
   // tensor map encoded on the stack (no cache: nothing is allocated, not even on the host heap)

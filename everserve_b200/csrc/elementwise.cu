@@ -5,6 +5,7 @@
 // its outputs once. Results do not depend on how many tokens are in the batch (one CTA per
 // token, fixed reduction trees), so a replayed step computes bit-identical rows.
 #include <algorithm>
+#include <cstdlib>
 
 #include "api.h"
 #include "common.cuh"
@@ -20,12 +21,30 @@ namespace {
 template <int VPT, bool kResidual>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
-                               int hidden, int x_stride, int y_stride, float eps) {
+                               int hidden, int x_stride, int y_stride, float eps, int early) {
+  const int nvec = hidden >> 3;
+  // the weight is no kernel's output: its loads can be in flight before the wait for the kernel
+  // before (ES_NORM_EARLY=0: after it)
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4 wv[VPT];
+  if (early) {
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+      const int i = threadIdx.x + j * blockDim.x;
+      if (i < nvec) wv[j] = wr[i];
+    }
+  }
   pdl_wait();
   pdl_launch();
+  if (!early) {
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+      const int i = threadIdx.x + j * blockDim.x;
+      if (i < nvec) wv[j] = wr[i];
+    }
+  }
   __shared__ float red[32];
   const int t = blockIdx.x;
-  const int nvec = hidden >> 3;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)t * x_stride);
   uint4* rr = kResidual ? reinterpret_cast<uint4*>(residual + (size_t)t * hidden) : nullptr;
   float v[VPT][8];
@@ -51,14 +70,13 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat1
   }
   ss = block_sum(ss, red);
   const float inv = rsqrtf(ss / (float)hidden + eps);
-  const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* yr = reinterpret_cast<uint4*>(y + (size_t)t * y_stride);
 #pragma unroll
   for (int j = 0; j < VPT; j++) {
     const int i = threadIdx.x + j * blockDim.x;
     if (i < nvec) {
       float wf[8], o[8];
-      unpack8(wr[i], wf);
+      unpack8(wv[j], wf);
 #pragma unroll
       for (int e = 0; e < 8; e++) o[e] = v[j][e] * inv * wf[e];
       yr[i] = pack8(o);
@@ -328,11 +346,15 @@ cudaError_t launch_rmsnorm(const void* x, void* residual, const void* w, void* y
   auto wp = static_cast<const __nv_bfloat16*>(w);
   auto yp = static_cast<__nv_bfloat16*>(y);
   const int xs = (int)x_stride, ys = (int)y_stride;
+  static const int early = [] {
+    const char* v = std::getenv("ES_NORM_EARLY");
+    return v && v[0] == '0' ? 0 : 1;
+  }();
 #define ES_LAUNCH_RMS(V)                                                                                      \
   return rp ? launch_ex(rmsnorm_kernel<V, true>, dim3((unsigned)rows), dim3(threads), 0, stream, 0, xp, rp, wp, yp, \
-                        hidden, xs, ys, eps)                                                                      \
+                        hidden, xs, ys, eps, early)                                                               \
             : launch_ex(rmsnorm_kernel<V, false>, dim3((unsigned)rows), dim3(threads), 0, stream, 0, xp, rp, wp, yp, \
-                        hidden, xs, ys, eps);
+                        hidden, xs, ys, eps, early);
   if (vpt == 1) {
     ES_LAUNCH_RMS(1)
   } else if (vpt == 2) {
