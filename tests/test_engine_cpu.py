@@ -144,3 +144,55 @@ def test_async_decode_matches_sync():
     s_out, _, _, _ = run(False, eos=eos)
     a_out, _, _, _ = run(True, eos=eos)
     assert a_out == s_out and s_out[0][-1] == eos and len(s_out[0]) <= 3
+
+
+def _run_all(eng, prompts, params):
+    ids = [eng.add_request(p, sp) for p, sp in zip(prompts, params)]
+    while eng.has_work():
+        eng.step()
+    return [eng.request(r) for r in ids]
+
+
+def test_async_decode_under_block_pressure():
+    """With few KV blocks the asynchronous loop must not take the block the scheduler would have
+    used (it enqueues a step ahead only when the blocks it needs are free): preemptions recompute,
+    and the tokens equal the synchronous loop's and a roomy engine's."""
+    prompts = [[1] * 30, [2] * 30, [3] * 30]
+    params = [SamplingParams(max_tokens=20) for _ in prompts]
+    outs = {}
+    for async_decode in (False, True):
+        eng = _engine(num_blocks=6, max_batch=4, async_decode=async_decode)
+        outs[async_decode] = [r.outputs for r in _run_all(eng, prompts, params)]
+        assert eng.blocks.free_blocks == 6  # every block given back
+    roomy = [r.outputs for r in _run_all(_engine(num_blocks=64), prompts, params)]
+    assert outs[True] == outs[False] == roomy
+
+
+def test_async_decode_with_logprobs_and_multistep():
+    """A request asking for log-probabilities keeps its batch synchronous (the records come from the
+    step's logits); multi-step decoding after asynchronous steps first applies the step in flight.
+    Both give the synchronous loop's tokens and records."""
+    def run(async_decode):
+        eng = _engine(async_decode=async_decode)
+        a = eng.add_request([4, 5, 6], SamplingParams(max_tokens=6, logprobs=2))
+        b = eng.add_request([7, 8], SamplingParams(max_tokens=6))
+        while eng.has_work():
+            eng.step()
+        ra, rb = eng.request(a), eng.request(b)
+        # a settled greedy batch: asynchronous steps, then a multi-step window, then more steps
+        c = eng.add_request([1, 2, 3], SamplingParams(max_tokens=14))
+        d = eng.add_request([3, 2, 1], SamplingParams(max_tokens=14))
+        for _ in range(4):
+            eng.step()
+        window = eng.decode_steps(3)  # after the flush: the in-flight step's token comes first
+        rc, rd = eng.request(c), eng.request(d)
+        for r, w in zip((rc, rd), window):
+            assert r.outputs[-3:] == w
+        while eng.has_work():
+            eng.step()
+        return (ra.outputs, [(round(lp, 5), [t for t, _ in top]) for lp, top in ra.logprobs], rb.outputs,
+                rc.outputs, rd.outputs)
+
+    sync, asyn = run(False), run(True)
+    assert asyn == sync
+    assert len(sync[3]) == 14 and len(sync[4]) == 14
