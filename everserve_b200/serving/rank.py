@@ -204,7 +204,9 @@ class RankProcess:
         else:
             barrier = lambda: self._store_barrier("tp/e0", members)  # noqa: E731
         coll = FusedTPCollective(dev, region=self.region, row=self.row, members=members, barrier=barrier)
-        coll.set_bound_ns(self.settings.bound_ns(0.0))
+        # generous until the step period is measured (_sample_step), then `detect_steps` periods
+        coll.set_bound_ns(self.settings.warmup_bound_ns())
+        self._step_dt = []
         coll.set_beat_limit_us(int(self.settings.beat_limit_ms * 1000))
         if not self.spare:
             self._start_watch(coll, members)
@@ -388,6 +390,16 @@ class RankProcess:
             except Exception:  # noqa: BLE001
                 pass
 
+    def _sample_step(self, seconds: float) -> None:
+        """Fit the collective's wait bound to this rank's measured step period: every `step_sample`
+        steps the median sets it to `detect_steps` periods (at least the floor)."""
+        self._step_dt.append(seconds)
+        n = max(1, self.settings.step_sample)
+        if len(self._step_dt) >= n:
+            period = sorted(self._step_dt)[len(self._step_dt) // 2]
+            self.collective.set_bound_ns(self.settings.bound_ns(period))
+            self._step_dt = []
+
     def _step(self, msg: dict) -> None:
         plan = msg["plan"]
         fail = msg.get("fail_rank")
@@ -399,12 +411,14 @@ class RankProcess:
         try:
             if msg["epoch"] != self.runtime.epoch:
                 raise RuntimeError(f"step of epoch {msg['epoch']} on a rank at epoch {self.runtime.epoch}")
+            t_exec = time.monotonic()
             out = self.worker.execute(plan)
             if self.region is not None:
                 if isinstance(out, torch.Tensor):
                     out = out.cpu()
                 else:
                     torch.cuda.synchronize(self.device)
+                self._sample_step(time.monotonic() - t_exec)
                 st = self.collective.status() or self.worker.model.ops.check_status()
                 if st:
                     raise RuntimeError(f"a collective of step {plan.step} failed (status {st}, late rows "
@@ -457,6 +471,9 @@ class RankProcess:
                 gone = [r for r in self.collective.members if r not in members]
                 self.collective.set_members(members, epoch)
                 self.collective.release_rows(gone)
+                # a new member's first steps carry one-off costs: back to the warm-up bound, re-measured
+                self.collective.set_bound_ns(self.settings.warmup_bound_ns())
+                self._step_dt = []
                 self.collective.resume()
                 self._store_barrier(f"tp/e{epoch}", members)
                 self._start_watch(self.collective, members)
