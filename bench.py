@@ -484,16 +484,23 @@ def count_launches(eng, ex) -> int:
     ops = ex.worker.model.ops
     C = ops.C
     counts = {"n": 0}
-    weights = {"paged_decode": 2}
+    # the bindings that launch kernels of this framework, with the launches of one call (the split
+    # decode attention is the attention kernel and its merge); the others (sizes, plans, buffers,
+    # switches) launch nothing
+    launches = {"rmsnorm": 1, "rope_kv_write": 1, "silu_mul": 1, "embed": 1, "argmax": 1, "sample": 1,
+                "decode_advance": 1, "gemm_bf16": 1, "paged_decode": 2, "gemm_silu": 1, "gemm_rope": 1,
+                "quant_fp8": 1, "gemm_fp8": 1, "paged_prefill": 1, "moe_route": 1, "moe_topk": 1, "moe_dispatch": 1,
+                "moe_ready": 1, "moe_combine": 1, "fdar": 1, "gemm_allreduce": 1, "gemm_allgather": 1,
+                "kv_gather": 1, "kv_scatter": 1}
 
     class Counting:
         def __getattr__(self, name):
             fn = getattr(C, name)
-            if not callable(fn) or name.startswith("gemm_pick") or name == "gemm_tiles":
+            if not callable(fn) or name not in launches:
                 return fn
 
             def wrapped(*a, **k):
-                counts["n"] += weights.get(name, 1)
+                counts["n"] += launches[name]
                 return fn(*a, **k)
 
             return wrapped
@@ -503,12 +510,15 @@ def count_launches(eng, ex) -> int:
     if coll is not None and hasattr(coll, "count_launches"):
         coll.count_launches(counts)
     runner = ex.worker.runner
-    saved = runner.use_graphs
+    saved, saved_async = runner.use_graphs, eng.async_decode
     runner.use_graphs = False
+    eng.flush()
+    eng.async_decode = False  # one step, not one step and the next enqueued behind it
     try:
         eng.step()
     finally:
         runner.use_graphs = saved
+        eng.async_decode = saved_async
         ops.C = C
         if coll is not None and hasattr(coll, "count_launches"):
             coll.count_launches(None)

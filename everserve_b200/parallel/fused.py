@@ -387,7 +387,7 @@ class FusedTPCollective:
         class Counting:
             def __getattr__(self, name):
                 fn = getattr(real, name)
-                if name in ("fdar", "gemm_allreduce"):
+                if name in ("fdar", "gemm_allreduce", "gemm_allgather"):
                     def wrapped(*a, **k):
                         counts["n"] += 1
                         return fn(*a, **k)
