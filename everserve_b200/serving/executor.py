@@ -390,11 +390,24 @@ class MultiprocExecutor:
     def change_pending(self) -> bool:
         return self.client is not None and self.client.pending_change.is_set()
 
-    def complete_change(self, engine, t_detect: float | None = None) -> ChangeRecord:
+    def complete_change(self, engine, t_detect: float | None = None, cause: RankLost | None = None) -> ChangeRecord:
+        """Wait for the coordinator's change and adopt it. `cause`: the loss this head saw in a
+        step. A rank that answered with an error is alive, so nothing else reports it: the head
+        reports it itself, unless a change for a fault is already under way; and a change that
+        never comes ends in EngineDown naming the cause, not in a bare timeout."""
         if self.client is None:
             raise EngineDown("no daemon link: a lost rank cannot be replaced")
         t_detect = t_detect or time.monotonic()
-        h = self.client.wait_committed(timeout_s=self.change_timeout_s, after_epoch=self.epoch)
+        if cause is not None and cause.ranks and not self._fault_pending():
+            try:
+                self.client.report_lost(cause.ranks, f"step failed on the rank: {cause.detail}"[:512])
+            except Exception:  # noqa: BLE001 - the wait below still bounds it
+                pass
+        try:
+            h = self.client.wait_committed(timeout_s=self.change_timeout_s, after_epoch=self.epoch)
+        except TimeoutError as e:
+            raise EngineDown(f"no membership change within {self.change_timeout_s} s"
+                             + (f" after {cause}" if cause is not None else "")) from e
         if h.kind == "abandoned":
             raise EngineDown(f"the coordinator abandoned epoch {h.epoch}: {h.detail}")
         mc = h.committed
@@ -481,8 +494,8 @@ def failover(executor: MultiprocExecutor, engine):
             while True:
                 try:
                     out = step_fn()
-                except RankLost:
-                    executor.complete_change(engine, t_detect=time.monotonic())
+                except RankLost as e:
+                    executor.complete_change(engine, t_detect=time.monotonic(), cause=e)
                     continue
                 if executor.change_pending():  # a planned change: complete it at this boundary
                     executor.complete_change(engine, t_detect=time.monotonic())
