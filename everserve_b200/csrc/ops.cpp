@@ -746,8 +746,21 @@ void heartbeat_stop(int64_t id) {
 }
 
 int64_t host_register_mapped(int64_t ptr, int64_t bytes) {
-  ES_CHECK_CUDA(cudaHostRegister(reinterpret_cast<void*>(ptr), (size_t)bytes,
-                                 cudaHostRegisterMapped | cudaHostRegisterPortable));
+  const cudaError_t e = cudaHostRegister(reinterpret_cast<void*>(ptr), (size_t)bytes,
+                                         cudaHostRegisterMapped | cudaHostRegisterPortable);
+  if (e != cudaSuccess) {
+    // pages the host cannot pin (a file on a disk-backed filesystem): the caller falls back to a
+    // pinned copy; the error is cleared first, or the next CUDA call of the process would report it
+    cudaGetLastError();
+    TORCH_CHECK(false, "cudaHostRegister of ", bytes, " bytes failed: ", cudaGetErrorString(e));
+  }
+  void* dev = nullptr;
+  ES_CHECK_CUDA(cudaHostGetDevicePointer(&dev, reinterpret_cast<void*>(ptr), 0));
+  return reinterpret_cast<int64_t>(dev);
+}
+
+// The device address of pinned host memory the CUDA runtime allocated (torch's pinned tensors).
+int64_t host_device_pointer(int64_t ptr) {
   void* dev = nullptr;
   ES_CHECK_CUDA(cudaHostGetDevicePointer(&dev, reinterpret_cast<void*>(ptr), 0));
   return reinterpret_cast<int64_t>(dev);
@@ -898,6 +911,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("heartbeat_start", &heartbeat_start, "advance a beat word every period_us from a native thread; returns its id");
   m.def("heartbeat_stop", &heartbeat_stop, "stop a heartbeat thread");
   m.def("host_unregister", &host_unregister);
+  m.def("host_device_pointer", &host_device_pointer, "device address of runtime-allocated pinned host memory");
   m.def("device_alloc", &device_alloc);
   m.def("device_free", &device_free);
   m.def("memset_async", &memset_async);

@@ -21,6 +21,7 @@ same store protocol; the B200 path gathers all layers in one kernel launch into 
 from __future__ import annotations
 
 import queue
+import os
 import threading
 import time
 from dataclasses import dataclass, field
@@ -103,12 +104,35 @@ class MirrorClient:
             pass
 
 
+def pinnable(path: str) -> bool:
+    """Whether pages of files under `path` can be pinned for the device: files on tmpfs (the
+    node's /dev/shm). Pinning a mapping of a file on a disk-backed filesystem fails, and has
+    crashed the process inside the registration, so it is never attempted there."""
+    try:
+        real = os.path.realpath(path)
+        best, fstype = "", ""
+        with open("/proc/mounts") as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) < 3:
+                    continue
+                mnt = parts[1].replace("\\040", " ")
+                if (real == mnt or real.startswith(mnt.rstrip("/") + "/")) and len(mnt) > len(best):
+                    best, fstype = mnt, parts[2]
+        return fstype == "tmpfs"
+    except OSError:
+        return False
+
+
 @dataclass
 class _Stage:
     name: str
     path: str
     tensor: torch.Tensor  # [layers, heads, cap, 2, d] over the shared file
     dev_ptr: int = 0
+    # where the file's pages cannot be pinned (a data directory on a disk-backed filesystem, not
+    # tmpfs), the gather writes this pinned copy and the sender thread copies it into the file
+    bounce: torch.Tensor | None = None
 
     @property
     def capacity(self) -> int:
@@ -149,6 +173,7 @@ class MirrorCommittedKV:
         self._error: BaseException | None = None
         self._committed: dict[str, int] = {}
         self.restored_step = -1  # the last step a restore covered
+        self._pinnable: bool | None = None  # staging files pinnable in place (see pinnable)
         self._pending_slots: list[int] = []
         self._history: list[dict] = []
         self.stats_record = {"commits": 0, "fence_waits": 0, "fence_wait_s": 0.0, "bytes": 0}
@@ -186,7 +211,14 @@ class MirrorCommittedKV:
         t = torch.from_file(path, shared=True, size=numel, dtype=self.dtype).view(shape)
         st = _Stage(name, path, t)
         if self._C is not None:
-            st.dev_ptr = int(self._C.host_register_mapped(t.data_ptr(), nbytes))
+            if self._pinnable is None:
+                self._pinnable = pinnable(self.rank_dir)
+            if self._pinnable:
+                st.dev_ptr = int(self._C.host_register_mapped(t.data_ptr(), nbytes))
+            else:
+                # runtime-allocated pinned memory the gather writes through its device address
+                st.bounce = torch.empty(shape, dtype=self.dtype, pin_memory=True)
+                st.dev_ptr = int(self._C.host_device_pointer(st.bounce.data_ptr()))
         return st
 
     def _release(self, st: _Stage) -> None:
@@ -194,7 +226,7 @@ class MirrorCommittedKV:
             if len(self._pool) <= self.depth + 1:
                 self._pool.append(st)
                 return
-        if self._C is not None and st.dev_ptr:
+        if self._C is not None and st.dev_ptr and st.bounce is None:
             self._C.host_unregister(st.tensor.data_ptr())
 
     # ---- the pipeline --------------------------------------------------------------------------
@@ -250,6 +282,9 @@ class MirrorCommittedKV:
             try:
                 if job.event is not None:
                     job.event.synchronize()
+                if job.stage.bounce is not None and job.slots:
+                    n = len(job.slots)
+                    job.stage.tensor[:, :, :n].copy_(job.stage.bounce[:, :, :n])
                 job.times["gathered"] = time.perf_counter()
                 staged = self._describe(job) if job.slots else None
                 self.client.commit(self.engine, self.rank, job.epoch, job.step, staged, job.counts)
@@ -325,7 +360,7 @@ class MirrorCommittedKV:
         with self._pool_lock:
             pool, self._pool = self._pool, []
         for st in pool:
-            if self._C is not None and st.dev_ptr:
+            if self._C is not None and st.dev_ptr and st.bounce is None:
                 self._C.host_unregister(st.tensor.data_ptr())
 
     # ---- restore -------------------------------------------------------------------------------
