@@ -104,24 +104,27 @@ class MirrorClient:
             pass
 
 
-def pinnable(path: str) -> bool:
+def pinnable(path: str, mounts: str | None = None) -> bool:
     """Whether pages of files under `path` can be pinned for the device: files on tmpfs (the
     node's /dev/shm). Pinning a mapping of a file on a disk-backed filesystem fails, and has
-    crashed the process inside the registration, so it is never attempted there."""
-    try:
-        real = os.path.realpath(path)
-        best, fstype = "", ""
-        with open("/proc/mounts") as f:
-            for line in f:
-                parts = line.split()
-                if len(parts) < 3:
-                    continue
-                mnt = parts[1].replace("\\040", " ")
-                if (real == mnt or real.startswith(mnt.rstrip("/") + "/")) and len(mnt) > len(best):
-                    best, fstype = mnt, parts[2]
-        return fstype == "tmpfs"
-    except OSError:
-        return False
+    crashed the process inside the registration, so it is never attempted there. `mounts`: the
+    text of /proc/mounts (read when not given)."""
+    if mounts is None:
+        try:
+            with open("/proc/mounts") as f:
+                mounts = f.read()
+        except OSError:
+            return False
+    real = os.path.realpath(path)
+    best, fstype = "", ""
+    for line in mounts.splitlines():
+        parts = line.split()
+        if len(parts) < 3:
+            continue
+        mnt = parts[1].replace("\\040", " ")
+        if (real == mnt or real.startswith(mnt.rstrip("/") + "/")) and len(mnt) > len(best):
+            best, fstype = mnt, parts[2]
+    return fstype == "tmpfs"
 
 
 @dataclass
