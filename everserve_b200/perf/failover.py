@@ -1,10 +1,11 @@
 """Failover latency: dead-rank detection, change commit, resume and the streams' pause.
 
     python -m everserve_b200.perf.failover [--trials 20] [--model tiny-qwen] [--full] [--device cpu]
-                                           [--tp 1 --pp 2] [--streams 8]
+                                           [--tp 1 --pp 2] [--streams 8] [--victim R]
 
 Each trial starts the control plane (coordinator, daemon, store) and an engine (TP1 PP2 by
-default; ``--tp 2 --pp 1`` for the tensor-parallel group whose collectives detect the loss) with a
+default; ``--tp 2 --pp 1`` for the tensor-parallel group whose collectives detect the loss;
+``--tp 1 --pp 1`` for a one-rank engine, whose rank 0 leaves: ``--victim`` picks the rank) with a
 spare for rank 1, generates the streams, kills rank 1 at a random decode step (SIGKILL on the CPU
 tier; between steps on GPUs, where the spare sits on the GPU after the engine's) and checks every
 stream against a no-fault run. Per trial it records, from the fault (the coordinator's stamps are
@@ -52,7 +53,7 @@ def _rate(stamps):
     return round(sum(n for _, n in stamps[1:]) / dt, 1) if dt > 0 else None
 
 
-def run_trial(workdir, model, prompts, tokens, kill_at, device, dtype, tp=1, pp=2):
+def run_trial(workdir, model, prompts, tokens, kill_at, device, dtype, tp=1, pp=2, victim=1):
     from ..engine.config import EngineConfig
     from ..engine.engine import Engine
     from ..serving.cluster import ControlPlane
@@ -66,7 +67,7 @@ def run_trial(workdir, model, prompts, tokens, kill_at, device, dtype, tp=1, pp=
     env = {"NCCL_NVLS_ENABLE": "0", "ES_NVLS": "0", "EVERSERVE_DETECT_FLOOR_MS": "20"} if gpu else None
     with ControlPlane(workdir, engines=[{"name": "e0", "pipelineParallel": pp, "tensorParallel": tp}]) as cp:
         ex = MultiprocExecutor(cfg, engine="e0", daemon=cp.daemon_socket, store=cp.store_socket,
-                               spares=(1,) if kill_at else (), node="n0", threads=2,
+                               spares=(victim,) if kill_at else (), node="n0", threads=2,
                                device="cuda" if gpu else "cpu", dtype="bfloat16" if gpu else "float32",
                                env=env)
         try:
@@ -75,7 +76,7 @@ def run_trial(workdir, model, prompts, tokens, kill_at, device, dtype, tp=1, pp=
             eng = Engine(cfg, executor=ex)
             eng.wrap_step(failover(ex, eng))
             if kill_at:
-                ex.kill_at_decode_step = (kill_at, 1)
+                ex.kill_at_decode_step = (kill_at, victim)
             from ..engine.request import SamplingParams
 
             ids = [eng.add_request(p, SamplingParams(max_tokens=tokens)) for p in prompts]
@@ -102,7 +103,11 @@ def main() -> None:
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--pp", type=int, default=2)
     ap.add_argument("--streams", type=int, default=8)
+    ap.add_argument("--victim", type=int, default=None,
+                    help="the rank that leaves (default 1; 0 for a one-rank engine, --tp 1 --pp 1)")
     a = ap.parse_args()
+    victim = a.victim if a.victim is not None else (1 if a.tp * a.pp > 1 else 0)
+    assert 0 <= victim < a.tp * a.pp, "the victim must be a rank of the engine"
     model = "qwen2.5-0.5b" if a.full else a.model
     from ..models.config import get_config
 
@@ -114,12 +119,12 @@ def main() -> None:
     root = tempfile.mkdtemp(prefix="es-failover-")
     try:
         base, _, base_stamps = run_trial(os.path.join(root, "base"), model, prompts, tokens, 0, a.device, dtype,
-                                         a.tp, a.pp)
+                                         a.tp, a.pp, victim)
         rows = []
         for t in range(a.trials):
             kill_at = 20 if a.full else rng.randrange(3, tokens - 4)
             outs, rec, stamps = run_trial(os.path.join(root, f"t{t}"), model, prompts, tokens, kill_at, a.device,
-                                          dtype, a.tp, a.pp)
+                                          dtype, a.tp, a.pp, victim)
             d = rec.as_dict()
             t_fault = rec.t_fault_wall
             rep_us = rec.coordinator.get("reported_at_us")
@@ -135,7 +140,7 @@ def main() -> None:
                 "spans": d["spans"], "acks_at_us": rec.coordinator.get("acks_at_us"),
             })
         summary = {"metric": "failover pause p99; dead-rank detect ms", "model": model, "device": a.device,
-                   "tp": a.tp, "pp": a.pp, "streams": a.streams, "trials": len(rows),
+                   "tp": a.tp, "pp": a.pp, "victim": victim, "streams": a.streams, "trials": len(rows),
                    "token_identical": all(r["identical"] for r in rows),
                    "tok_s_no_fault": _rate(base_stamps[1:])}
         for k in ("detect_ms", "commit_ms", "resumed_ms", "pause_ms", "tok_s_before", "tok_s_after"):
