@@ -6,7 +6,8 @@
 Each trial starts the control plane (coordinator, daemon, store) and an engine (TP1 PP2 by
 default; ``--tp 2 --pp 1`` for the tensor-parallel group whose collectives detect the loss;
 ``--tp 1 --pp 1`` for a one-rank engine, whose rank 0 leaves: ``--victim`` picks the rank) with a
-spare for rank 1, generates the streams, kills rank 1 at a random decode step (SIGKILL on the CPU
+spare for the victim rank (rank 1 by default), generates the streams, kills the victim at a random
+decode step (SIGKILL on the CPU
 tier; between steps on GPUs, where the spare sits on the GPU after the engine's) and checks every
 stream against a no-fault run. Per trial it records, from the fault (the coordinator's stamps are
 wall-clock microseconds of the same host):
