@@ -65,10 +65,10 @@ class Settings:
         return int(max(self.detect_steps * step_period_s * 1e3, self.detect_floor_ms) * 1e6)
 
     def warmup_bound_ns(self) -> int:
-        """The wait bound before the step period is measured (the first `step_sample` steps): the
-        hung-member limit, so the one-off costs of first steps (first launches, allocator growth,
-        graph captures) do not read as a late member. A member that dies is named by its heartbeat
-        (`beat_limit_ms`) whatever the bound."""
+        """The bound for naming a late member before the step period is measured (the first
+        `step_sample` steps): the hung-member limit, so the one-off costs of first steps (first
+        launches, allocator growth, graph captures) do not name a member late. The bound only
+        names; a member that dies is named by its heartbeat (`beat_limit_ms`) whatever it is."""
         return int(max(self.hang_s * 1e3, self.detect_floor_ms) * 1e6)
 
 
