@@ -151,8 +151,8 @@ class MultiprocExecutor:
         e = dict(os.environ)
         root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         e["PYTHONPATH"] = os.pathsep.join([root] + [p for p in e.get("PYTHONPATH", "").split(os.pathsep) if p])
-        # a rank's kernels load with its context, not at their first launch: a first launch in the
-        # middle of a step would hold one member back at the next collective
+        # a rank's kernels load with its context, not at their first launch, so no step (a spare's
+        # first one included) pays a module load that holds its member back at a collective
         e.setdefault("CUDA_MODULE_LOADING", "EAGER")
         e.update(env or {})
         e["EVERSERVE_CARRIER_TOKEN"] = self.token
